@@ -1,0 +1,412 @@
+"""Benchmark of the small-M quantized matmul (BASELINE config 2 at M=8).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one dflash_qmm call: x bf16 [8, 5120] against a 4-bit group-64 MLX-packed
+W [17408, 5120] (the MLP gate/up projection of the 27B target) -> y bf16 [8, 17408].
+Inputs are seeded synthetic data with the config's distributions (x ~ N(0,1),
+W ~ N(0, 0.02)), resident in HBM before the timed region.  L2 is defeated by rotating
+through enough distinct weight copies that every step streams its weights from HBM
+(> 4x the 126 MB L2).  The timed region replays a CUDA graph of the K launches and is
+bracketed by a barrier and device synchronisation; the time is the max over ranks.
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs its own copy of the workload
+(the path shards with no collective), so scaling is weak and `value` is the job total.
+
+--impl reference times this project's CPU restatement of the reference arithmetic
+(oracle/qmm_oracle.c) on the host cores: the reference's own path is Metal/MLX and
+cannot run on this machine.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "dflash-swift_b200"))
+
+METRIC = "M=8 4-bit qmatmul µs and HBM GB/s (% of 8 TB/s); M=8/M=1 time ratio"
+M, N, K, GROUP, BITS = 8, 17408, 5120, 64, 4
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 1024 * 1024
+PROFILE_SUMMARY = ROOT / "profiles" / "qmm_m8_k5120_n17408_4b_g64.json"
+
+
+def algorithmic_bytes(m: int, n: int = N, k: int = K, group: int = GROUP, bits: int = BITS) -> int:
+    """Packed W + bf16 scales + bf16 biases + x + y, each moved once."""
+    return n * k * bits // 8 + 2 * n * (k // group) * 2 + m * k * 2 + m * n * 2
+
+
+def config(m: int = M) -> dict:
+    return {"workload": "qmm_config2_gate_up", "M": m, "N": N, "K": K, "bits": BITS, "group_size": GROUP,
+            "x": "bf16 N(0,1)", "w": "N(0,0.02) MLX affine 4-bit g64",
+            "l2": "rotating distinct weight copies totalling > 4x L2 per pass",
+            "algorithmic_bytes_per_step": algorithmic_bytes(m)}
+
+
+def measured_peak():
+    try:
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ----------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while the GPU works."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.gpus = set(int(g) for g in gpu_indices)
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "50"], stdout=self.out, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.flush()
+        rows = []
+        for line in Path(self.out.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                if int(parts[0]) in self.gpus:
+                    rows.append(parts)
+            except ValueError:
+                continue
+        os.unlink(self.out.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+def to_dev(a, dev):
+    import torch
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint16:
+        return torch.from_numpy(a.view(np.int16)).to(dev).view(torch.bfloat16)
+    if a.dtype == np.uint32:
+        return torch.from_numpy(a.view(np.int32)).to(dev)
+    return torch.from_numpy(a).to(dev)
+
+
+def weight_copies(dev, wq, s, b):
+    """Enough distinct copies of (W, scales, biases) that consecutive steps never hit L2."""
+    import torch
+    per = wq.nbytes + s.nbytes + b.nbytes
+    n = max(2, -(-4 * L2_BYTES // per) + 1)
+    w0, s0, b0 = to_dev(wq, dev), to_dev(s, dev), to_dev(b, dev)
+    copies = [(w0, s0, b0)] + [(w0.clone(), s0.clone(), b0.clone()) for _ in range(n - 1)]
+    torch.cuda.synchronize()
+    return copies
+
+
+def time_graph(dc, dev, x_d, copies, y_d, ws, steps, warmup, m):
+    """Capture one launch per weight copy into a CUDA graph; replay to cover exactly
+    `warmup` then `steps` launches; return elapsed ms of the timed launches."""
+    import torch
+    stream = torch.cuda.Stream(dev)
+    R = len(copies)
+
+    def capture(count):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            # prime once outside capture (one-time kernel attribute setup)
+            dc.qmm(x_d[:m], copies[0][0], copies[0][1], copies[0][2], GROUP, BITS, out=y_d[:m], workspace=ws,
+                   stream=stream)
+        stream.synchronize()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(count):
+                w, s, b = copies[i % R]
+                dc.qmm(x_d[:m], w, s, b, GROUP, BITS, out=y_d[:m], workspace=ws, stream=stream)
+        return g
+
+    full = capture(R)
+    rest_n = steps % R
+    rest = capture(rest_n) if rest_n else None
+    warm_full, warm_rest = divmod(warmup, R)
+    warm_rest_g = capture(warm_rest) if warm_rest else None
+    with torch.cuda.stream(stream):
+        for _ in range(warm_full):
+            full.replay()
+        if warm_rest_g is not None:
+            warm_rest_g.replay()
+    stream.synchronize()
+    return stream, full, rest, steps // R
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import dflashcuda as dc
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O  # seeded input generation (and the CPU baseline below)
+
+    x = O.make_x(16, K, seed_x=0)
+    wq, s, b = O.make_weights(N, K, GROUP, BITS, seed_w=1)
+    copies = weight_copies(dev, wq, s, b)
+    x_d = to_dev(x, dev)
+    y_d = torch.empty((16, N), dtype=torch.bfloat16, device=dev)
+    ws = dc.Workspace(dc.qmm_workspace_bytes(16, N, K, GROUP, BITS), dev)
+
+    # correctness gate before timing
+    dc.qmm(x_d[:M], copies[0][0], copies[0][1], copies[0][2], GROUP, BITS, out=y_d[:M], workspace=ws)
+    torch.cuda.synchronize()
+    rows = np.arange(0, N, 97)
+    err = O.closeness(y_d[:M].float().cpu().numpy()[:, rows], O.qmm_f64(x[:M], wq[rows], s[rows], b[rows], GROUP, BITS))
+    if err > 1e-2:
+        raise SystemExit(f"parity gate failed before timing: closeness {err}")
+
+    def timed(m, steps, warmup, sample_clocks=False):
+        stream, full, rest, reps = time_graph(dc, dev, x_d, copies, y_d, ws, steps, warmup, m)
+        sampler = None
+        if sample_clocks and rank == 0:
+            sampler = ClockSampler(gpu_ids(world))
+            sampler.start()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(reps):
+                full.replay()
+            if rest is not None:
+                rest.replay()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        clocks = sampler.stop() if sampler else None
+        ms = t0.elapsed_time(t1)
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms, clocks
+
+    ms8, clocks = timed(M, args.steps, args.warmup, sample_clocks=True)
+    ms1, _ = timed(1, args.steps, args.warmup)
+    us8 = ms8 * 1e3 / args.steps
+    us1 = ms1 * 1e3 / args.steps
+    bytes8 = algorithmic_bytes(M)
+    per_gpu_gbs = bytes8 / (us8 * 1e-6) / 1e9
+    value = world * per_gpu_gbs
+
+    e2e = e2e_through_abi(dc, dev, x, copies, args, world)
+    if world > 1:
+        t = torch.tensor([e2e["ms"]], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e["ms"] = float(t.item())
+
+    peak, peak_kind = measured_peak()
+    traffic = None
+    if PROFILE_SUMMARY.exists():
+        try:
+            traffic = json.loads(PROFILE_SUMMARY.read_text()).get("dram_bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(O, x[:M], wq, s, b, budget_s=args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(us8 / 1e3, 6), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u4 weights, bf16 x/y, fp32 accumulate", "data": "synthetic",
+            "config": config(M),
+            "us_per_call": round(us8, 3), "us_per_call_m1": round(us1, 3), "m8_over_m1": round(us8 / us1, 4),
+            "pct_of_8TBs": round(100 * per_gpu_gbs / NOMINAL_HBM_GBS, 2),
+            "pct_of_measured_hbm": round(100 * per_gpu_gbs / peak, 2),
+            "roofline": {"bound": "hbm", "achieved": round(per_gpu_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(per_gpu_gbs / peak, 4), "peak_kind": peak_kind,
+                         "traffic": traffic, "algorithmic_bytes": bytes8},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(world * bytes8 / (e2e["ms"] * 1e-3 / args.steps) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                    "us_per_step": round(e2e["ms"] * 1e3 / args.steps, 3),
+                    "path": "pinned host x -> dflash_qmm (C ABI via ctypes) -> pinned host y, per step"},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "parity_closeness_before_timing": err,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def gpu_ids(world):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [int(v) for v in vis.split(",") if v.strip().isdigit()]
+        return ids[:world] if ids else list(range(world))
+    return list(range(world))
+
+
+def e2e_through_abi(dc, dev, x, copies, args, world):
+    """Per step: pinned host x -> device, dflash_qmm through the C ABI, device y ->
+    pinned host; CUDA events around the K steps on the launching stream."""
+    import torch
+    stream = torch.cuda.Stream(dev)
+    x_h = torch.from_numpy(np.ascontiguousarray(x[:M]).view(np.int16)).view(torch.bfloat16).pin_memory()
+    y_h = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    x_d = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
+    y_d = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    ws = dc.Workspace(dc.qmm_workspace_bytes(M, N, K, GROUP, BITS), dev)
+    R = len(copies)
+
+    def step(i):
+        w, s, b = copies[i % R]
+        x_d.copy_(x_h, non_blocking=True)
+        dc.qmm(x_d, w, s, b, GROUP, BITS, out=y_d, workspace=ws, stream=stream)
+        y_h.copy_(y_d, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for i in range(min(args.warmup, 200)):
+            step(i)
+    stream.synchronize()
+    steps = args.steps
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for i in range(steps):
+            step(i)
+        t1.record(stream)
+    stream.synchronize()
+    return {"ms": t0.elapsed_time(t1), "h2d": M * K * 2, "d2h": M * N * 2}
+
+
+def cpu_baseline(O, x, wq, s, b, budget_s: float):
+    """The CPU restatement on all host cores, on a bounded row sample of the same
+    workload; reported as algorithmic GB/s of the rows processed."""
+    threads = os.cpu_count() or 1
+    t = time.perf_counter()
+    y, used = O.qmm_cpu(x, wq, s, b, GROUP, BITS, 0, 256, threads)
+    per_row = (time.perf_counter() - t) / 256
+    n_rows = int(min(N, max(256, budget_s / max(per_row, 1e-9))))
+    t = time.perf_counter()
+    _, used = O.qmm_cpu(x, wq, s, b, GROUP, BITS, 0, n_rows, threads)
+    dt = time.perf_counter() - t
+    bytes_rows = algorithmic_bytes(M, n=n_rows)
+    return {"value": round(bytes_rows / dt / 1e9, 3), "unit": "GB/s", "cores": used, "kind": "port",
+            "sample": f"rows 0..{n_rows} of N={N} (M={M}, K={K}, 4-bit g64), one pass, {dt:.2f} s",
+            "us_per_call_equiv": round(dt * 1e6 * N / n_rows, 1)}
+
+
+# ----------------------------------------------------------------------------- reference arm
+
+def run_reference(args):
+    world, rank, local = dist_env()
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+    x = O.make_x(M, K, seed_x=0)
+    wq, s, b = O.make_weights(N, K, GROUP, BITS, seed_w=1)
+    threads = os.cpu_count() or 1
+    t = time.perf_counter()
+    O.qmm_cpu(x, wq, s, b, GROUP, BITS, 0, 512, threads)
+    per_row = (time.perf_counter() - t) / 512
+    total_steps = args.steps + args.warmup
+    rows = int(max(1, min(N, args.reference_budget_s / total_steps / max(per_row, 1e-9))))
+    out = np.zeros((M, N), dtype=np.uint16)
+    for i in range(args.warmup):
+        n0 = (i * rows) % (N - rows + 1)
+        O.qmm_cpu(x, wq, s, b, GROUP, BITS, n0, n0 + rows, threads, out=out)
+    t = time.perf_counter()
+    used = threads
+    for i in range(args.steps):
+        n0 = (i * rows) % (N - rows + 1)
+        _, used = O.qmm_cpu(x, wq, s, b, GROUP, BITS, n0, n0 + rows, threads, out=out)
+    dt = time.perf_counter() - t
+    gbs = algorithmic_bytes(M, n=rows) * args.steps / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 6),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u4 weights, bf16 x/y, fp32 accumulate", "data": "synthetic", "config": config(M),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": used, "kind": "port",
+                         "sample": f"each step: {rows} consecutive rows of W (of {N}), M={M}, K={K}"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference path is Metal/MLX on Apple GPUs (unavailable here); this is the project's C "
+                "restatement of its arithmetic on all host cores",
+    }
+    print(json.dumps(line))
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=2000)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--reference-budget-s", type=float, default=60.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

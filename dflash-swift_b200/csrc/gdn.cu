@@ -1,0 +1,329 @@
+// Gated-delta recurrence on sm_100a: the verify-time step (whose inputs are the
+// capture) and the rollback replay from the pre-round snapshot.
+//
+// Reference contract: rollbackGatedDeltaRound / rollbackGatedDeltaTree, called at
+// Sources/DFlashKit/DFlashSpeculativeGenerator.swift:455-460, must leave the state a
+// committed forward over the kept positions would have left
+// (Tests/DFlashKitTests/GatedDeltaRollbackTests.swift:84-111).  Both kernels here run
+// the per-position update through the same device function, so a replay of `keep`
+// positions performs exactly the arithmetic a committed step over those positions
+// does.
+//
+// Per head the fp32 state S is [dv, dk], dk contiguous.  Rows of S are independent:
+//     u_i   = v_i - alpha * sum_j S_ij k_j
+//     S_ij <- alpha * S_ij + (beta * u_i) * k_j
+// which is  S <- alpha S;  S <- S + beta (v - S k) k^T  with the decay applied first.
+// The work is bound by reading the snapshot and writing the new state once
+// (2 * 4 * dv * dk bytes per head); each row is held in registers by 8 threads
+// (16 floats each for dk = 128) for all positions, with 128-byte coalesced row access.
+#include "common.cuh"
+
+namespace dflash {
+namespace gdn {
+
+constexpr int kRowThreads = 8;         // threads per state row
+constexpr int kRowsPerBlock = 32;      // rows of S per block (256 threads)
+constexpr int kBlockThreads = kRowThreads * kRowsPerBlock;
+constexpr int kMaxPositions = 64;
+
+struct RowList {
+    int32_t r[kMaxPositions];
+};
+
+// Loads 4 consecutive bf16 (8-byte aligned, global or shared) and widens to fp32.
+__device__ __forceinline__ float4 ld_bf16x4(const uint16_t* p) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u),
+                       __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
+}
+
+// Sum over the 8 threads of a row (lanes 8r .. 8r+7 of a warp).
+__device__ __forceinline__ float row_sum(float v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    return v;
+}
+
+// One position of the recurrence for the slice of one row this thread holds.
+// s: CH float4 chunks of the row; k: the matching chunks of k_t (fp32).
+template <int CH>
+__device__ __forceinline__ void row_step(float4 (&s)[CH], const float4 (&k)[CH], float v, float alpha,
+                                         float beta) {
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        dot = fmaf(s[c].x, k[c].x, dot);
+        dot = fmaf(s[c].y, k[c].y, dot);
+        dot = fmaf(s[c].z, k[c].z, dot);
+        dot = fmaf(s[c].w, k[c].w, dot);
+    }
+    dot = row_sum(dot);
+    const float bu = beta * (v - alpha * dot);
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        s[c].x = fmaf(bu, k[c].x, alpha * s[c].x);
+        s[c].y = fmaf(bu, k[c].y, alpha * s[c].y);
+        s[c].z = fmaf(bu, k[c].z, alpha * s[c].z);
+        s[c].w = fmaf(bu, k[c].w, alpha * s[c].w);
+    }
+}
+
+template <int CH>
+__device__ __forceinline__ float row_dot(const float4 (&s)[CH], const float4 (&q)[CH]) {
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        dot = fmaf(s[c].x, q[c].x, dot);
+        dot = fmaf(s[c].y, q[c].y, dot);
+        dot = fmaf(s[c].z, q[c].z, dot);
+        dot = fmaf(s[c].w, q[c].w, dot);
+    }
+    return row_sum(dot);
+}
+
+struct ReplayParams {
+    const float* snapshot;
+    float* state_out;
+    const dflash_bf16* k;
+    const dflash_bf16* v;
+    const float* alpha;
+    const float* beta;
+    const dflash_bf16* q;     // step kernel only (may be null)
+    dflash_bf16* out;         // step kernel only (may be null)
+    float q_scale;
+    int keep, width, heads, dk, dv;
+    RowList rows;
+};
+
+// grid: (dv / 32, heads, layers); block: 256 threads = 32 rows x 8 threads.
+// Thread q of a row holds float4 chunks q, q+8, q+16, ... of the row (dk = 32 * CH).
+template <int CH>
+__global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constant__ ReplayParams p) {
+    constexpr int DK = 32 * CH;
+    // k and q of the replayed positions, kept as bf16 bits (widened on use)
+    __shared__ __align__(16) uint16_t ks[kMaxPositions][DK];
+    __shared__ __align__(16) uint16_t qs_sh[kMaxPositions][DK];
+    __shared__ float ab[kMaxPositions][2];
+
+    const int layer = blockIdx.z, h = blockIdx.y;
+    const int row0 = blockIdx.x * kRowsPerBlock;
+    const int tid = threadIdx.x;
+    const int rl = tid / kRowThreads, qd = tid % kRowThreads;
+    const int row = row0 + rl;
+    const bool want_out = p.out != nullptr && p.q != nullptr;
+
+    // Stage k (and q), alpha, beta of the replayed positions.
+    const size_t pos_stride = (size_t)p.heads;  // [width, H] per layer for alpha/beta
+    for (int idx = tid; idx < p.keep * (DK / 4); idx += kBlockThreads) {
+        const int r = idx / (DK / 4), c4 = (idx % (DK / 4)) * 4;
+        const int t = p.rows.r[r];
+        const size_t base = (((size_t)layer * p.width + t) * p.heads + h) * DK + c4;
+        *reinterpret_cast<uint2*>(&ks[r][c4]) = *reinterpret_cast<const uint2*>(p.k + base);
+        if (want_out) *reinterpret_cast<uint2*>(&qs_sh[r][c4]) = *reinterpret_cast<const uint2*>(p.q + base);
+    }
+    for (int r = tid; r < p.keep; r += kBlockThreads) {
+        const int t = p.rows.r[r];
+        const size_t ai = ((size_t)layer * p.width + t) * pos_stride + h;
+        ab[r][0] = p.alpha[ai];
+        ab[r][1] = p.beta[ai];
+    }
+
+    // This thread's slice of the state row.
+    const size_t head_base = (((size_t)layer * p.heads + h) * p.dv + row) * DK;
+    float4 s[CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c)
+        s[c] = __ldcs(reinterpret_cast<const float4*>(p.snapshot + head_base) + qd + c * kRowThreads);
+    __syncthreads();
+
+    for (int r = 0; r < p.keep; ++r) {
+        const int t = p.rows.r[r];
+        float4 k[CH];
+#pragma unroll
+        for (int c = 0; c < CH; ++c) k[c] = ld_bf16x4(&ks[r][4 * (qd + c * kRowThreads)]);
+        const size_t vi = (((size_t)layer * p.width + t) * p.heads + h) * p.dv + row;
+        const float v = __uint_as_float((uint32_t)p.v[vi] << 16);
+        row_step<CH>(s, k, v, ab[r][0], ab[r][1]);
+        if (want_out) {
+            float4 qv[CH];
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                const float4 raw = ld_bf16x4(&qs_sh[r][4 * (qd + c * kRowThreads)]);
+                qv[c] = make_float4(raw.x * p.q_scale, raw.y * p.q_scale, raw.z * p.q_scale, raw.w * p.q_scale);
+            }
+            const float o = row_dot<CH>(s, qv);
+            if (qd == 0) {
+                __nv_bfloat16 ob = __float2bfloat16_rn(o);
+                p.out[(((size_t)layer * p.width + t) * p.heads + h) * p.dv + row] =
+                    *reinterpret_cast<uint16_t*>(&ob);
+            }
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < CH; ++c)
+        __stcs(reinterpret_cast<float4*>(p.state_out + head_base) + qd + c * kRowThreads, s[c]);
+}
+
+int launch(const ReplayParams& p, int layers, cudaStream_t stream) {
+    dim3 grid(p.dv / kRowsPerBlock, p.heads, layers);
+    switch (p.dk) {
+        case 32: gdn_kernel<1><<<grid, kBlockThreads, 0, stream>>>(p); break;
+        case 64: gdn_kernel<2><<<grid, kBlockThreads, 0, stream>>>(p); break;
+        case 128: gdn_kernel<4><<<grid, kBlockThreads, 0, stream>>>(p); break;
+        default: return fail(DFLASH_ERR_UNSUPPORTED, "dk=%d not in {32, 64, 128}", p.dk);
+    }
+    DFLASH_CUDA_TRY(cudaGetLastError());
+    return DFLASH_OK;
+}
+
+int check_dims(int heads, int dk, int dv) {
+    if (heads < 1) return fail(DFLASH_ERR_INVALID_ARGUMENT, "heads=%d must be positive", heads);
+    if (dk != 32 && dk != 64 && dk != 128) return fail(DFLASH_ERR_UNSUPPORTED, "dk=%d not in {32, 64, 128}", dk);
+    if (dv < kRowsPerBlock || dv % kRowsPerBlock != 0)
+        return fail(DFLASH_ERR_UNSUPPORTED, "dv=%d must be a positive multiple of %d", dv, kRowsPerBlock);
+    return DFLASH_OK;
+}
+
+// conv window gather: out[l][r][:] = r+keep < kc1 ? window[l][r+keep][:] : conv_in[l][rows[r+keep-kc1]][:]
+__global__ void conv_rollback_kernel(const dflash_bf16* window, dflash_bf16* out, const dflash_bf16* conv_in,
+                                     RowList rows, int keep, int width, int kc1, int channels, int vec8) {
+    const int l = blockIdx.y, r = blockIdx.x;
+    const int pos = keep + r;
+    const dflash_bf16* src = (pos < kc1) ? window + ((size_t)l * kc1 + pos) * channels
+                                         : conv_in + ((size_t)l * width + rows.r[pos - kc1]) * channels;
+    dflash_bf16* dst = out + ((size_t)l * kc1 + r) * channels;
+    if (vec8) {
+        for (int c = threadIdx.x; c < channels / 8; c += blockDim.x)
+            reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(src)[c];
+    } else {
+        for (int c = threadIdx.x; c < channels; c += blockDim.x) dst[c] = src[c];
+    }
+}
+
+// Test hook: an mbarrier nothing ever arrives on, waited on with a bound.
+__global__ void bounded_wait_kernel(unsigned long long limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(&bar, 0)) {
+            if (globaltimer_ns() - t0 > limit_ns) {
+                atomicOr(&g_device_error, DFLASH_DEVERR_TEST_WAIT);
+                break;
+            }
+        }
+    }
+}
+
+int fill_rows(RowList& rl, const int32_t* rows, int keep, int width) {
+    for (int i = 0; i < keep; ++i) {
+        const int r = rows ? rows[i] : i;
+        if (r < 0 || r >= width)
+            return fail(DFLASH_ERR_INVALID_ARGUMENT, "rows[%d]=%d outside [0, %d)", i, r, width);
+        rl.r[i] = r;
+    }
+    return DFLASH_OK;
+}
+
+}  // namespace gdn
+}  // namespace dflash
+
+extern "C" int dflash_gdn_step(const float* state_in, float* state_out, const dflash_bf16* q,
+                               const dflash_bf16* k, const dflash_bf16* v, const float* alpha,
+                               const float* beta, dflash_bf16* out, int T, int heads, int dk, int dv,
+                               float q_scale, dflash_stream_t stream) {
+    using namespace dflash;
+    if (int st = gdn::check_dims(heads, dk, dv)) return st;
+    if (T < 1 || T > gdn::kMaxPositions)
+        return fail(DFLASH_ERR_UNSUPPORTED, "T=%d outside 1..%d", T, gdn::kMaxPositions);
+    if (!state_in || !state_out || !k || !v || !alpha || !beta || (out && !q))
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_gdn_step: null tensor pointer");
+    if (state_in == state_out)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_gdn_step: state_in and state_out must differ");
+    if (!aligned16(state_in) || !aligned16(state_out) || (reinterpret_cast<uintptr_t>(k) & 7) ||
+        (q && (reinterpret_cast<uintptr_t>(q) & 7)))
+        return fail(DFLASH_ERR_MISALIGNED, "dflash_gdn_step: state 16-byte, q/k 8-byte alignment required");
+    gdn::ReplayParams p{};
+    p.snapshot = state_in;
+    p.state_out = state_out;
+    p.k = k;
+    p.v = v;
+    p.alpha = alpha;
+    p.beta = beta;
+    p.q = q;
+    p.out = out;
+    p.q_scale = q_scale;
+    p.keep = T;
+    p.width = T;
+    p.heads = heads;
+    p.dk = dk;
+    p.dv = dv;
+    if (int st = gdn::fill_rows(p.rows, nullptr, T, T)) return st;
+    return gdn::launch(p, 1, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dflash_gdn_replay(const float* snapshot, float* state_out, const dflash_bf16* k,
+                                 const dflash_bf16* v, const float* alpha, const float* beta,
+                                 const int32_t* rows, int keep, int width, int layers, int heads, int dk,
+                                 int dv, dflash_stream_t stream) {
+    using namespace dflash;
+    if (int st = gdn::check_dims(heads, dk, dv)) return st;
+    if (layers < 1) return fail(DFLASH_ERR_INVALID_ARGUMENT, "layers=%d must be positive", layers);
+    if (width < 1 || width > gdn::kMaxPositions || keep < 1 || keep > width)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "need 1 <= keep (%d) <= width (%d) <= %d", keep, width,
+                    gdn::kMaxPositions);
+    if (!snapshot || !state_out || !k || !v || !alpha || !beta)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_gdn_replay: null tensor pointer");
+    if (snapshot == state_out)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_gdn_replay: snapshot and state_out must differ");
+    if (!aligned16(snapshot) || !aligned16(state_out) || (reinterpret_cast<uintptr_t>(k) & 7))
+        return fail(DFLASH_ERR_MISALIGNED, "dflash_gdn_replay: state 16-byte, k 8-byte alignment required");
+    gdn::ReplayParams p{};
+    p.snapshot = snapshot;
+    p.state_out = state_out;
+    p.k = k;
+    p.v = v;
+    p.alpha = alpha;
+    p.beta = beta;
+    p.keep = keep;
+    p.width = width;
+    p.heads = heads;
+    p.dk = dk;
+    p.dv = dv;
+    if (int st = gdn::fill_rows(p.rows, rows, keep, width)) return st;
+    return gdn::launch(p, layers, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dflash_gdn_conv_rollback(const dflash_bf16* window, dflash_bf16* window_out,
+                                        const dflash_bf16* conv_in, const int32_t* rows, int keep, int width,
+                                        int layers, int kc1, int channels, dflash_stream_t stream) {
+    using namespace dflash;
+    if (layers < 1 || kc1 < 1 || channels < 1)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "layers, kc1 and channels must be positive");
+    if (width < 1 || width > gdn::kMaxPositions || keep < 1 || keep > width)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "need 1 <= keep (%d) <= width (%d) <= %d", keep, width,
+                    gdn::kMaxPositions);
+    if (!window || !window_out || !conv_in)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_gdn_conv_rollback: null tensor pointer");
+    if (window == window_out)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_gdn_conv_rollback: window_out must not alias window");
+    gdn::RowList rl{};
+    if (int st = gdn::fill_rows(rl, rows, keep, width)) return st;
+    const int vec8 = (channels % 8 == 0) && aligned16(window) && aligned16(window_out) && aligned16(conv_in);
+    dim3 grid(kc1, layers);
+    gdn::conv_rollback_kernel<<<grid, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        window, window_out, conv_in, rl, keep, width, kc1, channels, vec8);
+    DFLASH_CUDA_TRY(cudaGetLastError());
+    return DFLASH_OK;
+}
+
+extern "C" int dflash_test_bounded_wait(uint64_t limit_ns, dflash_stream_t stream) {
+    using namespace dflash;
+    if (limit_ns == 0 || limit_ns > kWaitLimitNs)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "limit_ns must be in 1..%llu", kWaitLimitNs);
+    gdn::bounded_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(limit_ns);
+    DFLASH_CUDA_TRY(cudaGetLastError());
+    return DFLASH_OK;
+}

@@ -1,0 +1,617 @@
+// Small-M affine-quantized matmul for sm_100a:  y[M,N] = x[M,K] . deq(W)[N,K]^T.
+//
+// Replaces SmallMQuantizedMatmul.apply (Sources/DFlashKit/SmallMQuantizedMatmul.swift:
+// 210-224) and the stock quantizedMatmul it stands in for.  The work is bound by the
+// packed weight stream (M <= 16 rows against N*K quantized weights), so the kernel is
+// built around moving those bytes from HBM exactly once at full bandwidth:
+//
+//  * Persistent grid, one CTA per SM.  The weight matrix is cut into row tiles of 256
+//    output features; the (row tile, quantization group) pairs are split into equal
+//    contiguous ranges, one per CTA (stream-K), so every SM streams the same number
+//    of bytes whatever N and K are.  A row tile cut between CTAs is finished by the
+//    last CTA to arrive (fp32 partials in the workspace, fixed summation order).
+//  * One producer warp issues TMA tile loads (cp.async.bulk.tensor, no multicast)
+//    into a 4-deep shared-memory ring: per stage a [256 rows x 128 B] weight box with
+//    128-byte swizzle, the matching x columns, and the scale/bias columns.
+//  * 16 consumer warps: 8 row slices of 32 features x 2 stage parities.  Each
+//    dequantises in registers and contracts on mma.sync m16n8k16 with the weights as
+//    the 16-row A operand and x (<= 8 rows per n-tile) as the n=8 B operand, so a
+//    weight is read and dequantised once for all M rows.
+//
+// Dequantisation uses the factored form  sum_k x q s + b x  =  s (sum_k x q) + b (sum_k x)
+// per group: integer codes become bf16 exactly by OR-ing a nibble into the mantissa
+// of 128.0 (0x4300), one LOP3 per two weights; the group sum of x comes from an extra
+// MMA against an all-ones A operand; the 128 offset folds into the bias term.  8-bit
+// codes are split into two nibbles contracted against x and 16*x.  Within a thread's
+// slice of a group the k order is permuted identically for weights and x (sums do
+// not depend on k order), so weights are consumed exactly as MLX packs them.
+#include "common.cuh"
+
+namespace dflash {
+namespace qmm {
+
+constexpr int kRows = 256;            // output features per row tile
+constexpr int kRowBytes = 128;        // weight bytes per row per stage (one swizzle span)
+constexpr int kRowSlices = 8;         // 32-feature slices per tile (one per consumer warp)
+constexpr int kKSplit = 2;            // consumer warp groups, alternating stages
+constexpr int kConsumerWarps = kRowSlices * kKSplit;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;
+constexpr int kStages = 4;
+constexpr int kRedPitch = kRows + 4;  // floats per m row of the reduction buffer (bank spread)
+constexpr int kMaxCtas = 160;         // upper bound on the persistent grid (B200: 148 SMs)
+constexpr int kBarConsumers = 1;      // named barrier id used by the consumer warps
+
+template <int BITS_, int GROUP_, int NT_, bool STMA_>
+struct Cfg {
+    static constexpr int BITS = BITS_, GROUP = GROUP_, NT = NT_;
+    static constexpr bool STMA = STMA_;                  // scales/biases through TMA
+    static constexpr int GB = GROUP * BITS / 8;          // bytes per row per group
+    static constexpr int GPS = kRowBytes / GB;           // groups per stage
+    static constexpr int TB = GB / 4;                    // bytes per thread per row per group
+    static constexpr int KPS = GPS * GROUP;              // k per stage
+    static constexpr int XBOX = KPS / 64;                // x boxes (64 k each) per stage
+    static constexpr int XROWS = 8 * NT;
+    static constexpr int W_BYTES = kRows * kRowBytes;
+    static constexpr int XBOX_BYTES = XROWS * 128;
+    static constexpr int X_BYTES = XBOX * XBOX_BYTES;
+    static constexpr int S_BYTES = kRows * 16;           // [256 rows x 8 groups] bf16
+    static constexpr int STAGE_BYTES = W_BYTES + X_BYTES + 2 * S_BYTES;
+    static constexpr uint32_t TX_BYTES = W_BYTES + X_BYTES + (STMA ? 2 * S_BYTES : 0);
+    static constexpr int VPT = GROUP / 4;                // values per thread per row per group
+    static constexpr int PV = VPT < 16 ? VPT : 16;       // values per piece
+    static constexpr int PIECES = VPT / PV;
+    static constexpr int PB = PV * BITS / 8;             // bytes per piece per row
+    static constexpr int PW = PB / 4;                    // 32-bit words per piece per row
+    static constexpr int PSTEPS = PV / 4;                // k16 MMA steps per piece
+    static constexpr int PXCH = PV / 8;                  // 8-value x chunks per piece
+    static constexpr int RED_FLOATS = NT * 8 * kRedPitch;
+    static constexpr int SMEM_BYTES = kStages * STAGE_BYTES + RED_FLOATS * 4 + 256 + 1024;
+    static constexpr float OFFSET = BITS == 4 ? 128.f : 2176.f;  // magic-number offset per unit x
+    static_assert(GPS >= 1 && GPS <= 8 && (8 % GPS) == 0, "stage/group geometry");
+    static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte swizzle alignment");
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+struct Params {
+    dflash_bf16* y;
+    const dflash_bf16* scales;
+    const dflash_bf16* biases;
+    float* partials;
+    int* counters;
+    int M, N, K, GT, tiles, G;
+    long long U;
+    int y_vec;
+};
+
+__device__ __forceinline__ long long owner_of(long long u, const Params& p) {
+    return ((u + 1) * p.G - 1) / p.U;
+}
+__device__ __forceinline__ long long range_begin(long long c, const Params& p) {
+    return c * p.U / p.G;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    return __byte_perm(a, b, sel);
+}
+
+__device__ __forceinline__ uint32_t bf16x2_times16(uint32_t v) {
+    __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&v);
+    h = __hmul2(h, __floats2bfloat162_rn(16.f, 16.f));
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+constexpr uint32_t kMagic = 0x43004300u;   // bf16x2 (128.0, 128.0)
+constexpr uint32_t kNib = 0x000F000Fu;
+constexpr uint32_t kOnes = 0x3F803F80u;    // bf16x2 (1.0, 1.0)
+
+template <class C>
+__device__ __forceinline__ void load_words(uint32_t (&dst)[C::PW], uint32_t addr) {
+    if constexpr (C::PB == 4) {
+        dst[0] = lds32(addr);
+    } else if constexpr (C::PB == 8) {
+        uint2 v = lds64(addr);
+        dst[0] = v.x;
+        dst[1] = v.y;
+    } else {
+        uint4 v = lds128(addr);
+        dst[0] = v.x;
+        dst[1] = v.y;
+        dst[2] = v.z;
+        dst[3] = v.w;
+    }
+}
+
+// One quantization group of one stage for one consumer warp (32 rows x GROUP k).
+template <class C>
+__device__ __forceinline__ void consume_group(uint32_t w_base, uint32_t x_base,
+                                              const dflash_bf16* s_tile, const dflash_bf16* b_tile,
+                                              int gl, int G, int rb, int g, int tq, int tile_row0,
+                                              const Params& p, float (&acc)[2][C::NT][4]) {
+    float tmp[2][C::NT][4];
+    float xs[C::NT][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < C::NT; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) tmp[i][j][e] = 0.f;
+#pragma unroll
+    for (int j = 0; j < C::NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) xs[j][e] = 0.f;
+
+#pragma unroll
+    for (int pc = 0; pc < C::PIECES; ++pc) {
+        // B fragments: this thread's slice of x for activation rows 8j + g.
+        uint32_t xb[C::NT][C::PXCH][4];
+#pragma unroll
+        for (int j = 0; j < C::NT; ++j) {
+            const int m = 8 * j + g;
+#pragma unroll
+            for (int c = 0; c < C::PXCH; ++c) {
+                const int k = gl * C::GROUP + tq * C::VPT + pc * C::PV + 8 * c;  // stage-local
+                const int box = k >> 6, chunk = (k & 63) >> 3;
+                const uint4 r = lds128(x_base + box * C::XBOX_BYTES + m * 128 + ((chunk ^ (m & 7)) << 4));
+                if constexpr (C::BITS == 4) {
+                    xb[j][c][0] = prmt(r.x, r.z, 0x5410);  // (x0, x4)
+                    xb[j][c][1] = prmt(r.x, r.z, 0x7632);  // (x1, x5)
+                    xb[j][c][2] = prmt(r.y, r.w, 0x5410);  // (x2, x6)
+                    xb[j][c][3] = prmt(r.y, r.w, 0x7632);  // (x3, x7)
+                } else {
+                    xb[j][c][0] = prmt(r.x, r.y, 0x5410);  // (x0, x2)
+                    xb[j][c][1] = prmt(r.x, r.y, 0x7632);  // (x1, x3)
+                    xb[j][c][2] = prmt(r.z, r.w, 0x5410);  // (x4, x6)
+                    xb[j][c][3] = prmt(r.z, r.w, 0x7632);  // (x5, x7)
+                }
+            }
+        }
+        // A operand source: packed words of rows rb + 16i + 8h + g.
+        uint32_t wv[2][2][C::PW];
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r = rb + 16 * i + 8 * h + g;
+                const int off = gl * C::GB + tq * C::TB + pc * C::PB;
+                const uint32_t a = w_base + r * kRowBytes + (((off >> 4) ^ (r & 7)) << 4) + (off & 15);
+                load_words<C>(wv[i][h], a);
+            }
+#pragma unroll
+        for (int s = 0; s < C::PSTEPS; ++s) {
+            if constexpr (C::BITS == 4) {
+                const int w = s >> 1, q = (s & 1) * 2;
+#pragma unroll
+                for (int j = 0; j < C::NT; ++j) {
+                    const uint32_t b0 = xb[j][w][q], b1 = xb[j][w][q + 1];
+                    mma_bf16_16816(xs[j], kOnes, kOnes, kOnes, kOnes, b0, b1);
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        const uint32_t a0 = ((wv[i][0][w] >> (4 * q)) & kNib) | kMagic;
+                        const uint32_t a1 = ((wv[i][1][w] >> (4 * q)) & kNib) | kMagic;
+                        const uint32_t a2 = ((wv[i][0][w] >> (4 * q + 4)) & kNib) | kMagic;
+                        const uint32_t a3 = ((wv[i][1][w] >> (4 * q + 4)) & kNib) | kMagic;
+                        mma_bf16_16816(tmp[i][j], a0, a1, a2, a3, b0, b1);
+                    }
+                }
+            } else {
+                const int w = s, c = s >> 1, q = (s & 1) * 2;
+#pragma unroll
+                for (int j = 0; j < C::NT; ++j) {
+                    const uint32_t b0 = xb[j][c][q], b1 = xb[j][c][q + 1];
+                    const uint32_t h0 = bf16x2_times16(b0), h1 = bf16x2_times16(b1);
+                    mma_bf16_16816(xs[j], kOnes, kOnes, kOnes, kOnes, b0, b1);
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        const uint32_t w0 = wv[i][0][w], w1 = wv[i][1][w];
+                        mma_bf16_16816(tmp[i][j], (w0 & kNib) | kMagic, (w1 & kNib) | kMagic,
+                                       ((w0 >> 8) & kNib) | kMagic, ((w1 >> 8) & kNib) | kMagic, b0, b1);
+                        mma_bf16_16816(tmp[i][j], ((w0 >> 4) & kNib) | kMagic, ((w1 >> 4) & kNib) | kMagic,
+                                       ((w0 >> 12) & kNib) | kMagic, ((w1 >> 12) & kNib) | kMagic, h0, h1);
+                    }
+                }
+            }
+        }
+    }
+
+    // acc += s * tmp + (b - OFFSET * s) * xs, per feature row.
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int r = rb + 16 * i + 8 * h + g;
+            float s, b;
+            if constexpr (C::STMA) {
+                s = bf16_bits_to_float(s_tile[r * 8 + (G & 7)]);
+                b = bf16_bits_to_float(b_tile[r * 8 + (G & 7)]);
+            } else {
+                const int n = tile_row0 + r;
+                if (n < p.N) {
+                    const size_t idx = (size_t)n * p.GT + G;
+                    s = bf16_bits_to_float(__ldg(p.scales + idx));
+                    b = bf16_bits_to_float(__ldg(p.biases + idx));
+                } else {
+                    s = 0.f;
+                    b = 0.f;
+                }
+            }
+            const float bb = fmaf(-C::OFFSET, s, b);
+#pragma unroll
+            for (int j = 0; j < C::NT; ++j)
+#pragma unroll
+                for (int e = 0; e < 2; ++e)
+                    acc[i][j][2 * h + e] = fmaf(s, tmp[i][j][2 * h + e], fmaf(bb, xs[j][2 * h + e], acc[i][j][2 * h + e]));
+        }
+}
+
+// Writes the fp32 tile in `red` ([NT*8][kRedPitch]) to y as bf16.
+template <class C>
+__device__ __forceinline__ void write_tile(const float* red, int t, const Params& p, int ctid) {
+    const int n0 = t * kRows;
+    if (p.y_vec) {
+        for (int idx = ctid; idx < C::NT * 8 * (kRows / 8); idx += kConsumerThreads) {
+            const int m = idx / (kRows / 8), r0 = (idx % (kRows / 8)) * 8;
+            if (m >= p.M || n0 + r0 >= p.N) continue;
+            const float4 a = *reinterpret_cast<const float4*>(red + m * kRedPitch + r0);
+            const float4 b = *reinterpret_cast<const float4*>(red + m * kRedPitch + r0 + 4);
+            __nv_bfloat162 o0 = __floats2bfloat162_rn(a.x, a.y), o1 = __floats2bfloat162_rn(a.z, a.w);
+            __nv_bfloat162 o2 = __floats2bfloat162_rn(b.x, b.y), o3 = __floats2bfloat162_rn(b.z, b.w);
+            uint4 v;
+            v.x = *reinterpret_cast<uint32_t*>(&o0);
+            v.y = *reinterpret_cast<uint32_t*>(&o1);
+            v.z = *reinterpret_cast<uint32_t*>(&o2);
+            v.w = *reinterpret_cast<uint32_t*>(&o3);
+            *reinterpret_cast<uint4*>(p.y + (size_t)m * p.N + n0 + r0) = v;
+        }
+    } else {
+        for (int idx = ctid; idx < C::NT * 8 * kRows; idx += kConsumerThreads) {
+            const int m = idx / kRows, r = idx % kRows;
+            if (m >= p.M || n0 + r >= p.N) continue;
+            __nv_bfloat16 o = __float2bfloat16_rn(red[m * kRedPitch + r]);
+            p.y[(size_t)m * p.N + n0 + r] = *reinterpret_cast<uint16_t*>(&o);
+        }
+    }
+}
+
+template <class C>
+__global__ void __launch_bounds__(kThreads, 1)
+    qmm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+               const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_b,
+               const Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* red = reinterpret_cast<float*>(smem + kStages * C::STAGE_BYTES);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * C::STAGE_BYTES + C::RED_FLOATS * 4);
+    uint64_t* empty = full + kStages;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
+    volatile int* last_flag = abort_flag + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kRowSlices);
+        }
+        *abort_flag = 0;
+        *last_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    const long long c = blockIdx.x;
+    const long long u0 = range_begin(c, p), u1 = range_begin(c + 1, p);
+    const int first_tile = (int)(u0 / p.GT);
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------------------------------------ producer
+        if (lane != 0) return;
+        prefetch_tensormap(&tm_w);
+        prefetch_tensormap(&tm_x);
+        if constexpr (C::STMA) {
+            prefetch_tensormap(&tm_s);
+            prefetch_tensormap(&tm_b);
+        }
+        int j = 0;
+        bool ok = true;
+        for (long long u = u0; u < u1 && ok;) {
+            const int t = (int)(u / p.GT);
+            const int ga = (int)(u - (long long)t * p.GT);
+            const int gb = (int)min((long long)p.GT, u1 - (long long)t * p.GT);
+            for (int sc = ga / C::GPS; sc < (gb + C::GPS - 1) / C::GPS; ++sc, ++j) {
+                const int slot = j % kStages;
+                const uint32_t ph = (uint32_t)(j / kStages) & 1u;
+                if (!mbar_wait_bounded(&empty[slot], ph ^ 1u, abort_flag, DFLASH_DEVERR_QMM_PIPELINE)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* st = smem + slot * C::STAGE_BYTES;
+                mbar_arrive_expect_tx(&full[slot], C::TX_BYTES);
+                tma_load_2d(st, &tm_w, &full[slot], sc * (kRowBytes / 4), t * kRows);
+#pragma unroll
+                for (int b = 0; b < C::XBOX; ++b)
+                    tma_load_2d(st + C::W_BYTES + b * C::XBOX_BYTES, &tm_x, &full[slot], sc * C::KPS + 64 * b, 0);
+                if constexpr (C::STMA) {
+                    const int gx = (sc * C::GPS) & ~7;
+                    tma_load_2d(st + C::W_BYTES + C::X_BYTES, &tm_s, &full[slot], gx, t * kRows);
+                    tma_load_2d(st + C::W_BYTES + C::X_BYTES + C::S_BYTES, &tm_b, &full[slot], gx, t * kRows);
+                }
+            }
+            u = (long long)t * p.GT + gb;
+        }
+        // Drain: do not leave the CTA while issued copies may still be landing.
+        for (int i = max(0, j - kStages); i < j; ++i) {
+            const int slot = i % kStages;
+            const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+            const unsigned long long t0 = globaltimer_ns();
+            while (!mbar_try_wait(&full[slot], ph) && globaltimer_ns() - t0 < kWaitLimitNs) {
+            }
+        }
+        return;
+    }
+
+    // -------------------------------------------------------------- consumers
+    const int rs = warp % kRowSlices, par = warp / kRowSlices;
+    const int g = lane >> 2, tq = lane & 3;
+    const int rb = rs * 32;
+    const int ctid = threadIdx.x;  // 0 .. kConsumerThreads-1
+    int j = 0;
+
+    for (long long u = u0; u < u1;) {
+        const int t = (int)(u / p.GT);
+        const int ga = (int)(u - (long long)t * p.GT);
+        const int gb = (int)min((long long)p.GT, u1 - (long long)t * p.GT);
+        const int tile_row0 = t * kRows;
+
+        float acc[2][C::NT][4];
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int jj = 0; jj < C::NT; ++jj)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[i][jj][e] = 0.f;
+
+        for (int sc = ga / C::GPS; sc < (gb + C::GPS - 1) / C::GPS; ++sc, ++j) {
+            if ((j & 1) != par) continue;
+            const int slot = j % kStages;
+            const uint32_t ph = (uint32_t)(j / kStages) & 1u;
+            // mma.sync below is warp-collective: every lane must take the same branch
+            const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[slot], ph, abort_flag,
+                                                                       DFLASH_DEVERR_QMM_PIPELINE));
+            if (ok) {
+                const uint8_t* st = smem + slot * C::STAGE_BYTES;
+                const uint32_t w_base = smem_u32(st);
+                const uint32_t x_base = smem_u32(st + C::W_BYTES);
+                const dflash_bf16* s_tile = reinterpret_cast<const dflash_bf16*>(st + C::W_BYTES + C::X_BYTES);
+                const dflash_bf16* b_tile = s_tile + kRows * 8;
+#pragma unroll
+                for (int gl = 0; gl < C::GPS; ++gl) {
+                    const int G = sc * C::GPS + gl;
+                    if (G < ga || G >= gb) continue;
+                    consume_group<C>(w_base, x_base, s_tile, b_tile, gl, G, rb, g, tq, tile_row0, p, acc);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+
+        // ---- reduce the two stage-parity halves into `red`
+        named_bar_sync(kBarConsumers, kConsumerThreads);
+        if (par == 1) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int jj = 0; jj < C::NT; ++jj)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e)
+                            red[(8 * jj + 2 * tq + e) * kRedPitch + rb + 16 * i + 8 * h + g] = acc[i][jj][2 * h + e];
+        }
+        named_bar_sync(kBarConsumers, kConsumerThreads);
+        if (par == 0) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int jj = 0; jj < C::NT; ++jj)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e)
+                            red[(8 * jj + 2 * tq + e) * kRedPitch + rb + 16 * i + 8 * h + g] += acc[i][jj][2 * h + e];
+        }
+        named_bar_sync(kBarConsumers, kConsumerThreads);
+
+        if (ga == 0 && gb == p.GT) {
+            write_tile<C>(red, t, p, ctid);
+        } else {
+            // ---- stream-K: publish this CTA's partial, the last contributor finishes
+            const int slot = (t == first_tile) ? 0 : 1;
+            constexpr int TILE_FLOATS = C::NT * 8 * kRows;
+            float* dst = p.partials + (size_t)(c * 2 + slot) * TILE_FLOATS;
+            for (int idx = ctid; idx < TILE_FLOATS / 4; idx += kConsumerThreads) {
+                const int m = idx / (kRows / 4), r4 = (idx % (kRows / 4)) * 4;
+                __stcg(reinterpret_cast<float4*>(dst + m * kRows + r4),
+                       *reinterpret_cast<const float4*>(red + m * kRedPitch + r4));
+            }
+            __threadfence();
+            named_bar_sync(kBarConsumers, kConsumerThreads);
+            const long long cf = owner_of((long long)t * p.GT, p);
+            const long long cl = owner_of((long long)(t + 1) * p.GT - 1, p);
+            if (ctid == 0) {
+                const int need = (int)(cl - cf + 1);
+                const int old = atomicAdd(p.counters + t, 1);
+                const int last = (old == need - 1);
+                if (old >= need) atomicOr(&g_device_error, DFLASH_DEVERR_QMM_REDUCE);
+                if (last) {
+                    atomicExch(p.counters + t, 0);
+                    __threadfence();
+                }
+                *last_flag = last;
+            }
+            named_bar_sync(kBarConsumers, kConsumerThreads);
+            if (*last_flag) {
+                for (int idx = ctid; idx < TILE_FLOATS / 4; idx += kConsumerThreads) {
+                    const int m = idx / (kRows / 4), r4 = (idx % (kRows / 4)) * 4;
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (long long cc = cf; cc <= cl; ++cc) {
+                        const int sl = ((int)(range_begin(cc, p) / p.GT) == t) ? 0 : 1;
+                        const float4 q = __ldcg(reinterpret_cast<const float4*>(
+                            p.partials + (size_t)(cc * 2 + sl) * TILE_FLOATS + m * kRows + r4));
+                        v.x += q.x;
+                        v.y += q.y;
+                        v.z += q.z;
+                        v.w += q.w;
+                    }
+                    *reinterpret_cast<float4*>(red + m * kRedPitch + r4) = v;
+                }
+                named_bar_sync(kBarConsumers, kConsumerThreads);
+                write_tile<C>(red, t, p, ctid);
+            }
+        }
+        named_bar_sync(kBarConsumers, kConsumerThreads);
+        u = (long long)t * p.GT + gb;
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+struct Shape {
+    int M, N, K, group, bits;
+};
+
+inline int n_tiles(int N) { return (N + kRows - 1) / kRows; }
+
+inline size_t counters_bytes(int N) { return ((size_t)n_tiles(N) * 4 + 255) & ~size_t(255); }
+
+inline size_t partials_bytes() { return (size_t)kMaxCtas * 2 * 16 * kRows * 4; }
+
+template <class C>
+int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scales,
+           const dflash_bf16* biases, dflash_bf16* y, void* ws, cudaStream_t stream) {
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+        attr_err = cudaFuncSetAttribute(qmm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        C::SMEM_BYTES);
+    });
+    if (attr_err != cudaSuccess)
+        return fail(DFLASH_ERR_CUDA, "cudaFuncSetAttribute(qmm): %s", cudaGetErrorString(attr_err));
+
+    CUtensorMap tm_w, tm_x, tm_s, tm_b;
+    int st;
+    const uint64_t words = (uint64_t)s.K * s.bits / 32;
+    st = encode_tensor_map_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, words, (uint64_t)s.N,
+                              words * 4, kRowBytes / 4, kRows, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = encode_tensor_map_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)s.K, (uint64_t)s.M,
+                              (uint64_t)s.K * 2, 64, C::XROWS, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    const uint64_t gt = (uint64_t)(s.K / s.group);
+    if constexpr (C::STMA) {
+        st = encode_tensor_map_2d(&tm_s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, scales, gt, (uint64_t)s.N, gt * 2,
+                                  8, kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+        st = encode_tensor_map_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, biases, gt, (uint64_t)s.N, gt * 2,
+                                  8, kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+    } else {
+        tm_s = tm_w;
+        tm_b = tm_w;
+    }
+
+    int dev = 0;
+    DFLASH_CUDA_TRY(cudaGetDevice(&dev));
+    Params p;
+    p.y = y;
+    p.scales = scales;
+    p.biases = biases;
+    p.counters = reinterpret_cast<int*>(ws);
+    p.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + counters_bytes(s.N));
+    p.M = s.M;
+    p.N = s.N;
+    p.K = s.K;
+    p.GT = s.K / s.group;
+    p.tiles = n_tiles(s.N);
+    p.U = (long long)p.tiles * p.GT;
+    long long G = sm_count(dev);
+    if (G > kMaxCtas) G = kMaxCtas;
+    if (G > p.U) G = p.U;
+    p.G = (int)G;
+    p.y_vec = (s.N % 8 == 0) && aligned16(y);
+    qmm_kernel<C><<<p.G, kThreads, C::SMEM_BYTES, stream>>>(tm_w, tm_x, tm_s, tm_b, p);
+    DFLASH_CUDA_TRY(cudaGetLastError());
+    return DFLASH_OK;
+}
+
+template <int BITS, int GROUP, int NT>
+int dispatch_stma(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash_bf16* sc,
+                  const dflash_bf16* bi, dflash_bf16* y, void* ws, cudaStream_t st) {
+    const bool stma = ((s.K / s.group) % 8 == 0) && aligned16(sc) && aligned16(bi);
+    if (stma) return launch<Cfg<BITS, GROUP, NT, true>>(s, x, w, sc, bi, y, ws, st);
+    return launch<Cfg<BITS, GROUP, NT, false>>(s, x, w, sc, bi, y, ws, st);
+}
+
+template <int BITS, int GROUP>
+int dispatch_nt(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash_bf16* sc,
+                const dflash_bf16* bi, dflash_bf16* y, void* ws, cudaStream_t st) {
+    if (s.M <= 8) return dispatch_stma<BITS, GROUP, 1>(s, x, w, sc, bi, y, ws, st);
+    return dispatch_stma<BITS, GROUP, 2>(s, x, w, sc, bi, y, ws, st);
+}
+
+template <int BITS>
+int dispatch_group(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash_bf16* sc,
+                   const dflash_bf16* bi, dflash_bf16* y, void* ws, cudaStream_t st) {
+    switch (s.group) {
+        case 32: return dispatch_nt<BITS, 32>(s, x, w, sc, bi, y, ws, st);
+        case 64: return dispatch_nt<BITS, 64>(s, x, w, sc, bi, y, ws, st);
+        case 128: return dispatch_nt<BITS, 128>(s, x, w, sc, bi, y, ws, st);
+    }
+    return fail(DFLASH_ERR_UNSUPPORTED, "group_size %d not in {32, 64, 128}", s.group);
+}
+
+int validate(const Shape& s) {
+    if (s.bits != 4 && s.bits != 8) return fail(DFLASH_ERR_UNSUPPORTED, "bits %d not in {4, 8}", s.bits);
+    if (s.group != 32 && s.group != 64 && s.group != 128)
+        return fail(DFLASH_ERR_UNSUPPORTED, "group_size %d not in {32, 64, 128}", s.group);
+    if (s.M < 1 || s.M > 16) return fail(DFLASH_ERR_UNSUPPORTED, "M=%d outside 1..16", s.M);
+    if (s.N < 1 || s.K < 1) return fail(DFLASH_ERR_INVALID_ARGUMENT, "N=%d K=%d must be positive", s.N, s.K);
+    if (s.K % s.group != 0)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "K=%d is not a multiple of group_size %d", s.K, s.group);
+    return DFLASH_OK;
+}
+
+}  // namespace qmm
+}  // namespace dflash
+
+extern "C" size_t dflash_qmm_workspace_bytes(int M, int N, int K, int group_size, int bits) {
+    (void)M;
+    (void)K;
+    (void)group_size;
+    (void)bits;
+    if (N < 1) return 0;
+    return dflash::qmm::counters_bytes(N) + dflash::qmm::partials_bytes();
+}
+
+extern "C" int dflash_qmm_supported(int N, int K, int group_size, int bits) {
+    if ((bits != 4 && bits != 8) || (group_size != 32 && group_size != 64 && group_size != 128)) return 0;
+    if (N < 1 || K < 1 || K % group_size != 0) return 0;
+    return 1;
+}
+
+extern "C" int dflash_qmm(const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scales,
+                          const dflash_bf16* biases, dflash_bf16* y, int M, int N, int K, int group_size,
+                          int bits, void* workspace, size_t workspace_bytes, dflash_stream_t stream) {
+    using namespace dflash;
+    qmm::Shape s{M, N, K, group_size, bits};
+    if (int st = qmm::validate(s)) return st;
+    if (!x || !w || !scales || !biases || !y)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_qmm: null tensor pointer");
+    if (!aligned16(x) || !aligned16(w))
+        return fail(DFLASH_ERR_MISALIGNED, "dflash_qmm: x and w must be 16-byte aligned");
+    if (!workspace || !aligned16(workspace) || workspace_bytes < dflash_qmm_workspace_bytes(M, N, K, group_size, bits))
+        return fail(DFLASH_ERR_WORKSPACE, "dflash_qmm: workspace of %zu bytes required (got %zu)",
+                    dflash_qmm_workspace_bytes(M, N, K, group_size, bits), workspace_bytes);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (bits == 4) return qmm::dispatch_group<4>(s, x, w, scales, biases, y, workspace, st);
+    return qmm::dispatch_group<8>(s, x, w, scales, biases, y, workspace, st);
+}

@@ -1,0 +1,357 @@
+"""Python binding of libdflashcuda.so (ctypes over the C ABI in include/dflash_cuda.h).
+
+Torch is used here only as device-memory and stream plumbing: tensors are handed to the
+library as raw device pointers together with the current CUDA stream.  Every compute
+call goes to the CUDA library; there is no CPU path.  If the shared library is missing
+the import fails loudly.
+
+Reference interface mirrored (random1st/dflash-swift):
+  * ``SmallMQuantizedMatmul`` (Sources/DFlashKit/SmallMQuantizedMatmul.swift:27-225):
+    ``apply``, ``is_eligible``, ``tiles``, row-count constants.
+  * ``SmallMQuantizedLinear`` (:234-293): a quantized linear layer whose call routes
+    through the kernel, sharing (never copying) the layer's packed arrays.
+  * ``enable_small_m_quantized_matmul`` (:304-317): swaps every eligible layer of a
+    module tree and returns how many were swapped (idempotent).
+  * The gated-delta capture/replay used by rollbackGatedDeltaRound/Tree
+    (DFlashSpeculativeGenerator.swift:450-461): ``gdn_step``, ``gdn_replay``,
+    ``gdn_conv_rollback``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Optional, Sequence
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get("DFLASH_CUDA_LIB", HERE / "libdflashcuda.so"))
+
+DFLASH_OK = 0
+DFLASH_ERR_INVALID_ARGUMENT = 1
+DFLASH_ERR_UNSUPPORTED = 2
+DFLASH_ERR_MISALIGNED = 3
+DFLASH_ERR_CUDA = 4
+DFLASH_ERR_NCCL = 5
+DFLASH_ERR_TIMEOUT = 6
+DFLASH_ERR_WORKSPACE = 7
+
+DEVERR_QMM_PIPELINE = 0x1
+DEVERR_QMM_REDUCE = 0x2
+DEVERR_ALLREDUCE = 0x4
+DEVERR_TEST_WAIT = 0x80000000
+
+# Every symbol the header declares; tests check the library exports all of them.
+EXPORTED = (
+    "dflash_version", "dflash_last_error", "dflash_status_string", "dflash_device_error",
+    "dflash_test_bounded_wait", "dflash_qmm_workspace_bytes", "dflash_qmm", "dflash_qmm_supported",
+    "dflash_gdn_step", "dflash_gdn_replay", "dflash_gdn_conv_rollback",
+)
+
+
+class DFlashError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"status {status}: {message}")
+        self.status = status
+
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_sz = ctypes.c_size_t
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"libdflashcuda.so not found at {LIB_PATH}; build it with `python -c "
+            f"'import __graft_entry__ as g; g.build()'` (no CPU fallback exists)")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    sig = {
+        "dflash_version": ([], _i),
+        "dflash_last_error": ([], ctypes.c_char_p),
+        "dflash_status_string": ([_i], ctypes.c_char_p),
+        "dflash_device_error": ([ctypes.POINTER(ctypes.c_uint32), _vp], _i),
+        "dflash_test_bounded_wait": ([ctypes.c_uint64, _vp], _i),
+        "dflash_qmm_workspace_bytes": ([_i, _i, _i, _i, _i], _sz),
+        "dflash_qmm": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp], _i),
+        "dflash_qmm_supported": ([_i, _i, _i, _i], _i),
+        "dflash_gdn_step": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, ctypes.c_float, _vp], _i),
+        "dflash_gdn_replay": ([_vp, _vp, _vp, _vp, _vp, _vp, ctypes.POINTER(ctypes.c_int32), _i, _i, _i, _i,
+                               _i, _i, _vp], _i),
+        "dflash_gdn_conv_rollback": ([_vp, _vp, _vp, ctypes.POINTER(ctypes.c_int32), _i, _i, _i, _i, _i, _vp],
+                                     _i),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    return lib
+
+
+lib = _load()
+
+
+def last_error() -> str:
+    return lib.dflash_last_error().decode()
+
+
+def check(status: int) -> None:
+    if status != DFLASH_OK:
+        raise DFlashError(status, last_error())
+
+
+def _stream(stream=None) -> int:
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return stream.cuda_stream
+
+
+def _ptr(t) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def device_error(stream=None) -> int:
+    """Reads and clears the device error word (synchronises the stream)."""
+    bits = ctypes.c_uint32(0)
+    check(lib.dflash_device_error(ctypes.byref(bits), _stream(stream)))
+    return int(bits.value)
+
+
+def test_bounded_wait(limit_ns: int, stream=None) -> None:
+    check(lib.dflash_test_bounded_wait(int(limit_ns), _stream(stream)))
+
+
+# ----------------------------------------------------------------------------- qmm
+
+def qmm_workspace_bytes(M: int, N: int, K: int, group_size: int, bits: int) -> int:
+    return int(lib.dflash_qmm_workspace_bytes(M, N, K, group_size, bits))
+
+
+class Workspace:
+    """Zero-initialised device workspace for dflash_qmm (one per stream)."""
+
+    def __init__(self, nbytes: int, device=None):
+        import torch
+        self.nbytes = int(nbytes)
+        self.buf = torch.zeros(max(self.nbytes, 16), dtype=torch.uint8, device=device or "cuda")
+
+    def ensure(self, nbytes: int) -> "Workspace":
+        if nbytes > self.nbytes:
+            self.__init__(nbytes, self.buf.device)
+        return self
+
+
+_workspaces: dict = {}
+
+
+def default_workspace(nbytes: int, device) -> Workspace:
+    import torch
+    key = (str(device), torch.cuda.current_stream(device).cuda_stream)
+    ws = _workspaces.get(key)
+    if ws is None:
+        ws = _workspaces[key] = Workspace(nbytes, device)
+    return ws.ensure(nbytes)
+
+
+def qmm(x, w, scales, biases, group_size: int, bits: int, out=None, workspace: Optional[Workspace] = None,
+        stream=None):
+    """y = x . dequant(w)^T through dflash_qmm.  x: bf16 [M, K] (M <= 16) on the GPU."""
+    import torch
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    need = qmm_workspace_bytes(M, N, K, group_size, bits)
+    ws = workspace.ensure(need) if workspace is not None else default_workspace(need, x.device)
+    check(lib.dflash_qmm(_ptr(x), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out), M, N, K, group_size, bits,
+                         ws.buf.data_ptr(), ws.nbytes, _stream(stream)))
+    return out
+
+
+class SmallMQuantizedMatmul:
+    """Constants and dispatch of the small-M kernel (SmallMQuantizedMatmul.swift:27-225).
+
+    The reference kernel only wins from 6 rows (below that MLX's GEMV is at roofline,
+    :29-32) and stops at 16 (two 8-row MMA tiles, :36-37).  This library has no stock
+    op to defer to, so its kernel covers every row count 1..16; wider inputs are cut
+    into 16-row passes by SmallMQuantizedLinear.
+    """
+
+    minimum_rows = 1
+    maximum_rows = 16
+    rows_per_tile = 8
+    supported_bits = (4, 8)
+    supported_group_sizes = (32, 64, 128)
+
+    @staticmethod
+    def is_eligible(layer: "QuantizedLinear") -> bool:
+        """Static half of the test (SmallMQuantizedMatmul.swift:193-201): affine mode
+        with biases, a bit width and group size the kernel covers, and a shape it can
+        tile."""
+        if getattr(layer, "mode", "affine") != "affine" or layer.biases is None:
+            return False
+        out_features, in_features = layer.shape
+        return bool(lib.dflash_qmm_supported(out_features, in_features, layer.group_size, layer.bits))
+
+    @staticmethod
+    def tiles(rows: int) -> int:
+        """MMA n-tiles needed for `rows` (SmallMQuantizedMatmul.swift:205-207)."""
+        return 1 if rows <= SmallMQuantizedMatmul.rows_per_tile else 2
+
+    @staticmethod
+    def apply(x, weight, scales, biases, rows: int, output_features: int, input_features: int, bits: int,
+              group_size: int = 64):
+        """x[rows, K] . deq(weight)^T -> [rows, N] bf16 (SmallMQuantizedMatmul.swift:210-224)."""
+        assert x.shape[0] == rows and x.shape[1] == input_features and weight.shape[0] == output_features
+        return qmm(x, weight, scales, biases, group_size, bits)
+
+
+class QuantizedLinear:
+    """MLX-layout affine-quantized linear layer: packed uint32 weight [N, K*bits/32],
+    bf16 scales and biases [N, K/group_size], optional bf16 bias [N]."""
+
+    def __init__(self, weight, scales, biases, group_size: int, bits: int, bias=None, mode: str = "affine"):
+        self.weight, self.scales, self.biases, self.bias = weight, scales, biases, bias
+        self.group_size, self.bits, self.mode = int(group_size), int(bits), mode
+        self.frozen = False
+
+    @property
+    def shape(self):
+        return (self.weight.shape[0], self.weight.shape[1] * 32 // self.bits)
+
+    def freeze(self):
+        self.frozen = True
+        return self
+
+    def __call__(self, x):
+        raise NotImplementedError("the stock MLX quantizedMatmul is not part of this library; "
+                                  "wrap the layer in SmallMQuantizedLinear")
+
+
+class SmallMQuantizedLinear(QuantizedLinear):
+    """QuantizedLinear whose forward runs on dflash_qmm (SmallMQuantizedMatmul.swift:234-293).
+
+    Shares the wrapped layer's arrays (no copy) and stays frozen like the layer it
+    replaces (:243-252).  The call flattens leading dimensions to rows (:255-256,
+    :270), runs the kernel in passes of at most 16 rows (the kernel reads x rows in
+    place, so the reference's zero-padding concat of :271-281 is not needed), reshapes
+    back and adds the optional bias (:287-290).  Only bf16 input is accepted: the
+    kernel's fragments and output are bf16 (:257-263); other dtypes raise TypeError
+    rather than silently change the layer's output dtype.
+    """
+
+    def __init__(self, other: QuantizedLinear):
+        super().__init__(other.weight, other.scales, other.biases, other.group_size, other.bits,
+                         bias=other.bias, mode=other.mode)
+        self.kernel_eligible = SmallMQuantizedMatmul.is_eligible(other)
+        self.freeze()
+
+    def __call__(self, x, stream=None):
+        import torch
+        if not self.kernel_eligible:
+            raise DFlashError(DFLASH_ERR_UNSUPPORTED,
+                              f"layer {self.shape} bits={self.bits} group={self.group_size} is not covered")
+        if x.dtype != torch.bfloat16:
+            raise TypeError(f"SmallMQuantizedLinear takes bfloat16 input, got {x.dtype}")
+        lead = x.shape[:-1]
+        K = x.shape[-1]
+        N = self.weight.shape[0]
+        flat = x.reshape(-1, K)
+        if not flat.is_contiguous():
+            flat = flat.contiguous()
+        rows = flat.shape[0]
+        y = torch.empty((rows, N), dtype=torch.bfloat16, device=x.device)
+        step = SmallMQuantizedMatmul.maximum_rows
+        for r0 in range(0, rows, step):
+            r1 = min(rows, r0 + step)
+            qmm(flat[r0:r1], self.weight, self.scales, self.biases, self.group_size, self.bits, out=y[r0:r1],
+                stream=stream)
+        y = y.reshape(*lead, N)
+        if self.bias is not None:
+            y = y + self.bias
+        return y
+
+
+def enable_small_m_quantized_matmul(model) -> int:
+    """Swaps every eligible QuantizedLinear in `model` for a SmallMQuantizedLinear
+    (SmallMQuantizedMatmul.swift:304-317).  `model` is any object tree whose
+    attributes (or list/dict items) hold layers.  Returns the number swapped; a second
+    call returns 0 because wrapped layers are never wrapped again."""
+    count = 0
+
+    def visit(obj, seen):
+        nonlocal count
+        if id(obj) in seen:
+            return
+        seen.add(id(obj))
+        items = []
+        if isinstance(obj, dict):
+            items = list(obj.items())
+        elif isinstance(obj, (list, tuple)):
+            items = list(enumerate(obj))
+        elif hasattr(obj, "__dict__"):
+            items = list(vars(obj).items())
+        for key, child in items:
+            if isinstance(child, QuantizedLinear):
+                if isinstance(child, SmallMQuantizedLinear) or not SmallMQuantizedMatmul.is_eligible(child):
+                    continue
+                wrapped = SmallMQuantizedLinear(child)
+                if isinstance(obj, dict):
+                    obj[key] = wrapped
+                elif isinstance(obj, list):
+                    obj[key] = wrapped
+                elif isinstance(obj, tuple):
+                    continue
+                else:
+                    setattr(obj, key, wrapped)
+                count += 1
+            elif isinstance(child, (dict, list, tuple)) or (hasattr(child, "__dict__") and not _is_tensor(child)):
+                visit(child, seen)
+
+    visit(model, set())
+    return count
+
+
+def _is_tensor(obj) -> bool:
+    return type(obj).__module__.startswith("torch")
+
+
+# ----------------------------------------------------------------------------- gated delta
+
+def gdn_step(state_in, state_out, q, k, v, alpha, beta, out=None, q_scale: float = 1.0, stream=None):
+    """One layer's recurrence over T positions (the verify forward; its inputs are the capture)."""
+    T, H, dk = k.shape
+    dv = v.shape[-1]
+    check(lib.dflash_gdn_step(_ptr(state_in), _ptr(state_out), _ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(beta),
+                              _ptr(out), T, H, dk, dv, float(q_scale), _stream(stream)))
+    return state_out
+
+
+def _rows_arg(rows: Optional[Sequence[int]]):
+    if rows is None:
+        return None
+    arr = (ctypes.c_int32 * len(rows))(*[int(r) for r in rows])
+    return arr
+
+
+def gdn_replay(snapshot, state_out, k, v, alpha, beta, keep: int, rows: Optional[Sequence[int]] = None,
+               stream=None):
+    """Rollback replay for all layers at once.  k: [L, width, H, dk]; state: [L, H, dv, dk]."""
+    L, width, H, dk = k.shape
+    dv = v.shape[-1]
+    if rows is not None and len(rows) < keep:
+        raise ValueError("rows shorter than keep")
+    check(lib.dflash_gdn_replay(_ptr(snapshot), _ptr(state_out), _ptr(k), _ptr(v), _ptr(alpha), _ptr(beta),
+                                _rows_arg(rows), int(keep), width, L, H, dk, dv, _stream(stream)))
+    return state_out
+
+
+def gdn_conv_rollback(window, window_out, conv_in, keep: int, rows: Optional[Sequence[int]] = None, stream=None):
+    """Conv-window rebuild.  window: [L, kc1, C]; conv_in: [L, width, C]."""
+    L, kc1, C = window.shape
+    width = conv_in.shape[1]
+    if rows is not None and len(rows) < keep:
+        raise ValueError("rows shorter than keep")
+    check(lib.dflash_gdn_conv_rollback(_ptr(window), _ptr(window_out), _ptr(conv_in), _rows_arg(rows), int(keep),
+                                       width, L, kc1, C, _stream(stream)))
+    return window_out

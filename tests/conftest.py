@@ -1,0 +1,57 @@
+"""Test configuration.
+
+Marker `gpu`: needs a CUDA device (B200).  Everything else runs on CPU:
+    python -m pytest tests -m "not gpu"      # oracle, golden vectors, C-ABI surface, host logic, gloo ranks
+    python -m pytest tests -m gpu            # parity of the CUDA kernels against the oracle
+"""
+from __future__ import annotations
+
+import importlib.util
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+PKG = ROOT / "dflash-swift_b200"
+for p in (str(ROOT), str(ROOT / "oracle"), str(PKG)):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (runs on the B200 box)")
+
+
+def _ensure_built():
+    so = PKG / "libdflashcuda.so"
+    oracle_so = ROOT / "oracle" / "liboracle.so"
+    if not so.exists() or not oracle_so.exists():
+        spec = importlib.util.spec_from_file_location("graft_entry", ROOT / "__graft_entry__.py")
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        mod.build()
+
+
+_ensure_built()
+
+
+@pytest.fixture(scope="session")
+def dc():
+    import dflashcuda
+    return dflashcuda
+
+
+@pytest.fixture(scope="session")
+def O():
+    import oracle
+    return oracle
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.cuda.set_device(0)
+    return torch.device("cuda:0")

@@ -1,0 +1,143 @@
+"""C-ABI surface tests that need no GPU: the library loads, exports every symbol the
+header declares, and rejects bad arguments with the documented statuses before any
+CUDA call is made."""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "dflash_cuda.h"
+LIB = ROOT / "dflash-swift_b200" / "libdflashcuda.so"
+
+FAKE = 0x10000  # a 16-byte aligned non-null pointer value; never dereferenced by these calls
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(dflash_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_expected_surface(dc):
+    names = declared_functions()
+    assert set(names) == set(dc.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol():
+    out = subprocess.run(["nm", "-D", "--defined-only", str(LIB)], capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (dflash_[a-z0-9_]+)\b", out))
+    missing = [n for n in declared_functions() if n not in exported]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_version_and_status_strings(dc):
+    text = HEADER.read_text()
+    assert dc.lib.dflash_version() == int(re.search(r"#define DFLASH_VERSION (\d+)", text).group(1))
+    assert dc.lib.dflash_status_string(0) == b"ok"
+    for st in range(1, 8):
+        assert dc.lib.dflash_status_string(st) not in (b"ok", b"unknown status")
+    assert dc.lib.dflash_status_string(99) == b"unknown status"
+
+
+def _qmm(dc, M=8, N=4096, K=1024, group=64, bits=4, x=FAKE, w=FAKE, s=FAKE, b=FAKE, y=FAKE, ws=FAKE,
+         ws_bytes=None):
+    if ws_bytes is None:
+        ws_bytes = dc.qmm_workspace_bytes(M, N, K, group, bits)
+    return dc.lib.dflash_qmm(x, w, s, b, y, M, N, K, group, bits, ws, ws_bytes, None)
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(M=17), 2), (dict(M=0), 2), (dict(bits=3), 2), (dict(bits=2), 2), (dict(group=96), 2),
+    (dict(group=16), 2), (dict(K=1000), 1), (dict(N=0), 1), (dict(K=0), 1), (dict(x=0), 1), (dict(w=0), 1),
+    (dict(s=0), 1), (dict(b=0), 1), (dict(y=0), 1), (dict(x=FAKE + 2), 3), (dict(w=FAKE + 4), 3),
+    (dict(ws=0), 7), (dict(ws_bytes=16), 7), (dict(ws=FAKE + 8), 7),
+])
+def test_qmm_argument_errors(dc, kw, status):
+    assert _qmm(dc, **kw) == status
+    assert dc.last_error()
+
+
+def test_qmm_supported_table(dc):
+    f = dc.lib.dflash_qmm_supported
+    for bits in (4, 8):
+        for g in (32, 64, 128):
+            assert f(17408, 5120, g, bits) == 1
+    assert f(4096, 1024, 64, 3) == 0
+    assert f(4096, 1024, 96, 4) == 0
+    assert f(4096, 1000, 64, 4) == 0
+    assert f(0, 1024, 64, 4) == 0
+    # wider than the reference's gate (N >= 4096, K % 512 == 0, group 64 only)
+    assert f(2048, 1088, 64, 4) == 1
+    assert f(17, 64, 32, 8) == 1
+
+
+def test_workspace_size_is_shape_bounded(dc):
+    a = dc.qmm_workspace_bytes(8, 17408, 5120, 64, 4)
+    assert a == dc.qmm_workspace_bytes(16, 17408, 17408, 128, 8)  # does not depend on M, K, format
+    assert a > 0 and a < 16 << 20
+    assert dc.qmm_workspace_bytes(8, 248320, 5120, 64, 4) > a     # counters grow with N
+    assert dc.qmm_workspace_bytes(8, 0, 5120, 64, 4) == 0
+
+
+def _gdn_step(dc, T=8, H=4, dk=128, dv=128, si=FAKE, so=FAKE * 2, q=FAKE, k=FAKE, v=FAKE, a=FAKE, b=FAKE, out=0):
+    return dc.lib.dflash_gdn_step(si, so, q, k, v, a, b, out, T, H, dk, dv, 1.0, None)
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(T=0), 2), (dict(T=65), 2), (dict(dk=96), 2), (dict(dk=256), 2), (dict(dv=48), 2), (dict(dv=0), 2),
+    (dict(H=0), 1), (dict(si=0), 1), (dict(k=0), 1), (dict(so=FAKE), 1), (dict(si=FAKE + 4), 3),
+    (dict(out=FAKE, q=0), 1),
+])
+def test_gdn_step_argument_errors(dc, kw, status):
+    assert _gdn_step(dc, **kw) == status
+
+
+def test_gdn_replay_argument_errors(dc):
+    r = dc.lib.dflash_gdn_replay
+    ok_args = (FAKE, FAKE * 2, FAKE, FAKE, FAKE, FAKE)
+    assert r(*ok_args, None, 0, 8, 2, 4, 128, 128, None) == 1          # keep 0
+    assert r(*ok_args, None, 9, 8, 2, 4, 128, 128, None) == 1          # keep > width
+    assert r(*ok_args, None, 3, 65, 2, 4, 128, 128, None) == 1         # width > 64
+    assert r(*ok_args, None, 3, 8, 0, 4, 128, 128, None) == 1          # layers 0
+    rows = (ctypes.c_int32 * 3)(0, 1, 8)                               # row outside [0, width)
+    assert r(*ok_args, rows, 3, 8, 2, 4, 128, 128, None) == 1
+    assert "rows[2]=8" in dc.last_error()
+    assert r(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, None, 3, 8, 2, 4, 128, 128, None) == 1  # aliasing
+
+
+def test_conv_rollback_argument_errors(dc):
+    c = dc.lib.dflash_gdn_conv_rollback
+    assert c(FAKE, FAKE, FAKE, None, 3, 8, 2, 3, 64, None) == 1        # aliasing
+    assert c(FAKE, FAKE * 2, FAKE, None, 0, 8, 2, 3, 64, None) == 1    # keep 0
+    assert c(FAKE, FAKE * 2, FAKE, None, 3, 8, 2, 0, 64, None) == 1    # kc1 0
+    rows = (ctypes.c_int32 * 2)(0, -1)
+    assert c(FAKE, FAKE * 2, FAKE, rows, 2, 8, 2, 3, 64, None) == 1
+
+
+def test_bounded_wait_hook_argument_errors(dc):
+    assert dc.lib.dflash_test_bounded_wait(0, None) == 1
+    assert dc.lib.dflash_test_bounded_wait(10 ** 12, None) == 1
+
+
+def test_last_error_is_thread_local(dc):
+    import threading
+    assert _qmm(dc, M=17) == 2
+    main_msg = dc.last_error()
+    seen = {}
+
+    def worker():
+        seen["before"] = dc.last_error()
+        _qmm(dc, bits=3)
+        seen["after"] = dc.last_error()
+
+    t = threading.Thread(target=worker)
+    t.start()
+    t.join()
+    assert seen["before"] == ""
+    assert "bits" in seen["after"]
+    assert dc.last_error() == main_msg
