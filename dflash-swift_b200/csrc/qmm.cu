@@ -525,8 +525,10 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
     p.y = y;
     p.scales = scales;
     p.biases = biases;
-    p.counters = reinterpret_cast<int*>(ws);
-    p.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + counters_bytes(s.N));
+    // Layout independent of the shape, so one workspace serves calls of any N:
+    // [fp32 partials, fixed size][per-tile counters, tile t at the same offset always].
+    p.partials = reinterpret_cast<float*>(ws);
+    p.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ws) + partials_bytes());
     p.M = s.M;
     p.N = s.N;
     p.K = s.K;

@@ -171,8 +171,24 @@ def test_workspace_left_zeroed_and_no_device_error(dc, O, cuda):
     ws = dc.Workspace(dc.qmm_workspace_bytes(8, 17408, 5120, 64, 4), cuda)
     run(dc, cuda, x, wq, s, b, 64, 4, workspace=ws)
     n_tiles = (17408 + 255) // 256
-    assert int(ws.buf[: n_tiles * 4].view(torch.int32).abs().sum().item()) == 0
+    counters = ws.buf[ws.nbytes - ((n_tiles * 4 + 255) // 256) * 256:ws.nbytes]
+    assert int(counters.view(torch.int32).abs().sum().item()) == 0
     assert dc.device_error() == 0
+
+
+def test_workspace_shared_across_shapes(dc, O, cuda):
+    """One workspace serves calls of different N in any order (the tile counters sit at
+    fixed offsets and are left zeroed by every call)."""
+    ws = dc.Workspace(dc.qmm_workspace_bytes(16, 17408, 5120, 64, 4), cuda)
+    big = big_case(O, 12, 17408, 5120, 64, 4)
+    small = O.make_qmm_case(12, 1000, 1024, 64, 4)
+    rows = np.arange(0, 17408, 101)
+    for case in (big, small, big, small, big):
+        x, wq, s, b = case
+        N = wq.shape[0]
+        y = yf(run(dc, cuda, x, wq, s, b, 64, 4, workspace=ws))
+        r = rows if N == 17408 else np.arange(N)
+        assert O.closeness(y[:, r], O.qmm_f64(x, wq[r], s[r], b[r], 64, 4)) <= TIGHT
 
 
 def test_small_m_quantized_linear_with_bias_and_wide_input(dc, O, cuda):
