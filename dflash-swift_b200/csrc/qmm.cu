@@ -105,16 +105,72 @@ constexpr uint32_t kMagic = 0x43004300u;   // bf16x2 (128.0, 128.0)
 constexpr uint32_t kNib = 0x000F000Fu;
 constexpr uint32_t kOnes = 0x3F803F80u;    // bf16x2 (1.0, 1.0)
 
+// ------------------------------------------------------------------ fragment layout
+//
+// Fragment row g of 16-row block i of a warp's 32-feature slice maps to feature row
+//     rb + 16 i + 2 sigma(g) + h        (h = 0: fragment rows 0..7, h = 1: rows 8..15)
+// sigma spreads the 128-byte swizzle keys (row & 7) of the rows a half-warp (LDS.64)
+// or quarter-warp (LDS.128) reads, so the weight reads of a warp hit distinct banks.
+__device__ __forceinline__ int sigma(int g) { return (g & 4) | ((g & 1) << 1) | ((g >> 1) & 1); }
+
+// Per-thread offsets of the fragment layout, computed once per CTA.
 template <class C>
-__device__ __forceinline__ void load_words(uint32_t (&dst)[C::PW], uint32_t addr) {
-    if constexpr (C::PB == 4) {
+struct LaneLayout {
+    int row[2];                                   // feature row of (i = 0, h); i = 1 adds 16
+    uint32_t wofs[2];                             // stage-relative byte offset of group 0, piece 0
+    uint32_t xofs[C::NT][C::PIECES][C::PXCH];     // stage-relative x offset (from the x region), group 0
+};
+
+template <class C>
+__device__ __forceinline__ LaneLayout<C> lane_layout(int rb, int g, int tq) {
+    LaneLayout<C> L;
+    const uint32_t T = tq * C::TB;  // this thread's byte slice of a row's group
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int r = rb + 2 * sigma(g) + h;
+        L.row[h] = r;
+        L.wofs[h] = r * kRowBytes + ((((T >> 4) ^ (r & 7))) << 4) + (T & 15);
+    }
+#pragma unroll
+    for (int j = 0; j < C::NT; ++j) {
+        const int m = 8 * j + g;
+#pragma unroll
+        for (int pc = 0; pc < C::PIECES; ++pc)
+#pragma unroll
+            for (int c = 0; c < C::PXCH; ++c) {
+                const int kt = tq * C::VPT + pc * C::PV + 8 * c;  // k within group 0 of the stage
+                L.xofs[j][pc][c] = (kt >> 6) * C::XBOX_BYTES + m * 128 + ((((kt & 63) >> 3) ^ (m & 7)) << 4);
+            }
+    }
+    return L;
+}
+
+// Compile-time parts of the weight address of (group gl, piece pc): XOR into the
+// swizzled chunk bits, plus an in-chunk byte offset.
+template <class C> __device__ __forceinline__ constexpr uint32_t w_xor(int gl, int pc) {
+    return (uint32_t)(gl * C::GB + ((pc * C::PB) & ~15));
+}
+template <class C> __device__ __forceinline__ constexpr uint32_t w_add(int pc) {
+    return (uint32_t)((pc * C::PB) & 15);
+}
+// x address of group gl: XOR of the chunk bits (groups of 32) and a whole-box offset.
+template <class C> __device__ __forceinline__ constexpr uint32_t x_xor(int gl) {
+    return (uint32_t)(((gl * C::GROUP) & 63) << 1);
+}
+template <class C> __device__ __forceinline__ constexpr uint32_t x_add(int gl) {
+    return (uint32_t)(((gl * C::GROUP) >> 6) * C::XBOX_BYTES);
+}
+
+template <int PB>
+__device__ __forceinline__ void lds_words(uint32_t* dst, uint32_t addr) {
+    if constexpr (PB == 4) {
         dst[0] = lds32(addr);
-    } else if constexpr (C::PB == 8) {
-        uint2 v = lds64(addr);
+    } else if constexpr (PB == 8) {
+        const uint2 v = lds64(addr);
         dst[0] = v.x;
         dst[1] = v.y;
     } else {
-        uint4 v = lds128(addr);
+        const uint4 v = lds128(addr);
         dst[0] = v.x;
         dst[1] = v.y;
         dst[2] = v.z;
@@ -122,90 +178,98 @@ __device__ __forceinline__ void load_words(uint32_t (&dst)[C::PW], uint32_t addr
     }
 }
 
-// One quantization group of one stage for one consumer warp (32 rows x GROUP k).
+// D = A * B (accumulator starts at zero), m16n8k16 bf16 -> fp32.
+__device__ __forceinline__ void mma_bf16_16816_zero(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                    uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %10, %10, %10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+template <bool FIRST>
+__device__ __forceinline__ void mma_step(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    if constexpr (FIRST)
+        mma_bf16_16816_zero(d, a0, a1, a2, a3, b0, b1);
+    else
+        mma_bf16_16816(d, a0, a1, a2, a3, b0, b1);
+}
+
+// One quantization group (index gl within the stage) for one consumer warp:
+// 32 feature rows x GROUP k, all M rows.  wb[h] = stage base + wofs[h];
+// xb = x region base; sb[h] = scale-tile address of row[h] at this stage's group 0.
 template <class C>
-__device__ __forceinline__ void consume_group(uint32_t w_base, uint32_t x_base,
-                                              const dflash_bf16* s_tile, const dflash_bf16* b_tile,
-                                              int gl, int G, int rb, int g, int tq, int tile_row0,
+__device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const uint32_t (&wb)[2], uint32_t xb,
+                                              const uint32_t (&sb)[2], int gl, int G, int tile_row0,
                                               const Params& p, float (&acc)[2][C::NT][4]) {
     float tmp[2][C::NT][4];
     float xs[C::NT][4];
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int pc = 0; pc < C::PIECES; ++pc) {
+        // B fragments: this thread's slice of x for activation rows 8j + g.
+        uint32_t xf[C::NT][C::PXCH][4];
 #pragma unroll
         for (int j = 0; j < C::NT; ++j)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) tmp[i][j][e] = 0.f;
-#pragma unroll
-    for (int j = 0; j < C::NT; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) xs[j][e] = 0.f;
-
-#pragma unroll
-    for (int pc = 0; pc < C::PIECES; ++pc) {
-        // B fragments: this thread's slice of x for activation rows 8j + g.
-        uint32_t xb[C::NT][C::PXCH][4];
-#pragma unroll
-        for (int j = 0; j < C::NT; ++j) {
-            const int m = 8 * j + g;
-#pragma unroll
             for (int c = 0; c < C::PXCH; ++c) {
-                const int k = gl * C::GROUP + tq * C::VPT + pc * C::PV + 8 * c;  // stage-local
-                const int box = k >> 6, chunk = (k & 63) >> 3;
-                const uint4 r = lds128(x_base + box * C::XBOX_BYTES + m * 128 + ((chunk ^ (m & 7)) << 4));
+                const uint4 r = lds128(xb + ((L.xofs[j][pc][c] ^ x_xor<C>(gl)) + x_add<C>(gl)));
                 if constexpr (C::BITS == 4) {
-                    xb[j][c][0] = prmt(r.x, r.z, 0x5410);  // (x0, x4)
-                    xb[j][c][1] = prmt(r.x, r.z, 0x7632);  // (x1, x5)
-                    xb[j][c][2] = prmt(r.y, r.w, 0x5410);  // (x2, x6)
-                    xb[j][c][3] = prmt(r.y, r.w, 0x7632);  // (x3, x7)
+                    xf[j][c][0] = prmt(r.x, r.z, 0x5410);  // (x0, x4)
+                    xf[j][c][1] = prmt(r.x, r.z, 0x7632);  // (x1, x5)
+                    xf[j][c][2] = prmt(r.y, r.w, 0x5410);  // (x2, x6)
+                    xf[j][c][3] = prmt(r.y, r.w, 0x7632);  // (x3, x7)
                 } else {
-                    xb[j][c][0] = prmt(r.x, r.y, 0x5410);  // (x0, x2)
-                    xb[j][c][1] = prmt(r.x, r.y, 0x7632);  // (x1, x3)
-                    xb[j][c][2] = prmt(r.z, r.w, 0x5410);  // (x4, x6)
-                    xb[j][c][3] = prmt(r.z, r.w, 0x7632);  // (x5, x7)
+                    xf[j][c][0] = prmt(r.x, r.y, 0x5410);  // (x0, x2)
+                    xf[j][c][1] = prmt(r.x, r.y, 0x7632);  // (x1, x3)
+                    xf[j][c][2] = prmt(r.z, r.w, 0x5410);  // (x4, x6)
+                    xf[j][c][3] = prmt(r.z, r.w, 0x7632);  // (x5, x7)
                 }
             }
-        }
-        // A operand source: packed words of rows rb + 16i + 8h + g.
+        // A operand source: packed words of the 4 feature rows (i, h).
         uint32_t wv[2][2][C::PW];
 #pragma unroll
-        for (int i = 0; i < 2; ++i)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int r = rb + 16 * i + 8 * h + g;
-                const int off = gl * C::GB + tq * C::TB + pc * C::PB;
-                const uint32_t a = w_base + r * kRowBytes + (((off >> 4) ^ (r & 7)) << 4) + (off & 15);
-                load_words<C>(wv[i][h], a);
-            }
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t a = (wb[h] ^ w_xor<C>(gl, pc)) + w_add<C>(pc);
+            lds_words<C::PB>(wv[0][h], a);
+            lds_words<C::PB>(wv[1][h], a + 16 * kRowBytes);
+        }
 #pragma unroll
         for (int s = 0; s < C::PSTEPS; ++s) {
+            const bool first = (pc == 0 && s == 0);
             if constexpr (C::BITS == 4) {
                 const int w = s >> 1, q = (s & 1) * 2;
 #pragma unroll
                 for (int j = 0; j < C::NT; ++j) {
-                    const uint32_t b0 = xb[j][w][q], b1 = xb[j][w][q + 1];
-                    mma_bf16_16816(xs[j], kOnes, kOnes, kOnes, kOnes, b0, b1);
+                    const uint32_t b0 = xf[j][w][q], b1 = xf[j][w][q + 1];
+                    if (first) mma_step<true>(xs[j], kOnes, kOnes, kOnes, kOnes, b0, b1);
+                    else mma_step<false>(xs[j], kOnes, kOnes, kOnes, kOnes, b0, b1);
 #pragma unroll
                     for (int i = 0; i < 2; ++i) {
                         const uint32_t a0 = ((wv[i][0][w] >> (4 * q)) & kNib) | kMagic;
                         const uint32_t a1 = ((wv[i][1][w] >> (4 * q)) & kNib) | kMagic;
                         const uint32_t a2 = ((wv[i][0][w] >> (4 * q + 4)) & kNib) | kMagic;
                         const uint32_t a3 = ((wv[i][1][w] >> (4 * q + 4)) & kNib) | kMagic;
-                        mma_bf16_16816(tmp[i][j], a0, a1, a2, a3, b0, b1);
+                        if (first) mma_step<true>(tmp[i][j], a0, a1, a2, a3, b0, b1);
+                        else mma_step<false>(tmp[i][j], a0, a1, a2, a3, b0, b1);
                     }
                 }
             } else {
                 const int w = s, c = s >> 1, q = (s & 1) * 2;
 #pragma unroll
                 for (int j = 0; j < C::NT; ++j) {
-                    const uint32_t b0 = xb[j][c][q], b1 = xb[j][c][q + 1];
+                    const uint32_t b0 = xf[j][c][q], b1 = xf[j][c][q + 1];
                     const uint32_t h0 = bf16x2_times16(b0), h1 = bf16x2_times16(b1);
-                    mma_bf16_16816(xs[j], kOnes, kOnes, kOnes, kOnes, b0, b1);
+                    if (first) mma_step<true>(xs[j], kOnes, kOnes, kOnes, kOnes, b0, b1);
+                    else mma_step<false>(xs[j], kOnes, kOnes, kOnes, kOnes, b0, b1);
 #pragma unroll
                     for (int i = 0; i < 2; ++i) {
                         const uint32_t w0 = wv[i][0][w], w1 = wv[i][1][w];
-                        mma_bf16_16816(tmp[i][j], (w0 & kNib) | kMagic, (w1 & kNib) | kMagic,
-                                       ((w0 >> 8) & kNib) | kMagic, ((w1 >> 8) & kNib) | kMagic, b0, b1);
+                        const uint32_t l0 = (w0 & kNib) | kMagic, l1 = (w1 & kNib) | kMagic;
+                        const uint32_t l2 = ((w0 >> 8) & kNib) | kMagic, l3 = ((w1 >> 8) & kNib) | kMagic;
+                        if (first) mma_step<true>(tmp[i][j], l0, l1, l2, l3, b0, b1);
+                        else mma_step<false>(tmp[i][j], l0, l1, l2, l3, b0, b1);
                         mma_bf16_16816(tmp[i][j], ((w0 >> 4) & kNib) | kMagic, ((w1 >> 4) & kNib) | kMagic,
                                        ((w0 >> 12) & kNib) | kMagic, ((w1 >> 12) & kNib) | kMagic, h0, h1);
                     }
@@ -219,13 +283,13 @@ __device__ __forceinline__ void consume_group(uint32_t w_base, uint32_t x_base,
     for (int i = 0; i < 2; ++i)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const int r = rb + 16 * i + 8 * h + g;
             float s, b;
             if constexpr (C::STMA) {
-                s = bf16_bits_to_float(s_tile[r * 8 + (G & 7)]);
-                b = bf16_bits_to_float(b_tile[r * 8 + (G & 7)]);
+                const uint32_t a = sb[h] + i * 16 * 16 + 2 * gl;
+                s = bf16_bits_to_float(lds16(a));
+                b = bf16_bits_to_float(lds16(a + C::S_BYTES));
             } else {
-                const int n = tile_row0 + r;
+                const int n = tile_row0 + L.row[h] + 16 * i;
                 if (n < p.N) {
                     const size_t idx = (size_t)n * p.GT + G;
                     s = bf16_bits_to_float(__ldg(p.scales + idx));
@@ -242,6 +306,23 @@ __device__ __forceinline__ void consume_group(uint32_t w_base, uint32_t x_base,
                 for (int e = 0; e < 2; ++e)
                     acc[i][j][2 * h + e] = fmaf(s, tmp[i][j][2 * h + e], fmaf(bb, xs[j][2 * h + e], acc[i][j][2 * h + e]));
         }
+}
+
+// All groups of one stage.  CHECK: the stage is the first or last of a segment and
+// some of its groups fall outside [ga, gb).
+template <class C, bool CHECK>
+__device__ __forceinline__ void consume_stage(const LaneLayout<C>& L, uint32_t st, int sc, int ga, int gb,
+                                              int tile_row0, const Params& p, float (&acc)[2][C::NT][4]) {
+    const uint32_t wb[2] = {st + L.wofs[0], st + L.wofs[1]};
+    const uint32_t xb = st + C::W_BYTES;
+    const uint32_t s0 = st + C::W_BYTES + C::X_BYTES + 2 * ((sc * C::GPS) & 7);
+    const uint32_t sb[2] = {s0 + L.row[0] * 16, s0 + L.row[1] * 16};
+#pragma unroll
+    for (int gl = 0; gl < C::GPS; ++gl) {
+        const int G = sc * C::GPS + gl;
+        if (CHECK && (G < ga || G >= gb)) continue;
+        consume_group<C>(L, wb, xb, sb, gl, G, tile_row0, p, acc);
+    }
 }
 
 // Writes the fp32 tile in `red` ([NT*8][kRedPitch]) to y as bf16.
@@ -353,6 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int rs = warp % kRowSlices, par = warp / kRowSlices;
     const int g = lane >> 2, tq = lane & 3;
     const int rb = rs * 32;
+    const LaneLayout<C> L = lane_layout<C>(rb, g, tq);
     const int ctid = threadIdx.x;  // 0 .. kConsumerThreads-1
     int j = 0;
 
@@ -378,17 +460,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[slot], ph, abort_flag,
                                                                        DFLASH_DEVERR_QMM_PIPELINE));
             if (ok) {
-                const uint8_t* st = smem + slot * C::STAGE_BYTES;
-                const uint32_t w_base = smem_u32(st);
-                const uint32_t x_base = smem_u32(st + C::W_BYTES);
-                const dflash_bf16* s_tile = reinterpret_cast<const dflash_bf16*>(st + C::W_BYTES + C::X_BYTES);
-                const dflash_bf16* b_tile = s_tile + kRows * 8;
-#pragma unroll
-                for (int gl = 0; gl < C::GPS; ++gl) {
-                    const int G = sc * C::GPS + gl;
-                    if (G < ga || G >= gb) continue;
-                    consume_group<C>(w_base, x_base, s_tile, b_tile, gl, G, rb, g, tq, tile_row0, p, acc);
-                }
+                const uint32_t st = smem_u32(smem + slot * C::STAGE_BYTES);
+                if (sc * C::GPS >= ga && sc * C::GPS + C::GPS <= gb)
+                    consume_stage<C, false>(L, st, sc, ga, gb, tile_row0, p, acc);
+                else
+                    consume_stage<C, true>(L, st, sc, ga, gb, tile_row0, p, acc);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
@@ -405,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int jj = 0; jj < C::NT; ++jj)
 #pragma unroll
                         for (int e = 0; e < 2; ++e)
-                            red[(8 * jj + 2 * tq + e) * kRedPitch + rb + 16 * i + 8 * h + g] = acc[i][jj][2 * h + e];
+                            red[(8 * jj + 2 * tq + e) * kRedPitch + L.row[h] + 16 * i] = acc[i][jj][2 * h + e];
         }
         named_bar_sync(kBarConsumers, kConsumerThreads);
         if (par == 0) {
@@ -417,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int jj = 0; jj < C::NT; ++jj)
 #pragma unroll
                         for (int e = 0; e < 2; ++e)
-                            red[(8 * jj + 2 * tq + e) * kRedPitch + rb + 16 * i + 8 * h + g] += acc[i][jj][2 * h + e];
+                            red[(8 * jj + 2 * tq + e) * kRedPitch + L.row[h] + 16 * i] += acc[i][jj][2 * h + e];
         }
         named_bar_sync(kBarConsumers, kConsumerThreads);
 

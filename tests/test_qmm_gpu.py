@@ -225,7 +225,7 @@ def test_device_pointer_errors(dc, O, cuda):
     xd, wd, sd, bd = to_dev(x, cuda), to_dev(wq, cuda), to_dev(s, cuda), to_dev(b, cuda)
     flat = torch.zeros(wd.numel() + 4, dtype=torch.int32, device=cuda)
     with pytest.raises(dc.DFlashError) as e:
-        dc.qmm(xd, flat[1:].view_as(wd), sd, bd, 64, 4)
+        dc.qmm(xd, flat[1:1 + wd.numel()].view_as(wd), sd, bd, 64, 4)
     assert e.value.status == dc.DFLASH_ERR_MISALIGNED
     with pytest.raises(dc.DFlashError) as e:
         dc.qmm(torch.zeros(17, 512, dtype=torch.bfloat16, device=cuda), wd, sd, bd, 64, 4)
