@@ -2,29 +2,38 @@
 //
 // Replaces SmallMQuantizedMatmul.apply (Sources/DFlashKit/SmallMQuantizedMatmul.swift:
 // 210-224) and the stock quantizedMatmul it stands in for.  The work is bound by the
-// packed weight stream (M <= 16 rows against N*K quantized weights), so the kernel is
-// built around moving those bytes from HBM exactly once at full bandwidth:
+// packed weight stream (M <= 16 rows against N*K quantized weights), so everything is
+// arranged to move those bytes from HBM exactly once at full bandwidth:
 //
+//  * Two kernels per call, chained with programmatic dependent launch (PDL).  A tiny
+//    prep kernel writes x, permuted into MMA fragment order, and the fp32 group sums
+//    of x into the workspace.  The main kernel starts streaming weights, scales and
+//    biases before its grid dependency resolves (they are never written by the
+//    preceding kernels), so consecutive calls overlap launch latency and pipeline
+//    fill with the previous call's tail.
 //  * Persistent grid, one CTA per SM.  The weight matrix is cut into row tiles of 256
 //    output features; the (row tile, quantization group) pairs are split into equal
-//    contiguous ranges, one per CTA (stream-K), so every SM streams the same number
-//    of bytes whatever N and K are.  A row tile cut between CTAs is finished by the
-//    last CTA to arrive (fp32 partials in the workspace, fixed summation order).
-//  * One producer warp issues TMA tile loads (cp.async.bulk.tensor, no multicast)
+//    contiguous ranges, one per CTA (stream-K).  A row tile cut between CTAs is
+//    finished by the last CTA to arrive (fp32 partials in the workspace, fixed
+//    summation order, so results are deterministic).
+//  * One producer thread issues TMA tile loads (cp.async.bulk.tensor, no multicast)
 //    into a 4-deep shared-memory ring: per stage a [256 rows x 128 B] weight box with
-//    128-byte swizzle, the matching x columns, and the scale/bias columns.
-//  * 16 consumer warps: 8 row slices of 32 features x 2 stage parities.  Each
-//    dequantises in registers and contracts on mma.sync m16n8k16 with the weights as
-//    the 16-row A operand and x (<= 8 rows per n-tile) as the n=8 B operand, so a
+//    128-byte swizzle, the matching x columns and x group sums, and the scale/bias
+//    columns.
+//  * 16 consumer warps: 8 slices of 32 features x 2 groups that take alternate stages.
+//    Each dequantises in registers and contracts on mma.sync m16n8k16 with the weights
+//    as the 16-row A operand and x (<= 8 rows per n-tile) as the n=8 B operand, so a
 //    weight is read and dequantised once for all M rows.
 //
-// Dequantisation uses the factored form  sum_k x q s + b x  =  s (sum_k x q) + b (sum_k x)
-// per group: integer codes become bf16 exactly by OR-ing a nibble into the mantissa
-// of 128.0 (0x4300), one LOP3 per two weights; the group sum of x comes from an extra
-// MMA against an all-ones A operand; the 128 offset folds into the bias term.  8-bit
-// codes are split into two nibbles contracted against x and 16*x.  Within a thread's
-// slice of a group the k order is permuted identically for weights and x (sums do
-// not depend on k order), so weights are consumed exactly as MLX packs them.
+// Dequantisation uses the factored form  sum_k x (q s + b) = s (sum_k x q) + b (sum_k x)
+// per group.  An integer code becomes bf16 exactly by OR-ing its nibble into the
+// mantissa of 128.0 (0x4300): one LOP3 per two weights, with the nibble shifts done as
+// high multiplies on the FMA pipe so the ALU pipe only carries the LOP3s.  The MMA
+// then yields sum_k x (q + 128); the 128 (for 8-bit codes, split into two nibbles
+// contracted against x and 16 x: 2176) folds into the bias term with the precomputed
+// group sum.  Within a thread's slice of a group the k order is permuted identically
+// for weights and x (a sum does not depend on k order), so weights are consumed
+// exactly as MLX packs them.
 #include "common.cuh"
 
 namespace dflash {
@@ -40,7 +49,10 @@ constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kStages = 4;
 constexpr int kRedPitch = kRows + 4;  // floats per m row of the reduction buffer (bank spread)
 constexpr int kMaxCtas = 160;         // upper bound on the persistent grid (B200: 148 SMs)
+constexpr int kMaxTiles = 4096;       // N <= kMaxTiles * kRows
+constexpr int kXsWidth = 16;          // floats per group row of the x group-sum table
 constexpr int kBarConsumers = 1;      // named barrier id used by the consumer warps
+constexpr int kPrepThreads = 256;
 
 template <int BITS_, int GROUP_, int NT_, bool STMA_>
 struct Cfg {
@@ -56,8 +68,10 @@ struct Cfg {
     static constexpr int XBOX_BYTES = XROWS * 128;
     static constexpr int X_BYTES = XBOX * XBOX_BYTES;
     static constexpr int S_BYTES = kRows * 16;           // [256 rows x 8 groups] bf16
-    static constexpr int STAGE_BYTES = W_BYTES + X_BYTES + 2 * S_BYTES;
-    static constexpr uint32_t TX_BYTES = W_BYTES + X_BYTES + (STMA ? 2 * S_BYTES : 0);
+    static constexpr int XS_BYTES = GPS * XROWS * 4;     // [GPS groups x XROWS] fp32
+    static constexpr int XS_OFF = W_BYTES + X_BYTES + 2 * S_BYTES;
+    static constexpr int STAGE_BYTES = XS_OFF + 1024;
+    static constexpr uint32_t TX_BYTES = W_BYTES + X_BYTES + XS_BYTES + (STMA ? 2 * S_BYTES : 0);
     static constexpr int VPT = GROUP / 4;                // values per thread per row per group
     static constexpr int PV = VPT < 16 ? VPT : 16;       // values per piece
     static constexpr int PIECES = VPT / PV;
@@ -69,6 +83,7 @@ struct Cfg {
     static constexpr int SMEM_BYTES = kStages * STAGE_BYTES + RED_FLOATS * 4 + 256 + 1024;
     static constexpr float OFFSET = BITS == 4 ? 128.f : 2176.f;  // magic-number offset per unit x
     static_assert(GPS >= 1 && GPS <= 8 && (8 % GPS) == 0, "stage/group geometry");
+    static_assert(XS_BYTES <= 1024, "x group-sum stage slot");
     static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte swizzle alignment");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -82,17 +97,85 @@ struct Params {
     int M, N, K, GT, tiles, G;
     long long U;
     int y_vec;
+    // 2^28, 2^24, 2^20: the nibble shifts are high multiplies by these (run-time
+    // values, so they stay multiplies on the FMA pipe).
+    uint32_t mul4, mul8, mul12;
 };
+
+// ------------------------------------------------------------------ workspace layout
+//
+//   [fp32 partial tiles, kMaxCtas x 2 x 16 x 256][tile counters, kMaxTiles]
+//   [x group sums, GT x 16 fp32][x in fragment order, M x K bf16]
+// The partial and counter regions sit at fixed offsets whatever the shape, so one
+// workspace serves calls of any shape; the counters are left zeroed by every call.
+inline size_t partials_bytes() { return (size_t)kMaxCtas * 2 * 16 * kRows * 4; }
+inline size_t counters_bytes() { return (size_t)kMaxTiles * 4; }
+inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+inline size_t xs_offset() { return partials_bytes() + counters_bytes(); }
+inline size_t xperm_offset(int K, int group) { return xs_offset() + round_up((size_t)(K / group) * kXsWidth * 4, 1024); }
+inline size_t workspace_size(int M, int K, int group) {
+    return xperm_offset(K, group) + round_up((size_t)M * K * 2, 1024);
+}
+
+// ------------------------------------------------------------------ PDL
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ------------------------------------------------------------------ prep kernel
+//
+// x [M, K] bf16 -> xperm [M, K] with each run of 8 values reordered so that one
+// 16-byte load gives a thread its four B-fragment registers: 4-bit codes pair k with
+// k+4 ((0,4),(1,5),(2,6),(3,7)), 8-bit codes pair k with k+2 ((0,2),(1,3),(4,6),(5,7)).
+// xs[G][m] = sum of x[m, G*group .. G*group+group-1] in fp32 (rows m >= M are zero).
+template <int BITS>
+__global__ void __launch_bounds__(kPrepThreads) qmm_prep_kernel(const dflash_bf16* __restrict__ x,
+                                                              dflash_bf16* __restrict__ xperm,
+                                                              float* __restrict__ xs, int M, int K, int group) {
+    pdl_launch_dependents();
+    pdl_wait();  // the previous call may still be reading this workspace
+    const int chunks_per_row = K / 8;
+    const long long idx = (long long)blockIdx.x * kPrepThreads + threadIdx.x;
+    const bool live = idx < (long long)kXsWidth * chunks_per_row;
+    const int m = live ? (int)(idx / chunks_per_row) : kXsWidth;
+    const int c = live ? (int)(idx % chunks_per_row) : 0;
+    float sum = 0.f;
+    if (live && m < M) {
+        const uint4 r = *reinterpret_cast<const uint4*>(x + (size_t)m * K + (size_t)c * 8);
+        uint4 o;
+        if constexpr (BITS == 4) {
+            o.x = __byte_perm(r.x, r.z, 0x5410);
+            o.y = __byte_perm(r.x, r.z, 0x7632);
+            o.z = __byte_perm(r.y, r.w, 0x5410);
+            o.w = __byte_perm(r.y, r.w, 0x7632);
+        } else {
+            o.x = __byte_perm(r.x, r.y, 0x5410);
+            o.y = __byte_perm(r.x, r.y, 0x7632);
+            o.z = __byte_perm(r.z, r.w, 0x5410);
+            o.w = __byte_perm(r.z, r.w, 0x7632);
+        }
+        *reinterpret_cast<uint4*>(xperm + (size_t)m * K + (size_t)c * 8) = o;
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            sum += __uint_as_float(w[i] << 16);
+            sum += __uint_as_float(w[i] & 0xffff0000u);
+        }
+    }
+    // reduce the group's group/8 consecutive chunks (aligned lanes of one warp)
+    const int lanes = group / 8;
+    for (int off = 1; off < lanes; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (live && (c % lanes) == 0) xs[(size_t)(c / lanes) * kXsWidth + m] = sum;
+}
+
+// ------------------------------------------------------------------ main kernel helpers
 
 __device__ __forceinline__ long long owner_of(long long u, const Params& p) {
     return ((u + 1) * p.G - 1) / p.U;
 }
 __device__ __forceinline__ long long range_begin(long long c, const Params& p) {
     return c * p.U / p.G;
-}
-
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    return __byte_perm(a, b, sel);
 }
 
 __device__ __forceinline__ uint32_t bf16x2_times16(uint32_t v) {
@@ -103,10 +186,15 @@ __device__ __forceinline__ uint32_t bf16x2_times16(uint32_t v) {
 
 constexpr uint32_t kMagic = 0x43004300u;   // bf16x2 (128.0, 128.0)
 constexpr uint32_t kNib = 0x000F000Fu;
-constexpr uint32_t kOnes = 0x3F803F80u;    // bf16x2 (1.0, 1.0)
 
-// ------------------------------------------------------------------ fragment layout
-//
+// (v >> 4q) as a high multiply: v * 2^(32-4q) >> 32.
+__device__ __forceinline__ uint32_t shr_nib(uint32_t v, int q, const Params& p) {
+    if (q == 0) return v;
+    const uint32_t mul = q == 1 ? p.mul4 : (q == 2 ? p.mul8 : p.mul12);
+    return __umulhi(v, mul);
+}
+__device__ __forceinline__ uint32_t magic(uint32_t v) { return (v & kNib) | kMagic; }
+
 // Fragment row g of 16-row block i of a warp's 32-feature slice maps to feature row
 //     rb + 16 i + 2 sigma(g) + h        (h = 0: fragment rows 0..7, h = 1: rows 8..15)
 // sigma spreads the 128-byte swizzle keys (row & 7) of the rows a half-warp (LDS.64)
@@ -118,7 +206,7 @@ template <class C>
 struct LaneLayout {
     int row[2];                                   // feature row of (i = 0, h); i = 1 adds 16
     uint32_t wofs[2];                             // stage-relative byte offset of group 0, piece 0
-    uint32_t xofs[C::NT][C::PIECES][C::PXCH];     // stage-relative x offset (from the x region), group 0
+    uint32_t xofs[C::NT][C::PIECES][C::PXCH];     // offset within the x region, group 0
 };
 
 template <class C>
@@ -198,34 +286,27 @@ __device__ __forceinline__ void mma_step(float (&d)[4], uint32_t a0, uint32_t a1
 }
 
 // One quantization group (index gl within the stage) for one consumer warp:
-// 32 feature rows x GROUP k, all M rows.  wb[h] = stage base + wofs[h];
-// xb = x region base; sb[h] = scale-tile address of row[h] at this stage's group 0.
+// 32 feature rows x GROUP k, all M rows.  wb[h] = stage base + wofs[h]; xb = x region;
+// sb[h] = scale-tile address of row[h] at this stage's group 0; xsb = this thread's
+// x group-sum slot (group 0, n-tile 0) in the stage.
 template <class C>
 __device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const uint32_t (&wb)[2], uint32_t xb,
-                                              const uint32_t (&sb)[2], int gl, int G, int tile_row0,
+                                              const uint32_t (&sb)[2], uint32_t xsb, int gl, int G, int tile_row0,
                                               const Params& p, float (&acc)[2][C::NT][4]) {
     float tmp[2][C::NT][4];
-    float xs[C::NT][4];
 #pragma unroll
     for (int pc = 0; pc < C::PIECES; ++pc) {
-        // B fragments: this thread's slice of x for activation rows 8j + g.
+        // B fragments, already in register order (prep kernel)
         uint32_t xf[C::NT][C::PXCH][4];
 #pragma unroll
         for (int j = 0; j < C::NT; ++j)
 #pragma unroll
             for (int c = 0; c < C::PXCH; ++c) {
                 const uint4 r = lds128(xb + ((L.xofs[j][pc][c] ^ x_xor<C>(gl)) + x_add<C>(gl)));
-                if constexpr (C::BITS == 4) {
-                    xf[j][c][0] = prmt(r.x, r.z, 0x5410);  // (x0, x4)
-                    xf[j][c][1] = prmt(r.x, r.z, 0x7632);  // (x1, x5)
-                    xf[j][c][2] = prmt(r.y, r.w, 0x5410);  // (x2, x6)
-                    xf[j][c][3] = prmt(r.y, r.w, 0x7632);  // (x3, x7)
-                } else {
-                    xf[j][c][0] = prmt(r.x, r.y, 0x5410);  // (x0, x2)
-                    xf[j][c][1] = prmt(r.x, r.y, 0x7632);  // (x1, x3)
-                    xf[j][c][2] = prmt(r.z, r.w, 0x5410);  // (x4, x6)
-                    xf[j][c][3] = prmt(r.z, r.w, 0x7632);  // (x5, x7)
-                }
+                xf[j][c][0] = r.x;
+                xf[j][c][1] = r.y;
+                xf[j][c][2] = r.z;
+                xf[j][c][3] = r.w;
             }
         // A operand source: packed words of the 4 feature rows (i, h).
         uint32_t wv[2][2][C::PW];
@@ -241,43 +322,53 @@ __device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const uint
             if constexpr (C::BITS == 4) {
                 const int w = s >> 1, q = (s & 1) * 2;
 #pragma unroll
-                for (int j = 0; j < C::NT; ++j) {
-                    const uint32_t b0 = xf[j][w][q], b1 = xf[j][w][q + 1];
-                    if (first) mma_step<true>(xs[j], kOnes, kOnes, kOnes, kOnes, b0, b1);
-                    else mma_step<false>(xs[j], kOnes, kOnes, kOnes, kOnes, b0, b1);
+                for (int i = 0; i < 2; ++i) {
+                    const uint32_t a0 = magic(shr_nib(wv[i][0][w], q, p));
+                    const uint32_t a1 = magic(shr_nib(wv[i][1][w], q, p));
+                    const uint32_t a2 = magic(shr_nib(wv[i][0][w], q + 1, p));
+                    const uint32_t a3 = magic(shr_nib(wv[i][1][w], q + 1, p));
 #pragma unroll
-                    for (int i = 0; i < 2; ++i) {
-                        const uint32_t a0 = ((wv[i][0][w] >> (4 * q)) & kNib) | kMagic;
-                        const uint32_t a1 = ((wv[i][1][w] >> (4 * q)) & kNib) | kMagic;
-                        const uint32_t a2 = ((wv[i][0][w] >> (4 * q + 4)) & kNib) | kMagic;
-                        const uint32_t a3 = ((wv[i][1][w] >> (4 * q + 4)) & kNib) | kMagic;
+                    for (int j = 0; j < C::NT; ++j) {
+                        const uint32_t b0 = xf[j][w][q], b1 = xf[j][w][q + 1];
                         if (first) mma_step<true>(tmp[i][j], a0, a1, a2, a3, b0, b1);
                         else mma_step<false>(tmp[i][j], a0, a1, a2, a3, b0, b1);
                     }
                 }
             } else {
                 const int w = s, c = s >> 1, q = (s & 1) * 2;
+                uint32_t h0[C::NT], h1[C::NT];
 #pragma unroll
                 for (int j = 0; j < C::NT; ++j) {
-                    const uint32_t b0 = xf[j][c][q], b1 = xf[j][c][q + 1];
-                    const uint32_t h0 = bf16x2_times16(b0), h1 = bf16x2_times16(b1);
-                    if (first) mma_step<true>(xs[j], kOnes, kOnes, kOnes, kOnes, b0, b1);
-                    else mma_step<false>(xs[j], kOnes, kOnes, kOnes, kOnes, b0, b1);
+                    h0[j] = bf16x2_times16(xf[j][c][q]);
+                    h1[j] = bf16x2_times16(xf[j][c][q + 1]);
+                }
 #pragma unroll
-                    for (int i = 0; i < 2; ++i) {
-                        const uint32_t w0 = wv[i][0][w], w1 = wv[i][1][w];
-                        const uint32_t l0 = (w0 & kNib) | kMagic, l1 = (w1 & kNib) | kMagic;
-                        const uint32_t l2 = ((w0 >> 8) & kNib) | kMagic, l3 = ((w1 >> 8) & kNib) | kMagic;
+                for (int i = 0; i < 2; ++i) {
+                    const uint32_t w0 = wv[i][0][w], w1 = wv[i][1][w];
+                    const uint32_t l0 = magic(w0), l1 = magic(w1);
+                    const uint32_t l2 = magic(shr_nib(w0, 2, p)), l3 = magic(shr_nib(w1, 2, p));
+                    const uint32_t u0 = magic(shr_nib(w0, 1, p)), u1 = magic(shr_nib(w1, 1, p));
+                    const uint32_t u2 = magic(shr_nib(w0, 3, p)), u3 = magic(shr_nib(w1, 3, p));
+#pragma unroll
+                    for (int j = 0; j < C::NT; ++j) {
+                        const uint32_t b0 = xf[j][c][q], b1 = xf[j][c][q + 1];
                         if (first) mma_step<true>(tmp[i][j], l0, l1, l2, l3, b0, b1);
                         else mma_step<false>(tmp[i][j], l0, l1, l2, l3, b0, b1);
-                        mma_bf16_16816(tmp[i][j], ((w0 >> 4) & kNib) | kMagic, ((w1 >> 4) & kNib) | kMagic,
-                                       ((w0 >> 12) & kNib) | kMagic, ((w1 >> 12) & kNib) | kMagic, h0, h1);
+                        mma_bf16_16816(tmp[i][j], u0, u1, u2, u3, h0[j], h1[j]);
                     }
                 }
             }
         }
     }
 
+    // x group sums for this thread's output columns m = 8j + 2tq, 8j + 2tq + 1
+    float xs[C::NT][2];
+#pragma unroll
+    for (int j = 0; j < C::NT; ++j) {
+        const uint2 v = lds64(xsb + (gl * C::XROWS + 8 * j) * 4);
+        xs[j][0] = __uint_as_float(v.x);
+        xs[j][1] = __uint_as_float(v.y);
+    }
     // acc += s * tmp + (b - OFFSET * s) * xs, per feature row.
 #pragma unroll
     for (int i = 0; i < 2; ++i)
@@ -304,24 +395,25 @@ __device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const uint
             for (int j = 0; j < C::NT; ++j)
 #pragma unroll
                 for (int e = 0; e < 2; ++e)
-                    acc[i][j][2 * h + e] = fmaf(s, tmp[i][j][2 * h + e], fmaf(bb, xs[j][2 * h + e], acc[i][j][2 * h + e]));
+                    acc[i][j][2 * h + e] = fmaf(s, tmp[i][j][2 * h + e], fmaf(bb, xs[j][e], acc[i][j][2 * h + e]));
         }
 }
 
 // All groups of one stage.  CHECK: the stage is the first or last of a segment and
 // some of its groups fall outside [ga, gb).
 template <class C, bool CHECK>
-__device__ __forceinline__ void consume_stage(const LaneLayout<C>& L, uint32_t st, int sc, int ga, int gb,
+__device__ __forceinline__ void consume_stage(const LaneLayout<C>& L, uint32_t st, int sc, int ga, int gb, int tq,
                                               int tile_row0, const Params& p, float (&acc)[2][C::NT][4]) {
     const uint32_t wb[2] = {st + L.wofs[0], st + L.wofs[1]};
     const uint32_t xb = st + C::W_BYTES;
     const uint32_t s0 = st + C::W_BYTES + C::X_BYTES + 2 * ((sc * C::GPS) & 7);
     const uint32_t sb[2] = {s0 + L.row[0] * 16, s0 + L.row[1] * 16};
+    const uint32_t xsb = st + C::XS_OFF + 2 * tq * 4;
 #pragma unroll
     for (int gl = 0; gl < C::GPS; ++gl) {
         const int G = sc * C::GPS + gl;
         if (CHECK && (G < ga || G >= gb)) continue;
-        consume_group<C>(L, wb, xb, sb, gl, G, tile_row0, p, acc);
+        consume_group<C>(L, wb, xb, sb, xsb, gl, G, tile_row0, p, acc);
     }
 }
 
@@ -358,7 +450,7 @@ template <class C>
 __global__ void __launch_bounds__(kThreads, 1)
     qmm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_b,
-               const Params p) {
+               const __grid_constant__ CUtensorMap tm_xs, const Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* red = reinterpret_cast<float*>(smem + kStages * C::STAGE_BYTES);
@@ -367,6 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
     volatile int* last_flag = abort_flag + 1;
 
+    pdl_launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -388,12 +481,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane != 0) return;
         prefetch_tensormap(&tm_w);
         prefetch_tensormap(&tm_x);
+        prefetch_tensormap(&tm_xs);
         if constexpr (C::STMA) {
             prefetch_tensormap(&tm_s);
             prefetch_tensormap(&tm_b);
         }
+        // Stage j covers groups [sc*GPS, sc*GPS+GPS) of row tile t.  The weight-side
+        // loads (W, scales, biases) of the first ring fill go out before the grid
+        // dependency resolves; x and its group sums only after it.
         int j = 0;
-        bool ok = true;
+        bool ok = true, dep_resolved = false;
+        int pend_sc[kStages];
+        int n_pend = 0;
+        auto issue_x = [&](int slot, int sc) {
+            uint8_t* st = smem + slot * C::STAGE_BYTES;
+#pragma unroll
+            for (int b = 0; b < C::XBOX; ++b)
+                tma_load_2d(st + C::W_BYTES + b * C::XBOX_BYTES, &tm_x, &full[slot], sc * C::KPS + 64 * b, 0);
+            tma_load_2d(st + C::XS_OFF, &tm_xs, &full[slot], 0, sc * C::GPS);
+        };
         for (long long u = u0; u < u1 && ok;) {
             const int t = (int)(u / p.GT);
             const int ga = (int)(u - (long long)t * p.GT);
@@ -401,6 +507,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int sc = ga / C::GPS; sc < (gb + C::GPS - 1) / C::GPS; ++sc, ++j) {
                 const int slot = j % kStages;
                 const uint32_t ph = (uint32_t)(j / kStages) & 1u;
+                if (!dep_resolved && j == kStages) {
+                    pdl_wait();
+                    dep_resolved = true;
+                    for (int i = 0; i < n_pend; ++i) issue_x(i, pend_sc[i]);
+                }
                 if (!mbar_wait_bounded(&empty[slot], ph ^ 1u, abort_flag, DFLASH_DEVERR_QMM_PIPELINE)) {
                     ok = false;
                     break;
@@ -408,16 +519,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint8_t* st = smem + slot * C::STAGE_BYTES;
                 mbar_arrive_expect_tx(&full[slot], C::TX_BYTES);
                 tma_load_2d(st, &tm_w, &full[slot], sc * (kRowBytes / 4), t * kRows);
-#pragma unroll
-                for (int b = 0; b < C::XBOX; ++b)
-                    tma_load_2d(st + C::W_BYTES + b * C::XBOX_BYTES, &tm_x, &full[slot], sc * C::KPS + 64 * b, 0);
                 if constexpr (C::STMA) {
                     const int gx = (sc * C::GPS) & ~7;
                     tma_load_2d(st + C::W_BYTES + C::X_BYTES, &tm_s, &full[slot], gx, t * kRows);
                     tma_load_2d(st + C::W_BYTES + C::X_BYTES + C::S_BYTES, &tm_b, &full[slot], gx, t * kRows);
                 }
+                if (dep_resolved) {
+                    issue_x(slot, sc);
+                } else {
+                    pend_sc[n_pend++] = sc;
+                }
             }
             u = (long long)t * p.GT + gb;
+        }
+        if (!dep_resolved) {
+            pdl_wait();
+            for (int i = 0; i < n_pend; ++i) issue_x(i, pend_sc[i]);
         }
         // Drain: do not leave the CTA while issued copies may still be landing.
         for (int i = max(0, j - kStages); i < j; ++i) {
@@ -431,6 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // -------------------------------------------------------------- consumers
+    pdl_wait();  // y and the workspace may still be in use by the previous call
     const int rs = warp % kRowSlices, par = warp / kRowSlices;
     const int g = lane >> 2, tq = lane & 3;
     const int rb = rs * 32;
@@ -453,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int e = 0; e < 4; ++e) acc[i][jj][e] = 0.f;
 
         for (int sc = ga / C::GPS; sc < (gb + C::GPS - 1) / C::GPS; ++sc, ++j) {
-            if ((j & 1) != par) continue;
+            if ((j % kKSplit) != par) continue;
             const int slot = j % kStages;
             const uint32_t ph = (uint32_t)(j / kStages) & 1u;
             // mma.sync below is warp-collective: every lane must take the same branch
@@ -462,9 +580,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (ok) {
                 const uint32_t st = smem_u32(smem + slot * C::STAGE_BYTES);
                 if (sc * C::GPS >= ga && sc * C::GPS + C::GPS <= gb)
-                    consume_stage<C, false>(L, st, sc, ga, gb, tile_row0, p, acc);
+                    consume_stage<C, false>(L, st, sc, ga, gb, tq, tile_row0, p, acc);
                 else
-                    consume_stage<C, true>(L, st, sc, ga, gb, tile_row0, p, acc);
+                    consume_stage<C, true>(L, st, sc, ga, gb, tq, tile_row0, p, acc);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
@@ -557,9 +675,24 @@ struct Shape {
 
 inline int n_tiles(int N) { return (N + kRows - 1) / kRows; }
 
-inline size_t counters_bytes(int N) { return ((size_t)n_tiles(N) * 4 + 255) & ~size_t(255); }
-
-inline size_t partials_bytes() { return (size_t)kMaxCtas * 2 * 16 * kRows * 4; }
+// Launch with programmatic stream serialization: the kernel may begin while the
+// previous kernel in the stream is still running; griddepcontrol.wait in the kernel
+// orders everything that depends on it.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 template <class C>
 int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scales,
@@ -573,22 +706,29 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
     if (attr_err != cudaSuccess)
         return fail(DFLASH_ERR_CUDA, "cudaFuncSetAttribute(qmm): %s", cudaGetErrorString(attr_err));
 
-    CUtensorMap tm_w, tm_x, tm_s, tm_b;
+    uint8_t* wsb = reinterpret_cast<uint8_t*>(ws);
+    float* xs = reinterpret_cast<float*>(wsb + xs_offset());
+    dflash_bf16* xperm = reinterpret_cast<dflash_bf16*>(wsb + xperm_offset(s.K, s.group));
+    const int GT = s.K / s.group;
+
+    CUtensorMap tm_w, tm_x, tm_s, tm_b, tm_xs;
     int st;
     const uint64_t words = (uint64_t)s.K * s.bits / 32;
-    st = encode_tensor_map_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, words, (uint64_t)s.N,
-                              words * 4, kRowBytes / 4, kRows, CU_TENSOR_MAP_SWIZZLE_128B);
+    st = encode_tensor_map_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, words, (uint64_t)s.N, words * 4,
+                              kRowBytes / 4, kRows, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
-    st = encode_tensor_map_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)s.K, (uint64_t)s.M,
+    st = encode_tensor_map_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xperm, (uint64_t)s.K, (uint64_t)s.M,
                               (uint64_t)s.K * 2, 64, C::XROWS, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
-    const uint64_t gt = (uint64_t)(s.K / s.group);
+    st = encode_tensor_map_2d(&tm_xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xs, kXsWidth, (uint64_t)GT, kXsWidth * 4,
+                              C::XROWS, C::GPS, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
     if constexpr (C::STMA) {
-        st = encode_tensor_map_2d(&tm_s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, scales, gt, (uint64_t)s.N, gt * 2,
-                                  8, kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+        st = encode_tensor_map_2d(&tm_s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, scales, (uint64_t)GT, (uint64_t)s.N,
+                                  (uint64_t)GT * 2, 8, kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (st) return st;
-        st = encode_tensor_map_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, biases, gt, (uint64_t)s.N, gt * 2,
-                                  8, kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+        st = encode_tensor_map_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, biases, (uint64_t)GT, (uint64_t)s.N,
+                                  (uint64_t)GT * 2, 8, kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (st) return st;
     } else {
         tm_s = tm_w;
@@ -601,14 +741,12 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
     p.y = y;
     p.scales = scales;
     p.biases = biases;
-    // Layout independent of the shape, so one workspace serves calls of any N:
-    // [fp32 partials, fixed size][per-tile counters, tile t at the same offset always].
-    p.partials = reinterpret_cast<float*>(ws);
-    p.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ws) + partials_bytes());
+    p.partials = reinterpret_cast<float*>(wsb);
+    p.counters = reinterpret_cast<int*>(wsb + partials_bytes());
     p.M = s.M;
     p.N = s.N;
     p.K = s.K;
-    p.GT = s.K / s.group;
+    p.GT = GT;
     p.tiles = n_tiles(s.N);
     p.U = (long long)p.tiles * p.GT;
     long long G = sm_count(dev);
@@ -616,8 +754,20 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
     if (G > p.U) G = p.U;
     p.G = (int)G;
     p.y_vec = (s.N % 8 == 0) && aligned16(y);
-    qmm_kernel<C><<<p.G, kThreads, C::SMEM_BYTES, stream>>>(tm_w, tm_x, tm_s, tm_b, p);
-    DFLASH_CUDA_TRY(cudaGetLastError());
+    p.mul4 = 1u << 28;
+    p.mul8 = 1u << 24;
+    p.mul12 = 1u << 20;
+
+    const long long prep_threads = (long long)kXsWidth * (s.K / 8);
+    const int prep_blocks = (int)((prep_threads + kPrepThreads - 1) / kPrepThreads);
+    if (s.bits == 4)
+        DFLASH_CUDA_TRY(launch_pdl(qmm_prep_kernel<4>, dim3(prep_blocks), dim3(kPrepThreads), 0, stream, x, xperm, xs,
+                                   s.M, s.K, s.group));
+    else
+        DFLASH_CUDA_TRY(launch_pdl(qmm_prep_kernel<8>, dim3(prep_blocks), dim3(kPrepThreads), 0, stream, x, xperm, xs,
+                                   s.M, s.K, s.group));
+    DFLASH_CUDA_TRY(launch_pdl(qmm_kernel<C>, dim3(p.G), dim3(kThreads), (size_t)C::SMEM_BYTES, stream, tm_w, tm_x,
+                               tm_s, tm_b, tm_xs, p));
     return DFLASH_OK;
 }
 
@@ -653,6 +803,8 @@ int validate(const Shape& s) {
         return fail(DFLASH_ERR_UNSUPPORTED, "group_size %d not in {32, 64, 128}", s.group);
     if (s.M < 1 || s.M > 16) return fail(DFLASH_ERR_UNSUPPORTED, "M=%d outside 1..16", s.M);
     if (s.N < 1 || s.K < 1) return fail(DFLASH_ERR_INVALID_ARGUMENT, "N=%d K=%d must be positive", s.N, s.K);
+    if (s.N > kMaxTiles * kRows)
+        return fail(DFLASH_ERR_UNSUPPORTED, "N=%d above the supported %d", s.N, kMaxTiles * kRows);
     if (s.K % s.group != 0)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "K=%d is not a multiple of group_size %d", s.K, s.group);
     return DFLASH_OK;
@@ -662,17 +814,16 @@ int validate(const Shape& s) {
 }  // namespace dflash
 
 extern "C" size_t dflash_qmm_workspace_bytes(int M, int N, int K, int group_size, int bits) {
-    (void)M;
-    (void)K;
-    (void)group_size;
     (void)bits;
-    if (N < 1) return 0;
-    return dflash::qmm::counters_bytes(N) + dflash::qmm::partials_bytes();
+    if (N < 1 || K < 1 || M < 1 || M > 16 || (group_size != 32 && group_size != 64 && group_size != 128) ||
+        K % group_size != 0)
+        return 0;
+    return dflash::qmm::workspace_size(M, K, group_size);
 }
 
 extern "C" int dflash_qmm_supported(int N, int K, int group_size, int bits) {
     if ((bits != 4 && bits != 8) || (group_size != 32 && group_size != 64 && group_size != 128)) return 0;
-    if (N < 1 || K < 1 || K % group_size != 0) return 0;
+    if (N < 1 || K < 1 || K % group_size != 0 || N > dflash::qmm::kMaxTiles * dflash::qmm::kRows) return 0;
     return 1;
 }
 
@@ -686,9 +837,10 @@ extern "C" int dflash_qmm(const dflash_bf16* x, const uint32_t* w, const dflash_
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_qmm: null tensor pointer");
     if (!aligned16(x) || !aligned16(w))
         return fail(DFLASH_ERR_MISALIGNED, "dflash_qmm: x and w must be 16-byte aligned");
-    if (!workspace || !aligned16(workspace) || workspace_bytes < dflash_qmm_workspace_bytes(M, N, K, group_size, bits))
-        return fail(DFLASH_ERR_WORKSPACE, "dflash_qmm: workspace of %zu bytes required (got %zu)",
-                    dflash_qmm_workspace_bytes(M, N, K, group_size, bits), workspace_bytes);
+    const size_t need = dflash_qmm_workspace_bytes(M, N, K, group_size, bits);
+    if (!workspace || !aligned16(workspace) || workspace_bytes < need)
+        return fail(DFLASH_ERR_WORKSPACE, "dflash_qmm: workspace of %zu bytes required (got %zu)", need,
+                    workspace_bytes);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (bits == 4) return qmm::dispatch_group<4>(s, x, w, scales, biases, y, workspace, st);
     return qmm::dispatch_group<8>(s, x, w, scales, biases, y, workspace, st);

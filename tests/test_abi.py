@@ -77,11 +77,17 @@ def test_qmm_supported_table(dc):
 
 
 def test_workspace_size_is_shape_bounded(dc):
+    """Fixed partial/counter regions plus x in fragment order and its group sums:
+    independent of N, growing with M*K, zero for shapes the kernel rejects."""
     a = dc.qmm_workspace_bytes(8, 17408, 5120, 64, 4)
-    assert a == dc.qmm_workspace_bytes(16, 17408, 17408, 128, 8)  # does not depend on M, K, format
-    assert a > 0 and a < 16 << 20
-    assert dc.qmm_workspace_bytes(8, 248320, 5120, 64, 4) > a     # counters grow with N
+    assert a == dc.qmm_workspace_bytes(8, 5120, 5120, 64, 4) == dc.qmm_workspace_bytes(8, 248320, 5120, 64, 8)
+    assert dc.qmm_workspace_bytes(16, 17408, 5120, 64, 4) > a
+    assert dc.qmm_workspace_bytes(8, 17408, 17408, 64, 4) > a
+    fixed = 160 * 2 * 16 * 256 * 4 + 4096 * 4
+    assert fixed < a < fixed + (1 << 20)
     assert dc.qmm_workspace_bytes(8, 0, 5120, 64, 4) == 0
+    assert dc.qmm_workspace_bytes(17, 17408, 5120, 64, 4) == 0
+    assert dc.qmm_workspace_bytes(8, 17408, 5000, 64, 4) == 0
 
 
 def _gdn_step(dc, T=8, H=4, dk=128, dv=128, si=FAKE, so=FAKE * 2, q=FAKE, k=FAKE, v=FAKE, a=FAKE, b=FAKE, out=0):
