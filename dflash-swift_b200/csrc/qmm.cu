@@ -26,14 +26,20 @@
 //    weight is read and dequantised once for all M rows.
 //
 // Dequantisation uses the factored form  sum_k x (q s + b) = s (sum_k x q) + b (sum_k x)
-// per group.  An integer code becomes bf16 exactly by OR-ing its nibble into the
-// mantissa of 128.0 (0x4300): one LOP3 per two weights, with the nibble shifts done as
-// high multiplies on the FMA pipe so the ALU pipe only carries the LOP3s.  The MMA
-// then yields sum_k x (q + 128); the 128 (for 8-bit codes, split into two nibbles
-// contracted against x and 16 x: 2176) folds into the bias term with the precomputed
-// group sum.  Within a thread's slice of a group the k order is permuted identically
-// for weights and x (a sum does not depend on k order), so weights are consumed
-// exactly as MLX packs them.
+// per group, on fp16 MMA operands.  A code becomes an exact fp16 value by OR-ing its
+// nibble into the mantissa of a power of two, one LOP3 per two weights: a nibble in
+// bits 0-3 of a 16-bit lane over 1024.0 (0x6400) reads 1024 + q; a nibble in bits 4-7
+// over 64.0 (0x5400) reads 64 + q (the mantissa step there is 1/16), so both nibbles of
+// a byte unpack without a shift and a packed word costs 4 LOP3 and one shift for 8
+// weights.  The ALU pipe, which those LOP3s load, is what bounds the kernel.  The MMA
+// yields sum_k x (q + offset_k); the prep kernel supplies per group the sum of x and
+// z = sum_k offset_k x, so  y += (s f) tmp + b xs - s z  recovers the exact sum.  For
+// 8-bit codes the high nibble over 1024.0 reads 1024 + 16 q_hi, so both MMAs use the
+// same x and z = 2048 xs.  x enters fp16 scaled per (row, group) by a power of two
+// f^-1 that keeps it below 2^15 (exact: bf16 values fit fp16's significand), so no
+// input overflows.  Within a thread's slice of a group the k order is permuted
+// identically for weights and x (a sum does not depend on k order), so weights are
+// consumed exactly as MLX packs them.
 #include "common.cuh"
 
 namespace dflash {
@@ -50,7 +56,8 @@ constexpr int kStages = 4;
 constexpr int kRedPitch = kRows + 4;  // floats per m row of the reduction buffer (bank spread)
 constexpr int kMaxCtas = 160;         // upper bound on the persistent grid (B200: 148 SMs)
 constexpr int kMaxTiles = 4096;       // N <= kMaxTiles * kRows
-constexpr int kXsWidth = 16;          // floats per group row of the x group-sum table
+constexpr int kXsWidth = 16;          // x rows covered by the per-group table (M <= 16)
+constexpr int kTabWidth = 64;         // floats per group row of the table: xs[16] f[16] z[16] pad
 constexpr int kBarConsumers = 1;      // named barrier id used by the consumer warps
 constexpr int kPrepThreads = 256;
 
@@ -68,9 +75,10 @@ struct Cfg {
     static constexpr int XBOX_BYTES = XROWS * 128;
     static constexpr int X_BYTES = XBOX * XBOX_BYTES;
     static constexpr int S_BYTES = kRows * 16;           // [256 rows x 8 groups] bf16
-    static constexpr int XS_BYTES = GPS * XROWS * 4;     // [GPS groups x XROWS] fp32
+    static constexpr int TAB_ROW = 48;                   // floats loaded per group: xs, f, z
+    static constexpr int XS_BYTES = GPS * TAB_ROW * 4;   // [GPS groups x 48] fp32
     static constexpr int XS_OFF = W_BYTES + X_BYTES + 2 * S_BYTES;
-    static constexpr int STAGE_BYTES = XS_OFF + 1024;
+    static constexpr int STAGE_BYTES = XS_OFF + 2048;
     static constexpr uint32_t TX_BYTES = W_BYTES + X_BYTES + XS_BYTES + (STMA ? 2 * S_BYTES : 0);
     static constexpr int VPT = GROUP / 4;                // values per thread per row per group
     static constexpr int PV = VPT < 16 ? VPT : 16;       // values per piece
@@ -81,9 +89,8 @@ struct Cfg {
     static constexpr int PXCH = PV / 8;                  // 8-value x chunks per piece
     static constexpr int RED_FLOATS = NT * 8 * kRedPitch;
     static constexpr int SMEM_BYTES = kStages * STAGE_BYTES + RED_FLOATS * 4 + 256 + 1024;
-    static constexpr float OFFSET = BITS == 4 ? 128.f : 2176.f;  // magic-number offset per unit x
     static_assert(GPS >= 1 && GPS <= 8 && (8 % GPS) == 0, "stage/group geometry");
-    static_assert(XS_BYTES <= 1024, "x group-sum stage slot");
+    static_assert(XS_BYTES <= 2048, "x group-table stage slot");
     static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte swizzle alignment");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -97,22 +104,19 @@ struct Params {
     int M, N, K, GT, tiles, G;
     long long U;
     int y_vec;
-    // 2^28, 2^24, 2^20: the nibble shifts are high multiplies by these (run-time
-    // values, so they stay multiplies on the FMA pipe).
-    uint32_t mul4, mul8, mul12;
 };
 
 // ------------------------------------------------------------------ workspace layout
 //
 //   [fp32 partial tiles, kMaxCtas x 2 x 16 x 256][tile counters, kMaxTiles]
-//   [x group sums, GT x 16 fp32][x in fragment order, M x K bf16]
+//   [x group table, GT x 64 fp32][x in fragment order, M x K fp16]
 // The partial and counter regions sit at fixed offsets whatever the shape, so one
 // workspace serves calls of any shape; the counters are left zeroed by every call.
 inline size_t partials_bytes() { return (size_t)kMaxCtas * 2 * 16 * kRows * 4; }
 inline size_t counters_bytes() { return (size_t)kMaxTiles * 4; }
 inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 inline size_t xs_offset() { return partials_bytes() + counters_bytes(); }
-inline size_t xperm_offset(int K, int group) { return xs_offset() + round_up((size_t)(K / group) * kXsWidth * 4, 1024); }
+inline size_t xperm_offset(int K, int group) { return xs_offset() + round_up((size_t)(K / group) * kTabWidth * 4, 1024); }
 inline size_t workspace_size(int M, int K, int group) {
     return xperm_offset(K, group) + round_up((size_t)M * K * 2, 1024);
 }
@@ -125,14 +129,18 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 
 // ------------------------------------------------------------------ prep kernel
 //
-// x [M, K] bf16 -> xperm [M, K] with each run of 8 values reordered so that one
+// x [M, K] bf16 -> xperm [M, K] fp16, each run of 8 values reordered so that one
 // 16-byte load gives a thread its four B-fragment registers: 4-bit codes pair k with
 // k+4 ((0,4),(1,5),(2,6),(3,7)), 8-bit codes pair k with k+2 ((0,2),(1,3),(4,6),(5,7)).
-// xs[G][m] = sum of x[m, G*group .. G*group+group-1] in fp32 (rows m >= M are zero).
+// Per (row m, group G) the values are scaled by 2^-e, e >= 0 the smallest exponent that
+// keeps them below 2^15 (e = 0 for any ordinary activation), and the table row G holds
+//   xs[m] = sum_k x,  f[m] = 2^e,  z[m] = sum_k offset_k x
+// with offset_k = 1024 for k even and 64 for k odd (4-bit), 2048 (8-bit); rows m >= M
+// hold xs = z = 0, f = 1.
 template <int BITS>
 __global__ void __launch_bounds__(kPrepThreads) qmm_prep_kernel(const dflash_bf16* __restrict__ x,
-                                                              dflash_bf16* __restrict__ xperm,
-                                                              float* __restrict__ xs, int M, int K, int group) {
+                                                              uint16_t* __restrict__ xperm, float* __restrict__ tab,
+                                                              int M, int K, int group) {
     pdl_launch_dependents();
     pdl_wait();  // the previous call may still be reading this workspace
     const int chunks_per_row = K / 8;
@@ -140,33 +148,63 @@ __global__ void __launch_bounds__(kPrepThreads) qmm_prep_kernel(const dflash_bf1
     const bool live = idx < (long long)kXsWidth * chunks_per_row;
     const int m = live ? (int)(idx / chunks_per_row) : kXsWidth;
     const int c = live ? (int)(idx % chunks_per_row) : 0;
-    float sum = 0.f;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
     if (live && m < M) {
         const uint4 r = *reinterpret_cast<const uint4*>(x + (size_t)m * K + (size_t)c * 8);
-        uint4 o;
-        if constexpr (BITS == 4) {
-            o.x = __byte_perm(r.x, r.z, 0x5410);
-            o.y = __byte_perm(r.x, r.z, 0x7632);
-            o.z = __byte_perm(r.y, r.w, 0x5410);
-            o.w = __byte_perm(r.y, r.w, 0x7632);
-        } else {
-            o.x = __byte_perm(r.x, r.y, 0x5410);
-            o.y = __byte_perm(r.x, r.y, 0x7632);
-            o.z = __byte_perm(r.z, r.w, 0x5410);
-            o.w = __byte_perm(r.z, r.w, 0x7632);
-        }
-        *reinterpret_cast<uint4*>(xperm + (size_t)m * K + (size_t)c * 8) = o;
         const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            sum += __uint_as_float(w[i] << 16);
-            sum += __uint_as_float(w[i] & 0xffff0000u);
+            v[2 * i] = __uint_as_float(w[i] << 16);
+            v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
         }
     }
-    // reduce the group's group/8 consecutive chunks (aligned lanes of one warp)
+    float sum = 0.f, z = 0.f, amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        sum += v[i];
+        amax = fmaxf(amax, fabsf(v[i]));
+        if constexpr (BITS == 4) z = fmaf((i & 1) ? 64.f : 1024.f, v[i], z);
+    }
+    if constexpr (BITS == 8) z = 2048.f * sum;
+    // reduce over the group's group/8 consecutive chunks (aligned lanes of one warp)
     const int lanes = group / 8;
-    for (int off = 1; off < lanes; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    if (live && (c % lanes) == 0) xs[(size_t)(c / lanes) * kXsWidth + m] = sum;
+    for (int off = 1; off < lanes; off <<= 1) {
+        sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        z += __shfl_xor_sync(0xffffffffu, z, off);
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    }
+    int e = 0;
+    if (amax >= 32768.f && amax <= 3.0e38f) e = min(ilogbf(amax) - 14, 120);
+    if (live && m < M) {
+        const float sc = ldexpf(1.f, -e);
+        uint16_t h[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            __half hv = __float2half_rn(v[i] * sc);
+            h[i] = *reinterpret_cast<uint16_t*>(&hv);
+        }
+        uint4 o;
+        if constexpr (BITS == 4) {
+            o.x = h[0] | ((uint32_t)h[4] << 16);
+            o.y = h[1] | ((uint32_t)h[5] << 16);
+            o.z = h[2] | ((uint32_t)h[6] << 16);
+            o.w = h[3] | ((uint32_t)h[7] << 16);
+        } else {
+            o.x = h[0] | ((uint32_t)h[2] << 16);
+            o.y = h[1] | ((uint32_t)h[3] << 16);
+            o.z = h[4] | ((uint32_t)h[6] << 16);
+            o.w = h[5] | ((uint32_t)h[7] << 16);
+        }
+        *reinterpret_cast<uint4*>(xperm + (size_t)m * K + (size_t)c * 8) = o;
+    }
+    if (live && (c % lanes) == 0) {
+        float* row = tab + (size_t)(c / lanes) * kTabWidth;
+        row[m] = sum;
+        row[16 + m] = ldexpf(1.f, e);
+        row[32 + m] = z;
+    }
 }
 
 // ------------------------------------------------------------------ main kernel helpers
@@ -178,22 +216,11 @@ __device__ __forceinline__ long long range_begin(long long c, const Params& p) {
     return c * p.U / p.G;
 }
 
-__device__ __forceinline__ uint32_t bf16x2_times16(uint32_t v) {
-    __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&v);
-    h = __hmul2(h, __floats2bfloat162_rn(16.f, 16.f));
-    return *reinterpret_cast<uint32_t*>(&h);
-}
-
-constexpr uint32_t kMagic = 0x43004300u;   // bf16x2 (128.0, 128.0)
-constexpr uint32_t kNib = 0x000F000Fu;
-
-// (v >> 4q) as a high multiply: v * 2^(32-4q) >> 32.
-__device__ __forceinline__ uint32_t shr_nib(uint32_t v, int q, const Params& p) {
-    if (q == 0) return v;
-    const uint32_t mul = q == 1 ? p.mul4 : (q == 2 ? p.mul8 : p.mul12);
-    return __umulhi(v, mul);
-}
-__device__ __forceinline__ uint32_t magic(uint32_t v) { return (v & kNib) | kMagic; }
+constexpr uint32_t kLoNib = 0x000F000Fu;      // nibble in bits 0-3 of each 16-bit lane
+constexpr uint32_t kHiNib = 0x00F000F0u;      // nibble in bits 4-7 of each 16-bit lane
+constexpr uint32_t kMag1024 = 0x64006400u;    // fp16x2 (1024, 1024): + nibble in bits 0-3 (4-7: +16q)
+constexpr uint32_t kMag64 = 0x54005400u;      // fp16x2 (64, 64): + nibble in bits 4-7
+__device__ __forceinline__ uint32_t unpack(uint32_t v, uint32_t mask, uint32_t mag) { return (v & mask) | mag; }
 
 // Fragment row g of 16-row block i of a warp's 32-feature slice maps to feature row
 //     rb + 16 i + 2 sigma(g) + h        (h = 0: fragment rows 0..7, h = 1: rows 8..15)
@@ -266,23 +293,23 @@ __device__ __forceinline__ void lds_words(uint32_t* dst, uint32_t addr) {
     }
 }
 
-// D = A * B (accumulator starts at zero), m16n8k16 bf16 -> fp32.
-__device__ __forceinline__ void mma_bf16_16816_zero(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                                    uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %10, %10, %10};"
-        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
-}
-
+// D = A * B (+ D unless FIRST), m16n8k16 fp16 -> fp32.
 template <bool FIRST>
 __device__ __forceinline__ void mma_step(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-    if constexpr (FIRST)
-        mma_bf16_16816_zero(d, a0, a1, a2, a3, b0, b1);
-    else
-        mma_bf16_16816(d, a0, a1, a2, a3, b0, b1);
+    if constexpr (FIRST) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+            "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %10, %10, %10};"
+            : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+            "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    }
 }
 
 // One quantization group (index gl within the stage) for one consumer warp:
@@ -320,13 +347,15 @@ __device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const uint
         for (int s = 0; s < C::PSTEPS; ++s) {
             const bool first = (pc == 0 && s == 0);
             if constexpr (C::BITS == 4) {
+                // word w of the piece: step 2w uses nibbles (0,4) and (1,5), step 2w+1
+                // nibbles (2,6) and (3,7) of the word shifted right by 8.
                 const int w = s >> 1, q = (s & 1) * 2;
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {
-                    const uint32_t a0 = magic(shr_nib(wv[i][0][w], q, p));
-                    const uint32_t a1 = magic(shr_nib(wv[i][1][w], q, p));
-                    const uint32_t a2 = magic(shr_nib(wv[i][0][w], q + 1, p));
-                    const uint32_t a3 = magic(shr_nib(wv[i][1][w], q + 1, p));
+                    const uint32_t v0 = q ? (wv[i][0][w] >> 8) : wv[i][0][w];
+                    const uint32_t v1 = q ? (wv[i][1][w] >> 8) : wv[i][1][w];
+                    const uint32_t a0 = unpack(v0, kLoNib, kMag1024), a1 = unpack(v1, kLoNib, kMag1024);
+                    const uint32_t a2 = unpack(v0, kHiNib, kMag64), a3 = unpack(v1, kHiNib, kMag64);
 #pragma unroll
                     for (int j = 0; j < C::NT; ++j) {
                         const uint32_t b0 = xf[j][w][q], b1 = xf[j][w][q + 1];
@@ -335,41 +364,43 @@ __device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const uint
                     }
                 }
             } else {
+                // word s: bytes (0,2) in place and bytes (1,3) shifted right by 8; the low
+                // nibbles read 1024 + q_lo, the high ones 1024 + 16 q_hi, both against x.
                 const int w = s, c = s >> 1, q = (s & 1) * 2;
-                uint32_t h0[C::NT], h1[C::NT];
-#pragma unroll
-                for (int j = 0; j < C::NT; ++j) {
-                    h0[j] = bf16x2_times16(xf[j][c][q]);
-                    h1[j] = bf16x2_times16(xf[j][c][q + 1]);
-                }
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {
                     const uint32_t w0 = wv[i][0][w], w1 = wv[i][1][w];
-                    const uint32_t l0 = magic(w0), l1 = magic(w1);
-                    const uint32_t l2 = magic(shr_nib(w0, 2, p)), l3 = magic(shr_nib(w1, 2, p));
-                    const uint32_t u0 = magic(shr_nib(w0, 1, p)), u1 = magic(shr_nib(w1, 1, p));
-                    const uint32_t u2 = magic(shr_nib(w0, 3, p)), u3 = magic(shr_nib(w1, 3, p));
+                    const uint32_t t0 = w0 >> 8, t1 = w1 >> 8;
+                    const uint32_t l0 = unpack(w0, kLoNib, kMag1024), l1 = unpack(w1, kLoNib, kMag1024);
+                    const uint32_t l2 = unpack(t0, kLoNib, kMag1024), l3 = unpack(t1, kLoNib, kMag1024);
+                    const uint32_t u0 = unpack(w0, kHiNib, kMag1024), u1 = unpack(w1, kHiNib, kMag1024);
+                    const uint32_t u2 = unpack(t0, kHiNib, kMag1024), u3 = unpack(t1, kHiNib, kMag1024);
 #pragma unroll
                     for (int j = 0; j < C::NT; ++j) {
                         const uint32_t b0 = xf[j][c][q], b1 = xf[j][c][q + 1];
                         if (first) mma_step<true>(tmp[i][j], l0, l1, l2, l3, b0, b1);
                         else mma_step<false>(tmp[i][j], l0, l1, l2, l3, b0, b1);
-                        mma_bf16_16816(tmp[i][j], u0, u1, u2, u3, h0[j], h1[j]);
+                        mma_step<false>(tmp[i][j], u0, u1, u2, u3, b0, b1);
                     }
                 }
             }
         }
     }
 
-    // x group sums for this thread's output columns m = 8j + 2tq, 8j + 2tq + 1
-    float xs[C::NT][2];
+    // group table for this thread's output columns m = 8j + 2tq, 8j + 2tq + 1
+    float xs[C::NT][2], xf2[C::NT][2], zz[C::NT][2];
 #pragma unroll
     for (int j = 0; j < C::NT; ++j) {
-        const uint2 v = lds64(xsb + (gl * C::XROWS + 8 * j) * 4);
-        xs[j][0] = __uint_as_float(v.x);
-        xs[j][1] = __uint_as_float(v.y);
+        const uint32_t a = xsb + (gl * C::TAB_ROW + 8 * j) * 4;
+        const uint2 v0 = lds64(a), v1 = lds64(a + 16 * 4), v2 = lds64(a + 32 * 4);
+        xs[j][0] = __uint_as_float(v0.x);
+        xs[j][1] = __uint_as_float(v0.y);
+        xf2[j][0] = __uint_as_float(v1.x);
+        xf2[j][1] = __uint_as_float(v1.y);
+        zz[j][0] = __uint_as_float(v2.x);
+        zz[j][1] = __uint_as_float(v2.y);
     }
-    // acc += s * tmp + (b - OFFSET * s) * xs, per feature row.
+    // acc += (s f) tmp + b xs - s z, per feature row.
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
@@ -390,12 +421,16 @@ __device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const uint
                     b = 0.f;
                 }
             }
-            const float bb = fmaf(-C::OFFSET, s, b);
 #pragma unroll
             for (int j = 0; j < C::NT; ++j)
 #pragma unroll
-                for (int e = 0; e < 2; ++e)
-                    acc[i][j][2 * h + e] = fmaf(s, tmp[i][j][2 * h + e], fmaf(bb, xs[j][e], acc[i][j][2 * h + e]));
+                for (int e = 0; e < 2; ++e) {
+                    float a = acc[i][j][2 * h + e];
+                    a = fmaf(s * xf2[j][e], tmp[i][j][2 * h + e], a);
+                    a = fmaf(b, xs[j][e], a);
+                    a = fmaf(-s, zz[j][e], a);
+                    acc[i][j][2 * h + e] = a;
+                }
         }
 }
 
@@ -708,7 +743,7 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
 
     uint8_t* wsb = reinterpret_cast<uint8_t*>(ws);
     float* xs = reinterpret_cast<float*>(wsb + xs_offset());
-    dflash_bf16* xperm = reinterpret_cast<dflash_bf16*>(wsb + xperm_offset(s.K, s.group));
+    uint16_t* xperm = reinterpret_cast<uint16_t*>(wsb + xperm_offset(s.K, s.group));
     const int GT = s.K / s.group;
 
     CUtensorMap tm_w, tm_x, tm_s, tm_b, tm_xs;
@@ -717,11 +752,11 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
     st = encode_tensor_map_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, words, (uint64_t)s.N, words * 4,
                               kRowBytes / 4, kRows, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
-    st = encode_tensor_map_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xperm, (uint64_t)s.K, (uint64_t)s.M,
+    st = encode_tensor_map_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xperm, (uint64_t)s.K, (uint64_t)s.M,
                               (uint64_t)s.K * 2, 64, C::XROWS, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
-    st = encode_tensor_map_2d(&tm_xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xs, kXsWidth, (uint64_t)GT, kXsWidth * 4,
-                              C::XROWS, C::GPS, CU_TENSOR_MAP_SWIZZLE_NONE);
+    st = encode_tensor_map_2d(&tm_xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xs, kTabWidth, (uint64_t)GT, kTabWidth * 4,
+                              C::TAB_ROW, C::GPS, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
     if constexpr (C::STMA) {
         st = encode_tensor_map_2d(&tm_s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, scales, (uint64_t)GT, (uint64_t)s.N,
@@ -754,9 +789,6 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
     if (G > p.U) G = p.U;
     p.G = (int)G;
     p.y_vec = (s.N % 8 == 0) && aligned16(y);
-    p.mul4 = 1u << 28;
-    p.mul8 = 1u << 24;
-    p.mul12 = 1u << 20;
 
     const long long prep_threads = (long long)kXsWidth * (s.K / 8);
     const int prep_blocks = (int)((prep_threads + kPrepThreads - 1) / kPrepThreads);
