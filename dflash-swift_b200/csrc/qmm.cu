@@ -87,6 +87,11 @@ struct Cfg {
     static constexpr int PW = PB / 4;                    // 32-bit words per piece per row
     static constexpr int PSTEPS = PV / 4;                // k16 MMA steps per piece
     static constexpr int PXCH = PV / 8;                  // 8-value x chunks per piece
+    // Two warps share each 32-feature slice.  With at least two groups per stage they
+    // split the stage's groups (even / odd) and every consumer warp takes every stage;
+    // with one group per stage they take alternate stages.
+    static constexpr bool SPLIT = GPS >= 2;
+    static constexpr int EMPTY_ARRIVALS = SPLIT ? kConsumerWarps : kRowSlices;
     static constexpr int RED_FLOATS = NT * 8 * kRedPitch;
     static constexpr int SMEM_BYTES = kStages * STAGE_BYTES + RED_FLOATS * 4 + 256 + 1024;
     static_assert(GPS >= 1 && GPS <= 8 && (8 % GPS) == 0, "stage/group geometry");
@@ -220,7 +225,36 @@ constexpr uint32_t kLoNib = 0x000F000Fu;      // nibble in bits 0-3 of each 16-b
 constexpr uint32_t kHiNib = 0x00F000F0u;      // nibble in bits 4-7 of each 16-bit lane
 constexpr uint32_t kMag1024 = 0x64006400u;    // fp16x2 (1024, 1024): + nibble in bits 0-3 (4-7: +16q)
 constexpr uint32_t kMag64 = 0x54005400u;      // fp16x2 (64, 64): + nibble in bits 4-7
-__device__ __forceinline__ uint32_t unpack(uint32_t v, uint32_t mask, uint32_t mag) { return (v & mask) | mag; }
+// (v & mask) | mag as one LOP3: the mask is an immediate, the magic a register (left
+// to itself the compiler splits this into an AND and an OR with two immediates, which
+// doubles the load on the ALU pipe that bounds this kernel).
+template <uint32_t MASK>
+__device__ __forceinline__ uint32_t unpack(uint32_t v, uint32_t mag) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(v), "n"(MASK), "r"(mag));
+    return d;
+}
+// A constant the compiler cannot fold, so it stays in a register.
+template <uint32_t V>
+__device__ __forceinline__ uint32_t pinned() {
+    uint32_t d;
+    asm volatile("mov.b32 %0, %1;" : "=r"(d) : "n"(V));
+    return d;
+}
+// bf16 bits -> fp32 as an integer multiply (FMA pipe) by a register holding 65536.
+__device__ __forceinline__ float bf16_to_f32_fma(uint32_t b, uint32_t k65536) {
+    uint32_t d;
+    asm("mul.lo.u32 %0, %1, %2;" : "=r"(d) : "r"(b), "r"(k65536));
+    return __uint_as_float(d);
+}
+
+// Registers pinned for the unpack and the scale conversion.
+struct Pinned {
+    uint32_t mag1024, mag64, k65536;
+};
+__device__ __forceinline__ Pinned make_pinned() {
+    return Pinned{pinned<kMag1024>(), pinned<kMag64>(), pinned<65536u>()};
+}
 
 // Fragment row g of 16-row block i of a warp's 32-feature slice maps to feature row
 //     rb + 16 i + 2 sigma(g) + h        (h = 0: fragment rows 0..7, h = 1: rows 8..15)
@@ -317,9 +351,9 @@ __device__ __forceinline__ void mma_step(float (&d)[4], uint32_t a0, uint32_t a1
 // sb[h] = scale-tile address of row[h] at this stage's group 0; xsb = this thread's
 // x group-sum slot (group 0, n-tile 0) in the stage.
 template <class C>
-__device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const uint32_t (&wb)[2], uint32_t xb,
-                                              const uint32_t (&sb)[2], uint32_t xsb, int gl, int G, int tile_row0,
-                                              const Params& p, float (&acc)[2][C::NT][4]) {
+__device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const Pinned& P, const uint32_t (&wb)[2],
+                                              uint32_t xb, const uint32_t (&sb)[2], uint32_t xsb, int gl, int G,
+                                              int tile_row0, const Params& p, float (&acc)[2][C::NT][4]) {
     float tmp[2][C::NT][4];
 #pragma unroll
     for (int pc = 0; pc < C::PIECES; ++pc) {
@@ -354,8 +388,8 @@ __device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const uint
                 for (int i = 0; i < 2; ++i) {
                     const uint32_t v0 = q ? (wv[i][0][w] >> 8) : wv[i][0][w];
                     const uint32_t v1 = q ? (wv[i][1][w] >> 8) : wv[i][1][w];
-                    const uint32_t a0 = unpack(v0, kLoNib, kMag1024), a1 = unpack(v1, kLoNib, kMag1024);
-                    const uint32_t a2 = unpack(v0, kHiNib, kMag64), a3 = unpack(v1, kHiNib, kMag64);
+                    const uint32_t a0 = unpack<kLoNib>(v0, P.mag1024), a1 = unpack<kLoNib>(v1, P.mag1024);
+                    const uint32_t a2 = unpack<kHiNib>(v0, P.mag64), a3 = unpack<kHiNib>(v1, P.mag64);
 #pragma unroll
                     for (int j = 0; j < C::NT; ++j) {
                         const uint32_t b0 = xf[j][w][q], b1 = xf[j][w][q + 1];
@@ -371,10 +405,10 @@ __device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const uint
                 for (int i = 0; i < 2; ++i) {
                     const uint32_t w0 = wv[i][0][w], w1 = wv[i][1][w];
                     const uint32_t t0 = w0 >> 8, t1 = w1 >> 8;
-                    const uint32_t l0 = unpack(w0, kLoNib, kMag1024), l1 = unpack(w1, kLoNib, kMag1024);
-                    const uint32_t l2 = unpack(t0, kLoNib, kMag1024), l3 = unpack(t1, kLoNib, kMag1024);
-                    const uint32_t u0 = unpack(w0, kHiNib, kMag1024), u1 = unpack(w1, kHiNib, kMag1024);
-                    const uint32_t u2 = unpack(t0, kHiNib, kMag1024), u3 = unpack(t1, kHiNib, kMag1024);
+                    const uint32_t l0 = unpack<kLoNib>(w0, P.mag1024), l1 = unpack<kLoNib>(w1, P.mag1024);
+                    const uint32_t l2 = unpack<kLoNib>(t0, P.mag1024), l3 = unpack<kLoNib>(t1, P.mag1024);
+                    const uint32_t u0 = unpack<kHiNib>(w0, P.mag1024), u1 = unpack<kHiNib>(w1, P.mag1024);
+                    const uint32_t u2 = unpack<kHiNib>(t0, P.mag1024), u3 = unpack<kHiNib>(t1, P.mag1024);
 #pragma unroll
                     for (int j = 0; j < C::NT; ++j) {
                         const uint32_t b0 = xf[j][c][q], b1 = xf[j][c][q + 1];
@@ -400,7 +434,7 @@ __device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const uint
         zz[j][0] = __uint_as_float(v2.x);
         zz[j][1] = __uint_as_float(v2.y);
     }
-    // acc += (s f) tmp + b xs - s z, per feature row.
+    // acc += s (f tmp - z) + b xs, per feature row.
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
@@ -408,8 +442,8 @@ __device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const uint
             float s, b;
             if constexpr (C::STMA) {
                 const uint32_t a = sb[h] + i * 16 * 16 + 2 * gl;
-                s = bf16_bits_to_float(lds16(a));
-                b = bf16_bits_to_float(lds16(a + C::S_BYTES));
+                s = bf16_to_f32_fma(lds16(a), P.k65536);
+                b = bf16_to_f32_fma(lds16(a + C::S_BYTES), P.k65536);
             } else {
                 const int n = tile_row0 + L.row[h] + 16 * i;
                 if (n < p.N) {
@@ -425,20 +459,19 @@ __device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const uint
             for (int j = 0; j < C::NT; ++j)
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    float a = acc[i][j][2 * h + e];
-                    a = fmaf(s * xf2[j][e], tmp[i][j][2 * h + e], a);
-                    a = fmaf(b, xs[j][e], a);
-                    a = fmaf(-s, zz[j][e], a);
-                    acc[i][j][2 * h + e] = a;
+                    const float t = fmaf(xf2[j][e], tmp[i][j][2 * h + e], -zz[j][e]);
+                    acc[i][j][2 * h + e] = fmaf(s, t, fmaf(b, xs[j][e], acc[i][j][2 * h + e]));
                 }
         }
 }
 
-// All groups of one stage.  CHECK: the stage is the first or last of a segment and
-// some of its groups fall outside [ga, gb).
-template <class C, bool CHECK>
-__device__ __forceinline__ void consume_stage(const LaneLayout<C>& L, uint32_t st, int sc, int ga, int gb, int tq,
-                                              int tile_row0, const Params& p, float (&acc)[2][C::NT][4]) {
+// This warp's groups of one stage: all of them (PAR < 0) or those with gl % 2 == PAR.
+// CHECK: the stage is the first or last of a segment and some of its groups fall
+// outside [ga, gb).
+template <class C, bool CHECK, int PAR>
+__device__ __forceinline__ void consume_stage(const LaneLayout<C>& L, const Pinned& P, uint32_t st, int sc, int ga,
+                                              int gb, int tq, int tile_row0, const Params& p,
+                                              float (&acc)[2][C::NT][4]) {
     const uint32_t wb[2] = {st + L.wofs[0], st + L.wofs[1]};
     const uint32_t xb = st + C::W_BYTES;
     const uint32_t s0 = st + C::W_BYTES + C::X_BYTES + 2 * ((sc * C::GPS) & 7);
@@ -446,9 +479,10 @@ __device__ __forceinline__ void consume_stage(const LaneLayout<C>& L, uint32_t s
     const uint32_t xsb = st + C::XS_OFF + 2 * tq * 4;
 #pragma unroll
     for (int gl = 0; gl < C::GPS; ++gl) {
+        if (PAR >= 0 && (gl & 1) != PAR) continue;
         const int G = sc * C::GPS + gl;
         if (CHECK && (G < ga || G >= gb)) continue;
-        consume_group<C>(L, wb, xb, sb, xsb, gl, G, tile_row0, p, acc);
+        consume_group<C>(L, P, wb, xb, sb, xsb, gl, G, tile_row0, p, acc);
     }
 }
 
@@ -492,17 +526,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * C::STAGE_BYTES + C::RED_FLOATS * 4);
     uint64_t* empty = full + kStages;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
-    volatile int* last_flag = abort_flag + 1;
+    volatile int* fin_flag = abort_flag + 1;
 
     pdl_launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kRowSlices);
+            mbar_init(&empty[s], C::EMPTY_ARRIVALS);
         }
         *abort_flag = 0;
-        *last_flag = 0;
+        *fin_flag = 0;
         fence_barrier_init();
     }
     __syncthreads();
@@ -588,6 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int g = lane >> 2, tq = lane & 3;
     const int rb = rs * 32;
     const LaneLayout<C> L = lane_layout<C>(rb, g, tq);
+    const Pinned P = make_pinned();
     const int ctid = threadIdx.x;  // 0 .. kConsumerThreads-1
     int j = 0;
 
@@ -606,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int e = 0; e < 4; ++e) acc[i][jj][e] = 0.f;
 
         for (int sc = ga / C::GPS; sc < (gb + C::GPS - 1) / C::GPS; ++sc, ++j) {
-            if ((j % kKSplit) != par) continue;
+            if (!C::SPLIT && (j % kKSplit) != par) continue;
             const int slot = j % kStages;
             const uint32_t ph = (uint32_t)(j / kStages) & 1u;
             // mma.sync below is warp-collective: every lane must take the same branch
@@ -614,10 +649,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                                        DFLASH_DEVERR_QMM_PIPELINE));
             if (ok) {
                 const uint32_t st = smem_u32(smem + slot * C::STAGE_BYTES);
-                if (sc * C::GPS >= ga && sc * C::GPS + C::GPS <= gb)
-                    consume_stage<C, false>(L, st, sc, ga, gb, tq, tile_row0, p, acc);
-                else
-                    consume_stage<C, true>(L, st, sc, ga, gb, tq, tile_row0, p, acc);
+                const bool whole = sc * C::GPS >= ga && sc * C::GPS + C::GPS <= gb;
+                if constexpr (C::SPLIT) {
+                    if (par == 0) {
+                        if (whole) consume_stage<C, false, 0>(L, P, st, sc, ga, gb, tq, tile_row0, p, acc);
+                        else consume_stage<C, true, 0>(L, P, st, sc, ga, gb, tq, tile_row0, p, acc);
+                    } else {
+                        if (whole) consume_stage<C, false, 1>(L, P, st, sc, ga, gb, tq, tile_row0, p, acc);
+                        else consume_stage<C, true, 1>(L, P, st, sc, ga, gb, tq, tile_row0, p, acc);
+                    }
+                } else {
+                    if (whole) consume_stage<C, false, -1>(L, P, st, sc, ga, gb, tq, tile_row0, p, acc);
+                    else consume_stage<C, true, -1>(L, P, st, sc, ga, gb, tq, tile_row0, p, acc);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
@@ -653,48 +697,61 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ga == 0 && gb == p.GT) {
             write_tile<C>(red, t, p, ctid);
         } else {
-            // ---- stream-K: publish this CTA's partial, the last contributor finishes
-            const int slot = (t == first_tile) ? 0 : 1;
+            // ---- stream-K fixup.  The tile's contributors are CTAs cf..cl with
+            // contiguous ranges; the lowest, cf, holds the tile as its last segment and
+            // so reaches it last (a middle CTA, whose whole range lies in the tile, at
+            // about the same time; cl, for which it is the first segment, long before).
+            // cf therefore finishes: it waits (bounded) for the others' release-adds,
+            // then sums their partials onto its own in a fixed order.  The others publish
+            // a partial and move on without waiting.
             constexpr int TILE_FLOATS = C::NT * 8 * kRows;
-            float* dst = p.partials + (size_t)(c * 2 + slot) * TILE_FLOATS;
-            for (int idx = ctid; idx < TILE_FLOATS / 4; idx += kConsumerThreads) {
-                const int m = idx / (kRows / 4), r4 = (idx % (kRows / 4)) * 4;
-                __stcg(reinterpret_cast<float4*>(dst + m * kRows + r4),
-                       *reinterpret_cast<const float4*>(red + m * kRedPitch + r4));
-            }
-            __threadfence();
-            named_bar_sync(kBarConsumers, kConsumerThreads);
             const long long cf = owner_of((long long)t * p.GT, p);
             const long long cl = owner_of((long long)(t + 1) * p.GT - 1, p);
-            if (ctid == 0) {
-                const int need = (int)(cl - cf + 1);
-                const int old = atomicAdd(p.counters + t, 1);
-                const int last = (old == need - 1);
-                if (old >= need) atomicOr(&g_device_error, DFLASH_DEVERR_QMM_REDUCE);
-                if (last) {
-                    atomicExch(p.counters + t, 0);
-                    __threadfence();
-                }
-                *last_flag = last;
-            }
-            named_bar_sync(kBarConsumers, kConsumerThreads);
-            if (*last_flag) {
+            if (c != cf) {
+                const int slot = (t == first_tile) ? 0 : 1;
+                float* dst = p.partials + (size_t)(c * 2 + slot) * TILE_FLOATS;
                 for (int idx = ctid; idx < TILE_FLOATS / 4; idx += kConsumerThreads) {
                     const int m = idx / (kRows / 4), r4 = (idx % (kRows / 4)) * 4;
-                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (long long cc = cf; cc <= cl; ++cc) {
-                        const int sl = ((int)(range_begin(cc, p) / p.GT) == t) ? 0 : 1;
-                        const float4 q = __ldcg(reinterpret_cast<const float4*>(
-                            p.partials + (size_t)(cc * 2 + sl) * TILE_FLOATS + m * kRows + r4));
-                        v.x += q.x;
-                        v.y += q.y;
-                        v.z += q.z;
-                        v.w += q.w;
-                    }
-                    *reinterpret_cast<float4*>(red + m * kRedPitch + r4) = v;
+                    __stcg(reinterpret_cast<float4*>(dst + m * kRows + r4),
+                           *reinterpret_cast<const float4*>(red + m * kRedPitch + r4));
                 }
                 named_bar_sync(kBarConsumers, kConsumerThreads);
-                write_tile<C>(red, t, p, ctid);
+                if (ctid == 0) red_release_add(p.counters + t, 1);
+            } else {
+                if (ctid == 0) {
+                    const int need = (int)(cl - cf);
+                    const unsigned long long t0 = globaltimer_ns();
+                    int seen = ld_acquire(p.counters + t);
+                    while (seen < need) {
+                        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                            atomicOr(&g_device_error, DFLASH_DEVERR_QMM_REDUCE);
+                            break;
+                        }
+                        seen = ld_acquire(p.counters + t);
+                    }
+                    if (seen > need) atomicOr(&g_device_error, DFLASH_DEVERR_QMM_REDUCE);
+                    *fin_flag = (seen == need);
+                    p.counters[t] = 0;  // every contributor has arrived: ready for the next call
+                }
+                named_bar_sync(kBarConsumers, kConsumerThreads);
+                if (*fin_flag) {
+                    for (int idx = ctid; idx < TILE_FLOATS / 4; idx += kConsumerThreads) {
+                        const int m = idx / (kRows / 4), r4 = (idx % (kRows / 4)) * 4;
+                        float4 v = *reinterpret_cast<const float4*>(red + m * kRedPitch + r4);
+                        for (long long cc = cf + 1; cc <= cl; ++cc) {
+                            const int sl = ((int)(range_begin(cc, p) / p.GT) == t) ? 0 : 1;
+                            const float4 q = __ldcg(reinterpret_cast<const float4*>(
+                                p.partials + (size_t)(cc * 2 + sl) * TILE_FLOATS + m * kRows + r4));
+                            v.x += q.x;
+                            v.y += q.y;
+                            v.z += q.z;
+                            v.w += q.w;
+                        }
+                        *reinterpret_cast<float4*>(red + m * kRedPitch + r4) = v;
+                    }
+                    named_bar_sync(kBarConsumers, kConsumerThreads);
+                    write_tile<C>(red, t, p, ctid);
+                }
             }
         }
         named_bar_sync(kBarConsumers, kConsumerThreads);
