@@ -41,6 +41,7 @@ NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 1024 * 1024
 PROFILE_SUMMARY = ROOT / "profiles" / "qmm_m8_k5120_n17408_4b_g64.json"
+KERNELS_PER_CALL = 3  # prep (x to fragment order + group sums), main (weight stream), fixup (split tiles)
 
 
 def algorithmic_bytes(m: int, n: int = N, k: int = K, group: int = GROUP, bits: int = BITS) -> int:
@@ -280,7 +281,7 @@ def run_ours(args):
                     "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
                     "us_per_step": round(e2e["ms"] * 1e3 / args.steps, 3),
                     "path": "pinned host x -> dflash_qmm (C ABI via ctypes) -> pinned host y, per step"},
-            "gpu_launches": args.steps,
+            "gpu_launches": KERNELS_PER_CALL * args.steps,
             "clocks": clocks,
             "parity_closeness_before_timing": err,
         }

@@ -5,17 +5,18 @@
 // packed weight stream (M <= 16 rows against N*K quantized weights), so everything is
 // arranged to move those bytes from HBM exactly once at full bandwidth:
 //
-//  * Two kernels per call, chained with programmatic dependent launch (PDL).  A tiny
-//    prep kernel writes x, permuted into MMA fragment order, and the fp32 group sums
-//    of x into the workspace.  The main kernel starts streaming weights, scales and
-//    biases before its grid dependency resolves (they are never written by the
-//    preceding kernels), so consecutive calls overlap launch latency and pipeline
-//    fill with the previous call's tail.
+//  * Three kernels per call, chained with programmatic dependent launch (PDL).  A tiny
+//    prep kernel writes x, permuted into MMA fragment order, and per-group x sums into
+//    the workspace.  The main kernel starts streaming weights, scales and biases before
+//    its grid dependency resolves (they are never written by the preceding kernels),
+//    so consecutive calls overlap launch latency and pipeline fill with the previous
+//    call's tail.  A fixup kernel sums the partials of row tiles cut between CTAs.
 //  * Persistent grid, one CTA per SM.  The weight matrix is cut into row tiles of 256
 //    output features; the (row tile, quantization group) pairs are split into equal
-//    contiguous ranges, one per CTA (stream-K).  A row tile cut between CTAs is
-//    finished by the last CTA to arrive (fp32 partials in the workspace, fixed
-//    summation order, so results are deterministic).
+//    contiguous ranges, one per CTA (stream-K).  A CTA writes a row tile it covers
+//    whole straight to y; for a tile cut between CTAs it publishes an fp32 partial and
+//    moves on without waiting, and the fixup kernel adds the partials in a fixed order
+//    (results are deterministic).
 //  * One producer thread issues TMA tile loads (cp.async.bulk.tensor, no multicast)
 //    into a 4-deep shared-memory ring: per stage a [256 rows x 128 B] weight box with
 //    128-byte swizzle, the matching x columns and x group sums, and the scale/bias
@@ -105,7 +106,6 @@ struct Params {
     const dflash_bf16* scales;
     const dflash_bf16* biases;
     float* partials;
-    int* counters;
     int M, N, K, GT, tiles, G;
     long long U;
     int y_vec;
@@ -113,14 +113,13 @@ struct Params {
 
 // ------------------------------------------------------------------ workspace layout
 //
-//   [fp32 partial tiles, kMaxCtas x 2 x 16 x 256][tile counters, kMaxTiles]
+//   [fp32 partial tiles, kMaxCtas x 2 x 16 x 256]
 //   [x group table, GT x 64 fp32][x in fragment order, M x K fp16]
-// The partial and counter regions sit at fixed offsets whatever the shape, so one
-// workspace serves calls of any shape; the counters are left zeroed by every call.
+// Every region is rewritten by each call before it is read, so one workspace serves
+// calls of any shape and needs no initialisation.
 inline size_t partials_bytes() { return (size_t)kMaxCtas * 2 * 16 * kRows * 4; }
-inline size_t counters_bytes() { return (size_t)kMaxTiles * 4; }
 inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
-inline size_t xs_offset() { return partials_bytes() + counters_bytes(); }
+inline size_t xs_offset() { return partials_bytes(); }
 inline size_t xperm_offset(int K, int group) { return xs_offset() + round_up((size_t)(K / group) * kTabWidth * 4, 1024); }
 inline size_t workspace_size(int M, int K, int group) {
     return xperm_offset(K, group) + round_up((size_t)M * K * 2, 1024);
@@ -526,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * C::STAGE_BYTES + C::RED_FLOATS * 4);
     uint64_t* empty = full + kStages;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
-    volatile int* fin_flag = abort_flag + 1;
+
 
     pdl_launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -536,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&empty[s], C::EMPTY_ARRIVALS);
         }
         *abort_flag = 0;
-        *fin_flag = 0;
+
         fence_barrier_init();
     }
     __syncthreads();
@@ -697,65 +696,60 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ga == 0 && gb == p.GT) {
             write_tile<C>(red, t, p, ctid);
         } else {
-            // ---- stream-K fixup.  The tile's contributors are CTAs cf..cl with
-            // contiguous ranges; the lowest, cf, holds the tile as its last segment and
-            // so reaches it last (a middle CTA, whose whole range lies in the tile, at
-            // about the same time; cl, for which it is the first segment, long before).
-            // cf therefore finishes: it waits (bounded) for the others' release-adds,
-            // then sums their partials onto its own in a fixed order.  The others publish
-            // a partial and move on without waiting.
+            // ---- a tile cut between CTAs: publish this CTA's share as an fp32 partial
+            // in its slot (0: the tile is this CTA's first segment, 1: its last); the
+            // fixup kernel adds the contributors' partials in CTA order.
             constexpr int TILE_FLOATS = C::NT * 8 * kRows;
-            const long long cf = owner_of((long long)t * p.GT, p);
-            const long long cl = owner_of((long long)(t + 1) * p.GT - 1, p);
-            if (c != cf) {
-                const int slot = (t == first_tile) ? 0 : 1;
-                float* dst = p.partials + (size_t)(c * 2 + slot) * TILE_FLOATS;
-                for (int idx = ctid; idx < TILE_FLOATS / 4; idx += kConsumerThreads) {
-                    const int m = idx / (kRows / 4), r4 = (idx % (kRows / 4)) * 4;
-                    __stcg(reinterpret_cast<float4*>(dst + m * kRows + r4),
-                           *reinterpret_cast<const float4*>(red + m * kRedPitch + r4));
-                }
-                named_bar_sync(kBarConsumers, kConsumerThreads);
-                if (ctid == 0) red_release_add(p.counters + t, 1);
-            } else {
-                if (ctid == 0) {
-                    const int need = (int)(cl - cf);
-                    const unsigned long long t0 = globaltimer_ns();
-                    int seen = ld_acquire(p.counters + t);
-                    while (seen < need) {
-                        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                            atomicOr(&g_device_error, DFLASH_DEVERR_QMM_REDUCE);
-                            break;
-                        }
-                        seen = ld_acquire(p.counters + t);
-                    }
-                    if (seen > need) atomicOr(&g_device_error, DFLASH_DEVERR_QMM_REDUCE);
-                    *fin_flag = (seen == need);
-                    p.counters[t] = 0;  // every contributor has arrived: ready for the next call
-                }
-                named_bar_sync(kBarConsumers, kConsumerThreads);
-                if (*fin_flag) {
-                    for (int idx = ctid; idx < TILE_FLOATS / 4; idx += kConsumerThreads) {
-                        const int m = idx / (kRows / 4), r4 = (idx % (kRows / 4)) * 4;
-                        float4 v = *reinterpret_cast<const float4*>(red + m * kRedPitch + r4);
-                        for (long long cc = cf + 1; cc <= cl; ++cc) {
-                            const int sl = ((int)(range_begin(cc, p) / p.GT) == t) ? 0 : 1;
-                            const float4 q = __ldcg(reinterpret_cast<const float4*>(
-                                p.partials + (size_t)(cc * 2 + sl) * TILE_FLOATS + m * kRows + r4));
-                            v.x += q.x;
-                            v.y += q.y;
-                            v.z += q.z;
-                            v.w += q.w;
-                        }
-                        *reinterpret_cast<float4*>(red + m * kRedPitch + r4) = v;
-                    }
-                    named_bar_sync(kBarConsumers, kConsumerThreads);
-                    write_tile<C>(red, t, p, ctid);
-                }
+            const int slot = (t == first_tile) ? 0 : 1;
+            float* dst = p.partials + (size_t)(c * 2 + slot) * TILE_FLOATS;
+            for (int idx = ctid; idx < TILE_FLOATS / 4; idx += kConsumerThreads) {
+                const int m = idx / (kRows / 4), r4 = (idx % (kRows / 4)) * 4;
+                __stcg(reinterpret_cast<float4*>(dst + m * kRows + r4),
+                       *reinterpret_cast<const float4*>(red + m * kRedPitch + r4));
             }
         }
         named_bar_sync(kBarConsumers, kConsumerThreads);
         u = (long long)t * p.GT + gb;
+    }
+}
+
+// ------------------------------------------------------------------ fixup kernel
+//
+// One block per row tile.  A tile covered whole by one CTA was written by the main
+// kernel; for a tile cut between CTAs cf..cl the block sums their partials (slot 0 when
+// the tile is the CTA's first segment, else 1) in CTA order and writes y.
+template <int NT>
+__global__ void __launch_bounds__(256) qmm_fixup_kernel(const Params p) {
+    pdl_launch_dependents();
+    pdl_wait();  // the main kernel's partials
+    const int t = blockIdx.x;
+    const long long cf = owner_of((long long)t * p.GT, p);
+    const long long cl = owner_of((long long)(t + 1) * p.GT - 1, p);
+    if (cf == cl) return;
+    constexpr int TILE_FLOATS = NT * 8 * kRows;
+    const int n0 = t * kRows;
+    for (int idx = threadIdx.x; idx < TILE_FLOATS / 4; idx += blockDim.x) {
+        const int m = idx / (kRows / 4), r4 = (idx % (kRows / 4)) * 4;
+        if (m >= p.M) break;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (long long cc = cf; cc <= cl; ++cc) {
+            const int sl = ((int)(range_begin(cc, p) / p.GT) == t) ? 0 : 1;
+            const float4 q = __ldcg(reinterpret_cast<const float4*>(p.partials + (size_t)(cc * 2 + sl) * TILE_FLOATS +
+                                                                    m * kRows + r4));
+            v.x += q.x;
+            v.y += q.y;
+            v.z += q.z;
+            v.w += q.w;
+        }
+        const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int n = n0 + r4 + e;
+            if (n < p.N) {
+                __nv_bfloat16 o = __float2bfloat16_rn(vv[e]);
+                p.y[(size_t)m * p.N + n] = *reinterpret_cast<uint16_t*>(&o);
+            }
+        }
     }
 }
 
@@ -834,7 +828,6 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
     p.scales = scales;
     p.biases = biases;
     p.partials = reinterpret_cast<float*>(wsb);
-    p.counters = reinterpret_cast<int*>(wsb + partials_bytes());
     p.M = s.M;
     p.N = s.N;
     p.K = s.K;
@@ -857,6 +850,7 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
                                    s.M, s.K, s.group));
     DFLASH_CUDA_TRY(launch_pdl(qmm_kernel<C>, dim3(p.G), dim3(kThreads), (size_t)C::SMEM_BYTES, stream, tm_w, tm_x,
                                tm_s, tm_b, tm_xs, p));
+    DFLASH_CUDA_TRY(launch_pdl(qmm_fixup_kernel<C::NT>, dim3(p.tiles), dim3(256), 0, stream, p));
     return DFLASH_OK;
 }
 
