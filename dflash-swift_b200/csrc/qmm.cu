@@ -928,3 +928,61 @@ extern "C" int dflash_qmm(const dflash_bf16* x, const uint32_t* w, const dflash_
     if (bits == 4) return qmm::dispatch_group<4>(s, x, w, scales, biases, y, workspace, st);
     return qmm::dispatch_group<8>(s, x, w, scales, biases, y, workspace, st);
 }
+
+// ------------------------------------------------------------------ entry point without allocation
+//
+// For callers that cannot allocate device memory around a call: code running inside a
+// CUDA-graph capture they do not own, plugin hosts whose allocator is off limits,
+// real-time paths where a cudaMalloc could block or fail.  The scratch that
+// dflash_qmm takes as `workspace` lives instead in this file-scope device array, which
+// every GPU that loads the library holds until the process exits.
+namespace dflash {
+namespace qmm {
+
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB per device
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch on the current device, resolved once per device.
+int static_scratch(void** out) {
+    static std::mutex mu;
+    static void* ptr[64] = {nullptr};
+    int dev = 0;
+    DFLASH_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(DFLASH_ERR_UNSUPPORTED, "device ordinal %d above 63", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess)
+            return fail(DFLASH_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
+        ptr[dev] = p;
+    }
+    *out = ptr[dev];
+    return DFLASH_OK;
+}
+
+}  // namespace qmm
+}  // namespace dflash
+
+extern "C" int dflash_qmm_noalloc(const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scales,
+                                  const dflash_bf16* biases, dflash_bf16* y, int M, int N, int K, int group_size,
+                                  int bits, dflash_stream_t stream) {
+    using namespace dflash;
+    qmm::Shape s{M, N, K, group_size, bits};
+    if (int st = qmm::validate(s)) return st;
+    if (!x || !w || !scales || !biases || !y)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_qmm_noalloc: null tensor pointer");
+    if (!aligned16(x) || !aligned16(w))
+        return fail(DFLASH_ERR_MISALIGNED, "dflash_qmm_noalloc: x and w must be 16-byte aligned");
+    const size_t need = dflash_qmm_workspace_bytes(M, N, K, group_size, bits);
+    if (need > qmm::kStaticScratchBytes)
+        return fail(DFLASH_ERR_UNSUPPORTED,
+                    "dflash_qmm_noalloc: M=%d K=%d group %d needs %zu bytes of scratch, above the %zu-byte static "
+                    "maximum; use dflash_qmm with a caller-owned workspace",
+                    M, K, group_size, need, qmm::kStaticScratchBytes);
+    void* scratch = nullptr;
+    if (int st = qmm::static_scratch(&scratch)) return st;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (bits == 4) return qmm::dispatch_group<4>(s, x, w, scales, biases, y, scratch, st);
+    return qmm::dispatch_group<8>(s, x, w, scales, biases, y, scratch, st);
+}

@@ -43,7 +43,8 @@ DEVERR_TEST_WAIT = 0x80000000
 # Every symbol the header declares; tests check the library exports all of them.
 EXPORTED = (
     "dflash_version", "dflash_last_error", "dflash_status_string", "dflash_device_error",
-    "dflash_test_bounded_wait", "dflash_qmm_workspace_bytes", "dflash_qmm", "dflash_qmm_supported",
+    "dflash_test_bounded_wait", "dflash_qmm_workspace_bytes", "dflash_qmm", "dflash_qmm_noalloc",
+    "dflash_qmm_supported",
     "dflash_gdn_step", "dflash_gdn_replay", "dflash_gdn_conv_rollback",
 )
 
@@ -73,6 +74,7 @@ def _load() -> ctypes.CDLL:
         "dflash_test_bounded_wait": ([ctypes.c_uint64, _vp], _i),
         "dflash_qmm_workspace_bytes": ([_i, _i, _i, _i, _i], _sz),
         "dflash_qmm": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp], _i),
+        "dflash_qmm_noalloc": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp], _i),
         "dflash_qmm_supported": ([_i, _i, _i, _i], _i),
         "dflash_gdn_step": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, ctypes.c_float, _vp], _i),
         "dflash_gdn_replay": ([_vp, _vp, _vp, _vp, _vp, _vp, ctypes.POINTER(ctypes.c_int32), _i, _i, _i, _i,
@@ -165,6 +167,20 @@ def qmm(x, w, scales, biases, group_size: int, bits: int, out=None, workspace: O
     ws = workspace.ensure(need) if workspace is not None else default_workspace(need, x.device)
     check(lib.dflash_qmm(_ptr(x), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out), M, N, K, group_size, bits,
                          ws.buf.data_ptr(), ws.nbytes, _stream(stream)))
+    return out
+
+
+def qmm_noalloc(x, w, scales, biases, group_size: int, bits: int, out=None, stream=None):
+    """dflash_qmm without a workspace argument, for callers that may not allocate
+    device memory: the library's own static device scratch is used instead (shapes up
+    to its 8 MiB limit; calls that overlap on the GPU must not share a device)."""
+    import torch
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    check(lib.dflash_qmm_noalloc(_ptr(x), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out), M, N, K, group_size, bits,
+                                 _stream(stream)))
     return out
 
 

@@ -91,6 +91,26 @@ int dflash_qmm(const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scale
                const dflash_bf16* biases, dflash_bf16* y, int M, int N, int K, int group_size,
                int bits, void* workspace, size_t workspace_bytes, dflash_stream_t stream);
 
+/* dflash_qmm for callers that cannot allocate device memory (no counterpart in the
+ * reference, whose MLX runtime always owns allocation): code running inside a CUDA
+ * graph capture it does not control, plugin hosts whose allocator is off limits, or
+ * latency-critical paths where a cudaMalloc could block or fail.  Same arguments and
+ * results as dflash_qmm, without `workspace`: the scratch is a library-owned 8 MiB
+ * device array that every GPU loading this library keeps until the process exits.
+ *   - Shapes whose dflash_qmm_workspace_bytes exceeds 8 MiB are rejected with
+ *     DFLASH_ERR_UNSUPPORTED (at M = 16 that is K above about 78000; dflash_qmm
+ *     with a larger workspace covers those).
+ *   - The first call on a device resolves the array's device address; make that first
+ *     call outside any stream capture.
+ *   - Every call on a device shares the array: calls that can overlap on the GPU
+ *     (different streams without ordering between them) race and corrupt each other's
+ *     results.  Keep such calls on one stream, or use dflash_qmm with one workspace per
+ *     stream.
+ *   - Calls allocate nothing (no cudaMalloc, cudaFree or library allocator). */
+int dflash_qmm_noalloc(const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scales,
+                       const dflash_bf16* biases, dflash_bf16* y, int M, int N, int K, int group_size,
+                       int bits, dflash_stream_t stream);
+
 /* Static half of the reference's eligibility test (SmallMQuantizedMatmul.isEligible,
  * SmallMQuantizedMatmul.swift:193-201) for a layer of this library: 1 when
  * dflash_qmm covers (N, K, group_size, bits) for every M in 1..16, else 0.  Wider

@@ -62,6 +62,18 @@ def test_qmm_argument_errors(dc, kw, status):
     assert dc.last_error()
 
 
+def test_qmm_noalloc_argument_errors(dc):
+    """The no-allocation entry point validates like dflash_qmm, and rejects a shape
+    whose scratch would not fit its static array before touching the GPU."""
+    f = dc.lib.dflash_qmm_noalloc
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, 17, 4096, 1024, 64, 4, None) == 2
+    assert f(0, FAKE, FAKE, FAKE, FAKE, 8, 4096, 1024, 64, 4, None) == 1
+    assert f(FAKE + 2, FAKE, FAKE, FAKE, FAKE, 8, 4096, 1024, 64, 4, None) == 3
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, 16, 4096, 1 << 20, 64, 4, None) == 2
+    assert "static" in dc.last_error() and "dflash_qmm" in dc.last_error()
+    assert dc.qmm_workspace_bytes(16, 4096, 77824, 32, 4) <= 8 << 20 < dc.qmm_workspace_bytes(16, 4096, 79872, 32, 4)
+
+
 def test_qmm_supported_table(dc):
     f = dc.lib.dflash_qmm_supported
     for bits in (4, 8):
