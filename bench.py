@@ -41,7 +41,7 @@ NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 1024 * 1024
 PROFILE_SUMMARY = ROOT / "profiles" / "qmm_m8_k5120_n17408_4b_g64.json"
-KERNELS_PER_CALL = 3  # prep (x to fragment order + group sums), main (weight stream), fixup (split tiles)
+KERNELS_PER_CALL = 2  # prep (x packets: fp16 fragment order + segment sums), main (weight stream)
 
 
 def algorithmic_bytes(m: int, n: int = N, k: int = K, group: int = GROUP, bits: int = BITS) -> int:

@@ -90,16 +90,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Suspend time asked of a blocking try_wait: the thread sleeps until the phase
+// completes or this many nanoseconds pass, instead of spinning.
+constexpr uint32_t kSuspendHintNs = 20000;
+
+// try_wait that suspends the thread for up to kSuspendHintNs.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendHintNs)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Gives up after
 // kWaitLimitNs, records `errbit` in g_device_error and in *abort (shared), and returns
 // false.  Returns false at once when *abort is already set.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort, unsigned errbit) {
-    if (*abort) return false;
     if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
     const unsigned long long t0 = globaltimer_ns();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity)) return true;
         if (*abort) return false;
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
             atomicOr(&g_device_error, errbit);

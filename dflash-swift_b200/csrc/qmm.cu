@@ -3,28 +3,34 @@
 // Replaces SmallMQuantizedMatmul.apply (Sources/DFlashKit/SmallMQuantizedMatmul.swift:
 // 210-224) and the stock quantizedMatmul it stands in for.  The work is bound by the
 // packed weight stream (M <= 16 rows against N*K quantized weights), so everything is
-// arranged to move those bytes from HBM exactly once at full bandwidth:
+// arranged to move those bytes from HBM once, at full bandwidth, with one weight-stream
+// kernel per call:
 //
-//  * Three kernels per call, chained with programmatic dependent launch (PDL).  A tiny
-//    prep kernel writes x, permuted into MMA fragment order, and per-group x sums into
-//    the workspace.  The main kernel starts streaming weights, scales and biases before
-//    its grid dependency resolves (they are never written by the preceding kernels),
-//    so consecutive calls overlap launch latency and pipeline fill with the previous
-//    call's tail.  A fixup kernel sums the partials of row tiles cut between CTAs.
-//  * Persistent grid, one CTA per SM.  The weight matrix is cut into row tiles of 256
-//    output features; the (row tile, quantization group) pairs are split into equal
-//    contiguous ranges, one per CTA (stream-K).  A CTA writes a row tile it covers
-//    whole straight to y; for a tile cut between CTAs it publishes an fp32 partial and
-//    moves on without waiting, and the fixup kernel adds the partials in a fixed order
-//    (results are deterministic).
-//  * One producer thread issues TMA tile loads (cp.async.bulk.tensor, no multicast)
-//    into a 4-deep shared-memory ring: per stage a [256 rows x 128 B] weight box with
-//    128-byte swizzle, the matching x columns and x group sums, and the scale/bias
-//    columns.
-//  * 16 consumer warps: 8 slices of 32 features x 2 groups that take alternate stages.
-//    Each dequantises in registers and contracts on mma.sync m16n8k16 with the weights
-//    as the 16-row A operand and x (<= 8 rows per n-tile) as the n=8 B operand, so a
-//    weight is read and dequantised once for all M rows.
+//  * Two kernels per call, chained with programmatic dependent launch (PDL).  A small
+//    prep kernel turns x into per-stage "packets": x in fp16, permuted into MMA fragment
+//    order, plus per segment of k the sums the epilogue needs.  The main kernel starts
+//    streaming weights, scales and biases before its grid dependency resolves (they are
+//    not written by the preceding kernels), so back-to-back calls keep HBM busy across
+//    kernel boundaries.
+//  * The main grid is a set of 2-CTA thread-block clusters, one CTA per SM.  Output
+//    features are cut into row tiles of up to 256 rows, one TMA box high; each cluster
+//    takes whole tiles, and its two CTAs take the two halves of K.  Inside a CTA, the
+//    four k-lanes of consumer warps hold partial sums that are added in a fixed order
+//    through shared memory; the two CTAs then push each other the rows the other one
+//    writes, with distributed-shared-memory stores.  No CTA waits on a CTA outside its
+//    cluster, and results are deterministic.
+//  * One producer thread issues, per stage, one TMA box of [tile rows x 128 B] of packed
+//    weights (128-byte swizzle, no multicast) and one bulk copy of the x packet into a
+//    ring of up to 8 stages; scale and bias boxes of 8 groups go to a second ring.  The
+//    ring depth is chosen per launch to fill shared memory.
+//  * 16 consumer warps: k-lane (warp & 3) takes one 32-byte column slice of every
+//    stage, row quarter (warp >> 2) takes every fourth 16-row block.  The warps of one
+//    SM sub-partition share a k-lane, so the four sub-partitions get equal work for any
+//    tile height.  A warp first copies everything it needs from a stage into registers
+//    and releases the slot, then dequantises and contracts on mma.sync m16n8k16 with the
+//    weights as the 16-row A operand and x (<= 8 rows per n-tile) as the n=8 B operand,
+//    interleaving its blocks so that the MMA chains overlap.  A weight is read and
+//    dequantised once for all M rows.
 //
 // Dequantisation uses the factored form  sum_k x (q s + b) = s (sum_k x q) + b (sum_k x)
 // per group, on fp16 MMA operands.  A code becomes an exact fp16 value by OR-ing its
@@ -32,201 +38,85 @@
 // bits 0-3 of a 16-bit lane over 1024.0 (0x6400) reads 1024 + q; a nibble in bits 4-7
 // over 64.0 (0x5400) reads 64 + q (the mantissa step there is 1/16), so both nibbles of
 // a byte unpack without a shift and a packed word costs 4 LOP3 and one shift for 8
-// weights.  The ALU pipe, which those LOP3s load, is what bounds the kernel.  The MMA
-// yields sum_k x (q + offset_k); the prep kernel supplies per group the sum of x and
-// z = sum_k offset_k x, so  y += (s f) tmp + b xs - s z  recovers the exact sum.  For
-// 8-bit codes the high nibble over 1024.0 reads 1024 + 16 q_hi, so both MMAs use the
-// same x and z = 2048 xs.  x enters fp16 scaled per (row, group) by a power of two
-// f^-1 that keeps it below 2^15 (exact: bf16 values fit fp16's significand), so no
-// input overflows.  Within a thread's slice of a group the k order is permuted
-// identically for weights and x (a sum does not depend on k order), so weights are
-// consumed exactly as MLX packs them.
+// weights.  The MMA accumulator starts at -z, where z = sum_k offset_k x' comes with
+// the packet, so the MMA leaves exactly sum_k q x' and the combine is two FMAs per
+// output: acc += s tmp + b xs.  For 8-bit codes the high nibble over 1024.0 reads
+// 1024 + 16 q_hi, so both MMAs use the same x and z = 2048 sum x'.  x enters fp16 as
+// x' = x / f with f a power of two per segment that keeps |x'| < 2^15 (exact: bf16
+// values fit fp16's significand); f is 1 unless |x| >= 32768, and only then does the
+// combine multiply by f.  Within a lane's words the k order is permuted identically
+// for weights and x (a sum does not depend on k order), so weights are consumed exactly
+// as MLX packs them.
 #include "common.cuh"
 
 namespace dflash {
 namespace qmm {
 
-constexpr int kRows = 256;            // output features per row tile
-constexpr int kRowBytes = 128;        // weight bytes per row per stage (one swizzle span)
-constexpr int kRowSlices = 8;         // 32-feature slices per tile (one per consumer warp)
-constexpr int kKSplit = 2;            // consumer warp groups, alternating stages
-constexpr int kConsumerWarps = kRowSlices * kKSplit;
+constexpr int kConsumerWarps = 16;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;
-constexpr int kStages = 4;
-constexpr int kRedPitch = kRows + 4;  // floats per m row of the reduction buffer (bank spread)
-constexpr int kMaxCtas = 160;         // upper bound on the persistent grid (B200: 148 SMs)
-constexpr int kMaxTiles = 4096;       // N <= kMaxTiles * kRows
-constexpr int kXsWidth = 16;          // x rows covered by the per-group table (M <= 16)
-constexpr int kTabWidth = 64;         // floats per group row of the table: xs[16] f[16] z[16] pad
-constexpr int kBarConsumers = 1;      // named barrier id used by the consumer warps
-constexpr int kPrepThreads = 256;
+constexpr int kThreads = kConsumerThreads + 128;  // + the producer warpgroup (one thread issues)
+constexpr int kLaunchRegs = 96;                   // per thread at launch: 640 x 96 fits one SM
+constexpr int kConsumerRegs = 112;                // after setmaxnreg: 512 x 112 + 128 x 32 = 640 x 96
+constexpr int kProducerRegs = 32;
+static_assert(kConsumerThreads * kConsumerRegs + 128 * kProducerRegs <= kThreads * kLaunchRegs,
+              "setmaxnreg split exceeds the registers the block is launched with");
+constexpr int kKLanes = 4;                       // consumer warps per row quarter
+constexpr int kMaxTileBlocks = 16;               // 16-row blocks per row tile (TMA box <= 256 rows)
+constexpr int kRowBytes = 128;                   // packed weight bytes per row per stage
+constexpr int kMaxStages = 8;
+constexpr int kMaxSbStages = 8;
+constexpr int kMaxCluster = 2;
+constexpr int kSmemLimit = 232448;               // opt-in shared memory per block, sm_100
+constexpr int kBarConsumers = 1;                 // named barrier: all consumer warps
+constexpr int kBarLane0 = 2;                     // named barrier: the k-lane 0 warps
+constexpr int kPrepThreads = 32;                 // one warp per prep block: fits beside a running main CTA
+constexpr int kMaxN = 1 << 24;
+constexpr uint32_t kMag1024 = 0x64006400u;       // fp16x2 (1024, 1024): + nibble in bits 0-3 (4-7: +16q)
+constexpr uint32_t kMag64 = 0x54005400u;         // fp16x2 (64, 64): + nibble in bits 4-7
+constexpr uint32_t kLoNib = 0x000F000Fu;
+constexpr uint32_t kHiNib = 0x00F000F0u;
 
 template <int BITS_, int GROUP_, int NT_, bool STMA_>
 struct Cfg {
     static constexpr int BITS = BITS_, GROUP = GROUP_, NT = NT_;
-    static constexpr bool STMA = STMA_;                  // scales/biases through TMA
-    static constexpr int GB = GROUP * BITS / 8;          // bytes per row per group
-    static constexpr int GPS = kRowBytes / GB;           // groups per stage
-    static constexpr int TB = GB / 4;                    // bytes per thread per row per group
-    static constexpr int KPS = GPS * GROUP;              // k per stage
-    static constexpr int XBOX = KPS / 64;                // x boxes (64 k each) per stage
-    static constexpr int XROWS = 8 * NT;
-    static constexpr int W_BYTES = kRows * kRowBytes;
-    static constexpr int XBOX_BYTES = XROWS * 128;
-    static constexpr int X_BYTES = XBOX * XBOX_BYTES;
-    static constexpr int S_BYTES = kRows * 16;           // [256 rows x 8 groups] bf16
-    static constexpr int TAB_ROW = 48;                   // floats loaded per group: xs, f, z
-    static constexpr int XS_BYTES = GPS * TAB_ROW * 4;   // [GPS groups x 48] fp32
-    static constexpr int XS_OFF = W_BYTES + X_BYTES + 2 * S_BYTES;
-    static constexpr int STAGE_BYTES = XS_OFF + 2048;
-    static constexpr uint32_t TX_BYTES = W_BYTES + X_BYTES + XS_BYTES + (STMA ? 2 * S_BYTES : 0);
-    static constexpr int VPT = GROUP / 4;                // values per thread per row per group
-    static constexpr int PV = VPT < 16 ? VPT : 16;       // values per piece
-    static constexpr int PIECES = VPT / PV;
-    static constexpr int PB = PV * BITS / 8;             // bytes per piece per row
-    static constexpr int PW = PB / 4;                    // 32-bit words per piece per row
-    static constexpr int PSTEPS = PV / 4;                // k16 MMA steps per piece
-    static constexpr int PXCH = PV / 8;                  // 8-value x chunks per piece
-    // Two warps share each 32-feature slice.  With at least two groups per stage they
-    // split the stage's groups (even / odd) and every consumer warp takes every stage;
-    // with one group per stage they take alternate stages.
-    static constexpr bool SPLIT = GPS >= 2;
-    static constexpr int EMPTY_ARRIVALS = SPLIT ? kConsumerWarps : kRowSlices;
-    static constexpr int RED_FLOATS = NT * 8 * kRedPitch;
-    static constexpr int SMEM_BYTES = kStages * STAGE_BYTES + RED_FLOATS * 4 + 256 + 1024;
-    static_assert(GPS >= 1 && GPS <= 8 && (8 % GPS) == 0, "stage/group geometry");
-    static_assert(XS_BYTES <= 2048, "x group-table stage slot");
-    static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte swizzle alignment");
-    static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+    static constexpr bool STMA = STMA_;                   // scales/biases by TMA (else read from global)
+    static constexpr int MR = 8 * NT;                     // x rows in a packet (zero padded past M)
+    static constexpr int STAGE_K = kRowBytes * 8 / BITS;  // 256 (4-bit) or 128 (8-bit) k per stage
+    static constexpr int UNIT_K = STAGE_K / kKLanes;      // k per k-lane per stage: 64 or 32
+    static constexpr int UNIT_B = UNIT_K * 2;             // fp16 bytes of one x row of a unit
+    static constexpr int SEG_K = UNIT_K < GROUP ? UNIT_K : GROUP;  // k per combine segment
+    static constexpr int SEGS = UNIT_K / SEG_K;           // segments per unit: 2 for 4-bit g32, else 1
+    static constexpr int GPS = STAGE_K / GROUP;           // groups per stage
+    static constexpr int SBP = 8 / GPS;                   // stages per scale/bias box of 8 groups
+    static constexpr int X_BYTES = kKLanes * MR * UNIT_B;
+    static constexpr int T_BYTES = kKLanes * SEGS * MR * 16;
+    static constexpr int PKT = X_BYTES + T_BYTES;         // packet bytes per stage
+    static constexpr int XREGS = UNIT_B / 4 / 4;          // 32-bit B registers per lane per unit: 8 or 4
+    static_assert(PKT % 16 == 0, "bulk copies move multiples of 16 bytes");
+    static_assert(GPS >= 1 && 8 % GPS == 0, "scale boxes hold 8 groups");
 };
 
-struct Params {
-    dflash_bf16* y;
-    const dflash_bf16* scales;
-    const dflash_bf16* biases;
-    float* partials;
-    int M, N, K, GT, tiles, G;
-    long long U;
-    int y_vec;
-};
-
-// ------------------------------------------------------------------ workspace layout
-//
-//   [fp32 partial tiles, kMaxCtas x 2 x 16 x 256]
-//   [x group table, GT x 64 fp32][x in fragment order, M x K fp16]
-// Every region is rewritten by each call before it is read, so one workspace serves
-// calls of any shape and needs no initialisation.
-inline size_t partials_bytes() { return (size_t)kMaxCtas * 2 * 16 * kRows * 4; }
-inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
-inline size_t xs_offset() { return partials_bytes(); }
-inline size_t xperm_offset(int K, int group) { return xs_offset() + round_up((size_t)(K / group) * kTabWidth * 4, 1024); }
-inline size_t workspace_size(int M, int K, int group) {
-    return xperm_offset(K, group) + round_up((size_t)M * K * 2, 1024);
+// Packet layout (one per stage of STAGE_K columns of x; offsets in bytes):
+//   x region  [unit u][row m][UNIT_B]: the fp16 x' of k in [u UNIT_K, (u+1) UNIT_K) of the
+//             stage, in 16-byte chunks of 8 k.  Chunk c is stored at c ^ x_swizzle(m) and
+//             holds its 8 values in fragment order (4-bit: 0,4,1,5,2,6,3,7; 8-bit:
+//             0,2,1,3,4,6,5,7), so a lane's B fragments are two (4-bit) or one (8-bit)
+//             conflict-free 16-byte loads.
+//   table     [unit u][segment][row m] float4 (-z', xs, f, 0)
+template <class C>
+__host__ __device__ __forceinline__ constexpr int x_swizzle(int m) {
+    return C::BITS == 8 ? 0 : (C::SEGS == 2 ? ((m & 1) << 2) : (m & 1));
 }
 
-// ------------------------------------------------------------------ PDL
+// ------------------------------------------------------------------ small device helpers
 __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
-// ------------------------------------------------------------------ prep kernel
-//
-// x [M, K] bf16 -> xperm [M, K] fp16, each run of 8 values reordered so that one
-// 16-byte load gives a thread its four B-fragment registers: 4-bit codes pair k with
-// k+4 ((0,4),(1,5),(2,6),(3,7)), 8-bit codes pair k with k+2 ((0,2),(1,3),(4,6),(5,7)).
-// Per (row m, group G) the values are scaled by 2^-e, e >= 0 the smallest exponent that
-// keeps them below 2^15 (e = 0 for any ordinary activation), and the table row G holds
-//   xs[m] = sum_k x,  f[m] = 2^e,  z[m] = sum_k offset_k x
-// with offset_k = 1024 for k even and 64 for k odd (4-bit), 2048 (8-bit); rows m >= M
-// hold xs = z = 0, f = 1.
-template <int BITS>
-__global__ void __launch_bounds__(kPrepThreads) qmm_prep_kernel(const dflash_bf16* __restrict__ x,
-                                                              uint16_t* __restrict__ xperm, float* __restrict__ tab,
-                                                              int M, int K, int group) {
-    pdl_launch_dependents();
-    pdl_wait();  // the previous call may still be reading this workspace
-    const int chunks_per_row = K / 8;
-    const long long idx = (long long)blockIdx.x * kPrepThreads + threadIdx.x;
-    const bool live = idx < (long long)kXsWidth * chunks_per_row;
-    const int m = live ? (int)(idx / chunks_per_row) : kXsWidth;
-    const int c = live ? (int)(idx % chunks_per_row) : 0;
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = 0.f;
-    if (live && m < M) {
-        const uint4 r = *reinterpret_cast<const uint4*>(x + (size_t)m * K + (size_t)c * 8);
-        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            v[2 * i] = __uint_as_float(w[i] << 16);
-            v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-        }
-    }
-    float sum = 0.f, z = 0.f, amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        sum += v[i];
-        amax = fmaxf(amax, fabsf(v[i]));
-        if constexpr (BITS == 4) z = fmaf((i & 1) ? 64.f : 1024.f, v[i], z);
-    }
-    if constexpr (BITS == 8) z = 2048.f * sum;
-    // reduce over the group's group/8 consecutive chunks (aligned lanes of one warp)
-    const int lanes = group / 8;
-    for (int off = 1; off < lanes; off <<= 1) {
-        sum += __shfl_xor_sync(0xffffffffu, sum, off);
-        z += __shfl_xor_sync(0xffffffffu, z, off);
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    }
-    int e = 0;
-    if (amax >= 32768.f && amax <= 3.0e38f) e = min(ilogbf(amax) - 14, 120);
-    if (live && m < M) {
-        const float sc = ldexpf(1.f, -e);
-        uint16_t h[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            __half hv = __float2half_rn(v[i] * sc);
-            h[i] = *reinterpret_cast<uint16_t*>(&hv);
-        }
-        uint4 o;
-        if constexpr (BITS == 4) {
-            o.x = h[0] | ((uint32_t)h[4] << 16);
-            o.y = h[1] | ((uint32_t)h[5] << 16);
-            o.z = h[2] | ((uint32_t)h[6] << 16);
-            o.w = h[3] | ((uint32_t)h[7] << 16);
-        } else {
-            o.x = h[0] | ((uint32_t)h[2] << 16);
-            o.y = h[1] | ((uint32_t)h[3] << 16);
-            o.z = h[4] | ((uint32_t)h[6] << 16);
-            o.w = h[5] | ((uint32_t)h[7] << 16);
-        }
-        *reinterpret_cast<uint4*>(xperm + (size_t)m * K + (size_t)c * 8) = o;
-    }
-    if (live && (c % lanes) == 0) {
-        float* row = tab + (size_t)(c / lanes) * kTabWidth;
-        row[m] = sum;
-        row[16 + m] = ldexpf(1.f, e);
-        row[32 + m] = z;
-    }
-}
-
-// ------------------------------------------------------------------ main kernel helpers
-
-__device__ __forceinline__ long long owner_of(long long u, const Params& p) {
-    return ((u + 1) * p.G - 1) / p.U;
-}
-__device__ __forceinline__ long long range_begin(long long c, const Params& p) {
-    return c * p.U / p.G;
-}
-
-constexpr uint32_t kLoNib = 0x000F000Fu;      // nibble in bits 0-3 of each 16-bit lane
-constexpr uint32_t kHiNib = 0x00F000F0u;      // nibble in bits 4-7 of each 16-bit lane
-constexpr uint32_t kMag1024 = 0x64006400u;    // fp16x2 (1024, 1024): + nibble in bits 0-3 (4-7: +16q)
-constexpr uint32_t kMag64 = 0x54005400u;      // fp16x2 (64, 64): + nibble in bits 4-7
 // (v & mask) | mag as one LOP3: the mask is an immediate, the magic a register (left
 // to itself the compiler splits this into an AND and an OR with two immediates, which
-// doubles the load on the ALU pipe that bounds this kernel).
+// doubles the load on the ALU pipe).
 template <uint32_t MASK>
 __device__ __forceinline__ uint32_t unpack(uint32_t v, uint32_t mag) {
     uint32_t d;
@@ -240,517 +130,789 @@ __device__ __forceinline__ uint32_t pinned() {
     asm volatile("mov.b32 %0, %1;" : "=r"(d) : "n"(V));
     return d;
 }
-// bf16 bits -> fp32 as an integer multiply (FMA pipe) by a register holding 65536.
+
+// Per-warpgroup register budget changes (all 128 threads of a warpgroup execute them).
+template <uint32_t N>
+__device__ __forceinline__ void regs_raise() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_lower() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// D += A * B, m16n8k16, fp16 operands, fp32 accumulate.
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void tma_load_2d_u32(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t nclusters_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(addr), "r"(rank));
+    return d;
+}
+__device__ __forceinline__ void st_cluster_f32x2(uint32_t addr, float a, float b) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+// Arrive (release, cluster scope) on an mbarrier of another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendHintNs)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait with cluster-scope acquire, for hand-offs between the CTAs of a cluster.
+// Runs to its limit even after an abort elsewhere, so that both CTAs keep taking the
+// same steps; a timeout records `errbit` and the abort flag.
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                          unsigned errbit) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    while (true) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(&g_device_error, errbit);
+            *abort = 1;
+            return false;
+        }
+    }
+}
+// Bounded wait that ignores the abort flag: lets copies already in flight land before
+// the CTA leaves.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+    const unsigned long long t0 = globaltimer_ns();
+    while (!mbar_try_wait_sleep(bar, parity)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(&g_device_error, DFLASH_DEVERR_QMM_PIPELINE);
+            return;
+        }
+    }
+}
+__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Split cluster barrier: a relaxed arrive (orders nothing by itself; preceded by
+// fence.mbarrier_init it publishes barrier initialisation) and the matching wait.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// ------------------------------------------------------------------ prep kernel
+//
+// One thread per (x row m < MR, run of 8 k): reads 8 bf16 of x (zeros past M or K),
+// picks the segment's power-of-two scale, writes the fp16 run in fragment order and,
+// from the segment's first lane, the table entry.  Lanes of a segment are adjacent, so
+// the segment reductions are xor-shuffles (the same fixed-order sum on every lane).
+// Padding (rows past M, k past K) gets x' = 0 and a zero table entry, so the main
+// kernel needs no masks along k or m: those columns contribute exactly 0.
+template <class C>
+__global__ void __launch_bounds__(kPrepThreads) qmm_prep_kernel(const uint16_t* __restrict__ x,
+                                                                uint8_t* __restrict__ packets, int M, int K,
+                                                                int S) {
+    pdl_launch_dependents();
+    pdl_wait();  // x may be written by the preceding kernel
+    constexpr int CPR = C::STAGE_K / 8;  // runs of 8 per stage row
+    constexpr int SL = C::SEG_K / 8;     // lanes per segment: 4 or 8
+    const long long runs = (long long)S * CPR;
+    const long long idx = (long long)blockIdx.x * kPrepThreads + threadIdx.x;
+    if (idx >= runs * C::MR) return;  // whole warps only: runs * MR is a multiple of 32
+    const int m = (int)(idx / runs);
+    const int k0 = (int)(idx % runs) * 8;
+
+    float v[8];
+    if (m < M && k0 < K) {
+        const uint4 r = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * K + k0));
+        v[0] = bf16_lo(r.x);
+        v[1] = bf16_hi(r.x);
+        v[2] = bf16_lo(r.y);
+        v[3] = bf16_hi(r.y);
+        v[4] = bf16_lo(r.z);
+        v[5] = bf16_hi(r.z);
+        v[6] = bf16_lo(r.w);
+        v[7] = bf16_hi(r.w);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 1; o < SL; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    float f = 1.f, inv = 1.f;
+    if (amax >= 32768.f) {  // false for NaN: NaN inputs propagate unscaled
+        const int e = ((__float_as_int(amax) >> 23) & 0xff) - 127;  // floor(log2 amax); 128 for inf
+        const int sh = e - 14;                                      // amax / 2^sh in [2^14, 2^15)
+        f = __int_as_float((127 + sh) << 23);
+        inv = __int_as_float((127 - sh) << 23);
+    }
+    // fragment order of the run: 4-bit (0,4)(1,5)(2,6)(3,7); 8-bit (0,2)(1,3)(4,6)(5,7)
+    float r[8];
+    uint32_t h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int a = C::BITS == 4 ? i : ((i >> 1) << 2) + (i & 1);
+        const int b = C::BITS == 4 ? i + 4 : a + 2;
+        h[i] = pack_half2(v[a] * inv, v[b] * inv);
+        const __half2 hh = *reinterpret_cast<const __half2*>(&h[i]);
+        r[a] = __low2float(hh);
+        r[b] = __high2float(hh);
+    }
+    float z, xs = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    if constexpr (C::BITS == 4) {
+        // nibbles 0, 2, 4, 6 of a word read 1024 + q, nibbles 1, 3, 5, 7 read 64 + q
+        const float ev = (r[0] + r[2]) + (r[4] + r[6]);
+        const float od = (r[1] + r[3]) + (r[5] + r[7]);
+        z = fmaf(1024.f, ev, 64.f * od);
+    } else {
+        z = 2048.f * (((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7])));
+    }
+#pragma unroll
+    for (int o = 1; o < SL; o <<= 1) {
+        z += __shfl_xor_sync(0xffffffffu, z, o);
+        xs += __shfl_xor_sync(0xffffffffu, xs, o);
+    }
+    const int s = k0 / C::STAGE_K, kin = k0 % C::STAGE_K;
+    const int u = kin / C::UNIT_K, c = (kin % C::UNIT_K) / 8;
+    uint8_t* pkt = packets + (size_t)s * C::PKT;
+    *reinterpret_cast<uint4*>(pkt + (u * C::MR + m) * C::UNIT_B + ((c ^ x_swizzle<C>(m)) << 4)) =
+        make_uint4(h[0], h[1], h[2], h[3]);
+    if (kin % C::SEG_K == 0) {
+        const int seg = (kin % C::UNIT_K) / C::SEG_K;
+        *reinterpret_cast<float4*>(pkt + C::X_BYTES + ((u * C::SEGS + seg) * C::MR + m) * 16) =
+            make_float4(-z, xs, f, 0.f);
+    }
+}
+
+// ------------------------------------------------------------------ main kernel
+
+struct Params {
+    const uint8_t* packets;
+    const uint16_t* scales;  // read directly only without scale TMA
+    const uint16_t* biases;
+    uint16_t* y;
+    int M, N, K, GT;
+    int R, nb;    // tile rows = 16 nb
+    int nb0;      // blocks of a tile written by cluster rank 0 (rank 1 writes the rest)
+    int ntiles;   // ceil(N / R)
+    int S;        // stages along K
+    int NS, NSB;  // ring depths
+    uint32_t stage_bytes, sb_bytes, red_off, red_bytes, recv_off, bar_off;
+};
+
+// Shared-memory barrier block (at bar_off).
+struct Bars {
+    uint64_t full[kMaxStages], empty[kMaxStages];
+    uint64_t sbfull[kMaxSbStages], sbempty[kMaxSbStages];
+    uint64_t xfull, xdone;  // cluster exchange: the peer's rows for us have landed / it has read ours
+    int abort;
+};
+
+// MMA fragment row g (0..7) of a 16-row block maps to block row phys(g) (+8 for the
+// second half): even rows for g < 4, odd rows for g >= 4, so that each half-warp's
+// 64-bit weight loads hit 8 different 16-byte chunks of the 128-byte swizzle.
+__device__ __forceinline__ int phys_row(int g) { return ((g & 3) << 1) | (g >> 2); }
+
+struct StageCtx {
+    uint32_t wb;    // weight box of this stage
+    uint32_t pkt;   // packet of this stage
+    uint32_t sb;    // scale/bias slot (scale TMA only)
+    int sbcol0;     // group index of the slot's first column
+    int s;          // stage index along K
+    int tile_row0;  // first output row of the tile
+};
+
+// Shared-memory offsets of one consumer lane that do not change from stage to stage:
+// a warp always handles the same unit (k-lane) and the same blocks of every stage.
+// Block i of the warp sits 4 i blocks below block 0, so its offsets are immediates.
+struct LaneOfs {
+    uint32_t x0, x1;  // packet: this lane's two 16-byte B chunks (n-tile 0)
+    uint32_t tab;     // packet: table entry of column 2 tq (segment 0, n-tile 0)
+    uint32_t w0, w1;  // weight box: this lane's words of row 16 qd + pr (second word for 4-bit g32)
+    uint32_t sb;      // scale slot: row 16 qd + pr
+};
+
+template <class C>
+__device__ __forceinline__ LaneOfs lane_offsets(int kl, int qd, int g, int tq) {
+    LaneOfs o;
+    const int pr = phys_row(g);
+    const uint32_t xrow = (kl * C::MR + g) * C::UNIT_B;
+    if constexpr (C::BITS == 4) {
+        // SEGS 1: chunks 2tq, 2tq+1 (the lane's words 2tq, 2tq+1); SEGS 2: chunks tq, tq+4
+        const int c0 = C::SEGS == 2 ? tq : 2 * tq;
+        const int c1 = C::SEGS == 2 ? tq + 4 : 2 * tq + 1;
+        o.x0 = xrow + ((c0 ^ x_swizzle<C>(g)) << 4);
+        o.x1 = xrow + ((c1 ^ x_swizzle<C>(g)) << 4);
+    } else {
+        o.x0 = xrow + (tq << 4);
+        o.x1 = o.x0;
+    }
+    o.tab = C::X_BYTES + (kl * C::SEGS * C::MR + 2 * tq) * 16;
+    // the lane's words in a 128-byte row: unit kl is bytes [32 kl, 32 kl + 32);
+    // rows 16 b + pr and 16 b + pr + 8 both have (row & 7) == pr
+    const uint32_t rowb = (16 * qd + pr) * kRowBytes;
+    if constexpr (C::SEGS == 2) {
+        o.w0 = rowb + (((2 * kl) ^ pr) << 4) + tq * 4;
+        o.w1 = rowb + (((2 * kl + 1) ^ pr) << 4) + tq * 4;
+    } else {
+        o.w0 = rowb + (((2 * kl + (tq >> 1)) ^ pr) << 4) + (tq & 1) * 8;
+        o.w1 = o.w0 + 4;
+    }
+    o.sb = (16 * qd + pr) * 16;
+    return o;
+}
+
+// Everything one consumer warp takes from a stage: its x fragments and table entries
+// for unit kl, and the weight words of its NB blocks.
+template <class C, int NB>
+struct StageRegs {
+    uint32_t xb[C::NT][C::XREGS];
+    float tz[C::SEGS][C::NT][2], txs[C::SEGS][C::NT][2], tf[C::SEGS][C::NT][2];
+    bool slow[C::SEGS];
+    uint32_t w[NB][2][2];  // block, row half (r0 / r0 + 8), word
+};
+
+template <class C, int NB>
+__device__ __forceinline__ void load_stage(StageRegs<C, NB>& R, uint32_t wb, uint32_t pkt, const LaneOfs& o) {
+#pragma unroll
+    for (int nt = 0; nt < C::NT; ++nt) {
+        const uint4 v0 = lds128(pkt + o.x0 + nt * 8 * C::UNIT_B);
+        R.xb[nt][0] = v0.x;
+        R.xb[nt][1] = v0.y;
+        R.xb[nt][2] = v0.z;
+        R.xb[nt][3] = v0.w;
+        if constexpr (C::BITS == 4) {
+            const uint4 v1 = lds128(pkt + o.x1 + nt * 8 * C::UNIT_B);
+            R.xb[nt][4] = v1.x;
+            R.xb[nt][5] = v1.y;
+            R.xb[nt][6] = v1.z;
+            R.xb[nt][7] = v1.w;
+        }
+    }
+#pragma unroll
+    for (int sg = 0; sg < C::SEGS; ++sg) {
+        bool any = false;
+#pragma unroll
+        for (int nt = 0; nt < C::NT; ++nt) {
+            const uint32_t a = pkt + o.tab + (sg * C::MR + 8 * nt) * 16;
+            const uint4 v0 = lds128(a), v1 = lds128(a + 16);
+            R.tz[sg][nt][0] = __uint_as_float(v0.x);
+            R.txs[sg][nt][0] = __uint_as_float(v0.y);
+            R.tf[sg][nt][0] = __uint_as_float(v0.z);
+            R.tz[sg][nt][1] = __uint_as_float(v1.x);
+            R.txs[sg][nt][1] = __uint_as_float(v1.y);
+            R.tf[sg][nt][1] = __uint_as_float(v1.z);
+            any |= (v0.z != 0x3f800000u) | (v1.z != 0x3f800000u);
+        }
+        R.slow[sg] = __any_sync(0xffffffffu, any);
+    }
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+        const uint32_t a = wb + 4 * 16 * kRowBytes * i;
+        if constexpr (C::SEGS == 2) {
+            R.w[i][0][0] = lds32(a + o.w0);
+            R.w[i][0][1] = lds32(a + o.w1);
+            R.w[i][1][0] = lds32(a + o.w0 + 8 * kRowBytes);
+            R.w[i][1][1] = lds32(a + o.w1 + 8 * kRowBytes);
+        } else {
+            const uint2 u0 = lds64(a + o.w0), u1 = lds64(a + o.w0 + 8 * kRowBytes);
+            R.w[i][0][0] = u0.x;
+            R.w[i][0][1] = u0.y;
+            R.w[i][1][0] = u1.x;
+            R.w[i][1][1] = u1.y;
+        }
+    }
+}
+
+// bf16 bits -> fp32 as an integer multiply (FMA pipe) by a register holding 65536,
+// which keeps the conversion off the ALU pipe that the unpack loads.
 __device__ __forceinline__ float bf16_to_f32_fma(uint32_t b, uint32_t k65536) {
     uint32_t d;
     asm("mul.lo.u32 %0, %1, %2;" : "=r"(d) : "r"(b), "r"(k65536));
     return __uint_as_float(d);
 }
 
-// Registers pinned for the unpack and the scale conversion.
-struct Pinned {
-    uint32_t mag1024, mag64, k65536;
-};
-__device__ __forceinline__ Pinned make_pinned() {
-    return Pinned{pinned<kMag1024>(), pinned<kMag64>(), pinned<65536u>()};
+// D = A * B + C, m16n8k16, fp16 operands, fp32 accumulate, C from separate registers.
+__device__ __forceinline__ void mma_f16_c(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1, float c0, float c1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %11, %10, %11};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c0), "f"(c1));
 }
 
-// Fragment row g of 16-row block i of a warp's 32-feature slice maps to feature row
-//     rb + 16 i + 2 sigma(g) + h        (h = 0: fragment rows 0..7, h = 1: rows 8..15)
-// sigma spreads the 128-byte swizzle keys (row & 7) of the rows a half-warp (LDS.64)
-// or quarter-warp (LDS.128) reads, so the weight reads of a warp hit distinct banks.
-__device__ __forceinline__ int sigma(int g) { return (g & 4) | ((g & 1) << 1) | ((g >> 1) & 1); }
-
-// Per-thread offsets of the fragment layout, computed once per CTA.
-template <class C>
-struct LaneLayout {
-    int row[2];                                   // feature row of (i = 0, h); i = 1 adds 16
-    uint32_t wofs[2];                             // stage-relative byte offset of group 0, piece 0
-    uint32_t xofs[C::NT][C::PIECES][C::PXCH];     // offset within the x region, group 0
-};
-
-template <class C>
-__device__ __forceinline__ LaneLayout<C> lane_layout(int rb, int g, int tq) {
-    LaneLayout<C> L;
-    const uint32_t T = tq * C::TB;  // this thread's byte slice of a row's group
+// Dequantise and contract one stage from registers.  The blocks' MMA chains are issued
+// round-robin so that the latency of one chain hides behind the others; each chain
+// starts from the segment's -z.  `release` is the stage's empty barrier: the warp
+// arrives on it once its last MMAs have consumed every register loaded from the slot
+// (an arrive releases the warp's earlier shared-memory reads, complete by then, so it
+// does not stall).  Scales and biases come from the scale/bias ring (released later)
+// or, without scale TMA, from global memory.
+template <class C, int NB>
+__device__ __forceinline__ void compute_stage(const StageRegs<C, NB>& R, const StageCtx& x, const Params& p,
+                                              const LaneOfs& o, int kl, int qd, int pr, uint32_t mag1024,
+                                              uint32_t mag64, uint32_t k65536, int lane, uint64_t* release,
+                                              float (&acc)[4][C::NT][4]) {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int r = rb + 2 * sigma(g) + h;
-        L.row[h] = r;
-        L.wofs[h] = r * kRowBytes + ((((T >> 4) ^ (r & 7))) << 4) + (T & 15);
-    }
+    for (int nt = 0; nt < C::NT; ++nt) {
 #pragma unroll
-    for (int j = 0; j < C::NT; ++j) {
-        const int m = 8 * j + g;
+        for (int sg = 0; sg < C::SEGS; ++sg) {
+            float d[NB][4];
+            const float c0 = R.tz[sg][nt][0], c1 = R.tz[sg][nt][1];
 #pragma unroll
-        for (int pc = 0; pc < C::PIECES; ++pc)
+            for (int wi = 0; wi < 2; ++wi) {
+                if (C::SEGS == 2 && wi != sg) continue;  // 4-bit g32: segment sg is word sg
+                const bool first = (C::SEGS == 2) || wi == 0;
+                if constexpr (C::BITS == 4) {
+                    const uint32_t b0 = R.xb[nt][4 * wi + 0], b1 = R.xb[nt][4 * wi + 1];
+                    const uint32_t b2 = R.xb[nt][4 * wi + 2], b3 = R.xb[nt][4 * wi + 3];
 #pragma unroll
-            for (int c = 0; c < C::PXCH; ++c) {
-                const int kt = tq * C::VPT + pc * C::PV + 8 * c;  // k within group 0 of the stage
-                L.xofs[j][pc][c] = (kt >> 6) * C::XBOX_BYTES + m * 128 + ((((kt & 63) >> 3) ^ (m & 7)) << 4);
-            }
-    }
-    return L;
-}
-
-// Compile-time parts of the weight address of (group gl, piece pc): XOR into the
-// swizzled chunk bits, plus an in-chunk byte offset.
-template <class C> __device__ __forceinline__ constexpr uint32_t w_xor(int gl, int pc) {
-    return (uint32_t)(gl * C::GB + ((pc * C::PB) & ~15));
-}
-template <class C> __device__ __forceinline__ constexpr uint32_t w_add(int pc) {
-    return (uint32_t)((pc * C::PB) & 15);
-}
-// x address of group gl: XOR of the chunk bits (groups of 32) and a whole-box offset.
-template <class C> __device__ __forceinline__ constexpr uint32_t x_xor(int gl) {
-    return (uint32_t)(((gl * C::GROUP) & 63) << 1);
-}
-template <class C> __device__ __forceinline__ constexpr uint32_t x_add(int gl) {
-    return (uint32_t)(((gl * C::GROUP) >> 6) * C::XBOX_BYTES);
-}
-
-template <int PB>
-__device__ __forceinline__ void lds_words(uint32_t* dst, uint32_t addr) {
-    if constexpr (PB == 4) {
-        dst[0] = lds32(addr);
-    } else if constexpr (PB == 8) {
-        const uint2 v = lds64(addr);
-        dst[0] = v.x;
-        dst[1] = v.y;
-    } else {
-        const uint4 v = lds128(addr);
-        dst[0] = v.x;
-        dst[1] = v.y;
-        dst[2] = v.z;
-        dst[3] = v.w;
-    }
-}
-
-// D = A * B (+ D unless FIRST), m16n8k16 fp16 -> fp32.
-template <bool FIRST>
-__device__ __forceinline__ void mma_step(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-    if constexpr (FIRST) {
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-            "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %10, %10, %10};"
-            : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
-    } else {
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-            "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-    }
-}
-
-// One quantization group (index gl within the stage) for one consumer warp:
-// 32 feature rows x GROUP k, all M rows.  wb[h] = stage base + wofs[h]; xb = x region;
-// sb[h] = scale-tile address of row[h] at this stage's group 0; xsb = this thread's
-// x group-sum slot (group 0, n-tile 0) in the stage.
-template <class C>
-__device__ __forceinline__ void consume_group(const LaneLayout<C>& L, const Pinned& P, const uint32_t (&wb)[2],
-                                              uint32_t xb, const uint32_t (&sb)[2], uint32_t xsb, int gl, int G,
-                                              int tile_row0, const Params& p, float (&acc)[2][C::NT][4]) {
-    float tmp[2][C::NT][4];
-#pragma unroll
-    for (int pc = 0; pc < C::PIECES; ++pc) {
-        // B fragments, already in register order (prep kernel)
-        uint32_t xf[C::NT][C::PXCH][4];
-#pragma unroll
-        for (int j = 0; j < C::NT; ++j)
-#pragma unroll
-            for (int c = 0; c < C::PXCH; ++c) {
-                const uint4 r = lds128(xb + ((L.xofs[j][pc][c] ^ x_xor<C>(gl)) + x_add<C>(gl)));
-                xf[j][c][0] = r.x;
-                xf[j][c][1] = r.y;
-                xf[j][c][2] = r.z;
-                xf[j][c][3] = r.w;
-            }
-        // A operand source: packed words of the 4 feature rows (i, h).
-        uint32_t wv[2][2][C::PW];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const uint32_t a = (wb[h] ^ w_xor<C>(gl, pc)) + w_add<C>(pc);
-            lds_words<C::PB>(wv[0][h], a);
-            lds_words<C::PB>(wv[1][h], a + 16 * kRowBytes);
-        }
-#pragma unroll
-        for (int s = 0; s < C::PSTEPS; ++s) {
-            const bool first = (pc == 0 && s == 0);
-            if constexpr (C::BITS == 4) {
-                // word w of the piece: step 2w uses nibbles (0,4) and (1,5), step 2w+1
-                // nibbles (2,6) and (3,7) of the word shifted right by 8.
-                const int w = s >> 1, q = (s & 1) * 2;
-#pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const uint32_t v0 = q ? (wv[i][0][w] >> 8) : wv[i][0][w];
-                    const uint32_t v1 = q ? (wv[i][1][w] >> 8) : wv[i][1][w];
-                    const uint32_t a0 = unpack<kLoNib>(v0, P.mag1024), a1 = unpack<kLoNib>(v1, P.mag1024);
-                    const uint32_t a2 = unpack<kHiNib>(v0, P.mag64), a3 = unpack<kHiNib>(v1, P.mag64);
-#pragma unroll
-                    for (int j = 0; j < C::NT; ++j) {
-                        const uint32_t b0 = xf[j][w][q], b1 = xf[j][w][q + 1];
-                        if (first) mma_step<true>(tmp[i][j], a0, a1, a2, a3, b0, b1);
-                        else mma_step<false>(tmp[i][j], a0, a1, a2, a3, b0, b1);
+                    for (int i = 0; i < NB; ++i) {
+                        const uint32_t v0 = R.w[i][0][wi], v1 = R.w[i][1][wi];
+                        const uint32_t a0 = unpack<kLoNib>(v0, mag1024), a1 = unpack<kLoNib>(v1, mag1024);
+                        const uint32_t a2 = unpack<kHiNib>(v0, mag64), a3 = unpack<kHiNib>(v1, mag64);
+                        if (first) mma_f16_c(d[i], a0, a1, a2, a3, b0, b1, c0, c1);
+                        else mma_f16(d[i], a0, a1, a2, a3, b0, b1);
                     }
-                }
-            } else {
-                // word s: bytes (0,2) in place and bytes (1,3) shifted right by 8; the low
-                // nibbles read 1024 + q_lo, the high ones 1024 + 16 q_hi, both against x.
-                const int w = s, c = s >> 1, q = (s & 1) * 2;
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const uint32_t w0 = wv[i][0][w], w1 = wv[i][1][w];
-                    const uint32_t t0 = w0 >> 8, t1 = w1 >> 8;
-                    const uint32_t l0 = unpack<kLoNib>(w0, P.mag1024), l1 = unpack<kLoNib>(w1, P.mag1024);
-                    const uint32_t l2 = unpack<kLoNib>(t0, P.mag1024), l3 = unpack<kLoNib>(t1, P.mag1024);
-                    const uint32_t u0 = unpack<kHiNib>(w0, P.mag1024), u1 = unpack<kHiNib>(w1, P.mag1024);
-                    const uint32_t u2 = unpack<kHiNib>(t0, P.mag1024), u3 = unpack<kHiNib>(t1, P.mag1024);
-#pragma unroll
-                    for (int j = 0; j < C::NT; ++j) {
-                        const uint32_t b0 = xf[j][c][q], b1 = xf[j][c][q + 1];
-                        if (first) mma_step<true>(tmp[i][j], l0, l1, l2, l3, b0, b1);
-                        else mma_step<false>(tmp[i][j], l0, l1, l2, l3, b0, b1);
-                        mma_step<false>(tmp[i][j], u0, u1, u2, u3, b0, b1);
+                    for (int i = 0; i < NB; ++i) {
+                        const uint32_t t0 = R.w[i][0][wi] >> 8, t1 = R.w[i][1][wi] >> 8;
+                        mma_f16(d[i], unpack<kLoNib>(t0, mag1024), unpack<kLoNib>(t1, mag1024),
+                                unpack<kHiNib>(t0, mag64), unpack<kHiNib>(t1, mag64), b2, b3);
                     }
-                }
-            }
-        }
-    }
-
-    // group table for this thread's output columns m = 8j + 2tq, 8j + 2tq + 1
-    float xs[C::NT][2], xf2[C::NT][2], zz[C::NT][2];
-#pragma unroll
-    for (int j = 0; j < C::NT; ++j) {
-        const uint32_t a = xsb + (gl * C::TAB_ROW + 8 * j) * 4;
-        const uint2 v0 = lds64(a), v1 = lds64(a + 16 * 4), v2 = lds64(a + 32 * 4);
-        xs[j][0] = __uint_as_float(v0.x);
-        xs[j][1] = __uint_as_float(v0.y);
-        xf2[j][0] = __uint_as_float(v1.x);
-        xf2[j][1] = __uint_as_float(v1.y);
-        zz[j][0] = __uint_as_float(v2.x);
-        zz[j][1] = __uint_as_float(v2.y);
-    }
-    // acc += s (f tmp - z) + b xs, per feature row.
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            float s, b;
-            if constexpr (C::STMA) {
-                const uint32_t a = sb[h] + i * 16 * 16 + 2 * gl;
-                s = bf16_to_f32_fma(lds16(a), P.k65536);
-                b = bf16_to_f32_fma(lds16(a + C::S_BYTES), P.k65536);
-            } else {
-                const int n = tile_row0 + L.row[h] + 16 * i;
-                if (n < p.N) {
-                    const size_t idx = (size_t)n * p.GT + G;
-                    s = bf16_bits_to_float(__ldg(p.scales + idx));
-                    b = bf16_bits_to_float(__ldg(p.biases + idx));
                 } else {
-                    s = 0.f;
-                    b = 0.f;
+                    // bytes (0, 2) in place and (1, 3) shifted: low nibbles 1024 + q_lo,
+                    // high nibbles 1024 + 16 q_hi, against the same x
+                    const uint32_t b0 = R.xb[nt][2 * wi], b1 = R.xb[nt][2 * wi + 1];
+#pragma unroll
+                    for (int i = 0; i < NB; ++i) {
+                        const uint32_t v0 = R.w[i][0][wi], v1 = R.w[i][1][wi];
+                        const uint32_t t0 = v0 >> 8, t1 = v1 >> 8;
+                        const uint32_t a0 = unpack<kLoNib>(v0, mag1024), a1 = unpack<kLoNib>(v1, mag1024);
+                        const uint32_t a2 = unpack<kLoNib>(t0, mag1024), a3 = unpack<kLoNib>(t1, mag1024);
+                        if (first) mma_f16_c(d[i], a0, a1, a2, a3, b0, b1, c0, c1);
+                        else mma_f16(d[i], a0, a1, a2, a3, b0, b1);
+                    }
+#pragma unroll
+                    for (int i = 0; i < NB; ++i) {
+                        const uint32_t v0 = R.w[i][0][wi], v1 = R.w[i][1][wi];
+                        const uint32_t t0 = v0 >> 8, t1 = v1 >> 8;
+                        mma_f16(d[i], unpack<kHiNib>(v0, mag1024), unpack<kHiNib>(v1, mag1024),
+                                unpack<kHiNib>(t0, mag1024), unpack<kHiNib>(t1, mag1024), b0, b1);
+                    }
                 }
             }
+            if (nt == C::NT - 1 && sg == C::SEGS - 1) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(release);
+            }
+            const int col = (x.s * C::STAGE_K + kl * C::UNIT_K + sg * C::SEG_K) / C::GROUP;
+            const uint32_t sa = x.sb + o.sb + 2 * (col - x.sbcol0);
+            const uint32_t ba = sa + p.R * 16;
 #pragma unroll
-            for (int j = 0; j < C::NT; ++j)
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const float t = fmaf(xf2[j][e], tmp[i][j][2 * h + e], -zz[j][e]);
-                    acc[i][j][2 * h + e] = fmaf(s, t, fmaf(b, xs[j][e], acc[i][j][2 * h + e]));
+            for (int i = 0; i < NB; ++i) {
+                float e0 = d[i][0], e1 = d[i][1], e2 = d[i][2], e3 = d[i][3];
+                if (R.slow[sg]) {
+                    e0 *= R.tf[sg][nt][0];
+                    e1 *= R.tf[sg][nt][1];
+                    e2 *= R.tf[sg][nt][0];
+                    e3 *= R.tf[sg][nt][1];
                 }
+                float s0, s1, b0, b1;
+                if constexpr (C::STMA) {
+                    const uint32_t bo = 4 * 16 * 16 * i;  // block i: 64 rows down
+                    s0 = bf16_to_f32_fma(lds16(sa + bo), k65536);
+                    s1 = bf16_to_f32_fma(lds16(sa + bo + 8 * 16), k65536);
+                    b0 = bf16_to_f32_fma(lds16(ba + bo), k65536);
+                    b1 = bf16_to_f32_fma(lds16(ba + bo + 8 * 16), k65536);
+                } else {
+                    const int n0 = x.tile_row0 + 16 * (qd + 4 * i) + pr, n1 = n0 + 8;
+                    const bool in_k = col < p.GT;
+                    const bool ok0 = n0 < p.N && in_k, ok1 = n1 < p.N && in_k;
+                    const size_t i0 = (size_t)n0 * p.GT + col, i1 = (size_t)n1 * p.GT + col;
+                    s0 = ok0 ? bf16_bits_to_float(__ldg(p.scales + i0)) : 0.f;
+                    b0 = ok0 ? bf16_bits_to_float(__ldg(p.biases + i0)) : 0.f;
+                    s1 = ok1 ? bf16_bits_to_float(__ldg(p.scales + i1)) : 0.f;
+                    b1 = ok1 ? bf16_bits_to_float(__ldg(p.biases + i1)) : 0.f;
+                }
+                float* a = acc[i][nt];
+                a[0] = fmaf(s0, e0, fmaf(b0, R.txs[sg][nt][0], a[0]));
+                a[1] = fmaf(s0, e1, fmaf(b0, R.txs[sg][nt][1], a[1]));
+                a[2] = fmaf(s1, e2, fmaf(b1, R.txs[sg][nt][0], a[2]));
+                a[3] = fmaf(s1, e3, fmaf(b1, R.txs[sg][nt][1], a[3]));
+            }
         }
-}
-
-// This warp's groups of one stage: all of them (PAR < 0) or those with gl % 2 == PAR.
-// CHECK: the stage is the first or last of a segment and some of its groups fall
-// outside [ga, gb).
-template <class C, bool CHECK, int PAR>
-__device__ __forceinline__ void consume_stage(const LaneLayout<C>& L, const Pinned& P, uint32_t st, int sc, int ga,
-                                              int gb, int tq, int tile_row0, const Params& p,
-                                              float (&acc)[2][C::NT][4]) {
-    const uint32_t wb[2] = {st + L.wofs[0], st + L.wofs[1]};
-    const uint32_t xb = st + C::W_BYTES;
-    const uint32_t s0 = st + C::W_BYTES + C::X_BYTES + 2 * ((sc * C::GPS) & 7);
-    const uint32_t sb[2] = {s0 + L.row[0] * 16, s0 + L.row[1] * 16};
-    const uint32_t xsb = st + C::XS_OFF + 2 * tq * 4;
-#pragma unroll
-    for (int gl = 0; gl < C::GPS; ++gl) {
-        if (PAR >= 0 && (gl & 1) != PAR) continue;
-        const int G = sc * C::GPS + gl;
-        if (CHECK && (G < ga || G >= gb)) continue;
-        consume_group<C>(L, P, wb, xb, sb, xsb, gl, G, tile_row0, p, acc);
     }
 }
 
-// Writes the fp32 tile in `red` ([NT*8][kRedPitch]) to y as bf16.
+// The stages of one tile for one consumer warp with NB blocks.
+template <class C, int NB>
+__device__ __forceinline__ void run_tile(const Params& p, Bars* bars, volatile int* abort, uint32_t ring,
+                                         uint32_t sbring, const LaneOfs& o, int kl, int qd, int pr, int lane,
+                                         int s_beg, int s_end, int tile_row0, uint32_t mag1024, uint32_t mag64,
+                                         uint32_t k65536, int& slot, int& ph, int& qslot, int& qph,
+                                         float (&acc)[4][C::NT][4]) {
+    const uint32_t wbytes = (uint32_t)p.R * kRowBytes;
+    StageCtx cx;
+    cx.tile_row0 = tile_row0;
+    cx.sb = sbring;
+    cx.sbcol0 = 0;
+    for (int s = s_beg; s < s_end; ++s) {
+        if (C::STMA && (s == s_beg || s % C::SBP == 0)) {
+            mbar_wait_bounded(&bars->sbfull[qslot], qph, abort, DFLASH_DEVERR_QMM_PIPELINE);
+            cx.sb = sbring + qslot * p.sb_bytes;
+            cx.sbcol0 = (s / C::SBP) * 8;
+        }
+        const bool ready = mbar_wait_bounded(&bars->full[slot], ph, abort, DFLASH_DEVERR_QMM_PIPELINE);
+        if constexpr (NB > 0) {
+            if (ready) {
+                cx.wb = ring + slot * p.stage_bytes;
+                cx.pkt = cx.wb + wbytes;
+                cx.s = s;
+                StageRegs<C, NB> R;
+                load_stage<C, NB>(R, cx.wb, cx.pkt, o);
+                compute_stage<C, NB>(R, cx, p, o, kl, qd, pr, mag1024, mag64, k65536, lane, &bars->empty[slot], acc);
+            }
+        }
+        if (NB == 0 || !ready) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->empty[slot]);
+        }
+        if (++slot == p.NS) {
+            slot = 0;
+            ph ^= 1;
+        }
+        if (C::STMA && (s == s_end - 1 || (s + 1) % C::SBP == 0)) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->sbempty[qslot]);
+            if (++qslot == p.NSB) {
+                qslot = 0;
+                qph ^= 1;
+            }
+        }
+    }
+}
+
+// Producer: the j-th stage of a CTA is stage s_beg + j % nstages of tile
+// cid + (j / nstages) ncl; scale/bias slots open at the CTA's first stage of a tile and
+// at every multiple of SBP.  Returns false when a bounded wait gave up.
 template <class C>
-__device__ __forceinline__ void write_tile(const float* red, int t, const Params& p, int ctid) {
-    const int n0 = t * kRows;
-    if (p.y_vec) {
-        for (int idx = ctid; idx < C::NT * 8 * (kRows / 8); idx += kConsumerThreads) {
-            const int m = idx / (kRows / 8), r0 = (idx % (kRows / 8)) * 8;
-            if (m >= p.M || n0 + r0 >= p.N) continue;
-            const float4 a = *reinterpret_cast<const float4*>(red + m * kRedPitch + r0);
-            const float4 b = *reinterpret_cast<const float4*>(red + m * kRedPitch + r0 + 4);
-            __nv_bfloat162 o0 = __floats2bfloat162_rn(a.x, a.y), o1 = __floats2bfloat162_rn(a.z, a.w);
-            __nv_bfloat162 o2 = __floats2bfloat162_rn(b.x, b.y), o3 = __floats2bfloat162_rn(b.z, b.w);
-            uint4 v;
-            v.x = *reinterpret_cast<uint32_t*>(&o0);
-            v.y = *reinterpret_cast<uint32_t*>(&o1);
-            v.z = *reinterpret_cast<uint32_t*>(&o2);
-            v.w = *reinterpret_cast<uint32_t*>(&o3);
-            *reinterpret_cast<uint4*>(p.y + (size_t)m * p.N + n0 + r0) = v;
-        }
-    } else {
-        for (int idx = ctid; idx < C::NT * 8 * kRows; idx += kConsumerThreads) {
-            const int m = idx / kRows, r = idx % kRows;
-            if (m >= p.M || n0 + r >= p.N) continue;
-            __nv_bfloat16 o = __float2bfloat16_rn(red[m * kRedPitch + r]);
-            p.y[(size_t)m * p.N + n0 + r] = *reinterpret_cast<uint16_t*>(&o);
-        }
+__device__ __forceinline__ bool issue_stage(int j, bool with_packet, int& pq, Bars* bars, volatile int* abort,
+                                            const CUtensorMap& tm_w, const CUtensorMap& tm_s,
+                                            const CUtensorMap& tm_b, const Params& p, uint32_t ring, uint32_t sbring,
+                                            int cid, int ncl, int s_beg, int nstages, uint32_t wbytes) {
+    const int t = cid + (j / nstages) * ncl, s = s_beg + j % nstages;
+    if (C::STMA && (s == s_beg || s % C::SBP == 0)) {
+        const int q = pq % p.NSB;
+        if (!mbar_wait_bounded(&bars->sbempty[q], ((pq / p.NSB) & 1) ^ 1, abort, DFLASH_DEVERR_QMM_PIPELINE))
+            return false;
+        mbar_arrive_expect_tx(&bars->sbfull[q], 2u * p.R * 16);
+        const uint32_t dst = sbring + q * p.sb_bytes;
+        tma_load_2d_u32(dst, &tm_s, &bars->sbfull[q], (s / C::SBP) * 8, t * p.R);
+        tma_load_2d_u32(dst + p.R * 16, &tm_b, &bars->sbfull[q], (s / C::SBP) * 8, t * p.R);
+        ++pq;
     }
+    const int slot = j % p.NS;
+    if (!mbar_wait_bounded(&bars->empty[slot], ((j / p.NS) & 1) ^ 1, abort, DFLASH_DEVERR_QMM_PIPELINE))
+        return false;
+    const uint32_t st = ring + slot * p.stage_bytes;
+    mbar_arrive_expect_tx(&bars->full[slot], wbytes + C::PKT);
+    tma_load_2d_u32(st, &tm_w, &bars->full[slot], s * (kRowBytes / 4), t * p.R);
+    if (with_packet) bulk_copy_g2s(st + wbytes, p.packets + (size_t)s * C::PKT, C::PKT, &bars->full[slot]);
+    return true;
 }
 
 template <class C>
 __global__ void __launch_bounds__(kThreads, 1)
-    qmm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-               const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_b,
-               const __grid_constant__ CUtensorMap tm_xs, const Params p) {
-    extern __shared__ uint8_t smem_raw[];
+    qmm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
+               const __grid_constant__ CUtensorMap tm_b, const Params p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float* red = reinterpret_cast<float*>(smem + kStages * C::STAGE_BYTES);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * C::STAGE_BYTES + C::RED_FLOATS * 4);
-    uint64_t* empty = full + kStages;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
+    Bars* bars = reinterpret_cast<Bars*>(smem + p.bar_off);
+    volatile int* abort = &bars->abort;
+    const uint32_t ring = smem_u32(smem);
+    const uint32_t sbring = ring + p.NS * p.stage_bytes;
 
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t rank = cluster_rank(), cs = cluster_size();
+    const int cid = (int)cluster_id(), ncl = (int)nclusters_x();
+    const int s_beg = (int)((long long)p.S * rank / cs), s_end = (int)((long long)p.S * (rank + 1) / cs);
+    const int nstages = s_end - s_beg;
+    const int my_tiles = (nstages > 0 && cid < p.ntiles) ? (p.ntiles - 1 - cid) / ncl + 1 : 0;
+    const int total = my_tiles * nstages;
+    const int first_batch = total < p.NS ? total : p.NS;
+    const uint32_t wbytes = (uint32_t)p.R * kRowBytes;
 
     pdl_launch_dependents();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], C::EMPTY_ARRIVALS);
-        }
-        *abort_flag = 0;
 
+    int issued = 0, pq = 0;  // stages and scale/bias slots issued (producer thread)
+    if (tid == kConsumerThreads) {
+        for (int i = 0; i < p.NS; ++i) {
+            mbar_init(&bars->full[i], 1);
+            mbar_init(&bars->empty[i], kConsumerWarps);
+        }
+        for (int i = 0; i < p.NSB; ++i) {
+            mbar_init(&bars->sbfull[i], 1);
+            mbar_init(&bars->sbempty[i], kConsumerWarps);
+        }
+        mbar_init(&bars->xfull, 1);
+        mbar_init(&bars->xdone, 1);
+        bars->abort = 0;
         fence_barrier_init();
     }
+    // publishes the exchange barriers to the peer; its wait comes after the first loads
+    __syncwarp();
+    cluster_arrive_relaxed();
+    if (tid == kConsumerThreads) {
+        // The first ring's worth of weight boxes goes out before anything else: fresh
+        // slots, so these never wait.  Their x packets follow once the prep kernel is done.
+        for (; issued < first_batch; ++issued)
+            issue_stage<C>(issued, false, pq, bars, abort, tm_w, tm_s, tm_b, p, ring, sbring, cid, ncl, s_beg,
+                           nstages, wbytes);
+    }
     __syncthreads();
+    cluster_wait();
 
-    const long long c = blockIdx.x;
-    const long long u0 = range_begin(c, p), u1 = range_begin(c + 1, p);
-    const int first_tile = (int)(u0 / p.GT);
-
-    if (warp == kConsumerWarps) {
-        // ------------------------------------------------------------ producer
-        if (lane != 0) return;
-        prefetch_tensormap(&tm_w);
-        prefetch_tensormap(&tm_x);
-        prefetch_tensormap(&tm_xs);
-        if constexpr (C::STMA) {
-            prefetch_tensormap(&tm_s);
-            prefetch_tensormap(&tm_b);
+    if (warp >= kConsumerWarps) {
+        // ---------------------------------------------------------------- producer
+        regs_lower<kProducerRegs>();
+        if (tid == kConsumerThreads && total > 0) {
+            pdl_wait();  // the packets come from the prep kernel
+            for (int j = 0; j < first_batch; ++j)
+                bulk_copy_g2s(ring + j * p.stage_bytes + wbytes, p.packets + (size_t)(s_beg + j % nstages) * C::PKT,
+                              C::PKT, &bars->full[j]);
+            while (issued < total && issue_stage<C>(issued, true, pq, bars, abort, tm_w, tm_s, tm_b, p, ring, sbring,
+                                                     cid, ncl, s_beg, nstages, wbytes))
+                ++issued;
+            if (*abort) {
+                // let every copy already issued land before shared memory is released
+                const int lo = issued > p.NS ? issued - p.NS : 0;
+                for (int j = lo; j < issued; ++j) mbar_drain(&bars->full[j % p.NS], (j / p.NS) & 1);
+                const int qlo = pq > p.NSB ? pq - p.NSB : 0;
+                for (int j = qlo; j < pq; ++j) mbar_drain(&bars->sbfull[j % p.NSB], (j / p.NSB) & 1);
+            }
         }
-        // Stage j covers groups [sc*GPS, sc*GPS+GPS) of row tile t.  The weight-side
-        // loads (W, scales, biases) of the first ring fill go out before the grid
-        // dependency resolves; x and its group sums only after it.
-        int j = 0;
-        bool ok = true, dep_resolved = false;
-        int pend_sc[kStages];
-        int n_pend = 0;
-        auto issue_x = [&](int slot, int sc) {
-            uint8_t* st = smem + slot * C::STAGE_BYTES;
+    } else {
+        // ---------------------------------------------------------------- consumers
+        regs_raise<kConsumerRegs>();
+        if (total == 0) goto done;
+        const int kl = warp & (kKLanes - 1), qd = warp / kKLanes;
+        const int g = lane >> 2, tq = lane & 3;
+        const int nblk = p.nb > qd ? (p.nb - qd + 3) / 4 : 0;  // blocks qd, qd + 4, ... below nb
+        const int pr = phys_row(g);
+        const uint32_t mag1024 = pinned<kMag1024>(), mag64 = pinned<kMag64>(), k65536 = pinned<65536u>();
+        const LaneOfs lo = lane_offsets<C>(kl, qd, g, tq);
+        float* bufa = reinterpret_cast<float*>(smem + p.red_off);
+        float* bufb = reinterpret_cast<float*>(smem + p.red_off + p.red_bytes);
+        float* recv = reinterpret_cast<float*>(smem + p.recv_off);
+        constexpr int MR = C::MR;
+        pdl_wait();  // y may still be read or written by the preceding kernel
+        int slot = 0, ph = 0, qslot = 0, qph = 0, tt = 0;
+        for (int t = cid; t < p.ntiles; t += ncl, ++tt) {
+            float acc[4][C::NT][4];
 #pragma unroll
-            for (int b = 0; b < C::XBOX; ++b)
-                tma_load_2d(st + C::W_BYTES + b * C::XBOX_BYTES, &tm_x, &full[slot], sc * C::KPS + 64 * b, 0);
-            tma_load_2d(st + C::XS_OFF, &tm_xs, &full[slot], 0, sc * C::GPS);
-        };
-        for (long long u = u0; u < u1 && ok;) {
-            const int t = (int)(u / p.GT);
-            const int ga = (int)(u - (long long)t * p.GT);
-            const int gb = (int)min((long long)p.GT, u1 - (long long)t * p.GT);
-            for (int sc = ga / C::GPS; sc < (gb + C::GPS - 1) / C::GPS; ++sc, ++j) {
-                const int slot = j % kStages;
-                const uint32_t ph = (uint32_t)(j / kStages) & 1u;
-                if (!dep_resolved && j == kStages) {
-                    pdl_wait();
-                    dep_resolved = true;
-                    for (int i = 0; i < n_pend; ++i) issue_x(i, pend_sc[i]);
-                }
-                if (!mbar_wait_bounded(&empty[slot], ph ^ 1u, abort_flag, DFLASH_DEVERR_QMM_PIPELINE)) {
-                    ok = false;
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int nt = 0; nt < C::NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc[i][nt][e] = 0.f;
+            switch (nblk) {
+                case 4:
+                    run_tile<C, 4>(p, bars, abort, ring, sbring, lo, kl, qd, pr, lane, s_beg, s_end, t * p.R, mag1024,
+                                   mag64, k65536, slot, ph, qslot, qph, acc);
                     break;
-                }
-                uint8_t* st = smem + slot * C::STAGE_BYTES;
-                mbar_arrive_expect_tx(&full[slot], C::TX_BYTES);
-                tma_load_2d(st, &tm_w, &full[slot], sc * (kRowBytes / 4), t * kRows);
-                if constexpr (C::STMA) {
-                    const int gx = (sc * C::GPS) & ~7;
-                    tma_load_2d(st + C::W_BYTES + C::X_BYTES, &tm_s, &full[slot], gx, t * kRows);
-                    tma_load_2d(st + C::W_BYTES + C::X_BYTES + C::S_BYTES, &tm_b, &full[slot], gx, t * kRows);
-                }
-                if (dep_resolved) {
-                    issue_x(slot, sc);
-                } else {
-                    pend_sc[n_pend++] = sc;
+                case 3:
+                    run_tile<C, 3>(p, bars, abort, ring, sbring, lo, kl, qd, pr, lane, s_beg, s_end, t * p.R, mag1024,
+                                   mag64, k65536, slot, ph, qslot, qph, acc);
+                    break;
+                case 2:
+                    run_tile<C, 2>(p, bars, abort, ring, sbring, lo, kl, qd, pr, lane, s_beg, s_end, t * p.R, mag1024,
+                                   mag64, k65536, slot, ph, qslot, qph, acc);
+                    break;
+                case 1:
+                    run_tile<C, 1>(p, bars, abort, ring, sbring, lo, kl, qd, pr, lane, s_beg, s_end, t * p.R, mag1024,
+                                   mag64, k65536, slot, ph, qslot, qph, acc);
+                    break;
+                default:  // no block of this tile: keep the ring moving
+                    run_tile<C, 0>(p, bars, abort, ring, sbring, lo, kl, qd, pr, lane, s_beg, s_end, t * p.R, mag1024,
+                                   mag64, k65536, slot, ph, qslot, qph, acc);
+            }
+
+            // ---- tile epilogue.  Within the CTA: ((k-lane 0 + 1) + (k-lane 2 + 3)) through
+            // bufa/bufb; then the k-lane 0 warps hold the CTA's sum of their blocks and push
+            // the blocks the peer writes into the peer's recv buffer.
+            if (tt > 0) named_bar_sync(kBarConsumers, kConsumerThreads);  // last tile's bufa/bufb readers are done
+            if (kl & 1) {
+                float* buf = kl == 1 ? bufa : bufb;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (i >= nblk) break;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int nt = 0; nt < C::NT; ++nt)
+                            *reinterpret_cast<float2*>(buf + (16 * (qd + 4 * i) + pr + 8 * h) * MR + 8 * nt + 2 * tq) =
+                                make_float2(acc[i][nt][2 * h], acc[i][nt][2 * h + 1]);
                 }
             }
-            u = (long long)t * p.GT + gb;
-        }
-        if (!dep_resolved) {
-            pdl_wait();
-            for (int i = 0; i < n_pend; ++i) issue_x(i, pend_sc[i]);
-        }
-        // Drain: do not leave the CTA while issued copies may still be landing.
-        for (int i = max(0, j - kStages); i < j; ++i) {
-            const int slot = i % kStages;
-            const uint32_t ph = (uint32_t)(i / kStages) & 1u;
-            const unsigned long long t0 = globaltimer_ns();
-            while (!mbar_try_wait(&full[slot], ph) && globaltimer_ns() - t0 < kWaitLimitNs) {
+            named_bar_sync(kBarConsumers, kConsumerThreads);
+            if (!(kl & 1)) {
+                float* buf = kl == 0 ? bufa : bufb;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (i >= nblk) break;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int nt = 0; nt < C::NT; ++nt) {
+                            float2* q = reinterpret_cast<float2*>(buf + (16 * (qd + 4 * i) + pr + 8 * h) * MR + 8 * nt +
+                                                                  2 * tq);
+                            const float2 o = *q;
+                            acc[i][nt][2 * h] += o.x;
+                            acc[i][nt][2 * h + 1] += o.y;
+                            if (kl == 2) *q = make_float2(acc[i][nt][2 * h], acc[i][nt][2 * h + 1]);
+                        }
+                }
             }
-        }
-        return;
-    }
-
-    // -------------------------------------------------------------- consumers
-    pdl_wait();  // y and the workspace may still be in use by the previous call
-    const int rs = warp % kRowSlices, par = warp / kRowSlices;
-    const int g = lane >> 2, tq = lane & 3;
-    const int rb = rs * 32;
-    const LaneLayout<C> L = lane_layout<C>(rb, g, tq);
-    const Pinned P = make_pinned();
-    const int ctid = threadIdx.x;  // 0 .. kConsumerThreads-1
-    int j = 0;
-
-    for (long long u = u0; u < u1;) {
-        const int t = (int)(u / p.GT);
-        const int ga = (int)(u - (long long)t * p.GT);
-        const int gb = (int)min((long long)p.GT, u1 - (long long)t * p.GT);
-        const int tile_row0 = t * kRows;
-
-        float acc[2][C::NT][4];
+            named_bar_sync(kBarConsumers, kConsumerThreads);
+            if (kl == 0) {
+                const int own0 = cs > 1 ? (rank == 0 ? 0 : p.nb0) : 0;
+                const int own1 = cs > 1 ? (rank == 0 ? p.nb0 : p.nb) : p.nb;
+                const int peer0 = rank == 0 ? p.nb0 : 0;  // first block the peer writes
 #pragma unroll
-        for (int i = 0; i < 2; ++i)
+                for (int i = 0; i < 4; ++i) {
+                    if (i >= nblk) break;
 #pragma unroll
-            for (int jj = 0; jj < C::NT; ++jj)
+                    for (int h = 0; h < 2; ++h)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) acc[i][jj][e] = 0.f;
-
-        for (int sc = ga / C::GPS; sc < (gb + C::GPS - 1) / C::GPS; ++sc, ++j) {
-            if (!C::SPLIT && (j % kKSplit) != par) continue;
-            const int slot = j % kStages;
-            const uint32_t ph = (uint32_t)(j / kStages) & 1u;
-            // mma.sync below is warp-collective: every lane must take the same branch
-            const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[slot], ph, abort_flag,
-                                                                       DFLASH_DEVERR_QMM_PIPELINE));
-            if (ok) {
-                const uint32_t st = smem_u32(smem + slot * C::STAGE_BYTES);
-                const bool whole = sc * C::GPS >= ga && sc * C::GPS + C::GPS <= gb;
-                if constexpr (C::SPLIT) {
-                    if (par == 0) {
-                        if (whole) consume_stage<C, false, 0>(L, P, st, sc, ga, gb, tq, tile_row0, p, acc);
-                        else consume_stage<C, true, 0>(L, P, st, sc, ga, gb, tq, tile_row0, p, acc);
-                    } else {
-                        if (whole) consume_stage<C, false, 1>(L, P, st, sc, ga, gb, tq, tile_row0, p, acc);
-                        else consume_stage<C, true, 1>(L, P, st, sc, ga, gb, tq, tile_row0, p, acc);
+                        for (int nt = 0; nt < C::NT; ++nt) {
+                            const float2 o = *reinterpret_cast<const float2*>(
+                                bufb + (16 * (qd + 4 * i) + pr + 8 * h) * MR + 8 * nt + 2 * tq);
+                            acc[i][nt][2 * h] += o.x;
+                            acc[i][nt][2 * h + 1] += o.y;
+                        }
+                }
+                if (cs > 1) {
+                    if (tt > 0)  // the peer has read what we pushed for the previous tile
+                        mbar_wait_cluster_bounded(&bars->xdone, (tt - 1) & 1, abort, DFLASH_DEVERR_QMM_REDUCE);
+                    const uint32_t peer = rank ^ 1u;
+                    const uint32_t peer_recv = map_to_rank(smem_u32(recv), peer);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        if (i >= nblk) break;
+                        const int b = qd + 4 * i;
+                        if (b >= own0 && b < own1) continue;
+#pragma unroll
+                        for (int h = 0; h < 2; ++h)
+#pragma unroll
+                            for (int nt = 0; nt < C::NT; ++nt)
+                                st_cluster_f32x2(
+                                    peer_recv + (uint32_t)((16 * (b - peer0) + pr + 8 * h) * MR + 8 * nt + 2 * tq) * 4u,
+                                    acc[i][nt][2 * h], acc[i][nt][2 * h + 1]);
                     }
-                } else {
-                    if (whole) consume_stage<C, false, -1>(L, P, st, sc, ga, gb, tq, tile_row0, p, acc);
-                    else consume_stage<C, true, -1>(L, P, st, sc, ga, gb, tq, tile_row0, p, acc);
+                    fence_acq_rel_cluster();
+                    named_bar_sync(kBarLane0, kConsumerThreads / kKLanes);
+                    if (tid == 0) mbar_arrive_remote(map_to_rank(smem_u32(&bars->xfull), peer));
+                    mbar_wait_cluster_bounded(&bars->xfull, tt & 1, abort, DFLASH_DEVERR_QMM_REDUCE);
+                }
+                // write the blocks this CTA owns: rank 0's partial first, then rank 1's
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (i >= nblk) break;
+                    const int b = qd + 4 * i;
+                    if (b < own0 || b >= own1) continue;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int row = 16 * b + pr + 8 * h;
+                        const int n = t * p.R + row;
+#pragma unroll
+                        for (int nt = 0; nt < C::NT; ++nt)
+#pragma unroll
+                            for (int e = 0; e < 2; ++e) {
+                                const int m = 8 * nt + 2 * tq + e;
+                                float v = acc[i][nt][2 * h + e];
+                                if (cs > 1) {
+                                    const float o = recv[(16 * (b - own0) + pr + 8 * h) * MR + m];
+                                    v = rank == 0 ? v + o : o + v;
+                                }
+                                if (m < p.M && n < p.N) {
+                                    const __nv_bfloat16 o = __float2bfloat16_rn(v);
+                                    p.y[(size_t)m * p.N + n] = *reinterpret_cast<const uint16_t*>(&o);
+                                }
+                            }
+                    }
+                }
+                if (cs > 1) {
+                    named_bar_sync(kBarLane0, kConsumerThreads / kKLanes);
+                    if (tid == 0) mbar_arrive_remote(map_to_rank(smem_u32(&bars->xdone), rank ^ 1u));
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-        }
-
-        // ---- reduce the two stage-parity halves into `red`
-        named_bar_sync(kBarConsumers, kConsumerThreads);
-        if (par == 1) {
-#pragma unroll
-            for (int i = 0; i < 2; ++i)
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-#pragma unroll
-                    for (int jj = 0; jj < C::NT; ++jj)
-#pragma unroll
-                        for (int e = 0; e < 2; ++e)
-                            red[(8 * jj + 2 * tq + e) * kRedPitch + L.row[h] + 16 * i] = acc[i][jj][2 * h + e];
-        }
-        named_bar_sync(kBarConsumers, kConsumerThreads);
-        if (par == 0) {
-#pragma unroll
-            for (int i = 0; i < 2; ++i)
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-#pragma unroll
-                    for (int jj = 0; jj < C::NT; ++jj)
-#pragma unroll
-                        for (int e = 0; e < 2; ++e)
-                            red[(8 * jj + 2 * tq + e) * kRedPitch + L.row[h] + 16 * i] += acc[i][jj][2 * h + e];
-        }
-        named_bar_sync(kBarConsumers, kConsumerThreads);
-
-        if (ga == 0 && gb == p.GT) {
-            write_tile<C>(red, t, p, ctid);
-        } else {
-            // ---- a tile cut between CTAs: publish this CTA's share as an fp32 partial
-            // in its slot (0: the tile is this CTA's first segment, 1: its last); the
-            // fixup kernel adds the contributors' partials in CTA order.
-            constexpr int TILE_FLOATS = C::NT * 8 * kRows;
-            const int slot = (t == first_tile) ? 0 : 1;
-            float* dst = p.partials + (size_t)(c * 2 + slot) * TILE_FLOATS;
-            for (int idx = ctid; idx < TILE_FLOATS / 4; idx += kConsumerThreads) {
-                const int m = idx / (kRows / 4), r4 = (idx % (kRows / 4)) * 4;
-                __stcg(reinterpret_cast<float4*>(dst + m * kRows + r4),
-                       *reinterpret_cast<const float4*>(red + m * kRedPitch + r4));
-            }
-        }
-        named_bar_sync(kBarConsumers, kConsumerThreads);
-        u = (long long)t * p.GT + gb;
-    }
-}
-
-// ------------------------------------------------------------------ fixup kernel
-//
-// One block per row tile.  A tile covered whole by one CTA was written by the main
-// kernel; for a tile cut between CTAs cf..cl the block sums their partials (slot 0 when
-// the tile is the CTA's first segment, else 1) in CTA order and writes y.
-template <int NT>
-__global__ void __launch_bounds__(256) qmm_fixup_kernel(const Params p) {
-    pdl_launch_dependents();
-    pdl_wait();  // the main kernel's partials
-    const int t = blockIdx.x;
-    const long long cf = owner_of((long long)t * p.GT, p);
-    const long long cl = owner_of((long long)(t + 1) * p.GT - 1, p);
-    if (cf == cl) return;
-    constexpr int TILE_FLOATS = NT * 8 * kRows;
-    const int n0 = t * kRows;
-    for (int idx = threadIdx.x; idx < TILE_FLOATS / 4; idx += blockDim.x) {
-        const int m = idx / (kRows / 4), r4 = (idx % (kRows / 4)) * 4;
-        if (m >= p.M) break;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (long long cc = cf; cc <= cl; ++cc) {
-            const int sl = ((int)(range_begin(cc, p) / p.GT) == t) ? 0 : 1;
-            const float4 q = __ldcg(reinterpret_cast<const float4*>(p.partials + (size_t)(cc * 2 + sl) * TILE_FLOATS +
-                                                                    m * kRows + r4));
-            v.x += q.x;
-            v.y += q.y;
-            v.z += q.z;
-            v.w += q.w;
-        }
-        const float vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int n = n0 + r4 + e;
-            if (n < p.N) {
-                __nv_bfloat16 o = __float2bfloat16_rn(vv[e]);
-                p.y[(size_t)m * p.N + n] = *reinterpret_cast<uint16_t*>(&o);
-            }
         }
     }
+done:
+    // no CTA leaves while a peer may still write to or read its shared memory
+    __syncwarp();
+    cluster_sync_all();
 }
 
 // ------------------------------------------------------------------ host side
@@ -759,25 +921,85 @@ struct Shape {
     int M, N, K, group, bits;
 };
 
-inline int n_tiles(int N) { return (N + kRows - 1) / kRows; }
+struct Plan {
+    int cs, nclusters, R, nb, nb0, ntiles, S, NS, NSB;
+    uint32_t stage_bytes, sb_bytes, red_off, red_bytes, recv_off, bar_off;
+    size_t smem;
+};
 
-// Launch with programmatic stream serialization: the kernel may begin while the
-// previous kernel in the stream is still running; griddepcontrol.wait in the kernel
-// orders everything that depends on it.
-template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                       Args&&... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+template <class C>
+inline int stages_along_k(int K) {
+    return (K + C::STAGE_K - 1) / C::STAGE_K;
+}
+
+inline uint32_t round_up_u32(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
+// Scale/bias slots the producer opens within its first `ns` stage issues (the only
+// issues made before any consumer runs, so the ring must hold them all).
+template <class C>
+int first_batch_sb_slots(int S, int cs, int ns) {
+    int worst = 0;
+    for (int rank = 0; rank < cs; ++rank) {
+        const int s_beg = (int)((long long)S * rank / cs), s_end = (int)((long long)S * (rank + 1) / cs);
+        const int nst = s_end - s_beg;
+        if (nst <= 0) continue;
+        int slots = 0;
+        for (int j = 0; j < ns; ++j) {
+            const int s = s_beg + j % nst;
+            if (s == s_beg || s % C::SBP == 0) ++slots;
+        }
+        worst = slots > worst ? slots : worst;
+    }
+    return worst;
+}
+
+// Tile height and grid: clusters of 2 CTAs (one per SM) split K in halves; tiles of at
+// most 256 rows, sized so that every cluster gets the same number of tiles (to within
+// one) and the tiles the same height; then the deepest ring that fits.
+template <class C>
+Plan make_plan(const Shape& s, int sms) {
+    Plan pl;
+    pl.S = stages_along_k<C>(s.K);
+    pl.cs = pl.S >= 2 ? kMaxCluster : 1;
+    const int cmax = sms / pl.cs > 0 ? sms / pl.cs : 1;
+    const int NB = (s.N + 15) / 16;
+    const int T = (NB + kMaxTileBlocks * cmax - 1) / (kMaxTileBlocks * cmax);  // tiles per cluster
+    int nb = (NB + cmax * T - 1) / (cmax * T);
+    if (nb > kMaxTileBlocks) nb = kMaxTileBlocks;
+    if (nb < 1) nb = 1;
+    pl.nb = nb;
+    pl.nb0 = (nb + 1) / 2;
+    pl.R = 16 * nb;
+    pl.ntiles = (s.N + pl.R - 1) / pl.R;
+    pl.nclusters = pl.ntiles < cmax ? pl.ntiles : cmax;
+    pl.stage_bytes = round_up_u32((uint32_t)pl.R * kRowBytes + C::PKT, 1024);
+    pl.sb_bytes = C::STMA ? round_up_u32(2u * pl.R * 16, 128) : 0;
+    pl.red_bytes = round_up_u32((uint32_t)pl.R * C::MR * 4, 128);
+    const uint32_t recv_bytes = round_up_u32((uint32_t)pl.nb0 * 16 * C::MR * 4, 128);
+    const uint32_t bar_bytes = round_up_u32(sizeof(Bars), 128);
+    pl.NS = 0;
+    pl.NSB = 1;
+    for (int ns = kMaxStages; ns >= 2; --ns) {
+        int nsb = 1;
+        if (C::STMA) {
+            nsb = (ns + C::SBP - 1) / C::SBP + 1;
+            const int need = first_batch_sb_slots<C>(pl.S, pl.cs, ns);
+            if (nsb < need) nsb = need;
+            if (nsb > kMaxSbStages) continue;
+        }
+        const size_t total = 1024 + (size_t)ns * pl.stage_bytes + (C::STMA ? (size_t)nsb * pl.sb_bytes : 0) +
+                             2 * (size_t)pl.red_bytes + recv_bytes + bar_bytes;
+        if (total <= (size_t)kSmemLimit) {
+            pl.NS = ns;
+            pl.NSB = nsb;
+            break;
+        }
+    }
+    pl.red_off = pl.NS * pl.stage_bytes + (C::STMA ? pl.NSB * pl.sb_bytes : 0);
+    pl.recv_off = pl.red_off + 2 * pl.red_bytes;
+    pl.bar_off = pl.recv_off + recv_bytes;
+    pl.smem = 1024 + (size_t)pl.bar_off + bar_bytes;
+    return pl;
 }
 
 template <class C>
@@ -785,72 +1007,96 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
            const dflash_bf16* biases, dflash_bf16* y, void* ws, cudaStream_t stream) {
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
+    static int launch_regs = 0;
     std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(qmm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        C::SMEM_BYTES);
+        attr_err = cudaFuncSetAttribute(qmm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+        cudaFuncAttributes fa;
+        if (attr_err == cudaSuccess) attr_err = cudaFuncGetAttributes(&fa, qmm_kernel<C>);
+        if (attr_err == cudaSuccess) launch_regs = fa.numRegs;
     });
     if (attr_err != cudaSuccess)
         return fail(DFLASH_ERR_CUDA, "cudaFuncSetAttribute(qmm): %s", cudaGetErrorString(attr_err));
+    // the warpgroups' setmaxnreg shares must fit the registers the block is launched with
+    if (launch_regs * kThreads < kConsumerThreads * kConsumerRegs + 128 * kProducerRegs)
+        return fail(DFLASH_ERR_UNSUPPORTED, "qmm kernel built with %d registers per thread, %d needed", launch_regs,
+                    kLaunchRegs);
 
-    uint8_t* wsb = reinterpret_cast<uint8_t*>(ws);
-    float* xs = reinterpret_cast<float*>(wsb + xs_offset());
-    uint16_t* xperm = reinterpret_cast<uint16_t*>(wsb + xperm_offset(s.K, s.group));
+    int dev = 0;
+    DFLASH_CUDA_TRY(cudaGetDevice(&dev));
+    const Plan pl = make_plan<C>(s, sm_count(dev));
+    if (pl.NS < 2) return fail(DFLASH_ERR_UNSUPPORTED, "qmm: no shared-memory plan for N=%d K=%d", s.N, s.K);
     const int GT = s.K / s.group;
 
-    CUtensorMap tm_w, tm_x, tm_s, tm_b, tm_xs;
+    CUtensorMap tm_w, tm_s, tm_b;
     int st;
     const uint64_t words = (uint64_t)s.K * s.bits / 32;
     st = encode_tensor_map_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, words, (uint64_t)s.N, words * 4,
-                              kRowBytes / 4, kRows, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    st = encode_tensor_map_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xperm, (uint64_t)s.K, (uint64_t)s.M,
-                              (uint64_t)s.K * 2, 64, C::XROWS, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    st = encode_tensor_map_2d(&tm_xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xs, kTabWidth, (uint64_t)GT, kTabWidth * 4,
-                              C::TAB_ROW, C::GPS, CU_TENSOR_MAP_SWIZZLE_NONE);
+                              kRowBytes / 4, pl.R, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
     if constexpr (C::STMA) {
         st = encode_tensor_map_2d(&tm_s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, scales, (uint64_t)GT, (uint64_t)s.N,
-                                  (uint64_t)GT * 2, 8, kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+                                  (uint64_t)GT * 2, 8, pl.R, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (st) return st;
         st = encode_tensor_map_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, biases, (uint64_t)GT, (uint64_t)s.N,
-                                  (uint64_t)GT * 2, 8, kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+                                  (uint64_t)GT * 2, 8, pl.R, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (st) return st;
     } else {
         tm_s = tm_w;
         tm_b = tm_w;
     }
 
-    int dev = 0;
-    DFLASH_CUDA_TRY(cudaGetDevice(&dev));
     Params p;
-    p.y = y;
+    p.packets = reinterpret_cast<const uint8_t*>(ws);
     p.scales = scales;
     p.biases = biases;
-    p.partials = reinterpret_cast<float*>(wsb);
+    p.y = y;
     p.M = s.M;
     p.N = s.N;
     p.K = s.K;
     p.GT = GT;
-    p.tiles = n_tiles(s.N);
-    p.U = (long long)p.tiles * p.GT;
-    long long G = sm_count(dev);
-    if (G > kMaxCtas) G = kMaxCtas;
-    if (G > p.U) G = p.U;
-    p.G = (int)G;
-    p.y_vec = (s.N % 8 == 0) && aligned16(y);
+    p.R = pl.R;
+    p.nb = pl.nb;
+    p.nb0 = pl.nb0;
+    p.ntiles = pl.ntiles;
+    p.S = pl.S;
+    p.NS = pl.NS;
+    p.NSB = pl.NSB;
+    p.stage_bytes = pl.stage_bytes;
+    p.sb_bytes = pl.sb_bytes;
+    p.red_off = pl.red_off;
+    p.red_bytes = pl.red_bytes;
+    p.recv_off = pl.recv_off;
+    p.bar_off = pl.bar_off;
 
-    const long long prep_threads = (long long)kXsWidth * (s.K / 8);
-    const int prep_blocks = (int)((prep_threads + kPrepThreads - 1) / kPrepThreads);
-    if (s.bits == 4)
-        DFLASH_CUDA_TRY(launch_pdl(qmm_prep_kernel<4>, dim3(prep_blocks), dim3(kPrepThreads), 0, stream, x, xperm, xs,
-                                   s.M, s.K, s.group));
-    else
-        DFLASH_CUDA_TRY(launch_pdl(qmm_prep_kernel<8>, dim3(prep_blocks), dim3(kPrepThreads), 0, stream, x, xperm, xs,
-                                   s.M, s.K, s.group));
-    DFLASH_CUDA_TRY(launch_pdl(qmm_kernel<C>, dim3(p.G), dim3(kThreads), (size_t)C::SMEM_BYTES, stream, tm_w, tm_x,
-                               tm_s, tm_b, tm_xs, p));
-    DFLASH_CUDA_TRY(launch_pdl(qmm_fixup_kernel<C::NT>, dim3(p.tiles), dim3(256), 0, stream, p));
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = pl.cs;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    {
+        // prep: one thread per (x row, run of 8 k) of every stage
+        const long long threads = (long long)C::MR * pl.S * (C::STAGE_K / 8);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)((threads + kPrepThreads - 1) / kPrepThreads));
+        cfg.blockDim = dim3(kPrepThreads);
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        DFLASH_CUDA_TRY(cudaLaunchKernelEx(&cfg, qmm_prep_kernel<C>, reinterpret_cast<const uint16_t*>(x),
+                                           reinterpret_cast<uint8_t*>(ws), s.M, s.K, pl.S));
+    }
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(pl.nclusters * pl.cs));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = pl.smem;
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 2;
+        DFLASH_CUDA_TRY(cudaLaunchKernelEx(&cfg, qmm_kernel<C>, tm_w, tm_s, tm_b, p));
+    }
     return DFLASH_OK;
 }
 
@@ -880,14 +1126,30 @@ int dispatch_group(const Shape& s, const dflash_bf16* x, const uint32_t* w, cons
     return fail(DFLASH_ERR_UNSUPPORTED, "group_size %d not in {32, 64, 128}", s.group);
 }
 
+// The workspace holds the x packets of every stage along K: its size depends on bits,
+// group (segments per unit), M (x rows per packet) and K, not on N.
+template <int BITS, int GROUP>
+size_t packets_for(int M, int K) {
+    if (M <= 8) return (size_t)stages_along_k<Cfg<BITS, GROUP, 1, true>>(K) * Cfg<BITS, GROUP, 1, true>::PKT;
+    return (size_t)stages_along_k<Cfg<BITS, GROUP, 2, true>>(K) * Cfg<BITS, GROUP, 2, true>::PKT;
+}
+
+inline size_t workspace_size(int M, int K, int group, int bits) {
+    size_t b = 0;
+    if (bits == 4)
+        b = group == 32 ? packets_for<4, 32>(M, K) : group == 64 ? packets_for<4, 64>(M, K) : packets_for<4, 128>(M, K);
+    else
+        b = group == 32 ? packets_for<8, 32>(M, K) : group == 64 ? packets_for<8, 64>(M, K) : packets_for<8, 128>(M, K);
+    return (b + 255) / 256 * 256;
+}
+
 int validate(const Shape& s) {
     if (s.bits != 4 && s.bits != 8) return fail(DFLASH_ERR_UNSUPPORTED, "bits %d not in {4, 8}", s.bits);
     if (s.group != 32 && s.group != 64 && s.group != 128)
         return fail(DFLASH_ERR_UNSUPPORTED, "group_size %d not in {32, 64, 128}", s.group);
     if (s.M < 1 || s.M > 16) return fail(DFLASH_ERR_UNSUPPORTED, "M=%d outside 1..16", s.M);
     if (s.N < 1 || s.K < 1) return fail(DFLASH_ERR_INVALID_ARGUMENT, "N=%d K=%d must be positive", s.N, s.K);
-    if (s.N > kMaxTiles * kRows)
-        return fail(DFLASH_ERR_UNSUPPORTED, "N=%d above the supported %d", s.N, kMaxTiles * kRows);
+    if (s.N > kMaxN) return fail(DFLASH_ERR_UNSUPPORTED, "N=%d above the supported %d", s.N, kMaxN);
     if (s.K % s.group != 0)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "K=%d is not a multiple of group_size %d", s.K, s.group);
     return DFLASH_OK;
@@ -897,16 +1159,15 @@ int validate(const Shape& s) {
 }  // namespace dflash
 
 extern "C" size_t dflash_qmm_workspace_bytes(int M, int N, int K, int group_size, int bits) {
-    (void)bits;
     if (N < 1 || K < 1 || M < 1 || M > 16 || (group_size != 32 && group_size != 64 && group_size != 128) ||
-        K % group_size != 0)
+        K % group_size != 0 || (bits != 4 && bits != 8))
         return 0;
-    return dflash::qmm::workspace_size(M, K, group_size);
+    return dflash::qmm::workspace_size(M, K, group_size, bits);
 }
 
 extern "C" int dflash_qmm_supported(int N, int K, int group_size, int bits) {
     if ((bits != 4 && bits != 8) || (group_size != 32 && group_size != 64 && group_size != 128)) return 0;
-    if (N < 1 || K < 1 || K % group_size != 0 || N > dflash::qmm::kMaxTiles * dflash::qmm::kRows) return 0;
+    if (N < 1 || K < 1 || K % group_size != 0 || N > dflash::qmm::kMaxN) return 0;
     return 1;
 }
 
@@ -920,10 +1181,10 @@ extern "C" int dflash_qmm(const dflash_bf16* x, const uint32_t* w, const dflash_
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_qmm: null tensor pointer");
     if (!aligned16(x) || !aligned16(w))
         return fail(DFLASH_ERR_MISALIGNED, "dflash_qmm: x and w must be 16-byte aligned");
-    const size_t need = dflash_qmm_workspace_bytes(M, N, K, group_size, bits);
-    if (!workspace || !aligned16(workspace) || workspace_bytes < need)
-        return fail(DFLASH_ERR_WORKSPACE, "dflash_qmm: workspace of %zu bytes required (got %zu)", need,
-                    workspace_bytes);
+    const size_t need = qmm::workspace_size(M, K, group_size, bits);
+    if (!workspace || workspace_bytes < need || !aligned16(workspace))
+        return fail(DFLASH_ERR_WORKSPACE, "dflash_qmm: a 16-byte aligned workspace of %zu bytes is required (got %zu)",
+                    need, workspace_bytes);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (bits == 4) return qmm::dispatch_group<4>(s, x, w, scales, biases, y, workspace, st);
     return qmm::dispatch_group<8>(s, x, w, scales, biases, y, workspace, st);

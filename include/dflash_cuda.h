@@ -80,10 +80,12 @@ int dflash_test_bounded_wait(uint64_t limit_ns, dflash_stream_t stream);
  *   M in 1..16, bits in {4, 8}, group_size in {32, 64, 128}, K % group_size == 0.
  *
  * The dequantised weight is exact (fp32 q*s+b), products accumulate in fp32, y is
- * rounded once to bf16.  `workspace` holds split-K partial sums and per-tile
- * counters: size it with dflash_qmm_workspace_bytes, zero it once before its first
- * use (every call leaves it zeroed again), and give each concurrently running stream
- * its own.
+ * rounded once to bf16.  `workspace` (16-byte aligned, sized by
+ * dflash_qmm_workspace_bytes) receives x converted for the kernel; it needs no
+ * initialisation, and each concurrently running stream needs its own.  The call is two
+ * kernels chained by programmatic dependent launch: w, scales and biases are read
+ * before the preceding kernel in the stream has finished, so they must not be written
+ * by that kernel (x may be).
  * -------------------------------------------------------------------------------- */
 size_t dflash_qmm_workspace_bytes(int M, int N, int K, int group_size, int bits);
 
@@ -98,8 +100,8 @@ int dflash_qmm(const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scale
  * results as dflash_qmm, without `workspace`: the scratch is a library-owned 8 MiB
  * device array that every GPU loading this library keeps until the process exits.
  *   - Shapes whose dflash_qmm_workspace_bytes exceeds 8 MiB are rejected with
- *     DFLASH_ERR_UNSUPPORTED (at M = 16 that is K above about 78000; dflash_qmm
- *     with a larger workspace covers those).
+ *     DFLASH_ERR_UNSUPPORTED (at M = 16 and group 32 that is K above about 209000;
+ *     dflash_qmm with a larger workspace covers those).
  *   - The first call on a device resolves the array's device address; make that first
  *     call outside any stream capture.
  *   - Every call on a device shares the array: calls that can overlap on the GPU

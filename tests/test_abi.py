@@ -71,7 +71,7 @@ def test_qmm_noalloc_argument_errors(dc):
     assert f(FAKE + 2, FAKE, FAKE, FAKE, FAKE, 8, 4096, 1024, 64, 4, None) == 3
     assert f(FAKE, FAKE, FAKE, FAKE, FAKE, 16, 4096, 1 << 20, 64, 4, None) == 2
     assert "static" in dc.last_error() and "dflash_qmm" in dc.last_error()
-    assert dc.qmm_workspace_bytes(16, 4096, 77824, 32, 4) <= 8 << 20 < dc.qmm_workspace_bytes(16, 4096, 79872, 32, 4)
+    assert dc.qmm_workspace_bytes(16, 4096, 209664, 32, 4) <= 8 << 20 < dc.qmm_workspace_bytes(16, 4096, 209920, 32, 4)
 
 
 def test_qmm_supported_table(dc):
@@ -89,14 +89,15 @@ def test_qmm_supported_table(dc):
 
 
 def test_workspace_size_is_shape_bounded(dc):
-    """Fixed partial/counter regions plus x in fragment order and its group sums:
-    independent of N, growing with M*K, zero for shapes the kernel rejects."""
+    """The workspace holds x packets for every stage along K: independent of N, growing
+    with M (one or two n-tiles of 8 rows) and K, zero for shapes the kernel rejects."""
     a = dc.qmm_workspace_bytes(8, 17408, 5120, 64, 4)
-    assert a == dc.qmm_workspace_bytes(8, 5120, 5120, 64, 4) == dc.qmm_workspace_bytes(8, 248320, 5120, 64, 8)
-    assert dc.qmm_workspace_bytes(16, 17408, 5120, 64, 4) > a
+    assert a == dc.qmm_workspace_bytes(8, 5120, 5120, 64, 4) == dc.qmm_workspace_bytes(1, 248320, 5120, 64, 4)
+    # 20 stages of 256 k; per stage 4 units x 8 rows x 128 B of fp16 x plus 4 x 8 x 16 B of sums
+    assert a == 20 * (4 * 8 * 128 + 4 * 8 * 16)
+    assert dc.qmm_workspace_bytes(16, 17408, 5120, 64, 4) == 2 * a
     assert dc.qmm_workspace_bytes(8, 17408, 17408, 64, 4) > a
-    fixed = 160 * 2 * 16 * 256 * 4
-    assert fixed < a < fixed + (1 << 20)
+    assert dc.qmm_workspace_bytes(8, 17408, 5120, 64, 8) > a
     assert dc.qmm_workspace_bytes(8, 0, 5120, 64, 4) == 0
     assert dc.qmm_workspace_bytes(17, 17408, 5120, 64, 4) == 0
     assert dc.qmm_workspace_bytes(8, 17408, 5000, 64, 4) == 0
