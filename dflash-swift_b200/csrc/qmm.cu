@@ -68,7 +68,6 @@ constexpr int kMaxSbStages = 8;
 constexpr int kMaxCluster = 2;
 constexpr int kSmemLimit = 232448;               // opt-in shared memory per block, sm_100
 constexpr int kBarConsumers = 1;                 // named barrier: all consumer warps
-constexpr int kBarLane0 = 2;                     // named barrier: the k-lane 0 warps
 constexpr int kPrepThreads = 32;                 // one warp per prep block: fits beside a running main CTA
 constexpr int kMaxN = 1 << 24;
 constexpr uint32_t kMag1024 = 0x64006400u;       // fp16x2 (1024, 1024): + nibble in bits 0-3 (4-7: +16q)
@@ -192,8 +191,11 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(addr), "r"(rank));
     return d;
 }
-__device__ __forceinline__ void st_cluster_f32x2(uint32_t addr, float a, float b) {
-    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+// Store into another CTA's shared memory; the bytes complete on that CTA's mbarrier.
+__device__ __forceinline__ void st_async_f32x2(uint32_t addr, float a, float b, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+                 "f"(a), "f"(b), "r"(remote_bar)
+                 : "memory");
 }
 // Arrive (release, cluster scope) on an mbarrier of another CTA of the cluster.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
@@ -237,7 +239,6 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
         }
     }
 }
-__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -247,6 +248,9 @@ __device__ __forceinline__ void cluster_arrive_relaxed() {
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_sync_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
 
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
@@ -356,6 +360,7 @@ struct Params {
     int ntiles;   // ceil(N / R)
     int S;        // stages along K
     int NS, NSB;  // ring depths
+    int y_vec;    // y rows 16-byte aligned with N % 8 == 0: write y in 16-byte chunks
     uint32_t stage_bytes, sb_bytes, red_off, red_bytes, recv_off, bar_off;
 };
 
@@ -363,7 +368,7 @@ struct Params {
 struct Bars {
     uint64_t full[kMaxStages], empty[kMaxStages];
     uint64_t sbfull[kMaxSbStages], sbempty[kMaxSbStages];
-    uint64_t xfull, xdone;  // cluster exchange: the peer's rows for us have landed / it has read ours
+    uint64_t xfull, xdone;  // cluster exchange: the peer's rows for us have landed / it has read what we sent
     int abort;
 };
 
@@ -653,14 +658,30 @@ __device__ __forceinline__ void run_tile(const Params& p, Bars* bars, volatile i
     }
 }
 
-// Producer: the j-th stage of a CTA is stage s_beg + j % nstages of tile
-// cid + (j / nstages) ncl; scale/bias slots open at the CTA's first stage of a tile and
-// at every multiple of SBP.  Returns false when a bounded wait gave up.
+// Producers.  The j-th stage of a CTA is stage s_beg + j % nstages of tile
+// cid + (j / nstages) ncl.  Two threads in different warps (so on different SM
+// sub-partitions) share the work, because each TMA issue holds its thread for a while:
+// one issues the weight boxes, the other the x packets and the scale/bias boxes.  A
+// stage's full barrier takes one arrival from each.  Scale/bias slots open at the CTA's
+// first stage of a tile and at every multiple of SBP.  Both return false when a bounded
+// wait gave up.
 template <class C>
-__device__ __forceinline__ bool issue_stage(int j, bool with_packet, int& pq, Bars* bars, volatile int* abort,
-                                            const CUtensorMap& tm_w, const CUtensorMap& tm_s,
-                                            const CUtensorMap& tm_b, const Params& p, uint32_t ring, uint32_t sbring,
-                                            int cid, int ncl, int s_beg, int nstages, uint32_t wbytes) {
+__device__ __forceinline__ bool issue_weights(int j, Bars* bars, volatile int* abort, const CUtensorMap& tm_w,
+                                              const Params& p, uint32_t ring, int cid, int ncl, int s_beg, int nstages,
+                                              uint32_t wbytes) {
+    const int t = cid + (j / nstages) * ncl, s = s_beg + j % nstages;
+    const int slot = j % p.NS;
+    if (!mbar_wait_bounded(&bars->empty[slot], ((j / p.NS) & 1) ^ 1, abort, DFLASH_DEVERR_QMM_PIPELINE))
+        return false;
+    mbar_arrive_expect_tx(&bars->full[slot], wbytes);
+    tma_load_2d_u32(ring + slot * p.stage_bytes, &tm_w, &bars->full[slot], s * (kRowBytes / 4), t * p.R);
+    return true;
+}
+
+template <class C>
+__device__ __forceinline__ bool issue_aux(int j, int& pq, Bars* bars, volatile int* abort, const CUtensorMap& tm_s,
+                                          const CUtensorMap& tm_b, const Params& p, uint32_t ring, uint32_t sbring,
+                                          int cid, int ncl, int s_beg, int nstages, uint32_t wbytes) {
     const int t = cid + (j / nstages) * ncl, s = s_beg + j % nstages;
     if (C::STMA && (s == s_beg || s % C::SBP == 0)) {
         const int q = pq % p.NSB;
@@ -672,13 +693,12 @@ __device__ __forceinline__ bool issue_stage(int j, bool with_packet, int& pq, Ba
         tma_load_2d_u32(dst + p.R * 16, &tm_b, &bars->sbfull[q], (s / C::SBP) * 8, t * p.R);
         ++pq;
     }
+    if (j == 0) pdl_wait();  // the packets come from the prep kernel
     const int slot = j % p.NS;
     if (!mbar_wait_bounded(&bars->empty[slot], ((j / p.NS) & 1) ^ 1, abort, DFLASH_DEVERR_QMM_PIPELINE))
         return false;
-    const uint32_t st = ring + slot * p.stage_bytes;
-    mbar_arrive_expect_tx(&bars->full[slot], wbytes + C::PKT);
-    tma_load_2d_u32(st, &tm_w, &bars->full[slot], s * (kRowBytes / 4), t * p.R);
-    if (with_packet) bulk_copy_g2s(st + wbytes, p.packets + (size_t)s * C::PKT, C::PKT, &bars->full[slot]);
+    mbar_arrive_expect_tx(&bars->full[slot], C::PKT);
+    bulk_copy_g2s(ring + slot * p.stage_bytes + wbytes, p.packets + (size_t)s * C::PKT, C::PKT, &bars->full[slot]);
     return true;
 }
 
@@ -705,10 +725,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     pdl_launch_dependents();
 
-    int issued = 0, pq = 0;  // stages and scale/bias slots issued (producer thread)
+    constexpr int kAuxThread = kConsumerThreads + 32;  // lane 0 of the second producer warp
+    int issued = 0;  // weight boxes issued (first producer thread)
     if (tid == kConsumerThreads) {
+        prefetch_tensormap(&tm_w);
         for (int i = 0; i < p.NS; ++i) {
-            mbar_init(&bars->full[i], 1);
+            mbar_init(&bars->full[i], 2);  // weight thread + packet thread
             mbar_init(&bars->empty[i], kConsumerWarps);
         }
         for (int i = 0; i < p.NSB; ++i) {
@@ -725,31 +747,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     cluster_arrive_relaxed();
     if (tid == kConsumerThreads) {
         // The first ring's worth of weight boxes goes out before anything else: fresh
-        // slots, so these never wait.  Their x packets follow once the prep kernel is done.
+        // slots, so these never wait.
         for (; issued < first_batch; ++issued)
-            issue_stage<C>(issued, false, pq, bars, abort, tm_w, tm_s, tm_b, p, ring, sbring, cid, ncl, s_beg,
-                           nstages, wbytes);
+            issue_weights<C>(issued, bars, abort, tm_w, p, ring, cid, ncl, s_beg, nstages, wbytes);
     }
     __syncthreads();
     cluster_wait();
 
     if (warp >= kConsumerWarps) {
-        // ---------------------------------------------------------------- producer
+        // ---------------------------------------------------------------- producers
         regs_lower<kProducerRegs>();
         if (tid == kConsumerThreads && total > 0) {
-            pdl_wait();  // the packets come from the prep kernel
-            for (int j = 0; j < first_batch; ++j)
-                bulk_copy_g2s(ring + j * p.stage_bytes + wbytes, p.packets + (size_t)(s_beg + j % nstages) * C::PKT,
-                              C::PKT, &bars->full[j]);
-            while (issued < total && issue_stage<C>(issued, true, pq, bars, abort, tm_w, tm_s, tm_b, p, ring, sbring,
-                                                     cid, ncl, s_beg, nstages, wbytes))
+            while (issued < total &&
+                   issue_weights<C>(issued, bars, abort, tm_w, p, ring, cid, ncl, s_beg, nstages, wbytes))
                 ++issued;
             if (*abort) {
                 // let every copy already issued land before shared memory is released
                 const int lo = issued > p.NS ? issued - p.NS : 0;
                 for (int j = lo; j < issued; ++j) mbar_drain(&bars->full[j % p.NS], (j / p.NS) & 1);
+            }
+        } else if (tid == kAuxThread && total > 0) {
+            if constexpr (C::STMA) {
+                prefetch_tensormap(&tm_s);
+                prefetch_tensormap(&tm_b);
+            }
+            int j = 0, pq = 0;
+            while (j < total && issue_aux<C>(j, pq, bars, abort, tm_s, tm_b, p, ring, sbring, cid, ncl, s_beg, nstages,
+                                             wbytes))
+                ++j;
+            if (*abort) {
                 const int qlo = pq > p.NSB ? pq - p.NSB : 0;
-                for (int j = qlo; j < pq; ++j) mbar_drain(&bars->sbfull[j % p.NSB], (j / p.NSB) & 1);
+                for (int q = qlo; q < pq; ++q) mbar_drain(&bars->sbfull[q % p.NSB], (q / p.NSB) & 1);
             }
         }
     } else {
@@ -835,9 +863,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             named_bar_sync(kBarConsumers, kConsumerThreads);
+            const int own0 = cs > 1 ? (rank == 0 ? 0 : p.nb0) : 0;
+            const int own1 = cs > 1 ? (rank == 0 ? p.nb0 : p.nb) : p.nb;
+            const int own_rows = 16 * (own1 - own0);
+            uint16_t* stg = reinterpret_cast<uint16_t*>(bufa);  // bf16 y of the owned rows, [m][row]
             if (kl == 0) {
-                const int own0 = cs > 1 ? (rank == 0 ? 0 : p.nb0) : 0;
-                const int own1 = cs > 1 ? (rank == 0 ? p.nb0 : p.nb) : p.nb;
                 const int peer0 = rank == 0 ? p.nb0 : 0;  // first block the peer writes
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -853,10 +883,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                 }
                 if (cs > 1) {
-                    if (tt > 0)  // the peer has read what we pushed for the previous tile
+                    if (tt > 0)  // the peer has read what we sent for the previous tile
                         mbar_wait_cluster_bounded(&bars->xdone, (tt - 1) & 1, abort, DFLASH_DEVERR_QMM_REDUCE);
+                    if (tid == 0) mbar_arrive_expect_tx(&bars->xfull, (uint32_t)own_rows * MR * 4u);
                     const uint32_t peer = rank ^ 1u;
                     const uint32_t peer_recv = map_to_rank(smem_u32(recv), peer);
+                    const uint32_t peer_bar = map_to_rank(smem_u32(&bars->xfull), peer);
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         if (i >= nblk) break;
@@ -866,16 +898,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int h = 0; h < 2; ++h)
 #pragma unroll
                             for (int nt = 0; nt < C::NT; ++nt)
-                                st_cluster_f32x2(
+                                st_async_f32x2(
                                     peer_recv + (uint32_t)((16 * (b - peer0) + pr + 8 * h) * MR + 8 * nt + 2 * tq) * 4u,
-                                    acc[i][nt][2 * h], acc[i][nt][2 * h + 1]);
+                                    acc[i][nt][2 * h], acc[i][nt][2 * h + 1], peer_bar);
                     }
-                    fence_acq_rel_cluster();
-                    named_bar_sync(kBarLane0, kConsumerThreads / kKLanes);
-                    if (tid == 0) mbar_arrive_remote(map_to_rank(smem_u32(&bars->xfull), peer));
                     mbar_wait_cluster_bounded(&bars->xfull, tt & 1, abort, DFLASH_DEVERR_QMM_REDUCE);
                 }
-                // write the blocks this CTA owns: rank 0's partial first, then rank 1's
+                // the owned rows: rank 0's partial first, then rank 1's, rounded once to bf16
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     if (i >= nblk) break;
@@ -883,8 +912,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (b < own0 || b >= own1) continue;
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const int row = 16 * b + pr + 8 * h;
-                        const int n = t * p.R + row;
+                        const int rowl = 16 * (b - own0) + pr + 8 * h;
 #pragma unroll
                         for (int nt = 0; nt < C::NT; ++nt)
 #pragma unroll
@@ -892,27 +920,44 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 const int m = 8 * nt + 2 * tq + e;
                                 float v = acc[i][nt][2 * h + e];
                                 if (cs > 1) {
-                                    const float o = recv[(16 * (b - own0) + pr + 8 * h) * MR + m];
+                                    const float o = recv[rowl * MR + m];
                                     v = rank == 0 ? v + o : o + v;
                                 }
-                                if (m < p.M && n < p.N) {
-                                    const __nv_bfloat16 o = __float2bfloat16_rn(v);
-                                    p.y[(size_t)m * p.N + n] = *reinterpret_cast<const uint16_t*>(&o);
-                                }
+                                const __nv_bfloat16 o = __float2bfloat16_rn(v);
+                                stg[m * own_rows + rowl] = *reinterpret_cast<const uint16_t*>(&o);
                             }
                     }
                 }
-                if (cs > 1) {
-                    named_bar_sync(kBarLane0, kConsumerThreads / kKLanes);
-                    if (tid == 0) mbar_arrive_remote(map_to_rank(smem_u32(&bars->xdone), rank ^ 1u));
+            }
+            named_bar_sync(kBarConsumers, kConsumerThreads);
+            // the peer may refill recv once we are past reading it (only if it has another tile)
+            if (cs > 1 && tid == 0 && t + ncl < p.ntiles)
+                mbar_arrive_remote(map_to_rank(smem_u32(&bars->xdone), rank ^ 1u));
+            // y rows of the owned blocks, from the staging buffer
+            const int n0 = t * p.R + 16 * own0;
+            if (p.y_vec) {
+                const int chunks = own_rows / 8;
+                for (int e = tid; e < p.M * chunks; e += kConsumerThreads) {
+                    const int m = e / chunks, c = e - m * chunks;
+                    const int n = n0 + 8 * c;
+                    if (n < p.N)
+                        *reinterpret_cast<uint4*>(p.y + (size_t)m * p.N + n) =
+                            *reinterpret_cast<const uint4*>(stg + m * own_rows + 8 * c);
+                }
+            } else {
+                for (int e = tid; e < p.M * own_rows; e += kConsumerThreads) {
+                    const int m = e / own_rows, r = e - m * own_rows;
+                    if (n0 + r < p.N) p.y[(size_t)m * p.N + n0 + r] = stg[m * own_rows + r];
                 }
             }
         }
     }
 done:
-    // no CTA leaves while a peer may still write to or read its shared memory
+    // No CTA leaves while its peer may still touch its shared memory.  On the normal path
+    // the exchange barriers already guarantee that; this covers the error paths, where a
+    // bounded wait gave up.  Relaxed: it orders no memory, so it does not wait for y.
     __syncwarp();
-    cluster_sync_all();
+    cluster_sync_relaxed();
 }
 
 // ------------------------------------------------------------------ host side
@@ -1061,6 +1106,7 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
     p.S = pl.S;
     p.NS = pl.NS;
     p.NSB = pl.NSB;
+    p.y_vec = (s.N % 8 == 0) && aligned16(y);
     p.stage_bytes = pl.stage_bytes;
     p.sb_bytes = pl.sb_bytes;
     p.red_off = pl.red_off;
