@@ -3,3 +3,4 @@
 #include "abi.cu"
 #include "qmm.cu"
 #include "gdn.cu"
+#include "stack.cu"

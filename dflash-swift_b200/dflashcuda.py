@@ -46,6 +46,9 @@ EXPORTED = (
     "dflash_test_bounded_wait", "dflash_qmm_workspace_bytes", "dflash_qmm", "dflash_qmm_noalloc",
     "dflash_qmm_supported",
     "dflash_gdn_step", "dflash_gdn_replay", "dflash_gdn_conv_rollback",
+    # include/dflash_stack.h: glue of the tensor-parallel verify stack
+    "dflash_stack_add_rmsnorm", "dflash_stack_silu_mul", "dflash_stack_conv_silu", "dflash_stack_gdn_gates",
+    "dflash_stack_gated_norm", "dflash_stack_attn_prep", "dflash_stack_attn_decode",
 )
 
 
@@ -58,6 +61,7 @@ class DFlashError(RuntimeError):
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
 _sz = ctypes.c_size_t
+_f = ctypes.c_float
 
 
 def _load() -> ctypes.CDLL:
@@ -81,6 +85,13 @@ def _load() -> ctypes.CDLL:
                                _i, _i, _vp], _i),
         "dflash_gdn_conv_rollback": ([_vp, _vp, _vp, ctypes.POINTER(ctypes.c_int32), _i, _i, _i, _i, _i, _vp],
                                      _i),
+        "dflash_stack_add_rmsnorm": ([_vp, _vp, _vp, _vp, _i, _i, _f, _vp], _i),
+        "dflash_stack_silu_mul": ([_vp, _vp, _i, _i, _vp], _i),
+        "dflash_stack_conv_silu": ([_vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp], _i),
+        "dflash_stack_gdn_gates": ([_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp], _i),
+        "dflash_stack_gated_norm": ([_vp, _vp, _i, _vp, _vp, _i, _i, _i, _f, _vp], _i),
+        "dflash_stack_attn_prep": ([_vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _f, _vp], _i),
+        "dflash_stack_attn_decode": ([_vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp], _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -371,3 +382,61 @@ def gdn_conv_rollback(window, window_out, conv_in, keep: int, rows: Optional[Seq
     check(lib.dflash_gdn_conv_rollback(_ptr(window), _ptr(window_out), _ptr(conv_in), _rows_arg(rows), int(keep),
                                        width, L, kc1, C, _stream(stream)))
     return window_out
+
+
+# ----------------------------------------------------------------------------- verify-stack glue
+# (include/dflash_stack.h; tensors row-major with one row per token)
+
+def stack_add_rmsnorm(resid, delta, weight, out, eps: float, stream=None):
+    M, H = resid.shape
+    check(lib.dflash_stack_add_rmsnorm(_ptr(resid), _ptr(delta), _ptr(weight), _ptr(out), M, H, float(eps),
+                                       _stream(stream)))
+    return out
+
+
+def stack_silu_mul(gate_up, out, stream=None):
+    M, I = out.shape
+    check(lib.dflash_stack_silu_mul(_ptr(gate_up), _ptr(out), M, I, _stream(stream)))
+    return out
+
+
+def stack_conv_silu(x, window, weight, out, channels: int, parts: int, stream=None):
+    """x: [M, ld] (channels convolved at [0, channels)); window [kc-1, C]; out [parts, M, C/parts]."""
+    M, ld = x.shape[0], x.stride(0)
+    kc = weight.shape[1]
+    check(lib.dflash_stack_conv_silu(_ptr(x), ld, _ptr(window), _ptr(weight), _ptr(out), M, channels, kc, parts,
+                                     _stream(stream)))
+    return out
+
+
+def stack_gdn_gates(q, k, ab, a_log, dt_bias, alpha, beta, stream=None):
+    """q, k: [M, H, dk] (normalised in place); ab: [M, ld] with b then a; alpha, beta [M, H] fp32."""
+    M, H, dk = q.shape
+    check(lib.dflash_stack_gdn_gates(_ptr(q), _ptr(k), _ptr(ab), ab.stride(0), _ptr(a_log), _ptr(dt_bias),
+                                     _ptr(alpha), _ptr(beta), M, H, dk, _stream(stream)))
+
+
+def stack_gated_norm(o, z, weight, out, eps: float, stream=None):
+    """o: [M, H, dv]; z: [M, >= H*dv] rows; out: [M, H*dv]."""
+    M, H, dv = o.shape
+    check(lib.dflash_stack_gated_norm(_ptr(o), _ptr(z), z.stride(0), _ptr(weight), _ptr(out), M, H, dv, float(eps),
+                                      _stream(stream)))
+    return out
+
+
+def stack_attn_prep(qkv, q_norm, k_norm, cache_k, cache_v, hq: int, hkv: int, rot: int, pos0: int, eps: float,
+                    theta: float, stream=None):
+    """qkv rows [q | gate | k | v]; caches [hkv, max_len, d]."""
+    M = qkv.shape[0]
+    _, max_len, d = cache_k.shape
+    check(lib.dflash_stack_attn_prep(_ptr(qkv), qkv.stride(0), _ptr(q_norm), _ptr(k_norm), _ptr(cache_k),
+                                     _ptr(cache_v), M, hq, hkv, d, rot, pos0, max_len, float(eps), float(theta),
+                                     _stream(stream)))
+
+
+def stack_attn_decode(qkv, cache_k, cache_v, out, hq: int, hkv: int, pos0: int, scale: float, stream=None):
+    M = qkv.shape[0]
+    _, max_len, d = cache_k.shape
+    check(lib.dflash_stack_attn_decode(_ptr(qkv), qkv.stride(0), _ptr(cache_k), _ptr(cache_v), _ptr(out), M, hq,
+                                       hkv, d, pos0, max_len, float(scale), _stream(stream)))
+    return out

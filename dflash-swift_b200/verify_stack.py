@@ -1,0 +1,515 @@
+"""Tensor-parallel verify forward of a hybrid gated-delta / attention target.
+
+The reference verifies a drafted block with one forward of its Qwen3.5-style target
+(`target(verifyInput, cache: targetCache)`, Sources/DFlashKit/DFlashSpeculativeGenerator.swift:397,
+with gated-delta capture switched on at :389-393).  That model lives in an external MLX
+fork; its shape is fixed here as a 64-layer stack (48 gated-delta + 16 GQA attention
+layers, one attention layer per 4, `full_attention_interval`, Tests/DFlashKitTests/
+TinyHybridTarget.swift:37) whose every projection is an MLX affine-quantized matmul.
+
+Each rank (one process per GPU) owns a shard of every layer:
+  * column-sharded along N (heads / intermediate units): the gated-delta in_proj
+    [q | k | v | z | b | a], the attention qkv projection [q | gate | k | v] and the MLP
+    gate_up [gate | up];
+  * row-sharded along K (group-aligned): gated-delta out_proj, attention o_proj and the
+    MLP down projection, whose partial [M, hidden] outputs are summed by one all-reduce.
+So a layer has exactly two collectives (after the mixer and after the MLP), 128 per
+forward.  The residual stream is fp32 and replicated; everything between the shard
+boundaries is rank-local.  The projections run on dflash_qmm, the recurrence on
+dflash_gdn_step (its inputs are the rollback capture) and the glue on the dflash_stack_*
+kernels; the all-reduce is NCCL through torch.distributed.  The whole forward is
+captured once as a CUDA graph and replayed.
+
+Weights are seeded synthetic MLX-packed 4-bit tensors (no checkpoint is available):
+every rank draws the same global tensor from the same seed and keeps its shard, so a
+TP=P run computes the same function as TP=1.
+
+Run as a benchmark (one line of JSON per run):
+    python dflash-swift_b200/verify_stack.py                      # TP=1
+    python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 \\
+        dflash-swift_b200/verify_stack.py
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+from dataclasses import dataclass, asdict, replace
+from pathlib import Path
+from typing import Callable, Optional
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+
+
+@dataclass(frozen=True)
+class StackConfig:
+    layers: int = 64
+    hidden: int = 5120
+    intermediate: int = 17408
+    attn_interval: int = 4      # layer i is an attention layer when (i + 1) % attn_interval == 0
+    gdn_heads: int = 32         # gated-delta heads (q, k and v alike)
+    gdn_dk: int = 128
+    gdn_dv: int = 128
+    conv_kernel: int = 4
+    attn_heads: int = 24
+    kv_heads: int = 4
+    head_dim: int = 256
+    rotary_dim: int = 64        # partial rotary: the first 64 of 256 dims
+    rope_theta: float = 1.0e7
+    eps: float = 1.0e-6
+    group: int = 64
+    bits: int = 4
+    context: int = 1024         # tokens already in each attention cache
+    block: int = 8              # M: rows verified per forward
+
+    @property
+    def max_len(self) -> int:
+        return self.context + self.block
+
+    def is_attention(self, layer: int) -> bool:
+        return (layer + 1) % self.attn_interval == 0
+
+    def layer_kinds(self):
+        return ["attn" if self.is_attention(i) else "gdn" for i in range(self.layers)]
+
+
+# 64-layer hybrid, hidden 5120, MLP 17408, 48 GDN + 16 GQA, 4-bit g64, M=8.
+CONFIG4 = StackConfig()
+# A small stack of the same structure for parity tests (3 GDN + 1 attention layers).
+TINY = StackConfig(layers=4, hidden=256, intermediate=512, gdn_heads=4, gdn_dk=64, gdn_dv=64, attn_heads=4,
+                   kv_heads=2, head_dim=64, rotary_dim=64, rope_theta=1.0e4, context=24, block=8)
+
+
+# ----------------------------------------------------------------------------- shard plan
+
+@dataclass(frozen=True)
+class ShardPlan:
+    rank: int
+    world: int
+    gdn_heads: int          # gated-delta heads on this rank
+    gdn_head0: int
+    attn_heads: int         # q heads on this rank
+    attn_head0: int
+    kv_heads: int           # kv heads this rank computes (replicated when world > kv_heads)
+    kv_head0: int
+    inter: int              # MLP intermediate units on this rank
+    inter0: int
+
+
+def shard_plan(cfg: StackConfig, rank: int, world: int) -> ShardPlan:
+    """Which heads / units of each layer rank `rank` of `world` owns.
+
+    Gated-delta heads, q heads and intermediate units split evenly.  KV heads split
+    evenly when world divides them; with more ranks than kv heads each rank computes the
+    one kv head its q heads read (so that head is replicated on world / kv_heads ranks).
+    Row-sharded K extents (heads * dv, heads * head_dim, intermediate / world) must be
+    whole quantization groups."""
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world {world}")
+    for name, total in (("gdn_heads", cfg.gdn_heads), ("attn_heads", cfg.attn_heads),
+                        ("intermediate", cfg.intermediate)):
+        if total % world:
+            raise ValueError(f"{name}={total} does not split over {world} ranks")
+    if cfg.attn_heads % cfg.kv_heads:
+        raise ValueError("attn_heads must be a multiple of kv_heads")
+    if cfg.gdn_dk != cfg.gdn_dv:
+        raise ValueError("the gated-delta conv treats q, k and v as equal parts: gdn_dk must equal gdn_dv")
+    gh = cfg.gdn_heads // world
+    ah = cfg.attn_heads // world
+    q_per_kv = cfg.attn_heads // cfg.kv_heads
+    if cfg.kv_heads % world == 0:
+        kvh, kv0 = cfg.kv_heads // world, rank * (cfg.kv_heads // world)
+    elif q_per_kv % ah == 0:
+        kvh, kv0 = 1, (rank * ah) // q_per_kv
+    else:
+        raise ValueError(f"{world} ranks split the {q_per_kv} q heads of a kv head unevenly")
+    inter = cfg.intermediate // world
+    for name, k in (("gdn out_proj", gh * cfg.gdn_dv), ("o_proj", ah * cfg.head_dim), ("down", inter)):
+        if k % cfg.group:
+            raise ValueError(f"{name} shard K={k} is not a multiple of group {cfg.group}")
+    return ShardPlan(rank, world, gh, rank * gh, ah, rank * ah, kvh, kv0, inter, rank * inter)
+
+
+def _ranges_gdn_in(cfg: StackConfig, p: ShardPlan):
+    """Global row ranges of the in_proj [q | k | v | z | b | a] this rank keeps, in order."""
+    H, dk, dv = cfg.gdn_heads, cfg.gdn_dk, cfg.gdn_dv
+    h0, h1 = p.gdn_head0, p.gdn_head0 + p.gdn_heads
+    offs = [0, H * dk, 2 * H * dk, 2 * H * dk + H * dv, 2 * H * dk + 2 * H * dv, 2 * H * dk + 2 * H * dv + H]
+    widths = [dk, dk, dv, dv, 1, 1]
+    return [(o + h0 * w, o + h1 * w) for o, w in zip(offs, widths)]
+
+
+def _ranges_attn_qkv(cfg: StackConfig, p: ShardPlan):
+    """Global row ranges of the qkv projection [q | gate | k | v] this rank keeps."""
+    d, Hq, Hkv = cfg.head_dim, cfg.attn_heads, cfg.kv_heads
+    q0, q1 = p.attn_head0 * d, (p.attn_head0 + p.attn_heads) * d
+    k0, k1 = p.kv_head0 * d, (p.kv_head0 + p.kv_heads) * d
+    return [(q0, q1), (Hq * d + q0, Hq * d + q1), (2 * Hq * d + k0, 2 * Hq * d + k1),
+            (2 * Hq * d + Hkv * d + k0, 2 * Hq * d + Hkv * d + k1)]
+
+
+def _ranges_gate_up(cfg: StackConfig, p: ShardPlan):
+    I = cfg.intermediate
+    return [(p.inter0, p.inter0 + p.inter), (I + p.inter0, I + p.inter0 + p.inter)]
+
+
+# ----------------------------------------------------------------------------- weights
+
+@dataclass
+class Quant:
+    """MLX affine-quantized matrix: packed u32 (stored as int32) [N, K*bits/32], bf16
+    scales and biases [N, K/group]."""
+    w: torch.Tensor
+    scales: torch.Tensor
+    biases: torch.Tensor
+    group: int
+    bits: int
+
+    @property
+    def N(self) -> int:
+        return self.w.shape[0]
+
+    @property
+    def K(self) -> int:
+        return self.w.shape[1] * 32 // self.bits
+
+    def rows(self, ranges) -> "Quant":
+        idx = lambda t: torch.cat([t[a:b] for a, b in ranges]).contiguous()
+        return Quant(idx(self.w), idx(self.scales), idx(self.biases), self.group, self.bits)
+
+    def cols(self, k0: int, k1: int) -> "Quant":
+        if k0 % self.group or k1 % self.group:
+            raise ValueError("K shard must be group-aligned")
+        wpk = 32 // self.bits
+        return Quant(self.w[:, k0 // wpk:k1 // wpk].contiguous(), self.scales[:, k0 // self.group:k1 // self.group]
+                     .contiguous(), self.biases[:, k0 // self.group:k1 // self.group].contiguous(), self.group,
+                     self.bits)
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.w, self.scales, self.biases))
+
+
+def random_quant(gen: torch.Generator, N: int, K: int, group: int, bits: int, device, w_std: float = 0.02) -> Quant:
+    """Uniform random codes with per-group scales around w_std / std(code) and biases
+    centring the codes, so dequantised weights have roughly N(0, w_std) spread."""
+    words = K * bits // 32
+    w = torch.randint(-2 ** 31, 2 ** 31 - 1, (N, words), dtype=torch.int32, generator=gen, device=device)
+    levels = 2 ** bits
+    code_std = math.sqrt((levels * levels - 1) / 12.0)
+    s = (w_std / code_std) * (0.5 + torch.rand((N, K // group), generator=gen, device=device))
+    b = -(levels - 1) / 2.0 * s + 0.1 * w_std * torch.randn((N, K // group), generator=gen, device=device)
+    return Quant(w, s.to(torch.bfloat16), b.to(torch.bfloat16), group, bits)
+
+
+def _norm_weight(gen, n, device):
+    return (1.0 + 0.1 * torch.randn(n, generator=gen, device=device)).to(torch.bfloat16)
+
+
+def layer_seed(seed: int, layer: int, slot: int) -> int:
+    return (seed * 1_000_003 + layer * 101 + slot) & 0x7FFFFFFF
+
+
+def build_rank_weights(cfg: StackConfig, plan: ShardPlan, seed: int, device) -> dict:
+    """This rank's shard of every layer.  Each global tensor is drawn from its own seed
+    on `device` and sliced, so every rank (and an unsharded run) sees the same model."""
+    dev = torch.device(device)
+
+    def g(layer, slot):
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(layer_seed(seed, layer, slot))
+        return gen
+
+    H, G, B = cfg.hidden, cfg.group, cfg.bits
+    layers = []
+    for li, kind in enumerate(cfg.layer_kinds()):
+        L = {"kind": kind, "ln": _norm_weight(g(li, 0), H, dev), "post_ln": _norm_weight(g(li, 1), H, dev)}
+        if kind == "gdn":
+            Hg, dk, dv, kc = cfg.gdn_heads, cfg.gdn_dk, cfg.gdn_dv, cfg.conv_kernel
+            n_in = 2 * Hg * dk + 2 * Hg * dv + 2 * Hg
+            L["in_proj"] = random_quant(g(li, 2), n_in, H, G, B, dev).rows(_ranges_gdn_in(cfg, plan))
+            L["out_proj"] = random_quant(g(li, 3), H, Hg * dv, G, B, dev).cols(plan.gdn_head0 * dv,
+                                                                              (plan.gdn_head0 + plan.gdn_heads) * dv)
+            gg = g(li, 4)
+            conv = (0.5 * torch.randn(3 * Hg * dk, kc, generator=gg, device=dev)).to(torch.bfloat16)
+            a_log = torch.log(torch.empty(Hg, device=dev).uniform_(1.0, 16.0, generator=gg))
+            dt_bias = 0.5 * torch.randn(Hg, generator=gg, device=dev)
+            heads = slice(plan.gdn_head0, plan.gdn_head0 + plan.gdn_heads)
+            conv3 = conv.view(3, Hg, dk, kc)[:, heads].reshape(-1, kc).contiguous()
+            L.update(conv=conv3, a_log=a_log[heads].contiguous(), dt_bias=dt_bias[heads].contiguous(),
+                     gdn_norm=_norm_weight(gg, dv, dev))
+        else:
+            Hq, Hkv, d = cfg.attn_heads, cfg.kv_heads, cfg.head_dim
+            L["qkv"] = random_quant(g(li, 2), 2 * Hq * d + 2 * Hkv * d, H, G, B, dev).rows(_ranges_attn_qkv(cfg, plan))
+            L["o_proj"] = random_quant(g(li, 3), H, Hq * d, G, B, dev).cols(plan.attn_head0 * d,
+                                                                            (plan.attn_head0 + plan.attn_heads) * d)
+            gg = g(li, 4)
+            L.update(q_norm=_norm_weight(gg, d, dev), k_norm=_norm_weight(gg, d, dev))
+        I = cfg.intermediate
+        L["gate_up"] = random_quant(g(li, 5), 2 * I, H, G, B, dev).rows(_ranges_gate_up(cfg, plan))
+        L["down"] = random_quant(g(li, 6), H, I, G, B, dev).cols(plan.inter0, plan.inter0 + plan.inter)
+        layers.append(L)
+    final_norm = _norm_weight(g(cfg.layers, 0), H, dev)
+    return {"layers": layers, "final_norm": final_norm}
+
+
+def build_rank_state(cfg: StackConfig, plan: ShardPlan, seed: int, device) -> dict:
+    """Pre-round state of this rank's shard: gated-delta snapshots (fp32 [h, dv, dk]) and
+    conv windows (bf16 [kc-1, 3 h dk]); attention caches (bf16 [hkv, max_len, d]) holding
+    `context` random tokens."""
+    dev = torch.device(device)
+    out = []
+    for li, kind in enumerate(cfg.layer_kinds()):
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(layer_seed(seed + 7, li, 9))
+        if kind == "gdn":
+            Hg, dk, dv, kc = cfg.gdn_heads, cfg.gdn_dk, cfg.gdn_dv, cfg.conv_kernel
+            heads = slice(plan.gdn_head0, plan.gdn_head0 + plan.gdn_heads)
+            snap = 0.1 * torch.randn(Hg, dv, dk, generator=gen, device=dev)
+            win = torch.randn(kc - 1, 3, Hg, dk, generator=gen, device=dev).to(torch.bfloat16)
+            out.append({"snapshot": snap[heads].contiguous(),
+                        "window": win[:, :, heads].reshape(kc - 1, -1).contiguous()})
+        else:
+            Hkv, d = cfg.kv_heads, cfg.head_dim
+            kv = slice(plan.kv_head0, plan.kv_head0 + plan.kv_heads)
+            ck = torch.zeros(Hkv, cfg.max_len, d, dtype=torch.bfloat16, device=dev)
+            cv = torch.zeros_like(ck)
+            ck[:, :cfg.context] = torch.randn(Hkv, cfg.context, d, generator=gen, device=dev).to(torch.bfloat16)
+            cv[:, :cfg.context] = torch.randn(Hkv, cfg.context, d, generator=gen, device=dev).to(torch.bfloat16)
+            out.append({"cache_k": ck[kv].contiguous(), "cache_v": cv[kv].contiguous()})
+    return {"layers": out}
+
+
+def make_block(cfg: StackConfig, seed: int, device) -> torch.Tensor:
+    """The verify block's input hidden states, bf16 [M, hidden] ~ N(0, 1)."""
+    gen = torch.Generator(device=torch.device(device))
+    gen.manual_seed(layer_seed(seed + 3, 0, 0))
+    return torch.randn(cfg.block, cfg.hidden, generator=gen, device=device).to(torch.bfloat16)
+
+
+def weight_bytes(weights: dict) -> int:
+    n = 0
+    for L in weights["layers"]:
+        for v in L.values():
+            if isinstance(v, Quant):
+                n += v.nbytes()
+    return n
+
+
+# ----------------------------------------------------------------------------- the CUDA stack
+
+class VerifyStack:
+    """One rank's shard of the hybrid target, run on libdflashcuda.
+
+    forward(hidden) runs the verify forward of one block of `cfg.block` rows from the
+    pre-round state (gated-delta snapshots and conv windows are only read; the new
+    states go to `state_out`, the attention caches receive the block's k and v at
+    positions context .. context + M - 1), and returns the final-norm hidden states
+    bf16 [M, hidden] (identical on every rank)."""
+
+    def __init__(self, cfg: StackConfig, rank: int = 0, world: int = 1, seed: int = 0, device=None,
+                 group=None, weights: Optional[dict] = None, state: Optional[dict] = None):
+        import dflashcuda as dc
+        self.dc = dc
+        self.cfg = cfg
+        self.plan = shard_plan(cfg, rank, world)
+        self.world = world
+        self.pg = group
+        self.device = torch.device(device if device is not None else f"cuda:{torch.cuda.current_device()}")
+        if self.device.type != "cuda":
+            raise RuntimeError("VerifyStack runs on libdflashcuda only (no CPU path)")
+        self.w = weights if weights is not None else build_rank_weights(cfg, self.plan, seed, self.device)
+        self.state = state if state is not None else build_rank_state(cfg, self.plan, seed, self.device)
+        self._alloc()
+        self.graph = None
+
+    def _alloc(self):
+        cfg, p, dev = self.cfg, self.plan, self.device
+        M, H = cfg.block, cfg.hidden
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.resid = torch.zeros(M, H, **f32)
+        self.normed = torch.empty(M, H, **bf)
+        self.delta = torch.zeros(M, H, **bf)
+        self.out = torch.empty(M, H, **bf)
+        h, dk, dv = p.gdn_heads, cfg.gdn_dk, cfg.gdn_dv
+        self.gdn_proj = torch.empty(M, 2 * h * dk + 2 * h * dv + 2 * h, **bf)
+        # the conv output q | k | v is kept per layer: with alpha and beta it is the capture
+        n_gdn = sum(1 for k in cfg.layer_kinds() if k == "gdn")
+        self.capture_qkv = torch.empty(n_gdn, 3, M, h, dk, **bf)
+        self.capture_alpha = torch.empty(n_gdn, M, h, **f32)
+        self.capture_beta = torch.empty(n_gdn, M, h, **f32)
+        self.state_out = torch.empty(n_gdn, h, dv, dk, **f32)
+        self.gdn_o = torch.empty(M, h, dv, **bf)
+        self.gdn_normed = torch.empty(M, h * dv, **bf)
+        d = cfg.head_dim
+        self.qkv = torch.empty(M, (2 * p.attn_heads + 2 * p.kv_heads) * d, **bf)
+        self.attn_out = torch.empty(M, p.attn_heads * d, **bf)
+        self.gate_up = torch.empty(M, 2 * p.inter, **bf)
+        self.act = torch.empty(M, p.inter, **bf)
+        need = 0
+        for L in self.w["layers"]:
+            for v in L.values():
+                if isinstance(v, Quant):
+                    need = max(need, self.dc.qmm_workspace_bytes(M, v.N, v.K, v.group, v.bits))
+        self.ws = self.dc.Workspace(need, dev)
+
+    # -- pieces
+    def _qmm(self, x, q: Quant, out):
+        self.dc.qmm(x, q.w, q.scales, q.biases, q.group, q.bits, out=out, workspace=self.ws)
+
+    def _all_reduce(self, t):
+        if self.world > 1:
+            torch.distributed.all_reduce(t, group=self.pg)
+
+    def _gdn(self, L, S, gi):
+        cfg, p, dc = self.cfg, self.plan, self.dc
+        M, h, dk, dv = cfg.block, p.gdn_heads, cfg.gdn_dk, cfg.gdn_dv
+        self._qmm(self.normed, L["in_proj"], self.gdn_proj)
+        qkv = self.capture_qkv[gi]
+        dc.stack_conv_silu(self.gdn_proj, S["window"], L["conv"], qkv, channels=3 * h * dk, parts=3)
+        q, k, v = qkv[0], qkv[1], qkv[2]
+        ab = self.gdn_proj[:, 2 * h * dk + 2 * h * dv:]
+        alpha, beta = self.capture_alpha[gi], self.capture_beta[gi]
+        dc.stack_gdn_gates(q, k, ab, L["a_log"], L["dt_bias"], alpha, beta)
+        dc.gdn_step(S["snapshot"], self.state_out[gi], q, k, v, alpha, beta, out=self.gdn_o,
+                    q_scale=1.0 / math.sqrt(dk))
+        z = self.gdn_proj[:, 2 * h * dk + h * dv:]
+        dc.stack_gated_norm(self.gdn_o, z, L["gdn_norm"], self.gdn_normed, cfg.eps)
+        self._qmm(self.gdn_normed, L["out_proj"], self.delta)
+
+    def _attn(self, L, S):
+        cfg, p, dc = self.cfg, self.plan, self.dc
+        self._qmm(self.normed, L["qkv"], self.qkv)
+        dc.stack_attn_prep(self.qkv, L["q_norm"], L["k_norm"], S["cache_k"], S["cache_v"], p.attn_heads, p.kv_heads,
+                           cfg.rotary_dim, cfg.context, cfg.eps, cfg.rope_theta)
+        dc.stack_attn_decode(self.qkv, S["cache_k"], S["cache_v"], self.attn_out, p.attn_heads, p.kv_heads,
+                             cfg.context, 1.0 / math.sqrt(cfg.head_dim))
+        self._qmm(self.attn_out, L["o_proj"], self.delta)
+
+    def _mlp(self, L):
+        self._qmm(self.normed, L["gate_up"], self.gate_up)
+        self.dc.stack_silu_mul(self.gate_up, self.act)
+        self._qmm(self.act, L["down"], self.delta)
+
+    def _forward_body(self, hidden):
+        cfg, dc = self.cfg, self.dc
+        self.resid.zero_()
+        delta = hidden
+        gi = 0
+        for L, S in zip(self.w["layers"], self.state["layers"]):
+            dc.stack_add_rmsnorm(self.resid, delta, L["ln"], self.normed, cfg.eps)
+            if L["kind"] == "gdn":
+                self._gdn(L, S, gi)
+                gi += 1
+            else:
+                self._attn(L, S)
+            self._all_reduce(self.delta)
+            dc.stack_add_rmsnorm(self.resid, self.delta, L["post_ln"], self.normed, cfg.eps)
+            self._mlp(L)
+            self._all_reduce(self.delta)
+            delta = self.delta
+        dc.stack_add_rmsnorm(self.resid, delta, self.w["final_norm"], self.out, cfg.eps)
+        return self.out
+
+    def forward(self, hidden):
+        return self._forward_body(hidden)
+
+    def capture(self, hidden_buf):
+        """Capture forward(hidden_buf) as a CUDA graph (run it eagerly once first)."""
+        self._forward_body(hidden_buf)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._forward_body(hidden_buf)
+        self.graph = g
+        return g
+
+    def kernels_per_forward(self) -> int:
+        """Library kernel launches per forward (dflash_qmm is two launches)."""
+        n = 1  # final norm
+        for k in self.cfg.layer_kinds():
+            n += 2  # two add_rmsnorm
+            if k == "gdn":
+                n += 2 + 1 + 1 + 1 + 1 + 2  # in_proj, conv, gates, gdn_step, gated_norm, out_proj
+            else:
+                n += 2 + 1 + 1 + 2  # qkv, prep, decode, o_proj
+            n += 2 + 1 + 2  # gate_up, silu_mul, down
+        return n
+
+
+# ----------------------------------------------------------------------------- benchmark
+
+def _dist_env():
+    return int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), \
+        int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--tiny", action="store_true", help="the small parity-test stack instead of config 4")
+    ap.add_argument("--layers", type=int, default=None)
+    ap.add_argument("--context", type=int, default=None)
+    args = ap.parse_args(argv)
+
+    sys.path.insert(0, str(HERE))
+    world, rank, local = _dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    pg = None
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+        pg = torch.distributed.group.WORLD
+    cfg = TINY if args.tiny else CONFIG4
+    if args.layers is not None:
+        cfg = replace(cfg, layers=args.layers)
+    if args.context is not None:
+        cfg = replace(cfg, context=args.context)
+
+    stack = VerifyStack(cfg, rank, world, seed=args.seed, device=dev, group=pg)
+    hidden = make_block(cfg, args.seed, dev)
+    g = stack.capture(hidden)
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        g.replay()
+    stop.record()
+    torch.cuda.synchronize(dev)
+    ms = start.elapsed_time(stop) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    wbytes = weight_bytes(stack.w)
+    checksum = float(stack.out.float().abs().sum().item())
+    if rank == 0:
+        print(json.dumps({
+            "metric": "verify forward µs (M-row block through the full stack)",
+            "value": round(ms * 1000.0, 2), "unit": "us", "tokens_per_s": round(cfg.block / (ms / 1000.0), 1),
+            "tp": world, "steps": args.steps, "warmup": args.warmup,
+            "weight_bytes_per_gpu": wbytes, "weight_gbs_per_gpu": round(wbytes / (ms / 1000.0) / 1e9, 1),
+            "kernels_per_forward": stack.kernels_per_forward(), "all_reduces_per_forward": 2 * cfg.layers,
+            "config": {k: v for k, v in asdict(cfg).items()}, "out_abs_sum": checksum,
+        }), flush=True)
+    del g
+    stack.graph = None
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,66 @@
+/*
+ * libdflashcuda — glue kernels of the tensor-parallel verify stack (a hybrid
+ * gated-delta / attention target around the quantized projections of dflash_cuda.h).
+ * These have no single counterpart in the reference: there the same steps are MLX ops
+ * inside the target model's layers (the verify forward of
+ * Sources/DFlashKit/DFlashSpeculativeGenerator.swift:389-398).  Conventions as in
+ * dflash_cuda.h: device pointers, row-major with one row per token, stream-ordered,
+ * status return.
+ */
+#ifndef DFLASH_STACK_H
+#define DFLASH_STACK_H
+
+#include "dflash_cuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* resid (fp32 [M, H]) += delta (bf16 [M, H], NULL for none); out (bf16 [M, H]) =
+ * resid * rsqrt(mean(resid^2) + eps) * weight (bf16 [H]). */
+int dflash_stack_add_rmsnorm(float* resid, const dflash_bf16* delta, const dflash_bf16* weight, dflash_bf16* out,
+                             int M, int H, float eps, dflash_stream_t stream);
+
+/* gate_up bf16 [M, 2I] = [gate | up]; y bf16 [M, I] = silu(gate) * up. */
+int dflash_stack_silu_mul(const dflash_bf16* gate_up, dflash_bf16* y, int M, int I, dflash_stream_t stream);
+
+/* Causal depthwise convolution (width kc <= 8) over the M tokens of x (bf16, row stride ld,
+ * channels [0, C)) continuing the pre-round `window` (bf16 [kc-1, C], read only), then
+ * SiLU.  weight bf16 [C, kc] (last tap on the current token).  y receives `parts`
+ * contiguous blocks [M, C / parts]. */
+int dflash_stack_conv_silu(const dflash_bf16* x, int ld, const dflash_bf16* window, const dflash_bf16* weight,
+                           dflash_bf16* y, int M, int C, int kc, int parts, dflash_stream_t stream);
+
+/* Gated-delta gates: L2-normalise q and k (bf16 [M, heads * dk], in place); from ab (bf16,
+ * row stride ld_ab, b at [0, heads), a at [heads, 2 heads)) write fp32 [M, heads]
+ * alpha = exp(-exp(a_log) * softplus(a + dt_bias)) and beta = sigmoid(b). */
+int dflash_stack_gdn_gates(dflash_bf16* q, dflash_bf16* k, const dflash_bf16* ab, int ld_ab, const float* a_log,
+                           const float* dt_bias, float* alpha, float* beta, int M, int heads, int dk,
+                           dflash_stream_t stream);
+
+/* out bf16 [M, heads * dv] = rmsnorm(o per head) * weight (bf16 [dv]) * silu(z); z has row
+ * stride ld_z. */
+int dflash_stack_gated_norm(const dflash_bf16* o, const dflash_bf16* z, int ld_z, const dflash_bf16* weight,
+                            dflash_bf16* out, int M, int heads, int dv, float eps, dflash_stream_t stream);
+
+/* Attention prep.  qkv row t (stride ld) = [q (hq*d) | gate (hq*d) | k (hkv*d) | v (hkv*d)].
+ * q heads: RMSNorm (q_norm, bf16 [d]) then rotary embedding on the first rot dims, in
+ * place.  k heads: RMSNorm (k_norm) + rotary into cache_k[j, pos0 + t]; v into
+ * cache_v[j, pos0 + t].  Caches bf16 [hkv, max_len, d].  Rotary is rotate-half with
+ * frequency theta^(-2i/rot).  d in {64, 128, 256}; rot a multiple of 64, <= d. */
+int dflash_stack_attn_prep(dflash_bf16* qkv, int ld, const dflash_bf16* q_norm, const dflash_bf16* k_norm,
+                           dflash_bf16* cache_k, dflash_bf16* cache_v, int M, int hq, int hkv, int d, int rot,
+                           int pos0, int max_len, float eps, float theta, dflash_stream_t stream);
+
+/* Decode attention of the block: token t attends to cache rows 0 .. pos0 + t of kv head
+ * h / (hq / hkv).  out bf16 [M, hq * d] = softmax(q k^T * scale) v * sigmoid(gate), with q
+ * and gate read from qkv as laid out above. */
+int dflash_stack_attn_decode(const dflash_bf16* qkv, int ld, const dflash_bf16* cache_k, const dflash_bf16* cache_v,
+                             dflash_bf16* out, int M, int hq, int hkv, int d, int pos0, int max_len, float scale,
+                             dflash_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DFLASH_STACK_H */

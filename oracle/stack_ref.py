@@ -1,0 +1,191 @@
+"""CPU reference of the tensor-parallel verify stack (TEST INFRASTRUCTURE ONLY).
+
+Only tests/ import this module, as the checker of dflash-swift_b200/verify_stack.py.
+It runs one rank's shard of the hybrid gated-delta / attention stack on the CPU in
+fp32 (fp64 for the projections), rounding to bf16 exactly where the CUDA path stores
+bf16, so the two agree up to accumulation order.  The projections go through the
+pinned qmm oracle (``oracle.qmm_f64``, MLX affine dequantisation w = s*q + b,
+Sources/DFlashKit/SmallMQuantizedMatmul.swift:59) and the recurrence through the pinned
+gated-delta oracle (``oracle.gdn_recurrence``: S <- aS; u = v - Sk; S <- S + b u k^T;
+o = S q, the update the reference replays in rollbackGatedDeltaRound,
+DFlashSpeculativeGenerator.swift:455-460).  The layer glue (RMSNorm, the causal conv,
+q/k L2 normalisation and gates, gated output norm, rotary attention with an output
+gate, SiLU MLP) restates the Qwen3.5-style target that the reference's verify forward
+calls (DFlashSpeculativeGenerator.swift:397); that model is in an external MLX fork not
+present in the reference tree, so this part of the stack is parity unpinned beyond
+its self-consistency (TP=P equals TP=1).
+
+Weights and state come in the layout of verify_stack.build_rank_weights /
+build_rank_state (torch tensors, any device; copied to the CPU here).
+"""
+from __future__ import annotations
+
+import math
+from typing import Callable, Optional
+
+import numpy as np
+import torch
+
+import oracle as O
+
+
+def rb(t: torch.Tensor) -> torch.Tensor:
+    """Round fp32 to bf16 and back (a bf16 store)."""
+    return t.to(torch.bfloat16).to(torch.float32)
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().to("cpu").contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def qmm(x: torch.Tensor, q) -> torch.Tensor:
+    """rb(x . deq(W)^T) through the fp64 qmm oracle.  x: fp32 holding bf16 values [M, K]."""
+    y = O.qmm_f64(_bits(x.to(torch.bfloat16)), q.w.detach().cpu().contiguous().numpy().view(np.uint32),
+                  _bits(q.scales), _bits(q.biases), q.group, q.bits)
+    return rb(torch.from_numpy(y).to(torch.float32))
+
+
+def add_rmsnorm(resid: torch.Tensor, delta: Optional[torch.Tensor], w: torch.Tensor, eps: float) -> torch.Tensor:
+    if delta is not None:
+        resid += delta
+    rs = torch.rsqrt(resid.pow(2).mean(dim=1, keepdim=True) + eps)
+    return rb(resid * rs * w.float())
+
+
+def silu(t: torch.Tensor) -> torch.Tensor:
+    return t / (1.0 + torch.exp(-t))
+
+
+def conv_silu(x: torch.Tensor, window: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """x [M, C]; window [kc-1, C] (older first); w [C, kc], last tap on the current row."""
+    M = x.shape[0]
+    kc = w.shape[1]
+    hist = torch.cat([window.float(), x], dim=0)  # [kc-1+M, C]
+    out = torch.zeros_like(x)
+    for t in range(M):
+        seg = hist[t:t + kc]  # rows t .. t+kc-1; the last one is x[t]
+        out[t] = (seg * w.float().t()).sum(dim=0)
+    return rb(silu(out))
+
+
+def l2norm_heads(v: torch.Tensor) -> torch.Tensor:
+    """v [M, h, d] -> rb(v / sqrt(sum v^2 + 1e-6)) per head."""
+    return rb(v * torch.rsqrt(v.pow(2).sum(dim=-1, keepdim=True) + 1e-6))
+
+
+def gdn_gates(ab: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor, h: int):
+    b, a = ab[:, :h], ab[:, h:2 * h]
+    x = a + dt_bias.float()
+    sp = torch.where(x > 20.0, x, torch.log1p(torch.exp(x)))
+    alpha = torch.exp(-torch.exp(a_log.float()) * sp)
+    beta = 1.0 / (1.0 + torch.exp(-b))
+    return alpha, beta
+
+
+def gdn_step(snapshot: torch.Tensor, q, k, v, alpha, beta, q_scale: float):
+    """Through the C oracle: returns (state fp32 [h, dv, dk], o rb [M, h, dv])."""
+    M = q.shape[0]
+    s, o = O.gdn_recurrence(snapshot.detach().cpu().float().numpy(), _bits(k.to(torch.bfloat16)),
+                            _bits(v.to(torch.bfloat16)), alpha.numpy(), beta.numpy(), M,
+                            q_bits=_bits(q.to(torch.bfloat16)), q_scale=q_scale)
+    return torch.from_numpy(s).to(torch.float32), rb(torch.from_numpy(o).to(torch.float32))
+
+
+def gated_norm(o: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """o [M, h, dv]; z [M, h*dv]."""
+    M, h, dv = o.shape
+    rs = torch.rsqrt(o.pow(2).mean(dim=-1, keepdim=True) + eps)
+    return rb((o * rs * w.float()).reshape(M, h * dv) * silu(z))
+
+
+def rope(v: torch.Tensor, rot: int, theta: float, pos: torch.Tensor) -> torch.Tensor:
+    """Rotate-half over the first rot dims of v [M, h, d]; frequency theta^(-2i/rot)."""
+    half = rot // 2
+    i = torch.arange(half, dtype=torch.float32)
+    inv = torch.exp2(-(2.0 * i / rot) * math.log2(theta))
+    ang = pos.float()[:, None] * inv[None, :]  # [M, half]
+    cs, sn = torch.cos(ang)[:, None, :], torch.sin(ang)[:, None, :]
+    out = v.clone()
+    a, b = v[..., :half], v[..., half:rot]
+    out[..., :half] = a * cs - b * sn
+    out[..., half:rot] = b * cs + a * sn
+    return out
+
+
+def head_rmsnorm(v: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    return rb(v * torch.rsqrt(v.pow(2).mean(dim=-1, keepdim=True) + eps) * w.float())
+
+
+def attention(q, gate, cache_k, cache_v, pos0: int, scale: float):
+    """q, gate [M, hq, d]; caches [hkv, L, d] (fp32 holding bf16).  Token t sees keys
+    0 .. pos0 + t.  Returns rb(softmax(q K^T scale) V * sigmoid(gate)) [M, hq*d]."""
+    M, hq, d = q.shape
+    hkv = cache_k.shape[0]
+    out = torch.zeros(M, hq, d)
+    for h in range(hq):
+        kv = h // (hq // hkv)
+        for t in range(M):
+            n = pos0 + t + 1
+            s = (cache_k[kv, :n].double() @ q[t, h].double()) * scale
+            p = torch.softmax(s, dim=0)
+            out[t, h] = (p @ cache_v[kv, :n].double()).float()
+    return rb(out * torch.sigmoid(gate)).reshape(M, hq * d)
+
+
+def forward(cfg, plan, weights: dict, state: dict, hidden: torch.Tensor,
+            all_reduce: Optional[Callable[[torch.Tensor], None]] = None) -> dict:
+    """One rank's verify forward.  Returns the final hidden states and, per layer, the
+    capture and state the CUDA stack produces (gated-delta conv output, alpha, beta,
+    state after the block; attention cache rows written)."""
+    all_reduce = all_reduce or (lambda t: None)
+    M, H = cfg.block, cfg.hidden
+    eps = cfg.eps
+    resid = torch.zeros(M, H)
+    delta = hidden.detach().cpu().float()
+    cap = {"qkv": [], "alpha": [], "beta": [], "state": [], "cache_k": [], "cache_v": []}
+    h, dk, dv = plan.gdn_heads, cfg.gdn_dk, cfg.gdn_dv
+    d, hq, hkv = cfg.head_dim, plan.attn_heads, plan.kv_heads
+    cpu = lambda t: t.detach().cpu()
+    for L, S in zip(weights["layers"], state["layers"]):
+        L = {k: (cpu(v) if isinstance(v, torch.Tensor) else v) for k, v in L.items()}
+        normed = add_rmsnorm(resid, delta, L["ln"], eps)
+        if L["kind"] == "gdn":
+            proj = qmm(normed, L["in_proj"])
+            conv = conv_silu(proj[:, :3 * h * dk], cpu(S["window"]), L["conv"])
+            q, k, v = (conv[:, i * h * dk:(i + 1) * h * dk].reshape(M, h, dk) for i in range(3))
+            q, k = l2norm_heads(q), l2norm_heads(k)
+            ab = proj[:, 2 * h * dk + 2 * h * dv:]
+            alpha, beta = gdn_gates(ab, L["a_log"], L["dt_bias"], h)
+            st, o = gdn_step(cpu(S["snapshot"]), q, k, v, alpha, beta, 1.0 / math.sqrt(dk))
+            cap["qkv"].append(torch.stack([q, k, v]))
+            cap["alpha"].append(alpha)
+            cap["beta"].append(beta)
+            cap["state"].append(st)
+            z = proj[:, 2 * h * dk + h * dv:2 * h * dk + 2 * h * dv]
+            part = qmm(gated_norm(o, z, L["gdn_norm"], eps), L["out_proj"])
+        else:
+            qkv = qmm(normed, L["qkv"])
+            q = qkv[:, :hq * d].reshape(M, hq, d)
+            gate = qkv[:, hq * d:2 * hq * d].reshape(M, hq, d)
+            kn = qkv[:, 2 * hq * d:2 * hq * d + hkv * d].reshape(M, hkv, d)
+            vn = qkv[:, 2 * hq * d + hkv * d:].reshape(M, hkv, d)
+            pos = torch.arange(cfg.context, cfg.context + M)
+            q = rb(rope(head_rmsnorm(q, L["q_norm"], eps), cfg.rotary_dim, cfg.rope_theta, pos))
+            kn = rb(rope(head_rmsnorm(kn, L["k_norm"], eps), cfg.rotary_dim, cfg.rope_theta, pos))
+            ck, cv = cpu(S["cache_k"]).float().clone(), cpu(S["cache_v"]).float().clone()
+            ck[:, cfg.context:cfg.context + M] = kn.transpose(0, 1)
+            cv[:, cfg.context:cfg.context + M] = vn.transpose(0, 1)
+            cap["cache_k"].append(ck)
+            cap["cache_v"].append(cv)
+            part = qmm(attention(q, gate, ck, cv, cfg.context, 1.0 / math.sqrt(d)), L["o_proj"])
+        all_reduce(part)
+        delta = rb(part)
+        normed = add_rmsnorm(resid, delta, L["post_ln"], eps)
+        gu = qmm(normed, L["gate_up"])
+        I = plan.inter
+        act = rb(silu(gu[:, :I]) * gu[:, I:])
+        part = qmm(act, L["down"])
+        all_reduce(part)
+        delta = rb(part)
+    out = add_rmsnorm(resid, delta, cpu(weights["final_norm"]), eps)
+    return {"out": out, "resid": resid, **cap}

@@ -12,13 +12,14 @@ import pytest
 
 ROOT = Path(__file__).resolve().parent.parent
 HEADER = ROOT / "include" / "dflash_cuda.h"
+HEADERS = sorted((ROOT / "include").glob("*.h"))
 LIB = ROOT / "dflash-swift_b200" / "libdflashcuda.so"
 
 FAKE = 0x10000  # a 16-byte aligned non-null pointer value; never dereferenced by these calls
 
 
 def declared_functions():
-    text = HEADER.read_text()
+    text = "\n".join(h.read_text() for h in HEADERS)
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     return sorted(set(re.findall(r"\b(dflash_[a-z0-9_]+)\s*\(", text)))
 
@@ -160,3 +161,28 @@ def test_last_error_is_thread_local(dc):
     assert seen["before"] == ""
     assert "bits" in seen["after"]
     assert dc.last_error() == main_msg
+
+
+def test_stack_argument_errors(dc):
+    L = dc.lib
+    # conv width outside 1..8, channels not divisible into the parts, null pointers
+    assert L.dflash_stack_conv_silu(FAKE, 96, FAKE, FAKE, FAKE, 8, 96, 9, 3, None) == 2
+    assert L.dflash_stack_conv_silu(FAKE, 96, FAKE, FAKE, FAKE, 8, 96, 4, 5, None) == 1
+    assert L.dflash_stack_conv_silu(None, 96, FAKE, FAKE, FAKE, 8, 96, 4, 3, None) == 1
+    # attention: unsupported head dim, rotary dims, cache overflow, ragged GQA grouping
+    args = dict(ld=4096, M=8, hq=4, hkv=2, d=256, rot=64, pos0=0, max_len=64)
+    def prep(**kw):
+        a = {**args, **kw}
+        return L.dflash_stack_attn_prep(FAKE, a["ld"], FAKE, FAKE, FAKE, FAKE, a["M"], a["hq"], a["hkv"], a["d"],
+                                        a["rot"], a["pos0"], a["max_len"], 1e-6, 1e4, None)
+    def dec(**kw):
+        a = {**args, **kw}
+        return L.dflash_stack_attn_decode(FAKE, a["ld"], FAKE, FAKE, FAKE, a["M"], a["hq"], a["hkv"], a["d"],
+                                          a["pos0"], a["max_len"], 0.1, None)
+    assert prep(d=96) == 2 and prep(rot=32) == 2 and prep(rot=320) == 2
+    assert prep(pos0=60) == 1 and prep(ld=100) == 1
+    assert dec(hq=3) == 1 and dec(pos0=57) == 1 and dec(d=32) == 2
+    assert L.dflash_stack_add_rmsnorm(FAKE, None, FAKE, FAKE, 0, 64, 1e-6, None) == 1
+    assert L.dflash_stack_silu_mul(FAKE, None, 8, 64, None) == 1
+    assert L.dflash_stack_gdn_gates(FAKE, FAKE, FAKE, 8, FAKE, FAKE, None, FAKE, 8, 4, 128, None) == 1
+    assert L.dflash_stack_gated_norm(FAKE, FAKE, 8, FAKE, FAKE, 8, 0, 128, 1e-6, None) == 1

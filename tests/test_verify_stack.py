@@ -1,0 +1,254 @@
+"""Tensor-parallel verify stack: shard planning (CPU), TP=2 over gloo against TP=1 on the
+CPU reference, and the CUDA stack against that reference on the GPU.
+
+Tolerances: closeness = max|y - ref| / max(max|ref|, 1) (the reference's qmm test
+measure).  The CUDA stack against the CPU reference of the same shard: <= 2e-2 on the
+final hidden states after 4 layers (bf16 stores at every kernel boundary; the two sides
+differ only in accumulation order, amplified through the RMSNorms).  TP=2 against TP=1:
+<= 3e-2 (the partial sums are rounded to bf16 before the all-reduce).
+"""
+from __future__ import annotations
+
+import math
+import multiprocessing as mp
+import socket
+import sys
+from dataclasses import asdict
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(Path(__file__).resolve().parent))
+
+import verify_stack as vs  # noqa: E402
+
+
+def closeness(y, ref) -> float:
+    y = np.asarray(y, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    return float(np.max(np.abs(y - ref)) / max(float(np.max(np.abs(ref))), 1.0))
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+# ----------------------------------------------------------------------------- planning (CPU)
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_config4_shard_plan(world):
+    cfg = vs.CONFIG4
+    plans = [vs.shard_plan(cfg, r, world) for r in range(world)]
+    assert sum(p.gdn_heads for p in plans) == cfg.gdn_heads
+    assert sum(p.attn_heads for p in plans) == cfg.attn_heads
+    assert sum(p.inter for p in plans) == cfg.intermediate
+    q_per_kv = cfg.attn_heads // cfg.kv_heads
+    for p in plans:
+        # every q head of the rank reads a kv head the rank holds
+        for h in range(p.attn_head0, p.attn_head0 + p.attn_heads):
+            assert p.kv_head0 <= h // q_per_kv < p.kv_head0 + p.kv_heads
+        assert (p.inter % cfg.group, (p.gdn_heads * cfg.gdn_dv) % cfg.group,
+                (p.attn_heads * cfg.head_dim) % cfg.group) == (0, 0, 0)
+    if world == 8:  # 4 kv heads over 8 ranks: each kv head on two ranks
+        assert [p.kv_head0 for p in plans] == [0, 0, 1, 1, 2, 2, 3, 3]
+        assert all(p.kv_heads == 1 for p in plans)
+
+
+def test_shard_plan_rejects_uneven_splits():
+    with pytest.raises(ValueError):
+        vs.shard_plan(vs.CONFIG4, 0, 3)
+    with pytest.raises(ValueError):
+        vs.shard_plan(vs.StackConfig(intermediate=17408 + 64 * 7), 0, 8)
+    with pytest.raises(ValueError):
+        vs.shard_plan(vs.CONFIG4, 2, 2)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_column_shards_tile_the_global_rows(world):
+    """Across ranks, the kept rows of the column-sharded projections cover every global
+    row exactly once (kv rows excepted when they are replicated)."""
+    cfg = vs.CONFIG4
+    n_in = 2 * cfg.gdn_heads * cfg.gdn_dk + 2 * cfg.gdn_heads * cfg.gdn_dv + 2 * cfg.gdn_heads
+    for fn, total in ((vs._ranges_gdn_in, n_in), (vs._ranges_gate_up, 2 * cfg.intermediate)):
+        hits = np.zeros(total, dtype=np.int64)
+        for r in range(world):
+            for a, b in fn(cfg, vs.shard_plan(cfg, r, world)):
+                hits[a:b] += 1
+        assert (hits == 1).all()
+    d = cfg.head_dim
+    hits = np.zeros(2 * cfg.attn_heads * d, dtype=np.int64)
+    for r in range(world):
+        for a, b in vs._ranges_attn_qkv(cfg, vs.shard_plan(cfg, r, world))[:2]:
+            hits[a:b] += 1
+    assert (hits == 1).all()
+
+
+def test_quant_row_and_col_slices():
+    gen = torch.Generator().manual_seed(5)
+    q = vs.random_quant(gen, 64, 512, 64, 4, "cpu")
+    assert (q.N, q.K) == (64, 512) and q.w.shape == (64, 64) and q.scales.shape == (64, 8)
+    r = q.rows([(0, 8), (32, 40)])
+    assert torch.equal(r.w, torch.cat([q.w[:8], q.w[32:40]]))
+    c = q.cols(128, 256)
+    assert (c.N, c.K) == (64, 128) and torch.equal(c.scales, q.scales[:, 2:4])
+    with pytest.raises(ValueError):
+        q.cols(32, 128)
+
+
+def test_config4_weight_bytes_per_rank():
+    """Streamed bytes per forward: the packed weights, scales and biases of every
+    projection (about 13.7 GB at TP=1), split evenly by TP except the replicated kv rows."""
+    cfg = vs.CONFIG4
+    H, I, G = cfg.hidden, cfg.intermediate, cfg.group
+
+    def qbytes(N, K):
+        return N * K // 2 + 2 * 2 * N * (K // G)
+
+    gdn = qbytes(4 * 4096 + 64, H) + qbytes(H, 4096)
+    attn = qbytes(2 * 6144 + 2 * 1024, H) + qbytes(H, 6144)
+    mlp = qbytes(2 * I, H) + qbytes(H, I)
+    total = 48 * gdn + 16 * attn + 64 * mlp
+    assert 13.0e9 < total < 14.5e9
+
+
+# ----------------------------------------------------------------------------- gloo ranks (CPU)
+
+def _run_ranks(target, world, args_fn, timeout=300):
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=target, args=args_fn(r)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    return codes
+
+
+@pytest.fixture(scope="module")
+def tiny_tp1_reference():
+    import stack_ref
+    cfg = vs.TINY
+    plan = vs.shard_plan(cfg, 0, 1)
+    w = vs.build_rank_weights(cfg, plan, 0, "cpu")
+    st = vs.build_rank_state(cfg, plan, 0, "cpu")
+    return stack_ref.forward(cfg, plan, w, st, vs.make_block(cfg, 0, "cpu"))
+
+
+def test_tp2_gloo_matches_tp1_and_dropped_reduce_diverges(tmp_path, tiny_tp1_reference):
+    import stack_workers
+    ref = tiny_tp1_reference["out"].numpy()
+    results = {}
+    for drop in (False, True):
+        out = tmp_path / f"tp2_drop{int(drop)}.pt"
+        port = free_port()
+        codes = _run_ranks(stack_workers.gloo_reference_rank, 2,
+                           lambda r: (r, 2, port, str(out), asdict(vs.TINY), drop))
+        assert codes == [0, 0], codes
+        results[drop] = torch.load(out)["out"].numpy()
+    err, err_drop = closeness(results[False], ref), closeness(results[True], ref)
+    print(f"TP=2 vs TP=1: {err:.3e}; without the all-reduce: {err_drop:.3e}")
+    assert err <= 3e-2
+    assert err_drop > max(0.05, 10 * err)
+
+
+def test_reference_stack_is_self_consistent(tiny_tp1_reference):
+    """The CPU reference's pieces: outputs finite, normalised rows, alpha in (0, 1)."""
+    r = tiny_tp1_reference
+    assert torch.isfinite(r["out"]).all()
+    rms = r["out"].pow(2).mean(dim=1).sqrt()
+    assert (rms > 0.5).all() and (rms < 2.0).all()
+    for a in r["alpha"]:
+        assert ((a > 0) & (a < 1)).all()
+    for qkv in r["qkv"]:
+        n = qkv[1].float().pow(2).sum(-1).sqrt()  # k rows are unit length
+        assert torch.allclose(n, torch.ones_like(n), atol=1e-2)
+
+
+# ----------------------------------------------------------------------------- CUDA stack (GPU)
+
+@pytest.mark.gpu
+def test_cuda_stack_tp1_matches_reference(cuda):
+    import stack_ref
+    cfg = vs.TINY
+    stack = vs.VerifyStack(cfg, 0, 1, seed=0, device=cuda)
+    hidden = vs.make_block(cfg, 0, cuda)
+    out = stack.forward(hidden).float().cpu()
+    torch.cuda.synchronize()
+    plan = stack.plan
+    ref = stack_ref.forward(cfg, plan, stack.w, stack.state, hidden)
+    assert closeness(out.numpy(), ref["out"].numpy()) <= 2e-2
+    # the capture the rollback consumes, and the state after the block
+    for gi in range(len(ref["qkv"])):
+        assert closeness(stack.capture_qkv[gi].float().cpu().numpy(), ref["qkv"][gi].numpy()) <= 2e-2
+        assert closeness(stack.capture_alpha[gi].cpu().numpy(), ref["alpha"][gi].numpy()) <= 2e-2
+        assert closeness(stack.capture_beta[gi].cpu().numpy(), ref["beta"][gi].numpy()) <= 2e-2
+        s, sr = stack.state_out[gi].cpu().numpy(), ref["state"][gi].numpy()
+        assert np.max(np.abs(s - sr)) / np.max(np.abs(sr)) <= 2e-2
+    ai = 0
+    for L, S in zip(stack.w["layers"], stack.state["layers"]):
+        if L["kind"] == "attn":
+            for key in ("cache_k", "cache_v"):
+                got = S[key].float().cpu()[:, :cfg.context + cfg.block]
+                want = ref[key][ai][:, :cfg.context + cfg.block]
+                assert closeness(got.numpy(), want.numpy()) <= 2e-2
+            ai += 1
+
+
+@pytest.mark.gpu
+def test_cuda_stack_graph_replay_equals_eager(cuda):
+    cfg = vs.TINY
+    stack = vs.VerifyStack(cfg, 0, 1, seed=1, device=cuda)
+    hidden = vs.make_block(cfg, 1, cuda)
+    eager = stack.forward(hidden).clone()
+    g = stack.capture(hidden)
+    stack.out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(stack.out, eager)
+    del g
+
+
+@pytest.mark.gpu
+def test_cuda_stack_config4_shapes_run(cuda):
+    """Config-4 layer shapes (hidden 5120, MLP 17408, 32 x 128 gated-delta heads, 24 x 256
+    q heads with 4 kv heads) for one gated-delta and one attention layer: the forward is
+    finite and its graph replay is bit-identical to eager."""
+    from dataclasses import replace
+    cfg = replace(vs.CONFIG4, layers=4, attn_interval=2, context=256)
+    stack = vs.VerifyStack(cfg, 0, 1, seed=2, device=cuda)
+    hidden = vs.make_block(cfg, 2, cuda)
+    eager = stack.forward(hidden).clone()
+    assert torch.isfinite(eager.float()).all()
+    g = stack.capture(hidden)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(stack.out, eager)
+    del g
+
+
+@pytest.mark.gpu
+def test_cuda_stack_tp2_nccl_matches_tp1_reference(cuda, tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import stack_ref
+    import stack_workers
+    cfg = vs.TINY
+    plan = vs.shard_plan(cfg, 0, 1)
+    w = vs.build_rank_weights(cfg, plan, 0, cuda)
+    st = vs.build_rank_state(cfg, plan, 0, cuda)
+    ref = stack_ref.forward(cfg, plan, w, st, vs.make_block(cfg, 0, cuda))["out"].numpy()
+    out = tmp_path / "tp2_nccl.pt"
+    port = free_port()
+    codes = _run_ranks(stack_workers.nccl_stack_rank, 2, lambda r: (r, 2, port, str(out), asdict(cfg)))
+    assert codes == [0, 0], codes
+    res = torch.load(out)
+    assert torch.equal(res["eager"], res["graphed"])
+    assert closeness(res["eager"].float().numpy(), ref) <= 3e-2
