@@ -49,6 +49,8 @@
 // as MLX packs them.
 #include "common.cuh"
 
+#include <cstdlib>
+
 namespace dflash {
 namespace qmm {
 
@@ -65,7 +67,7 @@ constexpr int kMaxTileBlocks = 16;               // 16-row blocks per row tile (
 constexpr int kRowBytes = 128;                   // packed weight bytes per row per stage
 constexpr int kMaxStages = 8;
 constexpr int kMaxSbStages = 8;
-constexpr int kMaxCluster = 2;
+constexpr int kMaxCluster = 8;  // CTAs of a cluster, each taking a contiguous 1/cs of K
 constexpr int kSmemLimit = 232448;               // opt-in shared memory per block, sm_100
 constexpr int kBarConsumers = 1;                 // named barrier: all consumer warps
 constexpr int kPrepThreads = 32;                 // one warp per prep block: fits beside a running main CTA
@@ -108,10 +110,6 @@ __host__ __device__ __forceinline__ constexpr int x_swizzle(int m) {
 }
 
 // ------------------------------------------------------------------ small device helpers
-__device__ __forceinline__ void pdl_launch_dependents() {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // (v & mask) | mag as one LOP3: the mask is an immediate, the magic a register (left
 // to itself the compiler splits this into an AND and an OR with two immediates, which
@@ -165,16 +163,6 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
         : "memory");
 }
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t cluster_size() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
-    return r;
-}
 __device__ __forceinline__ uint32_t cluster_id() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
@@ -184,12 +172,6 @@ __device__ __forceinline__ uint32_t nclusters_x() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
     return r;
-}
-// Address of the same shared-memory offset in CTA `rank` of this cluster.
-__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
-    uint32_t d;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(addr), "r"(rank));
-    return d;
 }
 // Store into another CTA's shared memory; the bytes complete on that CTA's mbarrier.
 __device__ __forceinline__ void st_async_f32x2(uint32_t addr, float a, float b, uint32_t remote_bar) {
@@ -238,9 +220,6 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
             return;
         }
     }
-}
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 // Split cluster barrier: a relaxed arrive (orders nothing by itself; preceded by
 // fence.mbarrier_init it publishes barrier initialisation) and the matching wait.
@@ -356,7 +335,8 @@ struct Params {
     uint16_t* y;
     int M, N, K, GT;
     int R, nb;    // tile rows = 16 nb
-    int nb0;      // blocks of a tile written by cluster rank 0 (rank 1 writes the rest)
+    int nb0;         // clusters of 2: blocks of a tile written by rank 0 (rank 1 writes the rest)
+    int own_stride;  // clusters of 4 or 8: rows of one sender's slot in the receive buffer
     int ntiles;   // ceil(N / R)
     int S;        // stages along K
     int NS, NSB;  // ring depths
@@ -368,7 +348,7 @@ struct Params {
 struct Bars {
     uint64_t full[kMaxStages], empty[kMaxStages];
     uint64_t sbfull[kMaxSbStages], sbempty[kMaxSbStages];
-    uint64_t xfull, xdone;  // cluster exchange: the peer's rows for us have landed / it has read what we sent
+    uint64_t xfull, xdone;  // cluster exchange: the other CTAs' rows for us have landed / they have read ours
     int abort;
 };
 
@@ -702,7 +682,9 @@ __device__ __forceinline__ bool issue_aux(int j, int& pq, Bars* bars, volatile i
     return true;
 }
 
-template <class C>
+// CS: CTAs per cluster (1, 2, 4 or 8), fixed at compile time so that the exchange of
+// partials between them compiles to straight-line code.
+template <class C, int CS>
 __global__ void __launch_bounds__(kThreads, 1)
     qmm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
                const __grid_constant__ CUtensorMap tm_b, const Params p) {
@@ -714,7 +696,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sbring = ring + p.NS * p.stage_bytes;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t rank = cluster_rank(), cs = cluster_size();
+    constexpr uint32_t cs = CS;
+    const uint32_t rank = CS > 1 ? cluster_rank() : 0u;
     const int cid = (int)cluster_id(), ncl = (int)nclusters_x();
     const int s_beg = (int)((long long)p.S * rank / cs), s_end = (int)((long long)p.S * (rank + 1) / cs);
     const int nstages = s_end - s_beg;
@@ -738,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars->sbempty[i], kConsumerWarps);
         }
         mbar_init(&bars->xfull, 1);
-        mbar_init(&bars->xdone, 1);
+        mbar_init(&bars->xdone, CS > 1 ? CS - 1 : 1);
         bars->abort = 0;
         fence_barrier_init();
     }
@@ -863,76 +846,152 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             named_bar_sync(kBarConsumers, kConsumerThreads);
-            const int own0 = cs > 1 ? (rank == 0 ? 0 : p.nb0) : 0;
-            const int own1 = cs > 1 ? (rank == 0 ? p.nb0 : p.nb) : p.nb;
-            const int own_rows = 16 * (own1 - own0);
-            uint16_t* stg = reinterpret_cast<uint16_t*>(bufa);  // bf16 y of the owned rows, [m][row]
-            if (kl == 0) {
-                const int peer0 = rank == 0 ? p.nb0 : 0;  // first block the peer writes
+            int own0, own1, own_rows;
+            uint16_t* stg;
+            if constexpr (CS <= 2) {
+                own0 = cs > 1 ? (rank == 0 ? 0 : p.nb0) : 0;
+                own1 = cs > 1 ? (rank == 0 ? p.nb0 : p.nb) : p.nb;
+                own_rows = 16 * (own1 - own0);
+                stg = reinterpret_cast<uint16_t*>(bufa);  // bf16 y of the owned rows, [m][row]
+                if (kl == 0) {
+                    const int peer0 = rank == 0 ? p.nb0 : 0;  // first block the peer writes
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    if (i >= nblk) break;
+                    for (int i = 0; i < 4; ++i) {
+                        if (i >= nblk) break;
 #pragma unroll
-                    for (int h = 0; h < 2; ++h)
+                        for (int h = 0; h < 2; ++h)
 #pragma unroll
-                        for (int nt = 0; nt < C::NT; ++nt) {
-                            const float2 o = *reinterpret_cast<const float2*>(
-                                bufb + (16 * (qd + 4 * i) + pr + 8 * h) * MR + 8 * nt + 2 * tq);
-                            acc[i][nt][2 * h] += o.x;
-                            acc[i][nt][2 * h + 1] += o.y;
+                            for (int nt = 0; nt < C::NT; ++nt) {
+                                const float2 o = *reinterpret_cast<const float2*>(
+                                    bufb + (16 * (qd + 4 * i) + pr + 8 * h) * MR + 8 * nt + 2 * tq);
+                                acc[i][nt][2 * h] += o.x;
+                                acc[i][nt][2 * h + 1] += o.y;
+                            }
+                    }
+                    if (cs > 1) {
+                        if (tt > 0)  // the peer has read what we sent for the previous tile
+                            mbar_wait_cluster_bounded(&bars->xdone, (tt - 1) & 1, abort, DFLASH_DEVERR_QMM_REDUCE);
+                        if (tid == 0) mbar_arrive_expect_tx(&bars->xfull, (uint32_t)own_rows * MR * 4u);
+                        const uint32_t peer = rank ^ 1u;
+                        const uint32_t peer_recv = map_to_rank(smem_u32(recv), peer);
+                        const uint32_t peer_bar = map_to_rank(smem_u32(&bars->xfull), peer);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            if (i >= nblk) break;
+                            const int b = qd + 4 * i;
+                            if (b >= own0 && b < own1) continue;
+#pragma unroll
+                            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                                for (int nt = 0; nt < C::NT; ++nt)
+                                    st_async_f32x2(
+                                        peer_recv + (uint32_t)((16 * (b - peer0) + pr + 8 * h) * MR + 8 * nt + 2 * tq) * 4u,
+                                        acc[i][nt][2 * h], acc[i][nt][2 * h + 1], peer_bar);
                         }
-                }
-                if (cs > 1) {
-                    if (tt > 0)  // the peer has read what we sent for the previous tile
-                        mbar_wait_cluster_bounded(&bars->xdone, (tt - 1) & 1, abort, DFLASH_DEVERR_QMM_REDUCE);
-                    if (tid == 0) mbar_arrive_expect_tx(&bars->xfull, (uint32_t)own_rows * MR * 4u);
-                    const uint32_t peer = rank ^ 1u;
-                    const uint32_t peer_recv = map_to_rank(smem_u32(recv), peer);
-                    const uint32_t peer_bar = map_to_rank(smem_u32(&bars->xfull), peer);
+                        mbar_wait_cluster_bounded(&bars->xfull, tt & 1, abort, DFLASH_DEVERR_QMM_REDUCE);
+                    }
+                    // the owned rows: rank 0's partial first, then rank 1's, rounded once to bf16
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         if (i >= nblk) break;
                         const int b = qd + 4 * i;
-                        if (b >= own0 && b < own1) continue;
+                        if (b < own0 || b >= own1) continue;
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int rowl = 16 * (b - own0) + pr + 8 * h;
+#pragma unroll
+                            for (int nt = 0; nt < C::NT; ++nt)
+#pragma unroll
+                                for (int e = 0; e < 2; ++e) {
+                                    const int m = 8 * nt + 2 * tq + e;
+                                    float v = acc[i][nt][2 * h + e];
+                                    if (cs > 1) {
+                                        const float o = recv[rowl * MR + m];
+                                        v = rank == 0 ? v + o : o + v;
+                                    }
+                                    const __nv_bfloat16 o = __float2bfloat16_rn(v);
+                                    stg[m * own_rows + rowl] = *reinterpret_cast<const uint16_t*>(&o);
+                                }
+                        }
+                    }
+                }
+                named_bar_sync(kBarConsumers, kConsumerThreads);
+                // the peer may refill recv once we are past reading it (only if it has another tile)
+                if (cs > 1 && tid == 0 && t + ncl < p.ntiles)
+                    mbar_arrive_remote(map_to_rank(smem_u32(&bars->xdone), rank ^ 1u));
+            } else {
+                // Cluster rank r owns (reduces and writes) blocks [nb r / cs, nb (r + 1) / cs) of
+                // the tile.  The k-lane 0 warps park the CTA's partial of every block in bufa;
+                // then all consumer threads push the rows other ranks own into their receive
+                // buffers (slot = sender rank, skipping the owner), wait for their own rows
+                // from the other ranks, and sum them in rank order into the bf16 staging
+                // buffer (bufb).
+                own0 = (int)((uint32_t)p.nb * rank / cs);
+                own1 = (int)((uint32_t)p.nb * (rank + 1) / cs);
+                own_rows = 16 * (own1 - own0);
+                stg = reinterpret_cast<uint16_t*>(bufb);
+                if (kl == 0) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        if (i >= nblk) break;
 #pragma unroll
                         for (int h = 0; h < 2; ++h)
 #pragma unroll
-                            for (int nt = 0; nt < C::NT; ++nt)
-                                st_async_f32x2(
-                                    peer_recv + (uint32_t)((16 * (b - peer0) + pr + 8 * h) * MR + 8 * nt + 2 * tq) * 4u,
-                                    acc[i][nt][2 * h], acc[i][nt][2 * h + 1], peer_bar);
-                    }
-                    mbar_wait_cluster_bounded(&bars->xfull, tt & 1, abort, DFLASH_DEVERR_QMM_REDUCE);
-                }
-                // the owned rows: rank 0's partial first, then rank 1's, rounded once to bf16
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    if (i >= nblk) break;
-                    const int b = qd + 4 * i;
-                    if (b < own0 || b >= own1) continue;
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int rowl = 16 * (b - own0) + pr + 8 * h;
-#pragma unroll
-                        for (int nt = 0; nt < C::NT; ++nt)
-#pragma unroll
-                            for (int e = 0; e < 2; ++e) {
-                                const int m = 8 * nt + 2 * tq + e;
-                                float v = acc[i][nt][2 * h + e];
-                                if (cs > 1) {
-                                    const float o = recv[rowl * MR + m];
-                                    v = rank == 0 ? v + o : o + v;
-                                }
-                                const __nv_bfloat16 o = __float2bfloat16_rn(v);
-                                stg[m * own_rows + rowl] = *reinterpret_cast<const uint16_t*>(&o);
+                            for (int nt = 0; nt < C::NT; ++nt) {
+                                float2* q = reinterpret_cast<float2*>(bufa + (16 * (qd + 4 * i) + pr + 8 * h) * MR +
+                                                                      8 * nt + 2 * tq);
+                                const float2 o = *reinterpret_cast<const float2*>(
+                                    bufb + (16 * (qd + 4 * i) + pr + 8 * h) * MR + 8 * nt + 2 * tq);
+                                *q = make_float2(acc[i][nt][2 * h] + o.x, acc[i][nt][2 * h + 1] + o.y);
                             }
                     }
                 }
+                named_bar_sync(kBarConsumers, kConsumerThreads);
+                if (tt > 0)  // every receiver has read what we sent for the previous tile
+                    mbar_wait_cluster_bounded(&bars->xdone, (tt - 1) & 1, abort, DFLASH_DEVERR_QMM_REDUCE);
+                if (tid == 0) mbar_arrive_expect_tx(&bars->xfull, (cs - 1) * (uint32_t)own_rows * MR * 4u);
+                const uint32_t recv_base = smem_u32(recv), xfull_base = smem_u32(&bars->xfull);
+                const uint32_t recv_cap = (cs - 1) * (uint32_t)p.own_stride * MR * 4u;
+                constexpr int P2 = MR / 2;  // float2 per row
+                for (int e = tid; e < p.nb * 16 * P2; e += kConsumerThreads) {
+                    const int row = e / P2, c2 = e - row * P2, b = row >> 4;
+                    if (b >= own0 && b < own1) continue;
+                    uint32_t o = 0;  // owner of block b
+                    while (o + 1 < cs && (int)((uint32_t)p.nb * (o + 1) / cs) <= b) ++o;
+                    const int o0 = (int)((uint32_t)p.nb * o / cs);
+                    const uint32_t slot = rank < o ? rank : rank - 1;
+                    const uint32_t off = ((slot * (uint32_t)p.own_stride + (uint32_t)(row - 16 * o0)) * MR + 2 * c2) * 4u;
+                    if (off + 8u > recv_cap) {  // cannot happen for a consistent plan; never write past the buffer
+                        atomicOr(&g_device_error, DFLASH_DEVERR_QMM_REDUCE);
+                        continue;
+                    }
+                    const float2 v = *reinterpret_cast<const float2*>(bufa + row * MR + 2 * c2);
+                    st_async_f32x2(map_to_rank(recv_base, o) + off, v.x, v.y, map_to_rank(xfull_base, o));
+                }
+                mbar_wait_cluster_bounded(&bars->xfull, tt & 1, abort, DFLASH_DEVERR_QMM_REDUCE);
+                for (int e = tid; e < own_rows * MR; e += kConsumerThreads) {
+                    const int rowl = e / MR, m = e - rowl * MR;
+                    float v = 0.f;
+#pragma unroll
+                    for (uint32_t r = 0; r < cs; ++r) {
+                        if (r == rank) {
+                            v += bufa[(16 * own0 + rowl) * MR + m];
+                        } else {
+                            const uint32_t sl = r < rank ? r : r - 1;
+                            v += recv[(sl * p.own_stride + rowl) * MR + m];
+                        }
+                    }
+                    const __nv_bfloat16 o = __float2bfloat16_rn(v);
+                    stg[m * own_rows + rowl] = *reinterpret_cast<const uint16_t*>(&o);
+                }
+                named_bar_sync(kBarConsumers, kConsumerThreads);
+                // the senders may refill recv once we are past reading it (only if they have another tile)
+                if (tid == 0 && t + ncl < p.ntiles) {
+#pragma unroll
+                    for (uint32_t r = 0; r < cs; ++r)
+                        if (r != rank) mbar_arrive_remote(map_to_rank(smem_u32(&bars->xdone), r));
+                }
             }
-            named_bar_sync(kBarConsumers, kConsumerThreads);
-            // the peer may refill recv once we are past reading it (only if it has another tile)
-            if (cs > 1 && tid == 0 && t + ncl < p.ntiles)
-                mbar_arrive_remote(map_to_rank(smem_u32(&bars->xdone), rank ^ 1u));
             // y rows of the owned blocks, from the staging buffer
             const int n0 = t * p.R + 16 * own0;
             if (p.y_vec) {
@@ -967,7 +1026,7 @@ struct Shape {
 };
 
 struct Plan {
-    int cs, nclusters, R, nb, nb0, ntiles, S, NS, NSB;
+    int cs, nclusters, R, nb, nb0, own_stride, ntiles, S, NS, NSB;
     uint32_t stage_bytes, sb_bytes, red_off, red_bytes, recv_off, bar_off;
     size_t smem;
 };
@@ -998,29 +1057,59 @@ int first_batch_sb_slots(int S, int cs, int ns) {
     return worst;
 }
 
-// Tile height and grid: clusters of 2 CTAs (one per SM) split K in halves; tiles of at
-// most 256 rows, sized so that every cluster gets the same number of tiles (to within
-// one) and the tiles the same height; then the deepest ring that fits.
+// Cost model of one CTA's work, used to choose the cluster size and tile height: a stage
+// costs a fixed issue/hand-off time plus its bytes at one SM's share of the HBM stream,
+// and every tile ends in an epilogue that grows with the ranks exchanging partials.
+constexpr double kStageFixedUs = 0.25;
+constexpr double kSmBytesPerUs = 44000.0;
+constexpr double kEpilogueUs = 1.0, kEpiloguePerRankUs = 0.3;
+
+// Tile height and grid: clusters of cs CTAs (one per SM) split K into cs contiguous
+// ranges; tiles of at most 256 rows, sized so that every cluster gets the same number of
+// tiles (to within one) and the tiles the same height.  Among cs in {1, 2, 4, 8} and the
+// tiles-per-cluster counts, the plan with the lowest modelled time wins; then the deepest
+// ring that fits.  max_clusters[i] is how many clusters of 2^i CTAs fit on the device.
 template <class C>
-Plan make_plan(const Shape& s, int sms) {
+Plan make_plan(const Shape& s, const int* cmax_by_lg) {
     Plan pl;
     pl.S = stages_along_k<C>(s.K);
-    pl.cs = pl.S >= 2 ? kMaxCluster : 1;
-    const int cmax = sms / pl.cs > 0 ? sms / pl.cs : 1;
     const int NB = (s.N + 15) / 16;
-    const int T = (NB + kMaxTileBlocks * cmax - 1) / (kMaxTileBlocks * cmax);  // tiles per cluster
-    int nb = (NB + cmax * T - 1) / (cmax * T);
-    if (nb > kMaxTileBlocks) nb = kMaxTileBlocks;
-    if (nb < 1) nb = 1;
-    pl.nb = nb;
-    pl.nb0 = (nb + 1) / 2;
-    pl.R = 16 * nb;
+    double best = 1e30;
+    pl.cs = 1;
+    pl.nb = 1;
+    for (int lg = 0, cs = 1; cs <= kMaxCluster; ++lg, cs *= 2) {
+        if (cs > 1 && pl.S < cs) break;  // every CTA takes at least one stage
+        const int cmax = cmax_by_lg[lg];
+        if (cmax < 1) continue;
+        const int sp = (pl.S + cs - 1) / cs;
+        for (int T = 1; T <= 8; ++T) {
+            int nb = (NB + cmax * T - 1) / (cmax * T);
+            if (nb > kMaxTileBlocks) nb = kMaxTileBlocks;
+            if (nb < 1) nb = 1;
+            const int ntiles = (s.N + 16 * nb - 1) / (16 * nb);
+            const int ncl = ntiles < cmax ? ntiles : cmax;
+            const int teff = (ntiles + ncl - 1) / ncl;
+            const double cost = teff * (sp * (kStageFixedUs + 16.0 * nb * kRowBytes / kSmBytesPerUs) + kEpilogueUs +
+                                        kEpiloguePerRankUs * (cs - 1));
+            if (cost < best - 1e-9) {
+                best = cost;
+                pl.cs = cs;
+                pl.nb = nb;
+            }
+        }
+    }
+    pl.R = 16 * pl.nb;
     pl.ntiles = (s.N + pl.R - 1) / pl.R;
+    const int cmax = cmax_by_lg[pl.cs == 1 ? 0 : pl.cs == 2 ? 1 : pl.cs == 4 ? 2 : 3];
     pl.nclusters = pl.ntiles < cmax ? pl.ntiles : cmax;
+    pl.nb0 = (pl.nb + 1) / 2;
+    pl.own_stride = 16 * ((pl.nb + pl.cs - 1) / pl.cs);
     pl.stage_bytes = round_up_u32((uint32_t)pl.R * kRowBytes + C::PKT, 1024);
     pl.sb_bytes = C::STMA ? round_up_u32(2u * pl.R * 16, 128) : 0;
     pl.red_bytes = round_up_u32((uint32_t)pl.R * C::MR * 4, 128);
-    const uint32_t recv_bytes = round_up_u32((uint32_t)pl.nb0 * 16 * C::MR * 4, 128);
+    const uint32_t recv_bytes =
+        pl.cs <= 2 ? round_up_u32((uint32_t)pl.nb0 * 16 * C::MR * 4, 128)
+                   : round_up_u32((uint32_t)(pl.cs - 1) * pl.own_stride * C::MR * 4, 128);
     const uint32_t bar_bytes = round_up_u32(sizeof(Bars), 128);
     pl.NS = 0;
     pl.NSB = 1;
@@ -1048,16 +1137,67 @@ Plan make_plan(const Shape& s, int sms) {
 }
 
 template <class C>
+using QmmKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const Params);
+
+template <class C>
+QmmKernel<C> kernel_for(int cs) {
+    switch (cs) {
+        case 1: return qmm_kernel<C, 1>;
+        case 2: return qmm_kernel<C, 2>;
+        case 4: return qmm_kernel<C, 4>;
+        default: return qmm_kernel<C, 8>;
+    }
+}
+
+// How many clusters of 1, 2, 4 and 8 CTAs of qmm_kernel<C, cs> (full shared memory) fit on
+// `dev` at once; queried once per device (falls back to SMs / cs).
+template <class C>
+const int* max_clusters(int dev) {
+    static std::mutex mu;
+    static int cache[64][4];
+    static bool done[64] = {false};
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!done[dev]) {
+        const int sms = sm_count(dev);
+        for (int lg = 0, cs = 1; lg < 4; ++lg, cs *= 2) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)cs);
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = kSmemLimit;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = cs;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, kernel_for<C>(cs), &cfg) != cudaSuccess || n < 1) {
+                (void)cudaGetLastError();
+                n = sms / cs;
+            }
+            cache[dev][lg] = n;
+        }
+        done[dev] = true;
+    }
+    return cache[dev];
+}
+
+template <class C>
 int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scales,
            const dflash_bf16* biases, dflash_bf16* y, void* ws, cudaStream_t stream) {
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     static int launch_regs = 0;
     std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(qmm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-        cudaFuncAttributes fa;
-        if (attr_err == cudaSuccess) attr_err = cudaFuncGetAttributes(&fa, qmm_kernel<C>);
-        if (attr_err == cudaSuccess) launch_regs = fa.numRegs;
+        launch_regs = 1 << 30;
+        for (int cs = 1; cs <= kMaxCluster && attr_err == cudaSuccess; cs *= 2) {
+            attr_err = cudaFuncSetAttribute(kernel_for<C>(cs), cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+            cudaFuncAttributes fa;
+            if (attr_err == cudaSuccess) attr_err = cudaFuncGetAttributes(&fa, kernel_for<C>(cs));
+            if (attr_err == cudaSuccess && fa.numRegs < launch_regs) launch_regs = fa.numRegs;
+        }
     });
     if (attr_err != cudaSuccess)
         return fail(DFLASH_ERR_CUDA, "cudaFuncSetAttribute(qmm): %s", cudaGetErrorString(attr_err));
@@ -1068,7 +1208,15 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
 
     int dev = 0;
     DFLASH_CUDA_TRY(cudaGetDevice(&dev));
-    const Plan pl = make_plan<C>(s, sm_count(dev));
+    const int* cmax = max_clusters<C>(dev);
+    const Plan pl = make_plan<C>(s, cmax);
+    static const bool log_plan = getenv("DFLASH_QMM_LOG_PLAN") != nullptr;
+    if (log_plan)  // diagnostics: the plan of every launch on stderr
+        fprintf(stderr,
+                "dflash_qmm plan: M=%d N=%d K=%d g=%d b=%d -> cs=%d R=%d tiles=%d clusters=%d S=%d NS=%d NSB=%d "
+                "smem=%zu (fit: %d %d %d %d clusters of 1 2 4 8)\n",
+                s.M, s.N, s.K, s.group, s.bits, pl.cs, pl.R, pl.ntiles, pl.nclusters, pl.S, pl.NS, pl.NSB, pl.smem,
+                cmax[0], cmax[1], cmax[2], cmax[3]);
     if (pl.NS < 2) return fail(DFLASH_ERR_UNSUPPORTED, "qmm: no shared-memory plan for N=%d K=%d", s.N, s.K);
     const int GT = s.K / s.group;
 
@@ -1102,6 +1250,7 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
     p.R = pl.R;
     p.nb = pl.nb;
     p.nb0 = pl.nb0;
+    p.own_stride = pl.own_stride;
     p.ntiles = pl.ntiles;
     p.S = pl.S;
     p.NS = pl.NS;
@@ -1141,7 +1290,7 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
         cfg.stream = stream;
         cfg.attrs = attr;
         cfg.numAttrs = 2;
-        DFLASH_CUDA_TRY(cudaLaunchKernelEx(&cfg, qmm_kernel<C>, tm_w, tm_s, tm_b, p));
+        DFLASH_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel_for<C>(pl.cs), tm_w, tm_s, tm_b, p));
     }
     return DFLASH_OK;
 }

@@ -6,7 +6,9 @@
 // dflash_qmm and the recurrence is dflash_gdn_step.
 //
 // All tensors are row-major with one row per token (M rows, the verify block).  Every
-// kernel here is memory- or latency-bound and tiny next to the weight stream.
+// kernel here is latency-bound and tiny next to the weight stream, so each is launched
+// with programmatic dependent launch: it is scheduled while its predecessor drains and
+// waits (griddepcontrol.wait) before touching memory, then releases its successor.
 #include "common.cuh"
 #include "dflash_stack.h"
 
@@ -18,12 +20,28 @@ __device__ __forceinline__ uint16_t to_bf(float v) {
     const __nv_bfloat16 h = __float2bfloat16_rn(v);
     return *reinterpret_cast<const uint16_t*>(&h);
 }
+__device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 __device__ __forceinline__ float bf_round(float v) { return bf(to_bf(v)); }
 __device__ __forceinline__ float silu(float v) { return v / (1.f + __expf(-v)); }
+__device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
+    return static_cast<uint32_t>(to_bf(a)) | (static_cast<uint32_t>(to_bf(b)) << 16);
+}
 
-__device__ __forceinline__ float block_sum(float v, float* red) {
+// Wait for the predecessor, then let the successor be scheduled.
+__device__ __forceinline__ void chain_in() {
+    pdl_wait();
+    pdl_launch_dependents();
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
     __syncthreads();
     if (l == 0) red[w] = v;
@@ -33,10 +51,57 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
     return t;
 }
 
-// resid[m] += delta[m] (if given); out[m] = bf16(resid[m] * rsqrt(mean(resid[m]^2) + eps) * w)
-__global__ void add_rmsnorm_kernel(float* __restrict__ resid, const uint16_t* __restrict__ delta,
-                                   const uint16_t* __restrict__ w, uint16_t* __restrict__ out, int H, float eps) {
-    __shared__ float red[32];
+// resid[m] += delta[m] (if given); out[m] = bf16(resid[m] * rsqrt(mean(resid[m]^2) + eps) * w).
+// One CTA of 256 threads per row; each thread keeps VPT float4 of the row in registers
+// (H <= 1024 VPT, H a multiple of 4, delta / w / out 8-byte aligned).
+template <int VPT>
+__global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ resid, const uint16_t* __restrict__ delta,
+                                                          const uint16_t* __restrict__ w, uint16_t* __restrict__ out,
+                                                          int H, float eps) {
+    __shared__ float red[8];
+    chain_in();
+    const int m = blockIdx.x, H4 = H >> 2;
+    float4* r4 = reinterpret_cast<float4*>(resid + (size_t)m * H);
+    const uint2* d4 = reinterpret_cast<const uint2*>(delta + (size_t)m * H);
+    float4 v[VPT];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+        const int i = threadIdx.x + 256 * j;
+        if (i < H4) {
+            v[j] = r4[i];
+            if (delta) {
+                const uint2 d = d4[i];
+                v[j].x += bf16_lo(d.x);
+                v[j].y += bf16_hi(d.x);
+                v[j].z += bf16_lo(d.y);
+                v[j].w += bf16_hi(d.y);
+                r4[i] = v[j];
+            }
+            ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
+        }
+    }
+    const float rs = rsqrtf(block_sum(ss, red) / H + eps);
+    const uint2* w4 = reinterpret_cast<const uint2*>(w);
+    uint2* o4 = reinterpret_cast<uint2*>(out + (size_t)m * H);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+        const int i = threadIdx.x + 256 * j;
+        if (i < H4) {
+            const uint2 ww = w4[i];
+            o4[i] = make_uint2(pack_bf2(v[j].x * rs * bf16_lo(ww.x), v[j].y * rs * bf16_hi(ww.x)),
+                               pack_bf2(v[j].z * rs * bf16_lo(ww.y), v[j].w * rs * bf16_hi(ww.y)));
+        }
+    }
+}
+
+// The same for any H and alignment (row re-read from global memory for the second pass).
+__global__ void __launch_bounds__(256) add_rmsnorm_any_kernel(float* __restrict__ resid,
+                                                              const uint16_t* __restrict__ delta,
+                                                              const uint16_t* __restrict__ w,
+                                                              uint16_t* __restrict__ out, int H, float eps) {
+    __shared__ float red[8];
+    chain_in();
     const int m = blockIdx.x;
     float* r = resid + (size_t)m * H;
     float ss = 0.f;
@@ -54,6 +119,7 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ resid, const uint16_t* __
 
 // gu = [gate (I) | up (I)] per row -> y = silu(gate) * up
 __global__ void silu_mul_kernel(const uint16_t* __restrict__ gu, uint16_t* __restrict__ y, int M, int I) {
+    chain_in();
     const size_t n = (size_t)M * I;
     for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x) {
         const size_t m = e / I, i = e % I;
@@ -66,29 +132,32 @@ __global__ void silu_mul_kernel(const uint16_t* __restrict__ gu, uint16_t* __res
 // followed by SiLU.  x: [M, ld] with the convolved channels at [0, C); window: [kc-1, C];
 // w: [C, kc].  The C channels are `parts` equal parts (q, k, v); y holds each part as its
 // own contiguous [M, C / parts] block.  The window is the pre-round one and is only read:
-// after the round dflash_gdn_conv_rollback rebuilds it from the accepted inputs.
+// after the round dflash_gdn_conv_rollback rebuilds it from the accepted inputs.  One
+// thread per channel; the M <= 16 inputs are loaded up front.
 template <int KC>
 __global__ void conv_silu_kernel(const uint16_t* __restrict__ x, int ld, const uint16_t* __restrict__ window,
                                  const uint16_t* __restrict__ w, uint16_t* __restrict__ y, int M, int C, int parts) {
+    chain_in();
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= C) return;
     constexpr int h = KC - 1;
-    float hist[h > 0 ? h : 1];
+    float xs[h + 16];
 #pragma unroll
-    for (int i = 0; i < h; ++i) hist[i] = bf(window[(size_t)i * C + c]);
+    for (int i = 0; i < h; ++i) xs[i] = bf(window[(size_t)i * C + c]);
+#pragma unroll
+    for (int t = 0; t < 16; ++t) xs[h + t] = t < M ? bf(x[(size_t)t * ld + c]) : 0.f;
     float wk[KC];
 #pragma unroll
     for (int i = 0; i < KC; ++i) wk[i] = bf(w[(size_t)c * KC + i]);
     const int cp = C / parts, part = c / cp, cc = c - part * cp;
-    for (int t = 0; t < M; ++t) {
-        const float xt = bf(x[(size_t)t * ld + c]);
-        float acc = wk[KC - 1] * xt;
 #pragma unroll
-        for (int i = 0; i < h; ++i) acc = fmaf(wk[i], hist[i], acc);
-        y[((size_t)part * M + t) * cp + cc] = to_bf(silu(acc));
+    for (int t = 0; t < 16; ++t) {
+        if (t < M) {
+            float acc = 0.f;
 #pragma unroll
-        for (int i = 0; i + 1 < h; ++i) hist[i] = hist[i + 1];
-        if constexpr (h > 0) hist[h - 1] = xt;
+            for (int i = 0; i < KC; ++i) acc = fmaf(wk[i], xs[t + i], acc);
+            y[((size_t)part * M + t) * cp + cc] = to_bf(silu(acc));
+        }
     }
 }
 
@@ -99,6 +168,7 @@ __global__ void conv_silu_kernel(const uint16_t* __restrict__ x, int ld, const u
 __global__ void gdn_gates_kernel(uint16_t* __restrict__ q, uint16_t* __restrict__ k, const uint16_t* __restrict__ ab,
                                  int ld_ab, const float* __restrict__ a_log, const float* __restrict__ dt_bias,
                                  float* __restrict__ alpha, float* __restrict__ beta, int M, int heads, int dk) {
+    chain_in();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= M * heads) return;
     const int t = warp / heads, h = warp % heads;
@@ -106,9 +176,7 @@ __global__ void gdn_gates_kernel(uint16_t* __restrict__ q, uint16_t* __restrict_
         uint16_t* v = (part ? k : q) + ((size_t)t * heads + h) * dk;
         float ss = 0.f;
         for (int i = lane; i < dk; i += 32) ss = fmaf(bf(v[i]), bf(v[i]), ss);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float rs = rsqrtf(ss + 1e-6f);
+        const float rs = rsqrtf(warp_sum(ss) + 1e-6f);
         for (int i = lane; i < dk; i += 32) v[i] = to_bf(bf(v[i]) * rs);
     }
     if (lane == 0) {
@@ -124,15 +192,14 @@ __global__ void gdn_gates_kernel(uint16_t* __restrict__ q, uint16_t* __restrict_
 __global__ void gated_norm_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ z, int ld_z,
                                   const uint16_t* __restrict__ w, uint16_t* __restrict__ out, int M, int heads, int dv,
                                   float eps) {
+    chain_in();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= M * heads) return;
     const int t = warp / heads, h = warp % heads;
     const uint16_t* ov = o + ((size_t)t * heads + h) * dv;
     float ss = 0.f;
     for (int i = lane; i < dv; i += 32) ss = fmaf(bf(ov[i]), bf(ov[i]), ss);
-#pragma unroll
-    for (int s = 16; s > 0; s >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, s);
-    const float rs = rsqrtf(ss / dv + eps);
+    const float rs = rsqrtf(warp_sum(ss) / dv + eps);
     for (int i = lane; i < dv; i += 32) {
         const float zz = bf(z[(size_t)t * ld_z + (size_t)h * dv + i]);
         out[((size_t)t * heads + h) * dv + i] = to_bf(bf(ov[i]) * rs * bf(w[i]) * silu(zz));
@@ -151,6 +218,7 @@ __global__ void attn_prep_kernel(uint16_t* __restrict__ qkv, int ld, const uint1
                                  const uint16_t* __restrict__ k_norm, uint16_t* __restrict__ cache_k,
                                  uint16_t* __restrict__ cache_v, int M, int hq, int hkv, int rot, int pos0,
                                  int max_len, float eps, float theta) {
+    chain_in();
     constexpr int d = CH * 32;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int slots = hq + hkv;
@@ -174,9 +242,7 @@ __global__ void attn_prep_kernel(uint16_t* __restrict__ qkv, int ld, const uint1
         v[c] = bf(src[lane + 32 * c]);
         ss = fmaf(v[c], v[c], ss);
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float rs = rsqrtf(ss / d + eps);
+    const float rs = rsqrtf(warp_sum(ss) / d + eps);
 #pragma unroll
     for (int c = 0; c < CH; ++c) v[c] = bf_round(v[c] * rs * bf(nw[lane + 32 * c]));
     const int half_c = rot / 64;  // pair partner is c + half_c
@@ -203,11 +269,20 @@ __global__ void attn_prep_kernel(uint16_t* __restrict__ qkv, int ld, const uint1
     for (int c = 0; c < CH; ++c) dst[lane + 32 * c] = to_bf(v[c]);
 }
 
-// Attention of the M block tokens over the cache, one CTA (8 warps) per (q head, token).
-// Token t sees keys 0 .. pos0 + t (the cache prefix and the block causally).  q: row t of
-// qkv at head h; gate at [hq * d + h * d); q head h reads kv head h / (hq / hkv).
-// out[t, h * d + e] = softmax(q K^T * scale) V * sigmoid(gate).  Each warp runs an online
-// softmax over keys warp, warp + 8, ...; lane l holds dims [l * CH, l * CH + CH).
+// Decode attention of the block.  A cluster of kSplit CTAs serves one (kv head, token t):
+// the keys 0 .. pos0 + t that token t sees are cut into kSplit contiguous ranges, one per
+// CTA, and each CTA runs an online softmax over its range for all G = hq / hkv q heads
+// that read this kv head, in chunks of kChunk keys:
+//   scores: warp w takes keys w, w + 8, ...; lane l holds dims [l CH, l CH + CH) of q (G
+//           heads, in registers) and of the key row, so a key row is one coalesced read;
+//   p V:    warp w owns dims [w d/8, (w+1) d/8); its lanes split those dims and the keys.
+// The CTAs' (max, sum, p V) partials are merged by cluster rank 0 through distributed
+// shared memory, which also applies the output gate:
+//   out[t, h d + e] = softmax(q k^T scale) v * sigmoid(gate[t, h d + e]).
+constexpr int kSplit = 4;
+constexpr int kChunk = 256;
+constexpr int kMaxG = 8;
+
 template <int CH>
 __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __restrict__ qkv, int ld,
                                                           const uint16_t* __restrict__ cache_k,
@@ -215,56 +290,128 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __rest
                                                           uint16_t* __restrict__ out, int hq, int hkv, int pos0,
                                                           int max_len, float scale) {
     constexpr int d = CH * 32;
-    __shared__ float s_m[8], s_l[8];
-    __shared__ float s_acc[8][d];
-    const int h = blockIdx.x, t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kvh = h / (hq / hkv);
-    const uint16_t* qrow = qkv + (size_t)t * ld + (size_t)h * d + lane * CH;
-    float q[CH];
-#pragma unroll
-    for (int c = 0; c < CH; ++c) q[c] = bf(qrow[c]) * scale;
-    const uint16_t* kb = cache_k + (size_t)kvh * max_len * d + lane * CH;
-    const uint16_t* vb = cache_v + (size_t)kvh * max_len * d + lane * CH;
+    constexpr int DPW = d / 8;     // dims per warp in the p V pass
+    constexpr int KPL = 32 / DPW;  // key phases per warp in the p V pass
+    __shared__ float s_p[kMaxG][kChunk];
+    __shared__ float s_acc[kMaxG][d];  // this CTA's p V partial (read by rank 0)
+    __shared__ float s_m[kMaxG], s_l[kMaxG], s_corr[kMaxG];
+    chain_in();
+    const int G = hq / hkv;
+    const int kvh = blockIdx.x / kSplit, t = blockIdx.y;
+    const uint32_t rank = cluster_rank();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = pos0 + t + 1;
-    float m = -INFINITY, l = 0.f, acc[CH];
+    const int k0 = (int)((long long)n * rank / kSplit), k1 = (int)((long long)n * (rank + 1) / kSplit);
+
+    float q[kMaxG][CH];
+    const uint16_t* qrow = qkv + (size_t)t * ld + (size_t)kvh * G * d + lane * CH;
 #pragma unroll
-    for (int c = 0; c < CH; ++c) acc[c] = 0.f;
-    for (int j = warp; j < n; j += 8) {
-        const uint16_t* kr = kb + (size_t)j * d;
-        float sdot = 0.f;
+    for (int g = 0; g < kMaxG; ++g)
 #pragma unroll
-        for (int c = 0; c < CH; ++c) sdot = fmaf(q[c], bf(kr[c]), sdot);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, o);
-        const float mn = fmaxf(m, sdot);
-        const float corr = __expf(m - mn), p = __expf(sdot - mn);
-        l = l * corr + p;
-        const uint16_t* vr = vb + (size_t)j * d;
-#pragma unroll
-        for (int c = 0; c < CH; ++c) acc[c] = fmaf(p, bf(vr[c]), acc[c] * corr);
-        m = mn;
+        for (int c = 0; c < CH; ++c) q[g][c] = g < G ? bf(qrow[(size_t)g * d + c]) * scale : 0.f;
+    if (threadIdx.x < kMaxG) {
+        s_m[threadIdx.x] = -INFINITY;
+        s_l[threadIdx.x] = 0.f;
     }
-    if (lane == 0) {
-        s_m[warp] = m;
-        s_l[warp] = l;
-    }
+    const uint16_t* kb = cache_k + (size_t)kvh * max_len * d;
+    const uint16_t* vb = cache_v + (size_t)kvh * max_len * d;
+    const int e = warp * DPW + lane % DPW, kp = lane / DPW;
+    float acc[kMaxG];
 #pragma unroll
-    for (int c = 0; c < CH; ++c) s_acc[warp][lane * CH + c] = acc[c];
-    __syncthreads();
-    float mx = -INFINITY;
-    for (int w = 0; w < 8; ++w) mx = fmaxf(mx, s_m[w]);
-    float den = 0.f, f[8];
-    for (int w = 0; w < 8; ++w) {
-        f[w] = s_l[w] > 0.f ? __expf(s_m[w] - mx) : 0.f;
-        den = fmaf(s_l[w], f[w], den);
+    for (int g = 0; g < kMaxG; ++g) acc[g] = 0.f;
+
+    for (int c0 = k0; c0 < k1; c0 += kChunk) {
+        const int len = min(kChunk, k1 - c0);
+        __syncthreads();  // s_p of the previous chunk is consumed; s_m / s_l initialised
+        // scores
+        for (int j = warp; j < len; j += 8) {
+            const uint16_t* kr = kb + (size_t)(c0 + j) * d + lane * CH;
+            float kv[CH];
+            if constexpr (CH == 8) {
+                const uint4 u = *reinterpret_cast<const uint4*>(kr);
+                kv[0] = bf16_lo(u.x); kv[1] = bf16_hi(u.x); kv[2] = bf16_lo(u.y); kv[3] = bf16_hi(u.y);
+                kv[4] = bf16_lo(u.z); kv[5] = bf16_hi(u.z); kv[6] = bf16_lo(u.w); kv[7] = bf16_hi(u.w);
+            } else if constexpr (CH == 4) {
+                const uint2 u = *reinterpret_cast<const uint2*>(kr);
+                kv[0] = bf16_lo(u.x); kv[1] = bf16_hi(u.x); kv[2] = bf16_lo(u.y); kv[3] = bf16_hi(u.y);
+            } else {
+                const uint32_t u = *reinterpret_cast<const uint32_t*>(kr);
+                kv[0] = bf16_lo(u); kv[1] = bf16_hi(u);
+            }
+#pragma unroll
+            for (int g = 0; g < kMaxG; ++g) {
+                if (g < G) {
+                    float sdot = 0.f;
+#pragma unroll
+                    for (int c = 0; c < CH; ++c) sdot = fmaf(q[g][c], kv[c], sdot);
+                    sdot = warp_sum(sdot);
+                    if (lane == 0) s_p[g][j] = sdot;
+                }
+            }
+        }
+        __syncthreads();
+        // softmax bookkeeping: warp g owns head g
+        if (warp < G) {
+            float mc = -INFINITY;
+            for (int j = lane; j < len; j += 32) mc = fmaxf(mc, s_p[warp][j]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, o));
+            const float mold = s_m[warp], mnew = fmaxf(mold, mc);
+            float ls = 0.f;
+            for (int j = lane; j < len; j += 32) {
+                const float p = __expf(s_p[warp][j] - mnew);
+                s_p[warp][j] = p;
+                ls += p;
+            }
+            ls = warp_sum(ls);
+            if (lane == 0) {
+                const float corr = __expf(mold - mnew);  // 0 on the first chunk (mold = -inf)
+                s_corr[warp] = corr;
+                s_l[warp] = s_l[warp] * corr + ls;
+                s_m[warp] = mnew;
+            }
+        }
+        __syncthreads();
+        // p V
+#pragma unroll
+        for (int g = 0; g < kMaxG; ++g) acc[g] *= (g < G ? s_corr[g] : 0.f);
+        for (int j = kp; j < len; j += KPL) {
+            const float v = bf(vb[(size_t)(c0 + j) * d + e]);
+#pragma unroll
+            for (int g = 0; g < kMaxG; ++g)
+                if (g < G) acc[g] = fmaf(s_p[g][j], v, acc[g]);
+        }
     }
-    const uint16_t* grow = qkv + (size_t)t * ld + (size_t)(hq + h) * d;
-    for (int e = threadIdx.x; e < d; e += blockDim.x) {
-        float num = 0.f;
-        for (int w = 0; w < 8; ++w) num = fmaf(s_acc[w][e], f[w], num);
-        const float g = bf(grow[e]);
-        out[(size_t)t * hq * d + (size_t)h * d + e] = to_bf(num / den / (1.f + __expf(-g)));
+    // merge the key phases of the p V pass (lanes e, e + DPW, ...)
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) {
+#pragma unroll
+        for (int o = DPW; o < 32; o <<= 1) acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], o);
+        if (g < G && kp == 0) s_acc[g][e] = acc[g];
     }
+    cluster_sync_all();  // every CTA's partial is complete and visible to the cluster
+    if (rank == 0) {
+        for (int idx = threadIdx.x; idx < G * d; idx += blockDim.x) {
+            const int g = idx / d, ee = idx - g * d;
+            float mr[kSplit], mx = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < kSplit; ++r) {
+                mr[r] = ld_shared_cluster_f32(map_to_rank(smem_u32(&s_m[g]), r));
+                mx = fmaxf(mx, mr[r]);
+            }
+            float num = 0.f, den = 0.f;
+#pragma unroll
+            for (int r = 0; r < kSplit; ++r) {
+                const float f = mr[r] == -INFINITY ? 0.f : __expf(mr[r] - mx);
+                num = fmaf(f, ld_shared_cluster_f32(map_to_rank(smem_u32(&s_acc[g][ee]), r)), num);
+                den = fmaf(f, ld_shared_cluster_f32(map_to_rank(smem_u32(&s_l[g]), r)), den);
+            }
+            const int h = kvh * G + g;
+            const float gt = bf(qkv[(size_t)t * ld + (size_t)(hq + h) * d + ee]);
+            out[(size_t)t * hq * d + (size_t)h * d + ee] = to_bf(num / den / (1.f + __expf(-gt)));
+        }
+    }
+    cluster_sync_all();  // rank 0 is done reading the other CTAs' shared memory
 }
 
 inline unsigned grid_for(size_t n, int block) {
@@ -272,27 +419,40 @@ inline unsigned grid_for(size_t n, int block) {
     return (unsigned)(g < 4096 ? (g > 0 ? g : 1) : 4096);
 }
 
+inline cudaStream_t as_stream(dflash_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
 }  // namespace stack
 }  // namespace dflash
 
 using namespace dflash;
+using stack::as_stream;
 
 extern "C" int dflash_stack_add_rmsnorm(float* resid, const dflash_bf16* delta, const dflash_bf16* weight,
                                         dflash_bf16* out, int M, int H, float eps, dflash_stream_t stream) {
     if (!resid || !weight || !out || M < 1 || H < 1)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_add_rmsnorm: bad arguments");
-    stack::add_rmsnorm_kernel<<<M, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(resid, delta, weight, out, H,
-                                                                                         eps);
-    DFLASH_CUDA_TRY(cudaGetLastError());
+    const auto a8 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; };
+    const bool vec = H % 4 == 0 && H <= 8192 && aligned16(resid) && a8(weight) && a8(out) && (!delta || a8(delta));
+    const dim3 grid(M), block(256);
+    cudaStream_t s = as_stream(stream);
+    cudaError_t e;
+    if (!vec)
+        e = launch_chained(stack::add_rmsnorm_any_kernel, grid, block, 0, s, 1, resid, delta, weight, out, H, eps);
+    else if (H <= 2048)
+        e = launch_chained(stack::add_rmsnorm_kernel<2>, grid, block, 0, s, 1, resid, delta, weight, out, H, eps);
+    else if (H <= 4096)
+        e = launch_chained(stack::add_rmsnorm_kernel<4>, grid, block, 0, s, 1, resid, delta, weight, out, H, eps);
+    else
+        e = launch_chained(stack::add_rmsnorm_kernel<8>, grid, block, 0, s, 1, resid, delta, weight, out, H, eps);
+    DFLASH_CUDA_TRY(e);
     return DFLASH_OK;
 }
 
 extern "C" int dflash_stack_silu_mul(const dflash_bf16* gate_up, dflash_bf16* y, int M, int I, dflash_stream_t stream) {
     if (!gate_up || !y || M < 1 || I < 1) return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_silu_mul: bad arguments");
     const size_t n = (size_t)M * I;
-    stack::silu_mul_kernel<<<stack::grid_for(n, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(gate_up, y, M,
-                                                                                                       I);
-    DFLASH_CUDA_TRY(cudaGetLastError());
+    DFLASH_CUDA_TRY(launch_chained(stack::silu_mul_kernel, dim3(stack::grid_for(n, 256)), dim3(256), 0,
+                                   as_stream(stream), 1, gate_up, y, M, I));
     return DFLASH_OK;
 }
 
@@ -301,16 +461,20 @@ extern "C" int dflash_stack_conv_silu(const dflash_bf16* x, int ld, const dflash
     if (!x || !window || !weight || !y || M < 1 || C < 1 || ld < C || parts < 1 || C % parts)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_conv_silu: bad arguments");
     if (kc < 1 || kc > 8) return fail(DFLASH_ERR_UNSUPPORTED, "conv width %d not in 1..8", kc);
+    if (M > 16) return fail(DFLASH_ERR_UNSUPPORTED, "conv over M=%d tokens; at most 16", M);
     const dim3 grid((C + 127) / 128), block(128);
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaStream_t s = as_stream(stream);
+    cudaError_t e = cudaSuccess;
     switch (kc) {
-#define DFLASH_CONV_CASE(KC) \
-    case KC: stack::conv_silu_kernel<KC><<<grid, block, 0, s>>>(x, ld, window, weight, y, M, C, parts); break;
+#define DFLASH_CONV_CASE(KC)                                                                                        \
+    case KC:                                                                                                        \
+        e = launch_chained(stack::conv_silu_kernel<KC>, grid, block, 0, s, 1, x, ld, window, weight, y, M, C, parts); \
+        break;
         DFLASH_CONV_CASE(1) DFLASH_CONV_CASE(2) DFLASH_CONV_CASE(3) DFLASH_CONV_CASE(4)
         DFLASH_CONV_CASE(5) DFLASH_CONV_CASE(6) DFLASH_CONV_CASE(7) DFLASH_CONV_CASE(8)
 #undef DFLASH_CONV_CASE
     }
-    DFLASH_CUDA_TRY(cudaGetLastError());
+    DFLASH_CUDA_TRY(e);
     return DFLASH_OK;
 }
 
@@ -320,9 +484,8 @@ extern "C" int dflash_stack_gdn_gates(dflash_bf16* q, dflash_bf16* k, const dfla
     if (!q || !k || !ab || !a_log || !dt_bias || !alpha || !beta || M < 1 || heads < 1 || dk < 1)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_gdn_gates: bad arguments");
     const int warps = M * heads;
-    stack::gdn_gates_kernel<<<(warps + 7) / 8, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        q, k, ab, ld_ab, a_log, dt_bias, alpha, beta, M, heads, dk);
-    DFLASH_CUDA_TRY(cudaGetLastError());
+    DFLASH_CUDA_TRY(launch_chained(stack::gdn_gates_kernel, dim3((warps + 7) / 8), dim3(256), 0, as_stream(stream), 1,
+                                   q, k, ab, ld_ab, a_log, dt_bias, alpha, beta, M, heads, dk));
     return DFLASH_OK;
 }
 
@@ -331,9 +494,8 @@ extern "C" int dflash_stack_gated_norm(const dflash_bf16* o, const dflash_bf16* 
     if (!o || !z || !weight || !out || M < 1 || heads < 1 || dv < 1)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_gated_norm: bad arguments");
     const int warps = M * heads;
-    stack::gated_norm_kernel<<<(warps + 7) / 8, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(o, z, ld_z, weight,
-                                                                                                out, M, heads, dv, eps);
-    DFLASH_CUDA_TRY(cudaGetLastError());
+    DFLASH_CUDA_TRY(launch_chained(stack::gated_norm_kernel, dim3((warps + 7) / 8), dim3(256), 0, as_stream(stream), 1,
+                                   o, z, ld_z, weight, out, M, heads, dv, eps));
     return DFLASH_OK;
 }
 
@@ -344,16 +506,27 @@ extern "C" int dflash_stack_attn_prep(dflash_bf16* qkv, int ld, const dflash_bf1
         pos0 + M > max_len || ld < (2 * hq + 2 * hkv) * d)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_attn_prep: bad arguments");
     if ((d != 64 && d != 128 && d != 256) || rot < 0 || rot > d || rot % 64)
-        return fail(DFLASH_ERR_UNSUPPORTED, "head dim %d / rotary dims %d: need d in {64,128,256}, rot a multiple of 64", d, rot);
+        return fail(DFLASH_ERR_UNSUPPORTED, "head dim %d / rotary dims %d: need d in {64,128,256}, rot a multiple of 64",
+                    d, rot);
     const int warps = M * (hq + hkv);
     const dim3 grid((warps + 7) / 8), block(256);
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaStream_t s = as_stream(stream);
+    cudaError_t e;
     switch (d) {
-        case 64: stack::attn_prep_kernel<2><<<grid, block, 0, s>>>(qkv, ld, q_norm, k_norm, cache_k, cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta); break;
-        case 128: stack::attn_prep_kernel<4><<<grid, block, 0, s>>>(qkv, ld, q_norm, k_norm, cache_k, cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta); break;
-        default: stack::attn_prep_kernel<8><<<grid, block, 0, s>>>(qkv, ld, q_norm, k_norm, cache_k, cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta); break;
+        case 64:
+            e = launch_chained(stack::attn_prep_kernel<2>, grid, block, 0, s, 1, qkv, ld, q_norm, k_norm, cache_k,
+                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta);
+            break;
+        case 128:
+            e = launch_chained(stack::attn_prep_kernel<4>, grid, block, 0, s, 1, qkv, ld, q_norm, k_norm, cache_k,
+                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta);
+            break;
+        default:
+            e = launch_chained(stack::attn_prep_kernel<8>, grid, block, 0, s, 1, qkv, ld, q_norm, k_norm, cache_k,
+                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta);
+            break;
     }
-    DFLASH_CUDA_TRY(cudaGetLastError());
+    DFLASH_CUDA_TRY(e);
     return DFLASH_OK;
 }
 
@@ -364,13 +537,28 @@ extern "C" int dflash_stack_attn_decode(const dflash_bf16* qkv, int ld, const df
         pos0 + M > max_len || ld < (2 * hq + 2 * hkv) * d || M > 65535)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_attn_decode: bad arguments");
     if (d != 64 && d != 128 && d != 256) return fail(DFLASH_ERR_UNSUPPORTED, "head dim %d not in {64,128,256}", d);
-    const dim3 grid(hq, M), block(256);
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (hq / hkv > stack::kMaxG)
+        return fail(DFLASH_ERR_UNSUPPORTED, "%d q heads per kv head; at most %d", hq / hkv, stack::kMaxG);
+    if (!aligned16(cache_k) || !aligned16(cache_v) || !aligned16(qkv) || (ld * 2) % 16)
+        return fail(DFLASH_ERR_MISALIGNED, "dflash_stack_attn_decode: qkv, its row stride and the caches must be "
+                                           "16-byte aligned");
+    const dim3 grid(hkv * stack::kSplit, M), block(256);
+    cudaStream_t s = as_stream(stream);
+    cudaError_t e;
     switch (d) {
-        case 64: stack::attn_decode_kernel<2><<<grid, block, 0, s>>>(qkv, ld, cache_k, cache_v, out, hq, hkv, pos0, max_len, scale); break;
-        case 128: stack::attn_decode_kernel<4><<<grid, block, 0, s>>>(qkv, ld, cache_k, cache_v, out, hq, hkv, pos0, max_len, scale); break;
-        default: stack::attn_decode_kernel<8><<<grid, block, 0, s>>>(qkv, ld, cache_k, cache_v, out, hq, hkv, pos0, max_len, scale); break;
+        case 64:
+            e = launch_chained(stack::attn_decode_kernel<2>, grid, block, 0, s, stack::kSplit, qkv, ld, cache_k,
+                               cache_v, out, hq, hkv, pos0, max_len, scale);
+            break;
+        case 128:
+            e = launch_chained(stack::attn_decode_kernel<4>, grid, block, 0, s, stack::kSplit, qkv, ld, cache_k,
+                               cache_v, out, hq, hkv, pos0, max_len, scale);
+            break;
+        default:
+            e = launch_chained(stack::attn_decode_kernel<8>, grid, block, 0, s, stack::kSplit, qkv, ld, cache_k,
+                               cache_v, out, hq, hkv, pos0, max_len, scale);
+            break;
     }
-    DFLASH_CUDA_TRY(cudaGetLastError());
+    DFLASH_CUDA_TRY(e);
     return DFLASH_OK;
 }

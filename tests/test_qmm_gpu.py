@@ -126,6 +126,23 @@ def test_format_sweep_baseline_shapes(dc, O, cuda, M, bits, group, shape):
     assert O.closeness(y[:, rows], ref) <= TIGHT
 
 
+@pytest.mark.parametrize("M,N,K,group,bits", [
+    (8, 34816, 5120, 64, 4),   # clusters of one CTA (no exchange), two tiles per CTA
+    (8, 1024, 16384, 64, 4),   # clusters of eight CTAs
+    (12, 1024, 16384, 32, 8),  # eight CTAs, 8-bit, two MMA n-tiles
+    (3, 768, 24576, 128, 4),   # eight CTAs over three blocks: five ranks own no rows
+    (1, 256, 8192, 64, 8),     # eight CTAs, a single 16-row block
+    (8, 5120, 4096, 64, 4),    # clusters of four CTAs (the gated-delta out projection)
+    (16, 4352, 5120, 64, 4),   # four CTAs, a tensor-parallel gate/up shard
+])
+def test_cluster_sizes(dc, O, cuda, M, N, K, group, bits):
+    """Shapes for which the planner picks each cluster size (1, 2, 4, 8 CTAs splitting K)."""
+    x, wq, s, b = big_case(O, M, N, K, group, bits)
+    y = yf(run(dc, cuda, x, wq, s, b, group, bits))
+    rows = np.arange(0, N, 7)
+    assert O.closeness(y[:, rows], O.qmm_f64(x, wq[rows], s[rows], b[rows], group, bits)) <= TIGHT
+
+
 @pytest.mark.parametrize("M", list(range(1, 9)))
 def test_config2_gate_up_shape(dc, O, cuda, M):
     """K=5120, N=17408, 4-bit g64, M = 1..8."""
