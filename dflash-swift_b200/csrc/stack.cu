@@ -52,23 +52,30 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // resid[m] += delta[m] (if given); out[m] = bf16(resid[m] * rsqrt(mean(resid[m]^2) + eps) * w).
-// One CTA of 256 threads per row; each thread keeps VPT float4 of the row in registers
-// (H <= 1024 VPT, H a multiple of 4, delta / w / out 8-byte aligned).
+// A row is split over a cluster of kNormSplit CTAs of 128 threads (more loads in flight
+// than one CTA per row gives); each thread keeps up to VPT float4 of its part in
+// registers.  The parts' sums of squares are exchanged through distributed shared
+// memory and added in rank order, so every CTA uses the same scale.  Needs H a multiple
+// of 4 kNormSplit, H / kNormSplit <= 512 VPT, delta / w / out 8-byte aligned.
+constexpr int kNormSplit = 4;
+
 template <int VPT>
-__global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ resid, const uint16_t* __restrict__ delta,
+__global__ void __launch_bounds__(128) add_rmsnorm_kernel(float* __restrict__ resid, const uint16_t* __restrict__ delta,
                                                           const uint16_t* __restrict__ w, uint16_t* __restrict__ out,
                                                           int H, float eps) {
-    __shared__ float red[8];
+    __shared__ float red[4];
+    __shared__ float part;
     chain_in();
-    const int m = blockIdx.x, H4 = H >> 2;
-    float4* r4 = reinterpret_cast<float4*>(resid + (size_t)m * H);
-    const uint2* d4 = reinterpret_cast<const uint2*>(delta + (size_t)m * H);
+    const uint32_t rank = cluster_rank();
+    const int m = blockIdx.y, P4 = H / (4 * kNormSplit), base = (int)rank * P4;  // float4 units
+    float4* r4 = reinterpret_cast<float4*>(resid + (size_t)m * H) + base;
+    const uint2* d4 = reinterpret_cast<const uint2*>(delta + (size_t)m * H) + base;
     float4 v[VPT];
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
-        const int i = threadIdx.x + 256 * j;
-        if (i < H4) {
+        const int i = threadIdx.x + 128 * j;
+        if (i < P4) {
             v[j] = r4[i];
             if (delta) {
                 const uint2 d = d4[i];
@@ -81,18 +88,25 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ re
             ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
         }
     }
-    const float rs = rsqrtf(block_sum(ss, red) / H + eps);
-    const uint2* w4 = reinterpret_cast<const uint2*>(w);
-    uint2* o4 = reinterpret_cast<uint2*>(out + (size_t)m * H);
+    ss = block_sum(ss, red);
+    if (threadIdx.x == 0) part = ss;
+    cluster_sync_all();  // every part's sum is visible to the cluster
+    float tot = 0.f;
+#pragma unroll
+    for (int r = 0; r < kNormSplit; ++r) tot += ld_shared_cluster_f32(map_to_rank(smem_u32(&part), r));
+    const float rs = rsqrtf(tot / H + eps);
+    const uint2* w4 = reinterpret_cast<const uint2*>(w) + base;
+    uint2* o4 = reinterpret_cast<uint2*>(out + (size_t)m * H) + base;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
-        const int i = threadIdx.x + 256 * j;
-        if (i < H4) {
+        const int i = threadIdx.x + 128 * j;
+        if (i < P4) {
             const uint2 ww = w4[i];
             o4[i] = make_uint2(pack_bf2(v[j].x * rs * bf16_lo(ww.x), v[j].y * rs * bf16_hi(ww.x)),
                                pack_bf2(v[j].z * rs * bf16_lo(ww.y), v[j].w * rs * bf16_hi(ww.y)));
         }
     }
+    cluster_sync_all();  // the other CTAs are done reading `part`
 }
 
 // The same for any H and alignment (row re-read from global memory for the second pass).
@@ -272,29 +286,67 @@ __global__ void attn_prep_kernel(uint16_t* __restrict__ qkv, int ld, const uint1
 // Decode attention of the block.  A cluster of kSplit CTAs serves one (kv head, token t):
 // the keys 0 .. pos0 + t that token t sees are cut into kSplit contiguous ranges, one per
 // CTA, and each CTA runs an online softmax over its range for all G = hq / hkv q heads
-// that read this kv head, in chunks of kChunk keys:
-//   scores: warp w takes keys w, w + 8, ...; lane l holds dims [l CH, l CH + CH) of q (G
-//           heads, in registers) and of the key row, so a key row is one coalesced read;
-//   p V:    warp w owns dims [w d/8, (w+1) d/8); its lanes split those dims and the keys.
-// The CTAs' (max, sum, p V) partials are merged by cluster rank 0 through distributed
-// shared memory, which also applies the output gate:
+// that read this kv head, in chunks of kChunk keys.  Lane l holds dims [l CH, l CH + CH)
+// of every row it touches, so each key or value row is one coalesced read.
+//   scores: a warp takes KU = 32 / GP keys at a time (GP >= G, a power of two); every
+//           lane forms the KU x GP partial dot products over its dims and a butterfly
+//           reduce-scatter (16 + 8 + 4 + 2 + 1 exchanges) leaves lane u GP + g holding
+//           the full dot product of key u with head g;
+//   p V:    warp w takes keys w, w + 8, ... (kUnroll in flight); each lane accumulates its
+//           dims for the G heads; the 8 warps' partials are summed in a fixed order
+//           through shared memory.
+// The CTAs' (max, sum, p V) partials are merged through distributed shared memory, each
+// CTA of the cluster finishing a quarter of the outputs, with the output gate:
 //   out[t, h d + e] = softmax(q k^T scale) v * sigmoid(gate[t, h d + e]).
 constexpr int kSplit = 4;
 constexpr int kChunk = 256;
 constexpr int kMaxG = 8;
+constexpr int kUnroll = 4;
 
 template <int CH>
+__device__ __forceinline__ void load_row(const uint16_t* p, float (&v)[CH]) {
+    if constexpr (CH == 8) {
+        const uint4 u = *reinterpret_cast<const uint4*>(p);
+        v[0] = bf16_lo(u.x); v[1] = bf16_hi(u.x); v[2] = bf16_lo(u.y); v[3] = bf16_hi(u.y);
+        v[4] = bf16_lo(u.z); v[5] = bf16_hi(u.z); v[6] = bf16_lo(u.w); v[7] = bf16_hi(u.w);
+    } else if constexpr (CH == 4) {
+        const uint2 u = *reinterpret_cast<const uint2*>(p);
+        v[0] = bf16_lo(u.x); v[1] = bf16_hi(u.x); v[2] = bf16_lo(u.y); v[3] = bf16_hi(u.y);
+    } else {
+        const uint32_t u = *reinterpret_cast<const uint32_t*>(p);
+        v[0] = bf16_lo(u); v[1] = bf16_hi(u);
+    }
+}
+
+// Butterfly reduce-scatter of 32 values per lane: afterwards lane l holds the sum over
+// the warp of value l.
+__device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
+#pragma unroll
+    for (int lvl = 0; lvl < 5; ++lvl) {
+        const int m = 16 >> lvl, n = 32 >> lvl, h = n / 2;
+        const bool hi = (lane & m) != 0;
+#pragma unroll
+        for (int i = 0; i < h; ++i) {
+            const float send = hi ? v[i] : v[i + h];
+            const float keep = hi ? v[i + h] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+        }
+    }
+    return v[0];
+}
+
+template <int CH, int GP>
 __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __restrict__ qkv, int ld,
                                                           const uint16_t* __restrict__ cache_k,
                                                           const uint16_t* __restrict__ cache_v,
                                                           uint16_t* __restrict__ out, int hq, int hkv, int pos0,
                                                           int max_len, float scale) {
     constexpr int d = CH * 32;
-    constexpr int DPW = d / 8;     // dims per warp in the p V pass
-    constexpr int KPL = 32 / DPW;  // key phases per warp in the p V pass
+    constexpr int KU = 32 / GP;  // keys per warp step in the scores pass
+    static_assert(GP <= kMaxG && KU * CH <= 64, "score registers");
     __shared__ float s_p[kMaxG][kChunk];
-    __shared__ float s_acc[kMaxG][d];  // this CTA's p V partial (read by rank 0)
-    __shared__ float s_m[kMaxG], s_l[kMaxG], s_corr[kMaxG];
+    __shared__ __align__(16) float s_red[4][kMaxG][d];  // warp partials; s_red[0] ends as the CTA's p V
+    __shared__ float s_m[kMaxG], s_l[kMaxG], s_corr[kMaxG], s_f[kSplit][kMaxG], s_den[kMaxG];
     chain_in();
     const int G = hq / hkv;
     const int kvh = blockIdx.x / kSplit, t = blockIdx.y;
@@ -303,51 +355,52 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __rest
     const int n = pos0 + t + 1;
     const int k0 = (int)((long long)n * rank / kSplit), k1 = (int)((long long)n * (rank + 1) / kSplit);
 
-    float q[kMaxG][CH];
+    float q[GP][CH];
     const uint16_t* qrow = qkv + (size_t)t * ld + (size_t)kvh * G * d + lane * CH;
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g)
+    for (int g = 0; g < GP; ++g)
 #pragma unroll
         for (int c = 0; c < CH; ++c) q[g][c] = g < G ? bf(qrow[(size_t)g * d + c]) * scale : 0.f;
     if (threadIdx.x < kMaxG) {
         s_m[threadIdx.x] = -INFINITY;
         s_l[threadIdx.x] = 0.f;
     }
-    const uint16_t* kb = cache_k + (size_t)kvh * max_len * d;
-    const uint16_t* vb = cache_v + (size_t)kvh * max_len * d;
-    const int e = warp * DPW + lane % DPW, kp = lane / DPW;
-    float acc[kMaxG];
+    const uint16_t* kb = cache_k + (size_t)kvh * max_len * d + lane * CH;
+    const uint16_t* vb = cache_v + (size_t)kvh * max_len * d + lane * CH;
+    float acc[kMaxG][CH];
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g) acc[g] = 0.f;
+    for (int g = 0; g < kMaxG; ++g)
+#pragma unroll
+        for (int c = 0; c < CH; ++c) acc[g][c] = 0.f;
 
     for (int c0 = k0; c0 < k1; c0 += kChunk) {
         const int len = min(kChunk, k1 - c0);
         __syncthreads();  // s_p of the previous chunk is consumed; s_m / s_l initialised
-        // scores
-        for (int j = warp; j < len; j += 8) {
-            const uint16_t* kr = kb + (size_t)(c0 + j) * d + lane * CH;
-            float kv[CH];
-            if constexpr (CH == 8) {
-                const uint4 u = *reinterpret_cast<const uint4*>(kr);
-                kv[0] = bf16_lo(u.x); kv[1] = bf16_hi(u.x); kv[2] = bf16_lo(u.y); kv[3] = bf16_hi(u.y);
-                kv[4] = bf16_lo(u.z); kv[5] = bf16_hi(u.z); kv[6] = bf16_lo(u.w); kv[7] = bf16_hi(u.w);
-            } else if constexpr (CH == 4) {
-                const uint2 u = *reinterpret_cast<const uint2*>(kr);
-                kv[0] = bf16_lo(u.x); kv[1] = bf16_hi(u.x); kv[2] = bf16_lo(u.y); kv[3] = bf16_hi(u.y);
-            } else {
-                const uint32_t u = *reinterpret_cast<const uint32_t*>(kr);
-                kv[0] = bf16_lo(u); kv[1] = bf16_hi(u);
-            }
+        // scores: keys j0 + u, u < KU, for warp steps j0 = KU warp, KU (warp + 8), ...
+        for (int j0 = KU * warp; j0 < len; j0 += 8 * KU) {
+            float kv[KU][CH];
 #pragma unroll
-            for (int g = 0; g < kMaxG; ++g) {
-                if (g < G) {
-                    float sdot = 0.f;
+            for (int u = 0; u < KU; ++u) {
+                if (j0 + u < len) {
+                    load_row<CH>(kb + (size_t)(c0 + j0 + u) * d, kv[u]);
+                } else {
 #pragma unroll
-                    for (int c = 0; c < CH; ++c) sdot = fmaf(q[g][c], kv[c], sdot);
-                    sdot = warp_sum(sdot);
-                    if (lane == 0) s_p[g][j] = sdot;
+                    for (int c = 0; c < CH; ++c) kv[u][c] = 0.f;
                 }
             }
+            float v[32];
+#pragma unroll
+            for (int u = 0; u < KU; ++u)
+#pragma unroll
+                for (int g = 0; g < GP; ++g) {
+                    float sdot = 0.f;
+#pragma unroll
+                    for (int c = 0; c < CH; ++c) sdot = fmaf(q[g][c], kv[u][c], sdot);
+                    v[u * GP + g] = sdot;
+                }
+            const float dot = reduce_scatter32(v, lane);
+            const int u = lane / GP, g = lane % GP;
+            if (g < G && j0 + u < len) s_p[g][j0 + u] = dot;
         }
         __syncthreads();
         // softmax bookkeeping: warp g owns head g
@@ -374,44 +427,87 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __rest
         __syncthreads();
         // p V
 #pragma unroll
-        for (int g = 0; g < kMaxG; ++g) acc[g] *= (g < G ? s_corr[g] : 0.f);
-        for (int j = kp; j < len; j += KPL) {
-            const float v = bf(vb[(size_t)(c0 + j) * d + e]);
+        for (int g = 0; g < kMaxG; ++g) {
+            const float corr = g < G ? s_corr[g] : 0.f;
 #pragma unroll
-            for (int g = 0; g < kMaxG; ++g)
-                if (g < G) acc[g] = fmaf(s_p[g][j], v, acc[g]);
+            for (int c = 0; c < CH; ++c) acc[g][c] *= corr;
+        }
+        for (int j0 = warp; j0 < len; j0 += 8 * kUnroll) {
+            float vv[kUnroll][CH];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int j = j0 + 8 * u;
+                if (j < len) load_row<CH>(vb + (size_t)(c0 + j) * d, vv[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int j = j0 + 8 * u;
+                if (j < len) {
+#pragma unroll
+                    for (int g = 0; g < kMaxG; ++g) {
+                        if (g < G) {
+                            const float p = s_p[g][j];
+#pragma unroll
+                            for (int c = 0; c < CH; ++c) acc[g][c] = fmaf(p, vv[u][c], acc[g][c]);
+                        }
+                    }
+                }
+            }
         }
     }
-    // merge the key phases of the p V pass (lanes e, e + DPW, ...)
+    // the 8 warps' partials: warps 0-3 store, warps 4-7 add, then s_red[0] += s_red[1..3]
+    if (warp < 4) {
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g) {
+        for (int g = 0; g < kMaxG; ++g)
 #pragma unroll
-        for (int o = DPW; o < 32; o <<= 1) acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], o);
-        if (g < G && kp == 0) s_acc[g][e] = acc[g];
+            for (int c = 0; c < CH; ++c)
+                if (g < G) s_red[warp][g][lane * CH + c] = acc[g][c];
+    }
+    __syncthreads();
+    if (warp >= 4) {
+#pragma unroll
+        for (int g = 0; g < kMaxG; ++g)
+#pragma unroll
+            for (int c = 0; c < CH; ++c)
+                if (g < G) s_red[warp - 4][g][lane * CH + c] += acc[g][c];
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * d; idx += blockDim.x) {
+        const int g = idx / d, e = idx - g * d;
+        s_red[0][g][e] = ((s_red[0][g][e] + s_red[1][g][e]) + s_red[2][g][e]) + s_red[3][g][e];
     }
     cluster_sync_all();  // every CTA's partial is complete and visible to the cluster
-    if (rank == 0) {
-        for (int idx = threadIdx.x; idx < G * d; idx += blockDim.x) {
-            const int g = idx / d, ee = idx - g * d;
-            float mr[kSplit], mx = -INFINITY;
+    // merge weights per head: f_r = exp(m_r - max), den = sum_r f_r l_r
+    if (threadIdx.x < G) {
+        const int g = threadIdx.x;
+        float mr[kSplit], mx = -INFINITY;
 #pragma unroll
-            for (int r = 0; r < kSplit; ++r) {
-                mr[r] = ld_shared_cluster_f32(map_to_rank(smem_u32(&s_m[g]), r));
-                mx = fmaxf(mx, mr[r]);
-            }
-            float num = 0.f, den = 0.f;
-#pragma unroll
-            for (int r = 0; r < kSplit; ++r) {
-                const float f = mr[r] == -INFINITY ? 0.f : __expf(mr[r] - mx);
-                num = fmaf(f, ld_shared_cluster_f32(map_to_rank(smem_u32(&s_acc[g][ee]), r)), num);
-                den = fmaf(f, ld_shared_cluster_f32(map_to_rank(smem_u32(&s_l[g]), r)), den);
-            }
-            const int h = kvh * G + g;
-            const float gt = bf(qkv[(size_t)t * ld + (size_t)(hq + h) * d + ee]);
-            out[(size_t)t * hq * d + (size_t)h * d + ee] = to_bf(num / den / (1.f + __expf(-gt)));
+        for (int r = 0; r < kSplit; ++r) {
+            mr[r] = ld_shared_cluster_f32(map_to_rank(smem_u32(&s_m[g]), r));
+            mx = fmaxf(mx, mr[r]);
         }
+        float den = 0.f;
+#pragma unroll
+        for (int r = 0; r < kSplit; ++r) {
+            const float f = mr[r] == -INFINITY ? 0.f : __expf(mr[r] - mx);
+            s_f[r][g] = f;
+            den = fmaf(f, ld_shared_cluster_f32(map_to_rank(smem_u32(&s_l[g]), r)), den);
+        }
+        s_den[g] = den;
     }
-    cluster_sync_all();  // rank 0 is done reading the other CTAs' shared memory
+    __syncthreads();
+    // this CTA finishes outputs [rank, rank + kSplit, ...) of the G d
+    for (int idx = (int)rank + kSplit * threadIdx.x; idx < G * d; idx += kSplit * blockDim.x) {
+        const int g = idx / d, ee = idx - g * d;
+        float num = 0.f;
+#pragma unroll
+        for (int r = 0; r < kSplit; ++r)
+            num = fmaf(s_f[r][g], ld_shared_cluster_f32(map_to_rank(smem_u32(&s_red[0][g][ee]), r)), num);
+        const int h = kvh * G + g;
+        const float gt = bf(qkv[(size_t)t * ld + (size_t)(hq + h) * d + ee]);
+        out[(size_t)t * hq * d + (size_t)h * d + ee] = to_bf(num / s_den[g] / (1.f + __expf(-gt)));
+    }
+    cluster_sync_all();  // every CTA is done reading the others' shared memory
 }
 
 inline unsigned grid_for(size_t n, int block) {
@@ -429,21 +525,27 @@ using stack::as_stream;
 
 extern "C" int dflash_stack_add_rmsnorm(float* resid, const dflash_bf16* delta, const dflash_bf16* weight,
                                         dflash_bf16* out, int M, int H, float eps, dflash_stream_t stream) {
-    if (!resid || !weight || !out || M < 1 || H < 1)
+    if (!resid || !weight || !out || M < 1 || H < 1 || M > 65535)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_add_rmsnorm: bad arguments");
     const auto a8 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; };
-    const bool vec = H % 4 == 0 && H <= 8192 && aligned16(resid) && a8(weight) && a8(out) && (!delta || a8(delta));
-    const dim3 grid(M), block(256);
+    const int part4 = H / (4 * stack::kNormSplit);
+    const bool vec = H % (4 * stack::kNormSplit) == 0 && part4 <= 128 * 8 && aligned16(resid) && a8(weight) &&
+                     a8(out) && (!delta || a8(delta));
     cudaStream_t s = as_stream(stream);
     cudaError_t e;
+    const dim3 grid(stack::kNormSplit, M), block(128);
     if (!vec)
-        e = launch_chained(stack::add_rmsnorm_any_kernel, grid, block, 0, s, 1, resid, delta, weight, out, H, eps);
-    else if (H <= 2048)
-        e = launch_chained(stack::add_rmsnorm_kernel<2>, grid, block, 0, s, 1, resid, delta, weight, out, H, eps);
-    else if (H <= 4096)
-        e = launch_chained(stack::add_rmsnorm_kernel<4>, grid, block, 0, s, 1, resid, delta, weight, out, H, eps);
+        e = launch_chained(stack::add_rmsnorm_any_kernel, dim3(M), dim3(256), 0, s, 1, resid, delta, weight, out, H,
+                           eps);
+    else if (part4 <= 128 * 2)
+        e = launch_chained(stack::add_rmsnorm_kernel<2>, grid, block, 0, s, stack::kNormSplit, resid, delta, weight,
+                           out, H, eps);
+    else if (part4 <= 128 * 4)
+        e = launch_chained(stack::add_rmsnorm_kernel<4>, grid, block, 0, s, stack::kNormSplit, resid, delta, weight,
+                           out, H, eps);
     else
-        e = launch_chained(stack::add_rmsnorm_kernel<8>, grid, block, 0, s, 1, resid, delta, weight, out, H, eps);
+        e = launch_chained(stack::add_rmsnorm_kernel<8>, grid, block, 0, s, stack::kNormSplit, resid, delta, weight,
+                           out, H, eps);
     DFLASH_CUDA_TRY(e);
     return DFLASH_OK;
 }
@@ -544,21 +646,19 @@ extern "C" int dflash_stack_attn_decode(const dflash_bf16* qkv, int ld, const df
                                            "16-byte aligned");
     const dim3 grid(hkv * stack::kSplit, M), block(256);
     cudaStream_t s = as_stream(stream);
-    cudaError_t e;
-    switch (d) {
-        case 64:
-            e = launch_chained(stack::attn_decode_kernel<2>, grid, block, 0, s, stack::kSplit, qkv, ld, cache_k,
-                               cache_v, out, hq, hkv, pos0, max_len, scale);
-            break;
-        case 128:
-            e = launch_chained(stack::attn_decode_kernel<4>, grid, block, 0, s, stack::kSplit, qkv, ld, cache_k,
-                               cache_v, out, hq, hkv, pos0, max_len, scale);
-            break;
-        default:
-            e = launch_chained(stack::attn_decode_kernel<8>, grid, block, 0, s, stack::kSplit, qkv, ld, cache_k,
-                               cache_v, out, hq, hkv, pos0, max_len, scale);
-            break;
-    }
+    const int G = hq / hkv;
+    const int gmin = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;  // heads padded to a power of two
+    const int ch = d / 32;
+    const int gp = gmin > ch / 2 ? gmin : ch / 2;                 // keeps the score registers bounded
+    cudaError_t e = cudaErrorInvalidValue;
+#define DFLASH_ATTN_CASE(CH, GP)                                                                                   \
+    if (ch == CH && gp == GP)                                                                                      \
+        e = launch_chained(stack::attn_decode_kernel<CH, GP>, grid, block, 0, s, stack::kSplit, qkv, ld, cache_k,    \
+                           cache_v, out, hq, hkv, pos0, max_len, scale);
+    DFLASH_ATTN_CASE(2, 1) DFLASH_ATTN_CASE(2, 2) DFLASH_ATTN_CASE(2, 4) DFLASH_ATTN_CASE(2, 8)
+    DFLASH_ATTN_CASE(4, 2) DFLASH_ATTN_CASE(4, 4) DFLASH_ATTN_CASE(4, 8)
+    DFLASH_ATTN_CASE(8, 4) DFLASH_ATTN_CASE(8, 8)
+#undef DFLASH_ATTN_CASE
     DFLASH_CUDA_TRY(e);
     return DFLASH_OK;
 }
