@@ -3,4 +3,5 @@
 #include "abi.cu"
 #include "qmm.cu"
 #include "gdn.cu"
+#include "tp.cu"
 #include "stack.cu"

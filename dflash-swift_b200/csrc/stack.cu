@@ -109,6 +109,66 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(float* __restrict__ re
     cluster_sync_all();  // the other CTAs are done reading `part`
 }
 
+// add_rmsnorm whose delta is the tensor-parallel sum of the ranks' partials, read from
+// this rank's exchange buffer (set `set`, filled by dflash_tp_push on every rank): after a
+// bounded wait for every source's flag, delta = bf16(sum of the slots in rank order).
+template <int VPT>
+__global__ void __launch_bounds__(128) add_rmsnorm_reduce_kernel(float* __restrict__ resid, const void* xbase,
+                                                                 int world, int set, const uint16_t* __restrict__ w,
+                                                                 uint16_t* __restrict__ out, int M, int H, float eps) {
+    __shared__ float red[4];
+    __shared__ float part;
+    chain_in();
+    const tp::Header* hdr = static_cast<const tp::Header*>(xbase);
+    tp::wait_flags(hdr, world, set, hdr->seq[set] * (uint32_t)tp::kPushBlocks);
+    const uint32_t rank = cluster_rank();
+    const int m = blockIdx.y, P4 = H / (4 * kNormSplit), base = (int)rank * P4;  // float4 units
+    float4* r4 = reinterpret_cast<float4*>(resid + (size_t)m * H) + base;
+    float4 v[VPT];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+        const int i = threadIdx.x + 128 * j;
+        if (i < P4) {
+            float sx = 0.f, sy = 0.f, sz = 0.f, sw = 0.f;
+            for (int r = 0; r < world; ++r) {
+                const uint2 d = reinterpret_cast<const uint2*>(
+                    tp::slot_ptr(const_cast<void*>(xbase), world, M, H, set, r) + (size_t)m * H)[base + i];
+                sx += bf16_lo(d.x);
+                sy += bf16_hi(d.x);
+                sz += bf16_lo(d.y);
+                sw += bf16_hi(d.y);
+            }
+            v[j] = r4[i];
+            v[j].x += bf_round(sx);
+            v[j].y += bf_round(sy);
+            v[j].z += bf_round(sz);
+            v[j].w += bf_round(sw);
+            r4[i] = v[j];
+            ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
+        }
+    }
+    ss = block_sum(ss, red);
+    if (threadIdx.x == 0) part = ss;
+    cluster_sync_all();
+    float tot = 0.f;
+#pragma unroll
+    for (int r = 0; r < kNormSplit; ++r) tot += ld_shared_cluster_f32(map_to_rank(smem_u32(&part), r));
+    const float rs = rsqrtf(tot / H + eps);
+    const uint2* w4 = reinterpret_cast<const uint2*>(w) + base;
+    uint2* o4 = reinterpret_cast<uint2*>(out + (size_t)m * H) + base;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+        const int i = threadIdx.x + 128 * j;
+        if (i < P4) {
+            const uint2 ww = w4[i];
+            o4[i] = make_uint2(pack_bf2(v[j].x * rs * bf16_lo(ww.x), v[j].y * rs * bf16_hi(ww.x)),
+                               pack_bf2(v[j].z * rs * bf16_lo(ww.y), v[j].w * rs * bf16_hi(ww.y)));
+        }
+    }
+    cluster_sync_all();
+}
+
 // The same for any H and alignment (row re-read from global memory for the second pass).
 __global__ void __launch_bounds__(256) add_rmsnorm_any_kernel(float* __restrict__ resid,
                                                               const uint16_t* __restrict__ delta,
@@ -546,6 +606,34 @@ extern "C" int dflash_stack_add_rmsnorm(float* resid, const dflash_bf16* delta, 
     else
         e = launch_chained(stack::add_rmsnorm_kernel<8>, grid, block, 0, s, stack::kNormSplit, resid, delta, weight,
                            out, H, eps);
+    DFLASH_CUDA_TRY(e);
+    return DFLASH_OK;
+}
+
+extern "C" int dflash_stack_add_rmsnorm_reduce(float* resid, const void* exchange, int world, int set,
+                                               const dflash_bf16* weight, dflash_bf16* out, int M, int H, float eps,
+                                               dflash_stream_t stream) {
+    if (!resid || !exchange || !weight || !out || M < 1 || H < 1 || M > 65535 || world < 1 ||
+        world > tp::kMaxRanks || (set != 0 && set != 1))
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_add_rmsnorm_reduce: bad arguments");
+    const auto a8 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; };
+    const int part4 = H / (4 * stack::kNormSplit);
+    if (H % (4 * stack::kNormSplit) || part4 > 128 * 8 || !aligned16(resid) || !a8(weight) || !a8(out) ||
+        !aligned16(exchange))
+        return fail(DFLASH_ERR_UNSUPPORTED, "dflash_stack_add_rmsnorm_reduce: H=%d (a multiple of %d up to %d) and "
+                    "aligned buffers needed", H, 4 * stack::kNormSplit, 4 * stack::kNormSplit * 128 * 8);
+    cudaStream_t s = as_stream(stream);
+    const dim3 grid(stack::kNormSplit, M), block(128);
+    cudaError_t e;
+    if (part4 <= 128 * 2)
+        e = launch_chained(stack::add_rmsnorm_reduce_kernel<2>, grid, block, 0, s, stack::kNormSplit, resid, exchange,
+                           world, set, weight, out, M, H, eps);
+    else if (part4 <= 128 * 4)
+        e = launch_chained(stack::add_rmsnorm_reduce_kernel<4>, grid, block, 0, s, stack::kNormSplit, resid, exchange,
+                           world, set, weight, out, M, H, eps);
+    else
+        e = launch_chained(stack::add_rmsnorm_reduce_kernel<8>, grid, block, 0, s, stack::kNormSplit, resid, exchange,
+                           world, set, weight, out, M, H, eps);
     DFLASH_CUDA_TRY(e);
     return DFLASH_OK;
 }

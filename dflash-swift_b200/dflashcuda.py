@@ -49,6 +49,9 @@ EXPORTED = (
     # include/dflash_stack.h: glue of the tensor-parallel verify stack
     "dflash_stack_add_rmsnorm", "dflash_stack_silu_mul", "dflash_stack_conv_silu", "dflash_stack_gdn_gates",
     "dflash_stack_gated_norm", "dflash_stack_attn_prep", "dflash_stack_attn_decode",
+    "dflash_stack_add_rmsnorm_reduce", "dflash_tp_exchange_bytes", "dflash_tp_exchange_alloc",
+    "dflash_tp_exchange_free", "dflash_ipc_get_handle", "dflash_ipc_open_handle", "dflash_ipc_close_handle",
+    "dflash_tp_push",
 )
 
 
@@ -92,6 +95,14 @@ def _load() -> ctypes.CDLL:
         "dflash_stack_gated_norm": ([_vp, _vp, _i, _vp, _vp, _i, _i, _i, _f, _vp], _i),
         "dflash_stack_attn_prep": ([_vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _f, _vp], _i),
         "dflash_stack_attn_decode": ([_vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp], _i),
+        "dflash_stack_add_rmsnorm_reduce": ([_vp, _vp, _i, _i, _vp, _vp, _i, _i, _f, _vp], _i),
+        "dflash_tp_exchange_bytes": ([_i, _i, _i], _sz),
+        "dflash_tp_exchange_alloc": ([_sz, ctypes.POINTER(_vp)], _i),
+        "dflash_tp_exchange_free": ([_vp], _i),
+        "dflash_ipc_get_handle": ([_vp, _vp], _i),
+        "dflash_ipc_open_handle": ([_vp, ctypes.POINTER(_vp)], _i),
+        "dflash_ipc_close_handle": ([_vp], _i),
+        "dflash_tp_push": ([_vp, ctypes.POINTER(_vp), _i, _i, _i, _i, _i, _vp], _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -439,4 +450,63 @@ def stack_attn_decode(qkv, cache_k, cache_v, out, hq: int, hkv: int, pos0: int, 
     _, max_len, d = cache_k.shape
     check(lib.dflash_stack_attn_decode(_ptr(qkv), qkv.stride(0), _ptr(cache_k), _ptr(cache_v), _ptr(out), M, hq,
                                        hkv, d, pos0, max_len, float(scale), _stream(stream)))
+    return out
+
+
+# ----------------------------------------------------------------------------- tensor-parallel exchange
+
+IPC_HANDLE_BYTES = 64
+
+
+class PeerExchange:
+    """This rank's exchange buffer for the peer all-reduce (include/dflash_stack.h), mapped
+    into every rank of the node.  `handles` come from ``handle()`` on every rank (the
+    host exchanges them, e.g. with torch.distributed.all_gather_object)."""
+
+    def __init__(self, world: int, M: int, H: int):
+        self.world, self.M, self.H = world, M, H
+        self.nbytes = int(lib.dflash_tp_exchange_bytes(world, M, H))
+        if self.nbytes == 0:
+            raise DFlashError(DFLASH_ERR_INVALID_ARGUMENT, f"exchange of world {world}, [{M}, {H}] not supported")
+        ptr = ctypes.c_void_p()
+        check(lib.dflash_tp_exchange_alloc(self.nbytes, ctypes.byref(ptr)))
+        self.ptr = ptr.value
+        self.bases = None
+        self._opened = []
+
+    def handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        check(lib.dflash_ipc_get_handle(self.ptr, buf))
+        return buf.raw
+
+    def connect(self, rank: int, handles) -> None:
+        bases = []
+        for r, h in enumerate(handles):
+            if r == rank:
+                bases.append(self.ptr)
+                continue
+            p = ctypes.c_void_p()
+            check(lib.dflash_ipc_open_handle(ctypes.create_string_buffer(bytes(h), IPC_HANDLE_BYTES), ctypes.byref(p)))
+            self._opened.append(p.value)
+            bases.append(p.value)
+        self.rank = rank
+        self.bases = (ctypes.c_void_p * len(bases))(*bases)
+
+    def push(self, part, set_: int, stream=None) -> None:
+        M, H = part.shape
+        check(lib.dflash_tp_push(_ptr(part), self.bases, self.rank, self.world, M, H, set_, _stream(stream)))
+
+    def close(self) -> None:
+        for p in self._opened:
+            lib.dflash_ipc_close_handle(p)
+        self._opened = []
+        if self.ptr:
+            lib.dflash_tp_exchange_free(self.ptr)
+            self.ptr = None
+
+
+def stack_add_rmsnorm_reduce(resid, exchange: PeerExchange, set_: int, weight, out, eps: float, stream=None):
+    M, H = resid.shape
+    check(lib.dflash_stack_add_rmsnorm_reduce(_ptr(resid), exchange.ptr, exchange.world, set_, _ptr(weight), _ptr(out),
+                                              M, H, float(eps), _stream(stream)))
     return out

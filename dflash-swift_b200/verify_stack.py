@@ -17,7 +17,10 @@ So a layer has exactly two collectives (after the mixer and after the MLP), 128 
 forward.  The residual stream is fp32 and replicated; everything between the shard
 boundaries is rank-local.  The projections run on dflash_qmm, the recurrence on
 dflash_gdn_step (its inputs are the rollback capture) and the glue on the dflash_stack_*
-kernels; the all-reduce is NCCL through torch.distributed.  The whole forward is
+kernels.  The all-reduce runs over peer memory: each rank's partial is stored into every
+rank's exchange buffer over NVLink (dflash_tp_push) and the next RMSNorm sums the slots
+after a bounded flag wait (dflash_stack_add_rmsnorm_reduce); NCCL through
+torch.distributed is the alternative (`allreduce="nccl"`).  The whole forward is
 captured once as a CUDA graph and replayed.
 
 Weights are seeded synthetic MLX-packed 4-bit tensors (no checkpoint is available):
@@ -311,7 +314,7 @@ class VerifyStack:
     bf16 [M, hidden] (identical on every rank)."""
 
     def __init__(self, cfg: StackConfig, rank: int = 0, world: int = 1, seed: int = 0, device=None,
-                 group=None, weights: Optional[dict] = None, state: Optional[dict] = None):
+                 group=None, weights: Optional[dict] = None, state: Optional[dict] = None, allreduce: str = "peer"):
         import dflashcuda as dc
         self.dc = dc
         self.cfg = cfg
@@ -325,6 +328,33 @@ class VerifyStack:
         self.state = state if state is not None else build_rank_state(cfg, self.plan, seed, self.device)
         self._alloc()
         self.graph = None
+        if allreduce not in ("peer", "nccl"):
+            raise ValueError("allreduce is 'peer' (NVLink stores into the peers' exchange buffers) or 'nccl'")
+        self.allreduce = allreduce if world > 1 else "none"
+        self.exchange = None
+        self._set = 0
+        if self.allreduce == "peer":
+            self._connect_exchange(rank)
+
+    def _connect_exchange(self, rank):
+        """Allocate this rank's exchange buffer, swap IPC handles with the other ranks and
+        map theirs; the barrier ensures every buffer is zeroed before anyone pushes."""
+        ex = self.dc.PeerExchange(self.world, self.cfg.block, self.cfg.hidden)
+        handles = [None] * self.world
+        torch.distributed.all_gather_object(handles, ex.handle(), group=self.pg)
+        ex.connect(rank, handles)
+        torch.cuda.synchronize(self.device)
+        torch.distributed.barrier(group=self.pg)
+        self.exchange = ex
+
+    def close(self):
+        """Unmap the peers' exchange buffers and free this rank's (after a barrier, so no
+        peer still pushes into it)."""
+        if self.exchange is not None:
+            torch.cuda.synchronize(self.device)
+            torch.distributed.barrier(group=self.pg)
+            self.exchange.close()
+            self.exchange = None
 
     def _alloc(self):
         cfg, p, dev = self.cfg, self.plan, self.device
@@ -361,9 +391,23 @@ class VerifyStack:
     def _qmm(self, x, q: Quant, out):
         self.dc.qmm(x, q.w, q.scales, q.biases, q.group, q.bits, out=out, workspace=self.ws)
 
-    def _all_reduce(self, t):
-        if self.world > 1:
-            torch.distributed.all_reduce(t, group=self.pg)
+    def _reduce(self, part):
+        """Start the all-reduce of this rank's partial; returns what the next norm adds."""
+        if self.allreduce == "peer":
+            self.exchange.push(part, self._set)
+            pending = ("exchange", self._set)
+            self._set ^= 1
+            return pending
+        if self.allreduce == "nccl":
+            torch.distributed.all_reduce(part, group=self.pg)
+        return part
+
+    def _norm(self, pending, weight, out):
+        """resid += the pending delta (a local tensor or the peer exchange); out = RMSNorm(resid)."""
+        if isinstance(pending, tuple):
+            self.dc.stack_add_rmsnorm_reduce(self.resid, self.exchange, pending[1], weight, out, self.cfg.eps)
+        else:
+            self.dc.stack_add_rmsnorm(self.resid, pending, weight, out, self.cfg.eps)
 
     def _gdn(self, L, S, gi):
         cfg, p, dc = self.cfg, self.plan, self.dc
@@ -398,21 +442,20 @@ class VerifyStack:
     def _forward_body(self, hidden):
         cfg, dc = self.cfg, self.dc
         self.resid.zero_()
-        delta = hidden
+        pending = hidden
         gi = 0
         for L, S in zip(self.w["layers"], self.state["layers"]):
-            dc.stack_add_rmsnorm(self.resid, delta, L["ln"], self.normed, cfg.eps)
+            self._norm(pending, L["ln"], self.normed)
             if L["kind"] == "gdn":
                 self._gdn(L, S, gi)
                 gi += 1
             else:
                 self._attn(L, S)
-            self._all_reduce(self.delta)
-            dc.stack_add_rmsnorm(self.resid, self.delta, L["post_ln"], self.normed, cfg.eps)
+            pending = self._reduce(self.delta)
+            self._norm(pending, L["post_ln"], self.normed)
             self._mlp(L)
-            self._all_reduce(self.delta)
-            delta = self.delta
-        dc.stack_add_rmsnorm(self.resid, delta, self.w["final_norm"], self.out, cfg.eps)
+            pending = self._reduce(self.delta)
+        self._norm(pending, self.w["final_norm"], self.out)
         return self.out
 
     def forward(self, hidden):
@@ -438,6 +481,8 @@ class VerifyStack:
             else:
                 n += 2 + 1 + 1 + 2  # qkv, prep, decode, o_proj
             n += 2 + 1 + 2  # gate_up, silu_mul, down
+            if self.allreduce == "peer":
+                n += 2  # the pushes (the sums are inside the norms)
         return n
 
 
@@ -456,6 +501,9 @@ def main(argv=None) -> int:
     ap.add_argument("--tiny", action="store_true", help="the small parity-test stack instead of config 4")
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--context", type=int, default=None)
+    ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
+                    help="peer: NVLink stores into the other ranks' exchange buffers, summed by the next "
+                         "RMSNorm; nccl: torch.distributed.all_reduce")
     args = ap.parse_args(argv)
 
     sys.path.insert(0, str(HERE))
@@ -473,7 +521,7 @@ def main(argv=None) -> int:
     if args.context is not None:
         cfg = replace(cfg, context=args.context)
 
-    stack = VerifyStack(cfg, rank, world, seed=args.seed, device=dev, group=pg)
+    stack = VerifyStack(cfg, rank, world, seed=args.seed, device=dev, group=pg, allreduce=args.allreduce)
     hidden = make_block(cfg, args.seed, dev)
     g = stack.capture(hidden)
     for _ in range(args.warmup):
@@ -501,11 +549,13 @@ def main(argv=None) -> int:
             "tp": world, "steps": args.steps, "warmup": args.warmup,
             "weight_bytes_per_gpu": wbytes, "weight_gbs_per_gpu": round(wbytes / (ms / 1000.0) / 1e9, 1),
             "kernels_per_forward": stack.kernels_per_forward(), "all_reduces_per_forward": 2 * cfg.layers,
+            "allreduce": stack.allreduce,
             "config": {k: v for k, v in asdict(cfg).items()}, "out_abs_sum": checksum,
         }), flush=True)
     del g
     stack.graph = None
     if world > 1:
+        stack.close()
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
     return 0

@@ -47,7 +47,7 @@ def gloo_reference_rank(rank: int, world: int, port: int, out_path: str, cfg_kw:
         dist.destroy_process_group()
 
 
-def nccl_stack_rank(rank: int, world: int, port: int, out_path: str, cfg_kw: dict):
+def nccl_stack_rank(rank: int, world: int, port: int, out_path: str, cfg_kw: dict, allreduce: str = "peer"):
     import torch
     import verify_stack as vs
     torch.cuda.set_device(rank)
@@ -55,7 +55,7 @@ def nccl_stack_rank(rank: int, world: int, port: int, out_path: str, cfg_kw: dic
     dist = _init("nccl", rank, world, port, device=dev)
     try:
         cfg = vs.StackConfig(**cfg_kw)
-        stack = vs.VerifyStack(cfg, rank, world, seed=0, device=dev, group=dist.group.WORLD)
+        stack = vs.VerifyStack(cfg, rank, world, seed=0, device=dev, group=dist.group.WORLD, allreduce=allreduce)
         hidden = vs.make_block(cfg, 0, dev)
         eager = stack.forward(hidden).clone()
         g = stack.capture(hidden)
@@ -64,8 +64,11 @@ def nccl_stack_rank(rank: int, world: int, port: int, out_path: str, cfg_kw: dic
         graphed = stack.out.clone()
         del g
         stack.graph = None
+        import dflashcuda
+        dev_err = dflashcuda.device_error()
+        stack.close()
         if rank == 0:
-            torch.save({"eager": eager.cpu(), "graphed": graphed.cpu()}, out_path)
+            torch.save({"eager": eager.cpu(), "graphed": graphed.cpu(), "device_error": dev_err}, out_path)
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -235,7 +235,10 @@ def test_cuda_stack_config4_shapes_run(cuda):
 
 
 @pytest.mark.gpu
-def test_cuda_stack_tp2_nccl_matches_tp1_reference(cuda, tmp_path):
+def test_cuda_stack_tp2_matches_tp1_reference(cuda, tmp_path):
+    """TP=2 on two GPUs, all-reduce over peer memory and through NCCL: both match the TP=1
+    reference, agree bit for bit with each other (a two-term bf16 sum rounds once either
+    way), and graph replay equals eager."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import stack_ref
@@ -245,10 +248,14 @@ def test_cuda_stack_tp2_nccl_matches_tp1_reference(cuda, tmp_path):
     w = vs.build_rank_weights(cfg, plan, 0, cuda)
     st = vs.build_rank_state(cfg, plan, 0, cuda)
     ref = stack_ref.forward(cfg, plan, w, st, vs.make_block(cfg, 0, cuda))["out"].numpy()
-    out = tmp_path / "tp2_nccl.pt"
-    port = free_port()
-    codes = _run_ranks(stack_workers.nccl_stack_rank, 2, lambda r: (r, 2, port, str(out), asdict(cfg)))
-    assert codes == [0, 0], codes
-    res = torch.load(out)
-    assert torch.equal(res["eager"], res["graphed"])
-    assert closeness(res["eager"].float().numpy(), ref) <= 3e-2
+    res = {}
+    for mode in ("peer", "nccl"):
+        out = tmp_path / f"tp2_{mode}.pt"
+        port = free_port()
+        codes = _run_ranks(stack_workers.nccl_stack_rank, 2, lambda r: (r, 2, port, str(out), asdict(cfg), mode))
+        assert codes == [0, 0], (mode, codes)
+        res[mode] = torch.load(out)
+        assert res[mode]["device_error"] == 0
+        assert torch.equal(res[mode]["eager"], res[mode]["graphed"])
+        assert closeness(res[mode]["eager"].float().numpy(), ref) <= 3e-2
+    assert torch.equal(res["peer"]["eager"], res["nccl"]["eager"])
