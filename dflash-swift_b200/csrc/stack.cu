@@ -110,17 +110,18 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(float* __restrict__ re
 }
 
 // add_rmsnorm whose delta is the tensor-parallel sum of the ranks' partials, read from
-// this rank's exchange buffer (set `set`, filled by dflash_tp_push on every rank): after a
-// bounded wait for every source's flag, delta = bf16(sum of the slots in rank order).
+// this rank's exchange buffer (set `set`, filled by dflash_tp_push on every rank): each
+// data word is taken once it carries this exchange's epoch (bounded wait), and
+// delta = bf16(sum of the slots in rank order).
 template <int VPT>
-__global__ void __launch_bounds__(128) add_rmsnorm_reduce_kernel(float* __restrict__ resid, const void* xbase,
-                                                                 int world, int set, const uint16_t* __restrict__ w,
+__global__ void __launch_bounds__(128) add_rmsnorm_reduce_kernel(float* __restrict__ resid, void* xbase, int world,
+                                                                 int set, const uint16_t* __restrict__ w,
                                                                  uint16_t* __restrict__ out, int M, int H, float eps) {
     __shared__ float red[4];
     __shared__ float part;
     chain_in();
-    const tp::Header* hdr = static_cast<const tp::Header*>(xbase);
-    tp::wait_flags(hdr, world, set, hdr->seq[set] * (uint32_t)tp::kPushBlocks);
+    tp::Header* hdr = static_cast<tp::Header*>(xbase);
+    const uint32_t e = hdr->next[set];
     const uint32_t rank = cluster_rank();
     const int m = blockIdx.y, P4 = H / (4 * kNormSplit), base = (int)rank * P4;  // float4 units
     float4* r4 = reinterpret_cast<float4*>(resid + (size_t)m * H) + base;
@@ -131,13 +132,14 @@ __global__ void __launch_bounds__(128) add_rmsnorm_reduce_kernel(float* __restri
         const int i = threadIdx.x + 128 * j;
         if (i < P4) {
             float sx = 0.f, sy = 0.f, sz = 0.f, sw = 0.f;
+            const size_t word = ((size_t)m * H + 4 * (size_t)(base + i)) / 2;  // two data words per float4
             for (int r = 0; r < world; ++r) {
-                const uint2 d = reinterpret_cast<const uint2*>(
-                    tp::slot_ptr(const_cast<void*>(xbase), world, M, H, set, r) + (size_t)m * H)[base + i];
-                sx += bf16_lo(d.x);
-                sy += bf16_hi(d.x);
-                sz += bf16_lo(d.y);
-                sw += bf16_hi(d.y);
+                const uint64_t* src = tp::slot_ptr(xbase, world, M, H, set, r) + word;
+                const uint32_t d0 = tp::wait_word(src, e), d1 = tp::wait_word(src + 1, e);
+                sx += bf16_lo(d0);
+                sy += bf16_hi(d0);
+                sz += bf16_lo(d1);
+                sw += bf16_hi(d1);
             }
             v[j] = r4[i];
             v[j].x += bf_round(sx);
@@ -166,6 +168,8 @@ __global__ void __launch_bounds__(128) add_rmsnorm_reduce_kernel(float* __restri
                                pack_bf2(v[j].z * rs * bf16_lo(ww.y), v[j].w * rs * bf16_hi(ww.y)));
         }
     }
+    // this exchange is consumed: the next push into the set uses the following epoch
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) hdr->seq[set] = e;
     cluster_sync_all();
 }
 
@@ -610,7 +614,7 @@ extern "C" int dflash_stack_add_rmsnorm(float* resid, const dflash_bf16* delta, 
     return DFLASH_OK;
 }
 
-extern "C" int dflash_stack_add_rmsnorm_reduce(float* resid, const void* exchange, int world, int set,
+extern "C" int dflash_stack_add_rmsnorm_reduce(float* resid, void* exchange, int world, int set,
                                                const dflash_bf16* weight, dflash_bf16* out, int M, int H, float eps,
                                                dflash_stream_t stream) {
     if (!resid || !exchange || !weight || !out || M < 1 || H < 1 || M > 65535 || world < 1 ||

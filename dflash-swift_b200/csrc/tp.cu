@@ -3,18 +3,19 @@
 //
 // Every rank owns one exchange buffer (cudaMalloc, shared with the other ranks of the
 // node through CUDA IPC).  Layout, identical on every rank:
-//   flags [2][kMaxRanks] u32   flag[b][r]: CTAs of rank r's pushes into this buffer's slot
-//                              set b (monotonic, never reset)
-//   seq   [2] u32              this rank's own pushes into set b (monotonic)
-//   data  [2][world][M_max H]  set b, slot r: rank r's bf16 partial
-// A push (dflash_tp_push) stores this rank's partial into slot `rank` of set b of every
-// rank's buffer (own included) with plain vector stores over NVLink, then each CTA
-// releases a system-scope increment of the flag of every destination.  The consumer
-// (dflash_stack_add_rmsnorm_reduce) waits, bounded, until every source's flag has
-// reached seq[b] x push CTAs, and sums the slots in rank order, so every rank computes
-// the same bits.  Calls alternate b = 0, 1: a rank can only push into set b again after
-// it has consumed the other set's exchange, which every peer pushed only after it had
-// consumed set b; so two sets suffice and no slot is overwritten while it is read.
+//   header: seq[2], next[2] u32 (this rank's own bookkeeping, see below)
+//   data  [2 sets][world slots][M H / 2] u64 words
+// Each data word carries two bf16 of a partial in its low half and the exchange's epoch
+// in its high half, written with one 8-byte store, so a reader that sees the epoch it
+// expects has the data of that exchange: no fence and no separate flag is needed (the
+// scheme of low-latency collective protocols).  A push (dflash_tp_push) writes this
+// rank's partial into slot `rank` of set b of every rank's buffer (own included) with
+// epoch e = seq[b] + 1 and records next[b] = e; the consumer
+// (dflash_stack_add_rmsnorm_reduce) waits, bounded, until every word it reads carries
+// e = next[b], sums the slots in rank order (so every rank computes the same bits) and
+// records seq[b] = e.  Exchanges alternate b = 0, 1: a rank pushes into set b again only
+// after consuming the other set's exchange, which every peer pushed only after it had
+// consumed set b; so no slot is overwritten while it is read, and epochs never repeat.
 #include <cstring>
 
 #include "common.cuh"
@@ -24,77 +25,72 @@ namespace dflash {
 namespace tp {
 
 constexpr int kMaxRanks = 8;
-constexpr int kPushBlocks = 32;       // CTAs of a push; flags count CTAs
-constexpr size_t kHeaderBytes = 256;  // flags + seq, padded
+constexpr int kPushBlocks = 32;
+constexpr size_t kHeaderBytes = 256;
 
 struct Header {
-    uint32_t flags[2][kMaxRanks];
-    uint32_t seq[2];
+    uint32_t seq[2];   // epoch of the last exchange consumed in set b
+    uint32_t next[2];  // epoch of the exchange pushed into set b, not yet consumed
 };
 static_assert(sizeof(Header) <= kHeaderBytes, "header");
 
-__host__ __device__ inline size_t slot_elems(int M, int H) { return (size_t)M * H; }
+__host__ __device__ inline size_t slot_words(int M, int H) { return (size_t)M * H / 2; }
 __host__ __device__ inline size_t exchange_bytes(int world, int M, int H) {
-    return kHeaderBytes + 2 * (size_t)world * slot_elems(M, H) * 2;
+    return kHeaderBytes + 2 * (size_t)world * slot_words(M, H) * 8;
 }
-__host__ __device__ inline uint16_t* slot_ptr(void* base, int world, int M, int H, int set, int r) {
-    return reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(base) + kHeaderBytes) +
-           ((size_t)set * world + r) * slot_elems(M, H);
+__host__ __device__ inline uint64_t* slot_ptr(void* base, int world, int M, int H, int set, int r) {
+    return reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(base) + kHeaderBytes) +
+           ((size_t)set * world + r) * slot_words(M, H);
 }
 
 struct Bases {
     void* b[kMaxRanks];
 };
 
-__device__ __forceinline__ void red_release_sys_add(uint32_t* addr, uint32_t v) {
-    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* addr, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* addr) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
     return v;
 }
 
-// part: bf16 [M, H] (16-byte aligned, M H a multiple of 8).  Each CTA stores a contiguous
-// share of the 16-byte chunks into every destination, then bumps their flags.
-__global__ void __launch_bounds__(256) push_kernel(const uint4* __restrict__ part, Bases bases, int rank, int world,
+// part: bf16 [M, H] (4-byte aligned, H even).  Thread i of the grid handles data words
+// i, i + grid, ... and writes each to every destination.
+__global__ void __launch_bounds__(256) push_kernel(const uint32_t* __restrict__ part, Bases bases, int rank, int world,
                                                    int M, int H, int set) {
     pdl_wait();
     pdl_launch_dependents();
-    const size_t chunks = slot_elems(M, H) / 8;
-    const size_t per = (chunks + gridDim.x - 1) / gridDim.x;
-    const size_t c0 = per * blockIdx.x, c1 = c0 + per < chunks ? c0 + per : chunks;
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-        Header* own = reinterpret_cast<Header*>(bases.b[rank]);
-        own->seq[set] += 1;  // read by this rank's consumer, which runs after this kernel
-    }
-    for (int r = 0; r < world; ++r) {
-        uint4* dst = reinterpret_cast<uint4*>(slot_ptr(bases.b[r], world, M, H, set, rank));
-        for (size_t c = c0 + threadIdx.x; c < c1; c += blockDim.x) dst[c] = part[c];
-    }
-    __syncthreads();  // every store of this CTA is issued before the flags move
-    if (threadIdx.x < world) {
-        __threadfence_system();
-        Header* h = reinterpret_cast<Header*>(bases.b[threadIdx.x]);
-        red_release_sys_add(&h->flags[set][rank], 1u);
+    Header* own = reinterpret_cast<Header*>(bases.b[rank]);
+    const uint32_t e = own->seq[set] + 1u;
+    if (blockIdx.x == 0 && threadIdx.x == 0) own->next[set] = e;
+    const uint64_t hi = (uint64_t)e << 32;
+    const size_t words = slot_words(M, H);
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < words; i += (size_t)gridDim.x * blockDim.x) {
+        const uint64_t w = hi | part[i];
+        for (int r = 0; r < world; ++r) st_relaxed_sys_u64(slot_ptr(bases.b[r], world, M, H, set, rank) + i, w);
     }
 }
 
-// Bounded wait (about a second) until every source's flag of `set` has reached the
-// expected count; false after a timeout (the device error word records it).
-__device__ __forceinline__ bool wait_flags(const Header* h, int world, int set, uint32_t expect) {
-    for (int r = 0; r < world; ++r) {
-        if (ld_acquire_sys(&h->flags[set][r]) >= expect) continue;
-        const unsigned long long t0 = globaltimer_ns();
-        while (ld_acquire_sys(&h->flags[set][r]) < expect) {
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                atomicOr(&g_device_error, DFLASH_DEVERR_ALLREDUCE);
-                return false;
-            }
-            __nanosleep(64);
+// The data word `i` of source r's slot, once it carries epoch e (bounded wait, about a
+// second; after a timeout the device error word records it and 0 is returned).  Once an
+// exchange has timed out the ranks are out of step, so later waits give up at once
+// instead of each spending its second: the host reads the error word and stops.
+__device__ __forceinline__ uint32_t wait_word(const uint64_t* p, uint32_t e) {
+    uint64_t v = ld_relaxed_sys_u64(p);
+    if ((uint32_t)(v >> 32) == e) return (uint32_t)v;
+    if (*reinterpret_cast<volatile unsigned int*>(&g_device_error) & DFLASH_DEVERR_ALLREDUCE) return 0u;
+    const unsigned long long t0 = globaltimer_ns();
+    while (true) {
+        v = ld_relaxed_sys_u64(p);
+        if ((uint32_t)(v >> 32) == e) return (uint32_t)v;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(&g_device_error, DFLASH_DEVERR_ALLREDUCE);
+            return 0u;
         }
+        __nanosleep(32);
     }
-    return true;
 }
 
 }  // namespace tp
@@ -154,15 +150,15 @@ extern "C" int dflash_tp_push(const dflash_bf16* part, void* const* bases, int r
     if (!part || !bases || world < 1 || world > tp::kMaxRanks || rank < 0 || rank >= world || M < 1 || H < 1 ||
         (set != 0 && set != 1))
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_tp_push: bad arguments");
-    if (((size_t)M * H) % 8 || !aligned16(part))
-        return fail(DFLASH_ERR_MISALIGNED, "dflash_tp_push: the partial must be 16-byte aligned with M H a multiple of 8");
+    if (H % 2 || (reinterpret_cast<uintptr_t>(part) & 3u))
+        return fail(DFLASH_ERR_MISALIGNED, "dflash_tp_push: the partial must be 4-byte aligned with H even");
     tp::Bases b = {};
     for (int r = 0; r < world; ++r) {
         if (!bases[r] || !aligned16(bases[r])) return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_tp_push: bad base %d", r);
         b.b[r] = bases[r];
     }
     DFLASH_CUDA_TRY(launch_chained(tp::push_kernel, dim3(tp::kPushBlocks), dim3(256), 0,
-                                   reinterpret_cast<cudaStream_t>(stream), 1, reinterpret_cast<const uint4*>(part), b,
-                                   rank, world, M, H, set));
+                                   reinterpret_cast<cudaStream_t>(stream), 1, reinterpret_cast<const uint32_t*>(part),
+                                   b, rank, world, M, H, set));
     return DFLASH_OK;
 }

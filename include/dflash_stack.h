@@ -62,21 +62,22 @@ int dflash_stack_attn_decode(const dflash_bf16* qkv, int ld, const dflash_bf16* 
 /* ------------------------------------------------------------------------------
  * Tensor-parallel all-reduce over peer memory (one process per GPU of one node).
  * Each rank allocates one exchange buffer (dflash_tp_exchange_alloc, sized by
- * dflash_tp_exchange_bytes for the world size and the largest [M, H] reduced), shares
- * it through CUDA IPC (dflash_ipc_get_handle / dflash_ipc_open_handle, 64-byte handles
- * exchanged by the host), and then, for every all-reduce, in stream order:
+ * dflash_tp_exchange_bytes for the world size and the [M, H] reduced), shares it through
+ * CUDA IPC (dflash_ipc_get_handle / dflash_ipc_open_handle, 64-byte handles exchanged by
+ * the host), and then, for every all-reduce, in stream order:
  *   dflash_tp_push(part, bases, ...)            this rank's bf16 [M, H] partial into slot
- *                                               `rank` of every rank's buffer (NVLink stores)
- *   dflash_stack_add_rmsnorm_reduce(..., set)   waits for every rank's push, adds
- *                                               bf16(sum of the partials in rank order) to
- *                                               resid and normalises it
+ *                                               `rank` of every rank's buffer (NVLink stores
+ *                                               of 8-byte words: 2 bf16 + the exchange epoch)
+ *   dflash_stack_add_rmsnorm_reduce(..., set)   waits until every word carries the epoch,
+ *                                               adds bf16(sum of the partials in rank order)
+ *                                               to resid and normalises it
  * with `set` alternating 0, 1 from one all-reduce to the next (the same sequence on every
- * rank).  bases[r] is rank r's buffer as mapped in this process (bases[rank] = own).  The
- * wait is bounded (about a second): on timeout DFLASH_DEVERR_ALLREDUCE is raised in the
- * device error word and the output is not meaningful.  The buffer must be zero and every
- * rank's allocation complete before any rank's first push (a host barrier).
- * These replace the NCCL all-reduce the reference has no counterpart for (it runs on one
- * GPU); no TMA or multicast is involved.
+ * rank) and the same [M, H] for both calls of an exchange.  bases[r] is rank r's buffer
+ * as mapped in this process (bases[rank] = own).  The wait is bounded (about a second):
+ * on timeout DFLASH_DEVERR_ALLREDUCE is raised in the device error word and the output
+ * is not meaningful.  Every rank's buffer must be allocated (it starts zeroed) before any
+ * rank's first push (a host barrier).  The reference runs on one GPU and has no
+ * counterpart; no TMA or multicast is involved.
  * ------------------------------------------------------------------------------ */
 size_t dflash_tp_exchange_bytes(int world, int M, int H);
 int dflash_tp_exchange_alloc(size_t bytes, void** ptr);
@@ -86,7 +87,7 @@ int dflash_ipc_open_handle(const void* handle64, void** ptr);
 int dflash_ipc_close_handle(void* ptr);
 int dflash_tp_push(const dflash_bf16* part, void* const* bases, int rank, int world, int M, int H, int set,
                    dflash_stream_t stream);
-int dflash_stack_add_rmsnorm_reduce(float* resid, const void* exchange, int world, int set, const dflash_bf16* weight,
+int dflash_stack_add_rmsnorm_reduce(float* resid, void* exchange, int world, int set, const dflash_bf16* weight,
                                     dflash_bf16* out, int M, int H, float eps, dflash_stream_t stream);
 
 #ifdef __cplusplus
