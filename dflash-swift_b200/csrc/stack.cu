@@ -133,13 +133,28 @@ __global__ void __launch_bounds__(128) add_rmsnorm_reduce_kernel(float* __restri
         if (i < P4) {
             float sx = 0.f, sy = 0.f, sz = 0.f, sw = 0.f;
             const size_t word = ((size_t)m * H + 4 * (size_t)(base + i)) / 2;  // two data words per float4
-            for (int r = 0; r < world; ++r) {
-                const uint64_t* src = tp::slot_ptr(xbase, world, M, H, set, r) + word;
-                const uint32_t d0 = tp::wait_word(src, e), d1 = tp::wait_word(src + 1, e);
-                sx += bf16_lo(d0);
-                sy += bf16_hi(d0);
-                sz += bf16_lo(d1);
-                sw += bf16_hi(d1);
+            // every source's two words are requested before any is inspected, so the
+            // loads overlap; a word without the expected epoch is then waited for alone
+            uint64_t w0[tp::kMaxRanks], w1[tp::kMaxRanks];
+#pragma unroll
+            for (int r = 0; r < tp::kMaxRanks; ++r) {
+                if (r < world) {
+                    const uint64_t* src = tp::slot_ptr(xbase, world, M, H, set, r) + word;
+                    w0[r] = tp::ld_relaxed_sys_u64(src);
+                    w1[r] = tp::ld_relaxed_sys_u64(src + 1);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < tp::kMaxRanks; ++r) {
+                if (r < world) {
+                    const uint64_t* src = tp::slot_ptr(xbase, world, M, H, set, r) + word;
+                    const uint32_t d0 = (uint32_t)(w0[r] >> 32) == e ? (uint32_t)w0[r] : tp::wait_word(src, e);
+                    const uint32_t d1 = (uint32_t)(w1[r] >> 32) == e ? (uint32_t)w1[r] : tp::wait_word(src + 1, e);
+                    sx += bf16_lo(d0);
+                    sy += bf16_hi(d0);
+                    sz += bf16_lo(d1);
+                    sw += bf16_hi(d1);
+                }
             }
             v[j] = r4[i];
             v[j].x += bf_round(sx);

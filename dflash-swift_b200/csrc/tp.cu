@@ -25,7 +25,7 @@ namespace dflash {
 namespace tp {
 
 constexpr int kMaxRanks = 8;
-constexpr int kPushBlocks = 32;
+constexpr int kPushBlocks = 128;  // spreads the NVLink stores over many SMs
 constexpr size_t kHeaderBytes = 256;
 
 struct Header {
