@@ -48,6 +48,8 @@
 // for weights and x (a sum does not depend on k order), so weights are consumed exactly
 // as MLX packs them.
 #include "common.cuh"
+#include "dflash_stack.h"
+#include "tp_layout.cuh"
 
 #include <cstdlib>
 
@@ -247,7 +249,15 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
 // the segment reductions are xor-shuffles (the same fixed-order sum on every lane).
 // Padding (rows past M, k past K) gets x' = 0 and a zero table entry, so the main
 // kernel needs no masks along k or m: those columns contribute exactly 0.
-template <class C>
+// SWIGLU: x is [M, 2K] = [gate | up] and the matmul input is bf16(silu(gate) * up), the
+// activation between an MLP's gate/up and down projections, formed here instead of by a
+// separate kernel (the same arithmetic, so the result is the same bits).
+__device__ __forceinline__ float swiglu_bf16(float g, float u) {
+    const float a = g / (1.f + __expf(-g)) * u;
+    return bf16_bits_to_float(__bfloat16_as_ushort(__float2bfloat16_rn(a)));
+}
+
+template <class C, bool SWIGLU>
 __global__ void __launch_bounds__(kPrepThreads) qmm_prep_kernel(const uint16_t* __restrict__ x,
                                                                 uint8_t* __restrict__ packets, int M, int K,
                                                                 int S) {
@@ -263,7 +273,7 @@ __global__ void __launch_bounds__(kPrepThreads) qmm_prep_kernel(const uint16_t* 
 
     float v[8];
     if (m < M && k0 < K) {
-        const uint4 r = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * K + k0));
+        const uint4 r = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * (SWIGLU ? 2 * K : K) + k0));
         v[0] = bf16_lo(r.x);
         v[1] = bf16_hi(r.x);
         v[2] = bf16_lo(r.y);
@@ -272,6 +282,17 @@ __global__ void __launch_bounds__(kPrepThreads) qmm_prep_kernel(const uint16_t* 
         v[5] = bf16_hi(r.z);
         v[6] = bf16_lo(r.w);
         v[7] = bf16_hi(r.w);
+        if constexpr (SWIGLU) {
+            const uint4 q = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * 2 * K + K + k0));
+            v[0] = swiglu_bf16(v[0], bf16_lo(q.x));
+            v[1] = swiglu_bf16(v[1], bf16_hi(q.x));
+            v[2] = swiglu_bf16(v[2], bf16_lo(q.y));
+            v[3] = swiglu_bf16(v[3], bf16_hi(q.y));
+            v[4] = swiglu_bf16(v[4], bf16_lo(q.z));
+            v[5] = swiglu_bf16(v[5], bf16_hi(q.z));
+            v[6] = swiglu_bf16(v[6], bf16_lo(q.w));
+            v[7] = swiglu_bf16(v[7], bf16_hi(q.w));
+        }
     } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = 0.f;
@@ -341,6 +362,10 @@ struct Params {
     int S;        // stages along K
     int NS, NSB;  // ring depths
     int y_vec;    // y rows 16-byte aligned with N % 8 == 0: write y in 16-byte chunks
+    // push: instead of y, write the output into slot `rank` of exchange set `set` of every
+    // rank's exchange buffer (tp_layout.cuh) as epoch-tagged words (N % 8 == 0)
+    int push, rank, world, set;
+    tp::Bases xb;
     uint32_t stage_bytes, sb_bytes, red_off, red_bytes, recv_off, bar_off;
 };
 
@@ -778,6 +803,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* recv = reinterpret_cast<float*>(smem + p.recv_off);
         constexpr int MR = C::MR;
         pdl_wait();  // y may still be read or written by the preceding kernel
+        uint32_t push_epoch = 0;
+        if (p.push) {  // this exchange's epoch; CTA 0 records it for this rank's consumer
+            tp::Header* own = reinterpret_cast<tp::Header*>(p.xb.b[p.rank]);
+            push_epoch = own->seq[p.set] + 1u;
+            if (blockIdx.x == 0 && tid == 0) own->next[p.set] = push_epoch;
+        }
         int slot = 0, ph = 0, qslot = 0, qph = 0, tt = 0;
         for (int t = cid; t < p.ntiles; t += ncl, ++tt) {
             float acc[4][C::NT][4];
@@ -994,7 +1025,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // y rows of the owned blocks, from the staging buffer
             const int n0 = t * p.R + 16 * own0;
-            if (p.y_vec) {
+            if (p.push) {
+                const int chunks = own_rows / 8;
+                const uint64_t hi = (uint64_t)push_epoch << 32;
+                for (int e = tid; e < p.M * chunks; e += kConsumerThreads) {
+                    const int m = e / chunks, c = e - m * chunks;
+                    const int n = n0 + 8 * c;
+                    if (n < p.N) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(stg + m * own_rows + 8 * c);
+                        const size_t w0 = ((size_t)m * p.N + n) / 2;
+                        for (int r = 0; r < p.world; ++r) {
+                            uint64_t* d = tp::slot_ptr(p.xb.b[r], p.world, p.M, p.N, p.set, p.rank) + w0;
+                            tp::st_relaxed_sys_u64(d, hi | v.x);
+                            tp::st_relaxed_sys_u64(d + 1, hi | v.y);
+                            tp::st_relaxed_sys_u64(d + 2, hi | v.z);
+                            tp::st_relaxed_sys_u64(d + 3, hi | v.w);
+                        }
+                    }
+                }
+            } else if (p.y_vec) {
                 const int chunks = own_rows / 8;
                 for (int e = tid; e < p.M * chunks; e += kConsumerThreads) {
                     const int m = e / chunks, c = e - m * chunks;
@@ -1023,6 +1072,14 @@ done:
 
 struct Shape {
     int M, N, K, group, bits;
+};
+
+// Input transform and output destination of one call (dflash_qmm_ex).
+struct Options {
+    bool swiglu = false;  // x is [M, 2K] = [gate | up]; the input is bf16(silu(gate) * up)
+    bool push = false;    // y goes to the peer exchange instead of memory
+    int rank = 0, world = 1, set = 0;
+    tp::Bases xb = {};
 };
 
 struct Plan {
@@ -1186,7 +1243,7 @@ const int* max_clusters(int dev) {
 
 template <class C>
 int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scales,
-           const dflash_bf16* biases, dflash_bf16* y, void* ws, cudaStream_t stream) {
+           const dflash_bf16* biases, dflash_bf16* y, void* ws, cudaStream_t stream, const Options& o) {
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     static int launch_regs = 0;
@@ -1256,6 +1313,11 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
     p.NS = pl.NS;
     p.NSB = pl.NSB;
     p.y_vec = (s.N % 8 == 0) && aligned16(y);
+    p.push = o.push ? 1 : 0;
+    p.rank = o.rank;
+    p.world = o.world;
+    p.set = o.set;
+    p.xb = o.xb;
     p.stage_bytes = pl.stage_bytes;
     p.sb_bytes = pl.sb_bytes;
     p.red_off = pl.red_off;
@@ -1279,8 +1341,9 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
         cfg.stream = stream;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        DFLASH_CUDA_TRY(cudaLaunchKernelEx(&cfg, qmm_prep_kernel<C>, reinterpret_cast<const uint16_t*>(x),
-                                           reinterpret_cast<uint8_t*>(ws), s.M, s.K, pl.S));
+        DFLASH_CUDA_TRY(cudaLaunchKernelEx(&cfg, o.swiglu ? qmm_prep_kernel<C, true> : qmm_prep_kernel<C, false>,
+                                           reinterpret_cast<const uint16_t*>(x), reinterpret_cast<uint8_t*>(ws), s.M,
+                                           s.K, pl.S));
     }
     {
         cudaLaunchConfig_t cfg = {};
@@ -1297,26 +1360,26 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
 
 template <int BITS, int GROUP, int NT>
 int dispatch_stma(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash_bf16* sc,
-                  const dflash_bf16* bi, dflash_bf16* y, void* ws, cudaStream_t st) {
+                  const dflash_bf16* bi, dflash_bf16* y, void* ws, cudaStream_t st, const Options& o) {
     const bool stma = ((s.K / s.group) % 8 == 0) && aligned16(sc) && aligned16(bi);
-    if (stma) return launch<Cfg<BITS, GROUP, NT, true>>(s, x, w, sc, bi, y, ws, st);
-    return launch<Cfg<BITS, GROUP, NT, false>>(s, x, w, sc, bi, y, ws, st);
+    if (stma) return launch<Cfg<BITS, GROUP, NT, true>>(s, x, w, sc, bi, y, ws, st, o);
+    return launch<Cfg<BITS, GROUP, NT, false>>(s, x, w, sc, bi, y, ws, st, o);
 }
 
 template <int BITS, int GROUP>
 int dispatch_nt(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash_bf16* sc,
-                const dflash_bf16* bi, dflash_bf16* y, void* ws, cudaStream_t st) {
-    if (s.M <= 8) return dispatch_stma<BITS, GROUP, 1>(s, x, w, sc, bi, y, ws, st);
-    return dispatch_stma<BITS, GROUP, 2>(s, x, w, sc, bi, y, ws, st);
+                const dflash_bf16* bi, dflash_bf16* y, void* ws, cudaStream_t st, const Options& o) {
+    if (s.M <= 8) return dispatch_stma<BITS, GROUP, 1>(s, x, w, sc, bi, y, ws, st, o);
+    return dispatch_stma<BITS, GROUP, 2>(s, x, w, sc, bi, y, ws, st, o);
 }
 
 template <int BITS>
 int dispatch_group(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash_bf16* sc,
-                   const dflash_bf16* bi, dflash_bf16* y, void* ws, cudaStream_t st) {
+                   const dflash_bf16* bi, dflash_bf16* y, void* ws, cudaStream_t st, const Options& o = Options()) {
     switch (s.group) {
-        case 32: return dispatch_nt<BITS, 32>(s, x, w, sc, bi, y, ws, st);
-        case 64: return dispatch_nt<BITS, 64>(s, x, w, sc, bi, y, ws, st);
-        case 128: return dispatch_nt<BITS, 128>(s, x, w, sc, bi, y, ws, st);
+        case 32: return dispatch_nt<BITS, 32>(s, x, w, sc, bi, y, ws, st, o);
+        case 64: return dispatch_nt<BITS, 64>(s, x, w, sc, bi, y, ws, st, o);
+        case 128: return dispatch_nt<BITS, 128>(s, x, w, sc, bi, y, ws, st, o);
     }
     return fail(DFLASH_ERR_UNSUPPORTED, "group_size %d not in {32, 64, 128}", s.group);
 }
@@ -1383,6 +1446,48 @@ extern "C" int dflash_qmm(const dflash_bf16* x, const uint32_t* w, const dflash_
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (bits == 4) return qmm::dispatch_group<4>(s, x, w, scales, biases, y, workspace, st);
     return qmm::dispatch_group<8>(s, x, w, scales, biases, y, workspace, st);
+}
+
+extern "C" int dflash_qmm_ex(const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scales,
+                             const dflash_bf16* biases, dflash_bf16* y, int M, int N, int K, int group_size, int bits,
+                             void* workspace, size_t workspace_bytes, const dflash_qmm_options* opts,
+                             dflash_stream_t stream) {
+    using namespace dflash;
+    qmm::Shape s{M, N, K, group_size, bits};
+    if (int st = qmm::validate(s)) return st;
+    qmm::Options o;
+    if (opts) {
+        o.swiglu = opts->x_swiglu != 0;
+        o.push = opts->push != 0;
+    }
+    if (!x || !w || !scales || !biases || (!y && !o.push))
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_qmm_ex: null tensor pointer");
+    if (!aligned16(x) || !aligned16(w))
+        return fail(DFLASH_ERR_MISALIGNED, "dflash_qmm_ex: x and w must be 16-byte aligned");
+    if (o.swiglu && K % 8)
+        return fail(DFLASH_ERR_MISALIGNED, "dflash_qmm_ex: the up half of [gate | up] must start 16-byte aligned");
+    if (o.push) {
+        if (opts->world < 1 || opts->world > tp::kMaxRanks || opts->rank < 0 || opts->rank >= opts->world ||
+            (opts->set != 0 && opts->set != 1) || !opts->bases)
+            return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_qmm_ex: bad push rank/world/set/bases");
+        if (N % 8) return fail(DFLASH_ERR_UNSUPPORTED, "dflash_qmm_ex: pushing needs N %% 8 == 0 (N=%d)", N);
+        o.rank = opts->rank;
+        o.world = opts->world;
+        o.set = opts->set;
+        for (int r = 0; r < o.world; ++r) {
+            if (!opts->bases[r] || !aligned16(opts->bases[r]))
+                return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_qmm_ex: bad exchange base %d", r);
+            o.xb.b[r] = opts->bases[r];
+        }
+    }
+    const size_t need = qmm::workspace_size(M, K, group_size, bits);
+    if (!workspace || workspace_bytes < need || !aligned16(workspace))
+        return fail(DFLASH_ERR_WORKSPACE,
+                    "dflash_qmm_ex: a 16-byte aligned workspace of %zu bytes is required (got %zu)", need,
+                    workspace_bytes);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (bits == 4) return qmm::dispatch_group<4>(s, x, w, scales, biases, y, workspace, st, o);
+    return qmm::dispatch_group<8>(s, x, w, scales, biases, y, workspace, st, o);
 }
 
 // ------------------------------------------------------------------ entry point without allocation

@@ -20,41 +20,12 @@
 
 #include "common.cuh"
 #include "dflash_stack.h"
+#include "tp_layout.cuh"
 
 namespace dflash {
 namespace tp {
 
-constexpr int kMaxRanks = 8;
 constexpr int kPushBlocks = 128;  // spreads the NVLink stores over many SMs
-constexpr size_t kHeaderBytes = 256;
-
-struct Header {
-    uint32_t seq[2];   // epoch of the last exchange consumed in set b
-    uint32_t next[2];  // epoch of the exchange pushed into set b, not yet consumed
-};
-static_assert(sizeof(Header) <= kHeaderBytes, "header");
-
-__host__ __device__ inline size_t slot_words(int M, int H) { return (size_t)M * H / 2; }
-__host__ __device__ inline size_t exchange_bytes(int world, int M, int H) {
-    return kHeaderBytes + 2 * (size_t)world * slot_words(M, H) * 8;
-}
-__host__ __device__ inline uint64_t* slot_ptr(void* base, int world, int M, int H, int set, int r) {
-    return reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(base) + kHeaderBytes) +
-           ((size_t)set * world + r) * slot_words(M, H);
-}
-
-struct Bases {
-    void* b[kMaxRanks];
-};
-
-__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* addr, uint64_t v) {
-    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
-}
-__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* addr) {
-    uint64_t v;
-    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
-    return v;
-}
 
 // part: bf16 [M, H] (4-byte aligned, H even).  Thread i of the grid handles data words
 // i, i + grid, ... and writes each to every destination.

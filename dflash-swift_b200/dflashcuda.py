@@ -51,7 +51,7 @@ EXPORTED = (
     "dflash_stack_gated_norm", "dflash_stack_attn_prep", "dflash_stack_attn_decode",
     "dflash_stack_add_rmsnorm_reduce", "dflash_tp_exchange_bytes", "dflash_tp_exchange_alloc",
     "dflash_tp_exchange_free", "dflash_ipc_get_handle", "dflash_ipc_open_handle", "dflash_ipc_close_handle",
-    "dflash_tp_push",
+    "dflash_tp_push", "dflash_qmm_ex",
 )
 
 
@@ -103,6 +103,7 @@ def _load() -> ctypes.CDLL:
         "dflash_ipc_open_handle": ([_vp, ctypes.POINTER(_vp)], _i),
         "dflash_ipc_close_handle": ([_vp], _i),
         "dflash_tp_push": ([_vp, ctypes.POINTER(_vp), _i, _i, _i, _i, _i, _vp], _i),
+        "dflash_qmm_ex": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, ctypes.c_void_p, _vp], _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -492,6 +493,11 @@ class PeerExchange:
         self.rank = rank
         self.bases = (ctypes.c_void_p * len(bases))(*bases)
 
+    def connect_local(self, rank: int, ptrs) -> None:
+        """Use buffers of this process as the ranks' buffers (single-process tests)."""
+        self.rank = rank
+        self.bases = (ctypes.c_void_p * len(ptrs))(*ptrs)
+
     def push(self, part, set_: int, stream=None) -> None:
         M, H = part.shape
         check(lib.dflash_tp_push(_ptr(part), self.bases, self.rank, self.world, M, H, set_, _stream(stream)))
@@ -509,4 +515,31 @@ def stack_add_rmsnorm_reduce(resid, exchange: PeerExchange, set_: int, weight, o
     M, H = resid.shape
     check(lib.dflash_stack_add_rmsnorm_reduce(_ptr(resid), exchange.ptr, exchange.world, set_, _ptr(weight), _ptr(out),
                                               M, H, float(eps), _stream(stream)))
+    return out
+
+
+class QmmOptions(ctypes.Structure):
+    """dflash_qmm_options (include/dflash_stack.h)."""
+    _fields_ = [("x_swiglu", ctypes.c_int), ("push", ctypes.c_int), ("rank", ctypes.c_int), ("world", ctypes.c_int),
+                ("set", ctypes.c_int), ("bases", ctypes.c_void_p)]
+
+
+def qmm_ex(x, w, scales, biases, group_size: int, bits: int, out=None, workspace: Optional[Workspace] = None,
+           swiglu: bool = False, exchange: Optional[PeerExchange] = None, set_: int = 0, stream=None):
+    """dflash_qmm_ex: with swiglu, x is [M, 2K] = [gate | up]; with an exchange, the result
+    is pushed to every rank's exchange slot (set `set_`) instead of written to `out`."""
+    import torch
+    M = x.shape[0]
+    K = x.shape[1] // 2 if swiglu else x.shape[1]
+    N = w.shape[0]
+    if out is None and exchange is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    o = QmmOptions(int(bool(swiglu)), 0, 0, 1, 0, None)
+    if exchange is not None:
+        o.push, o.rank, o.world, o.set = 1, exchange.rank, exchange.world, int(set_)
+        o.bases = ctypes.cast(exchange.bases, ctypes.c_void_p)
+    need = qmm_workspace_bytes(M, N, K, group_size, bits)
+    ws = workspace.ensure(need) if workspace is not None else default_workspace(need, x.device)
+    check(lib.dflash_qmm_ex(_ptr(x), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out), M, N, K, group_size, bits,
+                            ws.buf.data_ptr(), ws.nbytes, ctypes.addressof(o), _stream(stream)))
     return out

@@ -17,10 +17,12 @@ So a layer has exactly two collectives (after the mixer and after the MLP), 128 
 forward.  The residual stream is fp32 and replicated; everything between the shard
 boundaries is rank-local.  The projections run on dflash_qmm, the recurrence on
 dflash_gdn_step (its inputs are the rollback capture) and the glue on the dflash_stack_*
-kernels.  The all-reduce runs over peer memory: each rank's partial is stored into every
-rank's exchange buffer over NVLink (dflash_tp_push) and the next RMSNorm sums the slots
-after a bounded flag wait (dflash_stack_add_rmsnorm_reduce); NCCL through
-torch.distributed is the alternative (`allreduce="nccl"`).  The whole forward is
+kernels (SwiGLU is folded into the down projection's input prep).  The all-reduce runs
+over peer memory: the row-sharded projection's qmm kernel stores its output into every
+rank's exchange buffer over NVLink as epoch-tagged words (dflash_qmm_ex with push) and
+the next RMSNorm sums the slots once every word carries the exchange's epoch
+(dflash_stack_add_rmsnorm_reduce); NCCL through torch.distributed is the alternative
+(`allreduce="nccl"`).  The whole forward is
 captured once as a CUDA graph and replayed.
 
 Weights are seeded synthetic MLX-packed 4-bit tensors (no checkpoint is available):
@@ -379,7 +381,6 @@ class VerifyStack:
         self.qkv = torch.empty(M, (2 * p.attn_heads + 2 * p.kv_heads) * d, **bf)
         self.attn_out = torch.empty(M, p.attn_heads * d, **bf)
         self.gate_up = torch.empty(M, 2 * p.inter, **bf)
-        self.act = torch.empty(M, p.inter, **bf)
         need = 0
         for L in self.w["layers"]:
             for v in L.values():
@@ -391,13 +392,23 @@ class VerifyStack:
     def _qmm(self, x, q: Quant, out):
         self.dc.qmm(x, q.w, q.scales, q.biases, q.group, q.bits, out=out, workspace=self.ws)
 
-    def _reduce(self, part):
-        """Start the all-reduce of this rank's partial; returns what the next norm adds."""
+    def _qmm_reduced(self, x, q: Quant, swiglu: bool = False):
+        """A row-sharded projection whose output is all-reduced: with the peer exchange the
+        qmm kernel pushes its result straight into every rank's slot; otherwise it writes
+        self.delta, which NCCL (or nothing, at TP=1) reduces.  Returns the pending delta
+        for the next norm."""
         if self.allreduce == "peer":
-            self.exchange.push(part, self._set)
+            self.dc.qmm_ex(x, q.w, q.scales, q.biases, q.group, q.bits, workspace=self.ws, swiglu=swiglu,
+                           exchange=self.exchange, set_=self._set)
             pending = ("exchange", self._set)
             self._set ^= 1
             return pending
+        self.dc.qmm_ex(x, q.w, q.scales, q.biases, q.group, q.bits, out=self.delta, workspace=self.ws, swiglu=swiglu)
+        return self._reduce(self.delta)
+
+    def _reduce(self, part):
+        """All-reduce of a partial written to memory (NCCL, or nothing at TP=1); returns
+        what the next norm adds."""
         if self.allreduce == "nccl":
             torch.distributed.all_reduce(part, group=self.pg)
         return part
@@ -423,7 +434,7 @@ class VerifyStack:
                     q_scale=1.0 / math.sqrt(dk))
         z = self.gdn_proj[:, 2 * h * dk + h * dv:]
         dc.stack_gated_norm(self.gdn_o, z, L["gdn_norm"], self.gdn_normed, cfg.eps)
-        self._qmm(self.gdn_normed, L["out_proj"], self.delta)
+        return self._qmm_reduced(self.gdn_normed, L["out_proj"])
 
     def _attn(self, L, S):
         cfg, p, dc = self.cfg, self.plan, self.dc
@@ -432,12 +443,11 @@ class VerifyStack:
                            cfg.rotary_dim, cfg.context, cfg.eps, cfg.rope_theta)
         dc.stack_attn_decode(self.qkv, S["cache_k"], S["cache_v"], self.attn_out, p.attn_heads, p.kv_heads,
                              cfg.context, 1.0 / math.sqrt(cfg.head_dim))
-        self._qmm(self.attn_out, L["o_proj"], self.delta)
+        return self._qmm_reduced(self.attn_out, L["o_proj"])
 
     def _mlp(self, L):
         self._qmm(self.normed, L["gate_up"], self.gate_up)
-        self.dc.stack_silu_mul(self.gate_up, self.act)
-        self._qmm(self.act, L["down"], self.delta)
+        return self._qmm_reduced(self.gate_up, L["down"], swiglu=True)  # SwiGLU inside the down qmm
 
     def _forward_body(self, hidden):
         cfg, dc = self.cfg, self.dc
@@ -447,14 +457,12 @@ class VerifyStack:
         for L, S in zip(self.w["layers"], self.state["layers"]):
             self._norm(pending, L["ln"], self.normed)
             if L["kind"] == "gdn":
-                self._gdn(L, S, gi)
+                pending = self._gdn(L, S, gi)
                 gi += 1
             else:
-                self._attn(L, S)
-            pending = self._reduce(self.delta)
+                pending = self._attn(L, S)
             self._norm(pending, L["post_ln"], self.normed)
-            self._mlp(L)
-            pending = self._reduce(self.delta)
+            pending = self._mlp(L)
         self._norm(pending, self.w["final_norm"], self.out)
         return self.out
 
@@ -480,9 +488,7 @@ class VerifyStack:
                 n += 2 + 1 + 1 + 1 + 1 + 2  # in_proj, conv, gates, gdn_step, gated_norm, out_proj
             else:
                 n += 2 + 1 + 1 + 2  # qkv, prep, decode, o_proj
-            n += 2 + 1 + 2  # gate_up, silu_mul, down
-            if self.allreduce == "peer":
-                n += 2  # the pushes (the sums are inside the norms)
+            n += 2 + 2  # gate_up, down (SwiGLU inside its prep; pushes inside the qmm epilogues)
         return n
 
 

@@ -90,6 +90,28 @@ int dflash_tp_push(const dflash_bf16* part, void* const* bases, int rank, int wo
 int dflash_stack_add_rmsnorm_reduce(float* resid, void* exchange, int world, int set, const dflash_bf16* weight,
                                     dflash_bf16* out, int M, int H, float eps, dflash_stream_t stream);
 
+/* ------------------------------------------------------------------------------
+ * dflash_qmm with an input transform and/or an output that goes to the peer exchange,
+ * so the SwiGLU and the all-reduce push need no kernel of their own.
+ *   x_swiglu: x is bf16 [M, 2K] = [gate | up] (row stride 2K) and the matmul input is
+ *             bf16(silu(gate) * up), the same bits dflash_stack_silu_mul would write.
+ *   push:     y is not written (may be NULL); the bf16 [M, N] result goes to slot `rank`
+ *             of exchange set `set` of every rank's buffer exactly as dflash_tp_push would
+ *             write it, to be summed by dflash_stack_add_rmsnorm_reduce (H = N).
+ * Other arguments, the workspace and the errors are dflash_qmm's.  No counterpart in the
+ * reference (its MLP activation and, on one GPU, no all-reduce at all).
+ * ------------------------------------------------------------------------------ */
+typedef struct dflash_qmm_options {
+    int x_swiglu;
+    int push;
+    int rank, world, set;
+    void* const* bases; /* [world] exchange buffers as mapped in this process */
+} dflash_qmm_options;
+
+int dflash_qmm_ex(const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scales, const dflash_bf16* biases,
+                  dflash_bf16* y, int M, int N, int K, int group_size, int bits, void* workspace,
+                  size_t workspace_bytes, const dflash_qmm_options* opts, dflash_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -203,6 +203,66 @@ def test_cuda_stack_tp1_matches_reference(cuda):
 
 
 @pytest.mark.gpu
+def test_qmm_swiglu_input_equals_separate_silu_mul(dc, O, cuda):
+    """dflash_qmm_ex with x_swiglu gives the same bits as dflash_stack_silu_mul followed by
+    dflash_qmm (the down projection of the MLP)."""
+    M, I, N = 8, 2048, 1024
+    gen = torch.Generator(device=cuda).manual_seed(3)
+    gu = torch.randn(M, 2 * I, generator=gen, device=cuda).to(torch.bfloat16)
+    q = vs.random_quant(gen, N, I, 64, 4, cuda)
+    act = torch.empty(M, I, dtype=torch.bfloat16, device=cuda)
+    dc.stack_silu_mul(gu, act)
+    want = dc.qmm(act, q.w, q.scales, q.biases, 64, 4)
+    got = dc.qmm_ex(gu, q.w, q.scales, q.biases, 64, 4, swiglu=True)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("via", ["push_kernel", "qmm_epilogue"])
+def test_peer_exchange_two_ranks_in_one_process(dc, cuda, via):
+    """The exchange protocol with two 'ranks' emulated by two buffers on one GPU (each
+    push completes before the sums are read, so nothing waits on another kernel): both
+    buffers' reducing norms equal add_rmsnorm with delta = bf16(y0 + y1), for two
+    consecutive exchanges (both slot sets) and a third that reuses set 0."""
+    M, H, K = 8, 512, 1024
+    gen = torch.Generator(device=cuda).manual_seed(4)
+    ex = [dc.PeerExchange(2, M, H) for _ in range(2)]
+    ptrs = [e.ptr for e in ex]
+    for r in range(2):
+        ex[r].connect_local(r, ptrs)
+    q = [vs.random_quant(gen, H, K, 64, 4, cuda) for _ in range(2)]
+    w = (1.0 + 0.1 * torch.randn(H, generator=gen, device=cuda)).to(torch.bfloat16)
+    resid0 = torch.randn(M, H, generator=gen, device=cuda)
+    resid = [resid0.clone(), resid0.clone()]
+    want_resid = resid0.clone()
+    try:
+        for step in range(3):
+            s = step % 2
+            xs = [torch.randn(M, K, generator=gen, device=cuda).to(torch.bfloat16) for _ in range(2)]
+            ys = [dc.qmm(xs[r], q[r].w, q[r].scales, q[r].biases, 64, 4) for r in range(2)]
+            for r in range(2):
+                if via == "push_kernel":
+                    ex[r].push(ys[r], s)
+                else:
+                    dc.qmm_ex(xs[r], q[r].w, q[r].scales, q[r].biases, 64, 4, exchange=ex[r], set_=s)
+            outs = [torch.empty(M, H, dtype=torch.bfloat16, device=cuda) for _ in range(2)]
+            for r in range(2):
+                dc.stack_add_rmsnorm_reduce(resid[r], ex[r], s, w, outs[r], 1e-6)
+            delta = (ys[0].float() + ys[1].float()).to(torch.bfloat16)
+            want = torch.empty(M, H, dtype=torch.bfloat16, device=cuda)
+            dc.stack_add_rmsnorm(want_resid, delta, w, want, 1e-6)
+            torch.cuda.synchronize()
+            assert dc.device_error() == 0
+            for r in range(2):
+                assert torch.equal(outs[r], want), (step, r)
+                assert torch.equal(resid[r], want_resid), (step, r)
+    finally:
+        for e in ex:
+            e.close()
+
+
+@pytest.mark.gpu
 def test_cuda_stack_graph_replay_equals_eager(cuda):
     cfg = vs.TINY
     stack = vs.VerifyStack(cfg, 0, 1, seed=1, device=cuda)
