@@ -260,9 +260,10 @@ __device__ __forceinline__ float swiglu_bf16(float g, float u) {
 template <class C, bool SWIGLU>
 __global__ void __launch_bounds__(kPrepThreads) qmm_prep_kernel(const uint16_t* __restrict__ x,
                                                                 uint8_t* __restrict__ packets, int M, int K,
-                                                                int S) {
+                                                                int S, unsigned long long* argmax_keys) {
     pdl_launch_dependents();
     pdl_wait();  // x may be written by the preceding kernel
+    if (argmax_keys && blockIdx.x == 0 && threadIdx.x < M) argmax_keys[threadIdx.x] = 0ull;
     constexpr int CPR = C::STAGE_K / 8;  // runs of 8 per stage row
     constexpr int SL = C::SEG_K / 8;     // lanes per segment: 4 or 8
     const long long runs = (long long)S * CPR;
@@ -366,6 +367,9 @@ struct Params {
     // rank's exchange buffer (tp_layout.cuh) as epoch-tagged words (N % 8 == 0)
     int push, rank, world, set;
     tp::Bases xb;
+    // argmax: instead of y, fold each row's (largest bf16 output, lowest index) into
+    // argmax_keys[m] with a 64-bit atomic max (zeroed by the prep kernel)
+    unsigned long long* argmax_keys;
     uint32_t stage_bytes, sb_bytes, red_off, red_bytes, recv_off, bar_off;
 };
 
@@ -1025,7 +1029,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // y rows of the owned blocks, from the staging buffer
             const int n0 = t * p.R + 16 * own0;
-            if (p.push) {
+            if (p.argmax_keys) {
+                // warp m scans row m of the owned outputs; lanes keep their best key, the
+                // warp reduces, lane 0 folds it into the row's global key
+                for (int m = warp; m < p.M; m += kConsumerWarps) {
+                    unsigned long long best = 0ull;
+                    for (int r = lane; r < own_rows; r += 32) {
+                        const int n = n0 + r;
+                        if (n >= p.N) break;
+                        const uint32_t u = static_cast<uint32_t>(stg[m * own_rows + r]) << 16;
+                        const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // order of the float
+                        const unsigned long long key = (static_cast<unsigned long long>(ord) << 32) | (~static_cast<uint32_t>(n));
+                        best = key > best ? key : best;
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+                        best = other > best ? other : best;
+                    }
+                    if (lane == 0 && best) atomicMax(p.argmax_keys + m, best);
+                }
+            } else if (p.push) {
                 const int chunks = own_rows / 8;
                 const uint64_t hi = (uint64_t)push_epoch << 32;
                 for (int e = tid; e < p.M * chunks; e += kConsumerThreads) {
@@ -1080,6 +1104,7 @@ struct Options {
     bool push = false;    // y goes to the peer exchange instead of memory
     int rank = 0, world = 1, set = 0;
     tp::Bases xb = {};
+    unsigned long long* argmax_keys = nullptr;  // y is reduced to per-row argmax keys instead
 };
 
 struct Plan {
@@ -1318,6 +1343,7 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
     p.world = o.world;
     p.set = o.set;
     p.xb = o.xb;
+    p.argmax_keys = o.argmax_keys;
     p.stage_bytes = pl.stage_bytes;
     p.sb_bytes = pl.sb_bytes;
     p.red_off = pl.red_off;
@@ -1343,7 +1369,7 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
         cfg.numAttrs = 1;
         DFLASH_CUDA_TRY(cudaLaunchKernelEx(&cfg, o.swiglu ? qmm_prep_kernel<C, true> : qmm_prep_kernel<C, false>,
                                            reinterpret_cast<const uint16_t*>(x), reinterpret_cast<uint8_t*>(ws), s.M,
-                                           s.K, pl.S));
+                                           s.K, pl.S, o.argmax_keys));
     }
     {
         cudaLaunchConfig_t cfg = {};
@@ -1459,8 +1485,13 @@ extern "C" int dflash_qmm_ex(const dflash_bf16* x, const uint32_t* w, const dfla
     if (opts) {
         o.swiglu = opts->x_swiglu != 0;
         o.push = opts->push != 0;
+        o.argmax_keys = reinterpret_cast<unsigned long long*>(opts->argmax_keys);
     }
-    if (!x || !w || !scales || !biases || (!y && !o.push))
+    if (o.push && o.argmax_keys)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_qmm_ex: push and argmax are exclusive");
+    if (o.argmax_keys && (reinterpret_cast<uintptr_t>(o.argmax_keys) & 7u))
+        return fail(DFLASH_ERR_MISALIGNED, "dflash_qmm_ex: argmax_keys must be 8-byte aligned");
+    if (!x || !w || !scales || !biases || (!y && !o.push && !o.argmax_keys))
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_qmm_ex: null tensor pointer");
     if (!aligned16(x) || !aligned16(w))
         return fail(DFLASH_ERR_MISALIGNED, "dflash_qmm_ex: x and w must be 16-byte aligned");

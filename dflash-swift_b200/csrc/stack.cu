@@ -589,6 +589,29 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __rest
     cluster_sync_all();  // every CTA is done reading the others' shared memory
 }
 
+// Greedy accept of a verify round from the LM head's argmax keys (dflash_qmm_ex with
+// argmax_keys): tokens[i] = the argmax of row i; match i = (proposals[i] == tokens[i]) for
+// i < drafts; accepted = the length of the leading run of matches.  One warp.
+__global__ void accept_kernel(const unsigned long long* __restrict__ keys, const int32_t* __restrict__ proposals,
+                              int drafts, int32_t* __restrict__ tokens, int32_t* __restrict__ accepted) {
+    chain_in();
+    const int lane = threadIdx.x;
+    int run = 0;
+    for (int base = 0; base <= drafts; base += 32) {
+        const int i = base + lane;
+        int32_t tok = 0;
+        if (i <= drafts) {
+            tok = (int32_t)(~(uint32_t)(keys[i] & 0xffffffffull));
+            tokens[i] = tok;
+        }
+        const bool miss = i < drafts && proposals[i] != tok;
+        const unsigned mm = __ballot_sync(0xffffffffu, miss);
+        const int valid = min(32, drafts - base);  // match slots in this chunk
+        if (run == base) run += mm ? min(__ffs(mm) - 1, valid) : max(valid, 0);
+    }
+    if (lane == 0) *accepted = run;
+}
+
 inline unsigned grid_for(size_t n, int block) {
     const size_t g = (n + block - 1) / block;
     return (unsigned)(g < 4096 ? (g > 0 ? g : 1) : 4096);
@@ -767,5 +790,14 @@ extern "C" int dflash_stack_attn_decode(const dflash_bf16* qkv, int ld, const df
     DFLASH_ATTN_CASE(8, 4) DFLASH_ATTN_CASE(8, 8)
 #undef DFLASH_ATTN_CASE
     DFLASH_CUDA_TRY(e);
+    return DFLASH_OK;
+}
+
+extern "C" int dflash_accept(const unsigned long long* argmax_keys, const int32_t* proposals, int drafts,
+                             int32_t* target_tokens, int32_t* accepted, dflash_stream_t stream) {
+    if (!argmax_keys || (!proposals && drafts > 0) || !target_tokens || !accepted || drafts < 0)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_accept: bad arguments");
+    DFLASH_CUDA_TRY(launch_chained(stack::accept_kernel, dim3(1), dim3(32), 0, as_stream(stream), 1, argmax_keys,
+                                   proposals, drafts, target_tokens, accepted));
     return DFLASH_OK;
 }

@@ -51,7 +51,7 @@ EXPORTED = (
     "dflash_stack_gated_norm", "dflash_stack_attn_prep", "dflash_stack_attn_decode",
     "dflash_stack_add_rmsnorm_reduce", "dflash_tp_exchange_bytes", "dflash_tp_exchange_alloc",
     "dflash_tp_exchange_free", "dflash_ipc_get_handle", "dflash_ipc_open_handle", "dflash_ipc_close_handle",
-    "dflash_tp_push", "dflash_qmm_ex",
+    "dflash_tp_push", "dflash_qmm_ex", "dflash_accept",
 )
 
 
@@ -104,6 +104,7 @@ def _load() -> ctypes.CDLL:
         "dflash_ipc_close_handle": ([_vp], _i),
         "dflash_tp_push": ([_vp, ctypes.POINTER(_vp), _i, _i, _i, _i, _i, _vp], _i),
         "dflash_qmm_ex": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, ctypes.c_void_p, _vp], _i),
+        "dflash_accept": ([_vp, _vp, _i, _vp, _vp, _vp], _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -521,20 +522,22 @@ def stack_add_rmsnorm_reduce(resid, exchange: PeerExchange, set_: int, weight, o
 class QmmOptions(ctypes.Structure):
     """dflash_qmm_options (include/dflash_stack.h)."""
     _fields_ = [("x_swiglu", ctypes.c_int), ("push", ctypes.c_int), ("rank", ctypes.c_int), ("world", ctypes.c_int),
-                ("set", ctypes.c_int), ("bases", ctypes.c_void_p)]
+                ("set", ctypes.c_int), ("bases", ctypes.c_void_p), ("argmax_keys", ctypes.c_void_p)]
 
 
 def qmm_ex(x, w, scales, biases, group_size: int, bits: int, out=None, workspace: Optional[Workspace] = None,
-           swiglu: bool = False, exchange: Optional[PeerExchange] = None, set_: int = 0, stream=None):
+           swiglu: bool = False, exchange: Optional[PeerExchange] = None, set_: int = 0, argmax_keys=None,
+           stream=None):
     """dflash_qmm_ex: with swiglu, x is [M, 2K] = [gate | up]; with an exchange, the result
-    is pushed to every rank's exchange slot (set `set_`) instead of written to `out`."""
+    is pushed to every rank's exchange slot (set `set_`) instead of written to `out`; with
+    argmax_keys (int64 [M] on the device) each row is reduced to its argmax key instead."""
     import torch
     M = x.shape[0]
     K = x.shape[1] // 2 if swiglu else x.shape[1]
     N = w.shape[0]
-    if out is None and exchange is None:
+    if out is None and exchange is None and argmax_keys is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
-    o = QmmOptions(int(bool(swiglu)), 0, 0, 1, 0, None)
+    o = QmmOptions(int(bool(swiglu)), 0, 0, 1, 0, None, _ptr(argmax_keys))
     if exchange is not None:
         o.push, o.rank, o.world, o.set = 1, exchange.rank, exchange.world, int(set_)
         o.bases = ctypes.cast(exchange.bases, ctypes.c_void_p)
@@ -543,3 +546,24 @@ def qmm_ex(x, w, scales, biases, group_size: int, bits: int, out=None, workspace
     check(lib.dflash_qmm_ex(_ptr(x), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out), M, N, K, group_size, bits,
                             ws.buf.data_ptr(), ws.nbytes, ctypes.addressof(o), _stream(stream)))
     return out
+
+
+def lm_head_argmax(x, w, scales, biases, group_size: int, bits: int, keys=None, workspace=None, stream=None):
+    """Argmax keys of x . deq(W)^T per row without writing the logits (int64 [M])."""
+    import torch
+    if keys is None:
+        keys = torch.empty(x.shape[0], dtype=torch.int64, device=x.device)
+    qmm_ex(x, w, scales, biases, group_size, bits, workspace=workspace, argmax_keys=keys, stream=stream)
+    return keys
+
+
+def accept(keys, proposals, tokens=None, accepted=None, stream=None):
+    """dflash_accept: (target tokens int32 [drafts + 1], accepted int32 [1]) on the device."""
+    import torch
+    drafts = proposals.shape[0]
+    if tokens is None:
+        tokens = torch.empty(drafts + 1, dtype=torch.int32, device=keys.device)
+    if accepted is None:
+        accepted = torch.empty(1, dtype=torch.int32, device=keys.device)
+    check(lib.dflash_accept(_ptr(keys), _ptr(proposals), drafts, _ptr(tokens), _ptr(accepted), _stream(stream)))
+    return tokens, accepted

@@ -98,19 +98,32 @@ int dflash_stack_add_rmsnorm_reduce(float* resid, void* exchange, int world, int
  *   push:     y is not written (may be NULL); the bf16 [M, N] result goes to slot `rank`
  *             of exchange set `set` of every rank's buffer exactly as dflash_tp_push would
  *             write it, to be summed by dflash_stack_add_rmsnorm_reduce (H = N).
+ *   argmax_keys (uint64 [M], device): y is not written; instead row m's largest bf16
+ *             output and its lowest index among equal maxima end in argmax_keys[m]
+ *             (high word: the value's order key, low word: ~index), the LM head's argmax
+ *             without writing [M, V] logits (zeroed by the call itself).  Exclusive with push.
  * Other arguments, the workspace and the errors are dflash_qmm's.  No counterpart in the
- * reference (its MLP activation and, on one GPU, no all-reduce at all).
+ * reference for push and SwiGLU (its MLP activation and, on one GPU, no all-reduce); the
+ * argmax is the first half of its accept test (DFlashSpeculativeGenerator.swift:564).
  * ------------------------------------------------------------------------------ */
 typedef struct dflash_qmm_options {
     int x_swiglu;
     int push;
     int rank, world, set;
     void* const* bases; /* [world] exchange buffers as mapped in this process */
+    void* argmax_keys;  /* uint64 [M] or NULL: see below */
 } dflash_qmm_options;
 
 int dflash_qmm_ex(const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scales, const dflash_bf16* biases,
                   dflash_bf16* y, int M, int N, int K, int group_size, int bits, void* workspace,
                   size_t workspace_bytes, const dflash_qmm_options* opts, dflash_stream_t stream);
+
+/* Greedy accept of a verify round (acceptedPrefix, DFlashSpeculativeGenerator.swift:555-571):
+ * from the LM head's argmax keys of drafts + 1 rows, target_tokens[i] = argmax of row i
+ * (int32 [drafts + 1]) and *accepted = the number of leading i < drafts with
+ * proposals[i] == target_tokens[i].  All device pointers; one tiny kernel. */
+int dflash_accept(const unsigned long long* argmax_keys, const int32_t* proposals, int drafts,
+                  int32_t* target_tokens, int32_t* accepted, dflash_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -223,3 +223,20 @@ def make_gdn_case(layers: int, width: int, heads: int, dk: int, dv: int, seed: i
     beta = r.uniform(0.0, 1.0, (layers, width, heads)).astype(np.float32)
     return dict(snapshot=np.ascontiguousarray(snap), q=bf16_bits(q), k=bf16_bits(k), v=bf16_bits(v),
                 alpha=alpha, beta=beta)
+
+
+# ----------------------------------------------------------------------------- accept
+
+def accepted_prefix(logits_bits, proposals):
+    """Greedy accept of a verify round (DFlashSpeculativeGenerator.swift:555-571):
+    target tokens = argmax over the vocabulary of each row of the bf16 logits (first
+    index among equal maxima, as argMax does), match[i] = proposals[i] == tokens[i] for
+    i < drafts, accepted = sum(cumprod(match)).  Returns (tokens int32 [drafts + 1],
+    accepted)."""
+    logits = bits_to_f32(np.asarray(logits_bits, dtype=np.uint16))
+    tokens = np.argmax(logits, axis=-1).astype(np.int32)
+    proposals = np.asarray(proposals, dtype=np.int32)
+    drafts = proposals.shape[0]
+    assert logits.shape[0] == drafts + 1
+    match = (proposals == tokens[:drafts]).astype(np.int32)
+    return tokens, int(np.cumprod(match).sum())
