@@ -11,6 +11,7 @@
 // waits (griddepcontrol.wait) before touching memory, then releases its successor.
 #include "common.cuh"
 #include "dflash_stack.h"
+#include "tp_layout.cuh"
 
 namespace dflash {
 namespace stack {
@@ -273,6 +274,63 @@ __global__ void gdn_gates_kernel(uint16_t* __restrict__ q, uint16_t* __restrict_
         for (int i = lane; i < dk; i += 32) v[i] = to_bf(bf(v[i]) * rs);
     }
     if (lane == 0) {
+        const float b = bf(ab[(size_t)t * ld_ab + h]);
+        const float a = bf(ab[(size_t)t * ld_ab + heads + h]);
+        const float sp = a + dt_bias[h] > 20.f ? a + dt_bias[h] : log1pf(__expf(a + dt_bias[h]));
+        alpha[(size_t)t * heads + h] = __expf(-__expf(a_log[h]) * sp);
+        beta[(size_t)t * heads + h] = 1.f / (1.f + __expf(-b));
+    }
+}
+
+// The gated-delta layer's conv and gates in one kernel (the same arithmetic as
+// conv_silu_kernel followed by gdn_gates_kernel, so the same bits): one warp per (token,
+// head, part q | k | v) covering the head's dk channels (lane l: channels l + 32 j), with
+// all of its conv inputs loaded at once.  Causal conv + SiLU, rounded to bf16; q and k
+// L2-normalised over the head; written to y as the parts' [M, heads dk] blocks.  The q
+// warp's lane 0 also writes alpha and beta of (token, head).
+template <int KC, int DJ>
+__global__ void gdn_conv_gates_kernel(const uint16_t* __restrict__ x, int ld, const uint16_t* __restrict__ window,
+                                      const uint16_t* __restrict__ w, uint16_t* __restrict__ y,
+                                      const uint16_t* __restrict__ ab, int ld_ab, const float* __restrict__ a_log,
+                                      const float* __restrict__ dt_bias, float* __restrict__ alpha,
+                                      float* __restrict__ beta, int M, int heads) {
+    chain_in();
+    constexpr int dk = 32 * DJ;
+    const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (wid >= M * heads * 3) return;
+    const int t = wid / (heads * 3), h = (wid / 3) % heads, part = wid % 3;
+    const int C = 3 * heads * dk, cp = heads * dk;
+    float xin[DJ][KC], wk[DJ][KC];
+#pragma unroll
+    for (int j = 0; j < DJ; ++j) {
+        const int c = part * cp + h * dk + lane + 32 * j;
+#pragma unroll
+        for (int i = 0; i < KC; ++i) {
+            wk[j][i] = bf(w[(size_t)c * KC + i]);
+            const int src = t + i - (KC - 1);  // < 0: the window's rows
+            xin[j][i] = src < 0 ? bf(window[(size_t)(KC - 1 + src) * C + c]) : bf(x[(size_t)src * ld + c]);
+        }
+    }
+    float v[DJ];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < DJ; ++j) {
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < KC; ++i) acc = fmaf(wk[j][i], xin[j][i], acc);
+        v[j] = bf_round(silu(acc));
+        ss = fmaf(v[j], v[j], ss);
+    }
+    uint16_t* out = y + ((size_t)part * M + t) * cp + (size_t)h * dk + lane;
+    if (part < 2) {
+        const float rs = rsqrtf(warp_sum(ss) + 1e-6f);
+#pragma unroll
+        for (int j = 0; j < DJ; ++j) out[32 * j] = to_bf(v[j] * rs);
+    } else {
+#pragma unroll
+        for (int j = 0; j < DJ; ++j) out[32 * j] = to_bf(v[j]);
+    }
+    if (part == 0 && lane == 0) {
         const float b = bf(ab[(size_t)t * ld_ab + h]);
         const float a = bf(ab[(size_t)t * ld_ab + heads + h]);
         const float sp = a + dt_bias[h] > 20.f ? a + dt_bias[h] : log1pf(__expf(a + dt_bias[h]));
@@ -799,5 +857,31 @@ extern "C" int dflash_accept(const unsigned long long* argmax_keys, const int32_
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_accept: bad arguments");
     DFLASH_CUDA_TRY(launch_chained(stack::accept_kernel, dim3(1), dim3(32), 0, as_stream(stream), 1, argmax_keys,
                                    proposals, drafts, target_tokens, accepted));
+    return DFLASH_OK;
+}
+
+extern "C" int dflash_stack_gdn_conv_gates(const dflash_bf16* x, int ld, const dflash_bf16* window,
+                                           const dflash_bf16* weight, dflash_bf16* y, const dflash_bf16* ab,
+                                           int ld_ab, const float* a_log, const float* dt_bias, float* alpha,
+                                           float* beta, int M, int heads, int dk, int kc, dflash_stream_t stream) {
+    if (!x || !window || !weight || !y || !ab || !a_log || !dt_bias || !alpha || !beta || M < 1 || heads < 1 ||
+        ld < 3 * heads * dk)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_gdn_conv_gates: bad arguments");
+    if ((dk != 32 && dk != 64 && dk != 128) || kc < 2 || kc > 4)
+        return fail(DFLASH_ERR_UNSUPPORTED, "dflash_stack_gdn_conv_gates: dk %d (32, 64, 128) / conv width %d (2..4)",
+                    dk, kc);
+    const int warps = 3 * heads * M;
+    const dim3 grid((warps + 7) / 8), block(256);
+    cudaStream_t s = as_stream(stream);
+    cudaError_t e = cudaSuccess;
+#define DFLASH_CG_CASE(KC, DJ)                                                                                   \
+    if (kc == KC && dk == 32 * DJ)                                                                               \
+        e = launch_chained(stack::gdn_conv_gates_kernel<KC, DJ>, grid, block, 0, s, 1, x, ld, window, weight, y, ab, \
+                           ld_ab, a_log, dt_bias, alpha, beta, M, heads);
+    DFLASH_CG_CASE(2, 1) DFLASH_CG_CASE(2, 2) DFLASH_CG_CASE(2, 4)
+    DFLASH_CG_CASE(3, 1) DFLASH_CG_CASE(3, 2) DFLASH_CG_CASE(3, 4)
+    DFLASH_CG_CASE(4, 1) DFLASH_CG_CASE(4, 2) DFLASH_CG_CASE(4, 4)
+#undef DFLASH_CG_CASE
+    DFLASH_CUDA_TRY(e);
     return DFLASH_OK;
 }

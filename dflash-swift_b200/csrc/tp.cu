@@ -44,26 +44,6 @@ __global__ void __launch_bounds__(256) push_kernel(const uint32_t* __restrict__ 
     }
 }
 
-// The data word `i` of source r's slot, once it carries epoch e (bounded wait, about a
-// second; after a timeout the device error word records it and 0 is returned).  Once an
-// exchange has timed out the ranks are out of step, so later waits give up at once
-// instead of each spending its second: the host reads the error word and stops.
-__device__ __forceinline__ uint32_t wait_word(const uint64_t* p, uint32_t e) {
-    uint64_t v = ld_relaxed_sys_u64(p);
-    if ((uint32_t)(v >> 32) == e) return (uint32_t)v;
-    if (*reinterpret_cast<volatile unsigned int*>(&g_device_error) & DFLASH_DEVERR_ALLREDUCE) return 0u;
-    const unsigned long long t0 = globaltimer_ns();
-    while (true) {
-        v = ld_relaxed_sys_u64(p);
-        if ((uint32_t)(v >> 32) == e) return (uint32_t)v;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            atomicOr(&g_device_error, DFLASH_DEVERR_ALLREDUCE);
-            return 0u;
-        }
-        __nanosleep(32);
-    }
-}
-
 }  // namespace tp
 }  // namespace dflash
 

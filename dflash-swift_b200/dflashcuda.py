@@ -51,7 +51,7 @@ EXPORTED = (
     "dflash_stack_gated_norm", "dflash_stack_attn_prep", "dflash_stack_attn_decode",
     "dflash_stack_add_rmsnorm_reduce", "dflash_tp_exchange_bytes", "dflash_tp_exchange_alloc",
     "dflash_tp_exchange_free", "dflash_ipc_get_handle", "dflash_ipc_open_handle", "dflash_ipc_close_handle",
-    "dflash_tp_push", "dflash_qmm_ex", "dflash_accept",
+    "dflash_tp_push", "dflash_qmm_ex", "dflash_accept", "dflash_stack_gdn_conv_gates",
 )
 
 
@@ -105,6 +105,8 @@ def _load() -> ctypes.CDLL:
         "dflash_tp_push": ([_vp, ctypes.POINTER(_vp), _i, _i, _i, _i, _i, _vp], _i),
         "dflash_qmm_ex": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, ctypes.c_void_p, _vp], _i),
         "dflash_accept": ([_vp, _vp, _i, _vp, _vp, _vp], _i),
+        "dflash_stack_gdn_conv_gates": ([_vp, _i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
+                                        _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -567,3 +569,12 @@ def accept(keys, proposals, tokens=None, accepted=None, stream=None):
         accepted = torch.empty(1, dtype=torch.int32, device=keys.device)
     check(lib.dflash_accept(_ptr(keys), _ptr(proposals), drafts, _ptr(tokens), _ptr(accepted), _stream(stream)))
     return tokens, accepted
+
+
+def stack_gdn_conv_gates(x, window, weight, out, ab, a_log, dt_bias, alpha, beta, heads: int, dk: int, stream=None):
+    """Conv + SiLU + q/k normalisation + gates in one kernel; out [3, M, heads, dk]."""
+    M = x.shape[0]
+    check(lib.dflash_stack_gdn_conv_gates(_ptr(x), x.stride(0), _ptr(window), _ptr(weight), _ptr(out), _ptr(ab),
+                                          ab.stride(0), _ptr(a_log), _ptr(dt_bias), _ptr(alpha), _ptr(beta), M, heads,
+                                          dk, weight.shape[1], _stream(stream)))
+    return out

@@ -425,11 +425,11 @@ class VerifyStack:
         M, h, dk, dv = cfg.block, p.gdn_heads, cfg.gdn_dk, cfg.gdn_dv
         self._qmm(self.normed, L["in_proj"], self.gdn_proj)
         qkv = self.capture_qkv[gi]
-        dc.stack_conv_silu(self.gdn_proj, S["window"], L["conv"], qkv, channels=3 * h * dk, parts=3)
         q, k, v = qkv[0], qkv[1], qkv[2]
         ab = self.gdn_proj[:, 2 * h * dk + 2 * h * dv:]
         alpha, beta = self.capture_alpha[gi], self.capture_beta[gi]
-        dc.stack_gdn_gates(q, k, ab, L["a_log"], L["dt_bias"], alpha, beta)
+        dc.stack_gdn_conv_gates(self.gdn_proj, S["window"], L["conv"], qkv, ab, L["a_log"], L["dt_bias"], alpha, beta,
+                                h, dk)
         dc.gdn_step(S["snapshot"], self.state_out[gi], q, k, v, alpha, beta, out=self.gdn_o,
                     q_scale=1.0 / math.sqrt(dk))
         z = self.gdn_proj[:, 2 * h * dk + h * dv:]
@@ -485,7 +485,7 @@ class VerifyStack:
         for k in self.cfg.layer_kinds():
             n += 2  # two add_rmsnorm
             if k == "gdn":
-                n += 2 + 1 + 1 + 1 + 1 + 2  # in_proj, conv, gates, gdn_step, gated_norm, out_proj
+                n += 2 + 1 + 1 + 1 + 2  # in_proj, conv + gates, gdn_step, gated_norm, out_proj
             else:
                 n += 2 + 1 + 1 + 2  # qkv, prep, decode, o_proj
             n += 2 + 2  # gate_up, down (SwiGLU inside its prep; pushes inside the qmm epilogues)

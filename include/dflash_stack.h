@@ -38,6 +38,15 @@ int dflash_stack_gdn_gates(dflash_bf16* q, dflash_bf16* k, const dflash_bf16* ab
                            const float* dt_bias, float* alpha, float* beta, int M, int heads, int dk,
                            dflash_stream_t stream);
 
+/* dflash_stack_conv_silu (parts = 3) followed by dflash_stack_gdn_gates on its q and k, in
+ * one kernel with the same results: x rows hold the q|k|v channels at [0, 3 heads dk);
+ * y receives the three [M, heads dk] blocks (q, k normalised); ab, a_log, dt_bias, alpha,
+ * beta as for the gates.  dk in {32, 64, 128}, kc in 2..4. */
+int dflash_stack_gdn_conv_gates(const dflash_bf16* x, int ld, const dflash_bf16* window, const dflash_bf16* weight,
+                                dflash_bf16* y, const dflash_bf16* ab, int ld_ab, const float* a_log,
+                                const float* dt_bias, float* alpha, float* beta, int M, int heads, int dk, int kc,
+                                dflash_stream_t stream);
+
 /* out bf16 [M, heads * dv] = rmsnorm(o per head) * weight (bf16 [dv]) * silu(z); z has row
  * stride ld_z. */
 int dflash_stack_gated_norm(const dflash_bf16* o, const dflash_bf16* z, int ld_z, const dflash_bf16* weight,

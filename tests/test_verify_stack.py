@@ -203,6 +203,28 @@ def test_cuda_stack_tp1_matches_reference(cuda):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("heads,dk,kc,M", [(32, 128, 4, 8), (4, 64, 4, 16), (3, 32, 2, 1)])
+def test_conv_gates_kernel_equals_separate_kernels(dc, cuda, heads, dk, kc, M):
+    gen = torch.Generator(device=cuda).manual_seed(heads + dk)
+    C = 3 * heads * dk
+    x = torch.randn(M, C + 4 * heads * dk + 2 * heads, generator=gen, device=cuda).to(torch.bfloat16)
+    win = torch.randn(kc - 1, C, generator=gen, device=cuda).to(torch.bfloat16)
+    w = (0.5 * torch.randn(C, kc, generator=gen, device=cuda)).to(torch.bfloat16)
+    ab = x[:, C + heads * dk * 4 - 0:]
+    a_log = torch.randn(heads, generator=gen, device=cuda)
+    dt = torch.randn(heads, generator=gen, device=cuda)
+    want = torch.empty(3, M, heads, dk, dtype=torch.bfloat16, device=cuda)
+    al1, be1 = (torch.empty(M, heads, device=cuda) for _ in range(2))
+    dc.stack_conv_silu(x, win, w, want, channels=C, parts=3)
+    dc.stack_gdn_gates(want[0], want[1], ab, a_log, dt, al1, be1)
+    got = torch.empty_like(want)
+    al2, be2 = (torch.empty(M, heads, device=cuda) for _ in range(2))
+    dc.stack_gdn_conv_gates(x, win, w, got, ab, a_log, dt, al2, be2, heads, dk)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want) and torch.equal(al1, al2) and torch.equal(be1, be2)
+
+
+@pytest.mark.gpu
 def test_qmm_swiglu_input_equals_separate_silu_mul(dc, O, cuda):
     """dflash_qmm_ex with x_swiglu gives the same bits as dflash_stack_silu_mul followed by
     dflash_qmm (the down projection of the MLP)."""
