@@ -280,7 +280,7 @@ def run_ours(args):
             "e2e": {"value": round(world * bytes8 / (e2e["ms"] * 1e-3 / args.steps) / 1e9, 1), "unit": "GB/s",
                     "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
                     "us_per_step": round(e2e["ms"] * 1e3 / args.steps, 3),
-                    "path": "pinned host x -> dflash_qmm (C ABI via ctypes) -> pinned host y, per step"},
+                    "path": "pinned host x -> dflash_qmm (C ABI via ctypes) -> pinned host y, every step; steps alternate over two streams so copies overlap kernels"},
             "gpu_launches": KERNELS_PER_CALL * args.steps,
             "clocks": clocks,
             "parity_closeness_before_timing": err,
@@ -300,36 +300,49 @@ def gpu_ids(world):
 
 
 def e2e_through_abi(dc, dev, x, copies, args, world):
-    """Per step: pinned host x -> device, dflash_qmm through the C ABI, device y ->
-    pinned host; CUDA events around the K steps on the launching stream."""
+    """Per step: pinned host x -> device, dflash_qmm through the C ABI (ctypes, the
+    library's entry point itself), device y -> pinned host; CUDA events around the K
+    steps.  Steps alternate between two streams, each with its own device buffers,
+    workspace and host output, so one step's copies overlap another step's kernels, as
+    a serving host would pipeline consecutive requests."""
+    import ctypes
     import torch
-    stream = torch.cuda.Stream(dev)
+    streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
     x_h = torch.from_numpy(np.ascontiguousarray(x[:M]).view(np.int16)).view(torch.bfloat16).pin_memory()
-    y_h = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
-    x_d = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
-    y_d = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-    ws = dc.Workspace(dc.qmm_workspace_bytes(M, N, K, GROUP, BITS), dev)
+    lanes = []
+    for st in streams:
+        lane = {"x_d": torch.empty((M, K), dtype=torch.bfloat16, device=dev),
+                "y_d": torch.empty((M, N), dtype=torch.bfloat16, device=dev),
+                "y_h": torch.empty((M, N), dtype=torch.bfloat16).pin_memory(),
+                "ws": dc.Workspace(dc.qmm_workspace_bytes(M, N, K, GROUP, BITS), dev), "stream": st}
+        lane["args"] = [(lane["x_d"].data_ptr(), w.data_ptr(), s_.data_ptr(), b.data_ptr(), lane["y_d"].data_ptr(), M,
+                         N, K, GROUP, BITS, lane["ws"].buf.data_ptr(), ctypes.c_size_t(lane["ws"].nbytes),
+                         st.cuda_stream) for (w, s_, b) in copies]
+        lanes.append(lane)
     R = len(copies)
 
     def step(i):
-        w, s, b = copies[i % R]
-        x_d.copy_(x_h, non_blocking=True)
-        dc.qmm(x_d, w, s, b, GROUP, BITS, out=y_d, workspace=ws, stream=stream)
-        y_h.copy_(y_d, non_blocking=True)
+        lane = lanes[i & 1]
+        with torch.cuda.stream(lane["stream"]):
+            lane["x_d"].copy_(x_h, non_blocking=True)
+            dc.check(dc.lib.dflash_qmm(*lane["args"][i % R]))
+            lane["y_h"].copy_(lane["y_d"], non_blocking=True)
 
-    with torch.cuda.stream(stream):
-        for i in range(min(args.warmup, 200)):
-            step(i)
-    stream.synchronize()
+    for i in range(min(args.warmup, 200)):
+        step(i)
+    torch.cuda.synchronize(dev)
     steps = args.steps
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        t0.record(stream)
-        for i in range(steps):
-            step(i)
-        t1.record(stream)
-    stream.synchronize()
+    t0.record(streams[0])
+    streams[1].wait_event(t0)
+    for i in range(steps):
+        step(i)
+    done = torch.cuda.Event()
+    done.record(streams[1])
+    streams[0].wait_event(done)
+    t1.record(streams[0])
+    torch.cuda.synchronize(dev)
     return {"ms": t0.elapsed_time(t1), "h2d": M * K * 2, "d2h": M * N * 2}
 
 

@@ -1290,8 +1290,38 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
 
     int dev = 0;
     DFLASH_CUDA_TRY(cudaGetDevice(&dev));
+    // The plan and the three tensor maps depend only on the device, the shape and the
+    // weight / scale / bias addresses: a small direct-mapped cache keeps them, so a call
+    // on weights seen before costs no planning and no tensor-map encoding on the host.
+    struct Entry {
+        bool valid;
+        int dev, N, K;
+        const void *w, *s, *b;
+        Plan pl;
+        CUtensorMap tm_w, tm_s, tm_b;
+    };
+    constexpr int kEntries = 512;
+    static std::mutex cache_mu;
+    static Entry cache[kEntries];
+    const size_t h = (reinterpret_cast<uintptr_t>(w) >> 8) ^ ((size_t)s.N * 2654435761u) ^ ((size_t)s.K * 40503u) ^
+                     ((size_t)dev << 7);
+    Entry& slot = cache[h % kEntries];
+    Plan pl;
+    CUtensorMap tm_w, tm_s, tm_b;
+    bool hit = false;
+    {
+        std::lock_guard<std::mutex> lock(cache_mu);
+        if (slot.valid && slot.dev == dev && slot.N == s.N && slot.K == s.K && slot.w == w && slot.s == scales &&
+            slot.b == biases) {
+            pl = slot.pl;
+            tm_w = slot.tm_w;
+            tm_s = slot.tm_s;
+            tm_b = slot.tm_b;
+            hit = true;
+        }
+    }
     const int* cmax = max_clusters<C>(dev);
-    const Plan pl = make_plan<C>(s, cmax);
+    if (!hit) pl = make_plan<C>(s, cmax);
     static const bool log_plan = getenv("DFLASH_QMM_LOG_PLAN") != nullptr;
     if (log_plan)  // diagnostics: the plan of every launch on stderr
         fprintf(stderr,
@@ -1302,22 +1332,35 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
     if (pl.NS < 2) return fail(DFLASH_ERR_UNSUPPORTED, "qmm: no shared-memory plan for N=%d K=%d", s.N, s.K);
     const int GT = s.K / s.group;
 
-    CUtensorMap tm_w, tm_s, tm_b;
-    int st;
-    const uint64_t words = (uint64_t)s.K * s.bits / 32;
-    st = encode_tensor_map_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, words, (uint64_t)s.N, words * 4,
-                              kRowBytes / 4, pl.R, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    if constexpr (C::STMA) {
-        st = encode_tensor_map_2d(&tm_s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, scales, (uint64_t)GT, (uint64_t)s.N,
-                                  (uint64_t)GT * 2, 8, pl.R, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!hit) {
+        int st;
+        const uint64_t words = (uint64_t)s.K * s.bits / 32;
+        st = encode_tensor_map_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, words, (uint64_t)s.N, words * 4,
+                                  kRowBytes / 4, pl.R, CU_TENSOR_MAP_SWIZZLE_128B);
         if (st) return st;
-        st = encode_tensor_map_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, biases, (uint64_t)GT, (uint64_t)s.N,
-                                  (uint64_t)GT * 2, 8, pl.R, CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (st) return st;
-    } else {
-        tm_s = tm_w;
-        tm_b = tm_w;
+        if constexpr (C::STMA) {
+            st = encode_tensor_map_2d(&tm_s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, scales, (uint64_t)GT, (uint64_t)s.N,
+                                      (uint64_t)GT * 2, 8, pl.R, CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (st) return st;
+            st = encode_tensor_map_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, biases, (uint64_t)GT, (uint64_t)s.N,
+                                      (uint64_t)GT * 2, 8, pl.R, CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (st) return st;
+        } else {
+            tm_s = tm_w;
+            tm_b = tm_w;
+        }
+        std::lock_guard<std::mutex> lock(cache_mu);
+        slot.valid = true;
+        slot.dev = dev;
+        slot.N = s.N;
+        slot.K = s.K;
+        slot.w = w;
+        slot.s = scales;
+        slot.b = biases;
+        slot.pl = pl;
+        slot.tm_w = tm_w;
+        slot.tm_s = tm_s;
+        slot.tm_b = tm_b;
     }
 
     Params p;
