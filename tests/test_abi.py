@@ -186,3 +186,41 @@ def test_stack_argument_errors(dc):
     assert L.dflash_stack_silu_mul(FAKE, None, 8, 64, None) == 1
     assert L.dflash_stack_gdn_gates(FAKE, FAKE, FAKE, 8, FAKE, FAKE, None, FAKE, 8, 4, 128, None) == 1
     assert L.dflash_stack_gated_norm(FAKE, FAKE, 8, FAKE, FAKE, 8, 0, 128, 1e-6, None) == 1
+
+
+def test_qmm_ex_tp_and_accept_argument_errors(dc):
+    import ctypes
+    L = dc.lib
+    ws = dc.qmm_workspace_bytes(8, 1024, 1024, 64, 4)
+    bases = (ctypes.c_void_p * 2)(FAKE, FAKE + 0x1000)
+
+    def ex(**kw):
+        o = dc.QmmOptions(kw.get("swiglu", 0), kw.get("push", 0), kw.get("rank", 0), kw.get("world", 1),
+                          kw.get("set", 0), ctypes.cast(bases, ctypes.c_void_p) if kw.get("bases", True) else None,
+                          kw.get("keys", None))
+        return L.dflash_qmm_ex(FAKE, FAKE, FAKE, FAKE, kw.get("y", FAKE), 8, kw.get("N", 1024), 1024, 64, 4, FAKE, ws,
+                               ctypes.addressof(o), None)
+
+    assert ex(push=1, world=3, rank=0) == 1            # bases hold fewer entries than world is not checkable,
+    assert ex(push=1, world=2, rank=2) == 1            # but rank outside world is
+    assert ex(push=1, world=2, set=2) == 1
+    assert ex(push=1, world=2, bases=False) == 1
+    assert ex(push=1, world=2, N=1020) == 2            # pushing needs N % 8 == 0
+    assert ex(push=1, world=2, keys=FAKE) == 1         # push and argmax are exclusive
+    assert ex(keys=FAKE + 4) == 3                      # keys 8-byte aligned
+    assert ex(y=0) == 1                                # no destination at all
+    assert L.dflash_qmm_ex(FAKE, FAKE, FAKE, FAKE, FAKE, 8, 1024, 1020, 4, 4, FAKE, ws, None, None) == 2
+    # accept
+    assert L.dflash_accept(None, FAKE, 7, FAKE, FAKE, None) == 1
+    assert L.dflash_accept(FAKE, None, 7, FAKE, FAKE, None) == 1
+    assert L.dflash_accept(FAKE, FAKE, -1, FAKE, FAKE, None) == 1
+    # exchange
+    assert L.dflash_tp_exchange_bytes(9, 8, 5120) == 0 and L.dflash_tp_exchange_bytes(0, 8, 5120) == 0
+    assert L.dflash_tp_exchange_bytes(8, 8, 5120) == 256 + 2 * 8 * 8 * 5120 // 2 * 8
+    assert L.dflash_tp_push(FAKE, bases, 2, 2, 8, 5120, 0, None) == 1
+    assert L.dflash_tp_push(FAKE, bases, 0, 2, 8, 5121, 0, None) == 3
+    assert L.dflash_tp_push(FAKE + 2, bases, 0, 2, 8, 5120, 0, None) == 3
+    assert L.dflash_stack_add_rmsnorm_reduce(FAKE, FAKE, 2, 2, FAKE, FAKE, 8, 5120, 1e-6, None) == 1
+    assert L.dflash_stack_add_rmsnorm_reduce(FAKE, FAKE, 2, 0, FAKE, FAKE, 8, 5122, 1e-6, None) == 2
+    assert L.dflash_stack_gdn_conv_gates(FAKE, 144, FAKE, FAKE, FAKE, FAKE, 8, FAKE, FAKE, FAKE, FAKE, 8, 1, 48, 4,
+                                         None) == 2
