@@ -201,8 +201,7 @@ def test_qmm_ex_tp_and_accept_argument_errors(dc):
         return L.dflash_qmm_ex(FAKE, FAKE, FAKE, FAKE, kw.get("y", FAKE), 8, kw.get("N", 1024), 1024, 64, 4, FAKE, ws,
                                ctypes.addressof(o), None)
 
-    assert ex(push=1, world=3, rank=0) == 1            # bases hold fewer entries than world is not checkable,
-    assert ex(push=1, world=2, rank=2) == 1            # but rank outside world is
+    assert ex(push=1, world=2, rank=2) == 1            # rank outside world
     assert ex(push=1, world=2, set=2) == 1
     assert ex(push=1, world=2, bases=False) == 1
     assert ex(push=1, world=2, N=1020) == 2            # pushing needs N % 8 == 0
