@@ -142,19 +142,21 @@ def tiny_tp1_reference():
     return stack_ref.forward(cfg, plan, w, st, vs.make_block(cfg, 0, "cpu"))
 
 
-def test_tp2_gloo_matches_tp1_and_dropped_reduce_diverges(tmp_path, tiny_tp1_reference):
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_gloo_matches_tp1_and_dropped_reduce_diverges(tmp_path, tiny_tp1_reference, world):
+    """TP=2, and TP=4 where the 2 kv heads are replicated over pairs of ranks."""
     import stack_workers
     ref = tiny_tp1_reference["out"].numpy()
     results = {}
     for drop in (False, True):
-        out = tmp_path / f"tp2_drop{int(drop)}.pt"
+        out = tmp_path / f"tp{world}_drop{int(drop)}.pt"
         port = free_port()
-        codes = _run_ranks(stack_workers.gloo_reference_rank, 2,
-                           lambda r: (r, 2, port, str(out), asdict(vs.TINY), drop))
-        assert codes == [0, 0], codes
+        codes = _run_ranks(stack_workers.gloo_reference_rank, world,
+                           lambda r: (r, world, port, str(out), asdict(vs.TINY), drop))
+        assert codes == [0] * world, codes
         results[drop] = torch.load(out)["out"].numpy()
     err, err_drop = closeness(results[False], ref), closeness(results[True], ref)
-    print(f"TP=2 vs TP=1: {err:.3e}; without the all-reduce: {err_drop:.3e}")
+    print(f"TP={world} vs TP=1: {err:.3e}; without the all-reduce: {err_drop:.3e}")
     assert err <= 3e-2
     assert err_drop > max(0.05, 10 * err)
 
