@@ -95,6 +95,9 @@ struct Cfg {
     static constexpr int T_BYTES = kKLanes * SEGS * MR * 16;
     static constexpr int PKT = X_BYTES + T_BYTES;         // packet bytes per stage
     static constexpr int XREGS = UNIT_B / 4 / 4;          // 32-bit B registers per lane per unit: 8 or 4
+    // 16-row blocks per consumer warp and tile: 4 (tiles up to 256 rows), 2 with two
+    // n-tiles (M > 8), whose doubled x fragments and accumulators would not fit 4
+    static constexpr int MAXB = NT == 2 ? 2 : 4;
     static_assert(PKT % 16 == 0, "bulk copies move multiples of 16 bytes");
     static_assert(GPS >= 1 && 8 % GPS == 0, "scale boxes hold 8 groups");
 };
@@ -526,7 +529,7 @@ template <class C, int NB>
 __device__ __forceinline__ void compute_stage(const StageRegs<C, NB>& R, const StageCtx& x, const Params& p,
                                               const LaneOfs& o, int kl, int qd, int pr, uint32_t mag1024,
                                               uint32_t mag64, uint32_t k65536, int lane, uint64_t* release,
-                                              float (&acc)[4][C::NT][4]) {
+                                              float (&acc)[C::MAXB][C::NT][4]) {
 #pragma unroll
     for (int nt = 0; nt < C::NT; ++nt) {
 #pragma unroll
@@ -625,7 +628,7 @@ __device__ __forceinline__ void run_tile(const Params& p, Bars* bars, volatile i
                                          uint32_t sbring, const LaneOfs& o, int kl, int qd, int pr, int lane,
                                          int s_beg, int s_end, int tile_row0, uint32_t mag1024, uint32_t mag64,
                                          uint32_t k65536, int& slot, int& ph, int& qslot, int& qph,
-                                         float (&acc)[4][C::NT][4]) {
+                                         float (&acc)[C::MAXB][C::NT][4]) {
     const uint32_t wbytes = (uint32_t)p.R * kRowBytes;
     StageCtx cx;
     cx.tile_row0 = tile_row0;
@@ -815,21 +818,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         int slot = 0, ph = 0, qslot = 0, qph = 0, tt = 0;
         for (int t = cid; t < p.ntiles; t += ncl, ++tt) {
-            float acc[4][C::NT][4];
+            float acc[C::MAXB][C::NT][4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < C::MAXB; ++i)
 #pragma unroll
                 for (int nt = 0; nt < C::NT; ++nt)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) acc[i][nt][e] = 0.f;
             switch (nblk) {
                 case 4:
-                    run_tile<C, 4>(p, bars, abort, ring, sbring, lo, kl, qd, pr, lane, s_beg, s_end, t * p.R, mag1024,
-                                   mag64, k65536, slot, ph, qslot, qph, acc);
+                    if constexpr (C::MAXB >= 4)
+                        run_tile<C, 4>(p, bars, abort, ring, sbring, lo, kl, qd, pr, lane, s_beg, s_end, t * p.R,
+                                       mag1024, mag64, k65536, slot, ph, qslot, qph, acc);
                     break;
                 case 3:
-                    run_tile<C, 3>(p, bars, abort, ring, sbring, lo, kl, qd, pr, lane, s_beg, s_end, t * p.R, mag1024,
-                                   mag64, k65536, slot, ph, qslot, qph, acc);
+                    if constexpr (C::MAXB >= 3)
+                        run_tile<C, 3>(p, bars, abort, ring, sbring, lo, kl, qd, pr, lane, s_beg, s_end, t * p.R,
+                                       mag1024, mag64, k65536, slot, ph, qslot, qph, acc);
                     break;
                 case 2:
                     run_tile<C, 2>(p, bars, abort, ring, sbring, lo, kl, qd, pr, lane, s_beg, s_end, t * p.R, mag1024,
@@ -851,7 +856,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (kl & 1) {
                 float* buf = kl == 1 ? bufa : bufb;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
+                for (int i = 0; i < C::MAXB; ++i) {
                     if (i >= nblk) break;
 #pragma unroll
                     for (int h = 0; h < 2; ++h)
@@ -865,7 +870,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!(kl & 1)) {
                 float* buf = kl == 0 ? bufa : bufb;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
+                for (int i = 0; i < C::MAXB; ++i) {
                     if (i >= nblk) break;
 #pragma unroll
                     for (int h = 0; h < 2; ++h)
@@ -891,7 +896,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (kl == 0) {
                     const int peer0 = rank == 0 ? p.nb0 : 0;  // first block the peer writes
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
+                    for (int i = 0; i < C::MAXB; ++i) {
                         if (i >= nblk) break;
 #pragma unroll
                         for (int h = 0; h < 2; ++h)
@@ -911,7 +916,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t peer_recv = map_to_rank(smem_u32(recv), peer);
                         const uint32_t peer_bar = map_to_rank(smem_u32(&bars->xfull), peer);
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
+                        for (int i = 0; i < C::MAXB; ++i) {
                             if (i >= nblk) break;
                             const int b = qd + 4 * i;
                             if (b >= own0 && b < own1) continue;
@@ -927,7 +932,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     // the owned rows: rank 0's partial first, then rank 1's, rounded once to bf16
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
+                    for (int i = 0; i < C::MAXB; ++i) {
                         if (i >= nblk) break;
                         const int b = qd + 4 * i;
                         if (b < own0 || b >= own1) continue;
@@ -967,7 +972,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 stg = reinterpret_cast<uint16_t*>(bufb);
                 if (kl == 0) {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
+                    for (int i = 0; i < C::MAXB; ++i) {
                         if (i >= nblk) break;
 #pragma unroll
                         for (int h = 0; h < 2; ++h)
@@ -1166,7 +1171,7 @@ Plan make_plan(const Shape& s, const int* cmax_by_lg) {
         const int sp = (pl.S + cs - 1) / cs;
         for (int T = 1; T <= 8; ++T) {
             int nb = (NB + cmax * T - 1) / (cmax * T);
-            if (nb > kMaxTileBlocks) nb = kMaxTileBlocks;
+            if (nb > kMaxTileBlocks / 4 * C::MAXB) nb = kMaxTileBlocks / 4 * C::MAXB;
             if (nb < 1) nb = 1;
             const int ntiles = (s.N + 16 * nb - 1) / (16 * nb);
             const int ncl = ntiles < cmax ? ntiles : cmax;
