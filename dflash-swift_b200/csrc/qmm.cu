@@ -373,6 +373,7 @@ struct Params {
     // argmax: instead of y, fold each row's (largest bf16 output, lowest index) into
     // argmax_keys[m] with a 64-bit atomic max (zeroed by the prep kernel)
     unsigned long long* argmax_keys;
+    int argmax_base;  // added to the output index in the keys (a vocabulary shard's first row)
     uint32_t stage_bytes, sb_bytes, red_off, red_bytes, recv_off, bar_off;
 };
 
@@ -1044,7 +1045,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (n >= p.N) break;
                         const uint32_t u = static_cast<uint32_t>(stg[m * own_rows + r]) << 16;
                         const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // order of the float
-                        const unsigned long long key = (static_cast<unsigned long long>(ord) << 32) | (~static_cast<uint32_t>(n));
+                        const unsigned long long key =
+                            (static_cast<unsigned long long>(ord) << 32) | (~static_cast<uint32_t>(n + p.argmax_base));
                         best = key > best ? key : best;
                     }
 #pragma unroll
@@ -1110,6 +1112,7 @@ struct Options {
     int rank = 0, world = 1, set = 0;
     tp::Bases xb = {};
     unsigned long long* argmax_keys = nullptr;  // y is reduced to per-row argmax keys instead
+    int argmax_base = 0;
 };
 
 struct Plan {
@@ -1392,6 +1395,7 @@ int launch(const Shape& s, const dflash_bf16* x, const uint32_t* w, const dflash
     p.set = o.set;
     p.xb = o.xb;
     p.argmax_keys = o.argmax_keys;
+    p.argmax_base = o.argmax_base;
     p.stage_bytes = pl.stage_bytes;
     p.sb_bytes = pl.sb_bytes;
     p.red_off = pl.red_off;
@@ -1534,6 +1538,9 @@ extern "C" int dflash_qmm_ex(const dflash_bf16* x, const uint32_t* w, const dfla
         o.swiglu = opts->x_swiglu != 0;
         o.push = opts->push != 0;
         o.argmax_keys = reinterpret_cast<unsigned long long*>(opts->argmax_keys);
+        o.argmax_base = opts->argmax_index_base;
+        if (opts->argmax_index_base < 0)
+            return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_qmm_ex: negative argmax_index_base");
     }
     if (o.push && o.argmax_keys)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_qmm_ex: push and argmax are exclusive");

@@ -670,6 +670,42 @@ __global__ void accept_kernel(const unsigned long long* __restrict__ keys, const
     if (lane == 0) *accepted = run;
 }
 
+// dflash_accept over the ranks' keys in an exchange buffer laid out for [M, 4] bf16
+// (8 bytes of a key = two data words: low then high half).  One warp; lane i < M takes
+// row i's key from every rank, keeps the largest, then the leading run of matches as in
+// accept_kernel.  Records the exchange as consumed.
+__global__ void accept_reduce_kernel(void* xbase, int world, int set, const int32_t* __restrict__ proposals,
+                                     int drafts, int32_t* __restrict__ tokens, int32_t* __restrict__ accepted) {
+    chain_in();
+    tp::Header* hdr = static_cast<tp::Header*>(xbase);
+    const uint32_t e = hdr->next[set];
+    const int M = drafts + 1, lane = threadIdx.x;
+    int run = 0;
+    for (int base = 0; base <= drafts; base += 32) {
+        const int i = base + lane;
+        int32_t tok = 0;
+        if (i <= drafts) {
+            unsigned long long best = 0ull;
+            for (int r = 0; r < world; ++r) {
+                const uint64_t* src = tp::slot_ptr(xbase, world, M, 4, set, r) + 2 * (size_t)i;
+                const uint32_t lo = tp::wait_word(src, e), hi = tp::wait_word(src + 1, e);
+                const unsigned long long key = (static_cast<unsigned long long>(hi) << 32) | lo;
+                best = key > best ? key : best;
+            }
+            tok = (int32_t)(~(uint32_t)(best & 0xffffffffull));
+            tokens[i] = tok;
+        }
+        const bool miss = i < drafts && proposals[i] != tok;
+        const unsigned mm = __ballot_sync(0xffffffffu, miss);
+        const int valid = min(32, drafts - base);
+        if (run == base) run += mm ? min(__ffs(mm) - 1, valid) : max(valid, 0);
+    }
+    if (lane == 0) {
+        *accepted = run;
+        hdr->seq[set] = e;
+    }
+}
+
 inline unsigned grid_for(size_t n, int block) {
     const size_t g = (n + block - 1) / block;
     return (unsigned)(g < 4096 ? (g > 0 ? g : 1) : 4096);
@@ -883,5 +919,15 @@ extern "C" int dflash_stack_gdn_conv_gates(const dflash_bf16* x, int ld, const d
     DFLASH_CG_CASE(4, 1) DFLASH_CG_CASE(4, 2) DFLASH_CG_CASE(4, 4)
 #undef DFLASH_CG_CASE
     DFLASH_CUDA_TRY(e);
+    return DFLASH_OK;
+}
+
+extern "C" int dflash_accept_reduce(void* exchange, int world, int set, const int32_t* proposals, int drafts,
+                                    int32_t* target_tokens, int32_t* accepted, dflash_stream_t stream) {
+    if (!exchange || world < 1 || world > tp::kMaxRanks || (set != 0 && set != 1) || (!proposals && drafts > 0) ||
+        !target_tokens || !accepted || drafts < 0)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_accept_reduce: bad arguments");
+    DFLASH_CUDA_TRY(launch_chained(stack::accept_reduce_kernel, dim3(1), dim3(32), 0, as_stream(stream), 1, exchange,
+                                   world, set, proposals, drafts, target_tokens, accepted));
     return DFLASH_OK;
 }

@@ -52,6 +52,7 @@ EXPORTED = (
     "dflash_stack_add_rmsnorm_reduce", "dflash_tp_exchange_bytes", "dflash_tp_exchange_alloc",
     "dflash_tp_exchange_free", "dflash_ipc_get_handle", "dflash_ipc_open_handle", "dflash_ipc_close_handle",
     "dflash_tp_push", "dflash_qmm_ex", "dflash_accept", "dflash_stack_gdn_conv_gates",
+    "dflash_accept_reduce",
 )
 
 
@@ -105,6 +106,7 @@ def _load() -> ctypes.CDLL:
         "dflash_tp_push": ([_vp, ctypes.POINTER(_vp), _i, _i, _i, _i, _i, _vp], _i),
         "dflash_qmm_ex": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, ctypes.c_void_p, _vp], _i),
         "dflash_accept": ([_vp, _vp, _i, _vp, _vp, _vp], _i),
+        "dflash_accept_reduce": ([_vp, _i, _i, _vp, _i, _vp, _vp, _vp], _i),
         "dflash_stack_gdn_conv_gates": ([_vp, _i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
                                         _i),
     }
@@ -524,12 +526,13 @@ def stack_add_rmsnorm_reduce(resid, exchange: PeerExchange, set_: int, weight, o
 class QmmOptions(ctypes.Structure):
     """dflash_qmm_options (include/dflash_stack.h)."""
     _fields_ = [("x_swiglu", ctypes.c_int), ("push", ctypes.c_int), ("rank", ctypes.c_int), ("world", ctypes.c_int),
-                ("set", ctypes.c_int), ("bases", ctypes.c_void_p), ("argmax_keys", ctypes.c_void_p)]
+                ("set", ctypes.c_int), ("bases", ctypes.c_void_p), ("argmax_keys", ctypes.c_void_p),
+                ("argmax_index_base", ctypes.c_int)]
 
 
 def qmm_ex(x, w, scales, biases, group_size: int, bits: int, out=None, workspace: Optional[Workspace] = None,
            swiglu: bool = False, exchange: Optional[PeerExchange] = None, set_: int = 0, argmax_keys=None,
-           stream=None):
+           argmax_index_base: int = 0, stream=None):
     """dflash_qmm_ex: with swiglu, x is [M, 2K] = [gate | up]; with an exchange, the result
     is pushed to every rank's exchange slot (set `set_`) instead of written to `out`; with
     argmax_keys (int64 [M] on the device) each row is reduced to its argmax key instead."""
@@ -539,7 +542,7 @@ def qmm_ex(x, w, scales, biases, group_size: int, bits: int, out=None, workspace
     N = w.shape[0]
     if out is None and exchange is None and argmax_keys is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
-    o = QmmOptions(int(bool(swiglu)), 0, 0, 1, 0, None, _ptr(argmax_keys))
+    o = QmmOptions(int(bool(swiglu)), 0, 0, 1, 0, None, _ptr(argmax_keys), int(argmax_index_base))
     if exchange is not None:
         o.push, o.rank, o.world, o.set = 1, exchange.rank, exchange.world, int(set_)
         o.bases = ctypes.cast(exchange.bases, ctypes.c_void_p)
@@ -550,12 +553,15 @@ def qmm_ex(x, w, scales, biases, group_size: int, bits: int, out=None, workspace
     return out
 
 
-def lm_head_argmax(x, w, scales, biases, group_size: int, bits: int, keys=None, workspace=None, stream=None):
-    """Argmax keys of x . deq(W)^T per row without writing the logits (int64 [M])."""
+def lm_head_argmax(x, w, scales, biases, group_size: int, bits: int, keys=None, workspace=None, index_base: int = 0,
+                   stream=None):
+    """Argmax keys of x . deq(W)^T per row without writing the logits (int64 [M]); with
+    index_base, W is a vocabulary shard starting at that row."""
     import torch
     if keys is None:
         keys = torch.empty(x.shape[0], dtype=torch.int64, device=x.device)
-    qmm_ex(x, w, scales, biases, group_size, bits, workspace=workspace, argmax_keys=keys, stream=stream)
+    qmm_ex(x, w, scales, biases, group_size, bits, workspace=workspace, argmax_keys=keys,
+           argmax_index_base=index_base, stream=stream)
     return keys
 
 
@@ -578,3 +584,17 @@ def stack_gdn_conv_gates(x, window, weight, out, ab, a_log, dt_bias, alpha, beta
                                           ab.stride(0), _ptr(a_log), _ptr(dt_bias), _ptr(alpha), _ptr(beta), M, heads,
                                           dk, weight.shape[1], _stream(stream)))
     return out
+
+
+def accept_reduce(exchange: PeerExchange, set_: int, proposals, tokens=None, accepted=None, stream=None):
+    """dflash_accept_reduce over the ranks' keys pushed into `exchange` (laid out for [M, 4])."""
+    import torch
+    drafts = proposals.shape[0]
+    dev = proposals.device
+    if tokens is None:
+        tokens = torch.empty(drafts + 1, dtype=torch.int32, device=dev)
+    if accepted is None:
+        accepted = torch.empty(1, dtype=torch.int32, device=dev)
+    check(lib.dflash_accept_reduce(exchange.ptr, exchange.world, int(set_), _ptr(proposals), drafts, _ptr(tokens),
+                                   _ptr(accepted), _stream(stream)))
+    return tokens, accepted

@@ -29,7 +29,7 @@ as its parts, whose rows are concatenated in the order listed):
                       .self_attn.o_proj, .self_attn.q_norm.weight, .self_attn.k_norm.weight
   every layer:        .mlp.gate_up_proj          = [gate | up]  (or gate_proj, up_proj)
                       .mlp.down_proj
-  model.norm.weight
+  model.norm.weight, lm_head (quantized, [vocab, hidden]; sharded by vocabulary rows)
 """
 from __future__ import annotations
 
@@ -246,7 +246,9 @@ def stack_from_checkpoint(cfg, plan, config: dict, tensors: Dict[str, torch.Tens
             elif isinstance(v, vs.Quant):
                 L[k] = vs.Quant(v.w.to(dev), v.scales.to(dev), v.biases.to(dev), v.group, v.bits)
         layers.append(L)
-    return {"layers": layers, "final_norm": get("model.norm.weight").to(torch.bfloat16).to(dev)}
+    head = quantized_layer(tensors, config, "lm_head").rows([(plan.vocab0, plan.vocab0 + plan.vocab)])
+    head = vs.Quant(head.w.to(dev), head.scales.to(dev), head.biases.to(dev), head.group, head.bits)
+    return {"layers": layers, "final_norm": get("model.norm.weight").to(torch.bfloat16).to(dev), "lm_head": head}
 
 
 def save_stack_checkpoint(directory, cfg, weights: dict, shard_bytes: int = 1 << 30) -> None:
@@ -275,6 +277,7 @@ def save_stack_checkpoint(directory, cfg, weights: dict, shard_bytes: int = 1 <<
             elif k in plain:
                 tensors[f"{pre}.{plain[k]}"] = v
     tensors["model.norm.weight"] = weights["final_norm"]
+    put_quant("lm_head", weights["lm_head"])
     config = {"model_type": "dflash_verify_stack", "hidden_size": cfg.hidden, "num_hidden_layers": cfg.layers,
               "intermediate_size": cfg.intermediate, "full_attention_interval": cfg.attn_interval,
               "linear_num_value_heads": cfg.gdn_heads, "linear_num_key_heads": cfg.gdn_heads,

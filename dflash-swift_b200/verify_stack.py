@@ -70,6 +70,7 @@ class StackConfig:
     bits: int = 4
     context: int = 1024         # tokens already in each attention cache
     block: int = 8              # M: rows verified per forward
+    vocab: int = 248320         # LM head rows (sharded by vocabulary over the ranks)
 
     @property
     def max_len(self) -> int:
@@ -86,7 +87,7 @@ class StackConfig:
 CONFIG4 = StackConfig()
 # A small stack of the same structure for parity tests (3 GDN + 1 attention layers).
 TINY = StackConfig(layers=4, hidden=256, intermediate=512, gdn_heads=4, gdn_dk=64, gdn_dv=64, attn_heads=4,
-                   kv_heads=2, head_dim=64, rotary_dim=64, rope_theta=1.0e4, context=24, block=8)
+                   kv_heads=2, head_dim=64, rotary_dim=64, rope_theta=1.0e4, context=24, block=8, vocab=1024)
 
 
 # ----------------------------------------------------------------------------- shard plan
@@ -103,6 +104,8 @@ class ShardPlan:
     kv_head0: int
     inter: int              # MLP intermediate units on this rank
     inter0: int
+    vocab: int = 0          # LM head rows on this rank
+    vocab0: int = 0
 
 
 def shard_plan(cfg: StackConfig, rank: int, world: int) -> ShardPlan:
@@ -136,7 +139,10 @@ def shard_plan(cfg: StackConfig, rank: int, world: int) -> ShardPlan:
     for name, k in (("gdn out_proj", gh * cfg.gdn_dv), ("o_proj", ah * cfg.head_dim), ("down", inter)):
         if k % cfg.group:
             raise ValueError(f"{name} shard K={k} is not a multiple of group {cfg.group}")
-    return ShardPlan(rank, world, gh, rank * gh, ah, rank * ah, kvh, kv0, inter, rank * inter)
+    if cfg.vocab % world:
+        raise ValueError(f"vocab={cfg.vocab} does not split over {world} ranks")
+    vr = cfg.vocab // world
+    return ShardPlan(rank, world, gh, rank * gh, ah, rank * ah, kvh, kv0, inter, rank * inter, vr, rank * vr)
 
 
 def _ranges_gdn_in(cfg: StackConfig, p: ShardPlan):
@@ -258,7 +264,8 @@ def build_rank_weights(cfg: StackConfig, plan: ShardPlan, seed: int, device) -> 
         L["down"] = random_quant(g(li, 6), H, I, G, B, dev).cols(plan.inter0, plan.inter0 + plan.inter)
         layers.append(L)
     final_norm = _norm_weight(g(cfg.layers, 0), H, dev)
-    return {"layers": layers, "final_norm": final_norm}
+    lm_head = random_quant(g(cfg.layers, 1), cfg.vocab, H, G, B, dev).rows([(plan.vocab0, plan.vocab0 + plan.vocab)])
+    return {"layers": layers, "final_norm": final_norm, "lm_head": lm_head}
 
 
 def build_rank_state(cfg: StackConfig, plan: ShardPlan, seed: int, device) -> dict:
@@ -335,19 +342,22 @@ class VerifyStack:
         self.allreduce = allreduce if world > 1 else "none"
         self.exchange = None
         self._set = 0
+        self.key_exchange = None
         if self.allreduce == "peer":
-            self._connect_exchange(rank)
+            self.exchange = self._connect_exchange(rank, self.cfg.hidden)
+            self.key_exchange = self._connect_exchange(rank, 4)  # the LM head's argmax keys, 8 bytes a row
 
-    def _connect_exchange(self, rank):
-        """Allocate this rank's exchange buffer, swap IPC handles with the other ranks and
-        map theirs; the barrier ensures every buffer is zeroed before anyone pushes."""
-        ex = self.dc.PeerExchange(self.world, self.cfg.block, self.cfg.hidden)
+    def _connect_exchange(self, rank, H):
+        """Allocate this rank's exchange buffer for [block, H], swap IPC handles with the
+        other ranks and map theirs; the barrier ensures every buffer is zeroed before
+        anyone pushes."""
+        ex = self.dc.PeerExchange(self.world, self.cfg.block, H)
         handles = [None] * self.world
         torch.distributed.all_gather_object(handles, ex.handle(), group=self.pg)
         ex.connect(rank, handles)
         torch.cuda.synchronize(self.device)
         torch.distributed.barrier(group=self.pg)
-        self.exchange = ex
+        return ex
 
     def close(self):
         """Unmap the peers' exchange buffers and free this rank's (after a barrier, so no
@@ -356,7 +366,8 @@ class VerifyStack:
             torch.cuda.synchronize(self.device)
             torch.distributed.barrier(group=self.pg)
             self.exchange.close()
-            self.exchange = None
+            self.key_exchange.close()
+            self.exchange = self.key_exchange = None
 
     def _alloc(self):
         cfg, p, dev = self.cfg, self.plan, self.device
@@ -367,6 +378,9 @@ class VerifyStack:
         self.normed = torch.empty(M, H, **bf)
         self.delta = torch.zeros(M, H, **bf)
         self.out = torch.empty(M, H, **bf)
+        self.keys = torch.empty(M, dtype=torch.int64, device=dev)
+        self.tokens = torch.empty(M, dtype=torch.int32, device=dev)
+        self.accepted = torch.empty(1, dtype=torch.int32, device=dev)
         h, dk, dv = p.gdn_heads, cfg.gdn_dk, cfg.gdn_dv
         self.gdn_proj = torch.empty(M, 2 * h * dk + 2 * h * dv + 2 * h, **bf)
         # the conv output q | k | v is kept per layer: with alpha and beta it is the capture
@@ -469,13 +483,45 @@ class VerifyStack:
     def forward(self, hidden):
         return self._forward_body(hidden)
 
-    def capture(self, hidden_buf):
-        """Capture forward(hidden_buf) as a CUDA graph (run it eagerly once first)."""
-        self._forward_body(hidden_buf)
+    def _accept_body(self, proposals):
+        """LM head of this rank's vocabulary shard reduced to argmax keys in its epilogue,
+        the keys combined over the ranks, and the greedy accept (acceptedPrefix,
+        DFlashSpeculativeGenerator.swift:555-571)."""
+        q, p, dc = self.w["lm_head"], self.plan, self.dc
+        dc.lm_head_argmax(self.out, q.w, q.scales, q.biases, q.group, q.bits, keys=self.keys, workspace=self.ws,
+                          index_base=p.vocab0)
+        if self.allreduce == "peer":
+            # one key exchange per round; the layers' all-reduces in between keep the ranks
+            # in step, so its slot set can stay fixed
+            self.key_exchange.push(self.keys.view(torch.bfloat16).view(self.cfg.block, 4), 0)
+            dc.accept_reduce(self.key_exchange, 0, proposals, self.tokens, self.accepted)
+        else:
+            if self.allreduce == "nccl":
+                # unsigned keys as signed int64 with the sign bit flipped keep their order
+                flip = torch.tensor(-(2 ** 63), dtype=torch.int64, device=self.device)
+                self.keys.bitwise_xor_(flip)
+                torch.distributed.all_reduce(self.keys, op=torch.distributed.ReduceOp.MAX, group=self.pg)
+                self.keys.bitwise_xor_(flip)
+            dc.accept(self.keys, proposals, self.tokens, self.accepted)
+        return self.tokens, self.accepted
+
+    def verify(self, hidden, proposals):
+        """One verify round: forward of the block, LM head, accept.  proposals: int32
+        [block - 1] on the device.  Returns (target tokens int32 [block], accepted int32
+        [1]), identical on every rank."""
+        self._forward_body(hidden)
+        return self._accept_body(proposals)
+
+    def capture(self, hidden_buf, proposals=None):
+        """Capture forward(hidden_buf) — or, with proposals, the whole verify round — as a
+        CUDA graph (run eagerly once first)."""
+        body = (lambda: self.verify(hidden_buf, proposals)) if proposals is not None else \
+            (lambda: self._forward_body(hidden_buf))
+        body()
         torch.cuda.synchronize(self.device)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            self._forward_body(hidden_buf)
+            body()
         self.graph = g
         return g
 
@@ -529,29 +575,37 @@ def main(argv=None) -> int:
 
     stack = VerifyStack(cfg, rank, world, seed=args.seed, device=dev, group=pg, allreduce=args.allreduce)
     hidden = make_block(cfg, args.seed, dev)
+    proposals = torch.zeros(cfg.block - 1, dtype=torch.int32, device=dev)
+
+    def timed(g):
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            g.replay()
+        stop.record()
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([start.elapsed_time(stop) / args.steps], device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
     g = stack.capture(hidden)
-    for _ in range(args.warmup):
-        g.replay()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        torch.distributed.barrier()
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(args.steps):
-        g.replay()
-    stop.record()
-    torch.cuda.synchronize(dev)
-    ms = start.elapsed_time(stop) / args.steps
-    t = torch.tensor([ms], device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms = float(t.item())
+    ms = timed(g)
+    del g
+    g = stack.capture(hidden, proposals)  # forward + LM head (vocabulary-sharded) + accept
+    ms_round = timed(g)
     wbytes = weight_bytes(stack.w)
     checksum = float(stack.out.float().abs().sum().item())
     if rank == 0:
         print(json.dumps({
             "metric": "verify forward µs (M-row block through the full stack)",
             "value": round(ms * 1000.0, 2), "unit": "us", "tokens_per_s": round(cfg.block / (ms / 1000.0), 1),
+            "round_us": round(ms_round * 1000.0, 2),
             "tp": world, "steps": args.steps, "warmup": args.warmup,
             "weight_bytes_per_gpu": wbytes, "weight_gbs_per_gpu": round(wbytes / (ms / 1000.0) / 1e9, 1),
             "kernels_per_forward": stack.kernels_per_forward(), "all_reduces_per_forward": 2 * cfg.layers,

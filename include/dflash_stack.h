@@ -121,6 +121,7 @@ typedef struct dflash_qmm_options {
     int rank, world, set;
     void* const* bases; /* [world] exchange buffers as mapped in this process */
     void* argmax_keys;  /* uint64 [M] or NULL: see below */
+    int argmax_index_base; /* added to the row index in the keys: a vocabulary shard's first row */
 } dflash_qmm_options;
 
 int dflash_qmm_ex(const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scales, const dflash_bf16* biases,
@@ -133,6 +134,16 @@ int dflash_qmm_ex(const dflash_bf16* x, const uint32_t* w, const dflash_bf16* sc
  * proposals[i] == target_tokens[i].  All device pointers; one tiny kernel. */
 int dflash_accept(const unsigned long long* argmax_keys, const int32_t* proposals, int drafts,
                   int32_t* target_tokens, int32_t* accepted, dflash_stream_t stream);
+
+/* The accept of a round whose LM head is sharded by vocabulary over the ranks: every rank
+ * computed the argmax keys of its rows (dflash_qmm_ex with argmax_keys and its shard's
+ * first row as argmax_index_base) and pushed them, as bf16 [drafts + 1, 4] (8 bytes per
+ * key), into an exchange buffer of its own for [drafts + 1, 4] (dflash_tp_push, H = 4).
+ * This waits (bounded) for every rank's keys, keeps the largest per row (the global
+ * argmax, lowest index among equal maxima) and computes target_tokens and *accepted as
+ * dflash_accept does. */
+int dflash_accept_reduce(void* exchange, int world, int set, const int32_t* proposals, int drafts,
+                         int32_t* target_tokens, int32_t* accepted, dflash_stream_t stream);
 
 #ifdef __cplusplus
 }

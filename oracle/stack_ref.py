@@ -189,3 +189,27 @@ def forward(cfg, plan, weights: dict, state: dict, hidden: torch.Tensor,
         delta = rb(part)
     out = add_rmsnorm(resid, delta, cpu(weights["final_norm"]), eps)
     return {"out": out, "resid": resid, **cap}
+
+
+def _order_key(v: np.ndarray) -> np.ndarray:
+    """uint32 keys ordering float32 values as the floats order."""
+    u = v.astype(np.float32).view(np.uint32)
+    return np.where(u & 0x80000000, ~u, u | 0x80000000).astype(np.uint64)
+
+
+def lm_head_accept(plan, weights: dict, out: torch.Tensor, proposals, combine=None):
+    """The LM head of this rank's vocabulary shard (rb logits through the qmm oracle),
+    each row's largest logit with its lowest global index as a 64-bit key (value order
+    high, ~index low), `combine` taking the maximum over the ranks (identity at TP=1),
+    then the greedy accept (acceptedPrefix, DFlashSpeculativeGenerator.swift:555-571).
+    Returns (tokens int32 [M], accepted)."""
+    logits = qmm(out.detach().cpu().float(), weights["lm_head"]).numpy()  # [M, vocab_r]
+    idx = np.argmax(logits, axis=1)  # first index of the maximum
+    val = logits[np.arange(logits.shape[0]), idx]
+    keys = (_order_key(val) << np.uint64(32)) | (~(idx + plan.vocab0).astype(np.uint32)).astype(np.uint64)
+    if combine is not None:
+        keys = combine(keys)
+    tokens = (~(keys & np.uint64(0xFFFFFFFF)).astype(np.uint32)).astype(np.int32)
+    proposals = np.asarray(proposals, dtype=np.int32)
+    match = (proposals == tokens[:len(proposals)]).astype(np.int32)
+    return tokens, int(np.cumprod(match).sum())

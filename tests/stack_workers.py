@@ -41,8 +41,16 @@ def gloo_reference_rank(rank: int, world: int, port: int, out_path: str, cfg_kw:
                 dist.all_reduce(t)
 
         r = stack_ref.forward(cfg, plan, w, st, hidden, all_reduce=reduce)
+
+        def combine(keys):  # max over the ranks: unsigned keys as signed with the sign bit flipped
+            import numpy as np
+            t = torch.from_numpy((keys ^ np.uint64(1 << 63)).view(np.int64).copy())
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return t.numpy().view(np.uint64) ^ np.uint64(1 << 63)
+
+        tokens, acc = stack_ref.lm_head_accept(plan, w, r["out"], list(range(cfg.block - 1)), combine=combine)
         if rank == 0:
-            torch.save({"out": r["out"]}, out_path)
+            torch.save({"out": r["out"], "tokens": torch.from_numpy(tokens)}, out_path)
     finally:
         dist.destroy_process_group()
 
@@ -63,12 +71,21 @@ def nccl_stack_rank(rank: int, world: int, port: int, out_path: str, cfg_kw: dic
         torch.cuda.synchronize(dev)
         graphed = stack.out.clone()
         del g
+        proposals = torch.arange(cfg.block - 1, dtype=torch.int32, device=dev)
+        tokens, acc = stack.verify(hidden, proposals)
+        tokens, acc = tokens.clone(), acc.clone()
+        g = stack.capture(hidden, proposals)
+        g.replay()
+        torch.cuda.synchronize(dev)
+        graphed_tokens = stack.tokens.clone()
+        del g
         stack.graph = None
         import dflashcuda
         dev_err = dflashcuda.device_error()
         stack.close()
         if rank == 0:
-            torch.save({"eager": eager.cpu(), "graphed": graphed.cpu(), "device_error": dev_err}, out_path)
+            torch.save({"eager": eager.cpu(), "graphed": graphed.cpu(), "device_error": dev_err, "tokens": tokens.cpu(),
+                        "graphed_tokens": graphed_tokens.cpu(), "accepted": int(acc.item())}, out_path)
         dist.barrier()
     finally:
         dist.destroy_process_group()

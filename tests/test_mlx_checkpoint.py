@@ -67,6 +67,8 @@ def _same_weights(a, b):
             else:
                 assert x == y
     assert torch.equal(a["final_norm"], b["final_norm"])
+    for f in ("w", "scales", "biases"):
+        assert torch.equal(getattr(a["lm_head"], f), getattr(b["lm_head"], f))
 
 
 @pytest.mark.parametrize("world", [1, 2])

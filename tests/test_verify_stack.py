@@ -139,7 +139,9 @@ def tiny_tp1_reference():
     plan = vs.shard_plan(cfg, 0, 1)
     w = vs.build_rank_weights(cfg, plan, 0, "cpu")
     st = vs.build_rank_state(cfg, plan, 0, "cpu")
-    return stack_ref.forward(cfg, plan, w, st, vs.make_block(cfg, 0, "cpu"))
+    r = stack_ref.forward(cfg, plan, w, st, vs.make_block(cfg, 0, "cpu"))
+    r["tokens"], _ = stack_ref.lm_head_accept(plan, w, r["out"], list(range(cfg.block - 1)))
+    return r
 
 
 @pytest.mark.parametrize("world", [2, 4])
@@ -154,11 +156,16 @@ def test_tp_gloo_matches_tp1_and_dropped_reduce_diverges(tmp_path, tiny_tp1_refe
         codes = _run_ranks(stack_workers.gloo_reference_rank, world,
                            lambda r: (r, world, port, str(out), asdict(vs.TINY), drop))
         assert codes == [0] * world, codes
-        results[drop] = torch.load(out)["out"].numpy()
+        res = torch.load(out)
+        results[drop] = res["out"].numpy()
+        if not drop:  # the vocabulary-sharded LM head's argmax, combined over the ranks
+            tok_tp = res["tokens"].numpy()
     err, err_drop = closeness(results[False], ref), closeness(results[True], ref)
     print(f"TP={world} vs TP=1: {err:.3e}; without the all-reduce: {err_drop:.3e}")
     assert err <= 3e-2
     assert err_drop > max(0.05, 10 * err)
+    # same tokens as TP=1 wherever TP=1's top logit is not within the TP rounding of a rival
+    assert (tok_tp == tiny_tp1_reference["tokens"]).mean() >= 0.75
 
 
 def test_reference_stack_is_self_consistent(tiny_tp1_reference):
@@ -287,6 +294,63 @@ def test_peer_exchange_two_ranks_in_one_process(dc, cuda, via):
 
 
 @pytest.mark.gpu
+def test_cuda_stack_verify_round_tp1(dc, cuda):
+    """forward + LM head argmax + accept: the tokens are the first maximum of the logits
+    the plain qmm writes for the stack's output, the accept count follows the planted
+    proposals, and the captured round replays the same tokens."""
+    cfg = vs.TINY
+    stack = vs.VerifyStack(cfg, 0, 1, seed=0, device=cuda)
+    hidden = vs.make_block(cfg, 0, cuda)
+    out = stack.forward(hidden).clone()
+    q = stack.w["lm_head"]
+    want = torch.argmax(dc.qmm(out, q.w, q.scales, q.biases, q.group, q.bits).float(), dim=1).to(torch.int32)
+    for plant in range(cfg.block):
+        prop = want[:cfg.block - 1].clone()
+        if plant < cfg.block - 1:
+            prop[plant] = (prop[plant] + 1) % cfg.vocab
+        tokens, acc = stack.verify(hidden, prop)
+        torch.cuda.synchronize()
+        assert torch.equal(tokens, want) and int(acc.item()) == min(plant, cfg.block - 1)
+    g = stack.capture(hidden, want[:cfg.block - 1].clone())
+    stack.tokens.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(stack.tokens, want) and int(stack.accepted.item()) == cfg.block - 1
+    del g
+
+
+@pytest.mark.gpu
+def test_accept_reduce_two_vocabulary_shards_in_one_process(dc, cuda):
+    """Keys of two vocabulary shards, pushed into two emulated ranks' key exchanges,
+    reduce to the tokens of the unsharded LM head (ties resolved to the lowest index)."""
+    M, V, K = 8, 2048, 512
+    gen = torch.Generator(device=cuda).manual_seed(6)
+    q = vs.random_quant(gen, V, K, 64, 4, cuda)
+    x = torch.randn(M, K, generator=gen, device=cuda).to(torch.bfloat16)
+    full = dc.lm_head_argmax(x, q.w, q.scales, q.biases, 64, 4)
+    want = ((~(full & 0xFFFFFFFF)) & 0xFFFFFFFF).to(torch.int32)
+    ex = [dc.PeerExchange(2, M, 4) for _ in range(2)]
+    try:
+        for r in range(2):
+            ex[r].connect_local(r, [e.ptr for e in ex])
+        for step in range(2):  # twice, so the epochs move on
+            for r in range(2):
+                half = q.rows([(r * V // 2, (r + 1) * V // 2)])
+                keys = dc.lm_head_argmax(x, half.w, half.scales, half.biases, 64, 4, index_base=r * V // 2)
+                ex[r].push(keys.view(torch.bfloat16).view(M, 4), 0)
+            prop = want[:M - 1].clone()
+            prop[3] += 1
+            for r in range(2):
+                tokens, acc = dc.accept_reduce(ex[r], 0, prop)
+                torch.cuda.synchronize()
+                assert torch.equal(tokens, want) and int(acc.item()) == 3
+        assert dc.device_error() == 0
+    finally:
+        for e in ex:
+            e.close()
+
+
+@pytest.mark.gpu
 def test_cuda_stack_graph_replay_equals_eager(cuda):
     cfg = vs.TINY
     stack = vs.VerifyStack(cfg, 0, 1, seed=1, device=cuda)
@@ -341,5 +405,7 @@ def test_cuda_stack_tp2_matches_tp1_reference(cuda, tmp_path):
         res[mode] = torch.load(out)
         assert res[mode]["device_error"] == 0
         assert torch.equal(res[mode]["eager"], res[mode]["graphed"])
+        assert torch.equal(res[mode]["tokens"], res[mode]["graphed_tokens"])
         assert closeness(res[mode]["eager"].float().numpy(), ref) <= 3e-2
     assert torch.equal(res["peer"]["eager"], res["nccl"]["eager"])
+    assert torch.equal(res["peer"]["tokens"], res["nccl"]["tokens"])
