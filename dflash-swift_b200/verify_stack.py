@@ -381,6 +381,9 @@ class VerifyStack:
         self.keys = torch.empty(M, dtype=torch.int64, device=dev)
         self.tokens = torch.empty(M, dtype=torch.int32, device=dev)
         self.accepted = torch.empty(1, dtype=torch.int32, device=dev)
+        # the sign bit, for ordering unsigned keys as signed int64 in a max all-reduce (made
+        # here: a host-to-device copy is not allowed while a CUDA graph is being captured)
+        self._sign = torch.full((1,), -(2 ** 63), dtype=torch.int64, device=dev)
         h, dk, dv = p.gdn_heads, cfg.gdn_dk, cfg.gdn_dv
         self.gdn_proj = torch.empty(M, 2 * h * dk + 2 * h * dv + 2 * h, **bf)
         # the conv output q | k | v is kept per layer: with alpha and beta it is the capture
@@ -498,10 +501,9 @@ class VerifyStack:
         else:
             if self.allreduce == "nccl":
                 # unsigned keys as signed int64 with the sign bit flipped keep their order
-                flip = torch.tensor(-(2 ** 63), dtype=torch.int64, device=self.device)
-                self.keys.bitwise_xor_(flip)
+                self.keys.bitwise_xor_(self._sign)
                 torch.distributed.all_reduce(self.keys, op=torch.distributed.ReduceOp.MAX, group=self.pg)
-                self.keys.bitwise_xor_(flip)
+                self.keys.bitwise_xor_(self._sign)
             dc.accept(self.keys, proposals, self.tokens, self.accepted)
         return self.tokens, self.accepted
 

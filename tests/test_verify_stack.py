@@ -118,13 +118,17 @@ def test_config4_weight_bytes_per_rank():
 
 # ----------------------------------------------------------------------------- gloo ranks (CPU)
 
-def _run_ranks(target, world, args_fn, timeout=300):
+def _run_ranks(target, world, args_fn, timeout=240):
+    """Run the ranks as spawned processes; all of them together get `timeout` seconds,
+    after which any still alive are killed (and reported with exit code None)."""
+    import time
     ctx = mp.get_context("spawn")
     procs = [ctx.Process(target=target, args=args_fn(r)) for r in range(world)]
     for p in procs:
         p.start()
+    deadline = time.monotonic() + timeout
     for p in procs:
-        p.join(timeout)
+        p.join(max(0.0, deadline - time.monotonic()))
     codes = [p.exitcode for p in procs]
     for p in procs:
         if p.is_alive():
