@@ -360,9 +360,16 @@ def cpu_baseline(O, x, wq, s, b, budget_s: float):
         _, used = O.qmm_cpu(x, wq, s, b, GROUP, BITS, 0, n_rows, threads)
     dt = time.perf_counter() - t
     bytes_rows = algorithmic_bytes(M, n=n_rows) * passes
+    # the same restatement on one thread, over a smaller sample (about a tenth of the budget)
+    n1 = int(min(N, max(64, 0.1 * budget_s / max(per_row * max(used, 1), 1e-9))))
+    t1 = time.perf_counter()
+    O.qmm_cpu(x, wq, s, b, GROUP, BITS, 0, n1, 1)
+    dt1 = time.perf_counter() - t1
     return {"value": round(bytes_rows / dt / 1e9, 3), "unit": "GB/s", "cores": used, "kind": "port",
             "sample": f"{passes} pass(es) over rows 0..{n_rows} of N={N} (M={M}, K={K}, 4-bit g64), {dt:.2f} s",
-            "us_per_call_equiv": round(dt * 1e6 * N / n_rows / passes, 1)}
+            "us_per_call_equiv": round(dt * 1e6 * N / n_rows / passes, 1),
+            "single_thread": {"value": round(algorithmic_bytes(M, n=n1) / dt1 / 1e9, 3), "unit": "GB/s",
+                              "sample": f"rows 0..{n1}, {dt1:.2f} s on 1 thread"}}
 
 
 # ----------------------------------------------------------------------------- reference arm
