@@ -192,6 +192,37 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// ---------------------------------------------------------------- speculative tree rows
+// A tree round's block rows carry a parent list in device memory: parents[0] = -1 (the
+// anchor) and parents[r] in [0, r) for r > 0, so every path from the anchor visits rows
+// in increasing order.  Tree rounds have at most kMaxTreeRows rows, so a set of rows is
+// one 32-bit mask.
+constexpr int kMaxTreeRows = 32;
+
+// parents[r] when it names an earlier row, else -1: a malformed list makes a row its own
+// root instead of sending any walk out of range.
+__device__ __forceinline__ int tree_parent(const int32_t* __restrict__ parents, int r) {
+    const int p = r > 0 ? parents[r] : -1;
+    return p >= 0 && p < r ? p : -1;
+}
+
+struct TreeRow {
+    uint32_t path;  // bit a set when row a lies on the anchor-to-row path (the row included)
+    int depth;      // parent steps from the row back to its root
+};
+
+// The path mask and depth of row t < kMaxTreeRows (at most t + 1 dependent loads).
+__device__ __forceinline__ TreeRow tree_walk(const int32_t* __restrict__ parents, int t) {
+    TreeRow w{0u, 0};
+    int r = t;
+    for (int s = 0; s < kMaxTreeRows && r >= 0; ++s) {
+        w.path |= 1u << r;
+        r = tree_parent(parents, r);
+        w.depth += r >= 0;
+    }
+    return w;
+}
+
 // ---------------------------------------------------------------- tensor maps (host)
 // Encodes a 2D tiled tensor map: global [rows, cols] row-major with `row_bytes`
 // pitch, box [box_rows, box_cols].  Returns DFLASH_OK or an error status.

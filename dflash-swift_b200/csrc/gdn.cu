@@ -94,36 +94,76 @@ struct ReplayParams {
     float q_scale;
     int keep, width, heads, dk, dv;
     RowList rows;
+    const int32_t* parents;   // tree step only: the block's parent list (device, width entries)
 };
 
-// grid: (dv / 32, heads, layers); block: 256 threads = 32 rows x 8 threads.
+// grid: (dv / 32, heads, layers) — (dv / 32, heads, width) for a tree step, block z taking
+// the z-th leaf of the tree in row order; block: 256 threads = 32 rows x 8 threads.
 // Thread q of a row holds float4 chunks q, q+8, q+16, ... of the row (dk = 32 * CH).
-template <int CH>
+//
+// Tree step (TREE): the recurrence of a tree row is that of its root-to-row path, so
+// each block runs the chain of one leaf's path from the same pre-round state and writes
+// the outputs of the path's rows that no earlier leaf's path holds (every row is written
+// by exactly one block; a row shared by several paths gets the same arithmetic on each).
+// No state is written: after the round, dflash_gdn_replay rebuilds it from the snapshot
+// over the accepted path.
+template <int CH, bool TREE>
 __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constant__ ReplayParams p) {
     constexpr int DK = 32 * CH;
     // k and q of the replayed positions, kept as bf16 bits (widened on use)
     __shared__ __align__(16) uint16_t ks[kMaxPositions][DK];
     __shared__ __align__(16) uint16_t qs_sh[kMaxPositions][DK];
     __shared__ float ab[kMaxPositions][2];
+    __shared__ int32_t path_rows[TREE ? kMaxTreeRows : 1];
+    __shared__ uint32_t path_info[2];  // tree: rows on this block's path, rows it writes
 
-    const int layer = blockIdx.z, h = blockIdx.y;
+    const int layer = TREE ? 0 : blockIdx.z, h = blockIdx.y;
     const int row0 = blockIdx.x * kRowsPerBlock;
     const int tid = threadIdx.x;
     const int rl = tid / kRowThreads, qd = tid % kRowThreads;
     const int row = row0 + rl;
     const bool want_out = p.out != nullptr && p.q != nullptr;
 
+    int keep = p.keep;
+    if constexpr (TREE) {
+        if (tid < 32) {  // warp 0, lane = block row (width <= 32)
+            const int lane = tid;
+            const int par = lane < p.width ? tree_parent(p.parents, lane) : -1;
+            const uint32_t path = lane < p.width ? tree_walk(p.parents, lane).path : 0u;
+            const uint32_t has_child = __reduce_or_sync(0xffffffffu, par >= 0 ? 1u << par : 0u);
+            const uint32_t leaves = __ballot_sync(0xffffffffu, lane < p.width && !((has_child >> lane) & 1u));
+            uint32_t m = leaves;  // drop the blockIdx.z lowest leaves
+            for (int i = 0; i < (int)blockIdx.z && m; ++i) m &= m - 1;
+            const int leaf = m ? __ffs(m) - 1 : -1;  // the same on every lane
+            const uint32_t mine = leaf >= 0 ? __shfl_sync(0xffffffffu, path, leaf) : 0u;
+            const uint32_t earlier = leaf >= 0 ? leaves & ((1u << leaf) - 1u) : 0u;
+            const uint32_t taken = __reduce_or_sync(0xffffffffu, (earlier >> lane) & 1u ? path : 0u);
+            if (lane == 0) {
+                path_info[0] = mine;
+                path_info[1] = mine & ~taken;
+            }
+            if ((mine >> lane) & 1u) path_rows[__popc(mine & ((1u << lane) - 1u))] = lane;
+        }
+        __syncthreads();
+        keep = __popc(path_info[0]);
+        if (keep == 0) return;  // fewer leaves than blocks along z (uniform over the block)
+    }
+    auto row_at = [&](int r) -> int {
+        if constexpr (TREE) return path_rows[r];
+        else return p.rows.r[r];
+    };
+
     // Stage k (and q), alpha, beta of the replayed positions.
     const size_t pos_stride = (size_t)p.heads;  // [width, H] per layer for alpha/beta
-    for (int idx = tid; idx < p.keep * (DK / 4); idx += kBlockThreads) {
+    for (int idx = tid; idx < keep * (DK / 4); idx += kBlockThreads) {
         const int r = idx / (DK / 4), c4 = (idx % (DK / 4)) * 4;
-        const int t = p.rows.r[r];
+        const int t = row_at(r);
         const size_t base = (((size_t)layer * p.width + t) * p.heads + h) * DK + c4;
         *reinterpret_cast<uint2*>(&ks[r][c4]) = *reinterpret_cast<const uint2*>(p.k + base);
         if (want_out) *reinterpret_cast<uint2*>(&qs_sh[r][c4]) = *reinterpret_cast<const uint2*>(p.q + base);
     }
-    for (int r = tid; r < p.keep; r += kBlockThreads) {
-        const int t = p.rows.r[r];
+    for (int r = tid; r < keep; r += kBlockThreads) {
+        const int t = row_at(r);
         const size_t ai = ((size_t)layer * p.width + t) * pos_stride + h;
         ab[r][0] = p.alpha[ai];
         ab[r][1] = p.beta[ai];
@@ -134,11 +174,13 @@ __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constan
     float4 s[CH];
 #pragma unroll
     for (int c = 0; c < CH; ++c)
-        s[c] = __ldcs(reinterpret_cast<const float4*>(p.snapshot + head_base) + qd + c * kRowThreads);
+        s[c] = TREE ? __ldg(reinterpret_cast<const float4*>(p.snapshot + head_base) + qd + c * kRowThreads)
+                    // every leaf's block reads the same state: keep it in L2
+                    : __ldcs(reinterpret_cast<const float4*>(p.snapshot + head_base) + qd + c * kRowThreads);
     __syncthreads();
 
-    for (int r = 0; r < p.keep; ++r) {
-        const int t = p.rows.r[r];
+    for (int r = 0; r < keep; ++r) {
+        const int t = row_at(r);
         float4 k[CH];
 #pragma unroll
         for (int c = 0; c < CH; ++c) k[c] = ld_bf16x4(&ks[r][4 * (qd + c * kRowThreads)]);
@@ -153,24 +195,32 @@ __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constan
                 qv[c] = make_float4(raw.x * p.q_scale, raw.y * p.q_scale, raw.z * p.q_scale, raw.w * p.q_scale);
             }
             const float o = row_dot<CH>(s, qv);
-            if (qd == 0) {
+            bool write = qd == 0;
+            if constexpr (TREE) write = write && ((path_info[1] >> t) & 1u);
+            if (write) {
                 __nv_bfloat16 ob = __float2bfloat16_rn(o);
                 p.out[(((size_t)layer * p.width + t) * p.heads + h) * p.dv + row] =
                     *reinterpret_cast<uint16_t*>(&ob);
             }
         }
     }
+    if constexpr (!TREE) {
 #pragma unroll
-    for (int c = 0; c < CH; ++c)
-        __stcs(reinterpret_cast<float4*>(p.state_out + head_base) + qd + c * kRowThreads, s[c]);
+        for (int c = 0; c < CH; ++c)
+            __stcs(reinterpret_cast<float4*>(p.state_out + head_base) + qd + c * kRowThreads, s[c]);
+    }
 }
 
 int launch(const ReplayParams& p, int layers, cudaStream_t stream) {
-    dim3 grid(p.dv / kRowsPerBlock, p.heads, layers);
-    switch (p.dk) {
-        case 32: gdn_kernel<1><<<grid, kBlockThreads, 0, stream>>>(p); break;
-        case 64: gdn_kernel<2><<<grid, kBlockThreads, 0, stream>>>(p); break;
-        case 128: gdn_kernel<4><<<grid, kBlockThreads, 0, stream>>>(p); break;
+    const bool tree = p.parents != nullptr;  // tree step: one layer, one block per leaf slot
+    dim3 grid(p.dv / kRowsPerBlock, p.heads, tree ? p.width : layers);
+    switch (p.dk * 2 + tree) {
+        case 64: gdn_kernel<1, false><<<grid, kBlockThreads, 0, stream>>>(p); break;
+        case 128: gdn_kernel<2, false><<<grid, kBlockThreads, 0, stream>>>(p); break;
+        case 256: gdn_kernel<4, false><<<grid, kBlockThreads, 0, stream>>>(p); break;
+        case 65: gdn_kernel<1, true><<<grid, kBlockThreads, 0, stream>>>(p); break;
+        case 129: gdn_kernel<2, true><<<grid, kBlockThreads, 0, stream>>>(p); break;
+        case 257: gdn_kernel<4, true><<<grid, kBlockThreads, 0, stream>>>(p); break;
         default: return fail(DFLASH_ERR_UNSUPPORTED, "dk=%d not in {32, 64, 128}", p.dk);
     }
     DFLASH_CUDA_TRY(cudaGetLastError());
@@ -261,6 +311,35 @@ extern "C" int dflash_gdn_step(const float* state_in, float* state_out, const df
     p.dk = dk;
     p.dv = dv;
     if (int st = gdn::fill_rows(p.rows, nullptr, T, T)) return st;
+    return gdn::launch(p, 1, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dflash_gdn_step_tree(const float* state_in, const dflash_bf16* q, const dflash_bf16* k,
+                                    const dflash_bf16* v, const float* alpha, const float* beta,
+                                    const int32_t* parents, dflash_bf16* out, int T, int heads, int dk, int dv,
+                                    float q_scale, dflash_stream_t stream) {
+    using namespace dflash;
+    if (int st = gdn::check_dims(heads, dk, dv)) return st;
+    if (T < 1 || T > kMaxTreeRows) return fail(DFLASH_ERR_UNSUPPORTED, "T=%d outside 1..%d", T, kMaxTreeRows);
+    if (!state_in || !q || !k || !v || !alpha || !beta || !parents || !out)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_gdn_step_tree: null pointer");
+    if (!aligned16(state_in) || (reinterpret_cast<uintptr_t>(k) & 7) || (reinterpret_cast<uintptr_t>(q) & 7))
+        return fail(DFLASH_ERR_MISALIGNED, "dflash_gdn_step_tree: state 16-byte, q/k 8-byte alignment required");
+    gdn::ReplayParams p{};
+    p.snapshot = state_in;
+    p.k = k;
+    p.v = v;
+    p.alpha = alpha;
+    p.beta = beta;
+    p.q = q;
+    p.out = out;
+    p.q_scale = q_scale;
+    p.keep = T;
+    p.width = T;
+    p.heads = heads;
+    p.dk = dk;
+    p.dv = dv;
+    p.parents = parents;
     return gdn::launch(p, 1, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -288,18 +288,33 @@ __global__ void gdn_gates_kernel(uint16_t* __restrict__ q, uint16_t* __restrict_
 // all of its conv inputs loaded at once.  Causal conv + SiLU, rounded to bf16; q and k
 // L2-normalised over the head; written to y as the parts' [M, heads dk] blocks.  The q
 // warp's lane 0 also writes alpha and beta of (token, head).
+// Tap i of row t reads the input KC-1-i steps back along t's history: the block rows
+// before it (a chain), or its ancestors when `parents` gives a tree (the convolution
+// of a tree row is that of its root-to-row path), then the window once the history
+// runs past the block's anchor: tap i of a row at depth D < KC-1-i reads window row
+// D + i (both forms).
 template <int KC, int DJ>
 __global__ void gdn_conv_gates_kernel(const uint16_t* __restrict__ x, int ld, const uint16_t* __restrict__ window,
                                       const uint16_t* __restrict__ w, uint16_t* __restrict__ y,
                                       const uint16_t* __restrict__ ab, int ld_ab, const float* __restrict__ a_log,
                                       const float* __restrict__ dt_bias, float* __restrict__ alpha,
-                                      float* __restrict__ beta, int M, int heads) {
+                                      float* __restrict__ beta, int M, int heads,
+                                      const int32_t* __restrict__ parents) {
     chain_in();
     constexpr int dk = 32 * DJ;
     const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (wid >= M * heads * 3) return;
     const int t = wid / (heads * 3), h = (wid / 3) % heads, part = wid % 3;
     const int C = 3 * heads * dk, cp = heads * dk;
+    // back[s]: the block row s steps back from t, or -1 once the history is in the window
+    int back[KC];
+    back[0] = t;
+#pragma unroll
+    for (int s = 1; s < KC; ++s)
+        back[s] = back[s - 1] < 0 ? -1 : parents ? tree_parent(parents, back[s - 1]) : back[s - 1] - 1;
+    int depth = 0;  // t's depth, capped at KC - 1 (only its comparison with s matters)
+#pragma unroll
+    for (int s = 1; s < KC; ++s) depth += back[s] >= 0;
     float xin[DJ][KC], wk[DJ][KC];
 #pragma unroll
     for (int j = 0; j < DJ; ++j) {
@@ -307,8 +322,8 @@ __global__ void gdn_conv_gates_kernel(const uint16_t* __restrict__ x, int ld, co
 #pragma unroll
         for (int i = 0; i < KC; ++i) {
             wk[j][i] = bf(w[(size_t)c * KC + i]);
-            const int src = t + i - (KC - 1);  // < 0: the window's rows
-            xin[j][i] = src < 0 ? bf(window[(size_t)(KC - 1 + src) * C + c]) : bf(x[(size_t)src * ld + c]);
+            const int src = back[KC - 1 - i];
+            xin[j][i] = src < 0 ? bf(window[(size_t)(depth + i) * C + c]) : bf(x[(size_t)src * ld + c]);
         }
     }
     float v[DJ];
@@ -364,11 +379,13 @@ __global__ void gated_norm_kernel(const uint16_t* __restrict__ o, const uint16_t
 // cache_v[j, pos0 + t].  Rotary: rotate-half over the first rot dims, frequency
 // theta^(-2i/rot) for pair (i, i + rot/2), position pos0 + t.  Lane l holds dims
 // l + 32 c, so with rot a multiple of 64 both halves of a pair sit in one lane.
+// With a tree parent list the rotary position is pos0 + depth(t) (a tree row sits at its
+// depth on its path); the cache slot stays pos0 + t.
 template <int CH>
 __global__ void attn_prep_kernel(uint16_t* __restrict__ qkv, int ld, const uint16_t* __restrict__ q_norm,
                                  const uint16_t* __restrict__ k_norm, uint16_t* __restrict__ cache_k,
                                  uint16_t* __restrict__ cache_v, int M, int hq, int hkv, int rot, int pos0,
-                                 int max_len, float eps, float theta) {
+                                 int max_len, float eps, float theta, const int32_t* __restrict__ parents) {
     chain_in();
     constexpr int d = CH * 32;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -397,7 +414,7 @@ __global__ void attn_prep_kernel(uint16_t* __restrict__ qkv, int ld, const uint1
 #pragma unroll
     for (int c = 0; c < CH; ++c) v[c] = bf_round(v[c] * rs * bf(nw[lane + 32 * c]));
     const int half_c = rot / 64;  // pair partner is c + half_c
-    const float pos = (float)(pos0 + t);
+    const float pos = (float)(pos0 + (parents ? tree_walk(parents, t).depth : t));
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
         if (c < half_c) {
@@ -435,6 +452,11 @@ __global__ void attn_prep_kernel(uint16_t* __restrict__ qkv, int ld, const uint1
 // The CTAs' (max, sum, p V) partials are merged through distributed shared memory, each
 // CTA of the cluster finishing a quarter of the outputs, with the output gate:
 //   out[t, h d + e] = softmax(q k^T scale) v * sigmoid(gate[t, h d + e]).
+// With a tree parent list, block key pos0 + a is visible to token t only when row a lies
+// on t's root-to-row path (the cached prefix stays visible); hidden keys score -inf.  A
+// chunk or CTA range may then hold no visible key: its exponent base stays finite (0)
+// so its weights come out 0, and the merge gives such a CTA weight 0 (t itself is
+// always visible, so some CTA holds a finite maximum).
 constexpr int kSplit = 4;
 constexpr int kChunk = 256;
 constexpr int kMaxG = 8;
@@ -477,7 +499,8 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __rest
                                                           const uint16_t* __restrict__ cache_k,
                                                           const uint16_t* __restrict__ cache_v,
                                                           uint16_t* __restrict__ out, int hq, int hkv, int pos0,
-                                                          int max_len, float scale) {
+                                                          int max_len, float scale,
+                                                          const int32_t* __restrict__ parents) {
     constexpr int d = CH * 32;
     constexpr int KU = 32 / GP;  // keys per warp step in the scores pass
     static_assert(GP <= kMaxG && KU * CH <= 64, "score registers");
@@ -491,6 +514,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __rest
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = pos0 + t + 1;
     const int k0 = (int)((long long)n * rank / kSplit), k1 = (int)((long long)n * (rank + 1) / kSplit);
+    const uint32_t visible = parents ? tree_walk(parents, t).path : 0u;  // tree rounds: t's path rows
 
     float q[GP][CH];
     const uint16_t* qrow = qkv + (size_t)t * ld + (size_t)kvh * G * d + lane * CH;
@@ -537,7 +561,10 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __rest
                 }
             const float dot = reduce_scatter32(v, lane);
             const int u = lane / GP, g = lane % GP;
-            if (g < G && j0 + u < len) s_p[g][j0 + u] = dot;
+            if (g < G && j0 + u < len) {
+                const int b = c0 + j0 + u - pos0;  // block row of the key (< 0: the prefix)
+                s_p[g][j0 + u] = parents && b >= 0 && !((visible >> b) & 1u) ? -INFINITY : dot;
+            }
         }
         __syncthreads();
         // softmax bookkeeping: warp g owns head g
@@ -547,15 +574,16 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __rest
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, o));
             const float mold = s_m[warp], mnew = fmaxf(mold, mc);
+            const float mbase = mnew == -INFINITY ? 0.f : mnew;  // no visible key yet: weights 0
             float ls = 0.f;
             for (int j = lane; j < len; j += 32) {
-                const float p = __expf(s_p[warp][j] - mnew);
+                const float p = __expf(s_p[warp][j] - mbase);
                 s_p[warp][j] = p;
                 ls += p;
             }
             ls = warp_sum(ls);
             if (lane == 0) {
-                const float corr = __expf(mold - mnew);  // 0 on the first chunk (mold = -inf)
+                const float corr = __expf(mold - mbase);  // 0 while mold = -inf
                 s_corr[warp] = corr;
                 s_l[warp] = s_l[warp] * corr + ls;
                 s_m[warp] = mnew;
@@ -713,6 +741,32 @@ inline unsigned grid_for(size_t n, int block) {
 
 inline cudaStream_t as_stream(dflash_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// After a tree round, cache rows pos0 + rows[i] move to pos0 + i.  grid (hkv, layers, 2):
+// cache_k for z = 0, cache_v for z = 1.  A block stages all `keep` source rows in shared
+// memory before writing any, so moves whose sources and destinations overlap are safe.
+struct CompactRows {
+    int32_t r[kMaxTreeRows];
+};
+
+__global__ void __launch_bounds__(256) kv_compact_kernel(uint16_t* __restrict__ cache_k, uint16_t* __restrict__ cache_v,
+                                                         long long layer_stride, int d, int pos0, int max_len,
+                                                         CompactRows rows, int keep) {
+    __shared__ uint4 buf[kMaxTreeRows * 32];  // keep rows of d <= 256 bf16
+    chain_in();
+    uint16_t* base = (blockIdx.z ? cache_v : cache_k) + (size_t)blockIdx.y * (size_t)layer_stride +
+                     ((size_t)blockIdx.x * max_len + pos0) * d;
+    const int per_row = d / 8;  // uint4 per cache row
+    for (int idx = threadIdx.x; idx < keep * per_row; idx += blockDim.x) {
+        const int i = idx / per_row, c = idx - i * per_row;
+        buf[idx] = reinterpret_cast<const uint4*>(base + (size_t)rows.r[i] * d)[c];
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < keep * per_row; idx += blockDim.x) {
+        const int i = idx / per_row, c = idx - i * per_row;
+        reinterpret_cast<uint4*>(base + (size_t)i * d)[c] = buf[idx];
+    }
+}
+
 }  // namespace stack
 }  // namespace dflash
 
@@ -825,9 +879,9 @@ extern "C" int dflash_stack_gated_norm(const dflash_bf16* o, const dflash_bf16* 
     return DFLASH_OK;
 }
 
-extern "C" int dflash_stack_attn_prep(dflash_bf16* qkv, int ld, const dflash_bf16* q_norm, const dflash_bf16* k_norm,
-                                      dflash_bf16* cache_k, dflash_bf16* cache_v, int M, int hq, int hkv, int d,
-                                      int rot, int pos0, int max_len, float eps, float theta, dflash_stream_t stream) {
+static int attn_prep(dflash_bf16* qkv, int ld, const dflash_bf16* q_norm, const dflash_bf16* k_norm,
+                     dflash_bf16* cache_k, dflash_bf16* cache_v, int M, int hq, int hkv, int d, int rot, int pos0,
+                     int max_len, float eps, float theta, const int32_t* parents, dflash_stream_t stream) {
     if (!qkv || !q_norm || !k_norm || !cache_k || !cache_v || M < 1 || hq < 1 || hkv < 1 || pos0 < 0 ||
         pos0 + M > max_len || ld < (2 * hq + 2 * hkv) * d)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_attn_prep: bad arguments");
@@ -841,24 +895,41 @@ extern "C" int dflash_stack_attn_prep(dflash_bf16* qkv, int ld, const dflash_bf1
     switch (d) {
         case 64:
             e = launch_chained(stack::attn_prep_kernel<2>, grid, block, 0, s, 1, qkv, ld, q_norm, k_norm, cache_k,
-                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta);
+                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta, parents);
             break;
         case 128:
             e = launch_chained(stack::attn_prep_kernel<4>, grid, block, 0, s, 1, qkv, ld, q_norm, k_norm, cache_k,
-                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta);
+                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta, parents);
             break;
         default:
             e = launch_chained(stack::attn_prep_kernel<8>, grid, block, 0, s, 1, qkv, ld, q_norm, k_norm, cache_k,
-                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta);
+                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta, parents);
             break;
     }
     DFLASH_CUDA_TRY(e);
     return DFLASH_OK;
 }
 
-extern "C" int dflash_stack_attn_decode(const dflash_bf16* qkv, int ld, const dflash_bf16* cache_k,
-                                        const dflash_bf16* cache_v, dflash_bf16* out, int M, int hq, int hkv, int d,
-                                        int pos0, int max_len, float scale, dflash_stream_t stream) {
+extern "C" int dflash_stack_attn_prep(dflash_bf16* qkv, int ld, const dflash_bf16* q_norm, const dflash_bf16* k_norm,
+                                      dflash_bf16* cache_k, dflash_bf16* cache_v, int M, int hq, int hkv, int d,
+                                      int rot, int pos0, int max_len, float eps, float theta, dflash_stream_t stream) {
+    return attn_prep(qkv, ld, q_norm, k_norm, cache_k, cache_v, M, hq, hkv, d, rot, pos0, max_len, eps, theta, nullptr,
+                     stream);
+}
+
+extern "C" int dflash_stack_attn_prep_tree(dflash_bf16* qkv, int ld, const dflash_bf16* q_norm,
+                                           const dflash_bf16* k_norm, dflash_bf16* cache_k, dflash_bf16* cache_v,
+                                           int M, int hq, int hkv, int d, int rot, int pos0, int max_len, float eps,
+                                           float theta, const int32_t* parents, dflash_stream_t stream) {
+    if (!parents || M > kMaxTreeRows)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_attn_prep_tree: need parents and M <= %d", kMaxTreeRows);
+    return attn_prep(qkv, ld, q_norm, k_norm, cache_k, cache_v, M, hq, hkv, d, rot, pos0, max_len, eps, theta, parents,
+                     stream);
+}
+
+static int attn_decode(const dflash_bf16* qkv, int ld, const dflash_bf16* cache_k, const dflash_bf16* cache_v,
+                       dflash_bf16* out, int M, int hq, int hkv, int d, int pos0, int max_len, float scale,
+                       const int32_t* parents, dflash_stream_t stream) {
     if (!qkv || !cache_k || !cache_v || !out || M < 1 || hq < 1 || hkv < 1 || hq % hkv || pos0 < 0 ||
         pos0 + M > max_len || ld < (2 * hq + 2 * hkv) * d || M > 65535)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_attn_decode: bad arguments");
@@ -878,13 +949,29 @@ extern "C" int dflash_stack_attn_decode(const dflash_bf16* qkv, int ld, const df
 #define DFLASH_ATTN_CASE(CH, GP)                                                                                   \
     if (ch == CH && gp == GP)                                                                                      \
         e = launch_chained(stack::attn_decode_kernel<CH, GP>, grid, block, 0, s, stack::kSplit, qkv, ld, cache_k,    \
-                           cache_v, out, hq, hkv, pos0, max_len, scale);
+                           cache_v, out, hq, hkv, pos0, max_len, scale, parents);
     DFLASH_ATTN_CASE(2, 1) DFLASH_ATTN_CASE(2, 2) DFLASH_ATTN_CASE(2, 4) DFLASH_ATTN_CASE(2, 8)
     DFLASH_ATTN_CASE(4, 2) DFLASH_ATTN_CASE(4, 4) DFLASH_ATTN_CASE(4, 8)
     DFLASH_ATTN_CASE(8, 4) DFLASH_ATTN_CASE(8, 8)
 #undef DFLASH_ATTN_CASE
     DFLASH_CUDA_TRY(e);
     return DFLASH_OK;
+}
+
+extern "C" int dflash_stack_attn_decode(const dflash_bf16* qkv, int ld, const dflash_bf16* cache_k,
+                                        const dflash_bf16* cache_v, dflash_bf16* out, int M, int hq, int hkv, int d,
+                                        int pos0, int max_len, float scale, dflash_stream_t stream) {
+    return attn_decode(qkv, ld, cache_k, cache_v, out, M, hq, hkv, d, pos0, max_len, scale, nullptr, stream);
+}
+
+extern "C" int dflash_stack_attn_decode_tree(const dflash_bf16* qkv, int ld, const dflash_bf16* cache_k,
+                                             const dflash_bf16* cache_v, dflash_bf16* out, int M, int hq, int hkv,
+                                             int d, int pos0, int max_len, float scale, const int32_t* parents,
+                                             dflash_stream_t stream) {
+    if (!parents || M > kMaxTreeRows)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_attn_decode_tree: need parents and M <= %d",
+                    kMaxTreeRows);
+    return attn_decode(qkv, ld, cache_k, cache_v, out, M, hq, hkv, d, pos0, max_len, scale, parents, stream);
 }
 
 extern "C" int dflash_accept(const unsigned long long* argmax_keys, const int32_t* proposals, int drafts,
@@ -896,10 +983,10 @@ extern "C" int dflash_accept(const unsigned long long* argmax_keys, const int32_
     return DFLASH_OK;
 }
 
-extern "C" int dflash_stack_gdn_conv_gates(const dflash_bf16* x, int ld, const dflash_bf16* window,
-                                           const dflash_bf16* weight, dflash_bf16* y, const dflash_bf16* ab,
-                                           int ld_ab, const float* a_log, const float* dt_bias, float* alpha,
-                                           float* beta, int M, int heads, int dk, int kc, dflash_stream_t stream) {
+static int gdn_conv_gates(const dflash_bf16* x, int ld, const dflash_bf16* window, const dflash_bf16* weight,
+                          dflash_bf16* y, const dflash_bf16* ab, int ld_ab, const float* a_log, const float* dt_bias,
+                          float* alpha, float* beta, int M, int heads, int dk, int kc, const int32_t* parents,
+                          dflash_stream_t stream) {
     if (!x || !window || !weight || !y || !ab || !a_log || !dt_bias || !alpha || !beta || M < 1 || heads < 1 ||
         ld < 3 * heads * dk)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_gdn_conv_gates: bad arguments");
@@ -913,13 +1000,33 @@ extern "C" int dflash_stack_gdn_conv_gates(const dflash_bf16* x, int ld, const d
 #define DFLASH_CG_CASE(KC, DJ)                                                                                   \
     if (kc == KC && dk == 32 * DJ)                                                                               \
         e = launch_chained(stack::gdn_conv_gates_kernel<KC, DJ>, grid, block, 0, s, 1, x, ld, window, weight, y, ab, \
-                           ld_ab, a_log, dt_bias, alpha, beta, M, heads);
+                           ld_ab, a_log, dt_bias, alpha, beta, M, heads, parents);
     DFLASH_CG_CASE(2, 1) DFLASH_CG_CASE(2, 2) DFLASH_CG_CASE(2, 4)
     DFLASH_CG_CASE(3, 1) DFLASH_CG_CASE(3, 2) DFLASH_CG_CASE(3, 4)
     DFLASH_CG_CASE(4, 1) DFLASH_CG_CASE(4, 2) DFLASH_CG_CASE(4, 4)
 #undef DFLASH_CG_CASE
     DFLASH_CUDA_TRY(e);
     return DFLASH_OK;
+}
+
+extern "C" int dflash_stack_gdn_conv_gates(const dflash_bf16* x, int ld, const dflash_bf16* window,
+                                           const dflash_bf16* weight, dflash_bf16* y, const dflash_bf16* ab,
+                                           int ld_ab, const float* a_log, const float* dt_bias, float* alpha,
+                                           float* beta, int M, int heads, int dk, int kc, dflash_stream_t stream) {
+    return gdn_conv_gates(x, ld, window, weight, y, ab, ld_ab, a_log, dt_bias, alpha, beta, M, heads, dk, kc, nullptr,
+                          stream);
+}
+
+extern "C" int dflash_stack_gdn_conv_gates_tree(const dflash_bf16* x, int ld, const dflash_bf16* window,
+                                                const dflash_bf16* weight, dflash_bf16* y, const dflash_bf16* ab,
+                                                int ld_ab, const float* a_log, const float* dt_bias, float* alpha,
+                                                float* beta, int M, int heads, int dk, int kc,
+                                                const int32_t* parents, dflash_stream_t stream) {
+    if (!parents || M > kMaxTreeRows)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_gdn_conv_gates_tree: need parents and M <= %d",
+                    kMaxTreeRows);
+    return gdn_conv_gates(x, ld, window, weight, y, ab, ld_ab, a_log, dt_bias, alpha, beta, M, heads, dk, kc, parents,
+                          stream);
 }
 
 extern "C" int dflash_accept_reduce(void* exchange, int world, int set, const int32_t* proposals, int drafts,
@@ -929,5 +1036,29 @@ extern "C" int dflash_accept_reduce(void* exchange, int world, int set, const in
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_accept_reduce: bad arguments");
     DFLASH_CUDA_TRY(launch_chained(stack::accept_reduce_kernel, dim3(1), dim3(32), 0, as_stream(stream), 1, exchange,
                                    world, set, proposals, drafts, target_tokens, accepted));
+    return DFLASH_OK;
+}
+
+extern "C" int dflash_stack_kv_compact(dflash_bf16* cache_k, dflash_bf16* cache_v, int layers, long long layer_stride,
+                                       int hkv, int d, int pos0, int max_len, const int32_t* rows, int keep,
+                                       dflash_stream_t stream) {
+    if (!cache_k || !cache_v || cache_k == cache_v || !rows || layers < 1 || layers > 65535 || hkv < 1 ||
+        hkv > 65535 || pos0 < 0 || max_len < 1 || keep < 1 || keep > kMaxTreeRows || layer_stride < 0 ||
+        (layers > 1 && layer_stride < (long long)hkv * max_len * d))
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_kv_compact: bad arguments");
+    if (d != 64 && d != 128 && d != 256) return fail(DFLASH_ERR_UNSUPPORTED, "head dim %d not in {64,128,256}", d);
+    if (!aligned16(cache_k) || !aligned16(cache_v) || (layer_stride * 2) % 16)
+        return fail(DFLASH_ERR_MISALIGNED, "dflash_stack_kv_compact: caches and layer stride must be 16-byte aligned");
+    stack::CompactRows rl{};
+    for (int i = 0; i < keep; ++i) {
+        if (rows[i] < 0 || pos0 + rows[i] >= max_len)
+            return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_kv_compact: rows[%d]=%d outside the cache", i,
+                        rows[i]);
+        rl.r[i] = rows[i];
+    }
+    if (pos0 + keep > max_len) return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_kv_compact: keep past max_len");
+    DFLASH_CUDA_TRY(launch_chained(stack::kv_compact_kernel, dim3(hkv, layers, 2), dim3(256), 0, as_stream(stream), 1,
+                                   reinterpret_cast<uint16_t*>(cache_k), reinterpret_cast<uint16_t*>(cache_v),
+                                   layer_stride, d, pos0, max_len, rl, keep));
     return DFLASH_OK;
 }

@@ -53,6 +53,9 @@ EXPORTED = (
     "dflash_tp_exchange_free", "dflash_ipc_get_handle", "dflash_ipc_open_handle", "dflash_ipc_close_handle",
     "dflash_tp_push", "dflash_qmm_ex", "dflash_accept", "dflash_stack_gdn_conv_gates",
     "dflash_accept_reduce",
+    # speculative tree rounds
+    "dflash_gdn_step_tree", "dflash_stack_gdn_conv_gates_tree", "dflash_stack_attn_prep_tree",
+    "dflash_stack_attn_decode_tree", "dflash_stack_kv_compact",
 )
 
 
@@ -109,6 +112,14 @@ def _load() -> ctypes.CDLL:
         "dflash_accept_reduce": ([_vp, _i, _i, _vp, _i, _vp, _vp, _vp], _i),
         "dflash_stack_gdn_conv_gates": ([_vp, _i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
                                         _i),
+        "dflash_gdn_step_tree": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp], _i),
+        "dflash_stack_gdn_conv_gates_tree": ([_vp, _i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i,
+                                              _vp, _vp], _i),
+        "dflash_stack_attn_prep_tree": ([_vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _f, _vp, _vp],
+                                        _i),
+        "dflash_stack_attn_decode_tree": ([_vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp, _vp], _i),
+        "dflash_stack_kv_compact": ([_vp, _vp, _i, ctypes.c_longlong, _i, _i, _i, _i,
+                                     ctypes.POINTER(ctypes.c_int32), _i, _vp], _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -371,6 +382,16 @@ def gdn_step(state_in, state_out, q, k, v, alpha, beta, out=None, q_scale: float
     return state_out
 
 
+def gdn_step_tree(state_in, q, k, v, alpha, beta, parents, out, q_scale: float = 1.0, stream=None):
+    """One layer's recurrence over the T rows of a tree round: row t gets the output of a
+    chain over its root-to-t path from state_in.  parents: device int32 [T]."""
+    T, H, dk = k.shape
+    dv = v.shape[-1]
+    check(lib.dflash_gdn_step_tree(_ptr(state_in), _ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(beta),
+                                   _ptr(parents), _ptr(out), T, H, dk, dv, float(q_scale), _stream(stream)))
+    return out
+
+
 def _rows_arg(rows: Optional[Sequence[int]]):
     if rows is None:
         return None
@@ -442,21 +463,43 @@ def stack_gated_norm(o, z, weight, out, eps: float, stream=None):
 
 
 def stack_attn_prep(qkv, q_norm, k_norm, cache_k, cache_v, hq: int, hkv: int, rot: int, pos0: int, eps: float,
-                    theta: float, stream=None):
-    """qkv rows [q | gate | k | v]; caches [hkv, max_len, d]."""
+                    theta: float, stream=None, parents=None):
+    """qkv rows [q | gate | k | v]; caches [hkv, max_len, d].  parents (device int32 [M]):
+    a tree round, rotary position pos0 + depth."""
     M = qkv.shape[0]
     _, max_len, d = cache_k.shape
-    check(lib.dflash_stack_attn_prep(_ptr(qkv), qkv.stride(0), _ptr(q_norm), _ptr(k_norm), _ptr(cache_k),
-                                     _ptr(cache_v), M, hq, hkv, d, rot, pos0, max_len, float(eps), float(theta),
-                                     _stream(stream)))
+    args = (_ptr(qkv), qkv.stride(0), _ptr(q_norm), _ptr(k_norm), _ptr(cache_k), _ptr(cache_v), M, hq, hkv, d, rot,
+            pos0, max_len, float(eps), float(theta))
+    if parents is None:
+        check(lib.dflash_stack_attn_prep(*args, _stream(stream)))
+    else:
+        check(lib.dflash_stack_attn_prep_tree(*args, _ptr(parents), _stream(stream)))
 
 
-def stack_attn_decode(qkv, cache_k, cache_v, out, hq: int, hkv: int, pos0: int, scale: float, stream=None):
+def stack_attn_decode(qkv, cache_k, cache_v, out, hq: int, hkv: int, pos0: int, scale: float, stream=None,
+                      parents=None):
+    """parents (device int32 [M]): a tree round, each token sees the prefix and its path."""
     M = qkv.shape[0]
     _, max_len, d = cache_k.shape
-    check(lib.dflash_stack_attn_decode(_ptr(qkv), qkv.stride(0), _ptr(cache_k), _ptr(cache_v), _ptr(out), M, hq,
-                                       hkv, d, pos0, max_len, float(scale), _stream(stream)))
+    args = (_ptr(qkv), qkv.stride(0), _ptr(cache_k), _ptr(cache_v), _ptr(out), M, hq, hkv, d, pos0, max_len,
+            float(scale))
+    if parents is None:
+        check(lib.dflash_stack_attn_decode(*args, _stream(stream)))
+    else:
+        check(lib.dflash_stack_attn_decode_tree(*args, _ptr(parents), _stream(stream)))
     return out
+
+
+def stack_kv_compact(cache_k, cache_v, pos0: int, rows: Sequence[int], stream=None):
+    """After a tree round: cache rows pos0 + rows[i] -> pos0 + i.  Caches [hkv, max_len, d]
+    (one layer) or [layers, hkv, max_len, d] (contiguous)."""
+    if cache_k.dim() == 3:
+        layers, (hkv, max_len, d), stride = 1, cache_k.shape, 0
+    else:
+        layers, hkv, max_len, d = cache_k.shape
+        stride = cache_k.stride(0)
+    check(lib.dflash_stack_kv_compact(_ptr(cache_k), _ptr(cache_v), layers, stride, hkv, d, pos0, max_len,
+                                      _rows_arg(rows), len(rows), _stream(stream)))
 
 
 # ----------------------------------------------------------------------------- tensor-parallel exchange
@@ -577,12 +620,17 @@ def accept(keys, proposals, tokens=None, accepted=None, stream=None):
     return tokens, accepted
 
 
-def stack_gdn_conv_gates(x, window, weight, out, ab, a_log, dt_bias, alpha, beta, heads: int, dk: int, stream=None):
-    """Conv + SiLU + q/k normalisation + gates in one kernel; out [3, M, heads, dk]."""
+def stack_gdn_conv_gates(x, window, weight, out, ab, a_log, dt_bias, alpha, beta, heads: int, dk: int, stream=None,
+                         parents=None):
+    """Conv + SiLU + q/k normalisation + gates in one kernel; out [3, M, heads, dk].
+    parents (device int32 [M]): a tree round, each row convolved along its path."""
     M = x.shape[0]
-    check(lib.dflash_stack_gdn_conv_gates(_ptr(x), x.stride(0), _ptr(window), _ptr(weight), _ptr(out), _ptr(ab),
-                                          ab.stride(0), _ptr(a_log), _ptr(dt_bias), _ptr(alpha), _ptr(beta), M, heads,
-                                          dk, weight.shape[1], _stream(stream)))
+    args = (_ptr(x), x.stride(0), _ptr(window), _ptr(weight), _ptr(out), _ptr(ab), ab.stride(0), _ptr(a_log),
+            _ptr(dt_bias), _ptr(alpha), _ptr(beta), M, heads, dk, weight.shape[1])
+    if parents is None:
+        check(lib.dflash_stack_gdn_conv_gates(*args, _stream(stream)))
+    else:
+        check(lib.dflash_stack_gdn_conv_gates_tree(*args, _ptr(parents), _stream(stream)))
     return out
 
 

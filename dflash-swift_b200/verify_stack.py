@@ -323,10 +323,12 @@ class VerifyStack:
     bf16 [M, hidden] (identical on every rank)."""
 
     def __init__(self, cfg: StackConfig, rank: int = 0, world: int = 1, seed: int = 0, device=None,
-                 group=None, weights: Optional[dict] = None, state: Optional[dict] = None, allreduce: str = "peer"):
+                 group=None, weights: Optional[dict] = None, state: Optional[dict] = None, allreduce: str = "peer",
+                 tree: bool = False):
         import dflashcuda as dc
         self.dc = dc
         self.cfg = cfg
+        self.tree = tree
         self.plan = shard_plan(cfg, rank, world)
         self.world = world
         self.pg = group
@@ -384,10 +386,16 @@ class VerifyStack:
         # the sign bit, for ordering unsigned keys as signed int64 in a max all-reduce (made
         # here: a host-to-device copy is not allowed while a CUDA graph is being captured)
         self._sign = torch.full((1,), -(2 ** 63), dtype=torch.int64, device=dev)
+        # tree rounds: the block's parent list, read by the tree kernels in stream order so a
+        # captured round replays with whatever tree set_tree last wrote (a chain until then)
+        self.parents = torch.tensor([-1] + list(range(M - 1)), dtype=torch.int32, device=dev) if self.tree else None
+        self.tree_plan = None
         h, dk, dv = p.gdn_heads, cfg.gdn_dk, cfg.gdn_dv
-        self.gdn_proj = torch.empty(M, 2 * h * dk + 2 * h * dv + 2 * h, **bf)
-        # the conv output q | k | v is kept per layer: with alpha and beta it is the capture
+        # per layer: the in-projection (its q | k | v channels are the conv inputs that
+        # commit() rebuilds the conv window from) and the conv output q | k | v, which with
+        # alpha and beta is the capture the recurrence replays
         n_gdn = sum(1 for k in cfg.layer_kinds() if k == "gdn")
+        self.gdn_proj = torch.empty(n_gdn, M, 2 * h * dk + 2 * h * dv + 2 * h, **bf)
         self.capture_qkv = torch.empty(n_gdn, 3, M, h, dk, **bf)
         self.capture_alpha = torch.empty(n_gdn, M, h, **f32)
         self.capture_beta = torch.empty(n_gdn, M, h, **f32)
@@ -440,16 +448,21 @@ class VerifyStack:
     def _gdn(self, L, S, gi):
         cfg, p, dc = self.cfg, self.plan, self.dc
         M, h, dk, dv = cfg.block, p.gdn_heads, cfg.gdn_dk, cfg.gdn_dv
-        self._qmm(self.normed, L["in_proj"], self.gdn_proj)
+        proj = self.gdn_proj[gi]
+        self._qmm(self.normed, L["in_proj"], proj)
         qkv = self.capture_qkv[gi]
         q, k, v = qkv[0], qkv[1], qkv[2]
-        ab = self.gdn_proj[:, 2 * h * dk + 2 * h * dv:]
+        ab = proj[:, 2 * h * dk + 2 * h * dv:]
         alpha, beta = self.capture_alpha[gi], self.capture_beta[gi]
-        dc.stack_gdn_conv_gates(self.gdn_proj, S["window"], L["conv"], qkv, ab, L["a_log"], L["dt_bias"], alpha, beta,
-                                h, dk)
-        dc.gdn_step(S["snapshot"], self.state_out[gi], q, k, v, alpha, beta, out=self.gdn_o,
-                    q_scale=1.0 / math.sqrt(dk))
-        z = self.gdn_proj[:, 2 * h * dk + h * dv:]
+        dc.stack_gdn_conv_gates(proj, S["window"], L["conv"], qkv, ab, L["a_log"], L["dt_bias"], alpha, beta,
+                                h, dk, parents=self.parents)
+        if self.parents is None:
+            dc.gdn_step(S["snapshot"], self.state_out[gi], q, k, v, alpha, beta, out=self.gdn_o,
+                        q_scale=1.0 / math.sqrt(dk))
+        else:  # no state after a tree round: commit() replays the accepted path
+            dc.gdn_step_tree(S["snapshot"], q, k, v, alpha, beta, self.parents, self.gdn_o,
+                             q_scale=1.0 / math.sqrt(dk))
+        z = proj[:, 2 * h * dk + h * dv:]
         dc.stack_gated_norm(self.gdn_o, z, L["gdn_norm"], self.gdn_normed, cfg.eps)
         return self._qmm_reduced(self.gdn_normed, L["out_proj"])
 
@@ -457,9 +470,9 @@ class VerifyStack:
         cfg, p, dc = self.cfg, self.plan, self.dc
         self._qmm(self.normed, L["qkv"], self.qkv)
         dc.stack_attn_prep(self.qkv, L["q_norm"], L["k_norm"], S["cache_k"], S["cache_v"], p.attn_heads, p.kv_heads,
-                           cfg.rotary_dim, cfg.context, cfg.eps, cfg.rope_theta)
+                           cfg.rotary_dim, cfg.context, cfg.eps, cfg.rope_theta, parents=self.parents)
         dc.stack_attn_decode(self.qkv, S["cache_k"], S["cache_v"], self.attn_out, p.attn_heads, p.kv_heads,
-                             cfg.context, 1.0 / math.sqrt(cfg.head_dim))
+                             cfg.context, 1.0 / math.sqrt(cfg.head_dim), parents=self.parents)
         return self._qmm_reduced(self.attn_out, L["o_proj"])
 
     def _mlp(self, L):
@@ -514,6 +527,65 @@ class VerifyStack:
         self._forward_body(hidden)
         return self._accept_body(proposals)
 
+    def set_tree(self, parents):
+        """The next rounds verify a speculative tree: parents[r] is row r's parent row (-1
+        for the anchor row 0), cfg.block rows.  Call between rounds, never while a round is
+        being captured."""
+        from tree import SpeculativeTreePlan
+        if not self.tree:
+            raise RuntimeError("this stack was built without tree=True")
+        plan = SpeculativeTreePlan(parents)
+        if plan.rows != self.cfg.block:
+            raise ValueError(f"a tree of {plan.rows} rows for a block of {self.cfg.block}")
+        self.parents.copy_(torch.tensor(plan.parents, dtype=torch.int32))
+        self.tree_plan = plan
+        return plan
+
+    def verify_tree(self, hidden, tokens):
+        """One tree round: forward of the block under the current tree, LM head argmax
+        combined over the ranks, then the accepted-path walk on the host
+        (DFlashDraftTree.acceptedPath).  tokens: the drafted token of every row (host
+        ints, row 0 the anchor's).  Returns (accepted rows, the target's next token)."""
+        from tree import accepted_path
+        plan = self.tree_plan or self.set_tree([-1] + list(range(self.cfg.block - 1)))
+        proposals = torch.tensor([int(t) for t in tokens[1:]], dtype=torch.int32, device=self.device)
+        target, _ = self.verify(hidden, proposals)  # the chain accept count is not used
+        return accepted_path(tokens, plan, target.cpu().tolist())
+
+    def commit(self, rows):
+        """After a round, make its accepted rows (anchor first: a chain's 0 .. keep-1, a
+        tree's accepted path) the committed state, as rollbackGatedDeltaRound / Tree do
+        (DFlashSpeculativeGenerator.swift:453-460): every gated-delta state is replayed
+        from its snapshot over those rows' capture (dflash_gdn_replay) and its conv window
+        rebuilt from their conv inputs (dflash_gdn_conv_rollback); after a tree round the
+        rows' attention cache entries move to context .. context + keep - 1
+        (dflash_stack_kv_compact).  The snapshots and windows are updated in place, so a
+        captured round keeps its pointers; advancing the context is the caller's."""
+        cfg, p, dc = self.cfg, self.plan, self.dc
+        rows = [int(r) for r in rows]
+        keep = len(rows)
+        if not 1 <= keep <= cfg.block or rows[0] != 0:
+            raise ValueError(f"accepted rows {rows}: 1..{cfg.block} rows starting at the anchor")
+        if self.tree_plan is not None and not self.tree_plan.is_root_path(rows):
+            raise ValueError(f"rows {rows} are not a root path of the current tree")
+        if self.tree_plan is None and rows != list(range(keep)):
+            raise ValueError(f"a chain round keeps rows 0 .. keep-1, not {rows}")
+        C = 3 * p.gdn_heads * cfg.gdn_dk
+        gi = 0
+        for L, S in zip(self.w["layers"], self.state["layers"]):
+            if L["kind"] == "gdn":
+                qkv = self.capture_qkv[gi]
+                dc.gdn_replay(S["snapshot"][None], self.state_out[gi][None], qkv[1][None], qkv[2][None],
+                              self.capture_alpha[gi][None], self.capture_beta[gi][None], keep=keep, rows=rows)
+                S["snapshot"].copy_(self.state_out[gi])
+                conv_in = self.gdn_proj[gi][:, :C].contiguous()
+                window = torch.empty_like(S["window"])
+                dc.gdn_conv_rollback(S["window"][None], window[None], conv_in[None], keep=keep, rows=rows)
+                S["window"].copy_(window)
+                gi += 1
+            elif rows != list(range(keep)):
+                dc.stack_kv_compact(S["cache_k"], S["cache_v"], cfg.context, rows)
+
     def capture(self, hidden_buf, proposals=None):
         """Capture forward(hidden_buf) — or, with proposals, the whole verify round — as a
         CUDA graph (run eagerly once first)."""
@@ -558,6 +630,9 @@ def main(argv=None) -> int:
     ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
                     help="peer: NVLink stores into the other ranks' exchange buffers, summed by the next "
                          "RMSNorm; nccl: torch.distributed.all_reduce")
+    ap.add_argument("--tree", default=None,
+                    help="verify a speculative tree instead of a chain: comma-separated parent rows, one per "
+                         "block row (-1 for the anchor), e.g. -1,0,0,1,1,2,3,5")
     args = ap.parse_args(argv)
 
     sys.path.insert(0, str(HERE))
@@ -575,7 +650,10 @@ def main(argv=None) -> int:
     if args.context is not None:
         cfg = replace(cfg, context=args.context)
 
-    stack = VerifyStack(cfg, rank, world, seed=args.seed, device=dev, group=pg, allreduce=args.allreduce)
+    stack = VerifyStack(cfg, rank, world, seed=args.seed, device=dev, group=pg, allreduce=args.allreduce,
+                        tree=args.tree is not None)
+    if args.tree is not None:
+        stack.set_tree([int(v) for v in args.tree.split(",")])
     hidden = make_block(cfg, args.seed, dev)
     proposals = torch.zeros(cfg.block - 1, dtype=torch.int32, device=dev)
 
@@ -611,7 +689,7 @@ def main(argv=None) -> int:
             "tp": world, "steps": args.steps, "warmup": args.warmup,
             "weight_bytes_per_gpu": wbytes, "weight_gbs_per_gpu": round(wbytes / (ms / 1000.0) / 1e9, 1),
             "kernels_per_forward": stack.kernels_per_forward(), "all_reduces_per_forward": 2 * cfg.layers,
-            "allreduce": stack.allreduce,
+            "allreduce": stack.allreduce, "tree": None if args.tree is None else stack.tree_plan.parents,
             "config": {k: v for k, v in asdict(cfg).items()}, "out_abs_sum": checksum,
         }), flush=True)
     del g

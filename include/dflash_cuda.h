@@ -139,6 +139,19 @@ int dflash_gdn_step(const float* state_in, float* state_out, const dflash_bf16* 
                     const float* beta, dflash_bf16* out, int T, int heads, int dk, int dv,
                     float q_scale, dflash_stream_t stream);
 
+/* The verify forward of one gated-delta layer over the T rows of a speculative tree
+ * round (the target forward run with mtpTreePlanKey, SpeculativeTreeTests.swift:108-140):
+ * parents (device int32 [T], read in stream order) gives each row's parent row, -1 for
+ * the anchor row 0 and an earlier row otherwise (a malformed entry makes its row a root).
+ * Row t's output is that of a chain step over its root-to-t path from state_in, the
+ * pre-round snapshot, which is left untouched; no state is written, since the state
+ * after the round is the replay (dflash_gdn_replay) of the accepted path's rows.
+ * Layouts as for dflash_gdn_step; 1 <= T <= 32. */
+int dflash_gdn_step_tree(const float* state_in, const dflash_bf16* q, const dflash_bf16* k,
+                         const dflash_bf16* v, const float* alpha, const float* beta,
+                         const int32_t* parents, dflash_bf16* out, int T, int heads, int dk, int dv,
+                         float q_scale, dflash_stream_t stream);
+
 /* Rollback of a verify round for `layers` gated-delta layers at once
  * (rollbackGatedDeltaRound / rollbackGatedDeltaTree, called at
  * DFlashSpeculativeGenerator.swift:455-460).  From the pre-round snapshot, replays

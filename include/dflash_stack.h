@@ -69,6 +69,45 @@ int dflash_stack_attn_decode(const dflash_bf16* qkv, int ld, const dflash_bf16* 
                              dflash_stream_t stream);
 
 /* ------------------------------------------------------------------------------
+ * Speculative tree rounds (the target forward run with mtpTreePlanKey,
+ * Tests/DFlashKitTests/SpeculativeTreeTests.swift:108-140).  The M block rows carry a
+ * parent list `parents` (device int32 [M], read in stream order, so a CUDA graph can be
+ * replayed with a new tree): -1 for the anchor row 0, an earlier row otherwise (a
+ * malformed entry makes its row a root).  Each row computes what a chain over its
+ * root-to-row path computes: M <= 32.
+ * -------------------------------------------------------------------------------- */
+
+/* dflash_stack_gdn_conv_gates over a tree: tap i of row t reads its ancestor kc-1-i steps
+ * up, and the window where that path runs past the anchor. */
+int dflash_stack_gdn_conv_gates_tree(const dflash_bf16* x, int ld, const dflash_bf16* window,
+                                     const dflash_bf16* weight, dflash_bf16* y, const dflash_bf16* ab, int ld_ab,
+                                     const float* a_log, const float* dt_bias, float* alpha, float* beta, int M,
+                                     int heads, int dk, int kc, const int32_t* parents, dflash_stream_t stream);
+
+/* dflash_stack_attn_prep over a tree: rotary position pos0 + depth(t); k and v still go
+ * to cache row pos0 + t. */
+int dflash_stack_attn_prep_tree(dflash_bf16* qkv, int ld, const dflash_bf16* q_norm, const dflash_bf16* k_norm,
+                                dflash_bf16* cache_k, dflash_bf16* cache_v, int M, int hq, int hkv, int d, int rot,
+                                int pos0, int max_len, float eps, float theta, const int32_t* parents,
+                                dflash_stream_t stream);
+
+/* dflash_stack_attn_decode over a tree: token t attends to cache rows 0 .. pos0 - 1 and to
+ * pos0 + a for each row a on its root-to-t path (the tree attention mask,
+ * SpeculativeTreeTests.swift:50-66). */
+int dflash_stack_attn_decode_tree(const dflash_bf16* qkv, int ld, const dflash_bf16* cache_k,
+                                  const dflash_bf16* cache_v, dflash_bf16* out, int M, int hq, int hkv, int d,
+                                  int pos0, int max_len, float scale, const int32_t* parents,
+                                  dflash_stream_t stream);
+
+/* After a tree round: moves cache rows pos0 + rows[i] to pos0 + i (i < keep) in cache_k
+ * and cache_v, so the accepted path sits where a chain round would have put it (its
+ * rotary positions pos0 + depth already match).  Caches bf16 [layers][hkv][max_len][d]
+ * with layer_stride elements between layers (0 when layers = 1); rows is a host array
+ * with 1 <= keep <= 32 and pos0 + rows[i] < max_len. */
+int dflash_stack_kv_compact(dflash_bf16* cache_k, dflash_bf16* cache_v, int layers, long long layer_stride, int hkv,
+                            int d, int pos0, int max_len, const int32_t* rows, int keep, dflash_stream_t stream);
+
+/* ------------------------------------------------------------------------------
  * Tensor-parallel all-reduce over peer memory (one process per GPU of one node).
  * Each rank allocates one exchange buffer (dflash_tp_exchange_alloc, sized by
  * dflash_tp_exchange_bytes for the world size and the [M, H] reduced), shares it through

@@ -56,14 +56,34 @@ def silu(t: torch.Tensor) -> torch.Tensor:
     return t / (1.0 + torch.exp(-t))
 
 
-def conv_silu(x: torch.Tensor, window: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    """x [M, C]; window [kc-1, C] (older first); w [C, kc], last tap on the current row."""
+def tree_paths(parents, M: int):
+    """For block rows with parent list `parents` (-1: a root; an entry outside [0, r) is
+    treated as -1): each row's root-to-row path (root first), and one path per leaf, the
+    leaves in row order.  A chain is parents = [-1, 0, 1, ...]."""
+    par = [int(p) if 0 <= int(p) < r else -1 for r, p in enumerate(parents)]
+    assert len(par) == M
+    anc = []
+    for r in range(M):
+        path = [r]
+        while par[path[-1]] >= 0:
+            path.append(par[path[-1]])
+        anc.append(path[::-1])
+    has_child = {p for p in par if p >= 0}
+    leaves = [r for r in range(M) if r not in has_child]
+    return anc, [anc[r] for r in leaves]
+
+
+def conv_silu(x: torch.Tensor, window: torch.Tensor, w: torch.Tensor, parents=None) -> torch.Tensor:
+    """x [M, C]; window [kc-1, C] (older first); w [C, kc], last tap on the current row.
+    Row t convolves the window followed by the rows before it (a chain) or by its
+    root-to-t path (a tree with parent list `parents`)."""
     M = x.shape[0]
     kc = w.shape[1]
-    hist = torch.cat([window.float(), x], dim=0)  # [kc-1+M, C]
+    anc, _ = tree_paths(parents if parents is not None else [-1] + list(range(M - 1)), M)
     out = torch.zeros_like(x)
     for t in range(M):
-        seg = hist[t:t + kc]  # rows t .. t+kc-1; the last one is x[t]
+        hist = torch.cat([window.float(), x[anc[t]]], dim=0)
+        seg = hist[-kc:]  # the last kc inputs of t's history; the last one is x[t]
         out[t] = (seg * w.float().t()).sum(dim=0)
     return rb(silu(out))
 
@@ -116,33 +136,40 @@ def head_rmsnorm(v: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     return rb(v * torch.rsqrt(v.pow(2).mean(dim=-1, keepdim=True) + eps) * w.float())
 
 
-def attention(q, gate, cache_k, cache_v, pos0: int, scale: float):
+def attention(q, gate, cache_k, cache_v, pos0: int, scale: float, visible=None):
     """q, gate [M, hq, d]; caches [hkv, L, d] (fp32 holding bf16).  Token t sees keys
-    0 .. pos0 + t.  Returns rb(softmax(q K^T scale) V * sigmoid(gate)) [M, hq*d]."""
+    0 .. pos0 + t, or (a tree) keys 0 .. pos0 - 1 and pos0 + a for the block rows a in
+    visible[t].  Returns rb(softmax(q K^T scale) V * sigmoid(gate)) [M, hq*d]."""
     M, hq, d = q.shape
     hkv = cache_k.shape[0]
     out = torch.zeros(M, hq, d)
     for h in range(hq):
         kv = h // (hq // hkv)
         for t in range(M):
-            n = pos0 + t + 1
-            s = (cache_k[kv, :n].double() @ q[t, h].double()) * scale
+            keys = list(range(pos0 + t + 1)) if visible is None else list(range(pos0)) + [pos0 + a for a in visible[t]]
+            s = (cache_k[kv, keys].double() @ q[t, h].double()) * scale
             p = torch.softmax(s, dim=0)
-            out[t, h] = (p @ cache_v[kv, :n].double()).float()
+            out[t, h] = (p @ cache_v[kv, keys].double()).float()
     return rb(out * torch.sigmoid(gate)).reshape(M, hq * d)
 
 
 def forward(cfg, plan, weights: dict, state: dict, hidden: torch.Tensor,
-            all_reduce: Optional[Callable[[torch.Tensor], None]] = None) -> dict:
-    """One rank's verify forward.  Returns the final hidden states and, per layer, the
-    capture and state the CUDA stack produces (gated-delta conv output, alpha, beta,
-    state after the block; attention cache rows written)."""
+            all_reduce: Optional[Callable[[torch.Tensor], None]] = None, parents=None) -> dict:
+    """One rank's verify forward over the M = hidden.shape[0] block rows.  Returns the final
+    hidden states and, per layer, the capture and state the CUDA stack produces
+    (gated-delta conv output, alpha, beta, state after the block; attention cache rows
+    written).  With a tree parent list (`parents`, the tree round of mtpTreePlanKey) every
+    row computes what a chain over its root-to-row path computes: convolution and
+    recurrence along the path, rotary position context + depth, attention to the prefix
+    and the path's rows; the state entry is then None (the state after a tree round is the
+    replay of the accepted path)."""
     all_reduce = all_reduce or (lambda t: None)
-    M, H = cfg.block, cfg.hidden
+    M, H = hidden.shape[0], cfg.hidden
+    anc, paths = tree_paths(parents, M) if parents is not None else (None, None)
     eps = cfg.eps
     resid = torch.zeros(M, H)
     delta = hidden.detach().cpu().float()
-    cap = {"qkv": [], "alpha": [], "beta": [], "state": [], "cache_k": [], "cache_v": []}
+    cap = {"qkv": [], "alpha": [], "beta": [], "state": [], "cache_k": [], "cache_v": [], "conv_in": []}
     h, dk, dv = plan.gdn_heads, cfg.gdn_dk, cfg.gdn_dv
     d, hq, hkv = cfg.head_dim, plan.attn_heads, plan.kv_heads
     cpu = lambda t: t.detach().cpu()
@@ -151,12 +178,23 @@ def forward(cfg, plan, weights: dict, state: dict, hidden: torch.Tensor,
         normed = add_rmsnorm(resid, delta, L["ln"], eps)
         if L["kind"] == "gdn":
             proj = qmm(normed, L["in_proj"])
-            conv = conv_silu(proj[:, :3 * h * dk], cpu(S["window"]), L["conv"])
+            cap["conv_in"].append(proj[:, :3 * h * dk])
+            conv = conv_silu(proj[:, :3 * h * dk], cpu(S["window"]), L["conv"], parents)
             q, k, v = (conv[:, i * h * dk:(i + 1) * h * dk].reshape(M, h, dk) for i in range(3))
             q, k = l2norm_heads(q), l2norm_heads(k)
             ab = proj[:, 2 * h * dk + 2 * h * dv:]
             alpha, beta = gdn_gates(ab, L["a_log"], L["dt_bias"], h)
-            st, o = gdn_step(cpu(S["snapshot"]), q, k, v, alpha, beta, 1.0 / math.sqrt(dk))
+            if parents is None:
+                st, o = gdn_step(cpu(S["snapshot"]), q, k, v, alpha, beta, 1.0 / math.sqrt(dk))
+            else:  # each row's output from the first leaf's path (row order) that holds it
+                st, o, done = None, torch.zeros(M, h, dv), set()
+                for path in paths:
+                    _, op = gdn_step(cpu(S["snapshot"]), q[path], k[path], v[path], alpha[path], beta[path],
+                                     1.0 / math.sqrt(dk))
+                    for i, r in enumerate(path):
+                        if r not in done:
+                            o[r] = op[i]
+                            done.add(r)
             cap["qkv"].append(torch.stack([q, k, v]))
             cap["alpha"].append(alpha)
             cap["beta"].append(beta)
@@ -169,7 +207,7 @@ def forward(cfg, plan, weights: dict, state: dict, hidden: torch.Tensor,
             gate = qkv[:, hq * d:2 * hq * d].reshape(M, hq, d)
             kn = qkv[:, 2 * hq * d:2 * hq * d + hkv * d].reshape(M, hkv, d)
             vn = qkv[:, 2 * hq * d + hkv * d:].reshape(M, hkv, d)
-            pos = torch.arange(cfg.context, cfg.context + M)
+            pos = cfg.context + (torch.arange(M) if parents is None else torch.tensor([len(a) - 1 for a in anc]))
             q = rb(rope(head_rmsnorm(q, L["q_norm"], eps), cfg.rotary_dim, cfg.rope_theta, pos))
             kn = rb(rope(head_rmsnorm(kn, L["k_norm"], eps), cfg.rotary_dim, cfg.rope_theta, pos))
             ck, cv = cpu(S["cache_k"]).float().clone(), cpu(S["cache_v"]).float().clone()
@@ -177,7 +215,7 @@ def forward(cfg, plan, weights: dict, state: dict, hidden: torch.Tensor,
             cv[:, cfg.context:cfg.context + M] = vn.transpose(0, 1)
             cap["cache_k"].append(ck)
             cap["cache_v"].append(cv)
-            part = qmm(attention(q, gate, ck, cv, cfg.context, 1.0 / math.sqrt(d)), L["o_proj"])
+            part = qmm(attention(q, gate, ck, cv, cfg.context, 1.0 / math.sqrt(d), anc), L["o_proj"])
         all_reduce(part)
         delta = rb(part)
         normed = add_rmsnorm(resid, delta, L["post_ln"], eps)

@@ -223,3 +223,39 @@ def test_qmm_ex_tp_and_accept_argument_errors(dc):
     assert L.dflash_stack_add_rmsnorm_reduce(FAKE, FAKE, 2, 0, FAKE, FAKE, 8, 5122, 1e-6, None) == 2
     assert L.dflash_stack_gdn_conv_gates(FAKE, 144, FAKE, FAKE, FAKE, FAKE, 8, FAKE, FAKE, FAKE, FAKE, 8, 1, 48, 4,
                                          None) == 2
+
+
+def test_tree_entry_argument_errors(dc):
+    """Tree rounds: a parent list is required, at most 32 rows, then the chain checks."""
+    L = dc.lib
+    cg = lambda parents, M=8, dk=128: L.dflash_stack_gdn_conv_gates_tree(
+        FAKE, 3 * 4 * dk + 8, FAKE, FAKE, FAKE, FAKE, 8, FAKE, FAKE, FAKE, FAKE, M, 4, dk, 4, parents, None)
+    assert cg(None) == 1 and cg(FAKE, M=33) == 1 and cg(FAKE, dk=48) == 2
+    prep = lambda parents, M=8, d=256: L.dflash_stack_attn_prep_tree(
+        FAKE, 4096, FAKE, FAKE, FAKE, FAKE, M, 4, 2, d, 64, 0, 64, 1e-6, 1e4, parents, None)
+    assert prep(None) == 1 and prep(FAKE, M=40) == 1 and prep(FAKE, d=96) == 2
+    dec = lambda parents, M=8, hq=4: L.dflash_stack_attn_decode_tree(
+        FAKE, 4096, FAKE, FAKE, FAKE, M, hq, 2, 256, 0, 64, 0.1, parents, None)
+    assert dec(None) == 1 and dec(FAKE, M=33) == 1 and dec(FAKE, hq=3) == 1
+    step = lambda parents, T=8, dk=128, out=FAKE: L.dflash_gdn_step_tree(
+        FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, parents, out, T, 4, dk, 128, 1.0, None)
+    assert step(None) == 1 and step(FAKE, out=None) == 1
+    assert step(FAKE, T=33) == 2 and step(FAKE, T=0) == 2 and step(FAKE, dk=96) == 2
+    assert L.dflash_gdn_step_tree(FAKE + 4, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 8, 4, 128, 128, 1.0,
+                                  None) == 3
+
+
+def test_kv_compact_argument_errors(dc):
+    L = dc.lib
+    rows = lambda *r: (ctypes.c_int32 * len(r))(*r)
+    kv = lambda ck=FAKE, cv=FAKE + 0x100000, layers=1, stride=0, d=128, pos0=30, max_len=40, r=rows(0, 2, 5), \
+        keep=3: L.dflash_stack_kv_compact(ck, cv, layers, stride, 2, d, pos0, max_len, r, keep, None)
+    assert kv(cv=FAKE) == 1                              # k and v must be distinct caches
+    assert kv(r=rows(0, 2, 10)) == 1                     # pos0 + 10 is past max_len
+    assert kv(r=rows(0, -1, 2)) == 1
+    assert kv(keep=0) == 1 and kv(keep=33) == 1
+    assert kv(layers=2, stride=100) == 1                 # layers would overlap
+    assert kv(layers=2, stride=2 * 40 * 128 + 4) == 3    # layer stride not 16-byte aligned
+    assert kv(d=96) == 2
+    assert kv(ck=FAKE + 8) == 3
+    assert L.dflash_stack_kv_compact(FAKE, FAKE + 0x100000, 1, 0, 2, 128, 30, 40, None, 3, None) == 1
