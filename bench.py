@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -247,10 +248,19 @@ def run_ours(args):
     value = world * per_gpu_gbs
 
     e2e = e2e_through_abi(dc, dev, x, copies, args, world)
-    if world > 1:
-        t = torch.tensor([e2e["ms"]], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e["ms"] = float(t.item())
+    try:  # the one-call host-buffer entry point, checked bit for bit before it is timed
+        want = []
+        for (w_, s_, b_) in copies:
+            dc.qmm(x_d[:M], w_, s_, b_, GROUP, BITS, out=y_d[:M], workspace=ws)
+            want.append(y_d[:M].cpu())
+        e2e_host = e2e_host_entry(dc, dev, x, copies, args, want)
+    except Exception as exc:  # reported; the three-call figure above stands
+        e2e_host = {"error": repr(exc)[:300], "ms": float("inf")}
+    if world > 1:  # every rank takes both reductions, failed or not
+        for rec in (e2e, e2e_host):
+            t = torch.tensor([min(rec["ms"], 1e30)], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            rec["ms"] = float(t.item()) if t.item() < 1e30 else float("inf")
 
     peak, peak_kind = measured_peak()
     traffic = None
@@ -283,10 +293,7 @@ def run_ours(args):
                          "frac": round(per_gpu_gbs / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic, "algorithmic_bytes": bytes8},
             "cpu_baseline": cpu,
-            "e2e": {"value": round(world * bytes8 / (e2e["ms"] * 1e-3 / args.steps) / 1e9, 1), "unit": "GB/s",
-                    "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                    "us_per_step": round(e2e["ms"] * 1e3 / args.steps, 3),
-                    "path": "pinned host x -> dflash_qmm (C ABI via ctypes) -> pinned host y, every step; steps alternate over two streams so copies overlap kernels"},
+            "e2e": e2e_line(e2e, e2e_host, world, bytes8, args.steps),
             "gpu_launches": KERNELS_PER_CALL * args.steps,
             "gdn_replay_config5": gdn,
             "clocks": clocks,
@@ -340,6 +347,78 @@ def gpu_ids(world):
         ids = [int(v) for v in vis.split(",") if v.strip().isdigit()]
         return ids[:world] if ids else list(range(world))
     return list(range(world))
+
+
+E2E_PATHS = {
+    "host_entry": "pinned host x -> dflash_qmm_host (C ABI via ctypes: copy in, matmul, copy out queued by one "
+                  "library call) -> pinned host y, every step; steps alternate over two streams so copies overlap "
+                  "kernels",
+    "three_calls": "pinned host x -> device (torch copy) -> dflash_qmm (C ABI via ctypes) -> pinned host y (torch "
+                   "copy), every step; steps alternate over two streams so copies overlap kernels",
+}
+
+
+def e2e_line(three, host, world, nbytes, steps):
+    """The e2e key: the one-call host-buffer entry point when it ran (and passed its
+    bit-exact check), else the three-call path; both figures are listed."""
+    def fig(rec):
+        if "error" in rec or not math.isfinite(rec["ms"]):
+            return {"error": rec.get("error", "not finite")}
+        return {"value": round(world * nbytes / (rec["ms"] * 1e-3 / steps) / 1e9, 1), "unit": "GB/s",
+                "us_per_step": round(rec["ms"] * 1e3 / steps, 3)}
+    figs = {"host_entry": fig(host), "three_calls": fig(three)}
+    best = "host_entry" if "value" in figs["host_entry"] else "three_calls"
+    return {**figs[best], "h2d_bytes_per_step": three["h2d"], "d2h_bytes_per_step": three["d2h"],
+            "path": E2E_PATHS[best], "paths": figs}
+
+
+def e2e_host_entry(dc, dev, x, copies, args, want):
+    """Per step ONE library call, dflash_qmm_host through ctypes: it queues the copy of
+    pinned host x into its workspace, the matmul and the copy of y to pinned host memory
+    on the step's stream.  Steps alternate between two streams (each with its own
+    workspace and host output), as in e2e_through_abi.  Before timing, one call per weight
+    copy must reproduce dflash_qmm's bits (`want`)."""
+    import ctypes
+    import torch
+    streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+    x_h = torch.from_numpy(np.ascontiguousarray(x[:M]).view(np.int16)).view(torch.bfloat16).pin_memory()
+    fn = dc.lib.dflash_qmm_host
+    lanes = []
+    for st in streams:
+        ws = dc.Workspace(dc.qmm_host_workspace_bytes(M, N, K, GROUP, BITS), dev)
+        y_h = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+        lanes.append({"ws": ws, "y_h": y_h, "stream": st,
+                      "args": [(x_h.data_ptr(), w.data_ptr(), s_.data_ptr(), b.data_ptr(), y_h.data_ptr(), M, N, K,
+                                GROUP, BITS, ws.buf.data_ptr(), ctypes.c_size_t(ws.nbytes), st.cuda_stream)
+                               for (w, s_, b) in copies]})
+    R = len(copies)
+    torch.cuda.synchronize(dev)
+    for r in range(R):
+        lane = lanes[r & 1]
+        dc.check(fn(*lane["args"][r]))
+        lane["stream"].synchronize()
+        if not torch.equal(lane["y_h"], want[r]):
+            raise RuntimeError(f"dflash_qmm_host differs from dflash_qmm on weight copy {r}")
+
+    def step(i):
+        lane = lanes[i & 1]
+        dc.check(fn(*lane["args"][i % R]))
+
+    for i in range(min(args.warmup, 200)):
+        step(i)
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(streams[0])
+    streams[1].wait_event(t0)
+    for i in range(args.steps):
+        step(i)
+    done = torch.cuda.Event()
+    done.record(streams[1])
+    streams[0].wait_event(done)
+    t1.record(streams[0])
+    torch.cuda.synchronize(dev)
+    return {"ms": t0.elapsed_time(t1), "h2d": M * K * 2, "d2h": M * N * 2}
 
 
 def e2e_through_abi(dc, dev, x, copies, args, world):

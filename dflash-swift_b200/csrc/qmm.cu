@@ -1526,6 +1526,52 @@ extern "C" int dflash_qmm(const dflash_bf16* x, const uint32_t* w, const dflash_
     return qmm::dispatch_group<8>(s, x, w, scales, biases, y, workspace, st);
 }
 
+// ------------------------------------------------------------------ entry point on host buffers
+//
+// dflash_qmm for x and y in host memory: the workspace also holds the device copies of
+// x and y, and the call queues the copy in, the two kernels and the copy out on the
+// stream, so a host issues one library call per matmul instead of three.
+namespace dflash {
+namespace qmm {
+
+inline size_t round256(size_t v) { return (v + 255) / 256 * 256; }
+
+}  // namespace qmm
+}  // namespace dflash
+
+extern "C" size_t dflash_qmm_host_workspace_bytes(int M, int N, int K, int group_size, int bits) {
+    const size_t packets = dflash_qmm_workspace_bytes(M, N, K, group_size, bits);
+    if (!packets) return 0;
+    return packets + dflash::qmm::round256((size_t)2 * M * K) + dflash::qmm::round256((size_t)2 * M * N);
+}
+
+extern "C" int dflash_qmm_host(const dflash_bf16* x_host, const uint32_t* w, const dflash_bf16* scales,
+                               const dflash_bf16* biases, dflash_bf16* y_host, int M, int N, int K, int group_size,
+                               int bits, void* workspace, size_t workspace_bytes, dflash_stream_t stream) {
+    using namespace dflash;
+    qmm::Shape s{M, N, K, group_size, bits};
+    if (int st = qmm::validate(s)) return st;
+    if (!x_host || !w || !scales || !biases || !y_host)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_qmm_host: null pointer");
+    if (!aligned16(w)) return fail(DFLASH_ERR_MISALIGNED, "dflash_qmm_host: w must be 16-byte aligned");
+    const size_t need = dflash_qmm_host_workspace_bytes(M, N, K, group_size, bits);
+    if (!workspace || workspace_bytes < need || !aligned16(workspace))
+        return fail(DFLASH_ERR_WORKSPACE,
+                    "dflash_qmm_host: a 16-byte aligned workspace of %zu bytes is required (got %zu)", need,
+                    workspace_bytes);
+    const size_t packets = qmm::workspace_size(M, K, group_size, bits);
+    uint8_t* base = static_cast<uint8_t*>(workspace);
+    dflash_bf16* x_dev = reinterpret_cast<dflash_bf16*>(base + packets);
+    dflash_bf16* y_dev = reinterpret_cast<dflash_bf16*>(base + packets + qmm::round256((size_t)2 * M * K));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    DFLASH_CUDA_TRY(cudaMemcpyAsync(x_dev, x_host, (size_t)2 * M * K, cudaMemcpyDefault, st));
+    const int r = bits == 4 ? qmm::dispatch_group<4>(s, x_dev, w, scales, biases, y_dev, workspace, st)
+                            : qmm::dispatch_group<8>(s, x_dev, w, scales, biases, y_dev, workspace, st);
+    if (r) return r;
+    DFLASH_CUDA_TRY(cudaMemcpyAsync(y_host, y_dev, (size_t)2 * M * N, cudaMemcpyDefault, st));
+    return DFLASH_OK;
+}
+
 extern "C" int dflash_qmm_ex(const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scales,
                              const dflash_bf16* biases, dflash_bf16* y, int M, int N, int K, int group_size, int bits,
                              void* workspace, size_t workspace_bytes, const dflash_qmm_options* opts,

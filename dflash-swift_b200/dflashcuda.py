@@ -44,7 +44,7 @@ DEVERR_TEST_WAIT = 0x80000000
 EXPORTED = (
     "dflash_version", "dflash_last_error", "dflash_status_string", "dflash_device_error",
     "dflash_test_bounded_wait", "dflash_qmm_workspace_bytes", "dflash_qmm", "dflash_qmm_noalloc",
-    "dflash_qmm_supported",
+    "dflash_qmm_supported", "dflash_qmm_host_workspace_bytes", "dflash_qmm_host",
     "dflash_gdn_step", "dflash_gdn_replay", "dflash_gdn_conv_rollback",
     # include/dflash_stack.h: glue of the tensor-parallel verify stack
     "dflash_stack_add_rmsnorm", "dflash_stack_silu_mul", "dflash_stack_conv_silu", "dflash_stack_gdn_gates",
@@ -87,6 +87,8 @@ def _load() -> ctypes.CDLL:
         "dflash_qmm": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp], _i),
         "dflash_qmm_noalloc": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp], _i),
         "dflash_qmm_supported": ([_i, _i, _i, _i], _i),
+        "dflash_qmm_host_workspace_bytes": ([_i, _i, _i, _i, _i], _sz),
+        "dflash_qmm_host": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp], _i),
         "dflash_gdn_step": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, ctypes.c_float, _vp], _i),
         "dflash_gdn_replay": ([_vp, _vp, _vp, _vp, _vp, _vp, ctypes.POINTER(ctypes.c_int32), _i, _i, _i, _i,
                                _i, _i, _vp], _i),
@@ -207,6 +209,27 @@ def qmm(x, w, scales, biases, group_size: int, bits: int, out=None, workspace: O
     check(lib.dflash_qmm(_ptr(x), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out), M, N, K, group_size, bits,
                          ws.buf.data_ptr(), ws.nbytes, _stream(stream)))
     return out
+
+
+def qmm_host_workspace_bytes(M: int, N: int, K: int, group_size: int, bits: int) -> int:
+    return int(lib.dflash_qmm_host_workspace_bytes(M, N, K, group_size, bits))
+
+
+def qmm_host(x_host, w, scales, biases, group_size: int, bits: int, out_host=None,
+             workspace: Optional[Workspace] = None, stream=None):
+    """dflash_qmm_host: x bf16 [M, K] and the result in HOST memory (pinned for
+    asynchronous copies), weights on the GPU; one library call queues copy in, matmul
+    and copy out on the stream.  The result is valid after the stream has run past it."""
+    import torch
+    M, K = x_host.shape
+    N = w.shape[0]
+    if out_host is None:
+        out_host = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    need = qmm_host_workspace_bytes(M, N, K, group_size, bits)
+    ws = workspace.ensure(need) if workspace is not None else default_workspace(need, w.device)
+    check(lib.dflash_qmm_host(_ptr(x_host), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out_host), M, N, K, group_size,
+                              bits, ws.buf.data_ptr(), ws.nbytes, _stream(stream)))
+    return out_host
 
 
 def qmm_noalloc(x, w, scales, biases, group_size: int, bits: int, out=None, stream=None):

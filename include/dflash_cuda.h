@@ -113,6 +113,20 @@ int dflash_qmm_noalloc(const dflash_bf16* x, const uint32_t* w, const dflash_bf1
                        const dflash_bf16* biases, dflash_bf16* y, int M, int N, int K, int group_size,
                        int bits, dflash_stream_t stream);
 
+/* dflash_qmm with x and y in HOST memory (the call a host makes when its activations
+ * live on the CPU side, e.g. a ctypes or Swift host holding MLX-style arrays): on
+ * `stream` it copies x in, runs the matmul, and copies y out, so the host issues one
+ * call instead of a copy, a matmul and a copy.  w, scales and biases are device memory as
+ * for dflash_qmm.  The workspace (device, 16-byte aligned) also holds the device copies of
+ * x and y: dflash_qmm_host_workspace_bytes gives its size (0 for an unsupported shape).
+ * Pinned host buffers (cudaHostAlloc / cudaHostRegister) make the copies asynchronous;
+ * y_host holds the result once the stream has run past the call (an event recorded
+ * after it, or a stream synchronise).  Give each stream its own workspace. */
+size_t dflash_qmm_host_workspace_bytes(int M, int N, int K, int group_size, int bits);
+int dflash_qmm_host(const dflash_bf16* x_host, const uint32_t* w, const dflash_bf16* scales,
+                    const dflash_bf16* biases, dflash_bf16* y_host, int M, int N, int K, int group_size,
+                    int bits, void* workspace, size_t workspace_bytes, dflash_stream_t stream);
+
 /* Static half of the reference's eligibility test (SmallMQuantizedMatmul.isEligible,
  * SmallMQuantizedMatmul.swift:193-201) for a layer of this library: 1 when
  * dflash_qmm covers (N, K, group_size, bits) for every M in 1..16, else 0.  Wider

@@ -259,3 +259,20 @@ def test_kv_compact_argument_errors(dc):
     assert kv(d=96) == 2
     assert kv(ck=FAKE + 8) == 3
     assert L.dflash_stack_kv_compact(FAKE, FAKE + 0x100000, 1, 0, 2, 128, 30, 40, None, 3, None) == 1
+
+
+def test_qmm_host_workspace_and_argument_errors(dc):
+    L = dc.lib
+    for (M, N, K, g, b) in [(8, 17408, 5120, 64, 4), (1, 4096, 1024, 32, 8), (16, 5120, 17408, 128, 4)]:
+        base = L.dflash_qmm_workspace_bytes(M, N, K, g, b)
+        r256 = lambda v: (v + 255) // 256 * 256
+        assert L.dflash_qmm_host_workspace_bytes(M, N, K, g, b) == base + r256(2 * M * K) + r256(2 * M * N)
+    assert L.dflash_qmm_host_workspace_bytes(17, 4096, 1024, 64, 4) == 0
+    assert L.dflash_qmm_host_workspace_bytes(8, 4096, 1000, 64, 4) == 0
+    need = L.dflash_qmm_host_workspace_bytes(8, 4096, 1024, 64, 4)
+    h = lambda x=FAKE, w=FAKE, y=FAKE, ws=FAKE, nbytes=need, M=8, bits=4: L.dflash_qmm_host(
+        x, w, FAKE, FAKE, y, M, 4096, 1024, 64, bits, ws, nbytes, None)
+    assert h(x=None) == 1 and h(y=None) == 1
+    assert h(w=FAKE + 4) == 3
+    assert h(nbytes=need - 1) == 7 and h(ws=None) == 7 and h(ws=FAKE + 8) == 7
+    assert h(M=17) == 2 and h(bits=3) == 2
