@@ -40,12 +40,39 @@ def build(force: bool = False, ptxas_verbose: bool = False, extra=()) -> Path:
     return OUT
 
 
+HOST = PKG / "host"
+HOST_OUT = PKG / "libdflashkit.so"
+
+
+def cuda_home() -> Path:
+    import shutil
+    nvcc = shutil.which("nvcc")
+    return Path(nvcc).resolve().parent.parent if nvcc else Path("/usr/local/cuda")
+
+
+def build_host(force: bool = False) -> Path:
+    """libdflashkit.so: the C++ host interface (host/dflashkit.{hpp,cpp}) over
+    libdflashcuda.so, linked against the shared CUDA runtime for its allocations."""
+    srcs = sorted(HOST.glob("*.cpp")) + sorted(HOST.glob("*.hpp")) + sorted((ROOT / "include").glob("*.h"))
+    if not force and HOST_OUT.exists() and OUT.exists() and all(
+            HOST_OUT.stat().st_mtime >= s.stat().st_mtime for s in srcs + [OUT]):
+        return HOST_OUT
+    cuda = cuda_home()
+    cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-Werror",
+           f"-I{ROOT / 'include'}", f"-I{cuda / 'include'}", str(HOST / "dflashkit.cpp"), "-o", str(HOST_OUT),
+           f"-L{PKG}", "-ldflashcuda", f"-L{cuda / 'lib64'}", "-lcudart",
+           "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{cuda / 'lib64'}"]
+    subprocess.run(cmd, check=True)
+    return HOST_OUT
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--ptxas-verbose", action="store_true")
     a = ap.parse_args(argv)
     print(build(a.force, a.ptxas_verbose))
+    print(build_host(a.force))
     return 0
 
 

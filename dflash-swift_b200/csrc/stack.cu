@@ -741,6 +741,15 @@ inline unsigned grid_for(size_t n, int block) {
 
 inline cudaStream_t as_stream(dflash_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// y[r, n] = bf16(y[r, n] + bias[n]): the bf16 add of a broadcast bias row that
+// QuantizedLinear applies after its matmul.  One thread per element.
+__global__ void bias_add_kernel(uint16_t* __restrict__ y, const uint16_t* __restrict__ bias, long long total, int N) {
+    chain_in();
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    y[i] = to_bf(bf(y[i]) + bf(bias[i % N]));
+}
+
 // After a tree round, cache rows pos0 + rows[i] move to pos0 + i.  grid (hkv, layers, 2):
 // cache_k for z = 0, cache_v for z = 1.  A block stages all `keep` source rows in shared
 // memory before writing any, so moves whose sources and destinations overlap are safe.
@@ -1060,5 +1069,15 @@ extern "C" int dflash_stack_kv_compact(dflash_bf16* cache_k, dflash_bf16* cache_
     DFLASH_CUDA_TRY(launch_chained(stack::kv_compact_kernel, dim3(hkv, layers, 2), dim3(256), 0, as_stream(stream), 1,
                                    reinterpret_cast<uint16_t*>(cache_k), reinterpret_cast<uint16_t*>(cache_v),
                                    layer_stride, d, pos0, max_len, rl, keep));
+    return DFLASH_OK;
+}
+
+extern "C" int dflash_bias_add(dflash_bf16* y, const dflash_bf16* bias, int rows, int N, dflash_stream_t stream) {
+    if (!y || !bias || rows < 1 || N < 1) return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_bias_add: bad arguments");
+    const long long total = (long long)rows * N;
+    const long long blocks = (total + 255) / 256;
+    if (blocks > 0x7fffffffLL) return fail(DFLASH_ERR_UNSUPPORTED, "dflash_bias_add: %lld elements", total);
+    DFLASH_CUDA_TRY(launch_chained(stack::bias_add_kernel, dim3((unsigned)blocks), dim3(256), 0, as_stream(stream), 1,
+                                   reinterpret_cast<uint16_t*>(y), reinterpret_cast<const uint16_t*>(bias), total, N));
     return DFLASH_OK;
 }

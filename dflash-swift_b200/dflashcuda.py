@@ -44,7 +44,7 @@ DEVERR_TEST_WAIT = 0x80000000
 EXPORTED = (
     "dflash_version", "dflash_last_error", "dflash_status_string", "dflash_device_error",
     "dflash_test_bounded_wait", "dflash_qmm_workspace_bytes", "dflash_qmm", "dflash_qmm_noalloc",
-    "dflash_qmm_supported", "dflash_qmm_host_workspace_bytes", "dflash_qmm_host",
+    "dflash_qmm_supported", "dflash_qmm_host_workspace_bytes", "dflash_qmm_host", "dflash_bias_add",
     "dflash_gdn_step", "dflash_gdn_replay", "dflash_gdn_conv_rollback",
     # include/dflash_stack.h: glue of the tensor-parallel verify stack
     "dflash_stack_add_rmsnorm", "dflash_stack_silu_mul", "dflash_stack_conv_silu", "dflash_stack_gdn_gates",
@@ -88,6 +88,7 @@ def _load() -> ctypes.CDLL:
         "dflash_qmm_noalloc": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp], _i),
         "dflash_qmm_supported": ([_i, _i, _i, _i], _i),
         "dflash_qmm_host_workspace_bytes": ([_i, _i, _i, _i, _i], _sz),
+        "dflash_bias_add": ([_vp, _vp, _i, _i, _vp], _i),
         "dflash_qmm_host": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp], _i),
         "dflash_gdn_step": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, ctypes.c_float, _vp], _i),
         "dflash_gdn_replay": ([_vp, _vp, _vp, _vp, _vp, _vp, ctypes.POINTER(ctypes.c_int32), _i, _i, _i, _i,
@@ -344,10 +345,9 @@ class SmallMQuantizedLinear(QuantizedLinear):
             r1 = min(rows, r0 + step)
             qmm(flat[r0:r1], self.weight, self.scales, self.biases, self.group_size, self.bits, out=y[r0:r1],
                 stream=stream)
-        y = y.reshape(*lead, N)
-        if self.bias is not None:
-            y = y + self.bias
-        return y
+        if self.bias is not None and rows > 0:
+            check(lib.dflash_bias_add(_ptr(y), _ptr(self.bias), rows, N, _stream(stream)))
+        return y.reshape(*lead, N)
 
 
 def enable_small_m_quantized_matmul(model) -> int:

@@ -127,6 +127,11 @@ int dflash_qmm_host(const dflash_bf16* x_host, const uint32_t* w, const dflash_b
                     const dflash_bf16* biases, dflash_bf16* y_host, int M, int N, int K, int group_size,
                     int bits, void* workspace, size_t workspace_bytes, dflash_stream_t stream);
 
+/* y bf16 [rows, N] += bias bf16 [N], rounded to bf16 per element: the optional bias of a
+ * quantized linear layer, added after the matmul (SmallMQuantizedLinear.callAsFunction,
+ * SmallMQuantizedMatmul.swift:287-290). */
+int dflash_bias_add(dflash_bf16* y, const dflash_bf16* bias, int rows, int N, dflash_stream_t stream);
+
 /* Static half of the reference's eligibility test (SmallMQuantizedMatmul.isEligible,
  * SmallMQuantizedMatmul.swift:193-201) for a layer of this library: 1 when
  * dflash_qmm covers (N, K, group_size, bits) for every M in 1..16, else 0.  Wider

@@ -276,3 +276,11 @@ def test_qmm_host_workspace_and_argument_errors(dc):
     assert h(w=FAKE + 4) == 3
     assert h(nbytes=need - 1) == 7 and h(ws=None) == 7 and h(ws=FAKE + 8) == 7
     assert h(M=17) == 2 and h(bits=3) == 2
+
+
+def test_bias_add_argument_errors(dc):
+    L = dc.lib
+    assert L.dflash_bias_add(None, FAKE, 8, 4096, None) == 1
+    assert L.dflash_bias_add(FAKE, None, 8, 4096, None) == 1
+    assert L.dflash_bias_add(FAKE, FAKE, 0, 4096, None) == 1
+    assert L.dflash_bias_add(FAKE, FAKE, 8, 0, None) == 1
