@@ -741,6 +741,35 @@ inline unsigned grid_for(size_t n, int block) {
 
 inline cudaStream_t as_stream(dflash_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// The accepted path of a tree round (DFlashDraftTree.acceptedPath,
+// Sources/DFlashKit/DFlashDraftTree.swift:122-141): from the anchor, step into the first
+// child (row order) whose drafted token is the target's token at the current row, until
+// no child is.  One warp, lane r standing for row r: a step is one ballot over the rows
+// whose parent is the current row.  Rows only increase along a path, so at most rows - 1
+// steps.
+__global__ void accept_tree_kernel(const int32_t* __restrict__ target, const int32_t* __restrict__ parents,
+                                   const int32_t* __restrict__ tokens, int rows, int32_t* __restrict__ path,
+                                   int32_t* __restrict__ path_len, int32_t* __restrict__ next_token) {
+    chain_in();
+    const int lane = threadIdx.x;
+    const int par = lane < rows ? tree_parent(parents, lane) : -1;
+    const int tok = lane < rows ? tokens[lane] : 0;
+    int row = 0, n = 1;
+    if (lane == 0) path[0] = 0;
+    for (int step = 1; step < rows; ++step) {
+        const int want = target[row];
+        const unsigned hit = __ballot_sync(0xffffffffu, par == row && tok == want);
+        if (!hit) break;
+        row = __ffs(hit) - 1;
+        if (lane == 0) path[n] = row;
+        ++n;
+    }
+    if (lane == 0) {
+        *path_len = n;
+        *next_token = target[row];
+    }
+}
+
 // y[r, n] = bf16(y[r, n] + bias[n]): the bf16 add of a broadcast bias row that
 // QuantizedLinear applies after its matmul.  One thread per element.
 __global__ void bias_add_kernel(uint16_t* __restrict__ y, const uint16_t* __restrict__ bias, long long total, int N) {
@@ -1079,5 +1108,16 @@ extern "C" int dflash_bias_add(dflash_bf16* y, const dflash_bf16* bias, int rows
     if (blocks > 0x7fffffffLL) return fail(DFLASH_ERR_UNSUPPORTED, "dflash_bias_add: %lld elements", total);
     DFLASH_CUDA_TRY(launch_chained(stack::bias_add_kernel, dim3((unsigned)blocks), dim3(256), 0, as_stream(stream), 1,
                                    reinterpret_cast<uint16_t*>(y), reinterpret_cast<const uint16_t*>(bias), total, N));
+    return DFLASH_OK;
+}
+
+extern "C" int dflash_accept_tree(const int32_t* target_tokens, const int32_t* parents, const int32_t* tokens,
+                                  int rows, int32_t* path, int32_t* path_len, int32_t* next_token,
+                                  dflash_stream_t stream) {
+    if (!target_tokens || !parents || !tokens || !path || !path_len || !next_token || rows < 1 ||
+        rows > kMaxTreeRows)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_accept_tree: bad arguments (1 <= rows <= %d)", kMaxTreeRows);
+    DFLASH_CUDA_TRY(launch_chained(stack::accept_tree_kernel, dim3(1), dim3(32), 0, as_stream(stream), 1,
+                                   target_tokens, parents, tokens, rows, path, path_len, next_token));
     return DFLASH_OK;
 }

@@ -55,7 +55,7 @@ EXPORTED = (
     "dflash_accept_reduce",
     # speculative tree rounds
     "dflash_gdn_step_tree", "dflash_stack_gdn_conv_gates_tree", "dflash_stack_attn_prep_tree",
-    "dflash_stack_attn_decode_tree", "dflash_stack_kv_compact",
+    "dflash_stack_attn_decode_tree", "dflash_stack_kv_compact", "dflash_accept_tree",
 )
 
 
@@ -123,6 +123,7 @@ def _load() -> ctypes.CDLL:
         "dflash_stack_attn_decode_tree": ([_vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp, _vp], _i),
         "dflash_stack_kv_compact": ([_vp, _vp, _i, ctypes.c_longlong, _i, _i, _i, _i,
                                      ctypes.POINTER(ctypes.c_int32), _i, _vp], _i),
+        "dflash_accept_tree": ([_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp], _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -511,6 +512,14 @@ def stack_attn_decode(qkv, cache_k, cache_v, out, hq: int, hkv: int, pos0: int, 
     else:
         check(lib.dflash_stack_attn_decode_tree(*args, _ptr(parents), _stream(stream)))
     return out
+
+
+def accept_tree(target_tokens, parents, tokens, path, path_len, next_token, stream=None):
+    """The accepted path of a tree round on the device: target_tokens, parents, tokens
+    int32 [rows]; writes path int32 [rows] (first path_len entries), path_len [1],
+    next_token [1]."""
+    check(lib.dflash_accept_tree(_ptr(target_tokens), _ptr(parents), _ptr(tokens), tokens.shape[0], _ptr(path),
+                                 _ptr(path_len), _ptr(next_token), _stream(stream)))
 
 
 def stack_kv_compact(cache_k, cache_v, pos0: int, rows: Sequence[int], stream=None):

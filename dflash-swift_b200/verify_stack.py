@@ -390,6 +390,11 @@ class VerifyStack:
         # captured round replays with whatever tree set_tree last wrote (a chain until then)
         self.parents = torch.tensor([-1] + list(range(M - 1)), dtype=torch.int32, device=dev) if self.tree else None
         self.tree_plan = None
+        if self.tree:  # the drafted token of every row, and the device walk's accepted path
+            self.tree_tokens = torch.zeros(M, dtype=torch.int32, device=dev)
+            self.path = torch.zeros(M, dtype=torch.int32, device=dev)
+            self.path_len = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.next_token = torch.zeros(1, dtype=torch.int32, device=dev)
         h, dk, dv = p.gdn_heads, cfg.gdn_dk, cfg.gdn_dv
         # per layer: the in-projection (its q | k | v channels are the conv inputs that
         # commit() rebuilds the conv window from) and the conv output q | k | v, which with
@@ -518,6 +523,8 @@ class VerifyStack:
                 torch.distributed.all_reduce(self.keys, op=torch.distributed.ReduceOp.MAX, group=self.pg)
                 self.keys.bitwise_xor_(self._sign)
             dc.accept(self.keys, proposals, self.tokens, self.accepted)
+        if self.tree:  # the accepted path over the tree, on the device
+            dc.accept_tree(self.tokens, self.parents, self.tree_tokens, self.path, self.path_len, self.next_token)
         return self.tokens, self.accepted
 
     def verify(self, hidden, proposals):
@@ -543,14 +550,21 @@ class VerifyStack:
 
     def verify_tree(self, hidden, tokens):
         """One tree round: forward of the block under the current tree, LM head argmax
-        combined over the ranks, then the accepted-path walk on the host
-        (DFlashDraftTree.acceptedPath).  tokens: the drafted token of every row (host
-        ints, row 0 the anchor's).  Returns (accepted rows, the target's next token)."""
-        from tree import accepted_path
-        plan = self.tree_plan or self.set_tree([-1] + list(range(self.cfg.block - 1)))
-        proposals = torch.tensor([int(t) for t in tokens[1:]], dtype=torch.int32, device=self.device)
-        target, _ = self.verify(hidden, proposals)  # the chain accept count is not used
-        return accepted_path(tokens, plan, target.cpu().tolist())
+        combined over the ranks, and the accepted-path walk on the device
+        (dflash_accept_tree, DFlashDraftTree.acceptedPath).  tokens: the drafted token of
+        every row (host ints, row 0 the anchor's), written to the stack's device buffer
+        like the parent list, so a captured round replays with new tokens.  Returns
+        (accepted rows, the target's next token)."""
+        if not self.tree:
+            raise RuntimeError("this stack was built without tree=True")
+        if self.tree_plan is None:
+            self.set_tree([-1] + list(range(self.cfg.block - 1)))
+        if len(tokens) != self.cfg.block:
+            raise ValueError(f"{len(tokens)} drafted tokens for a block of {self.cfg.block}")
+        self.tree_tokens.copy_(torch.tensor([int(t) for t in tokens], dtype=torch.int32))
+        self.verify(hidden, self.tree_tokens[1:])  # the chain accept count is not used
+        n = int(self.path_len.item())
+        return self.path[:n].tolist(), int(self.next_token.item())
 
     def commit(self, rows):
         """After a round, make its accepted rows (anchor first: a chain's 0 .. keep-1, a

@@ -99,6 +99,16 @@ int dflash_stack_attn_decode_tree(const dflash_bf16* qkv, int ld, const dflash_b
                                   int pos0, int max_len, float scale, const int32_t* parents,
                                   dflash_stream_t stream);
 
+/* The accepted path of a tree round on the device (DFlashDraftTree.acceptedPath,
+ * Sources/DFlashKit/DFlashDraftTree.swift:122-141), so a captured round needs no host
+ * round trip before its result is read: from the anchor, step into the first child (row
+ * order) whose drafted token tokens[c] equals target_tokens[row] (the target's argmax at
+ * the current row, as dflash_accept / dflash_accept_reduce write it), until none does.
+ * Writes path[0 .. *path_len - 1] (anchor first; path needs `rows` entries), *path_len,
+ * and *next_token = target_tokens[last row].  All device int32; 1 <= rows <= 32. */
+int dflash_accept_tree(const int32_t* target_tokens, const int32_t* parents, const int32_t* tokens, int rows,
+                       int32_t* path, int32_t* path_len, int32_t* next_token, dflash_stream_t stream);
+
 /* After a tree round: moves cache rows pos0 + rows[i] to pos0 + i (i < keep) in cache_k
  * and cache_v, so the accepted path sits where a chain round would have put it (its
  * rotary positions pos0 + depth already match).  Caches bf16 [layers][hkv][max_len][d]

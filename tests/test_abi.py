@@ -284,3 +284,11 @@ def test_bias_add_argument_errors(dc):
     assert L.dflash_bias_add(FAKE, None, 8, 4096, None) == 1
     assert L.dflash_bias_add(FAKE, FAKE, 0, 4096, None) == 1
     assert L.dflash_bias_add(FAKE, FAKE, 8, 0, None) == 1
+
+
+def test_accept_tree_argument_errors(dc):
+    L = dc.lib
+    assert L.dflash_accept_tree(None, FAKE, FAKE, 8, FAKE, FAKE, FAKE, None) == 1
+    assert L.dflash_accept_tree(FAKE, FAKE, FAKE, 0, FAKE, FAKE, FAKE, None) == 1
+    assert L.dflash_accept_tree(FAKE, FAKE, FAKE, 33, FAKE, FAKE, FAKE, None) == 1
+    assert L.dflash_accept_tree(FAKE, FAKE, FAKE, 8, FAKE, None, FAKE, None) == 1

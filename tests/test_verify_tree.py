@@ -253,6 +253,33 @@ def test_kv_compact_moves_the_accepted_rows(dc, cuda, rows):
     assert torch.equal(one_k, ck[1]) and torch.equal(one_v, cv[1])
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("seed", range(6))
+def test_accept_tree_matches_the_host_walk(dc, cuda, seed):
+    """dflash_accept_tree against tree.accepted_path on random trees of 1..32 rows, with
+    targets that mostly follow a drafted child (deep walks) and drafted tokens that repeat
+    across siblings (the first child in row order must win)."""
+    from tree import accepted_path
+    rng = np.random.default_rng(seed)
+    for rows in (1, 2, 8, 16, 32):
+        parents = [-1] + [int(rng.integers(0, r)) for r in range(1, rows)]
+        plan = SpeculativeTreePlan(parents)
+        tokens = [int(t) for t in rng.integers(0, 4, rows)]
+        target = []
+        for r in range(rows):
+            kids = plan.children[r]
+            follow = kids and rng.random() < 0.8
+            target.append(tokens[int(rng.choice(kids))] if follow else int(rng.integers(100, 200)))
+        want_rows, want_next = accepted_path(tokens, plan, target)
+        t = lambda v: torch.tensor(v, dtype=torch.int32, device=cuda)
+        path = torch.full((rows,), -7, dtype=torch.int32, device=cuda)
+        n, nxt = t([0]), t([0])
+        dc.accept_tree(t(target), t(parents), t(tokens), path, n, nxt)
+        torch.cuda.synchronize()
+        got = path[:int(n.item())].tolist()
+        assert got == want_rows and int(nxt.item()) == want_next, (rows, parents, tokens, target)
+
+
 # ----------------------------------------------------------------------------- CUDA stack (GPU)
 
 @pytest.mark.gpu
@@ -270,6 +297,12 @@ def test_cuda_stack_tree_matches_reference_and_replays_a_new_tree(cuda):
         for gi in range(len(ref["qkv"])):
             assert closeness(stack.capture_qkv[gi].float().cpu().numpy(), ref["qkv"][gi].numpy()) <= 2e-2
             assert closeness(stack.capture_alpha[gi].cpu().numpy(), ref["alpha"][gi].numpy()) <= 2e-2
+    # the device walk of the round equals the host walk over the round's target tokens
+    from tree import accepted_path
+    drafted = [11, 23, 37, 41, 37, 53, 5, 9]
+    rows, nxt = stack.verify_tree(hidden, drafted)
+    target = stack.tokens.cpu().tolist()
+    assert (rows, nxt) == accepted_path(drafted, stack.tree_plan, target)
     # a graph captured under one tree replays another: the kernels read the parent list
     stack.set_tree(TREES["star"])
     g = stack.capture(hidden)
