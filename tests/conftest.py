@@ -21,6 +21,13 @@ for p in (str(ROOT), str(ROOT / "oracle"), str(PKG)):
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (runs on the B200 box)")
+    config.addinivalue_line(
+        "markers", "unconfirmed: code whose GPU run has not yet been seen to pass on a B200; such tests are "
+                   "collected after all others, so a run stopping at its first failure has run every confirmed test")
+
+
+def pytest_collection_modifyitems(session, config, items):
+    items.sort(key=lambda item: item.get_closest_marker("unconfirmed") is not None)  # stable: order kept otherwise
 
 
 def _ensure_built():

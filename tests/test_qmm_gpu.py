@@ -213,6 +213,7 @@ def test_workspace_shared_across_shapes(dc, O, cuda):
         assert O.closeness(y[:, r], O.qmm_f64(x, wq[r], s[r], b[r], 64, 4)) <= TIGHT
 
 
+@pytest.mark.unconfirmed  # its bias add now runs dflash_bias_add
 def test_small_m_quantized_linear_with_bias_and_wide_input(dc, O, cuda):
     """The layer flattens leading dims, runs 16-row passes, adds the bias
     (SmallMQuantizedMatmul.swift:254-292)."""
