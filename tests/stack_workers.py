@@ -24,7 +24,8 @@ def _init(backend: str, rank: int, world: int, port: int, device=None):
     return dist
 
 
-def gloo_reference_rank(rank: int, world: int, port: int, out_path: str, cfg_kw: dict, drop_reduce: bool):
+def gloo_reference_rank(rank: int, world: int, port: int, out_path: str, cfg_kw: dict, drop_reduce: bool,
+                        parents=None, hidden_seed: int = 0):
     import torch
     import verify_stack as vs
     import stack_ref
@@ -34,13 +35,13 @@ def gloo_reference_rank(rank: int, world: int, port: int, out_path: str, cfg_kw:
         plan = vs.shard_plan(cfg, rank, world)
         w = vs.build_rank_weights(cfg, plan, 0, "cpu")
         st = vs.build_rank_state(cfg, plan, 0, "cpu")
-        hidden = vs.make_block(cfg, 0, "cpu")
+        hidden = vs.make_block(cfg, hidden_seed, "cpu")
 
         def reduce(t):
             if not drop_reduce:
                 dist.all_reduce(t)
 
-        r = stack_ref.forward(cfg, plan, w, st, hidden, all_reduce=reduce)
+        r = stack_ref.forward(cfg, plan, w, st, hidden, all_reduce=reduce, parents=parents)
 
         def combine(keys):  # max over the ranks: unsigned keys as signed with the sign bit flipped
             import numpy as np

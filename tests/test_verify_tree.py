@@ -139,6 +139,27 @@ def test_reference_commit_of_a_tree_path_is_the_path_chain(tiny_tree_reference, 
                 assert np.array_equal(win, bits(hist)), (path, keep, gi)
 
 
+def test_reference_tree_at_tp2_matches_tp1(tmp_path, tiny_tree_reference):
+    """The tree round sharded over two gloo ranks (column / row shards, all-reduce after
+    the row-sharded projections) matches the one-rank tree round, and dropping the
+    all-reduce does not."""
+    import stack_workers
+    from dataclasses import asdict
+    from test_verify_stack import _run_ranks, free_port
+    r = tiny_tree_reference
+    ref = r["tree"]["out"].numpy()
+    errs = {}
+    for drop in (False, True):
+        out = tmp_path / f"tree_tp2_drop{int(drop)}.pt"
+        port = free_port()
+        codes = _run_ranks(stack_workers.gloo_reference_rank, 2,
+                           lambda k: (k, 2, port, str(out), asdict(vs.TINY), drop, r["parents"], 3))
+        assert codes == [0, 0], codes
+        errs[drop] = closeness(torch.load(out)["out"].numpy(), ref)
+    assert errs[False] <= 3e-2
+    assert errs[True] > max(0.05, 10 * errs[False])
+
+
 # ----------------------------------------------------------------------------- kernels (GPU)
 
 def _gather_rows(t, rows):
