@@ -154,7 +154,8 @@ def attention(q, gate, cache_k, cache_v, pos0: int, scale: float, visible=None):
 
 
 def forward(cfg, plan, weights: dict, state: dict, hidden: torch.Tensor,
-            all_reduce: Optional[Callable[[torch.Tensor], None]] = None, parents=None) -> dict:
+            all_reduce: Optional[Callable[[torch.Tensor], None]] = None, parents=None,
+            context: Optional[int] = None) -> dict:
     """One rank's verify forward over the M = hidden.shape[0] block rows.  Returns the final
     hidden states and, per layer, the capture and state the CUDA stack produces
     (gated-delta conv output, alpha, beta, state after the block; attention cache rows
@@ -162,9 +163,11 @@ def forward(cfg, plan, weights: dict, state: dict, hidden: torch.Tensor,
     row computes what a chain over its root-to-row path computes: convolution and
     recurrence along the path, rotary position context + depth, attention to the prefix
     and the path's rows; the state entry is then None (the state after a tree round is the
-    replay of the accepted path)."""
+    replay of the accepted path).  `context`: tokens already in the attention caches
+    (cfg.context when not given); the block's rows go to cache rows context + row."""
     all_reduce = all_reduce or (lambda t: None)
     M, H = hidden.shape[0], cfg.hidden
+    ctx = cfg.context if context is None else int(context)
     anc, paths = tree_paths(parents, M) if parents is not None else (None, None)
     eps = cfg.eps
     resid = torch.zeros(M, H)
@@ -207,15 +210,15 @@ def forward(cfg, plan, weights: dict, state: dict, hidden: torch.Tensor,
             gate = qkv[:, hq * d:2 * hq * d].reshape(M, hq, d)
             kn = qkv[:, 2 * hq * d:2 * hq * d + hkv * d].reshape(M, hkv, d)
             vn = qkv[:, 2 * hq * d + hkv * d:].reshape(M, hkv, d)
-            pos = cfg.context + (torch.arange(M) if parents is None else torch.tensor([len(a) - 1 for a in anc]))
+            pos = ctx + (torch.arange(M) if parents is None else torch.tensor([len(a) - 1 for a in anc]))
             q = rb(rope(head_rmsnorm(q, L["q_norm"], eps), cfg.rotary_dim, cfg.rope_theta, pos))
             kn = rb(rope(head_rmsnorm(kn, L["k_norm"], eps), cfg.rotary_dim, cfg.rope_theta, pos))
             ck, cv = cpu(S["cache_k"]).float().clone(), cpu(S["cache_v"]).float().clone()
-            ck[:, cfg.context:cfg.context + M] = kn.transpose(0, 1)
-            cv[:, cfg.context:cfg.context + M] = vn.transpose(0, 1)
+            ck[:, ctx:ctx + M] = kn.transpose(0, 1)
+            cv[:, ctx:ctx + M] = vn.transpose(0, 1)
             cap["cache_k"].append(ck)
             cap["cache_v"].append(cv)
-            part = qmm(attention(q, gate, ck, cv, cfg.context, 1.0 / math.sqrt(d), anc), L["o_proj"])
+            part = qmm(attention(q, gate, ck, cv, ctx, 1.0 / math.sqrt(d), anc), L["o_proj"])
         all_reduce(part)
         delta = rb(part)
         normed = add_rmsnorm(resid, delta, L["post_ln"], eps)
@@ -227,6 +230,33 @@ def forward(cfg, plan, weights: dict, state: dict, hidden: torch.Tensor,
         delta = rb(part)
     out = add_rmsnorm(resid, delta, cpu(weights["final_norm"]), eps)
     return {"out": out, "resid": resid, **cap}
+
+
+def commit(state: dict, result: dict, rows, context: int) -> None:
+    """Make a round's accepted rows (anchor first) the committed state, in place, as
+    rollbackGatedDeltaRound / Tree do (DFlashSpeculativeGenerator.swift:453-460): each
+    gated-delta snapshot becomes the recurrence over those rows from it
+    (``oracle.gdn_recurrence``), each conv window the last kc-1 rows of [window || their
+    conv inputs] (``oracle.conv_window``), and each attention cache holds their k and v at
+    rows context .. context + keep - 1.  `result` is this round's forward()."""
+    rows = [int(r) for r in rows]
+    keep = len(rows)
+    gi = ai = 0
+    for S in state["layers"]:
+        if "snapshot" in S:
+            q, k, v = result["qkv"][gi]
+            s, _ = O.gdn_recurrence(S["snapshot"].detach().cpu().float().numpy(), _bits(k.to(torch.bfloat16)),
+                                    _bits(v.to(torch.bfloat16)), result["alpha"][gi].numpy(),
+                                    result["beta"][gi].numpy(), keep, rows=rows)
+            S["snapshot"].copy_(torch.from_numpy(s.astype(np.float32)))
+            win = O.conv_window(_bits(S["window"]), _bits(result["conv_in"][gi].to(torch.bfloat16)), keep, rows)
+            S["window"].copy_(torch.from_numpy(win.view(np.int16)).view(torch.bfloat16))
+            gi += 1
+        else:
+            for key in ("cache_k", "cache_v"):
+                src = result[key][ai][:, [context + r for r in rows]]
+                S[key][:, context:context + keep] = src.to(S[key].dtype)
+            ai += 1
 
 
 def _order_key(v: np.ndarray) -> np.ndarray:
