@@ -329,6 +329,10 @@ class VerifyStack:
         self.dc = dc
         self.cfg = cfg
         self.tree = tree
+        # tokens already in the attention caches: the block's rows go to cache rows
+        # context .. context + block - 1.  A captured graph keeps the value it was
+        # captured with; advance() moves it for eager rounds (a decode loop).
+        self.context = cfg.context
         self.plan = shard_plan(cfg, rank, world)
         self.world = world
         self.pg = group
@@ -475,9 +479,9 @@ class VerifyStack:
         cfg, p, dc = self.cfg, self.plan, self.dc
         self._qmm(self.normed, L["qkv"], self.qkv)
         dc.stack_attn_prep(self.qkv, L["q_norm"], L["k_norm"], S["cache_k"], S["cache_v"], p.attn_heads, p.kv_heads,
-                           cfg.rotary_dim, cfg.context, cfg.eps, cfg.rope_theta, parents=self.parents)
+                           cfg.rotary_dim, self.context, cfg.eps, cfg.rope_theta, parents=self.parents)
         dc.stack_attn_decode(self.qkv, S["cache_k"], S["cache_v"], self.attn_out, p.attn_heads, p.kv_heads,
-                             cfg.context, 1.0 / math.sqrt(cfg.head_dim), parents=self.parents)
+                             self.context, 1.0 / math.sqrt(cfg.head_dim), parents=self.parents)
         return self._qmm_reduced(self.attn_out, L["o_proj"])
 
     def _mlp(self, L):
@@ -574,7 +578,8 @@ class VerifyStack:
         rebuilt from their conv inputs (dflash_gdn_conv_rollback); after a tree round the
         rows' attention cache entries move to context .. context + keep - 1
         (dflash_stack_kv_compact).  The snapshots and windows are updated in place, so a
-        captured round keeps its pointers; advancing the context is the caller's."""
+        captured round keeps its pointers; advancing the context by len(rows) is the
+        caller's (advance)."""
         cfg, p, dc = self.cfg, self.plan, self.dc
         rows = [int(r) for r in rows]
         keep = len(rows)
@@ -598,7 +603,13 @@ class VerifyStack:
                 S["window"].copy_(window)
                 gi += 1
             elif rows != list(range(keep)):
-                dc.stack_kv_compact(S["cache_k"], S["cache_v"], cfg.context, rows)
+                dc.stack_kv_compact(S["cache_k"], S["cache_v"], self.context, rows)
+
+    def advance(self, n: int):
+        """After commit(rows): the caches now hold n = len(rows) more tokens."""
+        if n < 0 or any(S["cache_k"].shape[1] < self.context + n for S in self.state["layers"] if "cache_k" in S):
+            raise ValueError(f"advancing the context by {n} runs past the attention caches")
+        self.context += n
 
     def capture(self, hidden_buf, proposals=None):
         """Capture forward(hidden_buf) — or, with proposals, the whole verify round — as a

@@ -163,3 +163,87 @@ def test_committing_a_tree_path_as_chain_rows_leaves_greedy(model, greedy):
 
 def test_greedy_sequence_is_not_constant(greedy):
     assert len(set(greedy[0])) > 4
+
+
+# ----------------------------------------------------------------------------- CUDA stack (GPU)
+
+@pytest.mark.gpu
+@pytest.mark.unconfirmed
+def test_cuda_stack_speculative_rounds_emit_its_greedy_sequence(cuda):
+    """The same control on the CUDA stack: greedy is a one-row stack committing every
+    token; chain rounds and tree rounds run on eight-row stacks with the drafts built as
+    above, committing the accepted rows (commit + advance).  On the device a row's
+    arithmetic does not depend on the other rows of its block (each matmul row
+    accumulates in a fixed order, norms and attention are per row, the replay runs the
+    step's own per-position update), so the sequences agree; committing every verified
+    row instead leaves greedy."""
+    plan = vs.shard_plan(CFG, 0, 1)
+    w = vs.build_rank_weights(CFG, plan, 0, cuda)
+    gen = torch.Generator().manual_seed(5)
+    emb = torch.randn(CFG.vocab, CFG.hidden, generator=gen).to(torch.bfloat16).to(cuda)
+
+    def make(rows, tree=False):
+        cfg = replace(CFG, block=rows)  # caches stay sized for CFG (36 positions)
+        return vs.VerifyStack(cfg, 0, 1, device=cuda, weights=w, state=vs.build_rank_state(CFG, plan, 0, cuda),
+                              tree=tree)
+
+    g1 = make(1)
+    greedy, ghid, tok = [], [], FIRST
+    for _ in range(N_TOKENS + ROWS):
+        target, _ = g1.verify(emb[[tok]], torch.zeros(0, dtype=torch.int32, device=cuda))
+        g1.commit([0])
+        g1.advance(1)
+        tok = int(target[0].item())
+        greedy.append(tok)
+        ghid.append(g1.out[0].float().cpu())
+    ghid = torch.stack(ghid)
+    assert len(set(greedy)) > 4
+
+    def chain(commit_all=False):
+        s8 = make(ROWS)
+        out, hid, anchor, rnd = [], [], FIRST, 0
+        while len(out) < N_TOKENS:
+            p = len(out)
+            drafts = list(greedy[p:p + ROWS - 1])
+            bad = [3, None, 0, 5, 1][rnd % 5]
+            if bad is not None:
+                drafts[bad] = (drafts[bad] + 1) % CFG.vocab
+            target, acc = s8.verify(emb[[anchor] + drafts], torch.tensor(drafts, dtype=torch.int32, device=cuda))
+            acc, target = int(acc.item()), target.tolist()
+            s8.commit(list(range(ROWS if commit_all else acc + 1)))
+            s8.advance(acc + 1)
+            out += drafts[:acc] + [target[acc]]
+            hid += [s8.out[i].float().cpu() for i in range(acc + 1)]
+            anchor = target[acc]
+            rnd += 1
+        return out[:N_TOKENS], torch.stack(hid)[:N_TOKENS]
+
+    def tree():
+        st = make(ROWS, tree=True)
+        st.set_tree(BRANCHY)
+        out, hid, anchor, rnd = [], [], FIRST, 0
+        while len(out) < N_TOKENS:
+            p = len(out)
+            g = greedy[p:p + 3]
+            k = [3, 1, 2, 0][rnd % 4]
+            tokens = [anchor] + [(g[0] + 1 + i) % CFG.vocab for i in range(ROWS - 1)]
+            for depth, row in enumerate((2, 5, 7)):
+                if depth < k:
+                    tokens[row] = g[depth]
+            rows, bonus = st.verify_tree(emb[tokens], tokens)
+            st.commit(rows)
+            st.advance(len(rows))
+            out += [tokens[r] for r in rows[1:]] + [bonus]
+            hid += [st.out[r].float().cpu() for r in rows]
+            anchor = bonus
+            rnd += 1
+        return out[:N_TOKENS], torch.stack(hid)[:N_TOKENS]
+
+    out, hid = chain()
+    assert out == greedy[:N_TOKENS]
+    assert closeness(hid, ghid[:N_TOKENS]) <= 1e-2
+    out, hid = tree()
+    assert out == greedy[:N_TOKENS]
+    assert closeness(hid, ghid[:N_TOKENS]) <= 1e-2
+    out, hid = chain(commit_all=True)
+    assert out != greedy[:N_TOKENS] or closeness(hid, ghid[:N_TOKENS]) > 1e-2
