@@ -25,7 +25,8 @@ def _build_module():
 
 def _binary() -> Path:
     build = _build_module()
-    build.build()
+    if not build.OUT.exists():  # never rebuild the CUDA library under a process that has it loaded
+        build.build()
     kit = build.build_host()
     oracle = ROOT / "oracle" / "liboracle.so"
     deps = [SRC, kit, oracle, PKG / "host" / "dflashkit.hpp"]
