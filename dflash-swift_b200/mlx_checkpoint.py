@@ -209,6 +209,50 @@ def _fused(tensors, config, layer_prefix, name):
                  torch.cat([p.biases for p in parts]), g, bits)
 
 
+def stack_config_from_json(config: dict, context: int, block: int = 8):
+    """verify_stack.StackConfig of a checkpoint's config.json, in the keys of the target's
+    Qwen3.5 configuration (the reference's fixture spells them out:
+    Tests/DFlashKitTests/TinyHybridTarget.swift:20-44): hidden_size, num_hidden_layers,
+    intermediate_size, full_attention_interval, linear_num_value_heads /
+    linear_num_key_heads, linear_key_head_dim / linear_value_head_dim,
+    linear_conv_kernel_dim, num_attention_heads, num_key_value_heads, head_dim,
+    rope_parameters {rope_theta, partial_rotary_factor} (or the same keys at the top
+    level), rms_norm_eps, vocab_size, and the global "quantization" entry.  `context` and
+    `block` size the attention caches and the verify block.
+
+    The stack's gated-delta layers use one head count for q, k and v; a checkpoint with
+    fewer key heads than value heads (a key head shared by several value heads) is
+    rejected with CheckpointError, as is a rotary width the attention prep cannot take."""
+    import verify_stack as vs
+
+    def need(key):
+        if key not in config:
+            raise CheckpointError(f"config.json has no {key!r}")
+        return config[key]
+
+    rope = config.get("rope_parameters") or {}
+    theta = float(rope.get("rope_theta", config.get("rope_theta", 10000.0)))
+    factor = float(rope.get("partial_rotary_factor", config.get("partial_rotary_factor", 1.0)))
+    head_dim = int(need("head_dim"))
+    rot = int(round(head_dim * factor))
+    hv, hk = int(need("linear_num_value_heads")), int(need("linear_num_key_heads"))
+    if hv != hk:
+        raise CheckpointError(f"{hk} gated-delta key heads for {hv} value heads: the stack needs one head count")
+    if rot % 64 or rot > head_dim:
+        raise CheckpointError(f"rotary width {rot} of head dim {head_dim}: a multiple of 64 up to the head dim needed")
+    q = config.get("quantization") or config.get("quantization_config")
+    if not q:
+        raise CheckpointError("config.json has no quantization entry")
+    return vs.StackConfig(
+        layers=int(need("num_hidden_layers")), hidden=int(need("hidden_size")),
+        intermediate=int(need("intermediate_size")), attn_interval=int(need("full_attention_interval")),
+        gdn_heads=hv, gdn_dk=int(need("linear_key_head_dim")), gdn_dv=int(need("linear_value_head_dim")),
+        conv_kernel=int(need("linear_conv_kernel_dim")), attn_heads=int(need("num_attention_heads")),
+        kv_heads=int(need("num_key_value_heads")), head_dim=head_dim, rotary_dim=rot, rope_theta=theta,
+        eps=float(config.get("rms_norm_eps", 1e-6)), group=int(q["group_size"]), bits=int(q["bits"]),
+        context=int(context), block=int(block), vocab=int(need("vocab_size")))
+
+
 def stack_from_checkpoint(cfg, plan, config: dict, tensors: Dict[str, torch.Tensor], device) -> dict:
     """The rank's shard of a checkpoint in verify_stack's weight layout (the same
     structure build_rank_weights returns)."""
@@ -284,6 +328,9 @@ def save_stack_checkpoint(directory, cfg, weights: dict, shard_bytes: int = 1 <<
               "linear_key_head_dim": cfg.gdn_dk, "linear_value_head_dim": cfg.gdn_dv,
               "linear_conv_kernel_dim": cfg.conv_kernel, "num_attention_heads": cfg.attn_heads,
               "num_key_value_heads": cfg.kv_heads, "head_dim": cfg.head_dim, "rms_norm_eps": cfg.eps,
+              "vocab_size": cfg.vocab,
+              "rope_parameters": {"rope_type": "default", "rope_theta": cfg.rope_theta,
+                                  "partial_rotary_factor": cfg.rotary_dim / cfg.head_dim},
               "quantization": {"group_size": cfg.group, "bits": cfg.bits}}
     (directory / "config.json").write_text(json.dumps(config, indent=1))
     shard, size, n = {}, 0, 0

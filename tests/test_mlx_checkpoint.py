@@ -85,6 +85,34 @@ def test_stack_checkpoint_shards_like_synthetic_weights(tmp_path, world):
                       vs.build_rank_weights(cfg, plan, 0, "cpu"))
 
 
+def test_stack_config_from_config_json(tmp_path):
+    """The stack configuration comes back from a saved checkpoint's config.json, and the
+    Qwen3.5 keys map onto config 4's stack; what the stack cannot take is rejected."""
+    mc.save_stack_checkpoint(tmp_path, vs.TINY, vs.build_rank_weights(vs.TINY, vs.shard_plan(vs.TINY, 0, 1), 0,
+                                                                        "cpu"))
+    config, _ = mc.load_directory(tmp_path)
+    assert mc.stack_config_from_json(config, context=vs.TINY.context, block=vs.TINY.block) == vs.TINY
+    c4 = {"model_type": "qwen3_5", "hidden_size": 5120, "num_hidden_layers": 64, "intermediate_size": 17408,
+          "full_attention_interval": 4, "linear_num_value_heads": 32, "linear_num_key_heads": 32,
+          "linear_key_head_dim": 128, "linear_value_head_dim": 128, "linear_conv_kernel_dim": 4,
+          "num_attention_heads": 24, "num_key_value_heads": 4, "head_dim": 256, "rms_norm_eps": 1e-6,
+          "vocab_size": 248320, "rope_parameters": {"rope_type": "default", "rope_theta": 1.0e7,
+                                                    "partial_rotary_factor": 0.25},
+          "quantization": {"group_size": 64, "bits": 4}}
+    assert mc.stack_config_from_json(c4, context=1024) == vs.CONFIG4
+    # the reference's tiny fixture (TinyHybridTarget.swift:20-44): 2 key heads for 4 value
+    # heads, and a 4-wide rotary span
+    tiny = {**c4, "hidden_size": 64, "num_hidden_layers": 4, "intermediate_size": 128, "num_attention_heads": 4,
+            "num_key_value_heads": 2, "head_dim": 16, "linear_num_value_heads": 4, "linear_num_key_heads": 2,
+            "linear_key_head_dim": 32, "linear_value_head_dim": 32, "vocab_size": 64, "full_attention_interval": 2}
+    with pytest.raises(mc.CheckpointError, match="key heads"):
+        mc.stack_config_from_json(tiny, context=8)
+    with pytest.raises(mc.CheckpointError, match="rotary"):
+        mc.stack_config_from_json({**tiny, "linear_num_key_heads": 4}, context=8)
+    with pytest.raises(mc.CheckpointError, match="hidden_size"):
+        mc.stack_config_from_json({k: v for k, v in c4.items() if k != "hidden_size"}, context=8)
+
+
 def test_fused_projection_given_as_parts(tmp_path):
     """A checkpoint that stores gate_proj and up_proj separately loads to the same
     [gate | up] shards as one storing the fused gate_up_proj."""
