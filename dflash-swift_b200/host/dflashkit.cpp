@@ -381,6 +381,22 @@ bool SpeculativeTreePlan::isRootPath(const std::vector<int>& rs) const {
     return true;
 }
 
+AcceptOutcome acceptedPrefix(const std::vector<float>& targetLogits, int vocabulary,
+                             const std::vector<int32_t>& proposals) {
+    const size_t rows = proposals.size() + 1;
+    if (vocabulary < 1 || targetLogits.size() != rows * (size_t)vocabulary)
+        throw std::invalid_argument("acceptedPrefix: logits must be [proposals + 1, vocabulary]");
+    AcceptOutcome out;
+    out.proposals = proposals;
+    for (size_t r = 0; r < rows; ++r) {
+        const float* row = targetLogits.data() + r * vocabulary;
+        out.targetTokens.push_back((int32_t)(std::max_element(row, row + vocabulary) - row));  // first maximum
+    }
+    while (out.accepted < (int)proposals.size() && proposals[out.accepted] == out.targetTokens[out.accepted])
+        ++out.accepted;
+    return out;
+}
+
 std::pair<std::vector<int>, int> acceptedPath(const std::vector<int>& tokens, const SpeculativeTreePlan& plan,
                                               const std::vector<int>& targetTokens) {
     if ((int)tokens.size() != plan.rows() || (int)targetTokens.size() != plan.rows())

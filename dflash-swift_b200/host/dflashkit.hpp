@@ -12,6 +12,7 @@
 //   * rollbackGatedDeltaRound / rollbackGatedDeltaTree (called at
 //     DFlashSpeculativeGenerator.swift:455-460): rebuild each gated-delta layer's
 //     MambaCache (conv window, recurrent state) from the round's capture;
+//   * acceptedPrefix, the greedy accept of a chain round (DFlashSpeculativeGenerator.swift:555-571);
 //   * SpeculativeTreePlan and the accepted-path walk (SpeculativeTreeTests.swift:25-78,
 //     DFlashDraftTree.swift:122-141).
 // Arrays are device memory (DeviceArray); outputs that the reference's MLX runtime would
@@ -198,6 +199,20 @@ public:
     int pathLength = 0;
     std::vector<RowSource> rowSources;
 };
+
+// The greedy accept of a chain round on host logits (DFlashSpeculativeGenerator
+// .acceptedPrefix, DFlashSpeculativeGenerator.swift:555-571): the target's token per row
+// is the argmax of its logits (the first index among equal maxima), and `accepted` is the
+// length of the leading run of proposals equal to them; targetTokens[accepted] is the
+// bonus token committed after them.  targetLogits: float [proposals + 1, vocabulary]
+// row-major.  On the device the same test is dflash_accept over the LM head's argmax keys.
+struct AcceptOutcome {
+    std::vector<int32_t> targetTokens;
+    std::vector<int32_t> proposals;
+    int accepted = 0;
+};
+AcceptOutcome acceptedPrefix(const std::vector<float>& targetLogits, int vocabulary,
+                             const std::vector<int32_t>& proposals);
 
 // From the anchor, step into the first child (row order) whose drafted token the target
 // named, until none does: (accepted rows, anchor first; the target's next token).

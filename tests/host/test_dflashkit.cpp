@@ -1,7 +1,8 @@
 // Tests of the C++ host interface (dflash-swift_b200/host/dflashkit.hpp), laid out like
 // the reference's XCTest cases they mirror:
 //   cpu: SpeculativeTreeTests.swift:25-78 (plan shape), the accepted-path walk
-//        (DFlashDraftTree.swift:122-141), SmallMQuantizedMatmul eligibility and tiles
+//        (DFlashDraftTree.swift:122-141), AcceptLengthTests.swift:17-63 (the greedy
+//        accept on one-peak logits), SmallMQuantizedMatmul eligibility and tiles
 //        (SmallMQuantizedMatmul.swift:193-207), enableSmallMQuantizedMatmul's swap
 //        semantics (:304-317) and the argument errors every entry reports before any
 //        CUDA call;
@@ -156,6 +157,36 @@ static void testAcceptedPathWalksTheTargetsChoices() {
     CHECK(plan.isRootPath(rows4));
 }
 
+// AcceptLengthTests.swift:17-63: hand-built one-peak logits
+static AcceptOutcome accept(const std::vector<int32_t>& target, const std::vector<int32_t>& proposals) {
+    const int vocabulary = 10;
+    std::vector<float> logits(target.size() * vocabulary, 0.f);
+    for (size_t r = 0; r < target.size(); ++r) logits[r * vocabulary + target[r]] = 1.f;
+    return acceptedPrefix(logits, vocabulary, proposals);
+}
+
+static void testAcceptLength() {
+    auto full = accept({3, 4, 5, 6}, {3, 4, 5});
+    CHECK(full.accepted == 3 && full.targetTokens[full.accepted] == 6);
+    auto zero = accept({9, 4, 5, 6}, {3, 4, 5});
+    CHECK(zero.accepted == 0 && zero.targetTokens[zero.accepted] == 9);
+    auto partial = accept({3, 4, 8, 6, 1}, {3, 4, 5, 6});
+    CHECK(partial.accepted == 2 && partial.targetTokens[partial.accepted] == 8);
+    CHECK((partial.proposals == std::vector<int32_t>{3, 4, 5, 6}));
+    std::vector<float> ties(2 * 5, 0.f);  // equal maxima resolve to the first index
+    ties[1] = ties[3] = 2.f;
+    ties[5 + 0] = ties[5 + 4] = 2.f;
+    auto t = acceptedPrefix(ties, 5, {1});
+    CHECK((t.targetTokens == std::vector<int32_t>{1, 0}) && t.accepted == 1);
+    bool threw = false;
+    try {
+        acceptedPrefix(std::vector<float>(7), 5, {1});
+    } catch (const std::invalid_argument&) {
+        threw = true;
+    }
+    CHECK(threw);
+}
+
 static void testEligibilityAndTiles() {
     CHECK(SmallMQuantizedMatmul::isEligible(layer(4096, 1024, 64, 4)));
     CHECK(SmallMQuantizedMatmul::isEligible(layer(5120, 17408, 64, 8)));
@@ -235,6 +266,7 @@ static int runCpu() {
     testChainPlanIsTheDegenerateTree();
     testMalformedParentsAreRejected();
     testAcceptedPathWalksTheTargetsChoices();
+    testAcceptLength();
     testEligibilityAndTiles();
     testArgumentErrorsComeBeforeAnyCudaCall();
     testEnableSwapsEligibleLayersOnceAndSharesArrays();
