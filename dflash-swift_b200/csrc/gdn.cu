@@ -95,6 +95,7 @@ struct ReplayParams {
     int keep, width, heads, dk, dv;
     RowList rows;
     const int32_t* parents;   // tree step only: the block's parent list (device, width entries)
+    int k_heads;              // heads of q and k (0: = heads); value head h reads key head h / (heads / k_heads)
 };
 
 // grid: (dv / 32, heads, layers) — (dv / 32, heads, width) for a tree step, block z taking
@@ -153,12 +154,15 @@ __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constan
         else return p.rows.r[r];
     };
 
-    // Stage k (and q), alpha, beta of the replayed positions.
+    // Stage k (and q), alpha, beta of the replayed positions.  q and k have k_heads heads,
+    // each shared by heads / k_heads consecutive value heads.
+    const int kh = p.k_heads > 0 ? p.k_heads : p.heads;
+    const int hk = h / (p.heads / kh);
     const size_t pos_stride = (size_t)p.heads;  // [width, H] per layer for alpha/beta
     for (int idx = tid; idx < keep * (DK / 4); idx += kBlockThreads) {
         const int r = idx / (DK / 4), c4 = (idx % (DK / 4)) * 4;
         const int t = row_at(r);
-        const size_t base = (((size_t)layer * p.width + t) * p.heads + h) * DK + c4;
+        const size_t base = (((size_t)layer * p.width + t) * kh + hk) * DK + c4;
         *reinterpret_cast<uint2*>(&ks[r][c4]) = *reinterpret_cast<const uint2*>(p.k + base);
         if (want_out) *reinterpret_cast<uint2*>(&qs_sh[r][c4]) = *reinterpret_cast<const uint2*>(p.q + base);
     }
@@ -280,12 +284,25 @@ int fill_rows(RowList& rl, const int32_t* rows, int keep, int width) {
 }  // namespace gdn
 }  // namespace dflash
 
-extern "C" int dflash_gdn_step(const float* state_in, float* state_out, const dflash_bf16* q,
-                               const dflash_bf16* k, const dflash_bf16* v, const float* alpha,
-                               const float* beta, dflash_bf16* out, int T, int heads, int dk, int dv,
-                               float q_scale, dflash_stream_t stream) {
+namespace dflash {
+namespace gdn {
+
+// heads value heads share k_heads key heads (q and k): k_heads divides heads.
+int check_key_heads(int heads, int k_heads) {
+    if (k_heads < 1 || heads % k_heads != 0)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "k_heads=%d must divide heads=%d", k_heads, heads);
+    return DFLASH_OK;
+}
+
+}  // namespace gdn
+}  // namespace dflash
+
+static int gdn_step_impl(const float* state_in, float* state_out, const dflash_bf16* q, const dflash_bf16* k,
+                         const dflash_bf16* v, const float* alpha, const float* beta, dflash_bf16* out, int T,
+                         int heads, int k_heads, int dk, int dv, float q_scale, dflash_stream_t stream) {
     using namespace dflash;
     if (int st = gdn::check_dims(heads, dk, dv)) return st;
+    if (int st = gdn::check_key_heads(heads, k_heads)) return st;
     if (T < 1 || T > gdn::kMaxPositions)
         return fail(DFLASH_ERR_UNSUPPORTED, "T=%d outside 1..%d", T, gdn::kMaxPositions);
     if (!state_in || !state_out || !k || !v || !alpha || !beta || (out && !q))
@@ -308,18 +325,35 @@ extern "C" int dflash_gdn_step(const float* state_in, float* state_out, const df
     p.keep = T;
     p.width = T;
     p.heads = heads;
+    p.k_heads = k_heads;
     p.dk = dk;
     p.dv = dv;
     if (int st = gdn::fill_rows(p.rows, nullptr, T, T)) return st;
     return gdn::launch(p, 1, reinterpret_cast<cudaStream_t>(stream));
 }
 
-extern "C" int dflash_gdn_step_tree(const float* state_in, const dflash_bf16* q, const dflash_bf16* k,
-                                    const dflash_bf16* v, const float* alpha, const float* beta,
-                                    const int32_t* parents, dflash_bf16* out, int T, int heads, int dk, int dv,
-                                    float q_scale, dflash_stream_t stream) {
+extern "C" int dflash_gdn_step(const float* state_in, float* state_out, const dflash_bf16* q,
+                               const dflash_bf16* k, const dflash_bf16* v, const float* alpha,
+                               const float* beta, dflash_bf16* out, int T, int heads, int dk, int dv,
+                               float q_scale, dflash_stream_t stream) {
+    return gdn_step_impl(state_in, state_out, q, k, v, alpha, beta, out, T, heads, heads, dk, dv, q_scale, stream);
+}
+
+extern "C" int dflash_gdn_step_grouped(const float* state_in, float* state_out, const dflash_bf16* q,
+                                       const dflash_bf16* k, const dflash_bf16* v, const float* alpha,
+                                       const float* beta, dflash_bf16* out, int T, int heads, int k_heads, int dk,
+                                       int dv, float q_scale, dflash_stream_t stream) {
+    return gdn_step_impl(state_in, state_out, q, k, v, alpha, beta, out, T, heads, k_heads, dk, dv, q_scale,
+                         stream);
+}
+
+static int gdn_step_tree_impl(const float* state_in, const dflash_bf16* q, const dflash_bf16* k,
+                              const dflash_bf16* v, const float* alpha, const float* beta, const int32_t* parents,
+                              dflash_bf16* out, int T, int heads, int k_heads, int dk, int dv, float q_scale,
+                              dflash_stream_t stream) {
     using namespace dflash;
     if (int st = gdn::check_dims(heads, dk, dv)) return st;
+    if (int st = gdn::check_key_heads(heads, k_heads)) return st;
     if (T < 1 || T > kMaxTreeRows) return fail(DFLASH_ERR_UNSUPPORTED, "T=%d outside 1..%d", T, kMaxTreeRows);
     if (!state_in || !q || !k || !v || !alpha || !beta || !parents || !out)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_gdn_step_tree: null pointer");
@@ -337,18 +371,35 @@ extern "C" int dflash_gdn_step_tree(const float* state_in, const dflash_bf16* q,
     p.keep = T;
     p.width = T;
     p.heads = heads;
+    p.k_heads = k_heads;
     p.dk = dk;
     p.dv = dv;
     p.parents = parents;
     return gdn::launch(p, 1, reinterpret_cast<cudaStream_t>(stream));
 }
 
-extern "C" int dflash_gdn_replay(const float* snapshot, float* state_out, const dflash_bf16* k,
-                                 const dflash_bf16* v, const float* alpha, const float* beta,
-                                 const int32_t* rows, int keep, int width, int layers, int heads, int dk,
-                                 int dv, dflash_stream_t stream) {
+extern "C" int dflash_gdn_step_tree(const float* state_in, const dflash_bf16* q, const dflash_bf16* k,
+                                    const dflash_bf16* v, const float* alpha, const float* beta,
+                                    const int32_t* parents, dflash_bf16* out, int T, int heads, int dk, int dv,
+                                    float q_scale, dflash_stream_t stream) {
+    return gdn_step_tree_impl(state_in, q, k, v, alpha, beta, parents, out, T, heads, heads, dk, dv, q_scale,
+                              stream);
+}
+
+extern "C" int dflash_gdn_step_tree_grouped(const float* state_in, const dflash_bf16* q, const dflash_bf16* k,
+                                            const dflash_bf16* v, const float* alpha, const float* beta,
+                                            const int32_t* parents, dflash_bf16* out, int T, int heads,
+                                            int k_heads, int dk, int dv, float q_scale, dflash_stream_t stream) {
+    return gdn_step_tree_impl(state_in, q, k, v, alpha, beta, parents, out, T, heads, k_heads, dk, dv, q_scale,
+                              stream);
+}
+
+static int gdn_replay_impl(const float* snapshot, float* state_out, const dflash_bf16* k, const dflash_bf16* v,
+                           const float* alpha, const float* beta, const int32_t* rows, int keep, int width,
+                           int layers, int heads, int k_heads, int dk, int dv, dflash_stream_t stream) {
     using namespace dflash;
     if (int st = gdn::check_dims(heads, dk, dv)) return st;
+    if (int st = gdn::check_key_heads(heads, k_heads)) return st;
     if (layers < 1) return fail(DFLASH_ERR_INVALID_ARGUMENT, "layers=%d must be positive", layers);
     if (width < 1 || width > gdn::kMaxPositions || keep < 1 || keep > width)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "need 1 <= keep (%d) <= width (%d) <= %d", keep, width,
@@ -369,10 +420,27 @@ extern "C" int dflash_gdn_replay(const float* snapshot, float* state_out, const 
     p.keep = keep;
     p.width = width;
     p.heads = heads;
+    p.k_heads = k_heads;
     p.dk = dk;
     p.dv = dv;
     if (int st = gdn::fill_rows(p.rows, rows, keep, width)) return st;
     return gdn::launch(p, layers, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dflash_gdn_replay(const float* snapshot, float* state_out, const dflash_bf16* k,
+                                 const dflash_bf16* v, const float* alpha, const float* beta,
+                                 const int32_t* rows, int keep, int width, int layers, int heads, int dk,
+                                 int dv, dflash_stream_t stream) {
+    return gdn_replay_impl(snapshot, state_out, k, v, alpha, beta, rows, keep, width, layers, heads, heads, dk, dv,
+                           stream);
+}
+
+extern "C" int dflash_gdn_replay_grouped(const float* snapshot, float* state_out, const dflash_bf16* k,
+                                         const dflash_bf16* v, const float* alpha, const float* beta,
+                                         const int32_t* rows, int keep, int width, int layers, int heads,
+                                         int k_heads, int dk, int dv, dflash_stream_t stream) {
+    return gdn_replay_impl(snapshot, state_out, k, v, alpha, beta, rows, keep, width, layers, heads, k_heads, dk, dv,
+                           stream);
 }
 
 extern "C" int dflash_gdn_conv_rollback(const dflash_bf16* window, dflash_bf16* window_out,

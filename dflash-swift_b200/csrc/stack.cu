@@ -354,6 +354,77 @@ __global__ void gdn_conv_gates_kernel(const uint16_t* __restrict__ x, int ld, co
     }
 }
 
+// gdn_conv_gates_kernel for layers whose q and k have fewer heads than v: x rows hold
+// [q (k_heads dk) | k (k_heads dk) | v (heads dk)], each key head shared by heads / k_heads
+// value heads.  One warp per (token, slot), slots 0 .. k_heads-1 the q heads, then the k
+// heads, then the value heads; y receives [q: M x k_heads dk | k: M x k_heads dk |
+// v: M x heads dk]; the gates are per value head (ab holds b then a for each value head)
+// and written by the value warps.  Taps as in gdn_conv_gates_kernel (chain or tree).
+template <int KC, int DJ>
+__global__ void gdn_conv_gates_grouped_kernel(const uint16_t* __restrict__ x, int ld,
+                                              const uint16_t* __restrict__ window, const uint16_t* __restrict__ w,
+                                              uint16_t* __restrict__ y, const uint16_t* __restrict__ ab, int ld_ab,
+                                              const float* __restrict__ a_log, const float* __restrict__ dt_bias,
+                                              float* __restrict__ alpha, float* __restrict__ beta, int M, int heads,
+                                              int k_heads, const int32_t* __restrict__ parents) {
+    chain_in();
+    constexpr int dk = 32 * DJ;
+    const int slots = 2 * k_heads + heads;
+    const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (wid >= M * slots) return;
+    const int t = wid / slots, slot = wid % slots;
+    const int part = slot < k_heads ? 0 : slot < 2 * k_heads ? 1 : 2;
+    const int h = slot - part * k_heads;  // head within its part
+    const int C = slots * dk;
+    const int c0 = part * k_heads * dk + h * dk;  // first channel of this warp's head
+    int back[KC];
+    back[0] = t;
+#pragma unroll
+    for (int s = 1; s < KC; ++s)
+        back[s] = back[s - 1] < 0 ? -1 : parents ? tree_parent(parents, back[s - 1]) : back[s - 1] - 1;
+    int depth = 0;
+#pragma unroll
+    for (int s = 1; s < KC; ++s) depth += back[s] >= 0;
+    float xin[DJ][KC], wk[DJ][KC];
+#pragma unroll
+    for (int j = 0; j < DJ; ++j) {
+        const int c = c0 + lane + 32 * j;
+#pragma unroll
+        for (int i = 0; i < KC; ++i) {
+            wk[j][i] = bf(w[(size_t)c * KC + i]);
+            const int src = back[KC - 1 - i];
+            xin[j][i] = src < 0 ? bf(window[(size_t)(depth + i) * C + c]) : bf(x[(size_t)src * ld + c]);
+        }
+    }
+    float v[DJ];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < DJ; ++j) {
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < KC; ++i) acc = fmaf(wk[j][i], xin[j][i], acc);
+        v[j] = bf_round(silu(acc));
+        ss = fmaf(v[j], v[j], ss);
+    }
+    const int part_heads = part < 2 ? k_heads : heads;
+    uint16_t* out = y + (size_t)part * M * k_heads * dk + ((size_t)t * part_heads + h) * dk + lane;
+    if (part < 2) {
+        const float rs = rsqrtf(warp_sum(ss) + 1e-6f);
+#pragma unroll
+        for (int j = 0; j < DJ; ++j) out[32 * j] = to_bf(v[j] * rs);
+    } else {
+#pragma unroll
+        for (int j = 0; j < DJ; ++j) out[32 * j] = to_bf(v[j]);
+        if (lane == 0) {
+            const float b = bf(ab[(size_t)t * ld_ab + h]);
+            const float a = bf(ab[(size_t)t * ld_ab + heads + h]);
+            const float sp = a + dt_bias[h] > 20.f ? a + dt_bias[h] : log1pf(__expf(a + dt_bias[h]));
+            alpha[(size_t)t * heads + h] = __expf(-__expf(a_log[h]) * sp);
+            beta[(size_t)t * heads + h] = 1.f / (1.f + __expf(-b));
+        }
+    }
+}
+
 // out[t, h*dv + i] = rmsnorm(o[t, h, :]) * w[i] * silu(z[t, h*dv + i]); one warp per (t, h).
 __global__ void gated_norm_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ z, int ld_z,
                                   const uint16_t* __restrict__ w, uint16_t* __restrict__ out, int M, int heads, int dv,
@@ -1119,5 +1190,35 @@ extern "C" int dflash_accept_tree(const int32_t* target_tokens, const int32_t* p
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_accept_tree: bad arguments (1 <= rows <= %d)", kMaxTreeRows);
     DFLASH_CUDA_TRY(launch_chained(stack::accept_tree_kernel, dim3(1), dim3(32), 0, as_stream(stream), 1,
                                    target_tokens, parents, tokens, rows, path, path_len, next_token));
+    return DFLASH_OK;
+}
+
+extern "C" int dflash_stack_gdn_conv_gates_grouped(const dflash_bf16* x, int ld, const dflash_bf16* window,
+                                                   const dflash_bf16* weight, dflash_bf16* y, const dflash_bf16* ab,
+                                                   int ld_ab, const float* a_log, const float* dt_bias, float* alpha,
+                                                   float* beta, int M, int heads, int k_heads, int dk, int kc,
+                                                   const int32_t* parents, dflash_stream_t stream) {
+    if (!x || !window || !weight || !y || !ab || !a_log || !dt_bias || !alpha || !beta || M < 1 || heads < 1 ||
+        k_heads < 1 || heads % k_heads || ld < (2 * k_heads + heads) * dk || ld_ab < 2 * heads)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_gdn_conv_gates_grouped: bad arguments");
+    if (parents && M > kMaxTreeRows)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_gdn_conv_gates_grouped: a tree has at most %d rows",
+                    kMaxTreeRows);
+    if ((dk != 32 && dk != 64 && dk != 128) || kc < 2 || kc > 4)
+        return fail(DFLASH_ERR_UNSUPPORTED,
+                    "dflash_stack_gdn_conv_gates_grouped: dk %d (32, 64, 128) / conv width %d (2..4)", dk, kc);
+    const long long warps = (long long)M * (2 * k_heads + heads);
+    const dim3 grid((unsigned)((warps + 7) / 8)), block(256);
+    cudaStream_t s = as_stream(stream);
+    cudaError_t e = cudaSuccess;
+#define DFLASH_CGG_CASE(KC, DJ)                                                                                  \
+    if (kc == KC && dk == 32 * DJ)                                                                              \
+        e = launch_chained(stack::gdn_conv_gates_grouped_kernel<KC, DJ>, grid, block, 0, s, 1, x, ld, window, weight, \
+                           y, ab, ld_ab, a_log, dt_bias, alpha, beta, M, heads, k_heads, parents);
+    DFLASH_CGG_CASE(2, 1) DFLASH_CGG_CASE(2, 2) DFLASH_CGG_CASE(2, 4)
+    DFLASH_CGG_CASE(3, 1) DFLASH_CGG_CASE(3, 2) DFLASH_CGG_CASE(3, 4)
+    DFLASH_CGG_CASE(4, 1) DFLASH_CGG_CASE(4, 2) DFLASH_CGG_CASE(4, 4)
+#undef DFLASH_CGG_CASE
+    DFLASH_CUDA_TRY(e);
     return DFLASH_OK;
 }

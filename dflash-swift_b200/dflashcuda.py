@@ -56,6 +56,9 @@ EXPORTED = (
     # speculative tree rounds
     "dflash_gdn_step_tree", "dflash_stack_gdn_conv_gates_tree", "dflash_stack_attn_prep_tree",
     "dflash_stack_attn_decode_tree", "dflash_stack_kv_compact", "dflash_accept_tree",
+    # gated-delta layers with shared key heads
+    "dflash_gdn_step_grouped", "dflash_gdn_step_tree_grouped", "dflash_gdn_replay_grouped",
+    "dflash_stack_gdn_conv_gates_grouped",
 )
 
 
@@ -124,6 +127,12 @@ def _load() -> ctypes.CDLL:
         "dflash_stack_kv_compact": ([_vp, _vp, _i, ctypes.c_longlong, _i, _i, _i, _i,
                                      ctypes.POINTER(ctypes.c_int32), _i, _vp], _i),
         "dflash_accept_tree": ([_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp], _i),
+        "dflash_gdn_step_grouped": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp], _i),
+        "dflash_gdn_step_tree_grouped": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp], _i),
+        "dflash_gdn_replay_grouped": ([_vp, _vp, _vp, _vp, _vp, _vp, ctypes.POINTER(ctypes.c_int32), _i, _i, _i, _i,
+                                       _i, _i, _i, _vp], _i),
+        "dflash_stack_gdn_conv_gates_grouped": ([_vp, _i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i,
+                                                 _i, _vp, _vp], _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -398,21 +407,29 @@ def _is_tensor(obj) -> bool:
 # ----------------------------------------------------------------------------- gated delta
 
 def gdn_step(state_in, state_out, q, k, v, alpha, beta, out=None, q_scale: float = 1.0, stream=None):
-    """One layer's recurrence over T positions (the verify forward; its inputs are the capture)."""
-    T, H, dk = k.shape
-    dv = v.shape[-1]
-    check(lib.dflash_gdn_step(_ptr(state_in), _ptr(state_out), _ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(beta),
-                              _ptr(out), T, H, dk, dv, float(q_scale), _stream(stream)))
+    """One layer's recurrence over T positions (the verify forward; its inputs are the capture).
+    q, k [T, Hk, dk]; v [T, H, dv]: Hk < H shares each key head between H / Hk value heads."""
+    T, Hk, dk = k.shape
+    H, dv = v.shape[-2], v.shape[-1]
+    args = (_ptr(state_in), _ptr(state_out), _ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(beta), _ptr(out), T, H)
+    if Hk == H:
+        check(lib.dflash_gdn_step(*args, dk, dv, float(q_scale), _stream(stream)))
+    else:
+        check(lib.dflash_gdn_step_grouped(*args, Hk, dk, dv, float(q_scale), _stream(stream)))
     return state_out
 
 
 def gdn_step_tree(state_in, q, k, v, alpha, beta, parents, out, q_scale: float = 1.0, stream=None):
     """One layer's recurrence over the T rows of a tree round: row t gets the output of a
-    chain over its root-to-t path from state_in.  parents: device int32 [T]."""
-    T, H, dk = k.shape
-    dv = v.shape[-1]
-    check(lib.dflash_gdn_step_tree(_ptr(state_in), _ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(beta),
-                                   _ptr(parents), _ptr(out), T, H, dk, dv, float(q_scale), _stream(stream)))
+    chain over its root-to-t path from state_in.  parents: device int32 [T].  Key heads as
+    for gdn_step."""
+    T, Hk, dk = k.shape
+    H, dv = v.shape[-2], v.shape[-1]
+    args = (_ptr(state_in), _ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(beta), _ptr(parents), _ptr(out), T, H)
+    if Hk == H:
+        check(lib.dflash_gdn_step_tree(*args, dk, dv, float(q_scale), _stream(stream)))
+    else:
+        check(lib.dflash_gdn_step_tree_grouped(*args, Hk, dk, dv, float(q_scale), _stream(stream)))
     return out
 
 
@@ -425,13 +442,18 @@ def _rows_arg(rows: Optional[Sequence[int]]):
 
 def gdn_replay(snapshot, state_out, k, v, alpha, beta, keep: int, rows: Optional[Sequence[int]] = None,
                stream=None):
-    """Rollback replay for all layers at once.  k: [L, width, H, dk]; state: [L, H, dv, dk]."""
-    L, width, H, dk = k.shape
-    dv = v.shape[-1]
+    """Rollback replay for all layers at once.  k: [L, width, Hk, dk]; v: [L, width, H, dv];
+    state: [L, H, dv, dk] (Hk < H: shared key heads, as for gdn_step)."""
+    L, width, Hk, dk = k.shape
+    H, dv = v.shape[-2], v.shape[-1]
     if rows is not None and len(rows) < keep:
         raise ValueError("rows shorter than keep")
-    check(lib.dflash_gdn_replay(_ptr(snapshot), _ptr(state_out), _ptr(k), _ptr(v), _ptr(alpha), _ptr(beta),
-                                _rows_arg(rows), int(keep), width, L, H, dk, dv, _stream(stream)))
+    args = (_ptr(snapshot), _ptr(state_out), _ptr(k), _ptr(v), _ptr(alpha), _ptr(beta), _rows_arg(rows), int(keep),
+            width, L, H)
+    if Hk == H:
+        check(lib.dflash_gdn_replay(*args, dk, dv, _stream(stream)))
+    else:
+        check(lib.dflash_gdn_replay_grouped(*args, Hk, dk, dv, _stream(stream)))
     return state_out
 
 
@@ -653,10 +675,18 @@ def accept(keys, proposals, tokens=None, accepted=None, stream=None):
 
 
 def stack_gdn_conv_gates(x, window, weight, out, ab, a_log, dt_bias, alpha, beta, heads: int, dk: int, stream=None,
-                         parents=None):
+                         parents=None, k_heads: Optional[int] = None):
     """Conv + SiLU + q/k normalisation + gates in one kernel; out [3, M, heads, dk].
-    parents (device int32 [M]): a tree round, each row convolved along its path."""
+    parents (device int32 [M]): a tree round, each row convolved along its path.  k_heads
+    < heads: q and k have k_heads heads (dflash_stack_gdn_conv_gates_grouped); out then
+    holds [q: M x k_heads dk | k: M x k_heads dk | v: M x heads dk] contiguously."""
     M = x.shape[0]
+    if k_heads is not None and k_heads != heads:
+        check(lib.dflash_stack_gdn_conv_gates_grouped(
+            _ptr(x), x.stride(0), _ptr(window), _ptr(weight), _ptr(out), _ptr(ab), ab.stride(0), _ptr(a_log),
+            _ptr(dt_bias), _ptr(alpha), _ptr(beta), M, heads, k_heads, dk, weight.shape[1], _ptr(parents),
+            _stream(stream)))
+        return out
     args = (_ptr(x), x.stride(0), _ptr(window), _ptr(weight), _ptr(out), _ptr(ab), ab.stride(0), _ptr(a_log),
             _ptr(dt_bias), _ptr(alpha), _ptr(beta), M, heads, dk, weight.shape[1])
     if parents is None:

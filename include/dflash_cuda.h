@@ -171,6 +171,27 @@ int dflash_gdn_step_tree(const float* state_in, const dflash_bf16* q, const dfla
                          const int32_t* parents, dflash_bf16* out, int T, int heads, int dk, int dv,
                          float q_scale, dflash_stream_t stream);
 
+/* Layers whose q and k have fewer heads than v (k_heads key heads, each shared by
+ * heads / k_heads consecutive value heads: value head h reads key head
+ * h / (heads / k_heads)), as the target's Qwen3.5 configuration allows
+ * (linear_num_key_heads < linear_num_value_heads,
+ * Tests/DFlashKitTests/TinyHybridTarget.swift:27-30).  Same as the entries above with q
+ * and k laid out [T, k_heads, dk] (replay: [layers, width, k_heads, dk]); v, alpha, beta,
+ * out and the state keep `heads` value heads.  k_heads must divide heads; k_heads ==
+ * heads is the ungrouped entry. */
+int dflash_gdn_step_grouped(const float* state_in, float* state_out, const dflash_bf16* q,
+                            const dflash_bf16* k, const dflash_bf16* v, const float* alpha,
+                            const float* beta, dflash_bf16* out, int T, int heads, int k_heads, int dk,
+                            int dv, float q_scale, dflash_stream_t stream);
+int dflash_gdn_step_tree_grouped(const float* state_in, const dflash_bf16* q, const dflash_bf16* k,
+                                 const dflash_bf16* v, const float* alpha, const float* beta,
+                                 const int32_t* parents, dflash_bf16* out, int T, int heads, int k_heads,
+                                 int dk, int dv, float q_scale, dflash_stream_t stream);
+int dflash_gdn_replay_grouped(const float* snapshot, float* state_out, const dflash_bf16* k,
+                              const dflash_bf16* v, const float* alpha, const float* beta,
+                              const int32_t* rows, int keep, int width, int layers, int heads, int k_heads,
+                              int dk, int dv, dflash_stream_t stream);
+
 /* Rollback of a verify round for `layers` gated-delta layers at once
  * (rollbackGatedDeltaRound / rollbackGatedDeltaTree, called at
  * DFlashSpeculativeGenerator.swift:455-460).  From the pre-round snapshot, replays

@@ -47,6 +47,19 @@ int dflash_stack_gdn_conv_gates(const dflash_bf16* x, int ld, const dflash_bf16*
                                 const float* dt_bias, float* alpha, float* beta, int M, int heads, int dk, int kc,
                                 dflash_stream_t stream);
 
+/* dflash_stack_gdn_conv_gates for layers whose q and k have k_heads heads and v has `heads`
+ * (k_heads divides heads; see dflash_gdn_step_grouped): x rows hold
+ * [q (k_heads dk) | k (k_heads dk) | v (heads dk)], weight and window cover those
+ * (2 k_heads + heads) dk channels, y receives [q: M x k_heads dk | k: M x k_heads dk |
+ * v: M x heads dk], and the gates (ab: b then a, one per value head) go to alpha, beta
+ * fp32 [M, heads].  parents: NULL for a chain round, else a tree round's parent list
+ * (M <= 32) as for dflash_stack_gdn_conv_gates_tree. */
+int dflash_stack_gdn_conv_gates_grouped(const dflash_bf16* x, int ld, const dflash_bf16* window,
+                                        const dflash_bf16* weight, dflash_bf16* y, const dflash_bf16* ab, int ld_ab,
+                                        const float* a_log, const float* dt_bias, float* alpha, float* beta, int M,
+                                        int heads, int k_heads, int dk, int kc, const int32_t* parents,
+                                        dflash_stream_t stream);
+
 /* out bf16 [M, heads * dv] = rmsnorm(o per head) * weight (bf16 [dv]) * silu(z); z has row
  * stride ld_z. */
 int dflash_stack_gated_norm(const dflash_bf16* o, const dflash_bf16* z, int ld_z, const dflash_bf16* weight,

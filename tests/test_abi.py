@@ -292,3 +292,20 @@ def test_accept_tree_argument_errors(dc):
     assert L.dflash_accept_tree(FAKE, FAKE, FAKE, 0, FAKE, FAKE, FAKE, None) == 1
     assert L.dflash_accept_tree(FAKE, FAKE, FAKE, 33, FAKE, FAKE, FAKE, None) == 1
     assert L.dflash_accept_tree(FAKE, FAKE, FAKE, 8, FAKE, None, FAKE, None) == 1
+
+
+def test_grouped_key_head_argument_errors(dc):
+    L = dc.lib
+    step = lambda heads=8, kh=4: L.dflash_gdn_step_grouped(FAKE, FAKE + 0x100000, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE,
+                                                           8, heads, kh, 128, 128, 1.0, None)
+    assert step(kh=3) == 1 and step(kh=0) == 1 and step(kh=16) == 1
+    tree = lambda kh: L.dflash_gdn_step_tree_grouped(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 8, 8, kh, 128,
+                                                     128, 1.0, None)
+    assert tree(3) == 1 and tree(0) == 1
+    replay = lambda kh: L.dflash_gdn_replay_grouped(FAKE, FAKE + 0x100000, FAKE, FAKE, FAKE, FAKE, None, 4, 8, 2, 8,
+                                                    kh, 128, 128, None)
+    assert replay(5) == 1 and replay(0) == 1
+    cg = lambda heads=8, kh=4, ld=(2 * 4 + 8) * 64, M=8, parents=None, dk=64: L.dflash_stack_gdn_conv_gates_grouped(
+        FAKE, ld, FAKE, FAKE, FAKE, FAKE, 16, FAKE, FAKE, FAKE, FAKE, M, heads, kh, dk, 4, parents, None)
+    assert cg(kh=3) == 1 and cg(ld=100) == 1 and cg(M=33, parents=FAKE) == 1
+    assert cg(dk=48, ld=(2 * 4 + 8) * 48) == 2
