@@ -20,7 +20,7 @@ stored as separate parts loads through the part names.
 Stack tensor names (one prefix per projection; a fused projection may instead be given
 as its parts, whose rows are concatenated in the order listed):
   model.layers.{i}.input_layernorm.weight, .post_attention_layernorm.weight
-  gated-delta layer:  .linear_attn.in_proj       = [q | k | v | z | b | a]
+  gated-delta layer:  .linear_attn.in_proj       = [q | k | v | z | b | a] (q, k: key heads)
                         (or in_proj_q, in_proj_k, in_proj_v, in_proj_z, in_proj_b, in_proj_a)
                       .linear_attn.out_proj, .linear_attn.conv1d.weight [3·H·dk, kc],
                       .linear_attn.A_log, .linear_attn.dt_bias, .linear_attn.norm.weight
@@ -220,9 +220,10 @@ def stack_config_from_json(config: dict, context: int, block: int = 8):
     level), rms_norm_eps, vocab_size, and the global "quantization" entry.  `context` and
     `block` size the attention caches and the verify block.
 
-    The stack's gated-delta layers use one head count for q, k and v; a checkpoint with
-    fewer key heads than value heads (a key head shared by several value heads) is
-    rejected with CheckpointError, as is a rotary width the attention prep cannot take."""
+    Fewer key heads than value heads (each key head shared by linear_num_value_heads /
+    linear_num_key_heads value heads) becomes gdn_key_heads; a key-head count that does
+    not divide the value heads, or a rotary width the attention prep cannot take, is
+    rejected with CheckpointError."""
     import verify_stack as vs
 
     def need(key):
@@ -236,8 +237,8 @@ def stack_config_from_json(config: dict, context: int, block: int = 8):
     head_dim = int(need("head_dim"))
     rot = int(round(head_dim * factor))
     hv, hk = int(need("linear_num_value_heads")), int(need("linear_num_key_heads"))
-    if hv != hk:
-        raise CheckpointError(f"{hk} gated-delta key heads for {hv} value heads: the stack needs one head count")
+    if hk < 1 or hv % hk:
+        raise CheckpointError(f"{hk} gated-delta key heads do not divide {hv} value heads")
     if rot % 64 or rot > head_dim:
         raise CheckpointError(f"rotary width {rot} of head dim {head_dim}: a multiple of 64 up to the head dim needed")
     q = config.get("quantization") or config.get("quantization_config")
@@ -250,7 +251,7 @@ def stack_config_from_json(config: dict, context: int, block: int = 8):
         conv_kernel=int(need("linear_conv_kernel_dim")), attn_heads=int(need("num_attention_heads")),
         kv_heads=int(need("num_key_value_heads")), head_dim=head_dim, rotary_dim=rot, rope_theta=theta,
         eps=float(config.get("rms_norm_eps", 1e-6)), group=int(q["group_size"]), bits=int(q["bits"]),
-        context=int(context), block=int(block), vocab=int(need("vocab_size")))
+        context=int(context), block=int(block), vocab=int(need("vocab_size")), gdn_key_heads=hk if hk != hv else 0)
 
 
 def stack_from_checkpoint(cfg, plan, config: dict, tensors: Dict[str, torch.Tensor], device) -> dict:
@@ -265,13 +266,13 @@ def stack_from_checkpoint(cfg, plan, config: dict, tensors: Dict[str, torch.Tens
         L = {"kind": kind, "ln": get(f"{pre}.input_layernorm.weight").to(torch.bfloat16),
              "post_ln": get(f"{pre}.post_attention_layernorm.weight").to(torch.bfloat16)}
         if kind == "gdn":
-            Hg, dk, kc = cfg.gdn_heads, cfg.gdn_dk, cfg.conv_kernel
+            Hg, Hk, dk, kc = cfg.gdn_heads, cfg.gdn_kheads, cfg.gdn_dk, cfg.conv_kernel
             L["in_proj"] = _fused(tensors, config, pre, "linear_attn.in_proj").rows(vs._ranges_gdn_in(cfg, plan))
             out = quantized_layer(tensors, config, f"{pre}.linear_attn.out_proj")
             L["out_proj"] = out.cols(plan.gdn_head0 * cfg.gdn_dv, (plan.gdn_head0 + plan.gdn_heads) * cfg.gdn_dv)
-            conv = get(f"{pre}.linear_attn.conv1d.weight").to(torch.bfloat16).reshape(3 * Hg * dk, kc)
+            conv = get(f"{pre}.linear_attn.conv1d.weight").to(torch.bfloat16).reshape((2 * Hk + Hg) * dk, kc)
             heads = slice(plan.gdn_head0, plan.gdn_head0 + plan.gdn_heads)
-            L["conv"] = conv.view(3, Hg, dk, kc)[:, heads].reshape(-1, kc).contiguous()
+            L["conv"] = torch.cat([conv[a:b] for a, b in vs.gdn_conv_channels(cfg, plan)]).contiguous()
             L["a_log"] = get(f"{pre}.linear_attn.A_log").float()[heads].contiguous()
             L["dt_bias"] = get(f"{pre}.linear_attn.dt_bias").float()[heads].contiguous()
             L["gdn_norm"] = get(f"{pre}.linear_attn.norm.weight").to(torch.bfloat16)
@@ -324,7 +325,7 @@ def save_stack_checkpoint(directory, cfg, weights: dict, shard_bytes: int = 1 <<
     put_quant("lm_head", weights["lm_head"])
     config = {"model_type": "dflash_verify_stack", "hidden_size": cfg.hidden, "num_hidden_layers": cfg.layers,
               "intermediate_size": cfg.intermediate, "full_attention_interval": cfg.attn_interval,
-              "linear_num_value_heads": cfg.gdn_heads, "linear_num_key_heads": cfg.gdn_heads,
+              "linear_num_value_heads": cfg.gdn_heads, "linear_num_key_heads": cfg.gdn_kheads,
               "linear_key_head_dim": cfg.gdn_dk, "linear_value_head_dim": cfg.gdn_dv,
               "linear_conv_kernel_dim": cfg.conv_kernel, "num_attention_heads": cfg.attn_heads,
               "num_key_value_heads": cfg.kv_heads, "head_dim": cfg.head_dim, "rms_norm_eps": cfg.eps,

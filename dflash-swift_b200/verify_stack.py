@@ -71,6 +71,12 @@ class StackConfig:
     context: int = 1024         # tokens already in each attention cache
     block: int = 8              # M: rows verified per forward
     vocab: int = 248320         # LM head rows (sharded by vocabulary over the ranks)
+    gdn_key_heads: int = 0      # gated-delta q / k heads (0: gdn_heads); each shared by
+                                # gdn_heads / gdn_key_heads value heads (linear_num_key_heads)
+
+    @property
+    def gdn_kheads(self) -> int:
+        return self.gdn_key_heads or self.gdn_heads
 
     @property
     def max_len(self) -> int:
@@ -88,6 +94,9 @@ CONFIG4 = StackConfig()
 # A small stack of the same structure for parity tests (3 GDN + 1 attention layers).
 TINY = StackConfig(layers=4, hidden=256, intermediate=512, gdn_heads=4, gdn_dk=64, gdn_dv=64, attn_heads=4,
                    kv_heads=2, head_dim=64, rotary_dim=64, rope_theta=1.0e4, context=24, block=8, vocab=1024)
+# The same with 2 gated-delta key heads for the 4 value heads (as the reference's fixture
+# has, Tests/DFlashKitTests/TinyHybridTarget.swift:27-30).
+TINY_GROUPED = replace(TINY, gdn_key_heads=2)
 
 
 # ----------------------------------------------------------------------------- shard plan
@@ -106,6 +115,8 @@ class ShardPlan:
     inter0: int
     vocab: int = 0          # LM head rows on this rank
     vocab0: int = 0
+    gdn_key_heads: int = 0  # gated-delta q / k heads on this rank (those its value heads read)
+    gdn_key_head0: int = 0
 
 
 def shard_plan(cfg: StackConfig, rank: int, world: int) -> ShardPlan:
@@ -126,7 +137,10 @@ def shard_plan(cfg: StackConfig, rank: int, world: int) -> ShardPlan:
         raise ValueError("attn_heads must be a multiple of kv_heads")
     if cfg.gdn_dk != cfg.gdn_dv:
         raise ValueError("the gated-delta conv treats q, k and v as equal parts: gdn_dk must equal gdn_dv")
+    if cfg.gdn_heads % cfg.gdn_kheads or cfg.gdn_kheads % world:
+        raise ValueError(f"gdn_key_heads={cfg.gdn_kheads} must divide gdn_heads and split over {world} ranks")
     gh = cfg.gdn_heads // world
+    gkh = cfg.gdn_kheads // world  # value heads [rank gh, ...) read key heads [rank gkh, ...)
     ah = cfg.attn_heads // world
     q_per_kv = cfg.attn_heads // cfg.kv_heads
     if cfg.kv_heads % world == 0:
@@ -142,16 +156,29 @@ def shard_plan(cfg: StackConfig, rank: int, world: int) -> ShardPlan:
     if cfg.vocab % world:
         raise ValueError(f"vocab={cfg.vocab} does not split over {world} ranks")
     vr = cfg.vocab // world
-    return ShardPlan(rank, world, gh, rank * gh, ah, rank * ah, kvh, kv0, inter, rank * inter, vr, rank * vr)
+    return ShardPlan(rank, world, gh, rank * gh, ah, rank * ah, kvh, kv0, inter, rank * inter, vr, rank * vr,
+                     gkh, rank * gkh)
 
 
 def _ranges_gdn_in(cfg: StackConfig, p: ShardPlan):
-    """Global row ranges of the in_proj [q | k | v | z | b | a] this rank keeps, in order."""
-    H, dk, dv = cfg.gdn_heads, cfg.gdn_dk, cfg.gdn_dv
+    """Global row ranges of the in_proj [q | k | v | z | b | a] this rank keeps, in order
+    (q and k have gdn_kheads heads, the rest one entry per value head)."""
+    H, Hk, dk, dv = cfg.gdn_heads, cfg.gdn_kheads, cfg.gdn_dk, cfg.gdn_dv
     h0, h1 = p.gdn_head0, p.gdn_head0 + p.gdn_heads
-    offs = [0, H * dk, 2 * H * dk, 2 * H * dk + H * dv, 2 * H * dk + 2 * H * dv, 2 * H * dk + 2 * H * dv + H]
-    widths = [dk, dk, dv, dv, 1, 1]
-    return [(o + h0 * w, o + h1 * w) for o, w in zip(offs, widths)]
+    k0, k1 = p.gdn_key_head0, p.gdn_key_head0 + p.gdn_key_heads
+    v_off = 2 * Hk * dk
+    return [(k0 * dk, k1 * dk), (Hk * dk + k0 * dk, Hk * dk + k1 * dk), (v_off + h0 * dv, v_off + h1 * dv),
+            (v_off + H * dv + h0 * dv, v_off + H * dv + h1 * dv), (v_off + 2 * H * dv + h0, v_off + 2 * H * dv + h1),
+            (v_off + 2 * H * dv + H + h0, v_off + 2 * H * dv + H + h1)]
+
+
+def gdn_conv_channels(cfg: StackConfig, p: ShardPlan):
+    """Global channel ranges of the gated-delta conv [q | k | v] this rank keeps (its key
+    heads' q and k channels, its value heads' v channels), in order."""
+    Hk, dk = cfg.gdn_kheads, cfg.gdn_dk
+    k0, k1 = p.gdn_key_head0 * dk, (p.gdn_key_head0 + p.gdn_key_heads) * dk
+    h0, h1 = p.gdn_head0 * dk, (p.gdn_head0 + p.gdn_heads) * dk
+    return [(k0, k1), (Hk * dk + k0, Hk * dk + k1), (2 * Hk * dk + h0, 2 * Hk * dk + h1)]
 
 
 def _ranges_attn_qkv(cfg: StackConfig, p: ShardPlan):
@@ -239,17 +266,17 @@ def build_rank_weights(cfg: StackConfig, plan: ShardPlan, seed: int, device) -> 
     for li, kind in enumerate(cfg.layer_kinds()):
         L = {"kind": kind, "ln": _norm_weight(g(li, 0), H, dev), "post_ln": _norm_weight(g(li, 1), H, dev)}
         if kind == "gdn":
-            Hg, dk, dv, kc = cfg.gdn_heads, cfg.gdn_dk, cfg.gdn_dv, cfg.conv_kernel
-            n_in = 2 * Hg * dk + 2 * Hg * dv + 2 * Hg
+            Hg, Hk, dk, dv, kc = cfg.gdn_heads, cfg.gdn_kheads, cfg.gdn_dk, cfg.gdn_dv, cfg.conv_kernel
+            n_in = 2 * Hk * dk + 2 * Hg * dv + 2 * Hg
             L["in_proj"] = random_quant(g(li, 2), n_in, H, G, B, dev).rows(_ranges_gdn_in(cfg, plan))
             L["out_proj"] = random_quant(g(li, 3), H, Hg * dv, G, B, dev).cols(plan.gdn_head0 * dv,
                                                                               (plan.gdn_head0 + plan.gdn_heads) * dv)
             gg = g(li, 4)
-            conv = (0.5 * torch.randn(3 * Hg * dk, kc, generator=gg, device=dev)).to(torch.bfloat16)
+            conv = (0.5 * torch.randn((2 * Hk + Hg) * dk, kc, generator=gg, device=dev)).to(torch.bfloat16)
             a_log = torch.log(torch.empty(Hg, device=dev).uniform_(1.0, 16.0, generator=gg))
             dt_bias = 0.5 * torch.randn(Hg, generator=gg, device=dev)
             heads = slice(plan.gdn_head0, plan.gdn_head0 + plan.gdn_heads)
-            conv3 = conv.view(3, Hg, dk, kc)[:, heads].reshape(-1, kc).contiguous()
+            conv3 = torch.cat([conv[a:b] for a, b in gdn_conv_channels(cfg, plan)]).contiguous()
             L.update(conv=conv3, a_log=a_log[heads].contiguous(), dt_bias=dt_bias[heads].contiguous(),
                      gdn_norm=_norm_weight(gg, dv, dev))
         else:
@@ -270,20 +297,20 @@ def build_rank_weights(cfg: StackConfig, plan: ShardPlan, seed: int, device) -> 
 
 def build_rank_state(cfg: StackConfig, plan: ShardPlan, seed: int, device) -> dict:
     """Pre-round state of this rank's shard: gated-delta snapshots (fp32 [h, dv, dk]) and
-    conv windows (bf16 [kc-1, 3 h dk]); attention caches (bf16 [hkv, max_len, d]) holding
-    `context` random tokens."""
+    conv windows (bf16 [kc-1, (2 hk + h) dk]); attention caches (bf16 [hkv, max_len, d])
+    holding `context` random tokens."""
     dev = torch.device(device)
     out = []
     for li, kind in enumerate(cfg.layer_kinds()):
         gen = torch.Generator(device=dev)
         gen.manual_seed(layer_seed(seed + 7, li, 9))
         if kind == "gdn":
-            Hg, dk, dv, kc = cfg.gdn_heads, cfg.gdn_dk, cfg.gdn_dv, cfg.conv_kernel
+            Hg, Hk, dk, dv, kc = cfg.gdn_heads, cfg.gdn_kheads, cfg.gdn_dk, cfg.gdn_dv, cfg.conv_kernel
             heads = slice(plan.gdn_head0, plan.gdn_head0 + plan.gdn_heads)
             snap = 0.1 * torch.randn(Hg, dv, dk, generator=gen, device=dev)
-            win = torch.randn(kc - 1, 3, Hg, dk, generator=gen, device=dev).to(torch.bfloat16)
+            win = torch.randn(kc - 1, (2 * Hk + Hg) * dk, generator=gen, device=dev).to(torch.bfloat16)
             out.append({"snapshot": snap[heads].contiguous(),
-                        "window": win[:, :, heads].reshape(kc - 1, -1).contiguous()})
+                        "window": torch.cat([win[:, a:b] for a, b in gdn_conv_channels(cfg, plan)], 1).contiguous()})
         else:
             Hkv, d = cfg.kv_heads, cfg.head_dim
             kv = slice(plan.kv_head0, plan.kv_head0 + plan.kv_heads)
@@ -404,8 +431,12 @@ class VerifyStack:
         # commit() rebuilds the conv window from) and the conv output q | k | v, which with
         # alpha and beta is the capture the recurrence replays
         n_gdn = sum(1 for k in cfg.layer_kinds() if k == "gdn")
-        self.gdn_proj = torch.empty(n_gdn, M, 2 * h * dk + 2 * h * dv + 2 * h, **bf)
-        self.capture_qkv = torch.empty(n_gdn, 3, M, h, dk, **bf)
+        hk = p.gdn_key_heads or h
+        self.gdn_proj = torch.empty(n_gdn, M, 2 * hk * dk + 2 * h * dv + 2 * h, **bf)
+        # [3, M, h, dk] per layer; with shared key heads the q, k and v blocks are
+        # [M, hk, dk], [M, hk, dk], [M, h, dk] back to back (gdn_qkv gives the views)
+        self.capture_qkv = (torch.empty(n_gdn, 3, M, h, dk, **bf) if hk == h else
+                            torch.empty(n_gdn, M * (2 * hk + h) * dk, **bf))
         self.capture_alpha = torch.empty(n_gdn, M, h, **f32)
         self.capture_beta = torch.empty(n_gdn, M, h, **f32)
         self.state_out = torch.empty(n_gdn, h, dv, dk, **f32)
@@ -454,24 +485,35 @@ class VerifyStack:
         else:
             self.dc.stack_add_rmsnorm(self.resid, pending, weight, out, self.cfg.eps)
 
+    def gdn_qkv(self, gi):
+        """Layer gi's captured q, k ([M, hk, dk]) and v ([M, h, dv]) after the conv."""
+        M, h, dk = self.cfg.block, self.plan.gdn_heads, self.cfg.gdn_dk
+        hk = self.plan.gdn_key_heads or h
+        qkv = self.capture_qkv[gi]
+        if hk == h:
+            return qkv[0], qkv[1], qkv[2]
+        n = M * hk * dk
+        return qkv[:n].view(M, hk, dk), qkv[n:2 * n].view(M, hk, dk), qkv[2 * n:].view(M, h, dk)
+
     def _gdn(self, L, S, gi):
         cfg, p, dc = self.cfg, self.plan, self.dc
         M, h, dk, dv = cfg.block, p.gdn_heads, cfg.gdn_dk, cfg.gdn_dv
+        hk = p.gdn_key_heads or h
         proj = self.gdn_proj[gi]
         self._qmm(self.normed, L["in_proj"], proj)
         qkv = self.capture_qkv[gi]
-        q, k, v = qkv[0], qkv[1], qkv[2]
-        ab = proj[:, 2 * h * dk + 2 * h * dv:]
+        q, k, v = self.gdn_qkv(gi)
+        ab = proj[:, 2 * hk * dk + 2 * h * dv:]
         alpha, beta = self.capture_alpha[gi], self.capture_beta[gi]
         dc.stack_gdn_conv_gates(proj, S["window"], L["conv"], qkv, ab, L["a_log"], L["dt_bias"], alpha, beta,
-                                h, dk, parents=self.parents)
+                                h, dk, parents=self.parents, k_heads=hk)
         if self.parents is None:
             dc.gdn_step(S["snapshot"], self.state_out[gi], q, k, v, alpha, beta, out=self.gdn_o,
                         q_scale=1.0 / math.sqrt(dk))
         else:  # no state after a tree round: commit() replays the accepted path
             dc.gdn_step_tree(S["snapshot"], q, k, v, alpha, beta, self.parents, self.gdn_o,
                              q_scale=1.0 / math.sqrt(dk))
-        z = proj[:, 2 * h * dk + h * dv:]
+        z = proj[:, 2 * hk * dk + h * dv:]
         dc.stack_gated_norm(self.gdn_o, z, L["gdn_norm"], self.gdn_normed, cfg.eps)
         return self._qmm_reduced(self.gdn_normed, L["out_proj"])
 
@@ -589,12 +631,12 @@ class VerifyStack:
             raise ValueError(f"rows {rows} are not a root path of the current tree")
         if self.tree_plan is None and rows != list(range(keep)):
             raise ValueError(f"a chain round keeps rows 0 .. keep-1, not {rows}")
-        C = 3 * p.gdn_heads * cfg.gdn_dk
+        C = (2 * (p.gdn_key_heads or p.gdn_heads) + p.gdn_heads) * cfg.gdn_dk
         gi = 0
         for L, S in zip(self.w["layers"], self.state["layers"]):
             if L["kind"] == "gdn":
-                qkv = self.capture_qkv[gi]
-                dc.gdn_replay(S["snapshot"][None], self.state_out[gi][None], qkv[1][None], qkv[2][None],
+                _, k, v = self.gdn_qkv(gi)
+                dc.gdn_replay(S["snapshot"][None], self.state_out[gi][None], k[None], v[None],
                               self.capture_alpha[gi][None], self.capture_beta[gi][None], keep=keep, rows=rows)
                 S["snapshot"].copy_(self.state_out[gi])
                 conv_in = self.gdn_proj[gi][:, :C].contiguous()

@@ -180,29 +180,35 @@ def forward(cfg, plan, weights: dict, state: dict, hidden: torch.Tensor,
         L = {k: (cpu(v) if isinstance(v, torch.Tensor) else v) for k, v in L.items()}
         normed = add_rmsnorm(resid, delta, L["ln"], eps)
         if L["kind"] == "gdn":
+            # q and k have hk heads, each read by h / hk consecutive value heads
+            hk = getattr(plan, "gdn_key_heads", 0) or h
+            C = (2 * hk + h) * dk
             proj = qmm(normed, L["in_proj"])
-            cap["conv_in"].append(proj[:, :3 * h * dk])
-            conv = conv_silu(proj[:, :3 * h * dk], cpu(S["window"]), L["conv"], parents)
-            q, k, v = (conv[:, i * h * dk:(i + 1) * h * dk].reshape(M, h, dk) for i in range(3))
+            cap["conv_in"].append(proj[:, :C])
+            conv = conv_silu(proj[:, :C], cpu(S["window"]), L["conv"], parents)
+            q = conv[:, :hk * dk].reshape(M, hk, dk)
+            k = conv[:, hk * dk:2 * hk * dk].reshape(M, hk, dk)
+            v = conv[:, 2 * hk * dk:].reshape(M, h, dk)
             q, k = l2norm_heads(q), l2norm_heads(k)
-            ab = proj[:, 2 * h * dk + 2 * h * dv:]
+            qr, kr = q.repeat_interleave(h // hk, dim=1), k.repeat_interleave(h // hk, dim=1)
+            ab = proj[:, 2 * hk * dk + 2 * h * dv:]
             alpha, beta = gdn_gates(ab, L["a_log"], L["dt_bias"], h)
             if parents is None:
-                st, o = gdn_step(cpu(S["snapshot"]), q, k, v, alpha, beta, 1.0 / math.sqrt(dk))
+                st, o = gdn_step(cpu(S["snapshot"]), qr, kr, v, alpha, beta, 1.0 / math.sqrt(dk))
             else:  # each row's output from the first leaf's path (row order) that holds it
                 st, o, done = None, torch.zeros(M, h, dv), set()
                 for path in paths:
-                    _, op = gdn_step(cpu(S["snapshot"]), q[path], k[path], v[path], alpha[path], beta[path],
+                    _, op = gdn_step(cpu(S["snapshot"]), qr[path], kr[path], v[path], alpha[path], beta[path],
                                      1.0 / math.sqrt(dk))
                     for i, r in enumerate(path):
                         if r not in done:
                             o[r] = op[i]
                             done.add(r)
-            cap["qkv"].append(torch.stack([q, k, v]))
+            cap["qkv"].append(torch.stack([q, k, v]) if hk == h else (q, k, v))
             cap["alpha"].append(alpha)
             cap["beta"].append(beta)
             cap["state"].append(st)
-            z = proj[:, 2 * h * dk + h * dv:2 * h * dk + 2 * h * dv]
+            z = proj[:, 2 * hk * dk + h * dv:2 * hk * dk + 2 * h * dv]
             part = qmm(gated_norm(o, z, L["gdn_norm"], eps), L["out_proj"])
         else:
             qkv = qmm(normed, L["qkv"])
@@ -245,6 +251,7 @@ def commit(state: dict, result: dict, rows, context: int) -> None:
     for S in state["layers"]:
         if "snapshot" in S:
             q, k, v = result["qkv"][gi]
+            k = k.repeat_interleave(v.shape[1] // k.shape[1], dim=1)  # shared key heads, per value head
             s, _ = O.gdn_recurrence(S["snapshot"].detach().cpu().float().numpy(), _bits(k.to(torch.bfloat16)),
                                     _bits(v.to(torch.bfloat16)), result["alpha"][gi].numpy(),
                                     result["beta"][gi].numpy(), keep, rows=rows)

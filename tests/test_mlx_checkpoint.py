@@ -105,10 +105,12 @@ def test_stack_config_from_config_json(tmp_path):
     tiny = {**c4, "hidden_size": 64, "num_hidden_layers": 4, "intermediate_size": 128, "num_attention_heads": 4,
             "num_key_value_heads": 2, "head_dim": 16, "linear_num_value_heads": 4, "linear_num_key_heads": 2,
             "linear_key_head_dim": 32, "linear_value_head_dim": 32, "vocab_size": 64, "full_attention_interval": 2}
-    with pytest.raises(mc.CheckpointError, match="key heads"):
-        mc.stack_config_from_json(tiny, context=8)
     with pytest.raises(mc.CheckpointError, match="rotary"):
-        mc.stack_config_from_json({**tiny, "linear_num_key_heads": 4}, context=8)
+        mc.stack_config_from_json(tiny, context=8)
+    grouped = mc.stack_config_from_json({**tiny, "head_dim": 256}, context=8)  # rotary 0.25 x 256 = 64
+    assert (grouped.gdn_heads, grouped.gdn_key_heads, grouped.gdn_kheads) == (4, 2, 2)
+    with pytest.raises(mc.CheckpointError, match="key heads"):
+        mc.stack_config_from_json({**tiny, "head_dim": 256, "linear_num_key_heads": 3}, context=8)
     with pytest.raises(mc.CheckpointError, match="hidden_size"):
         mc.stack_config_from_json({k: v for k, v in c4.items() if k != "hidden_size"}, context=8)
 
