@@ -280,15 +280,17 @@ void rollback(std::vector<MambaCache>& caches, const std::vector<GatedDeltaCaptu
         expect(m.convWindow, DType::bfloat16, 2, "cache conv window");
         expect(c.convInputs, DType::bfloat16, 2, "capture conv inputs");
         const int64_t H = c.state.dim(0), dv = c.state.dim(1), dk = c.state.dim(2);
-        if (m.state.shape != c.state.shape || c.k.shape != std::vector<int64_t>{width, H, dk} ||
+        const int64_t Hk = c.k.dim(1);  // key heads: each shared by H / Hk value heads
+        if (Hk < 1 || H % Hk != 0 || m.state.shape != c.state.shape || c.k.shape != std::vector<int64_t>{width, Hk, dk} ||
             c.v.shape != std::vector<int64_t>{width, H, dv} || c.alpha.shape != std::vector<int64_t>{width, H} ||
             c.beta.shape != c.alpha.shape || m.convWindow.shape != c.convWindow.shape ||
             c.convInputs.dim(0) != width || c.convInputs.dim(1) != c.convWindow.dim(1))
             raise(DFLASH_ERR_INVALID_ARGUMENT, "rollback: layer " + std::to_string(i) + " shapes disagree");
-        check(dflash_gdn_replay(static_cast<const float*>(c.state.data), static_cast<float*>(m.state.data),
-                                static_cast<const dflash_bf16*>(c.k.data), static_cast<const dflash_bf16*>(c.v.data),
-                                static_cast<const float*>(c.alpha.data), static_cast<const float*>(c.beta.data), rows,
-                                keep, width, 1, (int)H, (int)dk, (int)dv, stream));
+        check(dflash_gdn_replay_grouped(static_cast<const float*>(c.state.data), static_cast<float*>(m.state.data),
+                                        static_cast<const dflash_bf16*>(c.k.data),
+                                        static_cast<const dflash_bf16*>(c.v.data),
+                                        static_cast<const float*>(c.alpha.data), static_cast<const float*>(c.beta.data),
+                                        rows, keep, width, 1, (int)H, (int)Hk, (int)dk, (int)dv, stream));
         check(dflash_gdn_conv_rollback(static_cast<const dflash_bf16*>(c.convWindow.data),
                                        static_cast<dflash_bf16*>(m.convWindow.data),
                                        static_cast<const dflash_bf16*>(c.convInputs.data), rows, keep, width, 1,

@@ -154,7 +154,8 @@ struct GatedDeltaCapture {
     DeviceArray convWindow;  // bf16 [kc-1, C], pre-round
     DeviceArray state;       // fp32 [H, dv, dk], pre-round
     DeviceArray convInputs;  // bf16 [width, C]: the rows' inputs to the conv
-    DeviceArray k;           // bf16 [width, H, dk] (after conv, L2-normalised)
+    DeviceArray k;           // bf16 [width, Hk, dk] (after conv, L2-normalised); Hk divides H, each
+                             // key head shared by H / Hk value heads (Hk = H: one head count)
     DeviceArray v;           // bf16 [width, H, dv]
     DeviceArray alpha;       // fp32 [width, H]
     DeviceArray beta;        // fp32 [width, H]

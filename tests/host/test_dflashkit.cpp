@@ -342,7 +342,7 @@ static void testSmallMQuantizedLinearMatchesTheOracle(int rows, bool withBias) {
     CHECK(c <= 1e-2);
 }
 
-static void testRollbackMatchesTheOracle(bool tree) {
+static void testRollbackMatchesTheOracle(bool tree, int Hk = 4) {
     const int L = 2, W = 8, H = 4, dk = 128, dv = 128, kc1 = 3, C = 384;
     std::mt19937 rng(tree ? 3 : 4);
     std::normal_distribution<float> n01(0.f, 1.f);
@@ -360,9 +360,9 @@ static void testRollbackMatchesTheOracle(bool tree) {
         Host& h = hosts[l];
         h.s0.resize((size_t)H * dv * dk);
         for (auto& v : h.s0) v = 0.1f * n01(rng);
-        std::vector<float> kf((size_t)W * H * dk);
+        std::vector<float> kf((size_t)W * Hk * dk);  // Hk key heads, each read by H / Hk value heads
         for (auto& v : kf) v = n01(rng);
-        for (int t = 0; t < W * H; ++t) {  // L2-normalised per head
+        for (int t = 0; t < W * Hk; ++t) {  // L2-normalised per head
             double ss = 0;
             for (int j = 0; j < dk; ++j) ss += (double)kf[(size_t)t * dk + j] * kf[(size_t)t * dk + j];
             for (int j = 0; j < dk; ++j) kf[(size_t)t * dk + j] = (float)(kf[(size_t)t * dk + j] / std::sqrt(ss));
@@ -378,7 +378,7 @@ static void testRollbackMatchesTheOracle(bool tree) {
         h.cin = randomBf16((size_t)W * C, rng);
         GatedDeltaCapture c;
         c.state = upload(h.s0, {H, dv, dk}, DType::float32);
-        c.k = upload(h.k, {W, H, dk}, DType::bfloat16);
+        c.k = upload(h.k, {W, Hk, dk}, DType::bfloat16);
         c.v = upload(h.v, {W, H, dv}, DType::bfloat16);
         c.alpha = upload(h.a, {W, H}, DType::float32);
         c.beta = upload(h.b, {W, H}, DType::float32);
@@ -395,8 +395,12 @@ static void testRollbackMatchesTheOracle(bool tree) {
     CHECK(cudaDeviceSynchronize() == cudaSuccess);
     for (int l = 0; l < L; ++l) {
         const Host& h = hosts[l];
+        std::vector<uint16_t> kv((size_t)W * H * dk);  // k per value head for the oracle
+        for (int t = 0; t < W; ++t)
+            for (int hv = 0; hv < H; ++hv)
+                std::memcpy(&kv[((size_t)t * H + hv) * dk], &h.k[((size_t)t * Hk + hv / (H / Hk)) * dk], dk * 2);
         std::vector<double> want((size_t)H * dv * dk);
-        oracle_gdn_recurrence(h.s0.data(), nullptr, h.k.data(), h.v.data(), h.a.data(), h.b.data(),
+        oracle_gdn_recurrence(h.s0.data(), nullptr, kv.data(), h.v.data(), h.a.data(), h.b.data(),
                               tree ? rows.data() : nullptr, keep, H, dk, dv, 1.0, want.data(), nullptr);
         const auto got = download<float>(caches[l].state);
         double diff = 0, scale = 0;
@@ -423,6 +427,8 @@ static int runGpu() {
     testSmallMQuantizedLinearMatchesTheOracle(1, false);
     testRollbackMatchesTheOracle(false);
     testRollbackMatchesTheOracle(true);
+    testRollbackMatchesTheOracle(true, 2);  // shared key heads
+    testRollbackMatchesTheOracle(false, 1);
     uint32_t bits = 0;
     CHECK(dflash_device_error(&bits, nullptr) == DFLASH_OK && bits == 0);
     return 0;
