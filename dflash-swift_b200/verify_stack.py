@@ -697,6 +697,8 @@ def main(argv=None) -> int:
     ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
                     help="peer: NVLink stores into the other ranks' exchange buffers, summed by the next "
                          "RMSNorm; nccl: torch.distributed.all_reduce")
+    ap.add_argument("--gdn-key-heads", type=int, default=None,
+                    help="gated-delta q / k heads, each shared by gdn_heads / this many value heads")
     ap.add_argument("--tree", default=None,
                     help="verify a speculative tree instead of a chain: comma-separated parent rows, one per "
                          "block row (-1 for the anchor), e.g. -1,0,0,1,1,2,3,5")
@@ -716,6 +718,8 @@ def main(argv=None) -> int:
         cfg = replace(cfg, layers=args.layers)
     if args.context is not None:
         cfg = replace(cfg, context=args.context)
+    if args.gdn_key_heads is not None:
+        cfg = replace(cfg, gdn_key_heads=args.gdn_key_heads)
 
     stack = VerifyStack(cfg, rank, world, seed=args.seed, device=dev, group=pg, allreduce=args.allreduce,
                         tree=args.tree is not None)
