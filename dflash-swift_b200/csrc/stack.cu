@@ -456,8 +456,16 @@ template <int CH>
 __global__ void attn_prep_kernel(uint16_t* __restrict__ qkv, int ld, const uint16_t* __restrict__ q_norm,
                                  const uint16_t* __restrict__ k_norm, uint16_t* __restrict__ cache_k,
                                  uint16_t* __restrict__ cache_v, int M, int hq, int hkv, int rot, int pos0,
-                                 int max_len, float eps, float theta, const int32_t* __restrict__ parents) {
+                                 int max_len, float eps, float theta, const int32_t* __restrict__ parents,
+                                 const int32_t* __restrict__ position) {
     chain_in();
+    if (position) {  // the cache position from device memory (a graph replayed at a new context)
+        pos0 = *position;
+        if (pos0 < 0 || pos0 + M > max_len) {
+            if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(&g_device_error, DFLASH_DEVERR_POSITION);
+            return;
+        }
+    }
     constexpr int d = CH * 32;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int slots = hq + hkv;
@@ -571,7 +579,8 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __rest
                                                           const uint16_t* __restrict__ cache_v,
                                                           uint16_t* __restrict__ out, int hq, int hkv, int pos0,
                                                           int max_len, float scale,
-                                                          const int32_t* __restrict__ parents) {
+                                                          const int32_t* __restrict__ parents,
+                                                          const int32_t* __restrict__ position) {
     constexpr int d = CH * 32;
     constexpr int KU = 32 / GP;  // keys per warp step in the scores pass
     static_assert(GP <= kMaxG && KU * CH <= 64, "score registers");
@@ -579,6 +588,13 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __rest
     __shared__ __align__(16) float s_red[4][kMaxG][d];  // warp partials; s_red[0] ends as the CTA's p V
     __shared__ float s_m[kMaxG], s_l[kMaxG], s_corr[kMaxG], s_f[kSplit][kMaxG], s_den[kMaxG];
     chain_in();
+    if (position) {  // the cache position from device memory (a graph replayed at a new context)
+        pos0 = *position;
+        if (pos0 < 0 || pos0 + (int)gridDim.y > max_len) {  // every CTA leaves here, before any cluster barrier
+            if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicOr(&g_device_error, DFLASH_DEVERR_POSITION);
+            return;
+        }
+    }
     const int G = hq / hkv;
     const int kvh = blockIdx.x / kSplit, t = blockIdx.y;
     const uint32_t rank = cluster_rank();
@@ -990,7 +1006,9 @@ extern "C" int dflash_stack_gated_norm(const dflash_bf16* o, const dflash_bf16* 
 
 static int attn_prep(dflash_bf16* qkv, int ld, const dflash_bf16* q_norm, const dflash_bf16* k_norm,
                      dflash_bf16* cache_k, dflash_bf16* cache_v, int M, int hq, int hkv, int d, int rot, int pos0,
-                     int max_len, float eps, float theta, const int32_t* parents, dflash_stream_t stream) {
+                     int max_len, float eps, float theta, const int32_t* parents, dflash_stream_t stream,
+                     const int32_t* position = nullptr) {
+    if (position) pos0 = 0;  // read on the device; the kernel checks it against max_len
     if (!qkv || !q_norm || !k_norm || !cache_k || !cache_v || M < 1 || hq < 1 || hkv < 1 || pos0 < 0 ||
         pos0 + M > max_len || ld < (2 * hq + 2 * hkv) * d)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_attn_prep: bad arguments");
@@ -1004,15 +1022,15 @@ static int attn_prep(dflash_bf16* qkv, int ld, const dflash_bf16* q_norm, const 
     switch (d) {
         case 64:
             e = launch_chained(stack::attn_prep_kernel<2>, grid, block, 0, s, 1, qkv, ld, q_norm, k_norm, cache_k,
-                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta, parents);
+                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta, parents, position);
             break;
         case 128:
             e = launch_chained(stack::attn_prep_kernel<4>, grid, block, 0, s, 1, qkv, ld, q_norm, k_norm, cache_k,
-                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta, parents);
+                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta, parents, position);
             break;
         default:
             e = launch_chained(stack::attn_prep_kernel<8>, grid, block, 0, s, 1, qkv, ld, q_norm, k_norm, cache_k,
-                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta, parents);
+                               cache_v, M, hq, hkv, rot, pos0, max_len, eps, theta, parents, position);
             break;
     }
     DFLASH_CUDA_TRY(e);
@@ -1038,7 +1056,8 @@ extern "C" int dflash_stack_attn_prep_tree(dflash_bf16* qkv, int ld, const dflas
 
 static int attn_decode(const dflash_bf16* qkv, int ld, const dflash_bf16* cache_k, const dflash_bf16* cache_v,
                        dflash_bf16* out, int M, int hq, int hkv, int d, int pos0, int max_len, float scale,
-                       const int32_t* parents, dflash_stream_t stream) {
+                       const int32_t* parents, dflash_stream_t stream, const int32_t* position = nullptr) {
+    if (position) pos0 = 0;  // read on the device; the kernel checks it against max_len
     if (!qkv || !cache_k || !cache_v || !out || M < 1 || hq < 1 || hkv < 1 || hq % hkv || pos0 < 0 ||
         pos0 + M > max_len || ld < (2 * hq + 2 * hkv) * d || M > 65535)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_attn_decode: bad arguments");
@@ -1058,7 +1077,7 @@ static int attn_decode(const dflash_bf16* qkv, int ld, const dflash_bf16* cache_
 #define DFLASH_ATTN_CASE(CH, GP)                                                                                   \
     if (ch == CH && gp == GP)                                                                                      \
         e = launch_chained(stack::attn_decode_kernel<CH, GP>, grid, block, 0, s, stack::kSplit, qkv, ld, cache_k,    \
-                           cache_v, out, hq, hkv, pos0, max_len, scale, parents);
+                           cache_v, out, hq, hkv, pos0, max_len, scale, parents, position);
     DFLASH_ATTN_CASE(2, 1) DFLASH_ATTN_CASE(2, 2) DFLASH_ATTN_CASE(2, 4) DFLASH_ATTN_CASE(2, 8)
     DFLASH_ATTN_CASE(4, 2) DFLASH_ATTN_CASE(4, 4) DFLASH_ATTN_CASE(4, 8)
     DFLASH_ATTN_CASE(8, 4) DFLASH_ATTN_CASE(8, 8)
@@ -1221,4 +1240,25 @@ extern "C" int dflash_stack_gdn_conv_gates_grouped(const dflash_bf16* x, int ld,
 #undef DFLASH_CGG_CASE
     DFLASH_CUDA_TRY(e);
     return DFLASH_OK;
+}
+
+extern "C" int dflash_stack_attn_prep_ex(dflash_bf16* qkv, int ld, const dflash_bf16* q_norm,
+                                         const dflash_bf16* k_norm, dflash_bf16* cache_k, dflash_bf16* cache_v, int M,
+                                         int hq, int hkv, int d, int rot, int pos0, int max_len, float eps,
+                                         float theta, const int32_t* parents, const int32_t* position,
+                                         dflash_stream_t stream) {
+    if (parents && M > kMaxTreeRows)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_attn_prep_ex: a tree has at most %d rows", kMaxTreeRows);
+    return attn_prep(qkv, ld, q_norm, k_norm, cache_k, cache_v, M, hq, hkv, d, rot, pos0, max_len, eps, theta, parents,
+                     stream, position);
+}
+
+extern "C" int dflash_stack_attn_decode_ex(const dflash_bf16* qkv, int ld, const dflash_bf16* cache_k,
+                                           const dflash_bf16* cache_v, dflash_bf16* out, int M, int hq, int hkv, int d,
+                                           int pos0, int max_len, float scale, const int32_t* parents,
+                                           const int32_t* position, dflash_stream_t stream) {
+    if (parents && M > kMaxTreeRows)
+        return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_attn_decode_ex: a tree has at most %d rows",
+                    kMaxTreeRows);
+    return attn_decode(qkv, ld, cache_k, cache_v, out, M, hq, hkv, d, pos0, max_len, scale, parents, stream, position);
 }

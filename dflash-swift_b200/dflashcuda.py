@@ -38,6 +38,7 @@ DFLASH_ERR_WORKSPACE = 7
 DEVERR_QMM_PIPELINE = 0x1
 DEVERR_QMM_REDUCE = 0x2
 DEVERR_ALLREDUCE = 0x4
+DEVERR_POSITION = 0x8
 DEVERR_TEST_WAIT = 0x80000000
 
 # Every symbol the header declares; tests check the library exports all of them.
@@ -59,6 +60,8 @@ EXPORTED = (
     # gated-delta layers with shared key heads
     "dflash_gdn_step_grouped", "dflash_gdn_step_tree_grouped", "dflash_gdn_replay_grouped",
     "dflash_stack_gdn_conv_gates_grouped",
+    # attention with a device-resident cache position
+    "dflash_stack_attn_prep_ex", "dflash_stack_attn_decode_ex",
 )
 
 
@@ -133,6 +136,9 @@ def _load() -> ctypes.CDLL:
                                        _i, _i, _i, _vp], _i),
         "dflash_stack_gdn_conv_gates_grouped": ([_vp, _i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i,
                                                  _i, _vp, _vp], _i),
+        "dflash_stack_attn_prep_ex": ([_vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _f, _vp, _vp, _vp],
+                                      _i),
+        "dflash_stack_attn_decode_ex": ([_vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp], _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -509,27 +515,33 @@ def stack_gated_norm(o, z, weight, out, eps: float, stream=None):
 
 
 def stack_attn_prep(qkv, q_norm, k_norm, cache_k, cache_v, hq: int, hkv: int, rot: int, pos0: int, eps: float,
-                    theta: float, stream=None, parents=None):
+                    theta: float, stream=None, parents=None, position=None):
     """qkv rows [q | gate | k | v]; caches [hkv, max_len, d].  parents (device int32 [M]):
-    a tree round, rotary position pos0 + depth."""
+    a tree round, rotary position pos0 + depth.  position (device int32 [1]): pos0 read on
+    the device instead (dflash_stack_attn_prep_ex)."""
     M = qkv.shape[0]
     _, max_len, d = cache_k.shape
     args = (_ptr(qkv), qkv.stride(0), _ptr(q_norm), _ptr(k_norm), _ptr(cache_k), _ptr(cache_v), M, hq, hkv, d, rot,
             pos0, max_len, float(eps), float(theta))
-    if parents is None:
+    if position is not None:
+        check(lib.dflash_stack_attn_prep_ex(*args, _ptr(parents), _ptr(position), _stream(stream)))
+    elif parents is None:
         check(lib.dflash_stack_attn_prep(*args, _stream(stream)))
     else:
         check(lib.dflash_stack_attn_prep_tree(*args, _ptr(parents), _stream(stream)))
 
 
 def stack_attn_decode(qkv, cache_k, cache_v, out, hq: int, hkv: int, pos0: int, scale: float, stream=None,
-                      parents=None):
-    """parents (device int32 [M]): a tree round, each token sees the prefix and its path."""
+                      parents=None, position=None):
+    """parents (device int32 [M]): a tree round, each token sees the prefix and its path.
+    position (device int32 [1]): pos0 read on the device (dflash_stack_attn_decode_ex)."""
     M = qkv.shape[0]
     _, max_len, d = cache_k.shape
     args = (_ptr(qkv), qkv.stride(0), _ptr(cache_k), _ptr(cache_v), _ptr(out), M, hq, hkv, d, pos0, max_len,
             float(scale))
-    if parents is None:
+    if position is not None:
+        check(lib.dflash_stack_attn_decode_ex(*args, _ptr(parents), _ptr(position), _stream(stream)))
+    elif parents is None:
         check(lib.dflash_stack_attn_decode(*args, _stream(stream)))
     else:
         check(lib.dflash_stack_attn_decode_tree(*args, _ptr(parents), _stream(stream)))

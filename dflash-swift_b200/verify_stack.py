@@ -351,15 +351,18 @@ class VerifyStack:
 
     def __init__(self, cfg: StackConfig, rank: int = 0, world: int = 1, seed: int = 0, device=None,
                  group=None, weights: Optional[dict] = None, state: Optional[dict] = None, allreduce: str = "peer",
-                 tree: bool = False):
+                 tree: bool = False, device_position: bool = False):
         import dflashcuda as dc
         self.dc = dc
         self.cfg = cfg
         self.tree = tree
         # tokens already in the attention caches: the block's rows go to cache rows
-        # context .. context + block - 1.  A captured graph keeps the value it was
-        # captured with; advance() moves it for eager rounds (a decode loop).
+        # context .. context + block - 1.  advance() moves it.  A captured graph keeps the
+        # value it was captured with, unless device_position: the attention kernels then
+        # read it from `position` (device int32), which advance() rewrites, so one captured
+        # round serves a whole decode loop.
         self.context = cfg.context
+        self.device_position = device_position
         self.plan = shard_plan(cfg, rank, world)
         self.world = world
         self.pg = group
@@ -419,6 +422,8 @@ class VerifyStack:
         self._sign = torch.full((1,), -(2 ** 63), dtype=torch.int64, device=dev)
         # tree rounds: the block's parent list, read by the tree kernels in stream order so a
         # captured round replays with whatever tree set_tree last wrote (a chain until then)
+        self.position = (torch.tensor([self.context], dtype=torch.int32, device=dev) if self.device_position
+                         else None)
         self.parents = torch.tensor([-1] + list(range(M - 1)), dtype=torch.int32, device=dev) if self.tree else None
         self.tree_plan = None
         if self.tree:  # the drafted token of every row, and the device walk's accepted path
@@ -521,9 +526,11 @@ class VerifyStack:
         cfg, p, dc = self.cfg, self.plan, self.dc
         self._qmm(self.normed, L["qkv"], self.qkv)
         dc.stack_attn_prep(self.qkv, L["q_norm"], L["k_norm"], S["cache_k"], S["cache_v"], p.attn_heads, p.kv_heads,
-                           cfg.rotary_dim, self.context, cfg.eps, cfg.rope_theta, parents=self.parents)
+                           cfg.rotary_dim, self.context, cfg.eps, cfg.rope_theta, parents=self.parents,
+                           position=self.position)
         dc.stack_attn_decode(self.qkv, S["cache_k"], S["cache_v"], self.attn_out, p.attn_heads, p.kv_heads,
-                             self.context, 1.0 / math.sqrt(cfg.head_dim), parents=self.parents)
+                             self.context, 1.0 / math.sqrt(cfg.head_dim), parents=self.parents,
+                             position=self.position)
         return self._qmm_reduced(self.attn_out, L["o_proj"])
 
     def _mlp(self, L):
@@ -652,6 +659,8 @@ class VerifyStack:
         if n < 0 or any(S["cache_k"].shape[1] < self.context + n for S in self.state["layers"] if "cache_k" in S):
             raise ValueError(f"advancing the context by {n} runs past the attention caches")
         self.context += n
+        if self.position is not None:  # stream-ordered after the round that was just read back
+            self.position.fill_(self.context)
 
     def capture(self, hidden_buf, proposals=None):
         """Capture forward(hidden_buf) — or, with proposals, the whole verify round — as a

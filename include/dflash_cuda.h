@@ -44,6 +44,7 @@ enum dflash_status {
 #define DFLASH_DEVERR_QMM_PIPELINE 0x1u   /* qmm TMA pipeline wait timed out */
 #define DFLASH_DEVERR_QMM_REDUCE 0x2u     /* qmm split-K reduction inconsistency */
 #define DFLASH_DEVERR_ALLREDUCE 0x4u      /* peer all-reduce flag wait timed out */
+#define DFLASH_DEVERR_POSITION 0x8u       /* a device-resident cache position left the cache */
 #define DFLASH_DEVERR_TEST_WAIT 0x80000000u /* raised only by dflash_test_bounded_wait */
 
 int dflash_version(void);

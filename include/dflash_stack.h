@@ -81,6 +81,21 @@ int dflash_stack_attn_decode(const dflash_bf16* qkv, int ld, const dflash_bf16* 
                              dflash_bf16* out, int M, int hq, int hkv, int d, int pos0, int max_len, float scale,
                              dflash_stream_t stream);
 
+/* dflash_stack_attn_prep / dflash_stack_attn_decode with both options at once: `parents`
+ * (NULL: a chain round; else a tree round as for the _tree entries, M <= 32) and
+ * `position` (NULL: pos0 as given; else a device int32 holding pos0, read in stream order,
+ * so a CUDA graph of the round replays at whatever position the host last wrote there).
+ * A device position outside 0 .. max_len - M makes the kernel write nothing and raise
+ * DFLASH_DEVERR_POSITION in the device error word. */
+int dflash_stack_attn_prep_ex(dflash_bf16* qkv, int ld, const dflash_bf16* q_norm, const dflash_bf16* k_norm,
+                              dflash_bf16* cache_k, dflash_bf16* cache_v, int M, int hq, int hkv, int d, int rot,
+                              int pos0, int max_len, float eps, float theta, const int32_t* parents,
+                              const int32_t* position, dflash_stream_t stream);
+int dflash_stack_attn_decode_ex(const dflash_bf16* qkv, int ld, const dflash_bf16* cache_k,
+                                const dflash_bf16* cache_v, dflash_bf16* out, int M, int hq, int hkv, int d, int pos0,
+                                int max_len, float scale, const int32_t* parents, const int32_t* position,
+                                dflash_stream_t stream);
+
 /* ------------------------------------------------------------------------------
  * Speculative tree rounds (the target forward run with mtpTreePlanKey,
  * Tests/DFlashKitTests/SpeculativeTreeTests.swift:108-140).  The M block rows carry a

@@ -309,3 +309,15 @@ def test_grouped_key_head_argument_errors(dc):
         FAKE, ld, FAKE, FAKE, FAKE, FAKE, 16, FAKE, FAKE, FAKE, FAKE, M, heads, kh, dk, 4, parents, None)
     assert cg(kh=3) == 1 and cg(ld=100) == 1 and cg(M=33, parents=FAKE) == 1
     assert cg(dk=48, ld=(2 * 4 + 8) * 48) == 2
+
+
+def test_attention_ex_argument_errors(dc):
+    L = dc.lib
+    prep = lambda M=8, pos0=0, parents=None, position=None, d=256: L.dflash_stack_attn_prep_ex(
+        FAKE, 4096, FAKE, FAKE, FAKE, FAKE, M, 4, 2, d, 64, pos0, 64, 1e-6, 1e4, parents, position, None)
+    assert prep(pos0=60) == 1                       # host position past the cache
+    assert prep(M=33, parents=FAKE) == 1            # a tree has at most 32 rows
+    assert prep(d=96, position=FAKE) == 2
+    dec = lambda M=8, pos0=0, parents=None, position=None, hq=4: L.dflash_stack_attn_decode_ex(
+        FAKE, 4096, FAKE, FAKE, FAKE, M, hq, 2, 256, pos0, 64, 0.1, parents, position, None)
+    assert dec(pos0=57) == 1 and dec(M=33, parents=FAKE) == 1 and dec(hq=3, position=FAKE) == 1
