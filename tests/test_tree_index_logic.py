@@ -7,7 +7,10 @@ path rows and owned rows (gdn_kernel<CH, true>, csrc/gdn.cu), each conv tap's so
 This file transcribes that logic line for line and checks it against the host plan
 (dflash-swift_b200/tree.py) on random trees of 1..32 rows: the blocks' paths are the plan's
 paths, every row is written by exactly one block, the taps are the last kc inputs of the
-row's history, the walk accepts the plan's rows.  It also checks that the grouped conv
+row's history, the walk accepts the plan's rows; and that the decode kernel's split online
+softmax with hidden keys at -inf (a finite exponent base while a range has seen no visible
+key, weight 0 for a range that never does) is the softmax over the visible keys.  It also
+checks that the grouped conv
 kernel's channel and output maps tile [0, C) and the output exactly.  The GPU tests check
 the kernels themselves; this pins the algorithm they implement.
 """
@@ -15,6 +18,8 @@ from __future__ import annotations
 
 import itertools
 import random
+
+import numpy as np
 
 from tree import SpeculativeTreePlan, accepted_path
 
@@ -176,3 +181,56 @@ def test_grouped_conv_maps_tile_channels_and_output():
         # value head h reads key head h // g in the recurrence kernel
         for h in range(H):
             assert h // (H // Hk) < Hk
+
+
+def decode_split_softmax(scores, values, visible_mask, pos0, t, split=4, chunk=256):
+    """attn_decode_kernel (csrc/stack.cu) for one token and head: the keys 0 .. pos0 + t cut
+    into `split` CTA ranges, an online softmax per range in chunks with hidden keys at -inf
+    and a finite exponent base while no key is visible, then the merge of the ranges'
+    (max, sum, p V) with weight 0 for a range whose max stayed -inf."""
+    n = pos0 + t + 1
+    parts = []
+    for rank in range(split):
+        k0, k1 = n * rank // split, n * (rank + 1) // split
+        m, l, acc = -np.inf, 0.0, np.zeros(values.shape[1])
+        for c0 in range(k0, k1, chunk):
+            j = np.arange(c0, min(k1, c0 + chunk))
+            b = j - pos0
+            s = np.where((b >= 0) & ~visible_mask[np.clip(b, 0, None)] if visible_mask is not None else False,
+                         -np.inf, scores[j])
+            mnew = max(m, s.max())
+            base = 0.0 if mnew == -np.inf else mnew
+            p = np.exp(s - base)
+            corr = np.exp(m - base)
+            l = l * corr + p.sum()
+            acc = acc * corr + p @ values[j]
+            m = mnew
+        parts.append((m, l, acc))
+    mx = max(m for m, _, _ in parts)
+    f = [0.0 if m == -np.inf else np.exp(m - mx) for m, _, _ in parts]
+    den = sum(fr * l for fr, (_, l, _) in zip(f, parts))
+    return sum(fr * acc for fr, (_, _, acc) in zip(f, parts)) / den
+
+
+def test_decode_masking_and_merge_are_the_masked_softmax():
+    """Including ranges whose keys are all hidden (a row deep in the block, pos0 = 0)."""
+    rng = np.random.default_rng(3)
+    for _ in range(300):
+        M = int(rng.integers(1, 17))
+        par = [-1] + [int(rng.integers(0, r)) for r in range(1, M)]
+        pos0 = int(rng.choice([0, 1, 5, 300, 700]))
+        n_keys = pos0 + M
+        scores_all = rng.standard_normal(n_keys) * 3
+        values = rng.standard_normal((n_keys, 4))
+        for t in range(M):
+            path, _ = tree_walk(par, t)
+            visible = np.array([(path >> b) & 1 == 1 for b in range(M)])
+            got = decode_split_softmax(scores_all, values, visible, pos0, t)
+            keys = list(range(pos0)) + [pos0 + a for a in range(M) if visible[a]]
+            w = np.exp(scores_all[keys] - scores_all[keys].max())
+            want = (w / w.sum()) @ values[keys]
+            assert np.allclose(got, want, rtol=1e-10, atol=1e-12), (par, pos0, t)
+            chain = decode_split_softmax(scores_all, values, None, pos0, t)
+            keys = list(range(pos0 + t + 1))
+            w = np.exp(scores_all[keys] - scores_all[keys].max())
+            assert np.allclose(chain, (w / w.sum()) @ values[keys], rtol=1e-10, atol=1e-12)
