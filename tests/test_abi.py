@@ -321,3 +321,19 @@ def test_attention_ex_argument_errors(dc):
     dec = lambda M=8, pos0=0, parents=None, position=None, hq=4: L.dflash_stack_attn_decode_ex(
         FAKE, 4096, FAKE, FAKE, FAKE, M, hq, 2, 256, pos0, 64, 0.1, parents, position, None)
     assert dec(pos0=57) == 1 and dec(M=33, parents=FAKE) == 1 and dec(hq=3, position=FAKE) == 1
+
+
+def test_no_cpu_path_anywhere(tmp_path):
+    """The product fails loudly without the CUDA library or a CUDA device: the binding
+    refuses to import when libdflashcuda.so is missing, and the verify stack refuses a
+    CPU device (there is no CPU fallback to run instead)."""
+    import subprocess
+    import sys
+    code = ("import os, sys; os.environ['DFLASH_CUDA_LIB'] = sys.argv[1]; sys.path.insert(0, sys.argv[2])\n"
+            "try:\n    import dflashcuda\nexcept ImportError as e:\n    print('refused:', e)\n")
+    r = subprocess.run([sys.executable, "-c", code, str(tmp_path / "missing.so"), str(ROOT / "dflash-swift_b200")],
+                       capture_output=True, text=True, timeout=120)
+    assert "refused:" in r.stdout and "no CPU fallback" in r.stdout
+    import verify_stack as vs
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        vs.VerifyStack(vs.TINY, device="cpu")
