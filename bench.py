@@ -243,6 +243,13 @@ def run_ours(args):
     ms1, _ = timed(1, args.steps, args.warmup)
     us8 = ms8 * 1e3 / args.steps
     us1 = ms1 * 1e3 / args.steps
+    m_sweep = None
+    if world == 1:  # BASELINE config 2 asks for every M in 1..8 (M = 1 and 8 timed above)
+        sweep_steps = max(200, min(args.steps, 4000))
+        m_sweep = {}
+        for m in range(1, 9):
+            us = us1 if m == 1 else us8 if m == M else timed(m, sweep_steps, args.warmup)[0] * 1e3 / sweep_steps
+            m_sweep[m] = {"us": round(us, 3), "GBs": round(algorithmic_bytes(m) / (us * 1e-6) / 1e9, 1)}
     bytes8 = algorithmic_bytes(M)
     per_gpu_gbs = bytes8 / (us8 * 1e-6) / 1e9
     value = world * per_gpu_gbs
@@ -273,12 +280,16 @@ def run_ours(args):
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_baseline(O, x[:M], wq, s, b, budget_s=args.cpu_seconds)
-    gdn = None
+    gdn = fmt = None
     if world == 1:
         try:
             gdn = gdn_replay_config5(dc, dev, peak)
         except Exception as exc:  # a side measurement: never costs the main line
             gdn = {"error": repr(exc)[:300]}
+        try:
+            fmt = format_sweep_config3(dc, dev)
+        except Exception as exc:  # a side measurement: never costs the main line
+            fmt = {"error": repr(exc)[:300]}
 
     if rank == 0:
         line = {
@@ -295,6 +306,8 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "e2e": e2e_line(e2e, e2e_host, world, bytes8, args.steps),
             "gpu_launches": KERNELS_PER_CALL * args.steps,
+            "m_sweep_config2": m_sweep,
+            "format_sweep_config3": fmt,
             "gdn_replay_config5": gdn,
             "clocks": clocks,
             "parity_closeness_before_timing": err,
@@ -342,6 +355,58 @@ def gdn_replay_config5(dc, dev, peak, reps=20):
     return {"us": round(us, 2), "GBs": round(gbs, 1), "algorithmic_bytes": nbytes, "frac_of_peak": round(gbs / peak, 4),
             "device_error": dc.device_error(), "workload": "48 layers x 32 heads x 128 x 128 fp32, keep 8 of 8",
             "l2": "replays alternate over two snapshot/state pairs (403 MB)"}
+
+
+def format_sweep_config3(dc, dev, steps=2000):
+    """BASELINE config 3 beside the main line: down-proj (K=17408, N=5120) and attention-out
+    (K=6144, N=5120) at bits 4 and 8, groups 32, 64 and 128, M = 1, 4 and 8.  Per
+    (shape, format) seeded random packed weights (the time does not depend on the values),
+    in enough distinct copies that a CUDA graph rotating through them never finds a copy in
+    L2; `steps` launches timed with CUDA events per point.  Reported: us per call and GB/s
+    of algorithmic bytes."""
+    import torch
+    import verify_stack as vs
+    out = {}
+    stream = torch.cuda.Stream(dev)
+    gen = torch.Generator(device=dev).manual_seed(3)
+    for (n, k, name) in ((5120, 17408, "down"), (5120, 6144, "attn_out")):
+        x = torch.randn(8, k, generator=gen, device=dev).to(torch.bfloat16)
+        y = torch.empty(8, n, dtype=torch.bfloat16, device=dev)
+        for bits in (4, 8):
+            for group in (32, 64, 128):
+                q0 = vs.random_quant(gen, n, k, group, bits, dev)
+                copies = [q0] + [vs.Quant(q0.w.clone(), q0.scales.clone(), q0.biases.clone(), group, bits)
+                                 for _ in range(max(1, -(-4 * L2_BYTES // q0.nbytes())))]
+                ws = dc.Workspace(dc.qmm_workspace_bytes(8, n, k, group, bits), dev)
+                for m in (1, 4, 8):
+                    with torch.cuda.stream(stream):
+                        dc.qmm(x[:m], q0.w, q0.scales, q0.biases, group, bits, out=y[:m], workspace=ws,
+                               stream=stream)
+                    stream.synchronize()
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=stream):
+                        for q in copies:
+                            dc.qmm(x[:m], q.w, q.scales, q.biases, group, bits, out=y[:m], workspace=ws,
+                                   stream=stream)
+                    reps = max(1, steps // len(copies))
+                    with torch.cuda.stream(stream):
+                        for _ in range(3):
+                            g.replay()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    with torch.cuda.stream(stream):
+                        for _ in range(reps):
+                            g.replay()
+                    e1.record(stream)
+                    stream.synchronize()
+                    us = e0.elapsed_time(e1) * 1e3 / (reps * len(copies))
+                    nbytes = algorithmic_bytes(m, n=n, k=k, group=group, bits=bits)
+                    out[f"{name}_b{bits}_g{group}_m{m}"] = {"us": round(us, 3),
+                                                            "GBs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+                    del g
+                del copies, q0, ws
+                torch.cuda.empty_cache()
+    return out
 
 
 def gpu_ids(world):
