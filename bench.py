@@ -280,7 +280,7 @@ def run_ours(args):
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_baseline(O, x[:M], wq, s, b, budget_s=args.cpu_seconds)
-    gdn = fmt = None
+    gdn = fmt = stack4 = None
     if world == 1:
         try:
             gdn = gdn_replay_config5(dc, dev, peak)
@@ -290,6 +290,10 @@ def run_ours(args):
             fmt = format_sweep_config3(dc, dev)
         except Exception as exc:  # a side measurement: never costs the main line
             fmt = {"error": repr(exc)[:300]}
+        try:
+            stack4 = verify_stack_config4(dev)
+        except Exception as exc:  # a side measurement: never costs the main line
+            stack4 = {"error": repr(exc)[:300]}
 
     if rank == 0:
         line = {
@@ -309,6 +313,7 @@ def run_ours(args):
             "m_sweep_config2": m_sweep,
             "format_sweep_config3": fmt,
             "gdn_replay_config5": gdn,
+            "verify_stack_config4_tp1": stack4,
             "clocks": clocks,
             "parity_closeness_before_timing": err,
         }
@@ -355,6 +360,48 @@ def gdn_replay_config5(dc, dev, peak, reps=20):
     return {"us": round(us, 2), "GBs": round(gbs, 1), "algorithmic_bytes": nbytes, "frac_of_peak": round(gbs / peak, 4),
             "device_error": dc.device_error(), "workload": "48 layers x 32 heads x 128 x 128 fp32, keep 8 of 8",
             "l2": "replays alternate over two snapshot/state pairs (403 MB)"}
+
+
+def verify_stack_config4(dev, steps=20, warmup=3):
+    """BASELINE config 4 at TP = 1 beside the main line: the 64-layer verify forward of an
+    8-row block (48 gated-delta + 16 attention layers, hidden 5120, MLP 17408, 4-bit g64
+    seeded random weights, 1024 cached tokens) and the whole verify round (forward, the
+    248,320-row LM head with its argmax, the accept), each replayed from a CUDA graph and
+    timed with CUDA events.  The tensor-parallel runs (TP 2 / 4 / 8) use
+    dflash-swift_b200/verify_stack.py under torchrun."""
+    import torch
+    import verify_stack as vs
+    cfg = vs.CONFIG4
+    stack = vs.VerifyStack(cfg, 0, 1, seed=0, device=dev)
+    hidden = vs.make_block(cfg, 0, dev)
+    proposals = torch.zeros(cfg.block - 1, dtype=torch.int32, device=dev)
+
+    def timed(g):
+        for _ in range(warmup):
+            g.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) * 1e3 / steps
+
+    g = stack.capture(hidden)
+    fwd = timed(g)
+    del g
+    g = stack.capture(hidden, proposals)
+    rnd = timed(g)
+    del g
+    stack.graph = None
+    wbytes = vs.weight_bytes(stack.w)
+    out = {"forward_us": round(fwd, 1), "round_us": round(rnd, 1), "tokens_per_s": round(cfg.block / (fwd * 1e-6), 1),
+           "weight_bytes": wbytes, "weight_GBs": round(wbytes / (fwd * 1e-6) / 1e9, 1),
+           "kernels_per_forward": stack.kernels_per_forward(), "steps": steps}
+    del stack
+    torch.cuda.empty_cache()
+    return out
 
 
 def format_sweep_config3(dc, dev, steps=2000):
