@@ -404,55 +404,65 @@ def verify_stack_config4(dev, steps=20, warmup=3):
     return out
 
 
+def _qmm_copies(dev, gen, n, k, group, bits):
+    """Seeded random packed weights (the time does not depend on the values) in enough
+    distinct copies that a CUDA graph rotating through them never finds one in L2."""
+    import verify_stack as vs
+    q0 = vs.random_quant(gen, n, k, group, bits, dev)
+    return [q0] + [vs.Quant(q0.w.clone(), q0.scales.clone(), q0.biases.clone(), group, bits)
+                   for _ in range(max(1, -(-4 * L2_BYTES // q0.nbytes())))]
+
+
+def _time_qmm(dc, dev, stream, copies, x, y, ws, m, steps):
+    """us per dflash_qmm call at M = m: a CUDA graph of one launch per copy, replayed to
+    cover about `steps` launches after 3 warm-up replays, timed with CUDA events."""
+    import torch
+    q0 = copies[0]
+    with torch.cuda.stream(stream):
+        dc.qmm(x[:m], q0.w, q0.scales, q0.biases, q0.group, q0.bits, out=y[:m], workspace=ws, stream=stream)
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for q in copies:
+            dc.qmm(x[:m], q.w, q.scales, q.biases, q.group, q.bits, out=y[:m], workspace=ws, stream=stream)
+    reps = max(1, steps // len(copies))
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            g.replay()
+    e1.record(stream)
+    stream.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / (reps * len(copies))
+
+
 def format_sweep_config3(dc, dev, steps=2000):
     """BASELINE config 3 beside the main line: down-proj (K=17408, N=5120) and attention-out
-    (K=6144, N=5120) at bits 4 and 8, groups 32, 64 and 128, M = 1, 4 and 8.  Per
-    (shape, format) seeded random packed weights (the time does not depend on the values),
-    in enough distinct copies that a CUDA graph rotating through them never finds a copy in
-    L2; `steps` launches timed with CUDA events per point.  Reported: us per call and GB/s
-    of algorithmic bytes."""
+    (K=6144, N=5120) at bits 4 and 8, groups 32, 64 and 128, M = 1, 4 and 8; and config 1's
+    shape (K=4096, N=4096, 4-bit g64, M=8) on the GPU.  `steps` timed launches per point;
+    reported as us per call and GB/s of algorithmic bytes."""
     import torch
-    import verify_stack as vs
     out = {}
     stream = torch.cuda.Stream(dev)
     gen = torch.Generator(device=dev).manual_seed(3)
-    for (n, k, name) in ((5120, 17408, "down"), (5120, 6144, "attn_out")):
+    points = [(5120, 17408, "down", bits, group, (1, 4, 8)) for bits in (4, 8) for group in (32, 64, 128)]
+    points += [(5120, 6144, "attn_out", bits, group, (1, 4, 8)) for bits in (4, 8) for group in (32, 64, 128)]
+    points += [(4096, 4096, "config1", 4, 64, (8,))]
+    for (n, k, name, bits, group, ms) in points:
         x = torch.randn(8, k, generator=gen, device=dev).to(torch.bfloat16)
         y = torch.empty(8, n, dtype=torch.bfloat16, device=dev)
-        for bits in (4, 8):
-            for group in (32, 64, 128):
-                q0 = vs.random_quant(gen, n, k, group, bits, dev)
-                copies = [q0] + [vs.Quant(q0.w.clone(), q0.scales.clone(), q0.biases.clone(), group, bits)
-                                 for _ in range(max(1, -(-4 * L2_BYTES // q0.nbytes())))]
-                ws = dc.Workspace(dc.qmm_workspace_bytes(8, n, k, group, bits), dev)
-                for m in (1, 4, 8):
-                    with torch.cuda.stream(stream):
-                        dc.qmm(x[:m], q0.w, q0.scales, q0.biases, group, bits, out=y[:m], workspace=ws,
-                               stream=stream)
-                    stream.synchronize()
-                    g = torch.cuda.CUDAGraph()
-                    with torch.cuda.graph(g, stream=stream):
-                        for q in copies:
-                            dc.qmm(x[:m], q.w, q.scales, q.biases, group, bits, out=y[:m], workspace=ws,
-                                   stream=stream)
-                    reps = max(1, steps // len(copies))
-                    with torch.cuda.stream(stream):
-                        for _ in range(3):
-                            g.replay()
-                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    e0.record(stream)
-                    with torch.cuda.stream(stream):
-                        for _ in range(reps):
-                            g.replay()
-                    e1.record(stream)
-                    stream.synchronize()
-                    us = e0.elapsed_time(e1) * 1e3 / (reps * len(copies))
-                    nbytes = algorithmic_bytes(m, n=n, k=k, group=group, bits=bits)
-                    out[f"{name}_b{bits}_g{group}_m{m}"] = {"us": round(us, 3),
-                                                            "GBs": round(nbytes / (us * 1e-6) / 1e9, 1)}
-                    del g
-                del copies, q0, ws
-                torch.cuda.empty_cache()
+        copies = _qmm_copies(dev, gen, n, k, group, bits)
+        ws = dc.Workspace(dc.qmm_workspace_bytes(8, n, k, group, bits), dev)
+        for m in ms:
+            us = _time_qmm(dc, dev, stream, copies, x, y, ws, m, steps)
+            nbytes = algorithmic_bytes(m, n=n, k=k, group=group, bits=bits)
+            out[f"{name}_b{bits}_g{group}_m{m}"] = {"us": round(us, 3), "GBs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+        del copies, ws
+        torch.cuda.empty_cache()
     return out
 
 
