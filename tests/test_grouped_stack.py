@@ -5,7 +5,7 @@ Value head h reads key head h / (H / Hk).  CPU: the stack reference on the group
 equals, bit for bit, the reference on the ungrouped model whose q and k rows (in_proj, conv
 weights, conv window) are the key heads' repeated per value head; the shard plan tiles
 the grouped in_proj; two gloo ranks match one; a grouped checkpoint loads back to the
-same shards.  GPU (not yet run on a B200): the CUDA stack against the reference."""
+same shards.  GPU: the CUDA stack against the reference."""
 from __future__ import annotations
 
 import sys
