@@ -27,7 +27,10 @@ def pytest_configure(config):
 
 
 def pytest_collection_modifyitems(session, config, items):
-    items.sort(key=lambda item: item.get_closest_marker("unconfirmed") is not None)  # stable: order kept otherwise
+    # stable sort, order kept otherwise: unconfirmed tests after the confirmed ones, and the
+    # allocation-free entry point's file after everything
+    items.sort(key=lambda item: (item.fspath.basename == "test_zz_no_alloc.py",
+                                 item.get_closest_marker("unconfirmed") is not None))
 
 
 def _ensure_built():

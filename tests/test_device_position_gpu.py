@@ -13,7 +13,7 @@ import torch
 
 import verify_stack as vs
 
-pytestmark = [pytest.mark.gpu, pytest.mark.unconfirmed]
+pytestmark = pytest.mark.gpu
 
 
 def test_one_graph_serves_a_decode_loop(cuda):

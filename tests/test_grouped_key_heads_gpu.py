@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu, pytest.mark.unconfirmed]
+pytestmark = pytest.mark.gpu
 
 
 def _repeat_heads(t, group, axis):

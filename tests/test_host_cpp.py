@@ -54,7 +54,6 @@ def test_host_cpp_cpu_cases():
 
 
 @pytest.mark.gpu
-@pytest.mark.unconfirmed
 def test_host_cpp_gpu_cases(cuda):
     r = _run("gpu")
     print(r.stdout, r.stderr)

@@ -8,7 +8,6 @@ import torch
 
 import verify_stack as vs
 
-pytestmark = pytest.mark.unconfirmed
 
 
 @pytest.mark.gpu

@@ -168,7 +168,6 @@ def test_greedy_sequence_is_not_constant(greedy):
 # ----------------------------------------------------------------------------- CUDA stack (GPU)
 
 @pytest.mark.gpu
-@pytest.mark.unconfirmed
 def test_cuda_stack_speculative_rounds_emit_its_greedy_sequence(cuda):
     """The same control on the CUDA stack: greedy is a one-row stack committing every
     token; chain rounds and tree rounds run on eight-row stacks with the drafts built as

@@ -30,7 +30,6 @@ sys.path.insert(0, str(Path(__file__).resolve().parent))
 import verify_stack as vs  # noqa: E402
 from tree import SpeculativeTreePlan  # noqa: E402
 
-pytestmark = pytest.mark.unconfirmed
 
 # 8-row trees (TINY's block): branching at the anchor and below, a deep chain, a star.
 TREES = {

@@ -3,9 +3,8 @@
 Such callers (code recorded inside a CUDA graph someone else captures, plugin hosts
 that forbid touching the allocator, latency-critical loops) get the same result as
 dflash_qmm with a caller-owned workspace; the scratch is the library's static device
-array instead.  This file is collected after the other confirmed tests (only tests
-marked `unconfirmed` follow it), so a run stopping at its first failure has already run
-them; it also passes on its own in a fresh process.
+array instead.  This file is collected after every other test, so a run stopping at its
+first failure has already run them; it also passes on its own in a fresh process.
 """
 from __future__ import annotations
 
