@@ -43,6 +43,7 @@ FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 1024 * 1024
 PROFILE_SUMMARY = ROOT / "profiles" / "qmm_m8_k5120_n17408_4b_g64.json"
 KERNELS_PER_CALL = 2  # prep (x packets: fp16 fragment order + segment sums), main (weight stream)
+WARM_LAUNCHES = 2000  # untimed launches before each timed region (~35 ms of device work)
 
 
 def algorithmic_bytes(m: int, n: int = N, k: int = K, group: int = GROUP, bits: int = BITS) -> int:
@@ -149,8 +150,10 @@ def weight_copies(dev, wq, s, b):
 
 
 def time_graph(dc, dev, x_d, copies, y_d, ws, steps, warmup, m):
-    """Capture one launch per weight copy into a CUDA graph; replay to cover exactly
-    `warmup` then `steps` launches; return elapsed ms of the timed launches."""
+    """Capture one launch per weight copy into a CUDA graph (plus a graph of the remainder
+    launches) so that the timed replays cover exactly `steps` launches. Every graph that the
+    timed region replays is replayed untimed first (its upload and first-launch cost stay
+    outside the timing), and at least `warmup` launches run before the timed region."""
     import torch
     stream = torch.cuda.Stream(dev)
     R = len(copies)
@@ -171,13 +174,13 @@ def time_graph(dc, dev, x_d, copies, y_d, ws, steps, warmup, m):
     full = capture(R)
     rest_n = steps % R
     rest = capture(rest_n) if rest_n else None
-    warm_full, warm_rest = divmod(warmup, R)
-    warm_rest_g = capture(warm_rest) if warm_rest else None
+    # at least `warmup` launches, and at least WARM_LAUNCHES, so that the GPU left idle by
+    # the host-side set-up before this call is back at its working clocks when timing starts
     with torch.cuda.stream(stream):
-        for _ in range(warm_full):
+        for _ in range(max(1, -(-max(warmup, WARM_LAUNCHES) // R))):
             full.replay()
-        if warm_rest_g is not None:
-            warm_rest_g.replay()
+        if rest is not None:
+            rest.replay()
     stream.synchronize()
     return stream, full, rest, steps // R
 
