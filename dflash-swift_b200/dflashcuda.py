@@ -252,7 +252,8 @@ def qmm_host(x_host, w, scales, biases, group_size: int, bits: int, out_host=Non
 def qmm_noalloc(x, w, scales, biases, group_size: int, bits: int, out=None, stream=None):
     """dflash_qmm without a workspace argument, for callers that may not allocate
     device memory: the library's own static device scratch is used instead (shapes up
-    to its 8 MiB limit; calls that overlap on the GPU must not share a device)."""
+    to its 8 MiB limit).  Calls on one device share the scratch: keep them ordered on
+    one stream, or use qmm with one workspace per stream."""
     import torch
     M, K = x.shape
     N = w.shape[0]

@@ -104,7 +104,8 @@ int dflash_qmm(const dflash_bf16* x, const uint32_t* w, const dflash_bf16* scale
  *     DFLASH_ERR_UNSUPPORTED (at M = 16 and group 32 that is K above about 209000;
  *     dflash_qmm with a larger workspace covers those).
  *   - The first call on a device resolves the array's device address; make that first
- *     call outside any stream capture.
+ *     call outside any stream capture.  A later call in a new context on that device
+ *     (after cudaDeviceReset) resolves it again, so it too belongs outside a capture.
  *   - Every call on a device shares the array: calls that can overlap on the GPU
  *     (different streams without ordering between them) race and corrupt each other's
  *     results.  Keep such calls on one stream, or use dflash_qmm with one workspace per
