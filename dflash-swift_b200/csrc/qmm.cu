@@ -42,9 +42,15 @@
 // the packet, so the MMA leaves exactly sum_k q x' and the combine is two FMAs per
 // output: acc += s tmp + b xs.  For 8-bit codes the high nibble over 1024.0 reads
 // 1024 + 16 q_hi, so both MMAs use the same x and z = 2048 sum x'.  x enters fp16 as
-// x' = x / f with f a power of two per segment that keeps |x'| < 2^15 (exact: bf16
-// values fit fp16's significand); f is 1 unless |x| >= 32768, and only then does the
-// combine multiply by f.  Within a lane's words the k order is permuted identically
+// x' = x / f with f a power of two per segment.  f is 1 for a segment whose largest |x|
+// lies in [2^-6, 2^15), and only otherwise does the combine multiply by f: larger
+// segments are scaled down below fp16's overflow, smaller ones up so that their largest
+// value lands in [2^14, 2^15).  bf16's 8-bit significand fits fp16's 11 bits, so a value
+// converts exactly when it lies within fp16's normal range (2^-14 upward) after the
+// scaling, i.e. within 14 + 6 = 20 binades of its segment's largest value in the worst
+// case; values further below become fp16 subnormals and lose low bits (below 2^-24 they
+// become zero), which moves the output by far less than its bf16 rounding.  Within a
+// lane's words the k order is permuted identically
 // for weights and x (a sum does not depend on k order), so weights are consumed exactly
 // as MLX packs them.
 #include "common.cuh"
@@ -307,8 +313,10 @@ __global__ void __launch_bounds__(kPrepThreads) qmm_prep_kernel(const uint16_t* 
 #pragma unroll
     for (int o = 1; o < SL; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     float f = 1.f, inv = 1.f;
-    if (amax >= 32768.f) {  // false for NaN: NaN inputs propagate unscaled
-        const int e = ((__float_as_int(amax) >> 23) & 0xff) - 127;  // floor(log2 amax); 128 for inf
+    // false for NaN (NaN inputs propagate unscaled), and for segments whose largest value is
+    // below 2^-100 (zero, or too small to register in any output: left to flush)
+    if (amax >= 32768.f || (amax < 0x1p-6f && amax >= 0x1p-100f)) {
+        const int e = ((__float_as_int(amax) >> 23) & 0xff) - 127;  // floor(log2 amax) in [-100, 128]
         const int sh = e - 14;                                      // amax / 2^sh in [2^14, 2^15)
         f = __int_as_float((127 + sh) << 23);
         inv = __int_as_float((127 - sh) << 23);
@@ -1635,20 +1643,42 @@ namespace qmm {
 constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB per device
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 
-// Device address of g_static_scratch on the current device, resolved once per device.
+// The calling thread's current CUDA context (driver API, resolved at run time like the
+// tensor-map encoder), or null when none is current yet.
+void* current_context() {
+    using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+    static CtxGetCurrentFn fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        const cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q);
+        return (e == cudaSuccess && q == cudaDriverEntryPointSuccess) ? reinterpret_cast<CtxGetCurrentFn>(f)
+                                                                      : nullptr;
+    }();
+    CUcontext c = nullptr;
+    if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+    return c;
+}
+
+// Device address of g_static_scratch on the current device.  Resolved on a device's first
+// call and cached together with the context it was resolved in; a different context on
+// that device (after cudaDeviceReset, the module is loaded again at a new address)
+// resolves it again, so a cached address never outlives its context.
 int static_scratch(void** out) {
     static std::mutex mu;
     static void* ptr[64] = {nullptr};
+    static void* ctx[64] = {nullptr};
     int dev = 0;
     DFLASH_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(DFLASH_ERR_UNSUPPORTED, "device ordinal %d above 63", dev);
     std::lock_guard<std::mutex> lock(mu);
-    if (!ptr[dev]) {
+    void* now = current_context();
+    if (!ptr[dev] || !now || now != ctx[dev]) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
         if (e != cudaSuccess)
             return fail(DFLASH_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
         ptr[dev] = p;
+        ctx[dev] = current_context();  // current now: the lookup above made the device's context current
     }
     *out = ptr[dev];
     return DFLASH_OK;

@@ -213,7 +213,6 @@ def test_workspace_shared_across_shapes(dc, O, cuda):
         assert O.closeness(y[:, r], O.qmm_f64(x, wq[r], s[r], b[r], 64, 4)) <= TIGHT
 
 
-@pytest.mark.unconfirmed  # its bias add now runs dflash_bias_add
 def test_small_m_quantized_linear_with_bias_and_wide_input(dc, O, cuda):
     """The layer flattens leading dims, runs 16-row passes, adds the bias
     (SmallMQuantizedMatmul.swift:254-292)."""
@@ -228,6 +227,42 @@ def test_small_m_quantized_linear_with_bias_and_wide_input(dc, O, cuda):
     assert y.shape == (2, 20, N) and y.dtype == torch.bfloat16
     ref = O.qmm_f64(x, wq, s, b, 64, 4) + O.bits_to_f32(bias)[None, :]
     assert O.closeness(yf(y).reshape(40, N), ref) <= TIGHT
+
+
+def _wide_range_x(O, M, K, lo_exp, hi_exp, seed):
+    """bf16 x with log-uniform magnitudes in [2^lo_exp, 2^hi_exp] and random signs, so that
+    every 64-wide segment of a row mixes values tens of binades apart."""
+    r = np.random.Generator(np.random.PCG64(seed))
+    mag = np.exp2(r.uniform(lo_exp, hi_exp, (M, K))).astype(np.float32)
+    return O.bf16_bits(np.where(r.random((M, K)) < 0.5, -mag, mag))
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_activations_spanning_forty_five_binades(dc, O, cuda, bits):
+    """x from 2^-30 to 2^15 inside every segment: values far below a segment's largest one
+    lose bits in the fp16 operands, but what they lose is far below the output's bf16
+    rounding, so the bar holds."""
+    x = _wide_range_x(O, 8, 2048, -30, 15, seed=41)
+    _, wq, s, b = O.make_qmm_case(8, 1024, 2048, 64, bits, seed_w=42)
+    y = yf(run(dc, cuda, x, wq, s, b, 64, bits))
+    assert O.closeness(y, O.qmm_f64(x, wq, s, b, 64, bits)) <= TOL
+
+
+@pytest.mark.parametrize("scale_exp", [-40, -20, -12, 16])
+def test_rows_of_tiny_or_huge_activations_keep_relative_accuracy(dc, O, cuda, scale_exp):
+    """Rows 0-3 of x are N(0,1) scaled by 2^scale_exp, rows 4-7 plain N(0,1).  Each row is
+    held to the bar relative to ITS OWN largest output: a row of values that fp16 can only
+    hold as subnormals (2^-20) or not at all (2^-40), or that overflow fp16 (2^16), is
+    computed as accurately as a plain one."""
+    x = O.make_x(8, 2048, seed_x=43)
+    xf = O.bits_to_f32(x).reshape(8, 2048).copy()
+    xf[:4] *= np.float32(2.0 ** scale_exp)
+    x = O.bf16_bits(xf)
+    _, wq, s, b = O.make_qmm_case(8, 1536, 2048, 64, 4, seed_w=44)
+    y = yf(run(dc, cuda, x, wq, s, b, 64, 4))
+    ref = O.qmm_f64(x, wq, s, b, 64, 4)
+    for m in range(8):
+        assert np.max(np.abs(y[m] - ref[m])) <= TOL * np.max(np.abs(ref[m])), m
 
 
 def test_bounded_wait_hook_leaves_context_usable(dc, O, cuda):
