@@ -12,6 +12,9 @@ bracketed by a barrier and device synchronisation; the time is the max over rank
 
 Multi-GPU (torchrun, one rank per GPU): every rank runs its own copy of the workload
 (the path shards with no collective), so scaling is weak and `value` is the job total.
+Beside that line, a job of N > 1 GPUs runs BASELINE config 4 tensor-parallel over its N
+GPUs (`verify_stack_config4_tp<N>`: a TP = N vs TP = 1 correctness gate, then the
+64-layer verify forward and round timed from CUDA graphs, max over ranks).
 
 --impl reference times this project's CPU restatement of the reference arithmetic
 (oracle/qmm_oracle.c) on the host cores: the reference's own path is Metal/MLX and
@@ -224,6 +227,11 @@ def run_ours(args):
         torch.cuda.synchronize()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
+        # An untimed replay queued ahead of the start event keeps the GPU busy while the host
+        # enqueues the timed replays, so the graph-launch latency of the host does not land
+        # inside the timed region (it would after the idle synchronize above).
+        with torch.cuda.stream(stream):
+            full.replay()
         t0.record(stream)
         with torch.cuda.stream(stream):
             for _ in range(reps):
@@ -286,7 +294,12 @@ def run_ours(args):
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_baseline(O, x[:M], wq, s, b, budget_s=args.cpu_seconds)
-    gdn = fmt = stack4 = None
+    gdn = fmt = stack4 = stack_tp = None
+    if world > 1:  # the tensor-parallel verify stack over the job's GPUs (collectives on every rank)
+        try:
+            stack_tp = verify_stack_tp(dev, world, rank)
+        except Exception as exc:
+            stack_tp = {"error": repr(exc)[:300]}
     if world == 1:
         try:
             gdn = gdn_replay_config5(dc, dev, peak)
@@ -320,6 +333,7 @@ def run_ours(args):
             "format_sweep_config3": fmt,
             "gdn_replay_config5": gdn,
             "verify_stack_config4_tp1": stack4,
+            f"verify_stack_config4_tp{world}" if world > 1 else "verify_stack_config4_tpN": stack_tp,
             "clocks": clocks,
             "parity_closeness_before_timing": err,
         }
@@ -408,6 +422,84 @@ def verify_stack_config4(dev, steps=20, warmup=3):
     del stack
     torch.cuda.empty_cache()
     return out
+
+
+def verify_stack_tp(dev, world, rank, steps=20, warmup=5):
+    """BASELINE config 4 tensor-parallel over the job's N GPUs (N > 1), beside the qmm line.
+
+    First a correctness gate on the same GPUs: verify_stack.TP_CHECK (a small stack that
+    shards over 2, 4 and 8 ranks) run at TP = N, its output compared on every rank with the
+    same stack run at TP = 1 on that rank's GPU (max|d| / max(max|ref|, 1) <= 3e-2, the
+    multi-rank stack tests' bar); a mismatch on any rank fails the entry.  Then the 64-layer
+    config-4 verify forward and whole verify round at TP = N, each from a CUDA graph, timed
+    with CUDA events and taken as the max over ranks, with the clocks sampled meanwhile.
+    Every rank takes the same collective steps in the same order."""
+    import torch
+    import torch.distributed as dist
+    import verify_stack as vs
+
+    def max_over_ranks(v: float) -> float:
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    cfg = vs.TP_CHECK
+    one = vs.VerifyStack(cfg, 0, 1, seed=0, device=dev)
+    hidden = vs.make_block(cfg, 0, dev)
+    ref = one.forward(hidden).float().cpu()
+    del one
+    tp = vs.VerifyStack(cfg, rank, world, seed=0, device=dev, group=dist.group.WORLD)
+    out = tp.forward(hidden).float().cpu()
+    torch.cuda.synchronize(dev)
+    tp.close()
+    del tp
+    err = max_over_ranks(float((out - ref).abs().max()) / max(float(ref.abs().max()), 1.0))
+    check = {"stack": "TP_CHECK (4 layers, hidden 512, 8 gated-delta / 8 q / 2 kv heads)", "closeness_vs_tp1": err,
+             "bar": 3e-2, "ok": err <= 3e-2}
+    if not check["ok"]:
+        return {"error": "TP = N differs from TP = 1", "tp_check": check}
+
+    cfg = vs.CONFIG4
+    stack = vs.VerifyStack(cfg, rank, world, seed=0, device=dev, group=dist.group.WORLD)
+    hidden = vs.make_block(cfg, 0, dev)
+    proposals = torch.zeros(cfg.block - 1, dtype=torch.int32, device=dev)
+
+    def timed(g, sample):
+        for _ in range(warmup):
+            g.replay()
+        torch.cuda.synchronize(dev)
+        sampler = ClockSampler(gpu_ids(world)) if sample and rank == 0 else None
+        if sampler:
+            sampler.start()
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        clocks = sampler.stop() if sampler else None
+        return max_over_ranks(e0.elapsed_time(e1) * 1e3 / steps), clocks
+
+    g = stack.capture(hidden)
+    fwd, clocks = timed(g, True)
+    del g
+    g = stack.capture(hidden, proposals)
+    rnd, _ = timed(g, False)
+    del g
+    stack.graph = None
+    wbytes = vs.weight_bytes(stack.w)
+    kernels = stack.kernels_per_forward()
+    stack.close()
+    del stack
+    torch.cuda.empty_cache()
+    return {"tp": world, "forward_us": round(fwd, 1), "round_us": round(rnd, 1),
+            "tokens_per_s": round(cfg.block / (fwd * 1e-6), 1), "weight_bytes_per_gpu": wbytes,
+            "weight_GBs_per_gpu": round(wbytes / (fwd * 1e-6) / 1e9, 1), "kernels_per_forward": kernels,
+            "allreduce": "peer (NVLink stores into the other ranks' exchange buffers)", "steps": steps,
+            "timing": "CUDA graph per forward, CUDA events, max over ranks", "clocks": clocks, "tp_check": check}
 
 
 def _qmm_copies(dev, gen, n, k, group, bits):

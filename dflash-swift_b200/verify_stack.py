@@ -97,6 +97,11 @@ TINY = StackConfig(layers=4, hidden=256, intermediate=512, gdn_heads=4, gdn_dk=6
 # The same with 2 gated-delta key heads for the 4 value heads (as the reference's fixture
 # has, Tests/DFlashKitTests/TinyHybridTarget.swift:27-30).
 TINY_GROUPED = replace(TINY, gdn_key_heads=2)
+# A small stack that shards over 1, 2, 4 and 8 ranks (every row-sharded K a whole number
+# of groups at 8 ranks; 2 kv heads, so at 4 and 8 ranks a kv head is replicated): the
+# benchmark's check that TP = N computes TP = 1's function on the same GPUs.
+TP_CHECK = StackConfig(layers=4, hidden=512, intermediate=1024, gdn_heads=8, gdn_dk=64, gdn_dv=64, attn_heads=8,
+                       kv_heads=2, head_dim=64, rotary_dim=64, rope_theta=1.0e4, context=24, block=8, vocab=2048)
 
 
 # ----------------------------------------------------------------------------- shard plan

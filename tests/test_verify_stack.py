@@ -13,6 +13,7 @@ import math
 import multiprocessing as mp
 import socket
 import sys
+import tempfile
 from dataclasses import asdict
 from pathlib import Path
 
@@ -170,6 +171,23 @@ def test_tp_gloo_matches_tp1_and_dropped_reduce_diverges(tmp_path, tiny_tp1_refe
     assert err_drop > max(0.05, 10 * err)
     # same tokens as TP=1 wherever TP=1's top logit is not within the TP rounding of a rival
     assert (tok_tp == tiny_tp1_reference["tokens"]).mean() >= 0.75
+
+
+def test_tp_check_config_at_eight_gloo_ranks_matches_tp1():
+    """The stack bench.py checks TP = N against at N = 2, 4, 8 (one q head, one gated-delta
+    head and 128 MLP units per rank at 8, each kv head replicated over four ranks): the
+    CPU reference of its 8-rank shards, summed by a real all-reduce, is TP = 1's function."""
+    import stack_ref
+    import stack_workers
+    cfg = vs.TP_CHECK
+    plan = vs.shard_plan(cfg, 0, 1)
+    ref = stack_ref.forward(cfg, plan, vs.build_rank_weights(cfg, plan, 0, "cpu"), vs.build_rank_state(cfg, plan, 0, "cpu"),
+                            vs.make_block(cfg, 0, "cpu"))["out"].numpy()
+    out = Path(tempfile.mkdtemp()) / "tp8.pt"
+    port = free_port()
+    codes = _run_ranks(stack_workers.gloo_reference_rank, 8, lambda r: (r, 8, port, str(out), asdict(cfg), False))
+    assert codes == [0] * 8, codes
+    assert closeness(torch.load(out)["out"].numpy(), ref) <= 3e-2
 
 
 def test_reference_stack_is_self_consistent(tiny_tp1_reference):
@@ -384,6 +402,19 @@ def test_cuda_stack_config4_shapes_run(cuda):
     torch.cuda.synchronize()
     assert torch.equal(stack.out, eager)
     del g
+
+
+@pytest.mark.gpu
+def test_cuda_tp_check_stack_matches_reference(cuda):
+    """The benchmark's TP check stack at TP = 1 on the GPU against the CPU reference."""
+    import stack_ref
+    cfg = vs.TP_CHECK
+    stack = vs.VerifyStack(cfg, 0, 1, seed=0, device=cuda)
+    hidden = vs.make_block(cfg, 0, cuda)
+    out = stack.forward(hidden).float().cpu().numpy()
+    torch.cuda.synchronize()
+    ref = stack_ref.forward(cfg, stack.plan, stack.w, stack.state, hidden)["out"].numpy()
+    assert closeness(out, ref) <= 2e-2
 
 
 @pytest.mark.gpu
