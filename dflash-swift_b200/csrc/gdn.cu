@@ -14,16 +14,22 @@
 //     S_ij <- alpha * S_ij + (beta * u_i) * k_j
 // which is  S <- alpha S;  S <- S + beta (v - S k) k^T  with the decay applied first.
 // The work is bound by reading the snapshot and writing the new state once
-// (2 * 4 * dv * dk bytes per head); each row is held in registers by 8 threads
-// (16 floats each for dk = 128) for all positions, with 128-byte coalesced row access.
+// (2 * 4 * dv * dk bytes per head).  Each row is held in registers by 8 threads (16 floats
+// each for dk = 128) for all positions, with 128-byte coalesced row access, and each
+// thread holds two rows (g and g + 16 of its block's 32): one shared-memory read of k_t
+// serves both, and the two rows' recurrences are independent chains the scheduler
+// interleaves.  k (and q), the block's v, alpha and beta of the positions are staged in
+// shared memory while the state loads are in flight, so the position loop reads no
+// global memory.
 #include "common.cuh"
 
 namespace dflash {
 namespace gdn {
 
-constexpr int kRowThreads = 8;         // threads per state row
-constexpr int kRowsPerBlock = 32;      // rows of S per block (256 threads)
-constexpr int kBlockThreads = kRowThreads * kRowsPerBlock;
+constexpr int kRowThreads = 8;                             // threads per state row
+constexpr int kRowsPerBlock = 32;                          // rows of S per block
+constexpr int kRowGroups = kRowsPerBlock / 2;              // a thread holds rows g and g + 16
+constexpr int kBlockThreads = kRowThreads * kRowGroups;    // 128
 constexpr int kMaxPositions = 64;
 
 struct RowList {
@@ -37,49 +43,57 @@ __device__ __forceinline__ float4 ld_bf16x4(const uint16_t* p) {
                        __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
 }
 
-// Sum over the 8 threads of a row (lanes 8r .. 8r+7 of a warp).
-__device__ __forceinline__ float row_sum(float v) {
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    v += __shfl_xor_sync(0xffffffffu, v, 2);
-    v += __shfl_xor_sync(0xffffffffu, v, 4);
-    return v;
+// Sums, over the 8 threads of a row group (lanes 8g .. 8g+7 of a warp), of the partial
+// dot products a (first row) and b (second row); every lane gets both.  The pair is
+// transposed across adjacent lanes first (even lanes go on with a, odd lanes with b), so
+// the two reductions take 4 shuffles, and every lane ends with the same bits.
+__device__ __forceinline__ float2 pair_sum(float a, float b) {
+    const bool odd = threadIdx.x & 1;
+    float mine = odd ? b : a;
+    mine += __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
+    mine += __shfl_xor_sync(0xffffffffu, mine, 2);
+    mine += __shfl_xor_sync(0xffffffffu, mine, 4);
+    const float theirs = __shfl_xor_sync(0xffffffffu, mine, 1);
+    return odd ? make_float2(theirs, mine) : make_float2(mine, theirs);
 }
 
-// One position of the recurrence for the slice of one row this thread holds.
-// s: CH float4 chunks of the row; k: the matching chunks of k_t (fp32).
+// Packed fp32 arithmetic (two lanes per instruction, sm_100): a float4 chunk of a row is
+// handled as two float2 halves.
+__device__ __forceinline__ float2 lo2(const float4& v) { return make_float2(v.x, v.y); }
+__device__ __forceinline__ float2 hi2(const float4& v) { return make_float2(v.z, v.w); }
+__device__ __forceinline__ float4 cat4(const float2& a, const float2& b) { return make_float4(a.x, a.y, b.x, b.y); }
+
+// Dot products of the thread's two row slices with CH chunks of a vector, summed over
+// the row group: {row g . x, row g+16 . x}.
 template <int CH>
-__device__ __forceinline__ void row_step(float4 (&s)[CH], const float4 (&k)[CH], float v, float alpha,
-                                         float beta) {
-    float dot = 0.f;
+__device__ __forceinline__ float2 rows_dot(const float4 (&s)[2][CH], const float4 (&x)[CH]) {
+    float2 d0 = make_float2(0.f, 0.f), d1 = d0;
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
-        dot = fmaf(s[c].x, k[c].x, dot);
-        dot = fmaf(s[c].y, k[c].y, dot);
-        dot = fmaf(s[c].z, k[c].z, dot);
-        dot = fmaf(s[c].w, k[c].w, dot);
+        d0 = __ffma2_rn(lo2(s[0][c]), lo2(x[c]), d0);
+        d1 = __ffma2_rn(lo2(s[1][c]), lo2(x[c]), d1);
+        d0 = __ffma2_rn(hi2(s[0][c]), hi2(x[c]), d0);
+        d1 = __ffma2_rn(hi2(s[1][c]), hi2(x[c]), d1);
     }
-    dot = row_sum(dot);
-    const float bu = beta * (v - alpha * dot);
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-        s[c].x = fmaf(bu, k[c].x, alpha * s[c].x);
-        s[c].y = fmaf(bu, k[c].y, alpha * s[c].y);
-        s[c].z = fmaf(bu, k[c].z, alpha * s[c].z);
-        s[c].w = fmaf(bu, k[c].w, alpha * s[c].w);
-    }
+    return pair_sum(d0.x + d0.y, d1.x + d1.y);
 }
 
+// One position of the recurrence for the two row slices a thread holds: s the rows'
+// CH float4 chunks, k the matching chunks of k_t (fp32), v the two rows' v_t.
 template <int CH>
-__device__ __forceinline__ float row_dot(const float4 (&s)[CH], const float4 (&q)[CH]) {
-    float dot = 0.f;
+__device__ __forceinline__ void rows_step(float4 (&s)[2][CH], const float4 (&k)[CH], float2 v, float alpha,
+                                          float beta) {
+    const float2 dot = rows_dot<CH>(s, k);
+    const float2 aa = make_float2(alpha, alpha);
+    const float bu0 = beta * (v.x - alpha * dot.x), bu1 = beta * (v.y - alpha * dot.y);
+    const float2 b0 = make_float2(bu0, bu0), b1 = make_float2(bu1, bu1);
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
-        dot = fmaf(s[c].x, q[c].x, dot);
-        dot = fmaf(s[c].y, q[c].y, dot);
-        dot = fmaf(s[c].z, q[c].z, dot);
-        dot = fmaf(s[c].w, q[c].w, dot);
+        s[0][c] = cat4(__ffma2_rn(b0, lo2(k[c]), __fmul2_rn(aa, lo2(s[0][c]))),
+                       __ffma2_rn(b0, hi2(k[c]), __fmul2_rn(aa, hi2(s[0][c]))));
+        s[1][c] = cat4(__ffma2_rn(b1, lo2(k[c]), __fmul2_rn(aa, lo2(s[1][c]))),
+                       __ffma2_rn(b1, hi2(k[c]), __fmul2_rn(aa, hi2(s[1][c]))));
     }
-    return row_sum(dot);
 }
 
 struct ReplayParams {
@@ -99,8 +113,9 @@ struct ReplayParams {
 };
 
 // grid: (dv / 32, heads, layers) — (dv / 32, heads, width) for a tree step, block z taking
-// the z-th leaf of the tree in row order; block: 256 threads = 32 rows x 8 threads.
-// Thread q of a row holds float4 chunks q, q+8, q+16, ... of the row (dk = 32 * CH).
+// the z-th leaf of the tree in row order; block: 128 threads = 16 row groups x 8 threads,
+// group g holding rows g and g + 16 of the block's 32.  Thread q of a group holds float4
+// chunks q, q+8, q+16, ... of both rows (dk = 32 * CH).
 //
 // Tree step (TREE): the recurrence of a tree row is that of its root-to-row path, so
 // each block runs the chain of one leaf's path from the same pre-round state and writes
@@ -108,22 +123,34 @@ struct ReplayParams {
 // by exactly one block; a row shared by several paths gets the same arithmetic on each).
 // No state is written: after the round, dflash_gdn_replay rebuilds it from the snapshot
 // over the accepted path.
+// Dynamic shared memory of a block over n positions: k (and q times q_scale) widened to
+// fp32 [n][dk], the block's 32 values of v per position (fp32, stored as the pairs a row
+// group reads), alpha and beta.  Staged once, so the position loop touches no global
+// memory and the snapshot loads are the only long waits.
+inline size_t smem_bytes(int n, int dk, bool with_q) {
+    return (size_t)n * dk * 4 * (with_q ? 2 : 1) + (size_t)n * kRowsPerBlock * 4 + (size_t)n * 8;
+}
+
 template <int CH, bool TREE>
 __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constant__ ReplayParams p) {
     constexpr int DK = 32 * CH;
-    // k and q of the replayed positions, kept as bf16 bits (widened on use)
-    __shared__ __align__(16) uint16_t ks[kMaxPositions][DK];
-    __shared__ __align__(16) uint16_t qs_sh[kMaxPositions][DK];
-    __shared__ float ab[kMaxPositions][2];
+    const bool want_out = p.out != nullptr && p.q != nullptr;
+    const int n = TREE ? p.width : p.keep;  // positions staged
+    extern __shared__ __align__(16) uint8_t dyn[];
+    float(*ks)[DK] = reinterpret_cast<float(*)[DK]>(dyn);
+    float(*qs_sh)[DK] = reinterpret_cast<float(*)[DK]>(dyn + (size_t)n * DK * 4);
+    // vs[r][g] = {v of row g, v of row g + 16} at position r
+    float2(*vs)[kRowGroups] =
+        reinterpret_cast<float2(*)[kRowGroups]>(dyn + (size_t)n * DK * 4 * (want_out ? 2 : 1));
+    float2* ab = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(vs) + (size_t)n * kRowsPerBlock * 4);
     __shared__ int32_t path_rows[TREE ? kMaxTreeRows : 1];
     __shared__ uint32_t path_info[2];  // tree: rows on this block's path, rows it writes
 
     const int layer = TREE ? 0 : blockIdx.z, h = blockIdx.y;
     const int row0 = blockIdx.x * kRowsPerBlock;
     const int tid = threadIdx.x;
-    const int rl = tid / kRowThreads, qd = tid % kRowThreads;
-    const int row = row0 + rl;
-    const bool want_out = p.out != nullptr && p.q != nullptr;
+    const int g = tid / kRowThreads, qd = tid % kRowThreads;
+    const int row = row0 + g;  // and row + kRowGroups
 
     int keep = p.keep;
     if constexpr (TREE) {
@@ -154,6 +181,19 @@ __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constan
         else return p.rows.r[r];
     };
 
+    // This thread's slices of its two state rows: requested first, so that the staging
+    // below runs while they are in flight.
+    const size_t head_base = (((size_t)layer * p.heads + h) * p.dv + row) * DK;
+    const float4* src = reinterpret_cast<const float4*>(p.snapshot + head_base) + qd;
+    constexpr int kSecond = kRowGroups * DK / 4;  // float4 offset of row + kRowGroups
+    float4 s[2][CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        // every leaf's block of a tree step reads the same state: keep it in L2 there
+        s[0][c] = TREE ? __ldg(src + c * kRowThreads) : __ldcs(src + c * kRowThreads);
+        s[1][c] = TREE ? __ldg(src + kSecond + c * kRowThreads) : __ldcs(src + kSecond + c * kRowThreads);
+    }
+
     // Stage k (and q), alpha, beta of the replayed positions.  q and k have k_heads heads,
     // each shared by heads / k_heads consecutive value heads.
     const int kh = p.k_heads > 0 ? p.k_heads : p.heads;
@@ -161,70 +201,79 @@ __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constan
     const size_t pos_stride = (size_t)p.heads;  // [width, H] per layer for alpha/beta
     for (int idx = tid; idx < keep * (DK / 4); idx += kBlockThreads) {
         const int r = idx / (DK / 4), c4 = (idx % (DK / 4)) * 4;
-        const int t = row_at(r);
-        const size_t base = (((size_t)layer * p.width + t) * kh + hk) * DK + c4;
-        *reinterpret_cast<uint2*>(&ks[r][c4]) = *reinterpret_cast<const uint2*>(p.k + base);
-        if (want_out) *reinterpret_cast<uint2*>(&qs_sh[r][c4]) = *reinterpret_cast<const uint2*>(p.q + base);
+        const size_t base = (((size_t)layer * p.width + row_at(r)) * kh + hk) * DK + c4;
+        *reinterpret_cast<float4*>(&ks[r][c4]) = ld_bf16x4(reinterpret_cast<const uint16_t*>(p.k + base));
+        if (want_out) {
+            const float4 qv = ld_bf16x4(reinterpret_cast<const uint16_t*>(p.q + base));
+            *reinterpret_cast<float4*>(&qs_sh[r][c4]) =
+                make_float4(qv.x * p.q_scale, qv.y * p.q_scale, qv.z * p.q_scale, qv.w * p.q_scale);
+        }
     }
     for (int r = tid; r < keep; r += kBlockThreads) {
-        const int t = row_at(r);
-        const size_t ai = ((size_t)layer * p.width + t) * pos_stride + h;
-        ab[r][0] = p.alpha[ai];
-        ab[r][1] = p.beta[ai];
+        const size_t ai = ((size_t)layer * p.width + row_at(r)) * pos_stride + h;
+        ab[r] = make_float2(p.alpha[ai], p.beta[ai]);
+    }
+    for (int idx = tid; idx < keep * kRowsPerBlock; idx += kBlockThreads) {  // the block's 32 rows of v
+        const int r = idx / kRowsPerBlock, j = idx % kRowsPerBlock;
+        const size_t vi = (((size_t)layer * p.width + row_at(r)) * p.heads + h) * p.dv + row0 + j;
+        reinterpret_cast<float*>(&vs[r][j % kRowGroups])[j / kRowGroups] = __uint_as_float((uint32_t)p.v[vi] << 16);
     }
 
-    // This thread's slice of the state row.
-    const size_t head_base = (((size_t)layer * p.heads + h) * p.dv + row) * DK;
-    float4 s[CH];
-#pragma unroll
-    for (int c = 0; c < CH; ++c)
-        s[c] = TREE ? __ldg(reinterpret_cast<const float4*>(p.snapshot + head_base) + qd + c * kRowThreads)
-                    // every leaf's block reads the same state: keep it in L2
-                    : __ldcs(reinterpret_cast<const float4*>(p.snapshot + head_base) + qd + c * kRowThreads);
     __syncthreads();
 
     for (int r = 0; r < keep; ++r) {
-        const int t = row_at(r);
         float4 k[CH];
 #pragma unroll
-        for (int c = 0; c < CH; ++c) k[c] = ld_bf16x4(&ks[r][4 * (qd + c * kRowThreads)]);
-        const size_t vi = (((size_t)layer * p.width + t) * p.heads + h) * p.dv + row;
-        const float v = __uint_as_float((uint32_t)p.v[vi] << 16);
-        row_step<CH>(s, k, v, ab[r][0], ab[r][1]);
+        for (int c = 0; c < CH; ++c) k[c] = *reinterpret_cast<const float4*>(&ks[r][4 * (qd + c * kRowThreads)]);
+        const float2 a_b = ab[r];
+        rows_step<CH>(s, k, vs[r][g], a_b.x, a_b.y);
         if (want_out) {
             float4 qv[CH];
 #pragma unroll
-            for (int c = 0; c < CH; ++c) {
-                const float4 raw = ld_bf16x4(&qs_sh[r][4 * (qd + c * kRowThreads)]);
-                qv[c] = make_float4(raw.x * p.q_scale, raw.y * p.q_scale, raw.z * p.q_scale, raw.w * p.q_scale);
-            }
-            const float o = row_dot<CH>(s, qv);
-            bool write = qd == 0;
+            for (int c = 0; c < CH; ++c) qv[c] = *reinterpret_cast<const float4*>(&qs_sh[r][4 * (qd + c * kRowThreads)]);
+            const float2 o = rows_dot<CH>(s, qv);
+            const int t = row_at(r);
+            bool write = qd < 2;  // lane 0 of the group writes row g, lane 1 row g + 16
             if constexpr (TREE) write = write && ((path_info[1] >> t) & 1u);
             if (write) {
-                __nv_bfloat16 ob = __float2bfloat16_rn(o);
-                p.out[(((size_t)layer * p.width + t) * p.heads + h) * p.dv + row] =
+                __nv_bfloat16 ob = __float2bfloat16_rn(qd ? o.y : o.x);
+                p.out[(((size_t)layer * p.width + t) * p.heads + h) * p.dv + row + qd * kRowGroups] =
                     *reinterpret_cast<uint16_t*>(&ob);
             }
         }
     }
     if constexpr (!TREE) {
+        float4* dst = reinterpret_cast<float4*>(p.state_out + head_base) + qd;
 #pragma unroll
-        for (int c = 0; c < CH; ++c)
-            __stcs(reinterpret_cast<float4*>(p.state_out + head_base) + qd + c * kRowThreads, s[c]);
+        for (int c = 0; c < CH; ++c) {
+            __stcs(dst + c * kRowThreads, s[0][c]);
+            __stcs(dst + kSecond + c * kRowThreads, s[1][c]);
+        }
     }
 }
 
 int launch(const ReplayParams& p, int layers, cudaStream_t stream) {
     const bool tree = p.parents != nullptr;  // tree step: one layer, one block per leaf slot
     dim3 grid(p.dv / kRowsPerBlock, p.heads, tree ? p.width : layers);
+    const size_t sm = smem_bytes(tree ? p.width : p.keep, p.dk, p.out != nullptr && p.q != nullptr);
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [] {  // up to 64 positions of fp32 k and q: past the 48 KB default
+        const int bytes = (int)smem_bytes(kMaxPositions, 128, true);
+        const void* fns[] = {(const void*)gdn_kernel<1, false>, (const void*)gdn_kernel<2, false>,
+                             (const void*)gdn_kernel<4, false>, (const void*)gdn_kernel<1, true>,
+                             (const void*)gdn_kernel<2, true>, (const void*)gdn_kernel<4, true>};
+        for (const void* f : fns)
+            if (attr == cudaSuccess) attr = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    });
+    if (attr != cudaSuccess) return fail(DFLASH_ERR_CUDA, "cudaFuncSetAttribute(gdn): %s", cudaGetErrorString(attr));
     switch (p.dk * 2 + tree) {
-        case 64: gdn_kernel<1, false><<<grid, kBlockThreads, 0, stream>>>(p); break;
-        case 128: gdn_kernel<2, false><<<grid, kBlockThreads, 0, stream>>>(p); break;
-        case 256: gdn_kernel<4, false><<<grid, kBlockThreads, 0, stream>>>(p); break;
-        case 65: gdn_kernel<1, true><<<grid, kBlockThreads, 0, stream>>>(p); break;
-        case 129: gdn_kernel<2, true><<<grid, kBlockThreads, 0, stream>>>(p); break;
-        case 257: gdn_kernel<4, true><<<grid, kBlockThreads, 0, stream>>>(p); break;
+        case 64: gdn_kernel<1, false><<<grid, kBlockThreads, sm, stream>>>(p); break;
+        case 128: gdn_kernel<2, false><<<grid, kBlockThreads, sm, stream>>>(p); break;
+        case 256: gdn_kernel<4, false><<<grid, kBlockThreads, sm, stream>>>(p); break;
+        case 65: gdn_kernel<1, true><<<grid, kBlockThreads, sm, stream>>>(p); break;
+        case 129: gdn_kernel<2, true><<<grid, kBlockThreads, sm, stream>>>(p); break;
+        case 257: gdn_kernel<4, true><<<grid, kBlockThreads, sm, stream>>>(p); break;
         default: return fail(DFLASH_ERR_UNSUPPORTED, "dk=%d not in {32, 64, 128}", p.dk);
     }
     DFLASH_CUDA_TRY(cudaGetLastError());

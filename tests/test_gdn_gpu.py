@@ -56,6 +56,35 @@ def test_step_matches_oracle(dc, O, cuda, dk, dv, H, T):
     assert rel_err(o.float().cpu().numpy(), want_o) <= 1e-2  # bf16 outputs
 
 
+@pytest.mark.parametrize("decays", ["halving", "vanishing", "zero", "none"])
+def test_decay_extremes_over_long_rounds(dc, O, cuda, decays):
+    """64 positions whose decays halve the state at every position (2^-64 of it left at the
+    end), drop it to 1e-30 or to 0 at once, or never decay it: the step stays within the
+    fp64 oracle's tolerance and the replay reproduces it bit for bit."""
+    import torch
+    T, H, dk, dv = 64, 2, 128, 128
+    c = O.make_gdn_case(1, T, H, dk, dv, seed=9)
+    a = c["alpha"]
+    if decays == "halving":
+        a[:] = 0.5
+    elif decays == "vanishing":
+        a[:, ::7] = 1e-30
+    elif decays == "zero":
+        a[:, 5::11] = 0.0
+    else:
+        a[:] = 1.0
+    c["alpha"] = np.ascontiguousarray(a, dtype=np.float32)
+    st, _ = step_layer(dc, cuda, c, 0, T, with_out=False)
+    want, _ = O.gdn_recurrence(c["snapshot"][0], c["k"][0], c["v"][0], c["alpha"][0], c["beta"][0], T)
+    assert rel_err(st.cpu().numpy(), want) <= REL
+    snap = dev(c["snapshot"], cuda)
+    replayed = torch.empty_like(snap)
+    dc.gdn_replay(snap, replayed, dev(c["k"], cuda), dev(c["v"], cuda), dev(c["alpha"], cuda), dev(c["beta"], cuda),
+                  keep=T)
+    torch.cuda.synchronize()
+    assert torch.equal(replayed[0], st)
+
+
 @pytest.mark.parametrize("keep", [1, 3, 7, 8])
 def test_replay_equals_committed_forward(dc, O, cuda, keep):
     import torch
