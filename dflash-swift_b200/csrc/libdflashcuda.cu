@@ -5,3 +5,4 @@
 #include "gdn.cu"
 #include "tp.cu"
 #include "stack.cu"
+#include "stack_driver.cu"

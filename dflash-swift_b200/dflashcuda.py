@@ -62,6 +62,9 @@ EXPORTED = (
     "dflash_stack_gdn_conv_gates_grouped",
     # attention with a device-resident cache position
     "dflash_stack_attn_prep_ex", "dflash_stack_attn_decode_ex",
+    # the verify stack as one object
+    "dflash_stack_create", "dflash_stack_forward", "dflash_stack_verify", "dflash_stack_commit",
+    "dflash_stack_advance", "dflash_stack_context", "dflash_stack_output", "dflash_stack_destroy",
 )
 
 
@@ -139,6 +142,14 @@ def _load() -> ctypes.CDLL:
         "dflash_stack_attn_prep_ex": ([_vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _f, _vp, _vp, _vp],
                                       _i),
         "dflash_stack_attn_decode_ex": ([_vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp], _i),
+        "dflash_stack_create": ([_vp, _i, ctypes.POINTER(_vp)], _i),
+        "dflash_stack_forward": ([_vp, _vp, _vp, _vp], _i),
+        "dflash_stack_verify": ([_vp, _vp, _vp, _vp, _vp, _vp], _i),
+        "dflash_stack_commit": ([_vp, ctypes.POINTER(ctypes.c_int32), _i, _vp], _i),
+        "dflash_stack_advance": ([_vp, _i], _i),
+        "dflash_stack_context": ([_vp], _i),
+        "dflash_stack_output": ([_vp], _vp),
+        "dflash_stack_destroy": ([_vp], None),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -721,3 +732,94 @@ def accept_reduce(exchange: PeerExchange, set_: int, proposals, tokens=None, acc
     check(lib.dflash_accept_reduce(exchange.ptr, exchange.world, int(set_), _ptr(proposals), drafts, _ptr(tokens),
                                    _ptr(accepted), _stream(stream)))
     return tokens, accepted
+
+
+# ----------------------------------------------------------------------------- the verify stack object
+
+class QWeight(ctypes.Structure):
+    """dflash_qweight (include/dflash_stack.h)."""
+    _fields_ = [("w", _vp), ("scales", _vp), ("biases", _vp), ("N", _i), ("K", _i)]
+
+
+class StackLayer(ctypes.Structure):
+    """dflash_stack_layer."""
+    _fields_ = [("attention", _i), ("ln", _vp), ("post_ln", _vp), ("in_proj", QWeight), ("out_proj", QWeight),
+                ("conv", _vp), ("a_log", _vp), ("dt_bias", _vp), ("gdn_norm", _vp), ("snapshot", _vp),
+                ("window", _vp), ("qkv", QWeight), ("o_proj", QWeight), ("q_norm", _vp), ("k_norm", _vp),
+                ("cache_k", _vp), ("cache_v", _vp), ("gate_up", QWeight), ("down", QWeight)]
+
+
+class StackDesc(ctypes.Structure):
+    """dflash_stack_desc."""
+    _fields_ = [("layers", _i), ("hidden", _i), ("block", _i), ("gdn_heads", _i), ("gdn_key_heads", _i),
+                ("gdn_dk", _i), ("gdn_dv", _i), ("conv_kernel", _i), ("attn_heads", _i), ("kv_heads", _i),
+                ("head_dim", _i), ("rotary_dim", _i), ("max_len", _i), ("rope_theta", _f), ("eps", _f),
+                ("group", _i), ("bits", _i), ("rank", _i), ("world", _i), ("vocab0", _i),
+                ("layer", ctypes.POINTER(StackLayer)), ("final_norm", _vp), ("lm_head", QWeight),
+                ("exchange", _vp), ("key_exchange", _vp)]
+
+
+def _qweight(q) -> QWeight:
+    return QWeight(_ptr(q.w), _ptr(q.scales), _ptr(q.biases), q.N, q.K) if q is not None else QWeight()
+
+
+class CStack:
+    """dflash_stack: the verify stack driven by the library alone (include/dflash_stack.h),
+    built over the shard weights and state of a verify_stack.VerifyStack-shaped shard (the
+    dicts of build_rank_weights / build_rank_state) — the same buffers, referenced.  The
+    exchanges (world > 1) are PeerExchange objects already connected to every rank."""
+
+    def __init__(self, cfg, plan, weights: dict, state: dict, context: int, exchange=None, key_exchange=None):
+        p, w = plan, weights
+        layers = []
+        for L, S in zip(w["layers"], state["layers"]):
+            if L["kind"] == "gdn":
+                layers.append(StackLayer(0, _ptr(L["ln"]), _ptr(L["post_ln"]), _qweight(L["in_proj"]),
+                                         _qweight(L["out_proj"]), _ptr(L["conv"]), _ptr(L["a_log"]),
+                                         _ptr(L["dt_bias"]), _ptr(L["gdn_norm"]), _ptr(S["snapshot"]),
+                                         _ptr(S["window"]), QWeight(), QWeight(), None, None, None, None,
+                                         _qweight(L["gate_up"]), _qweight(L["down"])))
+            else:
+                layers.append(StackLayer(1, _ptr(L["ln"]), _ptr(L["post_ln"]), QWeight(), QWeight(), None, None,
+                                         None, None, None, None, _qweight(L["qkv"]), _qweight(L["o_proj"]),
+                                         _ptr(L["q_norm"]), _ptr(L["k_norm"]), _ptr(S["cache_k"]),
+                                         _ptr(S["cache_v"]), _qweight(L["gate_up"]), _qweight(L["down"])))
+        self._layers = (StackLayer * len(layers))(*layers)
+        self._keep = (weights, state, exchange, key_exchange)  # referenced, not copied: keep alive
+        max_len = next((S["cache_k"].shape[1] for S in state["layers"] if "cache_k" in S), context + cfg.block)
+        self.desc = StackDesc(
+            cfg.layers, cfg.hidden, cfg.block, p.gdn_heads, p.gdn_key_heads or p.gdn_heads, cfg.gdn_dk, cfg.gdn_dv,
+            cfg.conv_kernel, p.attn_heads, p.kv_heads, cfg.head_dim, cfg.rotary_dim, max_len, cfg.rope_theta,
+            cfg.eps, cfg.group, cfg.bits, p.rank, p.world, p.vocab0, self._layers, _ptr(w["final_norm"]),
+            _qweight(w["lm_head"]), ctypes.cast(exchange.bases, _vp) if exchange is not None else None,
+            ctypes.cast(key_exchange.bases, _vp) if key_exchange is not None else None)
+        h = _vp()
+        check(lib.dflash_stack_create(ctypes.byref(self.desc), int(context), ctypes.byref(h)))
+        self.handle = h
+
+    def forward(self, hidden, out=None, stream=None):
+        check(lib.dflash_stack_forward(self.handle, _ptr(hidden), _ptr(out), _stream(stream)))
+        return out
+
+    def output_ptr(self) -> int:
+        return lib.dflash_stack_output(self.handle)
+
+    def verify(self, hidden, proposals, tokens, accepted, stream=None):
+        check(lib.dflash_stack_verify(self.handle, _ptr(hidden), _ptr(proposals), _ptr(tokens), _ptr(accepted),
+                                      _stream(stream)))
+        return tokens, accepted
+
+    def commit(self, keep: int, stream=None):
+        check(lib.dflash_stack_commit(self.handle, None, int(keep), _stream(stream)))
+
+    def advance(self, n: int):
+        check(lib.dflash_stack_advance(self.handle, int(n)))
+
+    @property
+    def context(self) -> int:
+        return int(lib.dflash_stack_context(self.handle))
+
+    def close(self):
+        if self.handle:
+            lib.dflash_stack_destroy(self.handle)
+            self.handle = None

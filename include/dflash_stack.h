@@ -222,6 +222,97 @@ int dflash_accept(const unsigned long long* argmax_keys, const int32_t* proposal
 int dflash_accept_reduce(void* exchange, int world, int set, const int32_t* proposals, int drafts,
                          int32_t* target_tokens, int32_t* accepted, dflash_stream_t stream);
 
+/* ------------------------------------------------------------------------------
+ * The verify stack as one object, for hosts that drive a verify round through this
+ * library alone (the reference's generator runs its verify forward, LM head and accept
+ * in-process: Sources/DFlashKit/DFlashSpeculativeGenerator.swift:389-398 and :555-571,
+ * and its rollback with rollbackGatedDeltaRound, :455-460).  It sequences the entry
+ * points above: per layer RMSNorm, the token mixer (gated delta: in-projection, conv +
+ * gates, recurrence step, gated norm, out-projection; attention: qkv, prep, decode,
+ * o-projection), RMSNorm, MLP (gate/up, then down with the SwiGLU folded into its input);
+ * the row-sharded projections' partials are summed over the ranks through the peer
+ * exchange (world > 1).  Chain rounds only (rows 0 .. keep-1 are accepted).
+ *
+ * Weights and state are this rank's shard in the caller's device memory, referenced, never
+ * copied: the caller keeps them alive until dflash_stack_destroy.  dflash_stack_create
+ * allocates the activations, the capture and the qmm workspace once (cudaMalloc); the
+ * round entry points allocate nothing, are stream-ordered and may be captured in a CUDA
+ * graph.  Exchange set-up (world > 1): each rank allocates two buffers with
+ * dflash_tp_exchange_alloc, one for [block, hidden] and one for [block, 4] (the LM head's
+ * argmax keys), shares them with dflash_ipc_get_handle / dflash_ipc_open_handle over the
+ * host's own channel, and passes both arrays of mapped bases (entry `rank` its own
+ * buffer); every rank's buffers must exist before any rank's first round.
+ * ------------------------------------------------------------------------------ */
+typedef struct dflash_qweight { /* one quantized projection: MLX affine layout, device memory */
+    const uint32_t* w;          /* [N, K * bits / 32] */
+    const dflash_bf16* scales;  /* [N, K / group] */
+    const dflash_bf16* biases;  /* [N, K / group] */
+    int N, K;
+} dflash_qweight;
+
+typedef struct dflash_stack_layer { /* one layer of this rank's shard (unused members NULL) */
+    int attention;                    /* 0: gated delta, 1: attention */
+    const dflash_bf16* ln;            /* [hidden] input RMSNorm weight */
+    const dflash_bf16* post_ln;       /* [hidden] post-mixer RMSNorm weight */
+    /* gated delta (heads h, key heads hk, dims dk = dv, conv kernel kc of the descriptor) */
+    dflash_qweight in_proj;           /* rows [q (hk dk) | k (hk dk) | v (h dv) | z (h dv) | b (h) | a (h)], K = hidden */
+    dflash_qweight out_proj;          /* [hidden, h dv] */
+    const dflash_bf16* conv;          /* [(2 hk + h) dk, kc] */
+    const float* a_log;               /* [h] */
+    const float* dt_bias;             /* [h] */
+    const dflash_bf16* gdn_norm;      /* [dv] */
+    float* snapshot;                  /* [h, dv, dk] pre-round state, read by rounds, rewritten by commit */
+    dflash_bf16* window;              /* [kc - 1, (2 hk + h) dk] conv window, rewritten by commit */
+    /* attention (hq q heads, hkv kv heads, head_dim d of the descriptor) */
+    dflash_qweight qkv;               /* rows [q (hq d) | gate (hq d) | k (hkv d) | v (hkv d)], K = hidden */
+    dflash_qweight o_proj;            /* [hidden, hq d] */
+    const dflash_bf16* q_norm;        /* [d] */
+    const dflash_bf16* k_norm;        /* [d] */
+    dflash_bf16* cache_k;             /* [hkv, max_len, d] */
+    dflash_bf16* cache_v;             /* [hkv, max_len, d] */
+    /* MLP (this rank's I units) */
+    dflash_qweight gate_up;           /* rows [gate (I) | up (I)], K = hidden */
+    dflash_qweight down;              /* [hidden, I] */
+} dflash_stack_layer;
+
+typedef struct dflash_stack_desc {
+    int layers, hidden, block;        /* block: rows M verified per round (1..16) */
+    int gdn_heads, gdn_key_heads, gdn_dk, gdn_dv, conv_kernel;  /* this rank's gated-delta heads */
+    int attn_heads, kv_heads, head_dim, rotary_dim, max_len;    /* this rank's attention heads; cache rows */
+    float rope_theta, eps;
+    int group, bits;                  /* quantization of every projection */
+    int rank, world;
+    int vocab0;                       /* first vocabulary row of this rank's LM-head shard */
+    const dflash_stack_layer* layer;  /* [layers], copied at creation */
+    const dflash_bf16* final_norm;    /* [hidden] */
+    dflash_qweight lm_head;           /* this rank's vocabulary shard, K = hidden */
+    void* const* exchange;            /* [world] mapped [block, hidden] exchange buffers (world > 1) */
+    void* const* key_exchange;        /* [world] mapped [block, 4] exchange buffers (world > 1) */
+} dflash_stack_desc;
+
+typedef struct dflash_stack dflash_stack;
+
+/* Checks the shard's shapes and allocates the round buffers; context: tokens already in the
+ * attention caches (the block's rows go to context .. context + block - 1). */
+int dflash_stack_create(const dflash_stack_desc* desc, int context, dflash_stack** out);
+/* The verify forward of one block: hidden bf16 [block, hidden] -> out bf16 [block, hidden]
+ * (NULL: the stack's own buffer, dflash_stack_output), identical on every rank. */
+int dflash_stack_forward(dflash_stack* s, const dflash_bf16* hidden, dflash_bf16* out, dflash_stream_t stream);
+/* A whole verify round: the forward, the LM head reduced to argmax keys, the accept
+ * (dflash_accept / dflash_accept_reduce): target_tokens int32 [block], *accepted; all device. */
+int dflash_stack_verify(dflash_stack* s, const dflash_bf16* hidden, const int32_t* proposals, int32_t* target_tokens,
+                        int32_t* accepted, dflash_stream_t stream);
+/* After a round: rows (host int32 [keep], NULL for 0 .. keep-1; only a chain's rows are
+ * accepted) become the committed state: every gated-delta snapshot is replayed over them
+ * and its conv window rebuilt.  The attention caches already hold them. */
+int dflash_stack_commit(dflash_stack* s, const int32_t* rows, int keep, dflash_stream_t stream);
+/* The caches hold n more committed tokens (host-side position, at most max_len; a round
+ * needs room for its block and fails with DFLASH_ERR_INVALID_ARGUMENT otherwise). */
+int dflash_stack_advance(dflash_stack* s, int n);
+int dflash_stack_context(const dflash_stack* s);
+const dflash_bf16* dflash_stack_output(const dflash_stack* s);
+void dflash_stack_destroy(dflash_stack* s);
+
 #ifdef __cplusplus
 }
 #endif
