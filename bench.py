@@ -780,6 +780,27 @@ def run_profile(args):
     print(f"profile run ok: {6} launches, M={m}, device error {dc.device_error()}")
 
 
+def run_profile_gdn(args):
+    """4 plain rollback replays of BASELINE config 5 (48 layers x 32 heads x 128 x 128 fp32,
+    keep 8), alternating over two snapshot/state pairs.  Used as the ncu target of gdn_kernel."""
+    import torch
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    import dflashcuda as dc
+    L, W, H, dk, dv, keep = 48, 8, 32, 128, 128, 8
+    g = torch.Generator(device=dev).manual_seed(2)
+    snaps = [0.1 * torch.randn(L, H, dv, dk, generator=g, device=dev) for _ in range(2)]
+    outs = [torch.empty_like(snaps[0]) for _ in range(2)]
+    k = torch.nn.functional.normalize(torch.randn(L, W, H, dk, generator=g, device=dev), dim=-1).to(torch.bfloat16)
+    v = torch.randn(L, W, H, dv, generator=g, device=dev).to(torch.bfloat16)
+    alpha = 0.9 + 0.1 * torch.rand(L, W, H, generator=g, device=dev)
+    beta = torch.rand(L, W, H, generator=g, device=dev)
+    for i in range(4):
+        dc.gdn_replay(snaps[i & 1], outs[i & 1], k, v, alpha, beta, keep=keep)
+    torch.cuda.synchronize()
+    print(f"gdn profile run ok: 4 replays, device error {dc.device_error()}")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -792,10 +813,14 @@ def main(argv=None):
     ap.add_argument("--profile", action="store_true",
                     help="a few plain launches of the workload for ncu (no graph, no timing line)")
     ap.add_argument("--profile-m", type=int, default=M)
+    ap.add_argument("--profile-gdn", action="store_true",
+                    help="a few plain rollback replays of config 5 for ncu (no timing line)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if args.profile:
+    if args.profile_gdn:
+        run_profile_gdn(args)
+    elif args.profile:
         run_profile(args)
     elif args.impl == "reference":
         run_reference(args)
