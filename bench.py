@@ -782,7 +782,7 @@ def run_profile(args):
 
 def run_profile_gdn(args):
     """4 plain rollback replays of BASELINE config 5 (48 layers x 32 heads x 128 x 128 fp32,
-    keep 8), alternating over two snapshot/state pairs.  Used as the ncu target of gdn_kernel."""
+    keep 8), alternating over two snapshot/state pairs: the target of a kernel capture of the replay."""
     import torch
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)

@@ -4,10 +4,10 @@
 // Reference contract: rollbackGatedDeltaRound / rollbackGatedDeltaTree, called at
 // Sources/DFlashKit/DFlashSpeculativeGenerator.swift:455-460, must leave the state a
 // committed forward over the kept positions would have left
-// (Tests/DFlashKitTests/GatedDeltaRollbackTests.swift:84-111).  Both kernels here run
-// the per-position update through the same device function, so a replay of `keep`
-// positions performs exactly the arithmetic a committed step over those positions
-// does.
+// (Tests/DFlashKitTests/GatedDeltaRollbackTests.swift:84-111).  The step, the tree
+// step and the replay are one kernel template run in three modes, and all run the
+// per-position update through the same device function, so a replay of `keep` positions
+// performs exactly the arithmetic a committed step over those positions does.
 //
 // Per head the fp32 state S is [dv, dk], dk contiguous.  Rows of S are independent:
 //     u_i   = v_i - alpha * sum_j S_ij k_j
@@ -16,11 +16,12 @@
 // The work is bound by reading the snapshot and writing the new state once
 // (2 * 4 * dv * dk bytes per head).  Each row is held in registers by 8 threads (16 floats
 // each for dk = 128) for all positions, with 128-byte coalesced row access, and each
-// thread holds two rows (g and g + 16 of its block's 32): one shared-memory read of k_t
-// serves both, and the two rows' recurrences are independent chains the scheduler
-// interleaves.  k (and q), the block's v, alpha and beta of the positions are staged in
-// shared memory while the state loads are in flight, so the position loop reads no
-// global memory.
+// thread holds four rows (g, g + 8, g + 16, g + 24 of its block's 32): one shared-memory
+// read of k_t serves all four, one transposed shuffle reduction sums their dot products,
+// and the four rows' recurrences are independent chains the scheduler interleaves.  The
+// arithmetic is packed fp32 (two lanes per FMA).  k (and q), the block's v, alpha and beta
+// of the positions are staged in shared memory while the state loads are in flight, so
+// the position loop reads no global memory.
 #include "common.cuh"
 
 namespace dflash {
@@ -28,8 +29,9 @@ namespace gdn {
 
 constexpr int kRowThreads = 8;                             // threads per state row
 constexpr int kRowsPerBlock = 32;                          // rows of S per block
-constexpr int kRowGroups = kRowsPerBlock / 2;              // a thread holds rows g and g + 16
-constexpr int kBlockThreads = kRowThreads * kRowGroups;    // 128
+constexpr int kRows = 4;                                   // rows a thread holds: g, g + 8, g + 16, g + 24
+constexpr int kRowGroups = kRowsPerBlock / kRows;          // 8
+constexpr int kBlockThreads = kRowThreads * kRowGroups;    // 64
 constexpr int kMaxPositions = 64;
 
 struct RowList {
@@ -43,18 +45,33 @@ __device__ __forceinline__ float4 ld_bf16x4(const uint16_t* p) {
                        __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
 }
 
-// Sums, over the 8 threads of a row group (lanes 8g .. 8g+7 of a warp), of the partial
-// dot products a (first row) and b (second row); every lane gets both.  The pair is
-// transposed across adjacent lanes first (even lanes go on with a, odd lanes with b), so
-// the two reductions take 4 shuffles, and every lane ends with the same bits.
-__device__ __forceinline__ float2 pair_sum(float a, float b) {
-    const bool odd = threadIdx.x & 1;
-    float mine = odd ? b : a;
-    mine += __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
-    mine += __shfl_xor_sync(0xffffffffu, mine, 2);
-    mine += __shfl_xor_sync(0xffffffffu, mine, 4);
-    const float theirs = __shfl_xor_sync(0xffffffffu, mine, 1);
-    return odd ? make_float2(theirs, mine) : make_float2(mine, theirs);
+// v of a row group's kRows rows at one position (one 16-byte shared-memory read).
+struct alignas(16) RowVals {
+    float x[kRows];
+};
+
+// Totals, over the 8 threads of a row group (lanes 8g' .. 8g'+7 of a warp), of the
+// partial dot products a[j] of the group's kRows rows; every lane gets all of them.  A
+// transposed reduction: each of three exchange steps halves the values a lane carries
+// (after the last, lanes 2j and 2j+1 of the group hold the total of row j), then three
+// exchanges hand every lane the other rows' totals.  Every lane ends with the same bits.
+__device__ __forceinline__ void group_sum(float (&a)[kRows]) {
+    const unsigned kAll = 0xffffffffu;
+    const bool b2 = threadIdx.x & 4, b1 = threadIdx.x & 2;
+    float k0 = b2 ? a[2] : a[0], k1 = b2 ? a[3] : a[1];  // rows kept: {0, 1} or {2, 3}
+    k0 += __shfl_xor_sync(kAll, b2 ? a[0] : a[2], 4);
+    k1 += __shfl_xor_sync(kAll, b2 ? a[1] : a[3], 4);
+    float t = b1 ? k1 : k0;  // row 2 b2 + b1
+    t += __shfl_xor_sync(kAll, b1 ? k0 : k1, 2);
+    t += __shfl_xor_sync(kAll, t, 1);
+    const float x2 = __shfl_xor_sync(kAll, t, 2);  // row 2 b2 + !b1
+    const float x4 = __shfl_xor_sync(kAll, t, 4);  // row 2 !b2 + b1
+    const float x6 = __shfl_xor_sync(kAll, t, 6);  // row 2 !b2 + !b1
+    const float lo = b1 ? x2 : t, hi = b1 ? t : x2, olo = b1 ? x6 : x4, ohi = b1 ? x4 : x6;
+    a[0] = b2 ? olo : lo;
+    a[1] = b2 ? ohi : hi;
+    a[2] = b2 ? lo : olo;
+    a[3] = b2 ? hi : ohi;
 }
 
 // Packed fp32 arithmetic (two lanes per instruction, sm_100): a float4 chunk of a row is
@@ -63,36 +80,41 @@ __device__ __forceinline__ float2 lo2(const float4& v) { return make_float2(v.x,
 __device__ __forceinline__ float2 hi2(const float4& v) { return make_float2(v.z, v.w); }
 __device__ __forceinline__ float4 cat4(const float2& a, const float2& b) { return make_float4(a.x, a.y, b.x, b.y); }
 
-// Dot products of the thread's two row slices with CH chunks of a vector, summed over
-// the row group: {row g . x, row g+16 . x}.
+// Dot products of the thread's kRows row slices with CH chunks of a vector, summed over
+// the row group, into d.
 template <int CH>
-__device__ __forceinline__ float2 rows_dot(const float4 (&s)[2][CH], const float4 (&x)[CH]) {
-    float2 d0 = make_float2(0.f, 0.f), d1 = d0;
+__device__ __forceinline__ void rows_dot(const float4 (&s)[kRows][CH], const float4 (&x)[CH], float (&d)[kRows]) {
+    float2 acc[kRows];
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) acc[j] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
-        d0 = __ffma2_rn(lo2(s[0][c]), lo2(x[c]), d0);
-        d1 = __ffma2_rn(lo2(s[1][c]), lo2(x[c]), d1);
-        d0 = __ffma2_rn(hi2(s[0][c]), hi2(x[c]), d0);
-        d1 = __ffma2_rn(hi2(s[1][c]), hi2(x[c]), d1);
+#pragma unroll
+        for (int j = 0; j < kRows; ++j) acc[j] = __ffma2_rn(lo2(s[j][c]), lo2(x[c]), acc[j]);
+#pragma unroll
+        for (int j = 0; j < kRows; ++j) acc[j] = __ffma2_rn(hi2(s[j][c]), hi2(x[c]), acc[j]);
     }
-    return pair_sum(d0.x + d0.y, d1.x + d1.y);
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) d[j] = acc[j].x + acc[j].y;
+    group_sum(d);
 }
 
-// One position of the recurrence for the two row slices a thread holds: s the rows'
-// CH float4 chunks, k the matching chunks of k_t (fp32), v the two rows' v_t.
+// One position of the recurrence for the kRows row slices a thread holds: s the rows'
+// CH float4 chunks, k the matching chunks of k_t (fp32), v the rows' v_t.
 template <int CH>
-__device__ __forceinline__ void rows_step(float4 (&s)[2][CH], const float4 (&k)[CH], float2 v, float alpha,
-                                          float beta) {
-    const float2 dot = rows_dot<CH>(s, k);
+__device__ __forceinline__ void rows_step(float4 (&s)[kRows][CH], const float4 (&k)[CH], const RowVals& v,
+                                          float alpha, float beta) {
+    float dot[kRows];
+    rows_dot<CH>(s, k, dot);
     const float2 aa = make_float2(alpha, alpha);
-    const float bu0 = beta * (v.x - alpha * dot.x), bu1 = beta * (v.y - alpha * dot.y);
-    const float2 b0 = make_float2(bu0, bu0), b1 = make_float2(bu1, bu1);
 #pragma unroll
-    for (int c = 0; c < CH; ++c) {
-        s[0][c] = cat4(__ffma2_rn(b0, lo2(k[c]), __fmul2_rn(aa, lo2(s[0][c]))),
-                       __ffma2_rn(b0, hi2(k[c]), __fmul2_rn(aa, hi2(s[0][c]))));
-        s[1][c] = cat4(__ffma2_rn(b1, lo2(k[c]), __fmul2_rn(aa, lo2(s[1][c]))),
-                       __ffma2_rn(b1, hi2(k[c]), __fmul2_rn(aa, hi2(s[1][c]))));
+    for (int j = 0; j < kRows; ++j) {
+        const float bu = beta * (v.x[j] - alpha * dot[j]);
+        const float2 bb = make_float2(bu, bu);
+#pragma unroll
+        for (int c = 0; c < CH; ++c)
+            s[j][c] = cat4(__ffma2_rn(bb, lo2(k[c]), __fmul2_rn(aa, lo2(s[j][c]))),
+                           __ffma2_rn(bb, hi2(k[c]), __fmul2_rn(aa, hi2(s[j][c]))));
     }
 }
 
@@ -113,9 +135,9 @@ struct ReplayParams {
 };
 
 // grid: (dv / 32, heads, layers) — (dv / 32, heads, width) for a tree step, block z taking
-// the z-th leaf of the tree in row order; block: 128 threads = 16 row groups x 8 threads,
-// group g holding rows g and g + 16 of the block's 32.  Thread q of a group holds float4
-// chunks q, q+8, q+16, ... of both rows (dk = 32 * CH).
+// the z-th leaf of the tree in row order; block: 64 threads = 8 row groups x 8 threads,
+// group g holding rows g, g + 8, g + 16 and g + 24 of the block's 32.  Thread q of a
+// group holds float4 chunks q, q+8, q+16, ... of its rows (dk = 32 * CH).
 //
 // Tree step (TREE): the recurrence of a tree row is that of its root-to-row path, so
 // each block runs the chain of one leaf's path from the same pre-round state and writes
@@ -124,24 +146,29 @@ struct ReplayParams {
 // No state is written: after the round, dflash_gdn_replay rebuilds it from the snapshot
 // over the accepted path.
 // Dynamic shared memory of a block over n positions: k (and q times q_scale) widened to
-// fp32 [n][dk], the block's 32 values of v per position (fp32, stored as the pairs a row
-// group reads), alpha and beta.  Staged once, so the position loop touches no global
+// fp32 [n][dk], the block's 32 values of v per position (fp32, stored as the quadruples a
+// row group reads), alpha and beta.  Staged once, so the position loop touches no global
 // memory and the snapshot loads are the only long waits.
-inline size_t smem_bytes(int n, int dk, bool with_q) {
+__host__ __device__ inline size_t smem_bytes(int n, int dk, bool with_q) {
     return (size_t)n * dk * 4 * (with_q ? 2 : 1) + (size_t)n * kRowsPerBlock * 4 + (size_t)n * 8;
 }
 
-template <int CH, bool TREE>
+// What a launch computes: the rollback replay (state only), the chain step (outputs and
+// state) or the tree step (outputs only).
+enum Mode { kReplay = 0, kStep = 1, kTree = 2 };
+
+template <int CH, int MODE>
 __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constant__ ReplayParams p) {
     constexpr int DK = 32 * CH;
-    const bool want_out = p.out != nullptr && p.q != nullptr;
+    constexpr bool TREE = MODE == kTree;
+    constexpr bool want_out = MODE != kReplay;
     const int n = TREE ? p.width : p.keep;  // positions staged
     extern __shared__ __align__(16) uint8_t dyn[];
     float(*ks)[DK] = reinterpret_cast<float(*)[DK]>(dyn);
     float(*qs_sh)[DK] = reinterpret_cast<float(*)[DK]>(dyn + (size_t)n * DK * 4);
-    // vs[r][g] = {v of row g, v of row g + 16} at position r
-    float2(*vs)[kRowGroups] =
-        reinterpret_cast<float2(*)[kRowGroups]>(dyn + (size_t)n * DK * 4 * (want_out ? 2 : 1));
+    // vs[r][g] = v of rows g, g + 8, g + 16, g + 24 at position r
+    RowVals(*vs)[kRowGroups] =
+        reinterpret_cast<RowVals(*)[kRowGroups]>(dyn + (size_t)n * DK * 4 * (want_out ? 2 : 1));
     float2* ab = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(vs) + (size_t)n * kRowsPerBlock * 4);
     __shared__ int32_t path_rows[TREE ? kMaxTreeRows : 1];
     __shared__ uint32_t path_info[2];  // tree: rows on this block's path, rows it writes
@@ -150,7 +177,7 @@ __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constan
     const int row0 = blockIdx.x * kRowsPerBlock;
     const int tid = threadIdx.x;
     const int g = tid / kRowThreads, qd = tid % kRowThreads;
-    const int row = row0 + g;  // and row + kRowGroups
+    const int row = row0 + g;  // and row + 8, row + 16, row + 24
 
     int keep = p.keep;
     if constexpr (TREE) {
@@ -181,18 +208,17 @@ __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constan
         else return p.rows.r[r];
     };
 
-    // This thread's slices of its two state rows: requested first, so that the staging
-    // below runs while they are in flight.
+    // This thread's slices of its state rows: requested first, so that the staging below
+    // runs while they are in flight.
     const size_t head_base = (((size_t)layer * p.heads + h) * p.dv + row) * DK;
     const float4* src = reinterpret_cast<const float4*>(p.snapshot + head_base) + qd;
-    constexpr int kSecond = kRowGroups * DK / 4;  // float4 offset of row + kRowGroups
-    float4 s[2][CH];
+    constexpr int kNext = kRowGroups * DK / 4;  // float4 offset of the group's next row
+    float4 s[kRows][CH];
 #pragma unroll
-    for (int c = 0; c < CH; ++c) {
-        // every leaf's block of a tree step reads the same state: keep it in L2 there
-        s[0][c] = TREE ? __ldg(src + c * kRowThreads) : __ldcs(src + c * kRowThreads);
-        s[1][c] = TREE ? __ldg(src + kSecond + c * kRowThreads) : __ldcs(src + kSecond + c * kRowThreads);
-    }
+    for (int j = 0; j < kRows; ++j)
+#pragma unroll
+        for (int c = 0; c < CH; ++c)  // every leaf's block of a tree step reads the same state: keep it in L2 there
+            s[j][c] = TREE ? __ldg(src + j * kNext + c * kRowThreads) : __ldcs(src + j * kNext + c * kRowThreads);
 
     // Stage k (and q), alpha, beta of the replayed positions.  q and k have k_heads heads,
     // each shared by heads / k_heads consecutive value heads.
@@ -216,11 +242,12 @@ __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constan
     for (int idx = tid; idx < keep * kRowsPerBlock; idx += kBlockThreads) {  // the block's 32 rows of v
         const int r = idx / kRowsPerBlock, j = idx % kRowsPerBlock;
         const size_t vi = (((size_t)layer * p.width + row_at(r)) * p.heads + h) * p.dv + row0 + j;
-        reinterpret_cast<float*>(&vs[r][j % kRowGroups])[j / kRowGroups] = __uint_as_float((uint32_t)p.v[vi] << 16);
+        vs[r][j % kRowGroups].x[j / kRowGroups] = __uint_as_float((uint32_t)p.v[vi] << 16);
     }
 
     __syncthreads();
 
+#pragma unroll 2
     for (int r = 0; r < keep; ++r) {
         float4 k[CH];
 #pragma unroll
@@ -231,12 +258,13 @@ __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constan
             float4 qv[CH];
 #pragma unroll
             for (int c = 0; c < CH; ++c) qv[c] = *reinterpret_cast<const float4*>(&qs_sh[r][4 * (qd + c * kRowThreads)]);
-            const float2 o = rows_dot<CH>(s, qv);
+            float o[kRows];
+            rows_dot<CH>(s, qv, o);
             const int t = row_at(r);
-            bool write = qd < 2;  // lane 0 of the group writes row g, lane 1 row g + 16
+            bool write = qd < kRows;  // lane j of the group writes row g + 8 j
             if constexpr (TREE) write = write && ((path_info[1] >> t) & 1u);
             if (write) {
-                __nv_bfloat16 ob = __float2bfloat16_rn(qd ? o.y : o.x);
+                __nv_bfloat16 ob = __float2bfloat16_rn(qd == 0 ? o[0] : qd == 1 ? o[1] : qd == 2 ? o[2] : o[3]);
                 p.out[(((size_t)layer * p.width + t) * p.heads + h) * p.dv + row + qd * kRowGroups] =
                     *reinterpret_cast<uint16_t*>(&ob);
             }
@@ -245,36 +273,43 @@ __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constan
     if constexpr (!TREE) {
         float4* dst = reinterpret_cast<float4*>(p.state_out + head_base) + qd;
 #pragma unroll
-        for (int c = 0; c < CH; ++c) {
-            __stcs(dst + c * kRowThreads, s[0][c]);
-            __stcs(dst + kSecond + c * kRowThreads, s[1][c]);
-        }
+        for (int j = 0; j < kRows; ++j)
+#pragma unroll
+            for (int c = 0; c < CH; ++c) __stcs(dst + j * kNext + c * kRowThreads, s[j][c]);
     }
 }
 
 int launch(const ReplayParams& p, int layers, cudaStream_t stream) {
     const bool tree = p.parents != nullptr;  // tree step: one layer, one block per leaf slot
-    dim3 grid(p.dv / kRowsPerBlock, p.heads, tree ? p.width : layers);
-    const size_t sm = smem_bytes(tree ? p.width : p.keep, p.dk, p.out != nullptr && p.q != nullptr);
+    const bool with_q = p.out != nullptr && p.q != nullptr;
+    const int mode = tree ? kTree : with_q ? kStep : kReplay;
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [] {  // up to 64 positions of fp32 k and q: past the 48 KB default
         const int bytes = (int)smem_bytes(kMaxPositions, 128, true);
-        const void* fns[] = {(const void*)gdn_kernel<1, false>, (const void*)gdn_kernel<2, false>,
-                             (const void*)gdn_kernel<4, false>, (const void*)gdn_kernel<1, true>,
-                             (const void*)gdn_kernel<2, true>, (const void*)gdn_kernel<4, true>};
+        const void* fns[] = {(const void*)gdn_kernel<1, kReplay>, (const void*)gdn_kernel<2, kReplay>,
+                             (const void*)gdn_kernel<4, kReplay>, (const void*)gdn_kernel<1, kStep>,
+                             (const void*)gdn_kernel<2, kStep>,   (const void*)gdn_kernel<4, kStep>,
+                             (const void*)gdn_kernel<1, kTree>,   (const void*)gdn_kernel<2, kTree>,
+                             (const void*)gdn_kernel<4, kTree>};
         for (const void* f : fns)
             if (attr == cudaSuccess) attr = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     });
     if (attr != cudaSuccess) return fail(DFLASH_ERR_CUDA, "cudaFuncSetAttribute(gdn): %s", cudaGetErrorString(attr));
-    switch (p.dk * 2 + tree) {
-        case 64: gdn_kernel<1, false><<<grid, kBlockThreads, sm, stream>>>(p); break;
-        case 128: gdn_kernel<2, false><<<grid, kBlockThreads, sm, stream>>>(p); break;
-        case 256: gdn_kernel<4, false><<<grid, kBlockThreads, sm, stream>>>(p); break;
-        case 65: gdn_kernel<1, true><<<grid, kBlockThreads, sm, stream>>>(p); break;
-        case 129: gdn_kernel<2, true><<<grid, kBlockThreads, sm, stream>>>(p); break;
-        case 257: gdn_kernel<4, true><<<grid, kBlockThreads, sm, stream>>>(p); break;
-        default: return fail(DFLASH_ERR_UNSUPPORTED, "dk=%d not in {32, 64, 128}", p.dk);
+    if (p.dk != 32 && p.dk != 64 && p.dk != 128) return fail(DFLASH_ERR_UNSUPPORTED, "dk=%d not in {32, 64, 128}", p.dk);
+
+    dim3 grid(p.dv / kRowsPerBlock, p.heads, tree ? p.width : layers);
+    const size_t sm = smem_bytes(tree ? p.width : p.keep, p.dk, with_q);
+    switch (p.dk * 4 + mode) {
+        case 32 * 4 + kReplay: gdn_kernel<1, kReplay><<<grid, kBlockThreads, sm, stream>>>(p); break;
+        case 64 * 4 + kReplay: gdn_kernel<2, kReplay><<<grid, kBlockThreads, sm, stream>>>(p); break;
+        case 128 * 4 + kReplay: gdn_kernel<4, kReplay><<<grid, kBlockThreads, sm, stream>>>(p); break;
+        case 32 * 4 + kStep: gdn_kernel<1, kStep><<<grid, kBlockThreads, sm, stream>>>(p); break;
+        case 64 * 4 + kStep: gdn_kernel<2, kStep><<<grid, kBlockThreads, sm, stream>>>(p); break;
+        case 128 * 4 + kStep: gdn_kernel<4, kStep><<<grid, kBlockThreads, sm, stream>>>(p); break;
+        case 32 * 4 + kTree: gdn_kernel<1, kTree><<<grid, kBlockThreads, sm, stream>>>(p); break;
+        case 64 * 4 + kTree: gdn_kernel<2, kTree><<<grid, kBlockThreads, sm, stream>>>(p); break;
+        case 128 * 4 + kTree: gdn_kernel<4, kTree><<<grid, kBlockThreads, sm, stream>>>(p); break;
     }
     DFLASH_CUDA_TRY(cudaGetLastError());
     return DFLASH_OK;

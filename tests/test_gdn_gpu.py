@@ -179,3 +179,43 @@ def test_config5_full_size(dc, O, cuda, keep):
                                    c["alpha"][layer][:, heads], c["beta"][layer][:, heads], keep)
         assert rel_err(out[layer][heads].cpu().numpy(), want) <= REL
     assert dc.device_error() == 0
+
+
+@pytest.mark.parametrize("dk,dv,H,Hk,width,rows", [
+    (128, 128, 32, 32, 8, None),
+    (128, 128, 32, 8, 8, [0, 2, 3, 5, 6]),
+    (64, 64, 48, 48, 12, [0, 2, 3, 5, 8, 9, 11]),
+    (32, 32, 100, 25, 5, None),
+    (128, 64, 20, 4, 64, None),
+])
+def test_multi_layer_replay_matches_per_layer_steps(dc, O, cuda, dk, dv, H, Hk, width, rows):
+    """A replay of several layers over a subset of a round's positions (shared key heads
+    included) equals, layer by layer, a step over those positions gathered: bit for bit,
+    and the oracle within tolerance."""
+    import torch
+    L = 3
+    keep = len(rows) if rows else width
+    c = O.make_gdn_case(L, width, H, dk, dv, seed=11)
+    if Hk != H:  # one key head per group of H / Hk value heads
+        c["k"] = np.ascontiguousarray(c["k"][:, :, ::H // Hk])
+        c["q"] = np.ascontiguousarray(c["q"][:, :, ::H // Hk])
+    snap = dev(c["snapshot"], cuda)
+    out = torch.empty_like(snap)
+    dc.gdn_replay(snap, out, dev(c["k"], cuda), dev(c["v"], cuda), dev(c["alpha"], cuda), dev(c["beta"], cuda),
+                  keep=keep, rows=rows)
+    torch.cuda.synchronize()
+    assert dc.device_error() == 0
+    sel = rows if rows else list(range(width))
+    for layer in range(L):
+        g = {key: np.ascontiguousarray(c[key][layer][sel]) for key in ("q", "k", "v", "alpha", "beta")}
+        st = torch.empty_like(snap[layer])
+        dc.gdn_step(snap[layer], st, dev(g["q"], cuda), dev(g["k"], cuda), dev(g["v"], cuda), dev(g["alpha"], cuda),
+                    dev(g["beta"], cuda))
+        torch.cuda.synchronize()
+        assert torch.equal(out[layer], st), f"layer {layer}"
+    heads = [0, H // 3, H - 1]
+    kh = [h // (H // Hk) for h in heads]
+    layer = L - 1
+    want, _ = O.gdn_recurrence(c["snapshot"][layer][heads], c["k"][layer][sel][:, kh], c["v"][layer][sel][:, heads],
+                               c["alpha"][layer][sel][:, heads], c["beta"][layer][sel][:, heads], keep)
+    assert rel_err(out[layer][heads].cpu().numpy(), want) <= REL
