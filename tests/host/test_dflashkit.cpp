@@ -10,19 +10,29 @@
 //        closeness measure, <= 1e-2), with bias and with more than 16 rows, and
 //        rollbackGatedDeltaRound / Tree against the recurrence oracle
 //        (GatedDeltaRollbackTests.swift:84-111: relative state error <= 1e-4, conv window
-//        bit-exact).
+//        bit-exact);
+//   stack <dir>: one verify round of the C-ABI stack object (include/dflash_stack.h) the
+//        way a host drives it (DFlashSpeculativeGenerator.swift:389-398, :455-460,
+//        :555-571): create over a shard's buffers, verify a block, commit the accepted
+//        rows, advance.  The buffers come from <dir>/blob.bin as <dir>/manifest.txt
+//        places them; what the round produced goes to <dir>/result.bin, placed by
+//        <dir>/result.txt, for the test that wrote the inputs to compare.
 // The oracle (oracle/liboracle.so) is the test's checker only.
 #include <cuda_runtime.h>
 
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <fstream>
 #include <functional>
+#include <map>
 #include <random>
 #include <set>
+#include <sstream>
 #include <string>
 #include <vector>
 
+#include "dflash_stack.h"
 #include "dflashkit.hpp"
 
 extern "C" {
@@ -434,11 +444,192 @@ static int runGpu() {
     return 0;
 }
 
+// ------------------------------------------------------------------ stack object
+
+struct StackInputs {
+    std::map<std::string, std::pair<size_t, size_t>> tensors;  // name -> (offset, bytes) in blob.bin
+    std::map<std::string, std::pair<int, int>> qshape;          // quantized projection -> (N, K)
+    std::map<std::string, double> cfg;
+    std::vector<int> attention;                                 // per layer: 0 gated delta, 1 attention
+    uint8_t* base = nullptr;                                    // blob.bin on the device
+};
+
+static bool readStackInputs(const std::string& dir, StackInputs& in) {
+    std::ifstream mf(dir + "/manifest.txt");
+    if (!mf) return false;
+    std::string line;
+    while (std::getline(mf, line)) {
+        std::istringstream ls(line);
+        std::string kind, name;
+        ls >> kind >> name;
+        if (kind == "cfg") {
+            double v;
+            ls >> v;
+            in.cfg[name] = v;
+        } else if (kind == "tensor") {
+            size_t off, bytes;
+            ls >> off >> bytes;
+            in.tensors[name] = {off, bytes};
+        } else if (kind == "qweight") {
+            int N, K;
+            ls >> N >> K;
+            in.qshape[name] = {N, K};
+        } else if (kind == "layer") {
+            int att;
+            ls >> att;
+            in.attention.push_back(att);
+        }
+    }
+    std::ifstream bf(dir + "/blob.bin", std::ios::binary);
+    if (!bf) return false;
+    std::vector<char> blob((std::istreambuf_iterator<char>(bf)), std::istreambuf_iterator<char>());
+    if (cudaMalloc(&in.base, blob.size()) != cudaSuccess) return false;
+    return cudaMemcpy(in.base, blob.data(), blob.size(), cudaMemcpyHostToDevice) == cudaSuccess;
+}
+
+static int runStack(const std::string& dir) {
+    StackInputs in;
+    if (!readStackInputs(dir, in)) {
+        std::fprintf(stderr, "cannot read the stack inputs in %s\n", dir.c_str());
+        return 2;
+    }
+    auto ptr = [&](const std::string& name) -> void* {
+        auto it = in.tensors.find(name);
+        return it == in.tensors.end() ? nullptr : in.base + it->second.first;
+    };
+    auto bf = [&](const std::string& name) { return static_cast<dflash_bf16*>(ptr(name)); };
+    auto qw = [&](const std::string& name) {
+        dflash_qweight q{};
+        auto it = in.qshape.find(name);
+        if (it == in.qshape.end()) return q;
+        q.w = static_cast<const uint32_t*>(ptr(name + ".w"));
+        q.scales = bf(name + ".scales");
+        q.biases = bf(name + ".biases");
+        q.N = it->second.first;
+        q.K = it->second.second;
+        return q;
+    };
+    auto cfg = [&](const char* key) { return (int)in.cfg.at(key); };
+
+    const int layers = (int)in.attention.size();
+    std::vector<dflash_stack_layer> L(layers);
+    for (int i = 0; i < layers; ++i) {
+        const std::string p = "L" + std::to_string(i) + ".";
+        dflash_stack_layer& l = L[i];
+        std::memset(&l, 0, sizeof(l));
+        l.attention = in.attention[i];
+        l.ln = bf(p + "ln");
+        l.post_ln = bf(p + "post_ln");
+        l.in_proj = qw(p + "in_proj");
+        l.out_proj = qw(p + "out_proj");
+        l.conv = bf(p + "conv");
+        l.a_log = static_cast<const float*>(ptr(p + "a_log"));
+        l.dt_bias = static_cast<const float*>(ptr(p + "dt_bias"));
+        l.gdn_norm = bf(p + "gdn_norm");
+        l.snapshot = static_cast<float*>(ptr(p + "snapshot"));
+        l.window = bf(p + "window");
+        l.qkv = qw(p + "qkv");
+        l.o_proj = qw(p + "o_proj");
+        l.q_norm = bf(p + "q_norm");
+        l.k_norm = bf(p + "k_norm");
+        l.cache_k = bf(p + "cache_k");
+        l.cache_v = bf(p + "cache_v");
+        l.gate_up = qw(p + "gate_up");
+        l.down = qw(p + "down");
+    }
+    dflash_stack_desc d{};
+    d.layers = layers;
+    d.hidden = cfg("hidden");
+    d.block = cfg("block");
+    d.gdn_heads = cfg("gdn_heads");
+    d.gdn_key_heads = cfg("gdn_key_heads");
+    d.gdn_dk = cfg("gdn_dk");
+    d.gdn_dv = cfg("gdn_dv");
+    d.conv_kernel = cfg("conv_kernel");
+    d.attn_heads = cfg("attn_heads");
+    d.kv_heads = cfg("kv_heads");
+    d.head_dim = cfg("head_dim");
+    d.rotary_dim = cfg("rotary_dim");
+    d.max_len = cfg("max_len");
+    d.rope_theta = (float)in.cfg.at("rope_theta");
+    d.eps = (float)in.cfg.at("eps");
+    d.group = cfg("group");
+    d.bits = cfg("bits");
+    d.rank = 0;
+    d.world = 1;
+    d.vocab0 = 0;
+    d.layer = L.data();
+    d.final_norm = bf("final_norm");
+    d.lm_head = qw("lm_head");
+
+    dflash_stack* st = nullptr;
+    const int context = cfg("context"), keep = cfg("keep"), block = d.block, hidden = d.hidden;
+    CHECK(dflash_stack_create(&d, context, &st) == DFLASH_OK);
+    if (!st) {
+        std::fprintf(stderr, "dflash_stack_create: %s\n", dflash_last_error());
+        return 1;
+    }
+    CHECK(dflash_stack_context(st) == context);
+    int32_t *tokens = nullptr, *accepted = nullptr;
+    CHECK(cudaMalloc(&tokens, block * sizeof(int32_t)) == cudaSuccess);
+    CHECK(cudaMalloc(&accepted, sizeof(int32_t)) == cudaSuccess);
+    CHECK(dflash_stack_verify(st, bf("hidden"), static_cast<const int32_t*>(ptr("proposals")), tokens, accepted,
+                              nullptr) == DFLASH_OK);
+    std::vector<uint16_t> out((size_t)block * hidden);
+    std::vector<int32_t> tok(block), acc(1);
+    CHECK(cudaMemcpy(out.data(), dflash_stack_output(st), out.size() * 2, cudaMemcpyDeviceToHost) == cudaSuccess);
+    CHECK(cudaMemcpy(tok.data(), tokens, block * 4, cudaMemcpyDeviceToHost) == cudaSuccess);
+    CHECK(cudaMemcpy(acc.data(), accepted, 4, cudaMemcpyDeviceToHost) == cudaSuccess);
+    // the forward alone, into a caller buffer, repeats the verify's forward bit for bit
+    dflash_bf16* again = nullptr;
+    CHECK(cudaMalloc(&again, out.size() * 2) == cudaSuccess);
+    CHECK(dflash_stack_forward(st, bf("hidden"), again, nullptr) == DFLASH_OK);
+    std::vector<uint16_t> out2(out.size());
+    CHECK(cudaMemcpy(out2.data(), again, out2.size() * 2, cudaMemcpyDeviceToHost) == cudaSuccess);
+    CHECK(out2 == out);
+    // a round with no room left in the caches is refused before any launch
+    CHECK(dflash_stack_advance(st, d.max_len) == DFLASH_ERR_INVALID_ARGUMENT);
+    CHECK(dflash_stack_commit(st, nullptr, keep, nullptr) == DFLASH_OK);
+    CHECK(dflash_stack_advance(st, keep) == DFLASH_OK);
+    CHECK(dflash_stack_context(st) == context + keep);
+    CHECK(cudaDeviceSynchronize() == cudaSuccess);
+    uint32_t bits = 0;
+    CHECK(dflash_device_error(&bits, nullptr) == DFLASH_OK && bits == 0);
+
+    // results: the round's output, tokens, accept count, and every layer's state after it
+    std::ofstream rb(dir + "/result.bin", std::ios::binary), rt(dir + "/result.txt");
+    size_t off = 0;
+    auto put = [&](const std::string& name, const void* host, size_t bytes) {
+        rb.write(static_cast<const char*>(host), (std::streamsize)bytes);
+        rt << name << " " << off << " " << bytes << "\n";
+        off += bytes;
+    };
+    put("out", out.data(), out.size() * 2);
+    put("tokens", tok.data(), tok.size() * 4);
+    put("accepted", acc.data(), 4);
+    for (int i = 0; i < layers; ++i)
+        for (const char* key : {"snapshot", "window", "cache_k", "cache_v"}) {
+            const std::string name = "L" + std::to_string(i) + "." + key;
+            auto it = in.tensors.find(name);
+            if (it == in.tensors.end()) continue;
+            std::vector<uint8_t> host(it->second.second);
+            CHECK(cudaMemcpy(host.data(), in.base + it->second.first, host.size(), cudaMemcpyDeviceToHost) ==
+                  cudaSuccess);
+            put(name, host.data(), host.size());
+        }
+    dflash_stack_destroy(st);
+    cudaFree(tokens);
+    cudaFree(accepted);
+    cudaFree(again);
+    cudaFree(in.base);
+    return 0;
+}
+
 int main(int argc, char** argv) {
     const std::string mode = argc > 1 ? argv[1] : "cpu";
     int rc = 0;
     try {
-        rc = mode == "gpu" ? runGpu() : runCpu();
+        rc = mode == "gpu" ? runGpu() : mode == "stack" ? runStack(argc > 2 ? argv[2] : ".") : runCpu();
     } catch (const std::exception& e) {
         std::fprintf(stderr, "uncaught: %s\n", e.what());
         return 3;
