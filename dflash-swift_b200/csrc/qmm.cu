@@ -76,7 +76,12 @@ constexpr int kRowBytes = 128;                   // packed weight bytes per row 
 constexpr int kMaxStages = 8;
 constexpr int kMaxSbStages = 8;
 constexpr int kMaxCluster = 8;  // CTAs of a cluster, each taking a contiguous 1/cs of K
-constexpr int kSmemLimit = 232448;               // opt-in shared memory per block, sm_100
+// Shared memory a weight-stream CTA plans for: the 227 KB opt-in maximum less 16 KB, so
+// that the small kernels chained around a call — the next call's prep blocks, the verify
+// stack's norms and glue — can be resident beside a running CTA instead of waiting for it
+// to exit (measured: config 2 17.4 -> 16.5 us per back-to-back call, the TP = 1 verify
+// forward 6.96 -> 6.69 ms; 8 KB of headroom gives the former, 16 KB both).
+constexpr int kSmemLimit = 232448 - 16384;
 constexpr int kBarConsumers = 1;                 // named barrier: all consumer warps
 constexpr int kPrepThreads = 32;                 // one warp per prep block: fits beside a running main CTA
 constexpr int kMaxN = 1 << 24;
