@@ -572,12 +572,18 @@ def gpu_ids(world):
     return list(range(world))
 
 
+# Streams the e2e legs rotate over.  The 278 KB copy of y back to the host takes 8.4 us of
+# the single device-to-host copy engine per step; with two streams it and the next steps'
+# copies pipeline poorly against the kernels (24.0 us per step), with three they hide
+# behind them (18.7 us, against 15-16.5 us for the kernels alone).
+E2E_STREAMS = 3
+
 E2E_PATHS = {
     "host_entry": "pinned host x -> dflash_qmm_host (C ABI via ctypes: copy in, matmul, copy out queued by one "
-                  "library call) -> pinned host y, every step; steps alternate over two streams so copies overlap "
+                  "library call) -> pinned host y, every step; steps rotate over three streams so copies overlap "
                   "kernels",
     "three_calls": "pinned host x -> device (torch copy) -> dflash_qmm (C ABI via ctypes) -> pinned host y (torch "
-                   "copy), every step; steps alternate over two streams so copies overlap kernels",
+                   "copy), every step; steps rotate over three streams so copies overlap kernels",
 }
 
 
@@ -599,12 +605,12 @@ def e2e_line(three, host, world, nbytes, steps):
 def e2e_host_entry(dc, dev, x, copies, args, want):
     """Per step ONE library call, dflash_qmm_host through ctypes: it queues the copy of
     pinned host x into its workspace, the matmul and the copy of y to pinned host memory
-    on the step's stream.  Steps alternate between two streams (each with its own
+    on the step's stream.  Steps rotate over E2E_STREAMS streams (each with its own
     workspace and host output), as in e2e_through_abi.  Before timing, one call per weight
     copy must reproduce dflash_qmm's bits (`want`)."""
     import ctypes
     import torch
-    streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+    streams = [torch.cuda.Stream(dev) for _ in range(E2E_STREAMS)]
     x_h = torch.from_numpy(np.ascontiguousarray(x[:M]).view(np.int16)).view(torch.bfloat16).pin_memory()
     fn = dc.lib.dflash_qmm_host
     lanes = []
@@ -618,14 +624,14 @@ def e2e_host_entry(dc, dev, x, copies, args, want):
     R = len(copies)
     torch.cuda.synchronize(dev)
     for r in range(R):
-        lane = lanes[r & 1]
+        lane = lanes[r % E2E_STREAMS]
         dc.check(fn(*lane["args"][r]))
         lane["stream"].synchronize()
         if not torch.equal(lane["y_h"], want[r]):
             raise RuntimeError(f"dflash_qmm_host differs from dflash_qmm on weight copy {r}")
 
     def step(i):
-        lane = lanes[i & 1]
+        lane = lanes[i % E2E_STREAMS]
         dc.check(fn(*lane["args"][i % R]))
 
     for i in range(min(args.warmup, 200)):
@@ -634,12 +640,14 @@ def e2e_host_entry(dc, dev, x, copies, args, want):
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(streams[0])
-    streams[1].wait_event(t0)
+    for st in streams[1:]:
+        st.wait_event(t0)
     for i in range(args.steps):
         step(i)
-    done = torch.cuda.Event()
-    done.record(streams[1])
-    streams[0].wait_event(done)
+    for st in streams[1:]:
+        done = torch.cuda.Event()
+        done.record(st)
+        streams[0].wait_event(done)
     t1.record(streams[0])
     torch.cuda.synchronize(dev)
     return {"ms": t0.elapsed_time(t1), "h2d": M * K * 2, "d2h": M * N * 2}
@@ -648,12 +656,12 @@ def e2e_host_entry(dc, dev, x, copies, args, want):
 def e2e_through_abi(dc, dev, x, copies, args, world):
     """Per step: pinned host x -> device, dflash_qmm through the C ABI (ctypes, the
     library's entry point itself), device y -> pinned host; CUDA events around the K
-    steps.  Steps alternate between two streams, each with its own device buffers,
+    steps.  Steps rotate over E2E_STREAMS streams, each with its own device buffers,
     workspace and host output, so one step's copies overlap another step's kernels, as
     a serving host would pipeline consecutive requests."""
     import ctypes
     import torch
-    streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+    streams = [torch.cuda.Stream(dev) for _ in range(E2E_STREAMS)]
     x_h = torch.from_numpy(np.ascontiguousarray(x[:M]).view(np.int16)).view(torch.bfloat16).pin_memory()
     lanes = []
     for st in streams:
@@ -668,7 +676,7 @@ def e2e_through_abi(dc, dev, x, copies, args, world):
     R = len(copies)
 
     def step(i):
-        lane = lanes[i & 1]
+        lane = lanes[i % E2E_STREAMS]
         with torch.cuda.stream(lane["stream"]):
             lane["x_d"].copy_(x_h, non_blocking=True)
             dc.check(dc.lib.dflash_qmm(*lane["args"][i % R]))
@@ -681,12 +689,14 @@ def e2e_through_abi(dc, dev, x, copies, args, world):
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(streams[0])
-    streams[1].wait_event(t0)
+    for st in streams[1:]:
+        st.wait_event(t0)
     for i in range(steps):
         step(i)
-    done = torch.cuda.Event()
-    done.record(streams[1])
-    streams[0].wait_event(done)
+    for st in streams[1:]:
+        done = torch.cuda.Event()
+        done.record(st)
+        streams[0].wait_event(done)
     t1.record(streams[0])
     torch.cuda.synchronize(dev)
     return {"ms": t0.elapsed_time(t1), "h2d": M * K * 2, "d2h": M * N * 2}
