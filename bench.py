@@ -574,16 +574,17 @@ def gpu_ids(world):
 
 # Streams the e2e legs rotate over.  The 278 KB copy of y back to the host takes 8.4 us of
 # the single device-to-host copy engine per step; with two streams it and the next steps'
-# copies pipeline poorly against the kernels (24.0 us per step), with three they hide
-# behind them (18.7 us, against 15-16.5 us for the kernels alone).
-E2E_STREAMS = 3
+# copies pipeline poorly against the kernels (24.1 us per step), with three better
+# (17.9 us), with four they hide behind the kernels entirely (15.6 us, the kernels alone
+# on the same streams: 15.2 us).
+E2E_STREAMS = 4
 
 E2E_PATHS = {
     "host_entry": "pinned host x -> dflash_qmm_host (C ABI via ctypes: copy in, matmul, copy out queued by one "
-                  "library call) -> pinned host y, every step; steps rotate over three streams so copies overlap "
+                  "library call) -> pinned host y, every step; steps rotate over four streams so copies overlap "
                   "kernels",
     "three_calls": "pinned host x -> device (torch copy) -> dflash_qmm (C ABI via ctypes) -> pinned host y (torch "
-                   "copy), every step; steps rotate over three streams so copies overlap kernels",
+                   "copy), every step; steps rotate over four streams so copies overlap kernels",
 }
 
 

@@ -516,8 +516,8 @@ __global__ void attn_prep_kernel(uint16_t* __restrict__ qkv, int ld, const uint1
     for (int c = 0; c < CH; ++c) dst[lane + 32 * c] = to_bf(v[c]);
 }
 
-// Decode attention of the block.  A cluster of kSplit CTAs serves one (kv head, token t):
-// the keys 0 .. pos0 + t that token t sees are cut into kSplit contiguous ranges, one per
+// Decode attention of the block.  A cluster of SPLIT CTAs serves one (kv head, token t):
+// the keys 0 .. pos0 + t that token t sees are cut into SPLIT contiguous ranges, one per
 // CTA, and each CTA runs an online softmax over its range for all G = hq / hkv q heads
 // that read this kv head, in chunks of kChunk keys.  Lane l holds dims [l CH, l CH + CH)
 // of every row it touches, so each key or value row is one coalesced read.
@@ -536,8 +536,9 @@ __global__ void attn_prep_kernel(uint16_t* __restrict__ qkv, int ld, const uint1
 // chunk or CTA range may then hold no visible key: its exponent base stays finite (0)
 // so its weights come out 0, and the merge gives such a CTA weight 0 (t itself is
 // always visible, so some CTA holds a finite maximum).
-constexpr int kSplit = 4;
-constexpr int kChunk = 256;
+constexpr int kSplit = 4;       // CTAs per (kv head, token) ...
+constexpr int kSplitSmall = 8;  // ... or, when the grid would leave most SMs idle, twice as many
+constexpr int kChunk = 384;     // keys a CTA scores per pass (a 1032-key context in one pass at SPLIT 4)
 constexpr int kMaxG = 8;
 constexpr int kUnroll = 4;
 
@@ -573,7 +574,7 @@ __device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
     return v[0];
 }
 
-template <int CH, int GP>
+template <int CH, int GP, int SPLIT>
 __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __restrict__ qkv, int ld,
                                                           const uint16_t* __restrict__ cache_k,
                                                           const uint16_t* __restrict__ cache_v,
@@ -586,7 +587,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __rest
     static_assert(GP <= kMaxG && KU * CH <= 64, "score registers");
     __shared__ float s_p[kMaxG][kChunk];
     __shared__ __align__(16) float s_red[4][kMaxG][d];  // warp partials; s_red[0] ends as the CTA's p V
-    __shared__ float s_m[kMaxG], s_l[kMaxG], s_corr[kMaxG], s_f[kSplit][kMaxG], s_den[kMaxG];
+    __shared__ float s_m[kMaxG], s_l[kMaxG], s_corr[kMaxG], s_f[SPLIT][kMaxG], s_den[kMaxG];
     chain_in();
     if (position) {  // the cache position from device memory (a graph replayed at a new context)
         pos0 = *position;
@@ -596,11 +597,11 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __rest
         }
     }
     const int G = hq / hkv;
-    const int kvh = blockIdx.x / kSplit, t = blockIdx.y;
+    const int kvh = blockIdx.x / SPLIT, t = blockIdx.y;
     const uint32_t rank = cluster_rank();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = pos0 + t + 1;
-    const int k0 = (int)((long long)n * rank / kSplit), k1 = (int)((long long)n * (rank + 1) / kSplit);
+    const int k0 = (int)((long long)n * rank / SPLIT), k1 = (int)((long long)n * (rank + 1) / SPLIT);
     const uint32_t visible = parents ? tree_walk(parents, t).path : 0u;  // tree rounds: t's path rows
 
     float q[GP][CH];
@@ -732,15 +733,15 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __rest
     // merge weights per head: f_r = exp(m_r - max), den = sum_r f_r l_r
     if (threadIdx.x < G) {
         const int g = threadIdx.x;
-        float mr[kSplit], mx = -INFINITY;
+        float mr[SPLIT], mx = -INFINITY;
 #pragma unroll
-        for (int r = 0; r < kSplit; ++r) {
+        for (int r = 0; r < SPLIT; ++r) {
             mr[r] = ld_shared_cluster_f32(map_to_rank(smem_u32(&s_m[g]), r));
             mx = fmaxf(mx, mr[r]);
         }
         float den = 0.f;
 #pragma unroll
-        for (int r = 0; r < kSplit; ++r) {
+        for (int r = 0; r < SPLIT; ++r) {
             const float f = mr[r] == -INFINITY ? 0.f : __expf(mr[r] - mx);
             s_f[r][g] = f;
             den = fmaf(f, ld_shared_cluster_f32(map_to_rank(smem_u32(&s_l[g]), r)), den);
@@ -748,12 +749,12 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const uint16_t* __rest
         s_den[g] = den;
     }
     __syncthreads();
-    // this CTA finishes outputs [rank, rank + kSplit, ...) of the G d
-    for (int idx = (int)rank + kSplit * threadIdx.x; idx < G * d; idx += kSplit * blockDim.x) {
+    // this CTA finishes outputs [rank, rank + SPLIT, ...) of the G d
+    for (int idx = (int)rank + SPLIT * threadIdx.x; idx < G * d; idx += SPLIT * blockDim.x) {
         const int g = idx / d, ee = idx - g * d;
         float num = 0.f;
 #pragma unroll
-        for (int r = 0; r < kSplit; ++r)
+        for (int r = 0; r < SPLIT; ++r)
             num = fmaf(s_f[r][g], ld_shared_cluster_f32(map_to_rank(smem_u32(&s_red[0][g][ee]), r)), num);
         const int h = kvh * G + g;
         const float gt = bf(qkv[(size_t)t * ld + (size_t)(hq + h) * d + ee]);
@@ -1067,7 +1068,13 @@ static int attn_decode(const dflash_bf16* qkv, int ld, const dflash_bf16* cache_
     if (!aligned16(cache_k) || !aligned16(cache_v) || !aligned16(qkv) || (ld * 2) % 16)
         return fail(DFLASH_ERR_MISALIGNED, "dflash_stack_attn_decode: qkv, its row stride and the caches must be "
                                            "16-byte aligned");
-    const dim3 grid(hkv * stack::kSplit, M), block(256);
+    int dev = 0;
+    DFLASH_CUDA_TRY(cudaGetDevice(&dev));
+    // twice the CTAs per (kv head, token) while the grid stays within half the SMs (measured:
+    // 64 CTAs of 8 beat 32 of 4 by a third; 128 of 8 lose to 64 of 4)
+    const bool small = 2LL * hkv * stack::kSplitSmall * M <= sm_count(dev);
+    const int split = small ? stack::kSplitSmall : stack::kSplit;
+    const dim3 grid(hkv * split, M), block(256);
     cudaStream_t s = as_stream(stream);
     const int G = hq / hkv;
     const int gmin = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;  // heads padded to a power of two
@@ -1076,8 +1083,12 @@ static int attn_decode(const dflash_bf16* qkv, int ld, const dflash_bf16* cache_
     cudaError_t e = cudaErrorInvalidValue;
 #define DFLASH_ATTN_CASE(CH, GP)                                                                                   \
     if (ch == CH && gp == GP)                                                                                      \
-        e = launch_chained(stack::attn_decode_kernel<CH, GP>, grid, block, 0, s, stack::kSplit, qkv, ld, cache_k,    \
-                           cache_v, out, hq, hkv, pos0, max_len, scale, parents, position);
+        e = small ? launch_chained(stack::attn_decode_kernel<CH, GP, stack::kSplitSmall>, grid, block, 0, s,        \
+                                   stack::kSplitSmall, qkv, ld, cache_k, cache_v, out, hq, hkv, pos0, max_len, scale, \
+                                   parents, position)                                                              \
+                  : launch_chained(stack::attn_decode_kernel<CH, GP, stack::kSplit>, grid, block, 0, s,             \
+                                   stack::kSplit, qkv, ld, cache_k, cache_v, out, hq, hkv, pos0, max_len, scale,    \
+                                   parents, position);
     DFLASH_ATTN_CASE(2, 1) DFLASH_ATTN_CASE(2, 2) DFLASH_ATTN_CASE(2, 4) DFLASH_ATTN_CASE(2, 8)
     DFLASH_ATTN_CASE(4, 2) DFLASH_ATTN_CASE(4, 4) DFLASH_ATTN_CASE(4, 8)
     DFLASH_ATTN_CASE(8, 4) DFLASH_ATTN_CASE(8, 8)

@@ -444,3 +444,37 @@ def test_cuda_stack_tp2_matches_tp1_reference(cuda, tmp_path):
         assert closeness(res[mode]["eager"].float().numpy(), ref) <= 3e-2
     assert torch.equal(res["peer"]["eager"], res["nccl"]["eager"])
     assert torch.equal(res["peer"]["tokens"], res["nccl"]["tokens"])
+
+
+# ----------------------------------------------------------------------------- decode attention (GPU)
+@pytest.mark.gpu
+@pytest.mark.parametrize("hq,hkv,M,ctx", [(3, 1, 8, 1024), (6, 1, 8, 700), (24, 4, 8, 1024), (12, 2, 8, 300),
+                                          (4, 2, 1, 40)])
+def test_decode_attention_matches_fp32_reference(dc, cuda, hq, hkv, M, ctx):
+    """dflash_stack_attn_decode against plain fp32 attention: token t of the block sees the
+    cached keys 0 .. ctx + t (its own and earlier block rows included), head h reads kv head
+    h / (hq / hkv), and the output is gated by sigmoid(gate).  The shapes cover both cluster
+    widths (8 CTAs per kv head and token when the grid is small, 4 otherwise) and one or
+    two passes over a CTA's keys."""
+    d = 256
+    g = torch.Generator(device=cuda).manual_seed(hq * 100 + hkv * 10 + M)
+    max_len = ctx + M + 16
+    qkv = torch.randn(M, (2 * hq + 2 * hkv) * d, generator=g, device=cuda).to(torch.bfloat16)
+    ck = torch.randn(hkv, max_len, d, generator=g, device=cuda).to(torch.bfloat16)
+    cv = torch.randn(hkv, max_len, d, generator=g, device=cuda).to(torch.bfloat16)
+    out = torch.empty(M, hq * d, dtype=torch.bfloat16, device=cuda)
+    scale = d ** -0.5
+    dc.stack_attn_decode(qkv, ck, cv, out, hq, hkv, ctx, scale)
+    torch.cuda.synchronize()
+    q = qkv[:, :hq * d].float().view(M, hq, d)
+    gate = qkv[:, hq * d:2 * hq * d].float().view(M, hq, d)
+    want = torch.empty(M, hq, d, device=cuda)
+    for t in range(M):
+        for h in range(hq):
+            j = h // (hq // hkv)
+            k = ck[j, :ctx + t + 1].float()
+            v = cv[j, :ctx + t + 1].float()
+            p = torch.softmax((k @ q[t, h]) * scale, dim=0)
+            want[t, h] = (p @ v) * torch.sigmoid(gate[t, h])
+    assert closeness(out.float().view(M, hq, d).cpu().numpy(), want.cpu().numpy()) <= 1e-2
+    assert dc.device_error() == 0
