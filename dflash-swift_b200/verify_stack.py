@@ -695,6 +695,70 @@ class VerifyStack:
 
 # ----------------------------------------------------------------------------- benchmark
 
+# Roles of the library calls in a forward, for the per-role time split of phase_times().
+PHASES = {
+    "qmm": "quantized projections", "qmm_ex": "quantized projections",
+    "stack_add_rmsnorm": "residual add + RMSNorm (+ all-reduce)",
+    "stack_add_rmsnorm_reduce": "residual add + RMSNorm (+ all-reduce)",
+    "stack_gdn_conv_gates": "gated-delta conv + gates", "gdn_step": "gated-delta step",
+    "gdn_step_tree": "gated-delta step", "stack_gated_norm": "gated norm",
+    "stack_attn_prep": "attention prep", "stack_attn_decode": "decode attention",
+}
+
+
+def phase_times(stack, hidden, rounds: int = 3, hold_ms: float = 60.0):
+    """Device time of one eager forward split by the role of each library call: every call is
+    bracketed by CUDA events on the current stream (which also serialises the calls, so the
+    parts add up to more than a graph-replayed forward; read them as shares).  A sleep kernel
+    of `hold_ms` at the head of the stream lets the host enqueue the whole forward before
+    the device starts it, so no span includes time the device spent waiting for the host.
+    The last of `rounds` forwards is kept; with several ranks each part is the max over the
+    ranks."""
+    dc = stack.dc
+    saved = {name: getattr(dc, name) for name in PHASES}
+    log = []
+
+    def wrap(name, fn):
+        def timed(*a, **k):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            r = fn(*a, **k)
+            e1.record()
+            log.append((PHASES[name], e0, e1))
+            return r
+        return timed
+
+    try:
+        for name, fn in saved.items():
+            setattr(dc, name, wrap(name, fn))
+        clock_khz = torch.cuda.get_device_properties(stack.device).clock_rate
+        for _ in range(rounds):
+            log.clear()
+            if stack.world > 1:
+                torch.distributed.barrier(group=stack.pg)
+            torch.cuda._sleep(int(hold_ms * clock_khz))
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record()
+            stack.forward(hidden)
+            t1.record()
+            torch.cuda.synchronize(stack.device)
+    finally:
+        for name, fn in saved.items():
+            setattr(dc, name, fn)
+    parts = {}
+    for role, e0, e1 in log:
+        parts[role] = parts.get(role, 0.0) + e0.elapsed_time(e1) * 1000.0
+    roles = sorted(set(PHASES.values()))
+    vec = torch.tensor([parts.get(r, 0.0) for r in roles] + [t0.elapsed_time(t1) * 1000.0], device=stack.device)
+    if stack.world > 1:
+        torch.distributed.all_reduce(vec, op=torch.distributed.ReduceOp.MAX, group=stack.pg)
+    vec = vec.tolist()
+    total = vec[-1]
+    return {"eager_forward_us": round(total, 1),
+            "parts_us": {r: round(v, 1) for r, v in zip(roles, vec[:-1]) if v > 0},
+            "parts_share": {r: round(v / total, 3) for r, v in zip(roles, vec[:-1]) if v > 0}}
+
+
 def _dist_env():
     return int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), \
         int(os.environ.get("LOCAL_RANK", "0"))
@@ -713,6 +777,8 @@ def main(argv=None) -> int:
                          "RMSNorm; nccl: torch.distributed.all_reduce")
     ap.add_argument("--gdn-key-heads", type=int, default=None,
                     help="gated-delta q / k heads, each shared by gdn_heads / this many value heads")
+    ap.add_argument("--phase-times", action="store_true",
+                    help="also report one eager forward's device time split by the role of each library call")
     ap.add_argument("--tree", default=None,
                     help="verify a speculative tree instead of a chain: comma-separated parent rows, one per "
                          "block row (-1 for the anchor), e.g. -1,0,0,1,1,2,3,5")
@@ -779,6 +845,10 @@ def main(argv=None) -> int:
         }), flush=True)
     del g
     stack.graph = None
+    if args.phase_times:
+        split = phase_times(stack, hidden)
+        if rank == 0:
+            print(json.dumps({"phase_times": split, "tp": world}), flush=True)
     if world > 1:
         stack.close()
         torch.distributed.barrier()
