@@ -15,63 +15,79 @@
 // which is  S <- alpha S;  S <- S + beta (v - S k) k^T  with the decay applied first.
 // The work is bound by reading the snapshot and writing the new state once
 // (2 * 4 * dv * dk bytes per head).  Each row is held in registers by 8 threads (16 floats
-// each for dk = 128) for all positions, with 128-byte coalesced row access, and each
-// thread holds four rows (g, g + 8, g + 16, g + 24 of its block's 32): one shared-memory
-// read of k_t serves all four, one transposed shuffle reduction sums their dot products,
-// and the four rows' recurrences are independent chains the scheduler interleaves.  The
-// arithmetic is packed fp32 (two lanes per FMA).  k (and q), the block's v, alpha and beta
-// of the positions are staged in shared memory while the state loads are in flight, so
-// the position loop reads no global memory.
+// each for dk = 128) for all positions, with 128-byte coalesced row access.  On large grids
+// each thread holds four rows (g, g + 8, g + 16, g + 24 of its block's 32): one
+// shared-memory read of k_t serves all four, one transposed shuffle reduction sums their
+// dot products, and the four rows' recurrences are independent chains the scheduler
+// interleaves.  Grids too small to fill the SMs that way (a single layer's step at a
+// verify block's 8 positions) hold one row per thread in blocks of 8 rows instead: four
+// times the blocks and a quarter of the per-position chain.  The sums of a row use the
+// same lane tree either way, so both layouts produce the same bits.  The arithmetic is
+// packed fp32 (two lanes per FMA).  k (and q), the block's v, alpha and beta of the
+// positions are staged in shared memory while the state loads are in flight, so the
+// position loop reads no global memory.
 #include "common.cuh"
 
 namespace dflash {
 namespace gdn {
 
 constexpr int kRowThreads = 8;                             // threads per state row
-constexpr int kRowsPerBlock = 32;                          // rows of S per block
-constexpr int kRows = 4;                                   // rows a thread holds: g, g + 8, g + 16, g + 24
-constexpr int kRowGroups = kRowsPerBlock / kRows;          // 8
+constexpr int kRowGroups = 8;                              // row groups per block
 constexpr int kBlockThreads = kRowThreads * kRowGroups;    // 64
+constexpr int kRowsPerBlock = 32;                          // rows of S per block, four rows per thread
 constexpr int kMaxPositions = 64;
+constexpr int kStageBatch = 4;                             // global loads per thread per staging round
+static_assert(kMaxPositions <= kBlockThreads, "alpha and beta are staged one position per thread");
 
 struct RowList {
     int32_t r[kMaxPositions];
 };
 
-// Loads 4 consecutive bf16 (8-byte aligned, global or shared) and widens to fp32.
-__device__ __forceinline__ float4 ld_bf16x4(const uint16_t* p) {
-    const uint2 v = *reinterpret_cast<const uint2*>(p);
+// Widens 4 consecutive bf16 (one 8-byte word) to fp32.
+__device__ __forceinline__ float4 widen_bf16x4(const uint2 v) {
     return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u),
                        __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
 }
 
-// v of a row group's kRows rows at one position (one 16-byte shared-memory read).
-struct alignas(16) RowVals {
-    float x[kRows];
+// v of a row group's R rows at one position (one shared-memory read).
+template <int R>
+struct alignas(4 * R) RowVals {
+    float x[R];
 };
 
 // Totals, over the 8 threads of a row group (lanes 8g' .. 8g'+7 of a warp), of the
-// partial dot products a[j] of the group's kRows rows; every lane gets all of them.  A
-// transposed reduction: each of three exchange steps halves the values a lane carries
-// (after the last, lanes 2j and 2j+1 of the group hold the total of row j), then three
-// exchanges hand every lane the other rows' totals.  Every lane ends with the same bits.
-__device__ __forceinline__ void group_sum(float (&a)[kRows]) {
+// partial dot products a[j] of the group's R rows; every lane gets all of them.  Each
+// total is ((a0 + a4) + (a2 + a6)) + ((a1 + a5) + (a3 + a7)) over the group's lanes, for
+// one row or four.  Four rows: a transposed reduction, where each of three exchange steps
+// halves the values a lane carries (after the last, lanes 2j and 2j+1 of the group hold
+// the total of row j), then three exchanges hand every lane the other rows' totals.
+// Every lane ends with the same bits.
+template <int R>
+__device__ __forceinline__ void group_sum(float (&a)[R]) {
     const unsigned kAll = 0xffffffffu;
-    const bool b2 = threadIdx.x & 4, b1 = threadIdx.x & 2;
-    float k0 = b2 ? a[2] : a[0], k1 = b2 ? a[3] : a[1];  // rows kept: {0, 1} or {2, 3}
-    k0 += __shfl_xor_sync(kAll, b2 ? a[0] : a[2], 4);
-    k1 += __shfl_xor_sync(kAll, b2 ? a[1] : a[3], 4);
-    float t = b1 ? k1 : k0;  // row 2 b2 + b1
-    t += __shfl_xor_sync(kAll, b1 ? k0 : k1, 2);
-    t += __shfl_xor_sync(kAll, t, 1);
-    const float x2 = __shfl_xor_sync(kAll, t, 2);  // row 2 b2 + !b1
-    const float x4 = __shfl_xor_sync(kAll, t, 4);  // row 2 !b2 + b1
-    const float x6 = __shfl_xor_sync(kAll, t, 6);  // row 2 !b2 + !b1
-    const float lo = b1 ? x2 : t, hi = b1 ? t : x2, olo = b1 ? x6 : x4, ohi = b1 ? x4 : x6;
-    a[0] = b2 ? olo : lo;
-    a[1] = b2 ? ohi : hi;
-    a[2] = b2 ? lo : olo;
-    a[3] = b2 ? hi : ohi;
+    if constexpr (R == 1) {
+        a[0] += __shfl_xor_sync(kAll, a[0], 4);
+        a[0] += __shfl_xor_sync(kAll, a[0], 2);
+        a[0] += __shfl_xor_sync(kAll, a[0], 1);
+        return;
+    } else {
+        static_assert(R == 4, "one or four rows per thread");
+        const bool b2 = threadIdx.x & 4, b1 = threadIdx.x & 2;
+        float k0 = b2 ? a[2] : a[0], k1 = b2 ? a[3] : a[1];  // rows kept: {0, 1} or {2, 3}
+        k0 += __shfl_xor_sync(kAll, b2 ? a[0] : a[2], 4);
+        k1 += __shfl_xor_sync(kAll, b2 ? a[1] : a[3], 4);
+        float t = b1 ? k1 : k0;  // row 2 b2 + b1
+        t += __shfl_xor_sync(kAll, b1 ? k0 : k1, 2);
+        t += __shfl_xor_sync(kAll, t, 1);
+        const float x2 = __shfl_xor_sync(kAll, t, 2);  // row 2 b2 + !b1
+        const float x4 = __shfl_xor_sync(kAll, t, 4);  // row 2 !b2 + b1
+        const float x6 = __shfl_xor_sync(kAll, t, 6);  // row 2 !b2 + !b1
+        const float lo = b1 ? x2 : t, hi = b1 ? t : x2, olo = b1 ? x6 : x4, ohi = b1 ? x4 : x6;
+        a[0] = b2 ? olo : lo;
+        a[1] = b2 ? ohi : hi;
+        a[2] = b2 ? lo : olo;
+        a[3] = b2 ? hi : ohi;
+    }
 }
 
 // Packed fp32 arithmetic (two lanes per instruction, sm_100): a float4 chunk of a row is
@@ -80,35 +96,35 @@ __device__ __forceinline__ float2 lo2(const float4& v) { return make_float2(v.x,
 __device__ __forceinline__ float2 hi2(const float4& v) { return make_float2(v.z, v.w); }
 __device__ __forceinline__ float4 cat4(const float2& a, const float2& b) { return make_float4(a.x, a.y, b.x, b.y); }
 
-// Dot products of the thread's kRows row slices with CH chunks of a vector, summed over
-// the row group, into d.
-template <int CH>
-__device__ __forceinline__ void rows_dot(const float4 (&s)[kRows][CH], const float4 (&x)[CH], float (&d)[kRows]) {
-    float2 acc[kRows];
+// Dot products of the thread's R row slices with CH chunks of a vector, summed over the
+// row group, into d.
+template <int CH, int R>
+__device__ __forceinline__ void rows_dot(const float4 (&s)[R][CH], const float4 (&x)[CH], float (&d)[R]) {
+    float2 acc[R];
 #pragma unroll
-    for (int j = 0; j < kRows; ++j) acc[j] = make_float2(0.f, 0.f);
+    for (int j = 0; j < R; ++j) acc[j] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
 #pragma unroll
-        for (int j = 0; j < kRows; ++j) acc[j] = __ffma2_rn(lo2(s[j][c]), lo2(x[c]), acc[j]);
+        for (int j = 0; j < R; ++j) acc[j] = __ffma2_rn(lo2(s[j][c]), lo2(x[c]), acc[j]);
 #pragma unroll
-        for (int j = 0; j < kRows; ++j) acc[j] = __ffma2_rn(hi2(s[j][c]), hi2(x[c]), acc[j]);
+        for (int j = 0; j < R; ++j) acc[j] = __ffma2_rn(hi2(s[j][c]), hi2(x[c]), acc[j]);
     }
 #pragma unroll
-    for (int j = 0; j < kRows; ++j) d[j] = acc[j].x + acc[j].y;
-    group_sum(d);
+    for (int j = 0; j < R; ++j) d[j] = acc[j].x + acc[j].y;
+    group_sum<R>(d);
 }
 
-// One position of the recurrence for the kRows row slices a thread holds: s the rows'
-// CH float4 chunks, k the matching chunks of k_t (fp32), v the rows' v_t.
-template <int CH>
-__device__ __forceinline__ void rows_step(float4 (&s)[kRows][CH], const float4 (&k)[CH], const RowVals& v,
+// One position of the recurrence for the R row slices a thread holds: s the rows' CH
+// float4 chunks, k the matching chunks of k_t (fp32), v the rows' v_t.
+template <int CH, int R>
+__device__ __forceinline__ void rows_step(float4 (&s)[R][CH], const float4 (&k)[CH], const RowVals<R>& v,
                                           float alpha, float beta) {
-    float dot[kRows];
-    rows_dot<CH>(s, k, dot);
+    float dot[R];
+    rows_dot<CH, R>(s, k, dot);
     const float2 aa = make_float2(alpha, alpha);
 #pragma unroll
-    for (int j = 0; j < kRows; ++j) {
+    for (int j = 0; j < R; ++j) {
         const float bu = beta * (v.x[j] - alpha * dot[j]);
         const float2 bb = make_float2(bu, bu);
 #pragma unroll
@@ -134,10 +150,10 @@ struct ReplayParams {
     int k_heads;              // heads of q and k (0: = heads); value head h reads key head h / (heads / k_heads)
 };
 
-// grid: (dv / 32, heads, layers) — (dv / 32, heads, width) for a tree step, block z taking
-// the z-th leaf of the tree in row order; block: 64 threads = 8 row groups x 8 threads,
-// group g holding rows g, g + 8, g + 16 and g + 24 of the block's 32.  Thread q of a
-// group holds float4 chunks q, q+8, q+16, ... of its rows (dk = 32 * CH).
+// grid: (dv / (8 R), heads, layers) — (dv / (8 R), heads, width) for a tree step, block z
+// taking the z-th leaf of the tree in row order; block: 64 threads = 8 row groups x 8
+// threads, group g holding rows g, g + 8, ..., g + 8 (R - 1) of the block's 8 R (R = 4 or
+// 1).  Thread q of a group holds float4 chunks q, q+8, q+16, ... of its rows (dk = 32 * CH).
 //
 // Tree step (TREE): the recurrence of a tree row is that of its root-to-row path, so
 // each block runs the chain of one leaf's path from the same pre-round state and writes
@@ -146,38 +162,39 @@ struct ReplayParams {
 // No state is written: after the round, dflash_gdn_replay rebuilds it from the snapshot
 // over the accepted path.
 // Dynamic shared memory of a block over n positions: k (and q times q_scale) widened to
-// fp32 [n][dk], the block's 32 values of v per position (fp32, stored as the quadruples a
+// fp32 [n][dk], the block's rpb values of v per position (fp32, stored as the R-tuples a
 // row group reads), alpha and beta.  Staged once, so the position loop touches no global
 // memory and the snapshot loads are the only long waits.
-__host__ __device__ inline size_t smem_bytes(int n, int dk, bool with_q) {
-    return (size_t)n * dk * 4 * (with_q ? 2 : 1) + (size_t)n * kRowsPerBlock * 4 + (size_t)n * 8;
+__host__ __device__ inline size_t smem_bytes(int n, int dk, bool with_q, int rpb) {
+    return (size_t)n * dk * 4 * (with_q ? 2 : 1) + (size_t)n * rpb * 4 + (size_t)n * 8;
 }
 
 // What a launch computes: the rollback replay (state only), the chain step (outputs and
 // state) or the tree step (outputs only).
 enum Mode { kReplay = 0, kStep = 1, kTree = 2 };
 
-template <int CH, int MODE>
+template <int CH, int MODE, int R>
 __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constant__ ReplayParams p) {
     constexpr int DK = 32 * CH;
+    constexpr int RPB = kRowGroups * R;  // rows of S per block
     constexpr bool TREE = MODE == kTree;
     constexpr bool want_out = MODE != kReplay;
     const int n = TREE ? p.width : p.keep;  // positions staged
     extern __shared__ __align__(16) uint8_t dyn[];
     float(*ks)[DK] = reinterpret_cast<float(*)[DK]>(dyn);
     float(*qs_sh)[DK] = reinterpret_cast<float(*)[DK]>(dyn + (size_t)n * DK * 4);
-    // vs[r][g] = v of rows g, g + 8, g + 16, g + 24 at position r
-    RowVals(*vs)[kRowGroups] =
-        reinterpret_cast<RowVals(*)[kRowGroups]>(dyn + (size_t)n * DK * 4 * (want_out ? 2 : 1));
-    float2* ab = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(vs) + (size_t)n * kRowsPerBlock * 4);
+    // vs[r][g] = v of rows g, g + 8, ..., g + 8 (R - 1) at position r
+    RowVals<R>(*vs)[kRowGroups] =
+        reinterpret_cast<RowVals<R>(*)[kRowGroups]>(dyn + (size_t)n * DK * 4 * (want_out ? 2 : 1));
+    float2* ab = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(vs) + (size_t)n * RPB * 4);
     __shared__ int32_t path_rows[TREE ? kMaxTreeRows : 1];
     __shared__ uint32_t path_info[2];  // tree: rows on this block's path, rows it writes
 
     const int layer = TREE ? 0 : blockIdx.z, h = blockIdx.y;
-    const int row0 = blockIdx.x * kRowsPerBlock;
+    const int row0 = blockIdx.x * RPB;
     const int tid = threadIdx.x;
     const int g = tid / kRowThreads, qd = tid % kRowThreads;
-    const int row = row0 + g;  // and row + 8, row + 16, row + 24
+    const int row = row0 + g;  // and row + 8, ..., row + 8 (R - 1)
 
     int keep = p.keep;
     if constexpr (TREE) {
@@ -213,36 +230,67 @@ __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constan
     const size_t head_base = (((size_t)layer * p.heads + h) * p.dv + row) * DK;
     const float4* src = reinterpret_cast<const float4*>(p.snapshot + head_base) + qd;
     constexpr int kNext = kRowGroups * DK / 4;  // float4 offset of the group's next row
-    float4 s[kRows][CH];
+    float4 s[R][CH];
 #pragma unroll
-    for (int j = 0; j < kRows; ++j)
+    for (int j = 0; j < R; ++j)
 #pragma unroll
         for (int c = 0; c < CH; ++c)  // every leaf's block of a tree step reads the same state: keep it in L2 there
             s[j][c] = TREE ? __ldg(src + j * kNext + c * kRowThreads) : __ldcs(src + j * kNext + c * kRowThreads);
 
-    // Stage k (and q), alpha, beta of the replayed positions.  q and k have k_heads heads,
-    // each shared by heads / k_heads consecutive value heads.
+    // Stage k (and q), v, alpha and beta of the replayed positions, in rounds of up to
+    // kStageBatch loads of each kind per thread.  A round issues all its global loads before
+    // its shared-memory stores, so it costs one memory latency, and the first overlaps the
+    // state loads above (a verify block of 8 positions takes one round).  q and k have
+    // k_heads heads, each shared by heads / k_heads consecutive value heads; alpha and beta
+    // are [width, heads] per layer.
     const int kh = p.k_heads > 0 ? p.k_heads : p.heads;
     const int hk = h / (p.heads / kh);
-    const size_t pos_stride = (size_t)p.heads;  // [width, H] per layer for alpha/beta
-    for (int idx = tid; idx < keep * (DK / 4); idx += kBlockThreads) {
-        const int r = idx / (DK / 4), c4 = (idx % (DK / 4)) * 4;
-        const size_t base = (((size_t)layer * p.width + row_at(r)) * kh + hk) * DK + c4;
-        *reinterpret_cast<float4*>(&ks[r][c4]) = ld_bf16x4(reinterpret_cast<const uint16_t*>(p.k + base));
-        if (want_out) {
-            const float4 qv = ld_bf16x4(reinterpret_cast<const uint16_t*>(p.q + base));
-            *reinterpret_cast<float4*>(&qs_sh[r][c4]) =
-                make_float4(qv.x * p.q_scale, qv.y * p.q_scale, qv.z * p.q_scale, qv.w * p.q_scale);
+    const int nk = keep * (DK / 4), nv = keep * RPB;
+    const uint16_t* kbits = reinterpret_cast<const uint16_t*>(p.k);
+    const uint16_t* qbits = reinterpret_cast<const uint16_t*>(p.q);
+    const uint16_t* vbits = reinterpret_cast<const uint16_t*>(p.v);
+    for (int i0 = 0; i0 < nk || i0 < nv; i0 += kStageBatch * kBlockThreads) {
+        uint2 kr[kStageBatch], qr[kStageBatch];
+        uint32_t vr[kStageBatch];
+#pragma unroll
+        for (int u = 0; u < kStageBatch; ++u) {
+            const int idx = i0 + u * kBlockThreads + tid;
+            if (idx < nk) {
+                const int r = idx / (DK / 4), c4 = (idx % (DK / 4)) * 4;
+                const size_t base = (((size_t)layer * p.width + row_at(r)) * kh + hk) * DK + c4;
+                kr[u] = __ldg(reinterpret_cast<const uint2*>(kbits + base));
+                if (want_out) qr[u] = __ldg(reinterpret_cast<const uint2*>(qbits + base));
+            }
+            if (idx < nv) {
+                const int r = idx / RPB, j = idx % RPB;
+                vr[u] = __ldg(vbits + (((size_t)layer * p.width + row_at(r)) * p.heads + h) * p.dv + row0 + j);
+            }
         }
-    }
-    for (int r = tid; r < keep; r += kBlockThreads) {
-        const size_t ai = ((size_t)layer * p.width + row_at(r)) * pos_stride + h;
-        ab[r] = make_float2(p.alpha[ai], p.beta[ai]);
-    }
-    for (int idx = tid; idx < keep * kRowsPerBlock; idx += kBlockThreads) {  // the block's 32 rows of v
-        const int r = idx / kRowsPerBlock, j = idx % kRowsPerBlock;
-        const size_t vi = (((size_t)layer * p.width + row_at(r)) * p.heads + h) * p.dv + row0 + j;
-        vs[r][j % kRowGroups].x[j / kRowGroups] = __uint_as_float((uint32_t)p.v[vi] << 16);
+        const bool with_ab = i0 == 0 && tid < keep;
+        float a = 0.f, b = 0.f;
+        if (with_ab) {
+            const size_t ai = ((size_t)layer * p.width + row_at(tid)) * p.heads + h;
+            a = __ldg(p.alpha + ai);
+            b = __ldg(p.beta + ai);
+        }
+#pragma unroll
+        for (int u = 0; u < kStageBatch; ++u) {
+            const int idx = i0 + u * kBlockThreads + tid;
+            if (idx < nk) {
+                const int r = idx / (DK / 4), c4 = (idx % (DK / 4)) * 4;
+                *reinterpret_cast<float4*>(&ks[r][c4]) = widen_bf16x4(kr[u]);
+                if (want_out) {
+                    const float4 qv = widen_bf16x4(qr[u]);
+                    *reinterpret_cast<float4*>(&qs_sh[r][c4]) =
+                        make_float4(qv.x * p.q_scale, qv.y * p.q_scale, qv.z * p.q_scale, qv.w * p.q_scale);
+                }
+            }
+            if (idx < nv) {
+                const int r = idx / RPB, j = idx % RPB;
+                vs[r][j % kRowGroups].x[j / kRowGroups] = __uint_as_float(vr[u] << 16);
+            }
+        }
+        if (with_ab) ab[tid] = make_float2(a, b);
     }
 
     __syncthreads();
@@ -253,18 +301,21 @@ __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constan
 #pragma unroll
         for (int c = 0; c < CH; ++c) k[c] = *reinterpret_cast<const float4*>(&ks[r][4 * (qd + c * kRowThreads)]);
         const float2 a_b = ab[r];
-        rows_step<CH>(s, k, vs[r][g], a_b.x, a_b.y);
+        rows_step<CH, R>(s, k, vs[r][g], a_b.x, a_b.y);
         if (want_out) {
             float4 qv[CH];
 #pragma unroll
             for (int c = 0; c < CH; ++c) qv[c] = *reinterpret_cast<const float4*>(&qs_sh[r][4 * (qd + c * kRowThreads)]);
-            float o[kRows];
-            rows_dot<CH>(s, qv, o);
+            float o[R];
+            rows_dot<CH, R>(s, qv, o);
             const int t = row_at(r);
-            bool write = qd < kRows;  // lane j of the group writes row g + 8 j
+            bool write = qd < R;  // lane j of the group writes row g + 8 j
             if constexpr (TREE) write = write && ((path_info[1] >> t) & 1u);
             if (write) {
-                __nv_bfloat16 ob = __float2bfloat16_rn(qd == 0 ? o[0] : qd == 1 ? o[1] : qd == 2 ? o[2] : o[3]);
+                float oj = o[0];
+#pragma unroll
+                for (int j = 1; j < R; ++j) oj = qd == j ? o[j] : oj;
+                __nv_bfloat16 ob = __float2bfloat16_rn(oj);
                 p.out[(((size_t)layer * p.width + t) * p.heads + h) * p.dv + row + qd * kRowGroups] =
                     *reinterpret_cast<uint16_t*>(&ob);
             }
@@ -273,10 +324,23 @@ __global__ void __launch_bounds__(kBlockThreads) gdn_kernel(const __grid_constan
     if constexpr (!TREE) {
         float4* dst = reinterpret_cast<float4*>(p.state_out + head_base) + qd;
 #pragma unroll
-        for (int j = 0; j < kRows; ++j)
+        for (int j = 0; j < R; ++j)
 #pragma unroll
             for (int c = 0; c < CH; ++c) __stcs(dst + j * kNext + c * kRowThreads, s[j][c]);
     }
+}
+
+// The kernels of one rows-per-thread layout, by [dk / 32 -> 0, 1, 2][mode].
+template <int R>
+const void* kernel_for(int dk, int mode) {
+    static const void* const table[3][3] = {
+        {(const void*)gdn_kernel<1, kReplay, R>, (const void*)gdn_kernel<1, kStep, R>,
+         (const void*)gdn_kernel<1, kTree, R>},
+        {(const void*)gdn_kernel<2, kReplay, R>, (const void*)gdn_kernel<2, kStep, R>,
+         (const void*)gdn_kernel<2, kTree, R>},
+        {(const void*)gdn_kernel<4, kReplay, R>, (const void*)gdn_kernel<4, kStep, R>,
+         (const void*)gdn_kernel<4, kTree, R>}};
+    return table[dk == 32 ? 0 : dk == 64 ? 1 : 2][mode];
 }
 
 int launch(const ReplayParams& p, int layers, cudaStream_t stream) {
@@ -286,32 +350,28 @@ int launch(const ReplayParams& p, int layers, cudaStream_t stream) {
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [] {  // up to 64 positions of fp32 k and q: past the 48 KB default
-        const int bytes = (int)smem_bytes(kMaxPositions, 128, true);
-        const void* fns[] = {(const void*)gdn_kernel<1, kReplay>, (const void*)gdn_kernel<2, kReplay>,
-                             (const void*)gdn_kernel<4, kReplay>, (const void*)gdn_kernel<1, kStep>,
-                             (const void*)gdn_kernel<2, kStep>,   (const void*)gdn_kernel<4, kStep>,
-                             (const void*)gdn_kernel<1, kTree>,   (const void*)gdn_kernel<2, kTree>,
-                             (const void*)gdn_kernel<4, kTree>};
-        for (const void* f : fns)
-            if (attr == cudaSuccess) attr = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        const int bytes = (int)smem_bytes(kMaxPositions, 128, true, kRowsPerBlock);
+        for (int dk : {32, 64, 128})
+            for (int m : {kReplay, kStep, kTree})
+                for (const void* f : {kernel_for<4>(dk, m), kernel_for<1>(dk, m)})
+                    if (attr == cudaSuccess)
+                        attr = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     });
     if (attr != cudaSuccess) return fail(DFLASH_ERR_CUDA, "cudaFuncSetAttribute(gdn): %s", cudaGetErrorString(attr));
     if (p.dk != 32 && p.dk != 64 && p.dk != 128) return fail(DFLASH_ERR_UNSUPPORTED, "dk=%d not in {32, 64, 128}", p.dk);
 
-    dim3 grid(p.dv / kRowsPerBlock, p.heads, tree ? p.width : layers);
-    const size_t sm = smem_bytes(tree ? p.width : p.keep, p.dk, with_q);
-    switch (p.dk * 4 + mode) {
-        case 32 * 4 + kReplay: gdn_kernel<1, kReplay><<<grid, kBlockThreads, sm, stream>>>(p); break;
-        case 64 * 4 + kReplay: gdn_kernel<2, kReplay><<<grid, kBlockThreads, sm, stream>>>(p); break;
-        case 128 * 4 + kReplay: gdn_kernel<4, kReplay><<<grid, kBlockThreads, sm, stream>>>(p); break;
-        case 32 * 4 + kStep: gdn_kernel<1, kStep><<<grid, kBlockThreads, sm, stream>>>(p); break;
-        case 64 * 4 + kStep: gdn_kernel<2, kStep><<<grid, kBlockThreads, sm, stream>>>(p); break;
-        case 128 * 4 + kStep: gdn_kernel<4, kStep><<<grid, kBlockThreads, sm, stream>>>(p); break;
-        case 32 * 4 + kTree: gdn_kernel<1, kTree><<<grid, kBlockThreads, sm, stream>>>(p); break;
-        case 64 * 4 + kTree: gdn_kernel<2, kTree><<<grid, kBlockThreads, sm, stream>>>(p); break;
-        case 128 * 4 + kTree: gdn_kernel<4, kTree><<<grid, kBlockThreads, sm, stream>>>(p); break;
-    }
-    DFLASH_CUDA_TRY(cudaGetLastError());
+    // Four rows per thread unless that leaves the grid under two blocks per SM; then one
+    // row per thread, in four times the blocks.
+    const int depth = tree ? p.width : layers;
+    int dev = 0;
+    DFLASH_CUDA_TRY(cudaGetDevice(&dev));
+    const bool one_row = (long long)(p.dv / kRowsPerBlock) * p.heads * depth <= 2LL * sm_count(dev);
+    const int rpb = one_row ? kRowGroups : kRowsPerBlock;
+    const dim3 grid(p.dv / rpb, p.heads, depth);
+    const size_t sm = smem_bytes(tree ? p.width : p.keep, p.dk, with_q, rpb);
+    const void* fn = one_row ? kernel_for<1>(p.dk, mode) : kernel_for<4>(p.dk, mode);
+    void* args[] = {const_cast<ReplayParams*>(&p)};
+    DFLASH_CUDA_TRY(cudaLaunchKernel(fn, grid, dim3(kBlockThreads), args, sm, stream));
     return DFLASH_OK;
 }
 

@@ -219,3 +219,32 @@ def test_multi_layer_replay_matches_per_layer_steps(dc, O, cuda, dk, dv, H, Hk, 
     want, _ = O.gdn_recurrence(c["snapshot"][layer][heads], c["k"][layer][sel][:, kh], c["v"][layer][sel][:, heads],
                                c["alpha"][layer][sel][:, heads], c["beta"][layer][sel][:, heads], keep)
     assert rel_err(out[layer][heads].cpu().numpy(), want) <= REL
+
+
+@pytest.mark.parametrize("dk,dv", [(128, 128), (64, 64), (32, 32)])
+@pytest.mark.parametrize("T", [1, 8, 29])
+def test_row_layouts_agree_bit_for_bit(dc, O, cuda, dk, dv, T):
+    """A step over few heads runs one state row per thread (its grid would leave SMs idle
+    with four) and one over many heads four rows per thread; the heads they share get the
+    same state and outputs, bit for bit."""
+    import torch
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    tiles = dv // 32
+    small = max(1, (2 * sms) // (4 * tiles))           # at most 2 x SMs blocks of 32 rows
+    big = (2 * sms) // tiles + 1                        # more than that
+    c = O.make_gdn_case(1, T, big, dk, dv, seed=13)
+
+    def run(H):
+        g = {key: dev(np.ascontiguousarray(c[key][0][:, :H]), cuda) for key in ("q", "k", "v", "alpha", "beta")}
+        snap = dev(np.ascontiguousarray(c["snapshot"][0][:H]), cuda)
+        st = torch.empty_like(snap)
+        o = torch.empty((T, H, dv), dtype=torch.bfloat16, device=cuda)
+        dc.gdn_step(snap, st, g["q"], g["k"], g["v"], g["alpha"], g["beta"], out=o, q_scale=dk ** -0.5)
+        torch.cuda.synchronize()
+        return st, o
+
+    st_s, o_s = run(small)
+    st_b, o_b = run(big)
+    assert torch.equal(st_s, st_b[:small])
+    assert torch.equal(o_s, o_b[:, :small])
+    assert dc.device_error() == 0
