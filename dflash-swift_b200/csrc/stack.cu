@@ -56,9 +56,21 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // A row is split over a cluster of kNormSplit CTAs of 128 threads (more loads in flight
 // than one CTA per row gives); each thread keeps up to VPT float4 of its part in
 // registers.  The parts' sums of squares are exchanged through distributed shared
-// memory and added in rank order, so every CTA uses the same scale.  Needs H a multiple
-// of 4 kNormSplit, H / kNormSplit <= 512 VPT, delta / w / out 8-byte aligned.
+// memory and added in rank order, so every CTA uses the same scale.  The weight (written by
+// no kernel of the stream) is requested before the wait on the predecessor.  Needs H a
+// multiple of 4 kNormSplit, H / kNormSplit <= 512 VPT, delta / w / out 8-byte aligned.
 constexpr int kNormSplit = 4;
+
+// This thread's VPT words (4 bf16 each) of a norm weight: words base + threadIdx.x + 128 j.
+template <int VPT>
+__device__ __forceinline__ void load_norm_weight(uint2 (&ww)[VPT], const uint16_t* __restrict__ w, int base, int P4) {
+    const uint2* w4 = reinterpret_cast<const uint2*>(w) + base;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+        const int i = threadIdx.x + 128 * j;
+        ww[j] = i < P4 ? __ldg(w4 + i) : make_uint2(0u, 0u);
+    }
+}
 
 template <int VPT>
 __global__ void __launch_bounds__(128) add_rmsnorm_kernel(float* __restrict__ resid, const uint16_t* __restrict__ delta,
@@ -66,9 +78,11 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(float* __restrict__ re
                                                           int H, float eps) {
     __shared__ float red[4];
     __shared__ float part;
-    chain_in();
     const uint32_t rank = cluster_rank();
     const int m = blockIdx.y, P4 = H / (4 * kNormSplit), base = (int)rank * P4;  // float4 units
+    uint2 ww[VPT];
+    load_norm_weight<VPT>(ww, w, base, P4);
+    chain_in();
     float4* r4 = reinterpret_cast<float4*>(resid + (size_t)m * H) + base;
     const uint2* d4 = reinterpret_cast<const uint2*>(delta + (size_t)m * H) + base;
     float4 v[VPT];
@@ -96,16 +110,13 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(float* __restrict__ re
 #pragma unroll
     for (int r = 0; r < kNormSplit; ++r) tot += ld_shared_cluster_f32(map_to_rank(smem_u32(&part), r));
     const float rs = rsqrtf(tot / H + eps);
-    const uint2* w4 = reinterpret_cast<const uint2*>(w) + base;
     uint2* o4 = reinterpret_cast<uint2*>(out + (size_t)m * H) + base;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
         const int i = threadIdx.x + 128 * j;
-        if (i < P4) {
-            const uint2 ww = w4[i];
-            o4[i] = make_uint2(pack_bf2(v[j].x * rs * bf16_lo(ww.x), v[j].y * rs * bf16_hi(ww.x)),
-                               pack_bf2(v[j].z * rs * bf16_lo(ww.y), v[j].w * rs * bf16_hi(ww.y)));
-        }
+        if (i < P4)
+            o4[i] = make_uint2(pack_bf2(v[j].x * rs * bf16_lo(ww[j].x), v[j].y * rs * bf16_hi(ww[j].x)),
+                               pack_bf2(v[j].z * rs * bf16_lo(ww[j].y), v[j].w * rs * bf16_hi(ww[j].y)));
     }
     cluster_sync_all();  // the other CTAs are done reading `part`
 }
@@ -120,11 +131,13 @@ __global__ void __launch_bounds__(128) add_rmsnorm_reduce_kernel(float* __restri
                                                                  uint16_t* __restrict__ out, int M, int H, float eps) {
     __shared__ float red[4];
     __shared__ float part;
+    const uint32_t rank = cluster_rank();
+    const int m = blockIdx.y, P4 = H / (4 * kNormSplit), base = (int)rank * P4;  // float4 units
+    uint2 ww[VPT];
+    load_norm_weight<VPT>(ww, w, base, P4);
     chain_in();
     tp::Header* hdr = static_cast<tp::Header*>(xbase);
     const uint32_t e = hdr->next[set];
-    const uint32_t rank = cluster_rank();
-    const int m = blockIdx.y, P4 = H / (4 * kNormSplit), base = (int)rank * P4;  // float4 units
     float4* r4 = reinterpret_cast<float4*>(resid + (size_t)m * H) + base;
     float4 v[VPT];
     float ss = 0.f;
@@ -173,16 +186,13 @@ __global__ void __launch_bounds__(128) add_rmsnorm_reduce_kernel(float* __restri
 #pragma unroll
     for (int r = 0; r < kNormSplit; ++r) tot += ld_shared_cluster_f32(map_to_rank(smem_u32(&part), r));
     const float rs = rsqrtf(tot / H + eps);
-    const uint2* w4 = reinterpret_cast<const uint2*>(w) + base;
     uint2* o4 = reinterpret_cast<uint2*>(out + (size_t)m * H) + base;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
         const int i = threadIdx.x + 128 * j;
-        if (i < P4) {
-            const uint2 ww = w4[i];
-            o4[i] = make_uint2(pack_bf2(v[j].x * rs * bf16_lo(ww.x), v[j].y * rs * bf16_hi(ww.x)),
-                               pack_bf2(v[j].z * rs * bf16_lo(ww.y), v[j].w * rs * bf16_hi(ww.y)));
-        }
+        if (i < P4)
+            o4[i] = make_uint2(pack_bf2(v[j].x * rs * bf16_lo(ww[j].x), v[j].y * rs * bf16_hi(ww[j].x)),
+                               pack_bf2(v[j].z * rs * bf16_lo(ww[j].y), v[j].w * rs * bf16_hi(ww[j].y)));
     }
     // this exchange is consumed: the next push into the set uses the following epoch
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) hdr->seq[set] = e;
@@ -300,12 +310,31 @@ __global__ void gdn_conv_gates_kernel(const uint16_t* __restrict__ x, int ld, co
                                       const float* __restrict__ dt_bias, float* __restrict__ alpha,
                                       float* __restrict__ beta, int M, int heads,
                                       const int32_t* __restrict__ parents) {
-    chain_in();
     constexpr int dk = 32 * DJ;
     const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (wid >= M * heads * 3) return;
+    const bool live = wid < M * heads * 3, gates = wid % 3 == 0 && lane == 0;
     const int t = wid / (heads * 3), h = (wid / 3) % heads, part = wid % 3;
     const int C = 3 * heads * dk, cp = heads * dk;
+    // the conv taps and gate parameters (written by no kernel of the stream) are requested
+    // before the wait on the predecessor, the gate inputs together with the conv inputs
+    float wk[DJ][KC], dtb = 0.f, alog = 0.f;
+    if (live) {
+#pragma unroll
+        for (int j = 0; j < DJ; ++j)
+#pragma unroll
+            for (int i = 0; i < KC; ++i) wk[j][i] = bf(__ldg(w + (size_t)(part * cp + h * dk + lane + 32 * j) * KC + i));
+        if (gates) {
+            dtb = __ldg(dt_bias + h);
+            alog = __ldg(a_log + h);
+        }
+    }
+    chain_in();
+    if (!live) return;
+    float gb = 0.f, ga = 0.f;
+    if (gates) {
+        gb = bf(ab[(size_t)t * ld_ab + h]);
+        ga = bf(ab[(size_t)t * ld_ab + heads + h]);
+    }
     // back[s]: the block row s steps back from t, or -1 once the history is in the window
     int back[KC];
     back[0] = t;
@@ -315,13 +344,12 @@ __global__ void gdn_conv_gates_kernel(const uint16_t* __restrict__ x, int ld, co
     int depth = 0;  // t's depth, capped at KC - 1 (only its comparison with s matters)
 #pragma unroll
     for (int s = 1; s < KC; ++s) depth += back[s] >= 0;
-    float xin[DJ][KC], wk[DJ][KC];
+    float xin[DJ][KC];
 #pragma unroll
     for (int j = 0; j < DJ; ++j) {
         const int c = part * cp + h * dk + lane + 32 * j;
 #pragma unroll
         for (int i = 0; i < KC; ++i) {
-            wk[j][i] = bf(w[(size_t)c * KC + i]);
             const int src = back[KC - 1 - i];
             xin[j][i] = src < 0 ? bf(window[(size_t)(depth + i) * C + c]) : bf(x[(size_t)src * ld + c]);
         }
@@ -345,12 +373,10 @@ __global__ void gdn_conv_gates_kernel(const uint16_t* __restrict__ x, int ld, co
 #pragma unroll
         for (int j = 0; j < DJ; ++j) out[32 * j] = to_bf(v[j]);
     }
-    if (part == 0 && lane == 0) {
-        const float b = bf(ab[(size_t)t * ld_ab + h]);
-        const float a = bf(ab[(size_t)t * ld_ab + heads + h]);
-        const float sp = a + dt_bias[h] > 20.f ? a + dt_bias[h] : log1pf(__expf(a + dt_bias[h]));
-        alpha[(size_t)t * heads + h] = __expf(-__expf(a_log[h]) * sp);
-        beta[(size_t)t * heads + h] = 1.f / (1.f + __expf(-b));
+    if (gates) {
+        const float sp = ga + dtb > 20.f ? ga + dtb : log1pf(__expf(ga + dtb));
+        alpha[(size_t)t * heads + h] = __expf(-__expf(alog) * sp);
+        beta[(size_t)t * heads + h] = 1.f / (1.f + __expf(-gb));
     }
 }
 
@@ -367,16 +393,35 @@ __global__ void gdn_conv_gates_grouped_kernel(const uint16_t* __restrict__ x, in
                                               const float* __restrict__ a_log, const float* __restrict__ dt_bias,
                                               float* __restrict__ alpha, float* __restrict__ beta, int M, int heads,
                                               int k_heads, const int32_t* __restrict__ parents) {
-    chain_in();
     constexpr int dk = 32 * DJ;
     const int slots = 2 * k_heads + heads;
     const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (wid >= M * slots) return;
+    const bool live = wid < M * slots;
     const int t = wid / slots, slot = wid % slots;
     const int part = slot < k_heads ? 0 : slot < 2 * k_heads ? 1 : 2;
     const int h = slot - part * k_heads;  // head within its part
     const int C = slots * dk;
     const int c0 = part * k_heads * dk + h * dk;  // first channel of this warp's head
+    const bool gates = part == 2 && lane == 0;
+    // weights before the wait on the predecessor, as in gdn_conv_gates_kernel
+    float wk[DJ][KC], dtb = 0.f, alog = 0.f;
+    if (live) {
+#pragma unroll
+        for (int j = 0; j < DJ; ++j)
+#pragma unroll
+            for (int i = 0; i < KC; ++i) wk[j][i] = bf(__ldg(w + (size_t)(c0 + lane + 32 * j) * KC + i));
+        if (gates) {
+            dtb = __ldg(dt_bias + h);
+            alog = __ldg(a_log + h);
+        }
+    }
+    chain_in();
+    if (!live) return;
+    float gb = 0.f, ga = 0.f;
+    if (gates) {
+        gb = bf(ab[(size_t)t * ld_ab + h]);
+        ga = bf(ab[(size_t)t * ld_ab + heads + h]);
+    }
     int back[KC];
     back[0] = t;
 #pragma unroll
@@ -385,13 +430,12 @@ __global__ void gdn_conv_gates_grouped_kernel(const uint16_t* __restrict__ x, in
     int depth = 0;
 #pragma unroll
     for (int s = 1; s < KC; ++s) depth += back[s] >= 0;
-    float xin[DJ][KC], wk[DJ][KC];
+    float xin[DJ][KC];
 #pragma unroll
     for (int j = 0; j < DJ; ++j) {
         const int c = c0 + lane + 32 * j;
 #pragma unroll
         for (int i = 0; i < KC; ++i) {
-            wk[j][i] = bf(w[(size_t)c * KC + i]);
             const int src = back[KC - 1 - i];
             xin[j][i] = src < 0 ? bf(window[(size_t)(depth + i) * C + c]) : bf(x[(size_t)src * ld + c]);
         }
@@ -415,31 +459,57 @@ __global__ void gdn_conv_gates_grouped_kernel(const uint16_t* __restrict__ x, in
     } else {
 #pragma unroll
         for (int j = 0; j < DJ; ++j) out[32 * j] = to_bf(v[j]);
-        if (lane == 0) {
-            const float b = bf(ab[(size_t)t * ld_ab + h]);
-            const float a = bf(ab[(size_t)t * ld_ab + heads + h]);
-            const float sp = a + dt_bias[h] > 20.f ? a + dt_bias[h] : log1pf(__expf(a + dt_bias[h]));
-            alpha[(size_t)t * heads + h] = __expf(-__expf(a_log[h]) * sp);
-            beta[(size_t)t * heads + h] = 1.f / (1.f + __expf(-b));
+        if (gates) {
+            const float sp = ga + dtb > 20.f ? ga + dtb : log1pf(__expf(ga + dtb));
+            alpha[(size_t)t * heads + h] = __expf(-__expf(alog) * sp);
+            beta[(size_t)t * heads + h] = 1.f / (1.f + __expf(-gb));
         }
     }
 }
 
 // out[t, h*dv + i] = rmsnorm(o[t, h, :]) * w[i] * silu(z[t, h*dv + i]); one warp per (t, h).
+// C = dv / 32 (1, 2, 4 or 8): lane l holds elements l + 32 c, the weight requested before
+// the wait on the predecessor and o and z together after it, so the kernel waits on
+// memory once.  C = 0: any dv, in loops.  Both sum the squares in the same order.
+template <int C>
 __global__ void gated_norm_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ z, int ld_z,
                                   const uint16_t* __restrict__ w, uint16_t* __restrict__ out, int M, int heads, int dv,
                                   float eps) {
-    chain_in();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (warp >= M * heads) return;
-    const int t = warp / heads, h = warp % heads;
-    const uint16_t* ov = o + ((size_t)t * heads + h) * dv;
-    float ss = 0.f;
-    for (int i = lane; i < dv; i += 32) ss = fmaf(bf(ov[i]), bf(ov[i]), ss);
-    const float rs = rsqrtf(warp_sum(ss) / dv + eps);
-    for (int i = lane; i < dv; i += 32) {
-        const float zz = bf(z[(size_t)t * ld_z + (size_t)h * dv + i]);
-        out[((size_t)t * heads + h) * dv + i] = to_bf(bf(ov[i]) * rs * bf(w[i]) * silu(zz));
+    if constexpr (C > 0) {
+        float wv[C];
+#pragma unroll
+        for (int c = 0; c < C; ++c) wv[c] = bf(__ldg(w + lane + 32 * c));
+        chain_in();
+        if (warp >= M * heads) return;
+        const int t = warp / heads, h = warp % heads;
+        const uint16_t* ov = o + ((size_t)t * heads + h) * dv;
+        const uint16_t* zv = z + (size_t)t * ld_z + (size_t)h * dv;
+        float ov_f[C], zv_f[C];
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            ov_f[c] = bf(ov[lane + 32 * c]);
+            zv_f[c] = bf(zv[lane + 32 * c]);
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < C; ++c) ss = fmaf(ov_f[c], ov_f[c], ss);
+        const float rs = rsqrtf(warp_sum(ss) / dv + eps);
+#pragma unroll
+        for (int c = 0; c < C; ++c)
+            out[((size_t)t * heads + h) * dv + lane + 32 * c] = to_bf(ov_f[c] * rs * wv[c] * silu(zv_f[c]));
+    } else {
+        chain_in();
+        if (warp >= M * heads) return;
+        const int t = warp / heads, h = warp % heads;
+        const uint16_t* ov = o + ((size_t)t * heads + h) * dv;
+        float ss = 0.f;
+        for (int i = lane; i < dv; i += 32) ss = fmaf(bf(ov[i]), bf(ov[i]), ss);
+        const float rs = rsqrtf(warp_sum(ss) / dv + eps);
+        for (int i = lane; i < dv; i += 32) {
+            const float zz = bf(z[(size_t)t * ld_z + (size_t)h * dv + i]);
+            out[((size_t)t * heads + h) * dv + i] = to_bf(bf(ov[i]) * rs * bf(w[i]) * silu(zz));
+        }
     }
 }
 
@@ -1000,8 +1070,22 @@ extern "C" int dflash_stack_gated_norm(const dflash_bf16* o, const dflash_bf16* 
     if (!o || !z || !weight || !out || M < 1 || heads < 1 || dv < 1)
         return fail(DFLASH_ERR_INVALID_ARGUMENT, "dflash_stack_gated_norm: bad arguments");
     const int warps = M * heads;
-    DFLASH_CUDA_TRY(launch_chained(stack::gated_norm_kernel, dim3((warps + 7) / 8), dim3(256), 0, as_stream(stream), 1,
-                                   o, z, ld_z, weight, out, M, heads, dv, eps));
+    const dim3 grid((warps + 7) / 8), block(256);
+    cudaStream_t s = as_stream(stream);
+    cudaError_t e;
+    switch (dv) {
+        case 32: e = launch_chained(stack::gated_norm_kernel<1>, grid, block, 0, s, 1, o, z, ld_z, weight, out, M,
+                                    heads, dv, eps); break;
+        case 64: e = launch_chained(stack::gated_norm_kernel<2>, grid, block, 0, s, 1, o, z, ld_z, weight, out, M,
+                                    heads, dv, eps); break;
+        case 128: e = launch_chained(stack::gated_norm_kernel<4>, grid, block, 0, s, 1, o, z, ld_z, weight, out, M,
+                                     heads, dv, eps); break;
+        case 256: e = launch_chained(stack::gated_norm_kernel<8>, grid, block, 0, s, 1, o, z, ld_z, weight, out, M,
+                                     heads, dv, eps); break;
+        default: e = launch_chained(stack::gated_norm_kernel<0>, grid, block, 0, s, 1, o, z, ld_z, weight, out, M,
+                                    heads, dv, eps);
+    }
+    DFLASH_CUDA_TRY(e);
     return DFLASH_OK;
 }
 
