@@ -61,6 +61,38 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // multiple of 4 kNormSplit, H / kNormSplit <= 512 VPT, delta / w / out 8-byte aligned.
 constexpr int kNormSplit = 4;
 
+// Cluster barrier halves: arrive (relaxed: orders nothing), arrive with release, wait with
+// acquire.  Every thread of every CTA of the cluster takes each step.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void st_shared_cluster_f32(uint32_t cluster_addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+
+// Hands this CTA's part of a row's sum of squares to the kNormSplit CTAs of the cluster and
+// returns the row's total, the parts added in rank order (the same bits in every CTA).
+// The part is stored into slot `rank` of every CTA's `parts`, so after the one barrier all
+// reads are local and no CTA touches another's shared memory again: a CTA may exit as soon
+// as it is done.  The caller arrived (relaxed) on the cluster barrier at its start, so that
+// every CTA is known to be running before it is written to; this waits for that phase first.
+__device__ __forceinline__ float cluster_row_total(float part, float* parts, uint32_t rank) {
+    cluster_wait_acquire();
+    if (threadIdx.x < kNormSplit) st_shared_cluster_f32(map_to_rank(smem_u32(&parts[rank]), threadIdx.x), part);
+    cluster_arrive_release();
+    cluster_wait_acquire();
+    float tot = 0.f;
+#pragma unroll
+    for (int r = 0; r < kNormSplit; ++r) tot += parts[r];
+    return tot;
+}
+
 // This thread's VPT words (4 bf16 each) of a norm weight: words base + threadIdx.x + 128 j.
 template <int VPT>
 __device__ __forceinline__ void load_norm_weight(uint2 (&ww)[VPT], const uint16_t* __restrict__ w, int base, int P4) {
@@ -77,9 +109,10 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(float* __restrict__ re
                                                           const uint16_t* __restrict__ w, uint16_t* __restrict__ out,
                                                           int H, float eps) {
     __shared__ float red[4];
-    __shared__ float part;
+    __shared__ float parts[kNormSplit];
     const uint32_t rank = cluster_rank();
     const int m = blockIdx.y, P4 = H / (4 * kNormSplit), base = (int)rank * P4;  // float4 units
+    cluster_arrive_relaxed();
     uint2 ww[VPT];
     load_norm_weight<VPT>(ww, w, base, P4);
     chain_in();
@@ -103,12 +136,7 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(float* __restrict__ re
             ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
         }
     }
-    ss = block_sum(ss, red);
-    if (threadIdx.x == 0) part = ss;
-    cluster_sync_all();  // every part's sum is visible to the cluster
-    float tot = 0.f;
-#pragma unroll
-    for (int r = 0; r < kNormSplit; ++r) tot += ld_shared_cluster_f32(map_to_rank(smem_u32(&part), r));
+    const float tot = cluster_row_total(block_sum(ss, red), parts, rank);
     const float rs = rsqrtf(tot / H + eps);
     uint2* o4 = reinterpret_cast<uint2*>(out + (size_t)m * H) + base;
 #pragma unroll
@@ -118,7 +146,6 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(float* __restrict__ re
             o4[i] = make_uint2(pack_bf2(v[j].x * rs * bf16_lo(ww[j].x), v[j].y * rs * bf16_hi(ww[j].x)),
                                pack_bf2(v[j].z * rs * bf16_lo(ww[j].y), v[j].w * rs * bf16_hi(ww[j].y)));
     }
-    cluster_sync_all();  // the other CTAs are done reading `part`
 }
 
 // add_rmsnorm whose delta is the tensor-parallel sum of the ranks' partials, read from
@@ -130,9 +157,10 @@ __global__ void __launch_bounds__(128) add_rmsnorm_reduce_kernel(float* __restri
                                                                  int set, const uint16_t* __restrict__ w,
                                                                  uint16_t* __restrict__ out, int M, int H, float eps) {
     __shared__ float red[4];
-    __shared__ float part;
+    __shared__ float parts[kNormSplit];
     const uint32_t rank = cluster_rank();
     const int m = blockIdx.y, P4 = H / (4 * kNormSplit), base = (int)rank * P4;  // float4 units
+    cluster_arrive_relaxed();
     uint2 ww[VPT];
     load_norm_weight<VPT>(ww, w, base, P4);
     chain_in();
@@ -179,12 +207,7 @@ __global__ void __launch_bounds__(128) add_rmsnorm_reduce_kernel(float* __restri
             ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
         }
     }
-    ss = block_sum(ss, red);
-    if (threadIdx.x == 0) part = ss;
-    cluster_sync_all();
-    float tot = 0.f;
-#pragma unroll
-    for (int r = 0; r < kNormSplit; ++r) tot += ld_shared_cluster_f32(map_to_rank(smem_u32(&part), r));
+    const float tot = cluster_row_total(block_sum(ss, red), parts, rank);
     const float rs = rsqrtf(tot / H + eps);
     uint2* o4 = reinterpret_cast<uint2*>(out + (size_t)m * H) + base;
 #pragma unroll
@@ -196,7 +219,6 @@ __global__ void __launch_bounds__(128) add_rmsnorm_reduce_kernel(float* __restri
     }
     // this exchange is consumed: the next push into the set uses the following epoch
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) hdr->seq[set] = e;
-    cluster_sync_all();
 }
 
 // The same for any H and alignment (row re-read from global memory for the second pass).
