@@ -550,7 +550,30 @@ __global__ void attn_prep_kernel(uint16_t* __restrict__ qkv, int ld, const uint1
                                  uint16_t* __restrict__ cache_v, int M, int hq, int hkv, int rot, int pos0,
                                  int max_len, float eps, float theta, const int32_t* __restrict__ parents,
                                  const int32_t* __restrict__ position) {
+    constexpr int d = CH * 32;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int slots = hq + hkv;
+    const bool live = warp < M * slots;
+    const int t = live ? warp / slots : 0, slot = warp % slots;
+    // the norm weight (written by no kernel of the stream) is requested before the wait on
+    // the predecessor; after it, the cache position and this warp's rows are requested together
+    const uint16_t* nw = slot < hq ? q_norm : k_norm;
+    float nwv[CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) nwv[c] = live ? bf(__ldg(nw + lane + 32 * c)) : 0.f;
     chain_in();
+    uint16_t* row = qkv + (size_t)t * ld;
+    uint16_t* src = slot < hq ? row + (size_t)slot * d : row + (size_t)(2 * hq + (slot - hq)) * d;
+    const uint16_t* vs = row + (size_t)(2 * hq + hkv + (slot - hq)) * d;  // slot >= hq: the v row
+    float v[CH];
+    uint16_t vcopy[CH];
+    if (live) {
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            v[c] = bf(src[lane + 32 * c]);
+            if (slot >= hq) vcopy[c] = vs[lane + 32 * c];
+        }
+    }
     if (position) {  // the cache position from device memory (a graph replayed at a new context)
         pos0 = *position;
         if (pos0 < 0 || pos0 + M > max_len) {
@@ -558,32 +581,19 @@ __global__ void attn_prep_kernel(uint16_t* __restrict__ qkv, int ld, const uint1
             return;
         }
     }
-    constexpr int d = CH * 32;
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    const int slots = hq + hkv;
-    if (warp >= M * slots) return;
-    const int t = warp / slots, slot = warp % slots;
-    uint16_t* row = qkv + (size_t)t * ld;
-    if (slot >= hq) {  // v copy first (independent of the k work)
-        const int j = slot - hq;
-        const uint16_t* vs = row + (size_t)(2 * hq + hkv + j) * d;
-        uint16_t* vd = cache_v + ((size_t)j * max_len + pos0 + t) * d;
+    if (!live) return;
+    if (slot >= hq) {
+        uint16_t* vd = cache_v + ((size_t)(slot - hq) * max_len + pos0 + t) * d;
 #pragma unroll
-        for (int c = 0; c < CH; ++c) vd[lane + 32 * c] = vs[lane + 32 * c];
+        for (int c = 0; c < CH; ++c) vd[lane + 32 * c] = vcopy[c];
     }
-    uint16_t* src = slot < hq ? row + (size_t)slot * d : row + (size_t)(2 * hq + (slot - hq)) * d;
     uint16_t* dst = slot < hq ? src : cache_k + ((size_t)(slot - hq) * max_len + pos0 + t) * d;
-    const uint16_t* nw = slot < hq ? q_norm : k_norm;
-    float v[CH];
     float ss = 0.f;
 #pragma unroll
-    for (int c = 0; c < CH; ++c) {
-        v[c] = bf(src[lane + 32 * c]);
-        ss = fmaf(v[c], v[c], ss);
-    }
+    for (int c = 0; c < CH; ++c) ss = fmaf(v[c], v[c], ss);
     const float rs = rsqrtf(warp_sum(ss) / d + eps);
 #pragma unroll
-    for (int c = 0; c < CH; ++c) v[c] = bf_round(v[c] * rs * bf(nw[lane + 32 * c]));
+    for (int c = 0; c < CH; ++c) v[c] = bf_round(v[c] * rs * nwv[c]);
     const int half_c = rot / 64;  // pair partner is c + half_c
     const float pos = (float)(pos0 + (parents ? tree_walk(parents, t).depth : t));
 #pragma unroll
