@@ -642,7 +642,7 @@ constexpr int kSplit = 4;       // CTAs per (kv head, token) ...
 constexpr int kSplitSmall = 8;  // ... or, when the grid would leave most SMs idle, twice as many
 constexpr int kChunk = 384;     // keys a CTA scores per pass (a 1032-key context in one pass at SPLIT 4)
 constexpr int kMaxG = 8;
-constexpr int kUnroll = 4;
+constexpr int kUnroll = 8;     // value rows a warp has in flight in the p V pass (its key order does not depend on it)
 
 template <int CH>
 __device__ __forceinline__ void load_row(const uint16_t* p, float (&v)[CH]) {
