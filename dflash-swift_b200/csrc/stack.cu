@@ -169,42 +169,57 @@ __global__ void __launch_bounds__(128) add_rmsnorm_reduce_kernel(float* __restri
     float4* r4 = reinterpret_cast<float4*>(resid + (size_t)m * H) + base;
     float4 v[VPT];
     float ss = 0.f;
+    // JB float4 slices at a time: their residual values and every source's two words per
+    // slice are all requested before any is inspected, so the loads overlap; a word without
+    // the expected epoch is then waited for alone.  Slices, sources and components are
+    // summed in the same order as one slice at a time would.
+    constexpr int JB = VPT < 4 ? VPT : VPT == 4 ? 4 : 2;  // 8 would spill (2 x 8 words per slice)
 #pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-        const int i = threadIdx.x + 128 * j;
-        if (i < P4) {
-            float sx = 0.f, sy = 0.f, sz = 0.f, sw = 0.f;
-            const size_t word = ((size_t)m * H + 4 * (size_t)(base + i)) / 2;  // two data words per float4
-            // every source's two words are requested before any is inspected, so the
-            // loads overlap; a word without the expected epoch is then waited for alone
-            uint64_t w0[tp::kMaxRanks], w1[tp::kMaxRanks];
+    for (int j0 = 0; j0 < VPT; j0 += JB) {
+        uint64_t w0[JB][tp::kMaxRanks], w1[JB][tp::kMaxRanks];
 #pragma unroll
-            for (int r = 0; r < tp::kMaxRanks; ++r) {
-                if (r < world) {
-                    const uint64_t* src = tp::slot_ptr(xbase, world, M, H, set, r) + word;
-                    w0[r] = tp::ld_relaxed_sys_u64(src);
-                    w1[r] = tp::ld_relaxed_sys_u64(src + 1);
+        for (int jj = 0; jj < JB; ++jj) {
+            const int i = threadIdx.x + 128 * (j0 + jj);
+            if (i < P4) {
+                v[j0 + jj] = r4[i];
+                const size_t word = ((size_t)m * H + 4 * (size_t)(base + i)) / 2;  // two data words per float4
+#pragma unroll
+                for (int r = 0; r < tp::kMaxRanks; ++r) {
+                    if (r < world) {
+                        const uint64_t* src = tp::slot_ptr(xbase, world, M, H, set, r) + word;
+                        w0[jj][r] = tp::ld_relaxed_sys_u64(src);
+                        w1[jj][r] = tp::ld_relaxed_sys_u64(src + 1);
+                    }
                 }
             }
+        }
 #pragma unroll
-            for (int r = 0; r < tp::kMaxRanks; ++r) {
-                if (r < world) {
-                    const uint64_t* src = tp::slot_ptr(xbase, world, M, H, set, r) + word;
-                    const uint32_t d0 = (uint32_t)(w0[r] >> 32) == e ? (uint32_t)w0[r] : tp::wait_word(src, e);
-                    const uint32_t d1 = (uint32_t)(w1[r] >> 32) == e ? (uint32_t)w1[r] : tp::wait_word(src + 1, e);
-                    sx += bf16_lo(d0);
-                    sy += bf16_hi(d0);
-                    sz += bf16_lo(d1);
-                    sw += bf16_hi(d1);
+        for (int jj = 0; jj < JB; ++jj) {
+            const int j = j0 + jj, i = threadIdx.x + 128 * j;
+            if (i < P4) {
+                const size_t word = ((size_t)m * H + 4 * (size_t)(base + i)) / 2;
+                float sx = 0.f, sy = 0.f, sz = 0.f, sw = 0.f;
+#pragma unroll
+                for (int r = 0; r < tp::kMaxRanks; ++r) {
+                    if (r < world) {
+                        const uint64_t* src = tp::slot_ptr(xbase, world, M, H, set, r) + word;
+                        const uint32_t d0 =
+                            (uint32_t)(w0[jj][r] >> 32) == e ? (uint32_t)w0[jj][r] : tp::wait_word(src, e);
+                        const uint32_t d1 =
+                            (uint32_t)(w1[jj][r] >> 32) == e ? (uint32_t)w1[jj][r] : tp::wait_word(src + 1, e);
+                        sx += bf16_lo(d0);
+                        sy += bf16_hi(d0);
+                        sz += bf16_lo(d1);
+                        sw += bf16_hi(d1);
+                    }
                 }
+                v[j].x += bf_round(sx);
+                v[j].y += bf_round(sy);
+                v[j].z += bf_round(sz);
+                v[j].w += bf_round(sw);
+                r4[i] = v[j];
+                ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
             }
-            v[j] = r4[i];
-            v[j].x += bf_round(sx);
-            v[j].y += bf_round(sy);
-            v[j].z += bf_round(sz);
-            v[j].w += bf_round(sw);
-            r4[i] = v[j];
-            ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
         }
     }
     const float tot = cluster_row_total(block_sum(ss, red), parts, rank);

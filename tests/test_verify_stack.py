@@ -273,13 +273,14 @@ def test_qmm_swiglu_input_equals_separate_silu_mul(dc, O, cuda):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("via", ["push_kernel", "qmm_epilogue"])
-@pytest.mark.parametrize("H", [512, 5120])
+@pytest.mark.parametrize("H", [512, 5120, 12288])
 def test_peer_exchange_two_ranks_in_one_process(dc, cuda, via, H):
     """The exchange protocol with two 'ranks' emulated by two buffers on one GPU (each
     push completes before the sums are read, so nothing waits on another kernel): both
     buffers' reducing norms equal add_rmsnorm with delta = bf16(y0 + y1), for two
     consecutive exchanges (both slot sets) and a third that reuses set 0.  H = 5120 is the
-    config-4 hidden size (four float4 per thread of a norm CTA, 512 two)."""
+    config-4 hidden size (four float4 per thread of a norm CTA, 512 two, 12288 eight: the
+    slices' loads are batched four, two and two at a time)."""
     M, K = 8, 1024
     gen = torch.Generator(device=cuda).manual_seed(4)
     ex = [dc.PeerExchange(2, M, H) for _ in range(2)]
